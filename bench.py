@@ -1,0 +1,396 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 MHA forward path — BASELINE metric "MHA prefill tok/s +
+decode tok/s at 1/2/4/8 B200; % of roofline".
+
+Default workload = BASELINE config 5 (the metric's 1/2/4/8-GPU configuration):
+batch 32 x seq 8192, d_model 4096, 32 heads x 128, causal, RoPE, BF16 activations
+and weights, FP32 accumulation. Heads are sharded 32/N per GPU, the output
+projection is row-sharded and summed with one NCCL all-reduce. A step = one
+prefill forward over all 262144 tokens; value = whole-job prefill tok/s. After the
+timed prefill, 256 autoregressive decode steps run against the resulting KV cache
+and are reported under "decode".
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+  torchrun --nproc-per-node N bench.py --gpus N ...      (N > 1)
+
+Data is synthetic (no dataset is named by the baseline): the counter-based
+SplitMix64 stream of welvet_b200_fill_synthetic — Xavier-uniform weights (seed 0,
+order Wq, Wk, Wv, Wo), N(0,1) inputs (seed 1). Inputs (x: 2.1 GB) exceed L2
+(126 MB), so no explicit flush is needed between steps.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "welvet.metal_b200"))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+WORKLOADS = {
+    # name: (batch, seq, d_model, heads, kv_heads, weight_format)
+    "cfg5": (32, 8192, 4096, 32, 32, 0),
+    "cfg4-fp8": (4, 4096, 4096, 32, 32, 1),
+    "cfg4-nf4": (4, 4096, 4096, 32, 32, 2),
+    "cfg2": (8, 2048, 1024, 16, 16, 0),
+}
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            j = json.load(f)
+        return dict(hbm=j["hbm_gbs"], bf16=j["bf16_tflops"], bf16_sus=j.get("bf16_tflops_sustained", j["bf16_tflops"]),
+                    src="measured")
+    return dict(hbm=6650.0, bf16=1590.0, bf16_sus=1400.0, src="fallback")
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region (SM clock, throttle reasons)."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[4:8]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+def flops_prefill(B, T, d, H, NK, hd):
+    qd, kd = H * hd, NK * hd
+    proj = 2.0 * B * T * d * (qd + 2 * kd) + 2.0 * B * T * qd * d
+    attn = 4.0 * hd * H * B * T * (T + 1) / 2
+    return proj, attn
+
+
+def cpu_sample(d, H, NK, T_s, threads=0):
+    """Times the FP64 oracle (multithreaded C++) on one sequence of T_s tokens of the
+    workload's layer shape; returns (seconds, flops)."""
+    import numpy as np
+
+    import oracle_py as O
+    import welvet_b200 as W
+    hd = d // H
+    Ws = W.xavier_weights(d, H * hd, NK * hd, seed=0)
+    x = W.synthetic(T_s * d, 1, 1, 1.0).reshape(T_s, d)
+    cfg = O.MhaCfg(d_model=d, num_heads=H, num_kv_heads=NK, per_sequence=1)
+    t0 = time.perf_counter()
+    O.mha_forward(cfg, 1, T_s, *Ws, x, threads=threads)
+    dt = time.perf_counter() - t0
+    pf, af = flops_prefill(1, T_s, d, H, NK, hd)
+    del np
+    return dt, pf + af
+
+
+def run_reference(args):
+    """Reference arm: the reference's own MHA code (mha.cpp + dense.cpp + soft-double
+    shaders, oracle/_ref) on the host cores through its one-shot entry
+    (welvet_mha_forward_f32 semantics: encode + mount + forward per call), each step a
+    bounded sample (1 sequence x T_r tokens of the workload's layer shape), scaled to the
+    workload's tok/s by algorithmic FLOPs per token. Falls back to the FP64 port when
+    oracle/_ref was not built."""
+    import numpy as np
+
+    import oracle_py as O
+    import welvet_b200 as W
+    B, T, d, H, NK, wf = WORKLOADS[args.workload]
+    hd = d // H
+    pf, af = flops_prefill(B, T, d, H, NK, hd)
+    flops_per_tok = (pf + af) / (B * T)
+    Ws = W.xavier_weights(d, H * hd, NK * hd, seed=0)
+    kind = "reference" if O.ref_available() else "port"
+    T_r = args.ref_tokens
+    x = W.synthetic(T_r * d, 1, 1, 1.0).reshape(T_r, d)
+    cfg = O.MhaCfg(d_model=d, num_heads=H, num_kv_heads=NK, max_seq_len=max(512, T_r))
+
+    def step():
+        if kind == "reference":
+            code, msg, _, _ = O.ref_mha_forward(cfg, 1, T_r, *Ws, x, 1)
+            if code:
+                raise RuntimeError(msg)
+        else:
+            O.mha_forward(cfg, 1, T_r, *Ws, x)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = (time.perf_counter() - t0) / args.steps
+    pf_s, af_s = flops_prefill(1, T_r, d, H, NK, hd)
+    value = (pf_s + af_s) / dt / flops_per_tok
+    cores = os.cpu_count()
+    sample = (f"1 sequence x {T_r} tokens of the {args.workload} layer (d={d}, {H}x{hd}) per step, FP32 "
+              f"reference semantics; tok/s scaled by algorithmic FLOPs/token of the full workload")
+    line = {"impl": "reference", "metric": "MHA prefill tok/s", "value": value, "unit": "tok/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64 (soft-double)",
+            "data": "synthetic", "config": {"workload": args.workload},
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": kind, "sample": sample},
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    del np
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--workload", default="cfg5", choices=sorted(WORKLOADS))
+    ap.add_argument("--batch", type=int, default=0, help="override batch (small ncu cases)")
+    ap.add_argument("--seq", type=int, default=0, help="override seq")
+    ap.add_argument("--decode-steps", type=int, default=256)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-tokens", type=int, default=1024)
+    ap.add_argument("--ref-tokens", type=int, default=16)
+    args = ap.parse_args()
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        if rank == 0:
+            run_reference(args)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    import welvet_b200 as W
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    B, T, d, H, NK, wf = WORKLOADS[args.workload]
+    B = args.batch or B
+    T = args.seq or T
+    hd = d // H
+    if H % world:
+        raise SystemExit(f"{H} heads do not shard over {world} GPUs")
+    hc = H // world
+    cfg = W.MhaConfig.make(d, H, NK, precision=1, weight_format=wf, head_begin=rank * hc, head_count=hc,
+                           device=local)
+    # Full FP32 weights generated on the device (same stream on every rank), then mounted.
+    shapes = [(H * hd, d), (NK * hd, d), (NK * hd, d), (d, H * hd)]
+    ws, off = [], 0
+    for r, c in shapes:
+        t = torch.empty(r, c, device="cuda", dtype=torch.float32)
+        a = (6.0 / (r + c)) ** 0.5 if wf == 0 else 0.02
+        W.fill_synthetic(t, 0, 0 if wf == 0 else 1, a, offset=off)
+        off += r * c
+        ws.append(t)
+    torch.cuda.synchronize()
+    layer = W.MhaLayer(cfg, *ws, dtype=1)
+    del ws
+    torch.cuda.empty_cache()
+    if world > 1:
+        uid = [W.comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        layer.attach_comm(uid[0], world, rank)
+
+    M = B * T
+    x = torch.empty(M, d, device="cuda", dtype=torch.bfloat16)
+    W.fill_synthetic(x, 1, 1, 1.0)
+    post = torch.empty(M, d, device="cuda", dtype=torch.bfloat16)
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        layer.forward(B, T, x, None, post, stream=stream)
+    barrier()
+    layer.check_device()
+
+    # ------------------------------------------------------------ timed prefill
+    clocks = Clocks(local)
+    clocks.start()
+    W.profile_read(reset=True)
+    W.profile_enable(True)
+    W.launch_count(reset=True)
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        layer.forward(B, T, x, None, post, stream=stream)
+    ev1.record(stream)
+    barrier()
+    launches = W.launch_count(reset=True)
+    W.profile_enable(False)
+    prof = W.profile_read(reset=True)
+    clk = clocks.stop()
+    layer.check_device()
+    ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps)
+    tokps = M / (ms / 1e3)
+
+    pk = peaks()
+    pf, af = flops_prefill(B, T, d, H, NK, hd)
+    kd_l = (hc // (H // NK)) * hd  # this rank's KV columns
+    per_launch = {"gemm_qkv": 2.0 * M * d * (hc * hd + 2 * kd_l),
+                  "attn_prefill": 4.0 * hd * hc * B * T * (T + 1) / 2,
+                  "gemm_o": 2.0 * M * hc * hd * d}
+    shares = {k: prof[k][0] for k in per_launch}
+    dom = max(shares, key=shares.get)
+    tot, cnt = prof[dom]
+    avg_ms = tot / max(cnt, 1)
+    achieved = per_launch[dom] / (avg_ms / 1e3) / 1e12
+    roof = {"bound": "tensor", "kernel": dom, "achieved": achieved, "peak": pk["bf16_sus"], "unit": "TFLOP/s",
+            "frac": achieved / pk["bf16_sus"], "peak_kind": f"{pk['src']} sustained bf16 (of {pk['src']})",
+            "traffic": None, "flops_per_launch": per_launch[dom], "avg_launch_ms": avg_ms,
+            "kernel_ms_per_step": {k: prof[k][0] / args.steps for k in per_launch},
+            "step_tflops": (pf + af) / world / (ms / 1e3) / 1e12}
+
+    # ---------------------------------------------------------------- e2e
+    e2e = None
+    if not args.no_e2e:
+        xh = x.cpu().pin_memory()
+        ph = torch.empty(M, d, dtype=torch.bfloat16).pin_memory()
+        layer.forward(B, T, xh, None, ph)  # warm the staging buffers
+        barrier()
+        t0 = time.perf_counter()
+        ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ea.record(stream)
+        n_e2e = max(1, min(args.steps, 3))
+        for _ in range(n_e2e):
+            layer.forward(B, T, xh, None, ph)  # H2D x, forward, D2H post, synchronise
+        eb.record(stream)
+        barrier()
+        e_ms = max_over_ranks(max(ea.elapsed_time(eb), (time.perf_counter() - t0) * 1e3) / n_e2e)
+        e2e = {"value": M / (e_ms / 1e3), "unit": "tok/s", "ms_per_step": e_ms, "h2d_bytes_per_step": M * d * 2,
+               "d2h_bytes_per_step": M * d * 2, "api": "welvet_b200_mha_forward (host buffers, pinned)"}
+        del xh, ph
+
+    # --------------------------------------------------------------- decode
+    decode = None
+    if args.decode_steps > 0:
+        del post
+        torch.cuda.empty_cache()
+        ctx_max = T + args.decode_steps + 16
+        kv = W.KvCache(layer, B, ctx_max)
+        post = torch.empty(M, d, device="cuda", dtype=torch.bfloat16)
+        layer.prefill(kv, B, T, x, None, post, stream=stream)
+        del post
+        xd = torch.empty(B, d, device="cuda", dtype=torch.bfloat16)
+        W.fill_synthetic(xd, 1, 1, 1.0, offset=M * d)
+        pd = torch.empty(B, d, device="cuda", dtype=torch.bfloat16)
+        barrier()
+        W.profile_read(reset=True)
+        W.profile_enable(True)
+        ev0.record(stream)
+        for _ in range(args.decode_steps):
+            layer.decode(kv, B, xd, None, pd, stream=stream)
+        ev1.record(stream)
+        barrier()
+        W.profile_enable(False)
+        dprof = W.profile_read(reset=True)
+        layer.check_device()
+        dms = max_over_ranks(ev0.elapsed_time(ev1) / args.decode_steps)
+        # algorithmic bytes of one decode-attention launch: the K and V rows of every
+        # cached position (average context over the steps) + q and the output
+        avg_ctx = T + (args.decode_steps + 1) / 2.0
+        attn_bytes = B * avg_ctx * kd_l * 2 * 2 + 2 * B * hc * hd * 2
+        at, ac = dprof["attn_decode"]
+        a_ms = at / max(ac, 1)
+        gbs = attn_bytes / (a_ms / 1e3) / 1e9
+        wbytes = (d * (hc * hd + 2 * kd_l) + hc * hd * d) * 2
+        step_bytes = attn_bytes + wbytes
+        decode = {"value": B / (dms / 1e3), "unit": "tok/s", "ms_per_step": dms, "steps": args.decode_steps,
+                  "context": f"{T}..{T + args.decode_steps}",
+                  "roofline": {"bound": "hbm", "kernel": "attn_decode", "achieved": gbs, "peak": pk["hbm"],
+                               "unit": "GB/s", "frac": gbs / pk["hbm"], "traffic": None,
+                               "bytes_per_launch": attn_bytes, "avg_launch_ms": a_ms,
+                               "step_bytes": step_bytes, "step_gbs": step_bytes / (dms / 1e3) / 1e9,
+                               "kernel_ms_per_step": {k: dprof[k][0] / args.decode_steps for k in
+                                                      ("gemm_qkv_decode", "attn_decode", "gemm_o_decode",
+                                                       "allreduce")}}}
+        kv.close()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        dt, fl = cpu_sample(d, H, NK, args.cpu_tokens)
+        per_tok = (pf + af) / M
+        cpu = {"value": fl / dt / per_tok, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+               "sample": f"FP64 oracle, 1 sequence x {args.cpu_tokens} tokens of the layer (d={d}, {H}x{hd}), "
+                         f"{dt:.1f} s; tok/s scaled by algorithmic FLOPs/token of the full workload"}
+
+    if rank == 0:
+        line = {"metric": "MHA prefill tok/s (BASELINE config 5; decode tok/s under 'decode')",
+                "value": tokps, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": "bf16", "data": "synthetic (SplitMix64 counter stream: Xavier weights seed 0, N(0,1) x seed 1)",
+                "config": {"workload": f"{args.workload}: B={B} T={T} d={d} H={H}x{hd} NK={NK} causal RoPE"
+                                       f"{' fp8 weights' if wf == 1 else ' nf4 weights' if wf == 2 else ''}",
+                           "global_batch": B, "seq_len": T, "parallelism": f"tp{world} (heads {hc}/GPU)",
+                           "l2": "inputs larger than L2 (x is %.1f GB)" % (M * d * 2 / 1e9)},
+                "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "clocks": clk,
+                "decode": decode, "profile_ms": {k: v[0] / args.steps for k, v in prof.items() if v[1]}}
+        print(json.dumps(line), flush=True)
+    layer.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

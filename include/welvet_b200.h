@@ -1,0 +1,172 @@
+#pragma once
+
+/* welvet B200 extension ABI (libwelvet_b200.so). Not part of the reference's
+ * include/welvet_c.h; every entry point states the reference interface it
+ * generalises, or that it has none.
+ *
+ * Conventions: plain pointers and sizes only. `on_device` = 1 means the buffer
+ * arguments are CUDA device pointers and the call is asynchronous on `stream`
+ * (a cudaStream_t, NULL = legacy default stream); 0 means host pointers, copied
+ * in and out inside the call, which returns after the results are on the host.
+ * Activations are FP32 when the layer's precision is 0 and BF16 (uint16 bit
+ * patterns) when it is 1. Statuses follow welvet_c.h (code 4 = CUDA/NCCL error,
+ * including a device-side timeout reported by a kernel's error word). */
+
+#include "welvet_c.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* welvet::mha::Config (reference include/welvet/mha.hpp:39-64) plus the B200
+ * execution choices. seq_mode 0 keeps the reference's stream semantics
+ * (shaders/ops_mha.metal:58-80); 1 treats each batch row as an independent
+ * sequence starting at position 0 (the usual LLM batch). */
+typedef struct welvet_b200_mha_config {
+  int32_t d_model, num_heads, num_kv_heads, head_dim, max_seq_len;
+  int32_t mask, pos, softmax, window, prefix_len, window_causal;
+  double rope_theta, scale_override;
+  int32_t seq_mode;      /* 0 stream (reference), 1 per sequence */
+  int32_t precision;     /* 0 FP32 activations (3xTF32 tensor cores), 1 BF16 */
+  int32_t weight_format; /* precision 1 only: 0 BF16 (from the decoded dtype), 1 FP8-E4M3 with
+                            one FP32 scale per output channel, 2 NF4 with one FP32 absmax per
+                            64 weights */
+  int32_t head_begin, head_count; /* this rank's query heads; head_count 0 = all heads */
+  int32_t device;                 /* CUDA ordinal; -1 = current device */
+} welvet_b200_mha_config;
+
+typedef struct welvet_b200_mha welvet_b200_mha;
+typedef struct welvet_b200_kv welvet_b200_kv;
+
+/* Fills `cfg` with the defaults of reference mha::decoder_causal
+ * (src/layers/mha/mha.cpp:96-106): causal mask, RoPE, theta 10000. */
+WELVET_API void welvet_b200_mha_config_default(welvet_b200_mha_config* cfg, int32_t d_model,
+                                               int32_t num_heads, int32_t num_kv_heads);
+
+/* Resident layer (generalises reference mha::new_configured,
+ * src/layers/mha/mha.cpp:108-136, plus the Dense resident mount of
+ * src/layers/dense/dense.cpp:50-97): weights are encoded once to `dtype`
+ * (FormatNone ids of reference include/welvet/dtype.hpp), decoded on the GPU and
+ * kept in HBM in the layer's compute format. Q/K/V/O are the full FP32 matrices
+ * (host or device per weights_on_device); a head shard keeps only its slices. */
+WELVET_API welvet_status welvet_b200_mha_mount(const welvet_b200_mha_config* cfg, int32_t dtype,
+                                               const float* Q, const float* K, const float* V,
+                                               const float* O, int32_t weights_on_device,
+                                               welvet_b200_mha** out);
+WELVET_API void welvet_b200_mha_release(welvet_b200_mha* layer);
+
+/* Forward of reference mha::forward (src/layers/mha/mha.cpp:138-205) on a resident
+ * layer: x [batch*seq, d_model] -> pre [batch*seq, q_dim_local], post
+ * [batch*seq, d_model]. pre may be NULL. With a communicator attached, post is the
+ * sum over ranks (all-reduce after the row-sharded output projection). */
+WELVET_API welvet_status welvet_b200_mha_forward(welvet_b200_mha* layer, int32_t batch,
+                                                 int32_t seq, const void* x, void* pre, void* post,
+                                                 int32_t on_device, void* stream);
+
+/* Reads and clears the device error word of the layer's device after a
+ * synchronisation; code 4 with the kernel's reason when a device-side bounded wait
+ * expired or a bound check failed. No reference counterpart. */
+WELVET_API welvet_status welvet_b200_mha_check(welvet_b200_mha* layer);
+
+/* ---- KV cache (no reference counterpart: the reference has no KV cache) ----
+ * Paged: pages of 16 tokens, pools laid out [page][kv_head][16][head_dim] in the
+ * layer's precision; each of max_batch sequences owns ceil(max_ctx/16) pages. */
+WELVET_API welvet_status welvet_b200_kv_create(welvet_b200_mha* layer, int32_t max_batch,
+                                               int32_t max_ctx, welvet_b200_kv** out);
+WELVET_API void welvet_b200_kv_release(welvet_b200_kv* kv);
+/* Sets the cached length of `batch` sequences to ctx_len and writes their rows
+ * [0, ctx_len) from k, v [batch, ctx_len, kv_dim_local] (keys as cached, i.e. after
+ * position encoding). k/v NULL only sets the lengths. */
+WELVET_API welvet_status welvet_b200_kv_fill(welvet_b200_kv* kv, int32_t batch, int32_t ctx_len,
+                                             const void* k, const void* v, int32_t on_device,
+                                             void* stream);
+/* Per-sequence prefill: forward of `seq` tokens per sequence (positions 0..seq-1)
+ * that also writes their keys/values into the cache (cached length := seq). */
+WELVET_API welvet_status welvet_b200_mha_prefill(welvet_b200_mha* layer, welvet_b200_kv* kv,
+                                                 int32_t batch, int32_t seq, const void* x,
+                                                 void* pre, void* post, int32_t on_device,
+                                                 void* stream);
+/* One decode step: x_new [batch, d_model], one token per sequence at position
+ * ctx_len[b]; appends its key/value, attends over the cache (split-KV), then the
+ * output projection. pre [batch, q_dim_local] may be NULL. */
+WELVET_API welvet_status welvet_b200_mha_decode(welvet_b200_mha* layer, welvet_b200_kv* kv,
+                                                int32_t batch, const void* x_new, void* pre,
+                                                void* post, int32_t on_device, void* stream);
+
+/* ---- multi-GPU (no reference counterpart: the reference is single-device) ----
+ * One process per GPU. Rank 0 creates the id, the caller distributes it; every
+ * rank attaches an NCCL communicator to its head-sharded layer. */
+WELVET_API welvet_status welvet_b200_comm_unique_id(uint8_t id[128]);
+WELVET_API welvet_status welvet_b200_comm_attach(welvet_b200_mha* layer, const uint8_t id[128],
+                                                 int32_t nranks, int32_t rank);
+
+/* ---- kernel-level entry points (device pointers, asynchronous on `stream`) ----
+ * Used by the parity tests and the benchmark to exercise one kernel at a time.
+ * No reference counterparts except where cited. Each returns code 4 on a launch
+ * failure; device-side faults show up in welvet_b200_device_check. */
+
+/* C[M,N] = A[M,K] B[N,K]^T (reference Dense MatVec, shaders/welvet_dense.metal:54-85).
+ * kind 0: A,B bf16 -> out bf16 (out_bf16=1) or fp32; kind 1: 3xTF32 with A=(a,a_lo),
+ * B=(b,b_lo) fp32 TF32 splits -> out fp32; kind 2: A bf16, B FP8-E4M3 codes with
+ * per-row scale b_scale [N]; kind 3: A bf16, B NF4 packed [N, K/2] with b_scale
+ * [N, K/64]. */
+WELVET_API welvet_status welvet_b200_gemm(int32_t kind, int32_t M, int32_t N, int32_t K,
+                                          const void* a, const void* a_lo, const void* b,
+                                          const void* b_lo, const float* b_scale, void* out,
+                                          int32_t out_bf16, void* stream);
+/* FP32 -> (hi, lo) TF32 split, hi + lo == x exactly. */
+WELVET_API welvet_status welvet_b200_split_tf32(const float* x, float* hi, float* lo, int64_t n,
+                                                void* stream);
+/* Attention forward over token-major q [*, q_dim], k/v [*, kv_dim] (RoPE already
+ * applied) -> out [*, q_dim] (reference op_attention forward,
+ * shaders/ops_mha.metal:31-127). impl 0 = best available, 1 = CUDA-core kernel,
+ * 2 = tensor-core kernel (fails when unsupported). */
+WELVET_API welvet_status welvet_b200_attention(const welvet_b200_mha_config* cfg, int32_t batch,
+                                               int32_t seq, const void* q, const void* k,
+                                               const void* v, void* out, int32_t impl,
+                                               void* stream);
+/* Codec kernels, bit-exact to the reference converters
+ * (src/core/float_codecs.cpp, src/weights/native_codec.cpp:189-813):
+ * roundtrip: out = decode(encode(w)) for FormatNone dtype; nf4 scale = absmax. */
+WELVET_API welvet_status welvet_b200_codec_roundtrip(int32_t dtype, const float* w, float* out,
+                                                     int64_t n, void* stream);
+WELVET_API welvet_status welvet_b200_codec_encode(int32_t dtype, const float* w, void* codes,
+                                                  float* scale_out, int64_t n, void* stream);
+WELVET_API welvet_status welvet_b200_codec_decode(int32_t dtype, const void* codes,
+                                                  const float* scale, float* out, int64_t n,
+                                                  void* stream);
+/* Extension weight formats (encode on the GPU; out_bf16 selects the decode type). */
+WELVET_API welvet_status welvet_b200_fp8_rowscale_encode(const float* w, int32_t rows,
+                                                         int32_t cols, uint8_t* codes,
+                                                         float* scales, void* stream);
+WELVET_API welvet_status welvet_b200_fp8_rowscale_decode(const uint8_t* codes,
+                                                         const float* scales, int32_t rows,
+                                                         int32_t cols, void* out,
+                                                         int32_t out_bf16, void* stream);
+WELVET_API welvet_status welvet_b200_nf4_block_encode(const float* w, int64_t n, uint8_t* packed,
+                                                      float* absmax, void* stream);
+WELVET_API welvet_status welvet_b200_nf4_block_decode(const uint8_t* packed, const float* absmax,
+                                                      int64_t n, void* out, int32_t out_bf16,
+                                                      void* stream);
+/* Deterministic synthetic data on the device: element i of counter stream `seed`
+ * (SplitMix64), kind 0 uniform(-a, a), kind 1 normal(0, a). */
+WELVET_API welvet_status welvet_b200_fill_synthetic(void* dst, int32_t is_bf16, int64_t n,
+                                                    uint64_t seed, uint64_t offset, int32_t kind,
+                                                    double a, void* stream);
+/* Reads and clears the current device's error word (synchronises the device). */
+WELVET_API welvet_status welvet_b200_device_check(void);
+/* Number of kernel launches this library issued since the last reset
+ * (benchmark accounting). No reference counterpart. */
+WELVET_API int64_t welvet_b200_launch_count(int32_t reset);
+/* Live per-kernel timing (no reference counterpart; the reference times whole calls
+ * with steady_clock, tools/dense_fwd/main.cpp:198-216). When enabled, each hot kernel
+ * of forward / decode is bracketed by CUDA events on its launch stream.
+ * welvet_b200_profile_read synchronises and returns, per kernel id, the summed
+ * milliseconds and launch counts (8 slots: 0 QKV GEMM, 1 prefill attention, 2 O GEMM,
+ * 3 decode attention, 4 decode QKV GEMM, 5 decode O GEMM, 6 all-reduce, 7 other). */
+WELVET_API void welvet_b200_profile_enable(int32_t on);
+WELVET_API void welvet_b200_profile_read(double ms[8], int64_t counts[8], int32_t reset);
+
+#ifdef __cplusplus
+}
+#endif

@@ -1,0 +1,57 @@
+#pragma once
+
+/* welvet C ABI — the multi-head-attention forward subset, served by the B200
+ * (sm_100a) CUDA backend in libwelvet_b200.so.
+ *
+ * Every declaration below has the same name, signature, argument meaning and
+ * status semantics as the reference header include/welvet_c.h of
+ * openfluke/welvet.metal; the line of the reference each one replaces is cited.
+ * The reference's other entry points (Dense/SwiGLU/norm/embedding families,
+ * model sessions, training) are not part of this library. */
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define WELVET_API __attribute__((visibility("default")))
+
+/* Reference include/welvet_c.h:22-25. code: 0 ok, 1 invalid argument,
+ * 2 unsupported, 3 gap, 4 internal (CUDA/NCCL failures map here). */
+typedef struct welvet_status {
+  int32_t code;
+  char message[256];
+} welvet_status;
+
+/* Reference include/welvet_c.h:28 (impl src/interop/c_abi.cpp:79-82). */
+WELVET_API const char* welvet_version(void);
+/* Reference include/welvet_c.h:29. Returns "cuda:<device name>:sm_<cc>:welvet-b200"
+ * (the reference returns "metal:..."). */
+WELVET_API const char* welvet_runtime_identity(void);
+/* Reference include/welvet_c.h:31 (impl c_abi.cpp:90-94): selects/initialises
+ * the compute device; the name is kept for ABI compatibility. */
+WELVET_API welvet_status welvet_metal_init(void);
+/* Reference include/welvet_c.h:32: 1 when a usable sm_100 device is present. */
+WELVET_API int32_t welvet_metal_available(void);
+
+/* Reference include/welvet_c.h:87-92 (impl src/interop/c_abi.cpp:209-247).
+ * MHA ModeSelf forward. Q [q_dim, d_model], K/V [kv_dim, d_model], O [d_model, q_dim]
+ * are FP32 initial weights, encoded to `dtype` (FormatNone) and decoded exactly as the
+ * reference does; x [batch*seq*d_model]; outputs pre [batch*seq*q_dim] (attention
+ * output) and post [batch*seq*d_model]. num_kv_heads/head_dim/max_seq_len <= 0 select
+ * the defaults; mask 0/1 causal, 2 bidirectional, 3 sliding window (window =
+ * max_seq_len), 4 prefix-LM (prefix 0), 5 custom (causal); pos 0 RoPE, 1 none,
+ * 2 ALiBi, 3 RoPE+ALiBi; backend is ignored. Batches form one stream of positions
+ * with a max_seq_len ring of keys, exactly as the reference attention kernel.
+ * All pointers are host memory owned by the caller; nothing is retained. */
+WELVET_API welvet_status welvet_mha_forward_f32(
+    int32_t batch, int32_t seq, int32_t d_model, int32_t num_heads, int32_t num_kv_heads,
+    int32_t head_dim, int32_t max_seq_len, int32_t mask, int32_t pos, int32_t dtype, int32_t backend,
+    const float* Q, const float* K, const float* V, const float* O, const float* x, float* pre,
+    float* post);
+
+#ifdef __cplusplus
+}
+#endif

@@ -1,0 +1,40 @@
+import json
+import os
+import sys
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+GOLDEN = os.path.join(ROOT, "tests", "golden")
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+sys.path.insert(0, os.path.join(ROOT, "welvet.metal_b200"))
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a B200 (sm_100) GPU")
+
+
+def golden_cases():
+    with open(os.path.join(GOLDEN, "mha_cases.json")) as f:
+        return json.load(f)
+
+
+def load_golden(name):
+    return dict(np.load(os.path.join(GOLDEN, f"mha_{name}.npz")))
+
+
+def rel_err(got, ref):
+    """max|got - ref| / max|ref| — the tolerance metric (robust near zeros)."""
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    denom = max(np.abs(ref).max(), 1e-30)
+    return float(np.abs(got - ref).max() / denom)
+
+
+@pytest.fixture(scope="session")
+def torch_cuda():
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch

@@ -1,0 +1,109 @@
+"""Generates tests/golden/*.npz from the REFERENCE ITSELF: oracle/_ref/libwelvet_ref.so
+is the reference's own src/layers/mha/mha.cpp, src/layers/dense/dense.cpp,
+src/weights/*.cpp, src/core/float_codecs.cpp and its soft-double shaders
+(shaders/welvet_dense.metal, ops_common.metal, ops_mha.metal) compiled for the CPU
+(recipe: oracle/Makefile `ref` target). Run here, where the reference sources exist:
+
+    make -C oracle ref && python tests/golden/make_golden.py
+
+Weights are regenerated at test time from the counter-based Xavier stream
+(welvet_b200.xavier_weights, seed 0 — integer arithmetic, platform independent);
+inputs x are stored, since the normal stream goes through libm.
+"""
+from __future__ import annotations
+
+import hashlib
+import json
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+sys.path.insert(0, os.path.join(ROOT, "welvet.metal_b200"))
+
+import oracle_py as O  # noqa: E402
+from welvet_b200 import synthetic, xavier_weights  # noqa: E402
+
+# name: (config kwargs, batch, seq, dtype)
+MHA_CASES = {
+    "cfg1_tiny_f32": (dict(d_model=64, num_heads=4), 1, 16, 1),
+    "gqa_stream": (dict(d_model=64, num_heads=4, num_kv_heads=2), 2, 8, 1),
+    "ring_wrap": (dict(d_model=64, num_heads=4, max_seq_len=16), 3, 8, 1),
+    "bidir_alibi": (dict(d_model=64, num_heads=4, mask=2, pos=2), 2, 8, 1),
+    "window_ropealibi_sigmoid": (dict(d_model=64, num_heads=4, mask=3, pos=3, window=3, softmax=1), 2, 8, 1),
+    "prefix_nopos_fp8": (dict(d_model=64, num_heads=4, mask=4, prefix_len=5, pos=1), 1, 16, 4),
+    "nf4": (dict(d_model=64, num_heads=4), 1, 16, 26),
+    "bf16": (dict(d_model=64, num_heads=4), 1, 16, 3),
+    "f16": (dict(d_model=64, num_heads=4), 2, 8, 2),
+    "e5m2": (dict(d_model=64, num_heads=4), 1, 12, 5),
+    "f64": (dict(d_model=64, num_heads=4), 1, 12, 0),
+    "hd64_two_seq": (dict(d_model=128, num_heads=2, max_seq_len=64), 2, 32, 1),
+    "hd128": (dict(d_model=256, num_heads=2, max_seq_len=64), 1, 24, 1),
+    "hd64_gqa_window": (dict(d_model=256, num_heads=4, num_kv_heads=2, mask=3, window=7, max_seq_len=64), 1, 40, 1),
+}
+
+
+def weights_for(cfg: O.MhaCfg):
+    c = cfg.resolved()
+    return xavier_weights(c.d_model, c.q_dim, c.kv_dim, seed=0)
+
+
+def wsum(ws) -> str:
+    h = hashlib.sha256()
+    for w in ws:
+        h.update(np.ascontiguousarray(w, np.float32).tobytes())
+    return h.hexdigest()
+
+
+def main():
+    if not O.ref_available():
+        raise SystemExit("oracle/_ref/libwelvet_ref.so missing: run `make -C oracle ref` first")
+    out = {}
+    for name, (kw, B, T, dtype) in MHA_CASES.items():
+        cfg = O.MhaCfg(**kw)
+        Wq, Wk, Wv, Wo = weights_for(cfg)
+        x = synthetic(B * T * cfg.d_model, 1, 1, 1.0).reshape(B * T, cfg.d_model)
+        code, msg, pre, post = O.ref_mha_forward(cfg, B, T, Wq, Wk, Wv, Wo, x, dtype)
+        if code:
+            raise SystemExit(f"{name}: reference returned {code} {msg}")
+        out[name] = dict(cfg=kw, batch=B, seq=T, dtype=dtype, wsum=wsum((Wq, Wk, Wv, Wo)))
+        np.savez_compressed(os.path.join(HERE, f"mha_{name}.npz"), x=x, pre=pre, post=post)
+    with open(os.path.join(HERE, "mha_cases.json"), "w") as f:
+        json.dump(out, f, indent=1, sort_keys=True)
+
+    # Codec known answers straight from the reference converters.
+    lib = O.ref_lib()
+    codes = np.arange(256, dtype=np.uint8)
+    e4m3_dec = np.array([lib.ref_fp8e4m3_decode(int(b)) for b in codes], np.float32)
+    e5m2_dec = np.array([lib.ref_fp8e5m2_decode(int(b)) for b in codes], np.float32)
+    probes = np.array([0.0, -0.0, 1.0, -1.0, 1.0625, 1.0624, 448.0, 449.0, 500.0, -500.0, 0.01, 0.001953125,
+                       0.0019, 0.015625, 0.0146, 0.5, 3.14159, -2.71828, 240.0, 1e-8, float("nan"),
+                       float("inf"), -float("inf"), 57344.0, 60000.0, 1.5e-5, 6.1e-5, 65504.0, 70000.0,
+                       1.00390625, 1.0078125, 0.33333334], np.float32)
+    rng = np.random.default_rng(7)
+    probes = np.concatenate([probes, (rng.standard_normal(2000) * np.exp(rng.uniform(-12, 8, 2000))).astype(np.float32)])
+    e4m3_enc = np.array([lib.ref_fp8e4m3_encode(float(f)) for f in probes], np.uint8)
+    e5m2_enc = np.array([lib.ref_fp8e5m2_encode(float(f)) for f in probes], np.uint8)
+    bf16_enc = np.array([lib.ref_bf16_encode(float(f)) for f in probes], np.uint16)
+    f16_enc = np.array([lib.ref_f16_encode(float(f)) for f in probes], np.uint16)
+    # FormatNone matrix round trips (WeightStore::make + export_f32) of a 32x64 matrix.
+    w = synthetic(32 * 64, 3, 1, 0.05).reshape(32, 64)
+    w[0, :8] = [0.5, -0.25, 0.1, -1.0, 0.0, 2.0, -3.0, 1e-6]
+    rt = {}
+    for dt in (0, 1, 2, 3, 4, 5, 26):
+        code, msg, native, scale, dec = O.ref_weight_roundtrip(dt, w)
+        if code:
+            raise SystemExit(f"roundtrip dtype {dt}: {code} {msg}")
+        rt[f"native_{dt}"] = native
+        rt[f"scale_{dt}"] = np.float32(scale)
+        rt[f"dec_{dt}"] = dec
+    np.savez_compressed(os.path.join(HERE, "codecs.npz"), e4m3_dec=e4m3_dec, e5m2_dec=e5m2_dec, probes=probes,
+                        e4m3_enc=e4m3_enc, e5m2_enc=e5m2_enc, bf16_enc=bf16_enc, f16_enc=f16_enc, w=w, **rt)
+    print(f"wrote {len(MHA_CASES)} MHA cases and codecs.npz to {HERE}")
+
+
+if __name__ == "__main__":
+    main()

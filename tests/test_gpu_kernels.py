@@ -1,0 +1,218 @@
+"""GPU parity tests of the individual sm_100a kernels, called through the C ABI
+(libwelvet_b200.so) on device buffers: the tcgen05 GEMMs against a float64 torch
+product of the same operands, the codec kernels bit-exactly against the
+reference's own converters (tests/golden/codecs.npz) and the oracle, and the
+attention kernels against the FP64 oracle."""
+import numpy as np
+import pytest
+
+import oracle_py as O
+import welvet_b200 as W
+from conftest import GOLDEN, rel_err
+
+pytestmark = pytest.mark.gpu
+
+
+def _dev(torch, a, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    return t.to(dtype) if dtype is not None else t
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (300, 512, 256), (1000, 768, 1024), (77, 1000, 512),
+                                   (4096, 3072, 2048)])
+def test_gemm_bf16_tcgen05(torch_cuda, M, N, K):
+    torch = torch_cuda
+    g = torch.Generator(device="cuda").manual_seed(M * 7 + N)
+    a = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+    b = torch.randn(N, K, device="cuda", generator=g).to(torch.bfloat16)
+    out = torch.empty(M, N, device="cuda", dtype=torch.float32)
+    W.gemm(0, M, N, K, a, b, out, out_bf16=0)
+    torch.cuda.synchronize()
+    W.device_check()
+    ref = a.double() @ b.double().T
+    # FP32 accumulation of exact bf16 products: ~1e-6 relative
+    assert rel_err(out.cpu().numpy(), ref.cpu().numpy()) < 1e-5
+
+
+def test_gemm_bf16_output_bf16(torch_cuda):
+    torch = torch_cuda
+    M, N, K = 512, 512, 512
+    a = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+    b = torch.randn(N, K, device="cuda").to(torch.bfloat16)
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    W.gemm(0, M, N, K, a, b, out, out_bf16=1)
+    torch.cuda.synchronize()
+    ref = (a.double() @ b.double().T)
+    assert rel_err(out.float().cpu().numpy(), ref.cpu().numpy()) < 8e-3
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 128, 32), (333, 384, 1024), (2048, 1024, 1024)])
+def test_gemm_tf32x3_is_fp32_accurate(torch_cuda, M, N, K):
+    torch = torch_cuda
+    a = torch.randn(M, K, device="cuda", dtype=torch.float32)
+    b = torch.randn(N, K, device="cuda", dtype=torch.float32)
+    ah, al, bh, bl = (torch.empty_like(t) for t in (a, a, b, b))
+    W.split_tf32(a, ah, al)
+    W.split_tf32(b, bh, bl)
+    torch.cuda.synchronize()
+    assert torch.equal(ah + al, a) and torch.equal(bh + bl, b)
+    out = torch.empty(M, N, device="cuda", dtype=torch.float32)
+    W.gemm(1, M, N, K, ah, bh, out, a_lo=al, b_lo=bl)
+    torch.cuda.synchronize()
+    W.device_check()
+    ref = a.double() @ b.double().T
+    # the FP32 path's budget is 1e-4; 3xTF32 lands near FP32 rounding
+    assert rel_err(out.cpu().numpy(), ref.cpu().numpy()) < 2e-6
+
+
+def test_gemm_fp8_rowscale_weights(torch_cuda):
+    torch = torch_cuda
+    M, N, K = 700, 512, 1024
+    w = W.synthetic(N * K, 11, 1, 0.02).reshape(N, K)
+    codes, scales, dec = O.fp8_rowscale(w)
+    x = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+    out = torch.empty(M, N, device="cuda", dtype=torch.float32)
+    W.gemm(2, M, N, K, x, _dev(torch, codes), out, b_scale=_dev(torch, scales))
+    torch.cuda.synchronize()
+    W.device_check()
+    ref = x.double() @ _dev(torch, dec).double().T
+    assert rel_err(out.cpu().numpy(), ref.cpu().numpy()) < 1e-5
+
+
+def test_gemm_nf4_block_weights(torch_cuda):
+    torch = torch_cuda
+    M, N, K = 513, 768, 512
+    w = W.synthetic(N * K, 12, 1, 0.02).reshape(N, K)
+    packed, amax, dec = O.nf4_block(w, 64)
+    x = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+    out = torch.empty(M, N, device="cuda", dtype=torch.float32)
+    W.gemm(3, M, N, K, x, _dev(torch, packed.reshape(N, K // 2)), out, b_scale=_dev(torch, amax))
+    torch.cuda.synchronize()
+    W.device_check()
+    ref = x.double() @ _dev(torch, dec).double().T
+    # weights are dequantised to bf16 in shared memory (2^-9 relative per weight)
+    assert rel_err(out.cpu().numpy(), ref.cpu().numpy()) < 4e-3
+
+
+# ------------------------------------------------------------------- codecs
+def test_codec_roundtrip_bitexact_against_reference(torch_cuda):
+    torch = torch_cuda
+    g = dict(np.load(f"{GOLDEN}/codecs.npz"))
+    w = _dev(torch, g["w"].ravel())
+    for dt in (0, 1, 2, 3, 4, 5, 26):
+        out = torch.empty_like(w)
+        W.codec_roundtrip(dt, w, out)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(out.cpu().numpy().view(np.uint32), g[f"dec_{dt}"].ravel().view(np.uint32),
+                                      err_msg=f"dtype {dt}")
+
+
+def test_codec_encode_bytes_match_reference(torch_cuda):
+    torch = torch_cuda
+    g = dict(np.load(f"{GOLDEN}/codecs.npz"))
+    w = _dev(torch, g["w"].ravel())
+    n = w.numel()
+    for dt, nbytes in ((0, 8 * n), (2, 2 * n), (3, 2 * n), (4, n), (5, n), (26, n // 2)):
+        codes = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+        scale = torch.zeros(1, dtype=torch.float32, device="cuda")
+        W.codec_encode(dt, w, codes, scale)
+        dec = torch.empty_like(w)
+        W.codec_decode(dt, codes, dec, scale)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(codes.cpu().numpy(), g[f"native_{dt}"], err_msg=f"dtype {dt}")
+        np.testing.assert_array_equal(dec.cpu().numpy().view(np.uint32), g[f"dec_{dt}"].ravel().view(np.uint32))
+        if dt == 26:
+            assert scale.item() == g["scale_26"]
+
+
+def test_codec_probe_values(torch_cuda):
+    torch = torch_cuda
+    g = dict(np.load(f"{GOLDEN}/codecs.npz"))
+    p = _dev(torch, g["probes"])
+    for dt, key, view in ((4, "e4m3_enc", np.uint8), (5, "e5m2_enc", np.uint8), (3, "bf16_enc", np.uint16),
+                          (2, "f16_enc", np.uint16)):
+        codes = torch.zeros(p.numel() * np.dtype(view).itemsize, dtype=torch.uint8, device="cuda")
+        W.codec_encode(dt, p, codes)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(codes.cpu().numpy().view(view), g[key], err_msg=key)
+    all_codes = torch.arange(256, dtype=torch.int32, device="cuda").to(torch.uint8)
+    for dt, key in ((4, "e4m3_dec"), (5, "e5m2_dec")):
+        out = torch.empty(256, dtype=torch.float32, device="cuda")
+        W.codec_decode(dt, all_codes, out)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(out.cpu().numpy().view(np.uint32), g[key].view(np.uint32))
+
+
+def test_extension_formats_bitexact_against_oracle(torch_cuda):
+    torch = torch_cuda
+    rows, cols = 96, 320
+    w = W.synthetic(rows * cols, 13, 1, 0.02).reshape(rows, cols)
+    w[3, :] = 0.0  # all-zero row -> scale 1
+    codes_o, scales_o, dec_o = O.fp8_rowscale(w)
+    wd = _dev(torch, w)
+    codes = torch.empty(rows, cols, dtype=torch.uint8, device="cuda")
+    scales = torch.empty(rows, dtype=torch.float32, device="cuda")
+    W.fp8_rowscale_encode(wd, codes, scales)
+    dec = torch.empty(rows, cols, dtype=torch.float32, device="cuda")
+    W.fp8_rowscale_decode(codes, scales, dec)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(codes.cpu().numpy(), codes_o)
+    np.testing.assert_array_equal(scales.cpu().numpy(), scales_o)
+    np.testing.assert_array_equal(dec.cpu().numpy(), dec_o)
+    packed_o, amax_o, ndec_o = O.nf4_block(w, 64)
+    packed = torch.empty(w.size // 2, dtype=torch.uint8, device="cuda")
+    amax = torch.empty(w.size // 64, dtype=torch.float32, device="cuda")
+    W.nf4_block_encode(wd, packed, amax)
+    ndec = torch.empty(w.size, dtype=torch.float32, device="cuda")
+    W.nf4_block_decode(packed, amax, ndec)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(packed.cpu().numpy(), packed_o)
+    np.testing.assert_array_equal(amax.cpu().numpy(), amax_o)
+    np.testing.assert_array_equal(ndec.cpu().numpy().reshape(rows, cols), ndec_o)
+
+
+# ---------------------------------------------------------------- attention
+ATTN_CASES = [
+    # (cfg kwargs, batch, seq)
+    (dict(d_model=64, num_heads=4, seq_mode=1), 2, 40),
+    (dict(d_model=256, num_heads=4, num_kv_heads=2, seq_mode=1), 2, 130),
+    (dict(d_model=256, num_heads=2, seq_mode=1), 1, 257),                  # hd 128
+    (dict(d_model=64, num_heads=4, seq_mode=0, max_seq_len=64), 3, 16),   # stream
+    (dict(d_model=64, num_heads=4, seq_mode=0, max_seq_len=20), 3, 16),   # stream, ring wrap
+    (dict(d_model=64, num_heads=4, seq_mode=1, mask=2, pos=2), 2, 33),
+    (dict(d_model=64, num_heads=4, seq_mode=1, mask=3, window=5, softmax=1), 1, 50),
+    (dict(d_model=64, num_heads=4, seq_mode=1, mask=3, window=6, window_causal=0), 1, 50),
+    (dict(d_model=64, num_heads=4, seq_mode=0, mask=4, prefix_len=9, max_seq_len=64), 2, 20),
+    (dict(d_model=48, num_heads=4, seq_mode=1), 2, 19),                   # hd 12
+]
+
+
+@pytest.mark.parametrize("kw,B,T", ATTN_CASES)
+@pytest.mark.parametrize("precision", [0, 1])
+def test_attention_against_oracle(torch_cuda, kw, B, T, precision):
+    torch = torch_cuda
+    kw = dict(kw)
+    cfg = W.MhaConfig.make(kw.pop("d_model"), kw.pop("num_heads"), kw.pop("num_kv_heads", 0), precision=precision,
+                           **kw)
+    hd, nk = cfg.resolved()
+    qd, kd = cfg.num_heads * hd, nk * hd
+    M = B * T
+    q = W.synthetic(M * qd, 21, 1, 1.0).reshape(M, qd)
+    k = W.synthetic(M * kd, 22, 1, 1.0).reshape(M, kd)
+    v = W.synthetic(M * kd, 23, 1, 1.0).reshape(M, kd)
+    if precision == 1:  # the oracle sees the same bf16-rounded inputs
+        q, k, v = (torch.from_numpy(a).to(torch.bfloat16).float().numpy() for a in (q, k, v))
+    oc = O.MhaCfg(d_model=cfg.d_model, num_heads=cfg.num_heads, num_kv_heads=nk, head_dim=hd,
+                  max_seq_len=cfg.max_seq_len, mask=cfg.mask, pos=1 if cfg.pos == 0 else cfg.pos,
+                  softmax=cfg.softmax, window=cfg.window, prefix_len=cfg.prefix_len,
+                  window_causal=cfg.window_causal, per_sequence=cfg.seq_mode)
+    # the kernel receives rotated q/k; compare with RoPE off on both sides
+    cfg.pos = oc.pos
+    ref = O.attention(oc, B, T, q, k, v)
+    dt = torch.float32 if precision == 0 else torch.bfloat16
+    out = torch.zeros(M, qd, device="cuda", dtype=dt)
+    W.attention(cfg, B, T, _dev(torch, q, dt), _dev(torch, k, dt), _dev(torch, v, dt), out)
+    torch.cuda.synchronize()
+    W.device_check()
+    tol = 1e-4 if precision == 0 else 2e-2
+    assert rel_err(out.float().cpu().numpy(), ref) < tol

@@ -1,0 +1,340 @@
+// Weight codecs, TF32 splitting, RoPE tables and synthetic-data generation.
+// These kernels are HBM-bound elementwise passes: grid-stride loops sized to a
+// multiple of the SM count, 16-byte accesses where the layout allows.
+#include "codec.cuh"
+#include "common.cuh"
+#include "kernels.h"
+
+namespace wv {
+namespace {
+
+inline int grid_for(int64_t n, int per_thread = 1) {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t blocks = (n / per_thread + 255) / 256;
+  return (int)std::max<int64_t>(1, std::min<int64_t>(blocks, (int64_t)sms * 8));
+}
+
+#define GRID_STRIDE(i, n) \
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < (n); i += (int64_t)gridDim.x * blockDim.x)
+
+__device__ __forceinline__ float roundtrip(int dtype, float w, float nf4s) {
+  switch (dtype) {
+  case 0: return (float)(double)w;  // Float64 holds double(w) exactly
+  case 1: return w;
+  case 2: return f16_decode(f16_encode(w));
+  case 3: return bf16_decode(bf16_encode_trunc(w));
+  case 4: return e4m3_decode(e4m3_encode(w));
+  case 5: return e5m2_decode(e5m2_encode(w));
+  case 26: return nf4_level(nf4_nearest(__fdiv_rn(w, nf4s))) * nf4s;
+  default: return 0.f;
+  }
+}
+
+__global__ void roundtrip_kernel(int dtype, const float* w, float* out, int64_t n, const float* nf4_scale) {
+  float s = 1.f;
+  if (dtype == 26) {
+    s = *nf4_scale;
+    if (s == 0.f) s = 1.f;
+  }
+  GRID_STRIDE(i, n) out[i] = roundtrip(dtype, w[i], s);
+}
+
+__global__ void encode_kernel(int dtype, const float* w, void* codes, int64_t n, const float* nf4_scale) {
+  if (dtype == 26) {
+    float s = *nf4_scale;
+    if (s == 0.f) s = 1.f;
+    uint8_t* out = static_cast<uint8_t*>(codes);
+    GRID_STRIDE(j, (n + 1) / 2) {
+      const int64_t i = 2 * j;
+      const int lo = nf4_nearest(__fdiv_rn(w[i], s));
+      const int hi = (i + 1 < n) ? nf4_nearest(__fdiv_rn(w[i + 1], s)) : 0;
+      out[j] = (uint8_t)(lo | (hi << 4));
+    }
+    return;
+  }
+  GRID_STRIDE(i, n) {
+    switch (dtype) {
+    case 0: static_cast<double*>(codes)[i] = (double)w[i]; break;
+    case 1: static_cast<float*>(codes)[i] = w[i]; break;
+    case 2: static_cast<uint16_t*>(codes)[i] = f16_encode(w[i]); break;
+    case 3: static_cast<uint16_t*>(codes)[i] = bf16_encode_trunc(w[i]); break;
+    case 4: static_cast<uint8_t*>(codes)[i] = e4m3_encode(w[i]); break;
+    case 5: static_cast<uint8_t*>(codes)[i] = e5m2_encode(w[i]); break;
+    default: break;
+    }
+  }
+}
+
+__global__ void decode_kernel(int dtype, const void* codes, float* out, int64_t n, const float* nf4_scale) {
+  float s = 1.f;
+  if (dtype == 26) {
+    s = *nf4_scale;
+    if (s == 0.f) s = 1.f;
+  }
+  GRID_STRIDE(i, n) {
+    float v = 0.f;
+    switch (dtype) {
+    case 0: v = (float)static_cast<const double*>(codes)[i]; break;
+    case 1: v = static_cast<const float*>(codes)[i]; break;
+    case 2: v = f16_decode(static_cast<const uint16_t*>(codes)[i]); break;
+    case 3: v = bf16_decode(static_cast<const uint16_t*>(codes)[i]); break;
+    case 4: v = e4m3_decode(static_cast<const uint8_t*>(codes)[i]); break;
+    case 5: v = e5m2_decode(static_cast<const uint8_t*>(codes)[i]); break;
+    case 26: {
+      const uint8_t b = static_cast<const uint8_t*>(codes)[i / 2];
+      v = nf4_level((i & 1) ? (b >> 4) : (b & 0xf)) * s;
+      break;
+    }
+    default: break;
+    }
+    out[i] = v;
+  }
+}
+
+// max |w| — per-block partial maxima, then one block folds them.
+__global__ void absmax_partial(const float* w, int64_t n, float* partial) {
+  float m = 0.f;
+  GRID_STRIDE(i, n) m = fmaxf(m, fabsf(w[i]));
+  __shared__ float red[32];
+  for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    m = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (threadIdx.x == 0) partial[blockIdx.x] = m;
+  }
+}
+
+// One warp per row: absmax/448 (1 when 0), then E4M3 codes of w/scale.
+__global__ void fp8_rowscale_encode_kernel(const float* w, int rows, int cols, uint8_t* codes, float* scales) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const float* r = w + (size_t)warp * cols;
+  float m = 0.f;
+  for (int c = lane; c < cols; c += 32) m = fmaxf(m, fabsf(r[c]));
+  for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  float s = __fdiv_rn(m, 448.0f);
+  if (s == 0.f) s = 1.f;
+  if (lane == 0) scales[warp] = s;
+  for (int c = lane; c < cols; c += 32) codes[(size_t)warp * cols + c] = e4m3_encode(__fdiv_rn(r[c], s));
+}
+
+__global__ void fp8_rowscale_decode_kernel(const uint8_t* codes, const float* scales, int rows, int cols,
+                                           void* out, int out_bf16) {
+  GRID_STRIDE(i, (int64_t)rows * cols) {
+    const float v = __fmul_rn(e4m3_decode(codes[i]), scales[i / cols]);
+    if (out_bf16)
+      static_cast<__nv_bfloat16*>(out)[i] = __float2bfloat16_rn(v);
+    else
+      static_cast<float*>(out)[i] = v;
+  }
+}
+
+// One warp per block of 64 elements (two per lane).
+__global__ void nf4_block_encode_kernel(const float* w, int64_t n, uint8_t* packed, float* absmax) {
+  const int64_t blk = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (blk * 64 >= n) return;
+  const int64_t i0 = blk * 64 + 2 * lane;
+  const float a = i0 < n ? w[i0] : 0.f, b = i0 + 1 < n ? w[i0 + 1] : 0.f;
+  float m = fmaxf(fabsf(a), fabsf(b));
+  for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (m == 0.f) m = 1.f;
+  if (lane == 0) absmax[blk] = m;
+  if (i0 < n) {
+    const int lo = nf4_nearest(__fdiv_rn(a, m));
+    const int hi = i0 + 1 < n ? nf4_nearest(__fdiv_rn(b, m)) : 0;
+    packed[i0 / 2] = (uint8_t)(lo | (hi << 4));
+  }
+}
+
+__global__ void nf4_block_decode_kernel(const uint8_t* packed, const float* absmax, int64_t n, void* out,
+                                        int out_bf16) {
+  GRID_STRIDE(i, n) {
+    const uint8_t b = packed[i / 2];
+    const float v = __fmul_rn(nf4_level((i & 1) ? (b >> 4) : (b & 0xf)), absmax[i / 64]);
+    if (out_bf16)
+      static_cast<__nv_bfloat16*>(out)[i] = __float2bfloat16_rn(v);
+    else
+      static_cast<float*>(out)[i] = v;
+  }
+}
+
+__global__ void fp8_lut_kernel(uint16_t* lut) {
+  const int i = threadIdx.x;
+  if (i < 256) {
+    // Every E4M3 value the reference decoder returns is exact in BF16.
+    lut[i] = (uint16_t)(__float_as_uint(e4m3_decode((uint8_t)i)) >> 16);
+  }
+}
+
+__global__ void split_tf32_kernel(const float* x, float* hi, float* lo, int64_t n) {
+  GRID_STRIDE(i, n) {
+    const float v = x[i];
+    const float h = to_tf32(v);
+    hi[i] = h;
+    lo[i] = v - h;
+  }
+}
+
+__global__ void cast_f32_bf16_kernel(const float* x, __nv_bfloat16* y, int64_t n) {
+  GRID_STRIDE(i, n) y[i] = __float2bfloat16_rn(x[i]);
+}
+__global__ void cast_bf16_f32_kernel(const __nv_bfloat16* x, float* y, int64_t n) {
+  GRID_STRIDE(i, n) y[i] = __bfloat162float(x[i]);
+}
+
+// rope_gpu (shaders/ops_mha.metal:13-30): power = theta^(fl32(2i/hd)),
+// angle = pos / power, evaluated in double and rounded once to float.
+__global__ void rope_table_kernel(float2* tab, int max_pos, int hd, double theta) {
+  const int half = hd / 2;
+  const double ltheta = log(theta);
+  GRID_STRIDE(idx, (int64_t)max_pos * half) {
+    const int pos = (int)(idx / half), i = (int)(idx % half);
+    const float e = __fdiv_rn((float)(2 * i), (float)hd);
+    const double power = exp(ltheta * (double)e);
+    const double angle = (double)pos / power;
+    double s, c;
+    sincos(angle, &s, &c);
+    tab[idx] = make_float2((float)c, (float)s);
+  }
+}
+
+__global__ void rope_apply_kernel(void* x, int is_bf16, int64_t M, int ld, int cols, int hd,
+                                  const float2* tab, int max_pos, const int* positions, int pos_mod) {
+  const int half = hd / 2;
+  const int pairs_per_row = (cols / hd) * half;
+  GRID_STRIDE(idx, M * pairs_per_row) {
+    const int64_t row = idx / pairs_per_row;
+    const int r = (int)(idx % pairs_per_row);
+    const int head = r / half, i = r % half;
+    int pos = positions ? positions[row] : (pos_mod > 0 ? (int)(row % pos_mod) : (int)row);
+    if (pos < 0 || pos >= max_pos) continue;
+    const float2 cs = tab[(size_t)pos * half + i];
+    const size_t ia = (size_t)row * ld + (size_t)head * hd + i, ib = ia + half;
+    if (is_bf16) {
+      __nv_bfloat16* p = static_cast<__nv_bfloat16*>(x);
+      const float a = __bfloat162float(p[ia]), b = __bfloat162float(p[ib]);
+      p[ia] = __float2bfloat16_rn(a * cs.x - b * cs.y);
+      p[ib] = __float2bfloat16_rn(a * cs.y + b * cs.x);
+    } else {
+      float* p = static_cast<float*>(x);
+      const float a = p[ia], b = p[ib];
+      p[ia] = a * cs.x - b * cs.y;
+      p[ib] = a * cs.y + b * cs.x;
+    }
+  }
+}
+
+// SplitMix64 finaliser on (seed * golden + index): a counter-based stream, so
+// element i is the same wherever and in whatever order it is generated.
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+__device__ __forceinline__ double unif01(uint64_t seed, uint64_t i) {
+  return (double)(mix64(seed * 0xD1B54A32D192ED03ull + i) >> 11) * 0x1.0p-53;
+}
+
+__global__ void fill_kernel(void* dst, int is_bf16, int64_t n, uint64_t seed, uint64_t offset, int kind,
+                            double a) {
+  GRID_STRIDE(i, n) {
+    const uint64_t gi = offset + (uint64_t)i;
+    double v;
+    if (kind == 0) {
+      v = a * (2.0 * unif01(seed, gi) - 1.0);
+    } else {
+      const double u1 = unif01(seed, 2 * gi), u2 = unif01(seed, 2 * gi + 1);
+      v = a * sqrt(-2.0 * log(1.0 - u1)) * cos(6.283185307179586 * u2);
+    }
+    if (is_bf16)
+      static_cast<__nv_bfloat16*>(dst)[i] = __float2bfloat16_rn((float)v);
+    else
+      static_cast<float*>(dst)[i] = (float)v;
+  }
+}
+
+} // namespace
+
+cudaError_t codec_roundtrip_f32(int dtype, const float* w, float* out, int64_t n, const float* nf4_scale,
+                                cudaStream_t s) {
+  roundtrip_kernel<<<grid_for(n), 256, 0, s>>>(dtype, w, out, n, nf4_scale);
+  return cudaGetLastError();
+}
+cudaError_t codec_encode(int dtype, const float* w, void* codes, int64_t n, const float* nf4_scale,
+                         cudaStream_t s) {
+  encode_kernel<<<grid_for(n), 256, 0, s>>>(dtype, w, codes, n, nf4_scale);
+  return cudaGetLastError();
+}
+cudaError_t codec_decode(int dtype, const void* codes, float* out, int64_t n, const float* nf4_scale,
+                         cudaStream_t s) {
+  decode_kernel<<<grid_for(n), 256, 0, s>>>(dtype, codes, out, n, nf4_scale);
+  return cudaGetLastError();
+}
+cudaError_t absmax_f32(const float* w, int64_t n, float* out, float* scratch, cudaStream_t s) {
+  const int g = std::min(grid_for(n), 1024);
+  absmax_partial<<<g, 256, 0, s>>>(w, n, scratch);
+  absmax_partial<<<1, 1024, 0, s>>>(scratch, g, out);
+  return cudaGetLastError();
+}
+cudaError_t fp8_rowscale_encode(const float* w, int rows, int cols, uint8_t* codes, float* scales,
+                                cudaStream_t s) {
+  fp8_rowscale_encode_kernel<<<(rows + 7) / 8, 256, 0, s>>>(w, rows, cols, codes, scales);
+  return cudaGetLastError();
+}
+cudaError_t fp8_rowscale_decode(const uint8_t* codes, const float* scales, int rows, int cols, void* out,
+                                int out_bf16, cudaStream_t s) {
+  fp8_rowscale_decode_kernel<<<grid_for((int64_t)rows * cols), 256, 0, s>>>(codes, scales, rows, cols, out,
+                                                                             out_bf16);
+  return cudaGetLastError();
+}
+cudaError_t nf4_block_encode(const float* w, int64_t n, uint8_t* packed, float* absmax, cudaStream_t s) {
+  const int64_t blocks = (n + 63) / 64;
+  nf4_block_encode_kernel<<<(int)((blocks + 7) / 8), 256, 0, s>>>(w, n, packed, absmax);
+  return cudaGetLastError();
+}
+cudaError_t nf4_block_decode(const uint8_t* packed, const float* absmax, int64_t n, void* out, int out_bf16,
+                             cudaStream_t s) {
+  nf4_block_decode_kernel<<<grid_for(n), 256, 0, s>>>(packed, absmax, n, out, out_bf16);
+  return cudaGetLastError();
+}
+cudaError_t fp8_lut_init(uint16_t* lut, cudaStream_t s) {
+  fp8_lut_kernel<<<1, 256, 0, s>>>(lut);
+  return cudaGetLastError();
+}
+cudaError_t split_tf32(const float* x, float* hi, float* lo, int64_t n, cudaStream_t s) {
+  split_tf32_kernel<<<grid_for(n), 256, 0, s>>>(x, hi, lo, n);
+  return cudaGetLastError();
+}
+cudaError_t cast_f32_bf16(const float* x, void* y, int64_t n, cudaStream_t s) {
+  cast_f32_bf16_kernel<<<grid_for(n), 256, 0, s>>>(x, static_cast<__nv_bfloat16*>(y), n);
+  return cudaGetLastError();
+}
+cudaError_t cast_bf16_f32(const void* x, float* y, int64_t n, cudaStream_t s) {
+  cast_bf16_f32_kernel<<<grid_for(n), 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), y, n);
+  return cudaGetLastError();
+}
+cudaError_t rope_table(float2* tab, int max_pos, int head_dim, double theta, cudaStream_t s) {
+  if (head_dim < 2) return cudaSuccess;
+  rope_table_kernel<<<grid_for((int64_t)max_pos * (head_dim / 2)), 256, 0, s>>>(tab, max_pos, head_dim, theta);
+  return cudaGetLastError();
+}
+cudaError_t rope_apply(void* x, int is_bf16, int64_t M, int ld, int cols, int head_dim, const float2* tab,
+                       int max_pos, const int* positions, int pos_mod, cudaStream_t s) {
+  if (head_dim < 2 || cols <= 0) return cudaSuccess;
+  rope_apply_kernel<<<grid_for(M * (cols / head_dim) * (head_dim / 2)), 256, 0, s>>>(
+      x, is_bf16, M, ld, cols, head_dim, tab, max_pos, positions, pos_mod);
+  return cudaGetLastError();
+}
+cudaError_t fill_synthetic(void* dst, int is_bf16, int64_t n, uint64_t seed, uint64_t offset, int kind,
+                           double a, cudaStream_t s) {
+  fill_kernel<<<grid_for(n), 256, 0, s>>>(dst, is_bf16, n, seed, offset, kind, a);
+  return cudaGetLastError();
+}
+
+} // namespace wv

@@ -1,0 +1,555 @@
+// Projection GEMMs of the MHA forward (the Q/K/V and O Dense layers,
+// src/layers/mha/mha.cpp:168-198, whose reference kernel is the one-thread-per-
+// output soft-double GEMV shaders/welvet_dense.metal:54-85) as a persistent,
+// warp-specialised tcgen05 GEMM for sm_100a:
+//   warp 0      TMA producer (one elected thread) filling a ring of smem stages
+//   warp 1      UMMA issuer (one thread); owns the TMEM allocation
+//   warps 2-5   epilogue: TMEM -> registers -> (RoPE) -> global, one row per thread
+//   warps 6-9   (FP8/NF4 only) dequantise B codes into a BF16 smem tile per stage
+// Accumulators are double-buffered in TMEM so the epilogue of tile i overlaps the
+// mainloop of tile i+1. Tiles: 128 x BN, K-blocks of 128 bytes per operand row
+// (128-byte swizzle, the canonical K-major UMMA layout).
+#include "codec.cuh"
+#include "common.cuh"
+#include "kernels.h"
+
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+
+namespace wv {
+namespace {
+
+constexpr int kBM = 128;
+
+template <int KIND> struct GT;
+template <> struct GT<kGemmBF16> {
+  static constexpr int BN = 256, BK = 64, STAGES = 4, UK = 16, NA = 1, NB = 1, ELEM = 2;
+  static constexpr uint32_t FMT = 1;
+  static constexpr int CODE_BYTES = 0;  // B arrives ready for UMMA
+  static constexpr int THREADS = 192;
+};
+template <> struct GT<kGemmTF32x3> {
+  static constexpr int BN = 128, BK = 32, STAGES = 3, UK = 8, NA = 2, NB = 2, ELEM = 4;
+  static constexpr uint32_t FMT = 2;
+  static constexpr int CODE_BYTES = 0;
+  static constexpr int THREADS = 192;
+};
+// FP8 / NF4 weights: TMA brings the codes (BN x 64 codes) into a staging buffer,
+// warps 6-9 write the BF16 tile that UMMA reads.
+template <> struct GT<kGemmFP8> {
+  static constexpr int BN = 256, BK = 64, STAGES = 3, UK = 16, NA = 1, NB = 1, ELEM = 2;
+  static constexpr uint32_t FMT = 1;
+  static constexpr int CODE_BYTES = 256 * 64;  // one byte per code
+  static constexpr int THREADS = 320;
+};
+template <> struct GT<kGemmNF4> {
+  static constexpr int BN = 256, BK = 64, STAGES = 3, UK = 16, NA = 1, NB = 1, ELEM = 2;
+  static constexpr uint32_t FMT = 1;
+  static constexpr int CODE_BYTES = 256 * 32;  // two codes per byte
+  static constexpr int THREADS = 320;
+};
+
+struct KParams {
+  int M, N, K, m_tiles, n_tiles, num_tiles, k_blocks;
+  void* out;
+  int ldo, out_bf16;
+  float* out_hi;
+  float* out_lo;
+  const float* b_scale;
+  int ldb;
+  const uint16_t* b_lut;
+  const float2* rope_tab;
+  int rope_cols, head_dim, rope_max_pos;
+  const int* positions;
+  int pos_mod;
+  void* kv_k;
+  void* kv_v;
+  const int* kv_slot;
+  int kv_col0, kv_dim;
+  uint32_t* err;
+};
+
+// Grouped rasterisation: 8 M-tiles advance together across N so the A rows and
+// B columns a wave of CTAs touches stay L2-resident.
+__device__ __forceinline__ void tile_coords(int t, const KParams& p, int& mb, int& nb) {
+  constexpr int GM = 8;
+  const int group = GM * p.n_tiles;
+  const int g = t / group, r = t % group;
+  const int first = g * GM;
+  const int gm = min(GM, p.m_tiles - first);
+  mb = first + r % gm;
+  nb = r / gm;
+}
+
+__device__ __forceinline__ void store_vals(const KParams& p, int row, int col, const float* v,
+                                           int nvalid) {
+  // Decode: K/V columns are scattered into the KV page pools.
+  if (p.kv_k && col >= p.kv_col0) {
+    int rel = col - p.kv_col0;
+    const bool is_v = rel >= p.kv_dim;
+    if (is_v) rel -= p.kv_dim;
+    const int slot = p.kv_slot[row];
+    if (slot < 0) return;
+    char* base = static_cast<char*>(is_v ? p.kv_v : p.kv_k);
+    // pool layout [page][kv_head][kPageTokens][head_dim]; a 32-column chunk stays
+    // inside one head (head_dim is a multiple of 32 on this path)
+    const int hd = p.head_dim, nk = p.kv_dim / hd;
+    const size_t off = (((size_t)(slot / kPageTokens) * nk + rel / hd) * kPageTokens +
+                        slot % kPageTokens) * hd + rel % hd;
+    if (p.out_bf16) {
+      __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(base) + off;
+      for (int e = 0; e < nvalid; ++e) d[e] = __float2bfloat16_rn(v[e]);
+    } else {
+      float* d = reinterpret_cast<float*>(base) + off;
+      for (int e = 0; e < nvalid; ++e) d[e] = v[e];
+    }
+    return;
+  }
+  const size_t off = (size_t)row * p.ldo + col;
+  if (p.out_bf16) {
+    __nv_bfloat16* d = static_cast<__nv_bfloat16*>(p.out) + off;
+    if (nvalid == 32 && (off % 8) == 0) {
+#pragma unroll
+      for (int e = 0; e < 32; e += 8)
+        st_global_v4(d + e, pack_bf16x2(v[e], v[e + 1]), pack_bf16x2(v[e + 2], v[e + 3]),
+                     pack_bf16x2(v[e + 4], v[e + 5]), pack_bf16x2(v[e + 6], v[e + 7]));
+    } else {
+      for (int e = 0; e < nvalid; ++e) d[e] = __float2bfloat16_rn(v[e]);
+    }
+    return;
+  }
+  float* d = static_cast<float*>(p.out) + off;
+  if (nvalid == 32 && (off % 4) == 0) {
+#pragma unroll
+    for (int e = 0; e < 32; e += 4)
+      st_global_v4(d + e, __float_as_uint(v[e]), __float_as_uint(v[e + 1]),
+                   __float_as_uint(v[e + 2]), __float_as_uint(v[e + 3]));
+  } else {
+    for (int e = 0; e < nvalid; ++e) d[e] = v[e];
+  }
+  if (p.out_hi) {
+    float* h = p.out_hi + off;
+    float* l = p.out_lo + off;
+    for (int e = 0; e < nvalid; ++e) {
+      const float hv = to_tf32(v[e]);
+      h[e] = hv;
+      l[e] = v[e] - hv;
+    }
+  }
+}
+
+template <int BN>
+__device__ __forceinline__ void epilogue_tile(const KParams& p, uint32_t tbase, int row, int n0) {
+  const bool row_ok = row < p.M;
+  const int hd = p.head_dim;
+  const bool fuse_rope = p.rope_cols > 0 && (hd == 64 || hd == 128 || hd == 256) && (BN % hd) == 0;
+  int pos = 0;
+  bool pos_ok = true;
+  if (fuse_rope && row_ok) {
+    pos = p.positions ? p.positions[row] : (p.pos_mod > 0 ? row % p.pos_mod : row);
+    pos_ok = pos >= 0 && pos < p.rope_max_pos;
+    if (!pos_ok) atomicCAS(p.err, 0u, 0x100u);
+  }
+  int c = 0;
+  while (c < BN) {
+    const int gcol = n0 + c;
+    if (gcol >= p.N) break;
+    if (fuse_rope && gcol < p.rope_cols) {
+      const int half = hd >> 1;
+      for (int j = 0; j < half; j += 32) {
+        uint32_t x[32], y[32];
+        tmem_ld32(tbase + c + j, x);
+        tmem_ld32(tbase + c + half + j, y);
+        tmem_ld_wait();
+        if (row_ok) {
+          float xo[32], yo[32];
+          const float2* tab = p.rope_tab + (size_t)(pos_ok ? pos : 0) * half + j;
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            float a = __uint_as_float(x[e]), b = __uint_as_float(y[e]);
+            if (p.b_scale && p.b_lut) {  // FP8 per-channel scale precedes the rotation
+              a *= p.b_scale[gcol + j + e];
+              b *= p.b_scale[gcol + half + j + e];
+            }
+            const float2 cs = pos_ok ? tab[e] : make_float2(1.f, 0.f);
+            xo[e] = a * cs.x - b * cs.y;
+            yo[e] = a * cs.y + b * cs.x;
+          }
+          store_vals(p, row, gcol + j, xo, 32);
+          store_vals(p, row, gcol + half + j, yo, 32);
+        }
+      }
+      c += hd;
+    } else {
+      uint32_t x[32];
+      tmem_ld32(tbase + c, x);
+      tmem_ld_wait();
+      if (row_ok) {
+        float v[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(x[e]);
+        if (p.b_scale && p.b_lut) {  // FP8: per-output-channel scale factors out of the K sum
+          for (int e = 0; e < 32 && gcol + e < p.N; ++e) v[e] *= p.b_scale[gcol + e];
+        }
+        store_vals(p, row, gcol, v, min(32, p.N - gcol));
+      }
+      c += 32;
+    }
+  }
+}
+
+// 16 bytes of a 128-byte-swizzled K-major row: chunk index XOR (row mod 8).
+__device__ __forceinline__ uint32_t sw128_offset(int row, int chunk16) {
+  return (uint32_t)(row * 128 + ((chunk16 ^ (row & 7)) << 4));
+}
+
+template <int KIND>
+__global__ void __launch_bounds__(GT<KIND>::THREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA2,
+                   const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmB2,
+                   const KParams p) {
+  using T = GT<KIND>;
+  constexpr int BN = T::BN, BK = T::BK, S = T::STAGES;
+  constexpr int A_BYTES = kBM * BK * T::ELEM;
+  constexpr int B_BYTES = BN * BK * T::ELEM;
+  constexpr bool XFORM = T::CODE_BYTES > 0;
+  constexpr int STAGE_BYTES = T::NA * A_BYTES + T::NB * B_BYTES + T::CODE_BYTES;
+  constexpr uint32_t IDESC = idesc_make(T::FMT, kBM, BN, 0, 0);
+  constexpr uint32_t TMEM_COLS = 2 * BN;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * STAGE_BYTES);
+  uint64_t* empty = full + S;
+  uint64_t* xfull = empty + S;  // dequantised B ready (FP8/NF4)
+  uint64_t* accf = xfull + S;
+  uint64_t* acce = accf + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(acce + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  uint16_t* lut = reinterpret_cast<uint16_t*>(tmem_holder + 4);  // FP8: 256 bf16 decode table
+  float* nf4s = reinterpret_cast<float*>(tmem_holder + 4);        // NF4: 16 levels
+
+  const int warp = (int)warp_id(), lane = (int)lane_id();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+      mbar_init(&xfull[s], 128);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&accf[a], 1);
+      mbar_init(&acce[a], 128);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if constexpr (KIND == kGemmFP8) {
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) lut[i] = p.b_lut[i];
+  }
+  if constexpr (KIND == kGemmNF4) {
+    if (threadIdx.x < 16) nf4s[threadIdx.x] = nf4_level(threadIdx.x);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
+        int mb, nb;
+        tile_coords(t, p, mb, nb);
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.err, kErrWaitEmpty)) goto done;
+          uint8_t* sb = smem + stage * STAGE_BYTES;
+          mbar_arrive_expect_tx(&full[stage], STAGE_BYTES - (XFORM ? B_BYTES : 0));
+          tma_load_2d(sb, &tmA, &full[stage], kb * BK, mb * kBM);
+          if constexpr (T::NA == 2) tma_load_2d(sb + A_BYTES, &tmA2, &full[stage], kb * BK, mb * kBM);
+          if constexpr (XFORM) {
+            // Codes for (BN rows) x (64 k): fp8 64 bytes/row, nf4 32 bytes/row.
+            constexpr int kx = (KIND == kGemmFP8) ? BK : BK / 2;
+            tma_load_2d(sb + T::NA * A_BYTES + B_BYTES, &tmB, &full[stage], kb * kx, nb * BN);
+          } else {
+            tma_load_2d(sb + T::NA * A_BYTES, &tmB, &full[stage], kb * BK, nb * BN);
+            if constexpr (T::NB == 2)
+              tma_load_2d(sb + T::NA * A_BYTES + B_BYTES, &tmB2, &full[stage], kb * BK, nb * BN);
+          }
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // --------------------------------------------------------- UMMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
+        if (!mbar_wait(&acce[acc], acc_phase ^ 1, abort_flag, p.err, kErrWaitAccEmpty)) goto done;
+        tc_fence_after();
+        const uint32_t d = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, p.err, kErrWaitFull)) goto done;
+          if constexpr (XFORM) {
+            if (!mbar_wait(&xfull[stage], phase, abort_flag, p.err, kErrWaitFull)) goto done;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(smem + stage * STAGE_BYTES);
+          const uint32_t a1 = a0 + A_BYTES;
+          const uint32_t b0 = a0 + T::NA * A_BYTES;
+          const uint32_t b1 = b0 + B_BYTES;
+#pragma unroll
+          for (int ks = 0; ks < BK / T::UK; ++ks) {
+            const uint32_t off = (uint32_t)(ks * T::UK * T::ELEM);
+            const uint64_t ad = sdesc_sw128(a0 + off, 16, 1024);
+            const uint64_t bd = sdesc_sw128(b0 + off, 16, 1024);
+            const uint32_t accum = (kb | ks) != 0;
+            if constexpr (KIND == kGemmTF32x3) {
+              umma_tf32_ss(d, sdesc_sw128(a1 + off, 16, 1024), bd, IDESC, accum);
+              umma_tf32_ss(d, ad, sdesc_sw128(b1 + off, 16, 1024), IDESC, 1);
+              umma_tf32_ss(d, ad, bd, IDESC, 1);
+            } else {
+              umma_f16_ss(d, ad, bd, IDESC, accum);
+            }
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        umma_commit(&accf[acc]);
+        acc ^= 1;
+        if (!acc) acc_phase ^= 1;
+      }
+    }
+  } else if (warp < 6) {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
+      int mb, nb;
+      tile_coords(t, p, mb, nb);
+      bool ok = mbar_wait(&accf[acc], acc_phase, abort_flag, p.err, kErrWaitAccFull);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
+      const uint32_t tbase = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * BN);
+      epilogue_tile<BN>(p, tbase, mb * kBM + 32 * q + lane, nb * BN);
+      tc_fence_before();
+      mbar_arrive(&acce[acc]);
+      acc ^= 1;
+      if (!acc) acc_phase ^= 1;
+    }
+  } else if constexpr (XFORM) {
+    // --------------------------------------------- B dequantisation (FP8/NF4)
+    // 128 threads; each writes 16-byte (8 x bf16) chunks of the swizzled tile.
+    const int xt = threadIdx.x - 192;
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
+      int mb, nb;
+      tile_coords(t, p, mb, nb);
+      for (int kb = 0; kb < p.k_blocks; ++kb) {
+        bool ok = mbar_wait(&full[stage], phase, abort_flag, p.err, kErrWaitFull);
+        if (!__all_sync(0xffffffffu, ok)) goto done;
+        uint8_t* sb = smem + stage * STAGE_BYTES;
+        uint8_t* btile = sb + T::NA * A_BYTES;
+        const uint8_t* codes = btile + B_BYTES;
+        // BN rows x 8 chunks of 8 codes.
+        for (int i = xt; i < BN * 8; i += 128) {
+          const int row = i >> 3, ch = i & 7;
+          uint32_t w[4];
+          if constexpr (KIND == kGemmFP8) {
+            const uint2 c8 = *reinterpret_cast<const uint2*>(codes + row * 64 + ch * 8);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const uint32_t word = e < 2 ? c8.x : c8.y;
+              const int sh = (e & 1) * 16;
+              const uint32_t lo = lut[(word >> sh) & 0xff], hi = lut[(word >> (sh + 8)) & 0xff];
+              w[e] = lo | (hi << 16);
+            }
+          } else {
+            const uint32_t c4 = *reinterpret_cast<const uint32_t*>(codes + row * 32 + ch * 4);
+            const int n = nb * BN + row;
+            const int kidx = kb * BK + ch * 8;
+            const float amax = (n < p.N) ? p.b_scale[(size_t)n * (p.K / 64) + kidx / 64] : 0.f;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const uint32_t byte = (c4 >> (8 * e)) & 0xff;
+              const float v0 = nf4s[byte & 0xf] * amax;
+              const float v1 = nf4s[byte >> 4] * amax;
+              w[e] = pack_bf16x2(v0, v1);
+            }
+          }
+          *reinterpret_cast<uint4*>(btile + sw128_offset(row, ch)) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&xfull[stage]);
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+  }
+done:
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, []() {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+bool make_map_2d(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int elem_bytes,
+                 uint64_t inner, uint64_t outer, uint64_t ld_elems, uint32_t box_inner,
+                 uint32_t box_outer, CUtensorMapSwizzle sw) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld_elems * (uint64_t)elem_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int KIND> size_t smem_bytes() {
+  using T = GT<KIND>;
+  const size_t stage = T::NA * kBM * T::BK * T::ELEM + T::NB * T::BN * T::BK * T::ELEM + T::CODE_BYTES;
+  return 1024 + T::STAGES * stage + 8 * (3 * T::STAGES + 4) + 16 + 512;
+}
+
+template <int KIND> cudaError_t launch(const GemmArgs& g, cudaStream_t stream) {
+  using T = GT<KIND>;
+  CUtensorMap ta{}, ta2{}, tb{}, tb2{};
+  const bool f32 = KIND == kGemmTF32x3;
+  const CUtensorMapDataType adt = f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const int ae = f32 ? 4 : 2;
+  if (!make_map_2d(&ta, g.a, adt, ae, g.K, g.M, g.lda, T::BK, kBM, CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorInvalidValue;
+  ta2 = ta;
+  if (f32 && !make_map_2d(&ta2, g.a_lo, adt, ae, g.K, g.M, g.lda, T::BK, kBM, CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorInvalidValue;
+  if (KIND == kGemmFP8) {
+    if (!make_map_2d(&tb, g.b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.K, g.N, g.ldb, 64, T::BN,
+                     CU_TENSOR_MAP_SWIZZLE_NONE))
+      return cudaErrorInvalidValue;
+  } else if (KIND == kGemmNF4) {
+    if (!make_map_2d(&tb, g.b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.K / 2, g.N, g.ldb / 2, 32, T::BN,
+                     CU_TENSOR_MAP_SWIZZLE_NONE))
+      return cudaErrorInvalidValue;
+  } else {
+    if (!make_map_2d(&tb, g.b, adt, ae, g.K, g.N, g.ldb, T::BK, T::BN, CU_TENSOR_MAP_SWIZZLE_128B))
+      return cudaErrorInvalidValue;
+  }
+  tb2 = tb;
+  if (f32 && !make_map_2d(&tb2, g.b_lo, adt, ae, g.K, g.N, g.ldb, T::BK, T::BN, CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorInvalidValue;
+
+  KParams p{};
+  p.M = g.M;
+  p.N = g.N;
+  p.K = g.K;
+  p.m_tiles = (g.M + kBM - 1) / kBM;
+  p.n_tiles = (g.N + T::BN - 1) / T::BN;
+  p.num_tiles = p.m_tiles * p.n_tiles;
+  p.k_blocks = (g.K + T::BK - 1) / T::BK;
+  p.out = g.out;
+  p.ldo = g.ldo;
+  p.out_bf16 = g.out_bf16;
+  p.out_hi = g.out_hi;
+  p.out_lo = g.out_lo;
+  p.b_scale = g.b_scale;
+  p.ldb = g.ldb;
+  p.b_lut = g.b_lut;
+  p.rope_tab = g.rope_tab;
+  p.rope_cols = g.rope_tab ? g.rope_cols : 0;
+  p.head_dim = g.head_dim;
+  p.rope_max_pos = g.rope_max_pos;
+  p.positions = g.positions;
+  p.pos_mod = g.pos_mod;
+  p.kv_k = g.kv_k;
+  p.kv_v = g.kv_v;
+  p.kv_slot = g.kv_slot;
+  p.kv_col0 = g.kv_col0;
+  p.kv_dim = g.kv_dim;
+  p.err = g.err;
+
+  const size_t smem = smem_bytes<KIND>();
+  static cudaError_t attr = cudaFuncSetAttribute(gemm_tc_kernel<KIND>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (attr != cudaSuccess) return attr;
+  const int grid = std::max(1, std::min(p.num_tiles, g.sm_count));
+  gemm_tc_kernel<KIND><<<grid, T::THREADS, smem, stream>>>(ta, ta2, tb, tb2, p);
+  return cudaGetLastError();
+}
+
+} // namespace
+
+bool gemm_tc_supported(const GemmArgs& g) {
+  if (g.M <= 0 || g.N <= 0 || g.K <= 0) return false;
+  const int ae = g.kind == kGemmTF32x3 ? 4 : 2;
+  // TMA: 16-byte aligned bases and row strides.
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (!al16(g.a) || ((size_t)g.lda * ae) % 16) return false;
+  if (g.kind == kGemmTF32x3 && (!al16(g.a_lo) || !al16(g.b_lo))) return false;
+  if (!al16(g.b)) return false;
+  if (g.kind == kGemmFP8 || g.kind == kGemmNF4) {
+    if (g.K % 64) return false;
+    if (g.kind == kGemmFP8 && (g.ldb % 16 || !g.b_lut || !g.b_scale)) return false;
+    if (g.kind == kGemmNF4 && ((g.ldb / 2) % 16 || !g.b_scale)) return false;
+  } else if (((size_t)g.ldb * ae) % 16) {
+    return false;
+  }
+  if (g.kv_k && (g.kv_dim % 32 || g.kv_col0 % 32 || g.head_dim % 32)) return false;
+  return encode_fn() != nullptr;
+}
+
+cudaError_t gemm_tc(const GemmArgs& g, cudaStream_t stream) {
+  if (!gemm_tc_supported(g)) return cudaErrorInvalidValue;
+  switch (g.kind) {
+  case kGemmBF16: return launch<kGemmBF16>(g, stream);
+  case kGemmTF32x3: return launch<kGemmTF32x3>(g, stream);
+  case kGemmFP8: return launch<kGemmFP8>(g, stream);
+  case kGemmNF4: return launch<kGemmNF4>(g, stream);
+  default: return cudaErrorInvalidValue;
+  }
+}
+
+} // namespace wv

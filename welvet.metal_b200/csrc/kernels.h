@@ -1,0 +1,176 @@
+// Launch interfaces of the sm_100a kernels (host C++ side). Every launcher takes
+// device pointers and a stream, allocates nothing, and returns a cudaError_t
+// from the launch; asynchronous failures surface through the error word
+// (`err`, device memory, one uint32) that every kernel writes on a bounded-wait
+// timeout or an argument fault detected on the device.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace wv {
+
+// Error word values (device -> host).
+enum : uint32_t {
+  kErrNone = 0,
+  kErrWaitFull = 1,   // MMA issuer waited too long for a TMA stage
+  kErrWaitEmpty = 2,  // producer waited too long for a free stage
+  kErrWaitAccFull = 3,
+  kErrWaitAccEmpty = 4,
+  kErrWaitOther = 5,
+};
+
+// --------------------------------------------------------------------- GEMM
+// C[M,N] = A[M,K] * B[N,K]^T with FP32 accumulation in TMEM. A and B are
+// row-major with K contiguous (the reference's W[out,in] layout,
+// src/layers/dense/dense.cpp:118). Operand encodings:
+enum GemmKind : int {
+  kGemmBF16 = 0,   // A bf16, B bf16
+  kGemmTF32x3 = 1, // A = a_hi + a_lo, B = b_hi + b_lo (FP32 arrays holding TF32 values);
+                   // three TF32 products per k (hi*hi + hi*lo + lo*hi), ~FP32 accuracy
+  kGemmFP8 = 2,    // A bf16, B FP8-E4M3 codes (+ one FP32 scale per B row, epilogue)
+  kGemmNF4 = 3,    // A bf16, B NF4 codes two per byte (+ FP32 absmax per 64 codes)
+};
+
+struct GemmArgs {
+  int kind = kGemmBF16;
+  int M = 0, N = 0, K = 0;
+  const void* a = nullptr;  // bf16 [M,lda] or fp32 hi [M,lda]
+  const void* a_lo = nullptr;
+  int lda = 0;              // elements
+  const void* b = nullptr;  // bf16 / fp32 hi / fp8 codes / nf4 packed, [N,ldb]
+  const void* b_lo = nullptr;
+  int ldb = 0;              // elements (codes for fp8; bytes*2 for nf4 = K)
+  const float* b_scale = nullptr;  // fp8: [N]; nf4: [N, K/64]
+  const uint16_t* b_lut = nullptr; // fp8: 256-entry bf16 decode table (device)
+  // epilogue
+  void* out = nullptr;      // [M, ldo]
+  int ldo = 0;
+  int out_bf16 = 0;         // 1: bf16 output, 0: fp32
+  float* out_hi = nullptr;  // optional TF32 split of the output (fp32 outputs only)
+  float* out_lo = nullptr;
+  // RoPE fused on columns [0, rope_cols), heads of head_dim columns, pairs (i, i+hd/2)
+  const float2* rope_tab = nullptr; // [max_pos, head_dim/2] (cos, sin)
+  int rope_cols = 0;
+  int head_dim = 0;
+  int rope_max_pos = 0;
+  const int* positions = nullptr;   // per output row; else (row % pos_mod) or row
+  int pos_mod = 0;
+  // KV-cache scatter of the K/V column ranges (decode): columns [kv_col0, kv_col0+2*kd)
+  // go to page pools instead of `out` when kv_k != null.
+  void* kv_k = nullptr;
+  void* kv_v = nullptr;
+  const int* kv_slot = nullptr;     // per row: destination row index in the pools
+  int kv_col0 = 0, kv_dim = 0;
+  uint32_t* err = nullptr;
+  int sm_count = 148;
+};
+
+// True when the tensor-core GEMM supports these shapes (TMA alignment).
+bool gemm_tc_supported(const GemmArgs& a);
+cudaError_t gemm_tc(const GemmArgs& a, cudaStream_t stream);
+// CUDA-core fallback for shapes the TMA path cannot address (FP32 and BF16
+// operands only; same epilogue semantics, RoPE excluded).
+cudaError_t gemm_simt(const GemmArgs& a, cudaStream_t stream);
+
+// ----------------------------------------------------------------- codecs
+// decode(encode(w)) of a FormatNone dtype, elementwise, bit-exact to the
+// reference scalar codecs; NF4 (dtype 26) needs `nf4_scale` (per tensor).
+cudaError_t codec_roundtrip_f32(int dtype, const float* w, float* out, int64_t n,
+                                const float* nf4_scale, cudaStream_t s);
+// Encoders/decoders of the stored byte formats.
+cudaError_t codec_encode(int dtype, const float* w, void* codes, int64_t n, const float* nf4_scale,
+                         cudaStream_t s);
+cudaError_t codec_decode(int dtype, const void* codes, float* out, int64_t n,
+                         const float* nf4_scale, cudaStream_t s);
+// absmax over n floats into *out (device), via a two-pass reduction using `scratch`
+// (>= 1024 floats).
+cudaError_t absmax_f32(const float* w, int64_t n, float* out, float* scratch, cudaStream_t s);
+// Extension formats: per-row FP8 scale and block-64 NF4.
+cudaError_t fp8_rowscale_encode(const float* w, int rows, int cols, uint8_t* codes, float* scales,
+                                cudaStream_t s);
+cudaError_t fp8_rowscale_decode(const uint8_t* codes, const float* scales, int rows, int cols,
+                                void* out, int out_bf16, cudaStream_t s);
+cudaError_t nf4_block_encode(const float* w, int64_t n, uint8_t* packed, float* absmax,
+                             cudaStream_t s);
+cudaError_t nf4_block_decode(const uint8_t* packed, const float* absmax, int64_t n, void* out,
+                             int out_bf16, cudaStream_t s);
+// The E4M3 decode table of the reference converter as bf16 bits (device, 256 entries).
+cudaError_t fp8_lut_init(uint16_t* lut, cudaStream_t s);
+
+// ------------------------------------------------------------- elementwise
+cudaError_t split_tf32(const float* x, float* hi, float* lo, int64_t n, cudaStream_t s);
+cudaError_t cast_f32_bf16(const float* x, void* y, int64_t n, cudaStream_t s);
+cudaError_t cast_bf16_f32(const void* x, float* y, int64_t n, cudaStream_t s);
+// (cos, sin) of pos / theta^(fl32(2i/hd)) in double, rounded to float.
+cudaError_t rope_table(float2* tab, int max_pos, int head_dim, double theta, cudaStream_t s);
+// In-place RoPE on a [M, ld] matrix, columns [0, cols), heads of head_dim.
+cudaError_t rope_apply(void* x, int is_bf16, int64_t M, int ld, int cols, int head_dim,
+                       const float2* tab, int max_pos, const int* positions, int pos_mod,
+                       cudaStream_t s);
+// Deterministic synthetic data: element i of stream `seed` (SplitMix64 counter).
+// kind 0: uniform(-a, a); kind 1: normal(0, a) (Box-Muller, double).
+cudaError_t fill_synthetic(void* dst, int is_bf16, int64_t n, uint64_t seed, uint64_t offset,
+                           int kind, double a, cudaStream_t s);
+
+// ---------------------------------------------------------------- attention
+struct AttnArgs {
+  // q [*, ldq], k/v [*, ldk] token-major rows; head h at columns [h*hd, (h+1)*hd).
+  const void* q = nullptr;
+  const void* k = nullptr;
+  const void* v = nullptr;
+  int ldq = 0, ldk = 0;
+  void* out = nullptr;  // [*, ldo]
+  int ldo = 0;
+  int is_bf16 = 0;
+  int batch = 0, seq = 0;          // sequences x queries per sequence
+  int num_heads = 0, num_kv_heads = 0, head_dim = 0;
+  int stream_mode = 0;             // 1: reference stream semantics (single stream, block ends)
+  int mask = 1, window = 0, max_seq_len = 512, prefix_len = 0, window_causal = 1;
+  int alibi = 0, sigmoid = 0;
+  int head_base = 0, total_heads = 0;  // ALiBi slope uses the global head index
+  float scale = 0.f;
+  float* out_hi = nullptr;         // optional TF32 split of the output
+  float* out_lo = nullptr;
+  uint32_t* err = nullptr;
+  int sm_count = 148;
+};
+bool attn_tc_supported(const AttnArgs& a);
+cudaError_t attn_prefill_tc(const AttnArgs& a, cudaStream_t s);
+cudaError_t attn_prefill_simt(const AttnArgs& a, cudaStream_t s);
+
+// Split-KV decode over a paged cache. Pools hold pages of kPageTokens rows of
+// kd values (K and V separately, bf16 or fp32); block_table[b, j] names the
+// page of tokens [16j, 16j+16) of sequence b. ctx_len[b] = tokens in the cache
+// INCLUDING the new one (already appended).
+constexpr int kPageTokens = 16;
+struct DecodeArgs {
+  const void* q = nullptr;  // [B, ldq] (after RoPE)
+  int ldq = 0;
+  const void* k_pool = nullptr;
+  const void* v_pool = nullptr;
+  const int* block_table = nullptr;
+  int max_pages = 0;        // row stride of block_table
+  const int* ctx_len = nullptr;
+  void* out = nullptr;      // [B, ldo]
+  int ldo = 0;
+  int is_bf16 = 1;
+  int batch = 0, num_heads = 0, num_kv_heads = 0, head_dim = 0;
+  int alibi = 0, sigmoid = 0;
+  int head_base = 0, total_heads = 0;  // ALiBi slope uses the global head index
+  float scale = 0.f;
+  int splits = 0;           // KV splits per (b, kv head); 0 = choose
+  int max_ctx = 0;          // upper bound of ctx_len (split sizing)
+  float* partial = nullptr; // scratch: [B, NH, splits, head_dim + 2]
+  uint32_t* err = nullptr;
+  int sm_count = 148;
+};
+int decode_splits(const DecodeArgs& a);
+size_t decode_scratch_floats(const DecodeArgs& a);
+cudaError_t attn_decode(const DecodeArgs& a, cudaStream_t s);
+// Append rows of k/v (token-major [rows, ld]) into the page pools at slot[row].
+// Pool layout: [page][kv_head][kPageTokens][head_dim]; slot = page*kPageTokens + row.
+cudaError_t kv_append(const void* k, const void* v, int ld, int rows, int kd, int head_dim,
+                      int is_bf16, const int* slot, void* k_pool, void* v_pool, cudaStream_t s);
+
+} // namespace wv

@@ -1,0 +1,833 @@
+// Host orchestration of the MHA forward on B200. See engine.hpp.
+//
+// Weight layouts in HBM (per layer, for this rank's head shard):
+//   wqkv  [nqkv, d]   rows = Wq[heads h0..h0+hc) | Wk[kv heads] | Wv[kv heads]
+//                     precision 0: TF32 hi part (fp32), wqkv_lo the lo part
+//                     precision 1: bf16, or FP8 codes (+ wqkv_scale [nqkv]) or
+//                     NF4 packed [nqkv, d/2] (+ wqkv_scale [nqkv, d/64])
+//   wo    [d, qd_l]   the Wo columns of this shard (row-sharded output projection)
+// Activations are token-major: x [M, d], qkv [M, nqkv], attn [M, qd_l], post [M, d].
+#include "engine.hpp"
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+
+namespace wv {
+
+std::atomic<int64_t> g_launches{0};
+
+// ---------------------------------------------------------------- profiler
+namespace {
+struct ProfState {
+  std::mutex mu;
+  bool on = false;
+  struct Rec {
+    int id;
+    cudaEvent_t a, b;
+    bool closed;
+  };
+  std::vector<Rec> pending;
+  std::vector<cudaEvent_t> pool;
+  double ms[kProfCount] = {};
+  int64_t counts[kProfCount] = {};
+  cudaEvent_t get() {
+    if (!pool.empty()) {
+      cudaEvent_t e = pool.back();
+      pool.pop_back();
+      return e;
+    }
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    return e;
+  }
+};
+ProfState g_prof;
+} // namespace
+
+void prof_enable(bool on) {
+  std::lock_guard<std::mutex> lock(g_prof.mu);
+  g_prof.on = on;
+}
+bool prof_on() { return g_prof.on; }
+void prof_begin(int id, cudaStream_t s) {
+  if (!g_prof.on) return;
+  std::lock_guard<std::mutex> lock(g_prof.mu);
+  ProfState::Rec r{id, g_prof.get(), g_prof.get(), false};
+  cudaEventRecord(r.a, s);
+  g_prof.pending.push_back(r);
+}
+void prof_end(int id, cudaStream_t s) {
+  if (!g_prof.on) return;
+  std::lock_guard<std::mutex> lock(g_prof.mu);
+  for (auto it = g_prof.pending.rbegin(); it != g_prof.pending.rend(); ++it)
+    if (it->id == id && !it->closed) {
+      cudaEventRecord(it->b, s);
+      it->closed = true;
+      return;
+    }
+}
+void prof_read(double* ms, int64_t* counts, bool reset) {
+  std::lock_guard<std::mutex> lock(g_prof.mu);
+  for (auto& r : g_prof.pending) {
+    if (r.closed) {
+      cudaEventSynchronize(r.b);
+      float t = 0.f;
+      if (cudaEventElapsedTime(&t, r.a, r.b) == cudaSuccess) {
+        g_prof.ms[r.id] += t;
+        g_prof.counts[r.id] += 1;
+      }
+    }
+    g_prof.pool.push_back(r.a);
+    g_prof.pool.push_back(r.b);
+  }
+  g_prof.pending.clear();
+  for (int i = 0; i < kProfCount; ++i) {
+    if (ms) ms[i] = g_prof.ms[i];
+    if (counts) counts[i] = g_prof.counts[i];
+    if (reset) {
+      g_prof.ms[i] = 0;
+      g_prof.counts[i] = 0;
+    }
+  }
+}
+
+welvet_status to_c(const Status& s) {
+  welvet_status out{};
+  out.code = s.code;
+  std::snprintf(out.message, sizeof(out.message), "%s", s.msg.c_str());
+  return out;
+}
+
+Status cuda_status(cudaError_t e, const char* what) {
+  return Status::err(4, std::string("cuda: ") + what + ": " + cudaGetErrorString(e));
+}
+
+// ------------------------------------------------------------------ devices
+namespace {
+std::mutex g_dev_mu;
+std::map<int, DeviceCtx*> g_devs;
+
+const char* err_reason(uint32_t code) {
+  switch (code) {
+  case kErrWaitFull: return "device wait timeout (TMA stage)";
+  case kErrWaitEmpty: return "device wait timeout (free stage)";
+  case kErrWaitAccFull: return "device wait timeout (accumulator full)";
+  case kErrWaitAccEmpty: return "device wait timeout (accumulator empty)";
+  case kErrWaitOther: return "device wait timeout";
+  case 0x100: return "RoPE position outside the table";
+  default: return "device error";
+  }
+}
+} // namespace
+
+Status device_ctx(int device, DeviceCtx** out) {
+  if (device < 0) WV_CUDA(cudaGetDevice(&device), "cudaGetDevice");
+  std::lock_guard<std::mutex> lock(g_dev_mu);
+  auto it = g_devs.find(device);
+  if (it != g_devs.end()) {
+    *out = it->second;
+    return cudaSetDevice(device) == cudaSuccess ? Status::ok() : Status::err(4, "cudaSetDevice");
+  }
+  WV_CUDA(cudaSetDevice(device), "cudaSetDevice");
+  cudaDeviceProp prop{};
+  WV_CUDA(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+  if (prop.major < 10)
+    return Status::err(2, std::string("device ") + prop.name + " is not sm_100 (Blackwell)");
+  auto* d = new DeviceCtx();
+  d->device = device;
+  d->sm_count = prop.multiProcessorCount;
+  d->cc_major = prop.major;
+  d->cc_minor = prop.minor;
+  d->name = prop.name;
+  WV_CUDA(cudaMalloc(&d->err, 256), "cudaMalloc err");
+  WV_CUDA(cudaMemset(d->err, 0, 256), "cudaMemset err");
+  WV_CUDA(cudaMalloc(&d->fp8_lut, 512), "cudaMalloc lut");
+  WV_CUDA(fp8_lut_init(d->fp8_lut, 0), "fp8 lut");
+  count_launch();
+  WV_CUDA(cudaMalloc(&d->scratch, 4096 * sizeof(float)), "cudaMalloc scratch");
+  WV_CUDA(cudaMalloc(&d->scalars, 64 * sizeof(float)), "cudaMalloc scalars");
+  WV_CUDA(cudaDeviceSynchronize(), "init");
+  g_devs[device] = d;
+  *out = d;
+  return Status::ok();
+}
+
+Status check_device_error(DeviceCtx* d) {
+  WV_CUDA(cudaSetDevice(d->device), "cudaSetDevice");
+  WV_CUDA(cudaDeviceSynchronize(), "synchronize");
+  uint32_t code = 0;
+  WV_CUDA(cudaMemcpy(&code, d->err, 4, cudaMemcpyDeviceToHost), "read error word");
+  if (code) {
+    cudaMemset(d->err, 0, 4);
+    char buf[96];
+    std::snprintf(buf, sizeof(buf), "kernel error 0x%x: %s", code, err_reason(code));
+    return Status::err(4, buf);
+  }
+  return Status::ok();
+}
+
+// ------------------------------------------------------------------- config
+Status resolve_config(const welvet_b200_mha_config& in, Cfg* out) {
+  Cfg r;
+  r.c = in;
+  auto& c = r.c;
+  if (c.d_model <= 0 || c.num_heads <= 0)
+    return Status::err(1, "mha: need DModel>0 and NumHeads>0");
+  if (c.head_dim <= 0) {
+    if (c.d_model % c.num_heads != 0)
+      return Status::err(1, "mha: HeadDim unset and DModel%NumHeads!=0");
+    c.head_dim = c.d_model / c.num_heads;
+  }
+  if (c.num_kv_heads <= 0) c.num_kv_heads = c.num_heads;
+  if (c.num_heads % c.num_kv_heads != 0)
+    return Status::err(1, "mha: NumHeads not divisible by NumKVHeads");
+  if (c.max_seq_len <= 0) c.max_seq_len = 512;
+  if (c.mask == 0) c.mask = 1;
+  if (c.rope_theta <= 0) c.rope_theta = 10000;
+  if (c.softmax != 0 && c.softmax != 1) return Status::err(1, "mha: unknown Softmax");
+  if (c.precision != 0 && c.precision != 1) return Status::err(1, "mha: precision must be 0 or 1");
+  if (c.weight_format < 0 || c.weight_format > 2 || (c.precision == 0 && c.weight_format != 0))
+    return Status::err(1, "mha: weight_format 1/2 need precision 1 (BF16)");
+  r.hd = c.head_dim;
+  r.nk = c.num_kv_heads;
+  r.msl = c.max_seq_len;
+  r.group = c.num_heads / c.num_kv_heads;
+  r.qd = c.num_heads * r.hd;
+  r.kd = r.nk * r.hd;
+  // ops_mha.metal:46-48: the override is used unless its float high part is 0.
+  r.scale = ((float)c.scale_override != 0.f) ? (float)c.scale_override
+                                               : (float)(1.0 / std::sqrt((double)r.hd));
+  r.rope = c.pos == 0 || c.pos == 3;
+  r.alibi = c.pos == 2 || c.pos == 3;
+  if (c.head_count == 0) {
+    c.head_begin = 0;
+    c.head_count = c.num_heads;
+  }
+  if (c.head_begin < 0 || c.head_count < 0 || c.head_begin + c.head_count > c.num_heads)
+    return Status::err(1, "mha: head shard outside [0, num_heads)");
+  if (c.head_count != c.num_heads &&
+      (c.head_begin % r.group != 0 || c.head_count % r.group != 0))
+    return Status::err(1, "mha: head shard must cover whole KV groups");
+  *out = r;
+  return Status::ok();
+}
+
+// -------------------------------------------------------------------- mount
+Mha::~Mha() { comm_release(this); }
+
+namespace {
+
+// Encode -> decode of one full FP32 matrix on the device (FormatNone dtype), in place.
+Status roundtrip_inplace(DeviceCtx* d, int dtype, float* w, int64_t n, cudaStream_t s) {
+  switch (dtype) {
+  case 0: case 1: case 2: case 3: case 4: case 5: case 26: break;
+  default: {
+    char buf[128];
+    std::snprintf(buf, sizeof(buf),
+                  "mha: weight dtype %d is not implemented by the B200 path (supported: 0-5, 26)", dtype);
+    return Status::err(2, buf);
+  }
+  }
+  if (dtype == 1) return Status::ok();
+  const float* scale = nullptr;
+  if (dtype == 26) {
+    WV_CUDA(absmax_f32(w, n, d->scalars, d->scratch, s), "absmax");
+    count_launch(2);
+    scale = d->scalars;
+  }
+  WV_CUDA(codec_roundtrip_f32(dtype, w, w, n, scale, s), "codec roundtrip");
+  count_launch();
+  return Status::ok();
+}
+
+} // namespace
+
+Status mha_mount(const welvet_b200_mha_config& cin, int dtype, const float* Q, const float* K,
+                 const float* V, const float* O, bool on_device, Mha** out) {
+  if (!Q || !K || !V || !O || !out) return Status::err(1, "mha: invalid argument");
+  Cfg cfg;
+  WV_TRY(resolve_config(cin, &cfg));
+  DeviceCtx* d = nullptr;
+  WV_TRY(device_ctx(cfg.c.device, &d));
+  auto m = std::make_unique<Mha>();
+  m->cfg = cfg;
+  m->dev = d;
+  m->precision = cfg.c.precision;
+  m->wfmt = cfg.c.weight_format;
+  m->h0 = cfg.c.head_begin;
+  m->hc = cfg.c.head_count;
+  m->kh0 = m->h0 / cfg.group;
+  m->khc = std::max(1, m->hc / cfg.group);
+  m->qd_l = m->hc * cfg.hd;
+  m->kd_l = m->khc * cfg.hd;
+  m->nqkv = m->qd_l + 2 * m->kd_l;
+  const int dm = cfg.c.d_model, hd = cfg.hd;
+  const int64_t nq = (int64_t)cfg.qd * dm, nkv = (int64_t)cfg.kd * dm, no = (int64_t)dm * cfg.qd;
+  cudaStream_t s = 0;
+
+  // Full FP32 matrices on the device.
+  DevBuf fq, fk, fv, fo;
+  WV_TRY(fq.ensure(nq * 4));
+  WV_TRY(fk.ensure(nkv * 4));
+  WV_TRY(fv.ensure(nkv * 4));
+  WV_TRY(fo.ensure(no * 4));
+  const cudaMemcpyKind kind = on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+  WV_CUDA(cudaMemcpyAsync(fq.p, Q, nq * 4, kind, s), "upload Q");
+  WV_CUDA(cudaMemcpyAsync(fk.p, K, nkv * 4, kind, s), "upload K");
+  WV_CUDA(cudaMemcpyAsync(fv.p, V, nkv * 4, kind, s), "upload V");
+  WV_CUDA(cudaMemcpyAsync(fo.p, O, no * 4, kind, s), "upload O");
+
+  const size_t qrow0 = (size_t)m->h0 * hd, krow0 = (size_t)m->kh0 * hd;
+  if (m->wfmt == 0) {
+    // FormatNone dtype round trip of each full matrix (reference WeightStore::make
+    // + decode_row_f64, src/weights/store.cpp:7-22, native_codec.cpp:835-870).
+    WV_TRY(roundtrip_inplace(d, dtype, fq.as<float>(), nq, s));
+    WV_TRY(roundtrip_inplace(d, dtype, fk.as<float>(), nkv, s));
+    WV_TRY(roundtrip_inplace(d, dtype, fv.as<float>(), nkv, s));
+    WV_TRY(roundtrip_inplace(d, dtype, fo.as<float>(), no, s));
+    // Shard slices: W_qkv [nqkv, d] and Wo [d, qd_l].
+    DevBuf wqkv32, wo32;
+    WV_TRY(wqkv32.ensure((size_t)m->nqkv * dm * 4));
+    WV_TRY(wo32.ensure((size_t)dm * m->qd_l * 4));
+    float* dst = wqkv32.as<float>();
+    WV_CUDA(cudaMemcpyAsync(dst, fq.as<float>() + qrow0 * dm, (size_t)m->qd_l * dm * 4,
+                            cudaMemcpyDeviceToDevice, s), "slice Wq");
+    WV_CUDA(cudaMemcpyAsync(dst + (size_t)m->qd_l * dm, fk.as<float>() + krow0 * dm,
+                            (size_t)m->kd_l * dm * 4, cudaMemcpyDeviceToDevice, s), "slice Wk");
+    WV_CUDA(cudaMemcpyAsync(dst + (size_t)(m->qd_l + m->kd_l) * dm, fv.as<float>() + krow0 * dm,
+                            (size_t)m->kd_l * dm * 4, cudaMemcpyDeviceToDevice, s), "slice Wv");
+    WV_CUDA(cudaMemcpy2DAsync(wo32.p, (size_t)m->qd_l * 4, fo.as<float>() + qrow0,
+                              (size_t)cfg.qd * 4, (size_t)m->qd_l * 4, dm,
+                              cudaMemcpyDeviceToDevice, s), "slice Wo");
+    const int64_t n1 = (int64_t)m->nqkv * dm, n2 = (int64_t)dm * m->qd_l;
+    if (m->precision == 0) {
+      WV_TRY(m->wqkv.ensure(n1 * 4));
+      WV_TRY(m->wqkv_lo.ensure(n1 * 4));
+      WV_TRY(m->wo.ensure(n2 * 4));
+      WV_TRY(m->wo_lo.ensure(n2 * 4));
+      WV_CUDA(split_tf32(wqkv32.as<float>(), m->wqkv.as<float>(), m->wqkv_lo.as<float>(), n1, s), "split");
+      WV_CUDA(split_tf32(wo32.as<float>(), m->wo.as<float>(), m->wo_lo.as<float>(), n2, s), "split");
+      count_launch(2);
+    } else {
+      WV_TRY(m->wqkv.ensure(n1 * 2));
+      WV_TRY(m->wo.ensure(n2 * 2));
+      WV_CUDA(cast_f32_bf16(wqkv32.as<float>(), m->wqkv.p, n1, s), "cast");
+      WV_CUDA(cast_f32_bf16(wo32.as<float>(), m->wo.p, n2, s), "cast");
+      count_launch(2);
+    }
+    WV_CUDA(cudaStreamSynchronize(s), "mount");
+  } else {
+    // Extension formats encode the FP32 inits directly. Scales are computed on the
+    // full matrices, then the shard's slice of codes and scales is kept.
+    const bool fp8 = m->wfmt == 1;
+    if (dm % 64 || cfg.qd % 64 || (m->qd_l % 64))
+      return Status::err(2, "mha: FP8/NF4 weight formats need d_model and head slices % 64 == 0");
+    DevBuf cq, ck, cv, co, sq, sk, sv, so;
+    auto enc = [&](const DevBuf& w, int rows, int cols, DevBuf& codes, DevBuf& sc) -> Status {
+      const int64_t n = (int64_t)rows * cols;
+      WV_TRY(codes.ensure(fp8 ? n : n / 2));
+      WV_TRY(sc.ensure(fp8 ? (size_t)rows * 4 : (size_t)(n / 64) * 4));
+      if (fp8)
+        WV_CUDA(fp8_rowscale_encode(w.as<float>(), rows, cols, codes.as<uint8_t>(), sc.as<float>(), s), "fp8 enc");
+      else
+        WV_CUDA(nf4_block_encode(w.as<float>(), n, codes.as<uint8_t>(), sc.as<float>(), s), "nf4 enc");
+      count_launch();
+      return Status::ok();
+    };
+    WV_TRY(enc(fq, cfg.qd, dm, cq, sq));
+    WV_TRY(enc(fk, cfg.kd, dm, ck, sk));
+    WV_TRY(enc(fv, cfg.kd, dm, cv, sv));
+    WV_TRY(enc(fo, dm, cfg.qd, co, so));
+    const size_t rb = fp8 ? (size_t)dm : (size_t)dm / 2;   // code bytes per W_qkv row
+    const size_t srow = fp8 ? 1 : (size_t)dm / 64;         // scales per W_qkv row
+    WV_TRY(m->wqkv.ensure((size_t)m->nqkv * rb));
+    WV_TRY(m->wqkv_scale.ensure((size_t)m->nqkv * srow * 4));
+    auto cp = [&](void* dstp, const void* srcp, size_t bytes) -> Status {
+      WV_CUDA(cudaMemcpyAsync(dstp, srcp, bytes, cudaMemcpyDeviceToDevice, s), "slice codes");
+      return Status::ok();
+    };
+    uint8_t* wc = m->wqkv.as<uint8_t>();
+    float* wsc = m->wqkv_scale.as<float>();
+    WV_TRY(cp(wc, cq.as<uint8_t>() + qrow0 * rb, (size_t)m->qd_l * rb));
+    WV_TRY(cp(wc + (size_t)m->qd_l * rb, ck.as<uint8_t>() + krow0 * rb, (size_t)m->kd_l * rb));
+    WV_TRY(cp(wc + (size_t)(m->qd_l + m->kd_l) * rb, cv.as<uint8_t>() + krow0 * rb, (size_t)m->kd_l * rb));
+    WV_TRY(cp(wsc, sq.as<float>() + qrow0 * srow, (size_t)m->qd_l * srow * 4));
+    WV_TRY(cp(wsc + (size_t)m->qd_l * srow, sk.as<float>() + krow0 * srow, (size_t)m->kd_l * srow * 4));
+    WV_TRY(cp(wsc + (size_t)(m->qd_l + m->kd_l) * srow, sv.as<float>() + krow0 * srow,
+              (size_t)m->kd_l * srow * 4));
+    // Wo [d, qd]: keep columns [qrow0, qrow0 + qd_l) of every row.
+    const size_t ob = fp8 ? (size_t)cfg.qd : (size_t)cfg.qd / 2, ob_l = fp8 ? (size_t)m->qd_l : (size_t)m->qd_l / 2;
+    const size_t oc0 = fp8 ? qrow0 : qrow0 / 2;
+    WV_TRY(m->wo.ensure((size_t)dm * ob_l));
+    WV_CUDA(cudaMemcpy2DAsync(m->wo.p, ob_l, co.as<uint8_t>() + oc0, ob, ob_l, dm,
+                              cudaMemcpyDeviceToDevice, s), "slice Wo codes");
+    if (fp8) {
+      WV_TRY(m->wo_scale.ensure((size_t)dm * 4));
+      WV_TRY(cp(m->wo_scale.p, so.p, (size_t)dm * 4));
+    } else {
+      const size_t sb = (size_t)cfg.qd / 64, sb_l = (size_t)m->qd_l / 64;
+      WV_TRY(m->wo_scale.ensure((size_t)dm * sb_l * 4));
+      WV_CUDA(cudaMemcpy2DAsync(m->wo_scale.p, sb_l * 4, so.as<float>() + qrow0 / 64, sb * 4, sb_l * 4, dm,
+                                cudaMemcpyDeviceToDevice, s), "slice Wo absmax");
+    }
+    WV_CUDA(cudaStreamSynchronize(s), "mount");
+  }
+  WV_TRY(check_device_error(d));
+  *out = m.release();
+  return Status::ok();
+}
+
+// ------------------------------------------------------------------ forward
+namespace {
+
+Status ensure_rope(Mha* m, int max_pos, cudaStream_t s) {
+  if (!m->cfg.rope || m->cfg.hd < 2) return Status::ok();
+  if (max_pos <= m->rope_max_pos) return Status::ok();
+  const int want = std::max(max_pos, std::max(m->rope_max_pos * 2, 1024));
+  // The table may be in use by work queued on another stream of this layer.
+  WV_CUDA(cudaDeviceSynchronize(), "rope table sync");
+  WV_TRY(m->rope_tab.ensure((size_t)want * (m->cfg.hd / 2) * sizeof(float2)));
+  WV_CUDA(rope_table(m->rope_tab.as<float2>(), want, m->cfg.hd, m->cfg.c.rope_theta, s), "rope table");
+  count_launch();
+  m->rope_max_pos = want;
+  return Status::ok();
+}
+
+// One projection: out[M, N] = A[M, K] * W[N, K]^T with the layer's format.
+// RoPE (rope_cols > 0) and the KV scatter (kv) are fused where the tensor-core
+// path allows, applied by separate kernels otherwise.
+struct Proj {
+  const void* a = nullptr;
+  const void* a_lo = nullptr;
+  int M = 0, K = 0, lda = 0;
+  const void* w = nullptr;
+  const void* w_lo = nullptr;
+  const float* w_scale = nullptr;
+  int N = 0;
+  void* out = nullptr;
+  int ldo = 0;
+  float* out_hi = nullptr;
+  float* out_lo = nullptr;
+  int rope_cols = 0;
+  const int* positions = nullptr;
+  int pos_mod = 0;
+};
+
+Status run_proj(Mha* m, const Proj& pj, cudaStream_t s) {
+  const bool f32 = m->precision == 0;
+  GemmArgs g;
+  g.kind = f32 ? kGemmTF32x3 : (m->wfmt == 1 ? kGemmFP8 : (m->wfmt == 2 ? kGemmNF4 : kGemmBF16));
+  g.M = pj.M;
+  g.N = pj.N;
+  g.K = pj.K;
+  g.a = pj.a;
+  g.a_lo = pj.a_lo;
+  g.lda = pj.lda;
+  g.b = pj.w;
+  g.b_lo = pj.w_lo;
+  g.ldb = pj.K;
+  g.b_scale = pj.w_scale;
+  g.b_lut = m->dev->fp8_lut;
+  g.out = pj.out;
+  g.ldo = pj.ldo;
+  g.out_bf16 = f32 ? 0 : 1;
+  g.out_hi = pj.out_hi;
+  g.out_lo = pj.out_lo;
+  g.err = m->dev->err;
+  g.sm_count = m->dev->sm_count;
+  const bool rope = pj.rope_cols > 0 && m->cfg.rope;
+  if (rope) {
+    g.rope_tab = m->rope_tab.as<float2>();
+    g.rope_cols = pj.rope_cols;
+    g.head_dim = m->cfg.hd;
+    g.rope_max_pos = m->rope_max_pos;
+    g.positions = pj.positions;
+    g.pos_mod = pj.pos_mod;
+  }
+  const int hd = m->cfg.hd;
+  const int bn = f32 ? 128 : 256;
+  const bool fused_rope = rope && (hd == 64 || hd == 128 || hd == 256) && bn % hd == 0;
+  if (gemm_tc_supported(g)) {
+    WV_CUDA(gemm_tc(g, s), "gemm_tc");
+    count_launch();
+  } else {
+    if (g.kind == kGemmFP8 || g.kind == kGemmNF4)
+      return Status::err(2, "mha: quantised weight GEMM needs TMA-aligned shapes");
+    WV_CUDA(gemm_simt(g, s), "gemm_simt");
+    count_launch();
+  }
+  if (rope && !(fused_rope && gemm_tc_supported(g))) {
+    WV_CUDA(rope_apply(pj.out, f32 ? 0 : 1, pj.M, pj.ldo, pj.rope_cols, hd, m->rope_tab.as<float2>(),
+                       m->rope_max_pos, pj.positions, pj.pos_mod, s), "rope");
+    count_launch();
+    if (pj.out_hi) {  // keep the TF32 split in step with the rotated values
+      WV_CUDA(split_tf32(static_cast<const float*>(pj.out), pj.out_hi, pj.out_lo, (int64_t)pj.M * pj.ldo, s),
+              "split");
+      count_launch();
+    }
+  }
+  return Status::ok();
+}
+
+AttnArgs attn_args(Mha* m, int batch, int seq, bool stream_mode) {
+  AttnArgs a;
+  const auto& c = m->cfg;
+  a.batch = batch;
+  a.seq = seq;
+  a.num_heads = m->hc;
+  a.num_kv_heads = m->khc;
+  a.head_dim = c.hd;
+  a.stream_mode = stream_mode ? 1 : 0;
+  a.mask = c.c.mask;
+  a.window = c.c.window;
+  a.max_seq_len = c.msl;
+  a.prefix_len = c.c.prefix_len;
+  a.window_causal = c.c.window_causal;
+  a.alibi = c.alibi;
+  a.sigmoid = c.c.softmax == 1;
+  a.head_base = m->h0;
+  a.total_heads = c.c.num_heads;
+  a.scale = c.scale;
+  a.is_bf16 = m->precision == 1;
+  a.err = m->dev->err;
+  a.sm_count = m->dev->sm_count;
+  return a;
+}
+
+Status run_attention(Mha* m, AttnArgs a, cudaStream_t s) {
+  (void)m;
+  if (attn_tc_supported(a)) {
+    WV_CUDA(attn_prefill_tc(a, s), "attn_prefill_tc");
+  } else {
+    WV_CUDA(attn_prefill_simt(a, s), "attn_prefill_simt");
+  }
+  count_launch();
+  return Status::ok();
+}
+
+} // namespace
+
+Status mha_forward(Mha* m, int batch, int seq, const void* x, void* pre, void* post, bool on_device,
+                   cudaStream_t s, Kv* kv) {
+  if (!m || !x || !post || batch <= 0 || seq <= 0) return Status::err(1, "mha: invalid argument");
+  std::lock_guard<std::mutex> lock(m->mu);
+  const auto& c = m->cfg;
+  const bool stream_mode = c.c.seq_mode == 0;
+  if (stream_mode && seq > c.msl) return Status::err(1, "mha: seq > MaxSeqLen");  // mha.cpp:159-161
+  WV_CUDA(cudaSetDevice(m->dev->device), "cudaSetDevice");
+  const int64_t M = (int64_t)batch * seq;
+  if (M > (int64_t)INT32_MAX / std::max(m->nqkv, c.c.d_model)) return Status::err(1, "mha: batch too large");
+  const int dm = c.c.d_model;
+  const bool f32 = m->precision == 0;
+  const size_t es = f32 ? 4 : 2;
+
+  // Host buffers: stage through device copies inside the call.
+  const void* xd = x;
+  void* pred = pre;
+  void* postd = post;
+  if (!on_device) {
+    WV_TRY(m->x_io.ensure(M * dm * es));
+    WV_TRY(m->post_io.ensure(M * dm * es));
+    WV_CUDA(cudaMemcpyAsync(m->x_io.p, x, M * dm * es, cudaMemcpyHostToDevice, s), "H2D x");
+    xd = m->x_io.p;
+    postd = m->post_io.p;
+    pred = nullptr;
+  }
+  WV_TRY(m->qkv.ensure(M * m->nqkv * es));
+  void* attn = pred;
+  if (!attn) {
+    WV_TRY(m->attn.ensure(M * m->qd_l * es));
+    attn = m->attn.p;
+  }
+  // RoPE positions: stream mode -> row index (global position), else row % seq.
+  const int max_pos = stream_mode ? (int)M : seq;
+  WV_TRY(ensure_rope(m, max_pos, s));
+
+  Proj q;
+  q.M = (int)M;
+  q.K = dm;
+  q.lda = dm;
+  q.N = m->nqkv;
+  q.out = m->qkv.p;
+  q.ldo = m->nqkv;
+  q.rope_cols = m->qd_l + m->kd_l;
+  q.pos_mod = stream_mode ? 0 : seq;
+  q.w = m->wqkv.p;
+  q.w_lo = m->wqkv_lo.p;
+  q.w_scale = m->wqkv_scale.as<float>();
+  if (f32) {
+    WV_TRY(m->x_hi.ensure(M * dm * 4));
+    WV_TRY(m->x_lo.ensure(M * dm * 4));
+    WV_CUDA(split_tf32(static_cast<const float*>(xd), m->x_hi.as<float>(), m->x_lo.as<float>(), M * dm, s), "split x");
+    count_launch();
+    q.a = m->x_hi.p;
+    q.a_lo = m->x_lo.p;
+  } else {
+    q.a = xd;
+  }
+  prof_begin(kProfGemmQkv, s);
+  WV_TRY(run_proj(m, q, s));
+  prof_end(kProfGemmQkv, s);
+
+  if (kv) {  // prefill: K/V rows into the cache pages of each sequence
+    WV_TRY(m->slots.ensure(M * 4));
+    WV_CUDA(make_prefill_slots(m->slots.as<int>(), batch, seq, kv->pages_per_seq, s), "slots");
+    const char* base = static_cast<const char*>(m->qkv.p);
+    WV_CUDA(kv_append(base + (size_t)m->qd_l * es, base + (size_t)(m->qd_l + m->kd_l) * es, m->nqkv, (int)M,
+                      m->kd_l, c.hd, f32 ? 0 : 1, m->slots.as<int>(), kv->k_pool.p, kv->v_pool.p, s), "kv append");
+    WV_CUDA(set_ctx(kv->ctx_len.as<int>(), batch, seq, s), "ctx");
+    count_launch(3);
+    for (int b = 0; b < batch; ++b) kv->ctx_host[b] = seq;
+  }
+
+  AttnArgs a = attn_args(m, batch, seq, stream_mode);
+  const char* base = static_cast<const char*>(m->qkv.p);
+  a.q = base;
+  a.k = base + (size_t)m->qd_l * es;
+  a.v = base + (size_t)(m->qd_l + m->kd_l) * es;
+  a.ldq = a.ldk = m->nqkv;
+  a.out = attn;
+  a.ldo = m->qd_l;
+  if (f32) {
+    WV_TRY(m->attn_hi.ensure(M * m->qd_l * 4));
+    WV_TRY(m->attn_lo.ensure(M * m->qd_l * 4));
+    a.out_hi = m->attn_hi.as<float>();
+    a.out_lo = m->attn_lo.as<float>();
+  }
+  prof_begin(kProfAttnPrefill, s);
+  WV_TRY(run_attention(m, a, s));
+  prof_end(kProfAttnPrefill, s);
+
+  Proj o;
+  o.M = (int)M;
+  o.K = m->qd_l;
+  o.lda = m->qd_l;
+  o.N = dm;
+  o.out = postd;
+  o.ldo = dm;
+  o.w = m->wo.p;
+  o.w_lo = m->wo_lo.p;
+  o.w_scale = m->wo_scale.as<float>();
+  if (f32) {
+    o.a = m->attn_hi.p;
+    o.a_lo = m->attn_lo.p;
+  } else {
+    o.a = attn;
+  }
+  prof_begin(kProfGemmO, s);
+  WV_TRY(run_proj(m, o, s));
+  prof_end(kProfGemmO, s);
+  if (m->comm) {
+    prof_begin(kProfAllReduce, s);
+    WV_TRY(comm_allreduce(m, postd, (size_t)M * dm, !f32, s));
+    prof_end(kProfAllReduce, s);
+  }
+
+  if (!on_device) {
+    WV_CUDA(cudaMemcpyAsync(post, postd, M * dm * es, cudaMemcpyDeviceToHost, s), "D2H post");
+    if (pre) WV_CUDA(cudaMemcpyAsync(pre, attn, M * m->qd_l * es, cudaMemcpyDeviceToHost, s), "D2H pre");
+    WV_CUDA(cudaStreamSynchronize(s), "forward");
+    WV_TRY(check_device_error(m->dev));
+  }
+  return Status::ok();
+}
+
+// ------------------------------------------------------------------ KV cache
+Status kv_create(Mha* m, int max_batch, int max_ctx, Kv** out) {
+  if (!m || max_batch <= 0 || max_ctx <= 0 || !out) return Status::err(1, "kv: invalid argument");
+  WV_CUDA(cudaSetDevice(m->dev->device), "cudaSetDevice");
+  auto kv = std::make_unique<Kv>();
+  kv->layer = m;
+  kv->max_batch = max_batch;
+  kv->max_ctx = max_ctx;
+  kv->pages_per_seq = (max_ctx + kPageTokens - 1) / kPageTokens;
+  const size_t es = m->precision == 0 ? 4 : 2;
+  const size_t pool = (size_t)max_batch * kv->pages_per_seq * kPageTokens * m->kd_l * es;
+  WV_TRY(kv->k_pool.ensure(pool));
+  WV_TRY(kv->v_pool.ensure(pool));
+  WV_TRY(kv->block_table.ensure((size_t)max_batch * kv->pages_per_seq * 4));
+  WV_TRY(kv->ctx_len.ensure((size_t)max_batch * 4));
+  WV_CUDA(make_block_table(kv->block_table.as<int>(), max_batch, kv->pages_per_seq, 0), "block table");
+  WV_CUDA(set_ctx(kv->ctx_len.as<int>(), max_batch, 0, 0), "ctx");
+  count_launch(2);
+  WV_CUDA(cudaDeviceSynchronize(), "kv create");
+  kv->ctx_host.assign(max_batch, 0);
+  *out = kv.release();
+  return Status::ok();
+}
+
+Status kv_fill(Kv* kv, int batch, int ctx, const void* k, const void* v, bool on_device, cudaStream_t s) {
+  if (!kv || batch <= 0 || batch > kv->max_batch || ctx < 0 || ctx > kv->max_ctx)
+    return Status::err(1, "kv: invalid fill");
+  Mha* m = kv->layer;
+  std::lock_guard<std::mutex> lock(m->mu);
+  WV_CUDA(cudaSetDevice(m->dev->device), "cudaSetDevice");
+  const size_t es = m->precision == 0 ? 4 : 2;
+  const int64_t rows = (int64_t)batch * ctx;
+  if (k && v && rows > 0) {
+    const void* kd = k;
+    const void* vd = v;
+    DevBuf tk, tv;
+    if (!on_device) {
+      WV_TRY(tk.ensure(rows * m->kd_l * es));
+      WV_TRY(tv.ensure(rows * m->kd_l * es));
+      WV_CUDA(cudaMemcpyAsync(tk.p, k, rows * m->kd_l * es, cudaMemcpyHostToDevice, s), "H2D k");
+      WV_CUDA(cudaMemcpyAsync(tv.p, v, rows * m->kd_l * es, cudaMemcpyHostToDevice, s), "H2D v");
+      kd = tk.p;
+      vd = tv.p;
+    }
+    WV_TRY(m->slots.ensure(rows * 4));
+    WV_CUDA(make_prefill_slots(m->slots.as<int>(), batch, ctx, kv->pages_per_seq, s), "slots");
+    WV_CUDA(kv_append(kd, vd, m->kd_l, (int)rows, m->kd_l, m->cfg.hd, m->precision == 1, m->slots.as<int>(),
+                      kv->k_pool.p, kv->v_pool.p, s), "kv append");
+    count_launch(2);
+    if (!on_device) WV_CUDA(cudaStreamSynchronize(s), "kv fill");
+  }
+  WV_CUDA(set_ctx(kv->ctx_len.as<int>(), batch, ctx, s), "ctx");
+  count_launch();
+  for (int b = 0; b < batch; ++b) kv->ctx_host[b] = ctx;
+  if (!on_device) WV_CUDA(cudaStreamSynchronize(s), "kv fill");
+  return Status::ok();
+}
+
+Status mha_decode(Mha* m, Kv* kv, int batch, const void* x, void* pre, void* post, bool on_device,
+                  cudaStream_t s) {
+  if (!m || !kv || kv->layer != m || !x || !post || batch <= 0 || batch > kv->max_batch)
+    return Status::err(1, "mha decode: invalid argument");
+  std::lock_guard<std::mutex> lock(m->mu);
+  WV_CUDA(cudaSetDevice(m->dev->device), "cudaSetDevice");
+  const auto& c = m->cfg;
+  const int dm = c.c.d_model;
+  const bool f32 = m->precision == 0;
+  const size_t es = f32 ? 4 : 2;
+  int max_ctx = 0;
+  for (int b = 0; b < batch; ++b) max_ctx = std::max(max_ctx, kv->ctx_host[b]);
+  if (max_ctx + 1 > kv->max_ctx) return Status::err(1, "mha decode: KV cache full");
+  WV_TRY(ensure_rope(m, max_ctx + 1, s));
+
+  const void* xd = x;
+  void* postd = post;
+  if (!on_device) {
+    WV_TRY(m->x_io.ensure((size_t)batch * dm * es));
+    WV_TRY(m->post_io.ensure((size_t)batch * dm * es));
+    WV_CUDA(cudaMemcpyAsync(m->x_io.p, x, (size_t)batch * dm * es, cudaMemcpyHostToDevice, s), "H2D x");
+    xd = m->x_io.p;
+    postd = m->post_io.p;
+  }
+  WV_TRY(m->positions.ensure((size_t)batch * 4));
+  WV_TRY(m->slots.ensure((size_t)batch * 4));
+  // positions[b] = ctx[b]; slots[b] = page slot of that position; ctx[b] += 1
+  WV_CUDA(make_decode_rows(kv->ctx_len.as<int>(), m->positions.as<int>(), m->slots.as<int>(), batch,
+                           kv->pages_per_seq, s), "decode rows");
+  count_launch();
+  WV_TRY(m->qkv.ensure((size_t)batch * m->nqkv * es));
+
+  Proj q;
+  q.M = batch;
+  q.K = dm;
+  q.lda = dm;
+  q.N = m->nqkv;
+  q.out = m->qkv.p;
+  q.ldo = m->nqkv;
+  q.rope_cols = m->qd_l + m->kd_l;
+  q.positions = m->positions.as<int>();
+  q.w = m->wqkv.p;
+  q.w_lo = m->wqkv_lo.p;
+  q.w_scale = m->wqkv_scale.as<float>();
+  if (f32) {
+    WV_TRY(m->x_hi.ensure((size_t)batch * dm * 4));
+    WV_TRY(m->x_lo.ensure((size_t)batch * dm * 4));
+    WV_CUDA(split_tf32(static_cast<const float*>(xd), m->x_hi.as<float>(), m->x_lo.as<float>(),
+                       (int64_t)batch * dm, s), "split x");
+    count_launch();
+    q.a = m->x_hi.p;
+    q.a_lo = m->x_lo.p;
+  } else {
+    q.a = xd;
+  }
+  prof_begin(kProfGemmQkvDecode, s);
+  WV_TRY(run_proj(m, q, s));
+  prof_end(kProfGemmQkvDecode, s);
+  const char* base = static_cast<const char*>(m->qkv.p);
+  WV_CUDA(kv_append(base + (size_t)m->qd_l * es, base + (size_t)(m->qd_l + m->kd_l) * es, m->nqkv, batch,
+                    m->kd_l, c.hd, f32 ? 0 : 1, m->slots.as<int>(), kv->k_pool.p, kv->v_pool.p, s), "kv append");
+  count_launch();
+
+  void* attn = pre;
+  if (!attn || !on_device) {
+    WV_TRY(m->attn.ensure((size_t)batch * m->qd_l * es));
+    attn = m->attn.p;
+  }
+  DecodeArgs d;
+  d.q = m->qkv.p;
+  d.ldq = m->nqkv;
+  d.k_pool = kv->k_pool.p;
+  d.v_pool = kv->v_pool.p;
+  d.block_table = kv->block_table.as<int>();
+  d.max_pages = kv->pages_per_seq;
+  d.ctx_len = kv->ctx_len.as<int>();
+  d.out = attn;
+  d.ldo = m->qd_l;
+  d.is_bf16 = f32 ? 0 : 1;
+  d.batch = batch;
+  d.num_heads = m->hc;
+  d.num_kv_heads = m->khc;
+  d.head_dim = c.hd;
+  d.alibi = c.alibi;
+  d.sigmoid = c.c.softmax == 1;
+  d.head_base = m->h0;
+  d.total_heads = c.c.num_heads;
+  d.scale = c.scale;
+  d.max_ctx = max_ctx + 1;
+  d.err = m->dev->err;
+  d.sm_count = m->dev->sm_count;
+  WV_TRY(kv->scratch.ensure(decode_scratch_floats(d) * 4));
+  d.partial = kv->scratch.as<float>();
+  prof_begin(kProfAttnDecode, s);
+  WV_CUDA(attn_decode(d, s), "attn_decode");
+  prof_end(kProfAttnDecode, s);
+  count_launch(2);
+
+  Proj o;
+  o.M = batch;
+  o.K = m->qd_l;
+  o.lda = m->qd_l;
+  o.N = dm;
+  o.out = postd;
+  o.ldo = dm;
+  o.w = m->wo.p;
+  o.w_lo = m->wo_lo.p;
+  o.w_scale = m->wo_scale.as<float>();
+  if (f32) {
+    WV_TRY(m->attn_hi.ensure((size_t)batch * m->qd_l * 4));
+    WV_TRY(m->attn_lo.ensure((size_t)batch * m->qd_l * 4));
+    WV_CUDA(split_tf32(static_cast<const float*>(attn), m->attn_hi.as<float>(), m->attn_lo.as<float>(),
+                       (int64_t)batch * m->qd_l, s), "split attn");
+    count_launch();
+    o.a = m->attn_hi.p;
+    o.a_lo = m->attn_lo.p;
+  } else {
+    o.a = attn;
+  }
+  prof_begin(kProfGemmODecode, s);
+  WV_TRY(run_proj(m, o, s));
+  prof_end(kProfGemmODecode, s);
+  if (m->comm) {
+    prof_begin(kProfAllReduce, s);
+    WV_TRY(comm_allreduce(m, postd, (size_t)batch * dm, !f32, s));
+    prof_end(kProfAllReduce, s);
+  }
+  for (int b = 0; b < batch; ++b) kv->ctx_host[b] += 1;
+  if (!on_device) {
+    WV_CUDA(cudaMemcpyAsync(post, postd, (size_t)batch * dm * es, cudaMemcpyDeviceToHost, s), "D2H post");
+    if (pre) WV_CUDA(cudaMemcpyAsync(pre, attn, (size_t)batch * m->qd_l * es, cudaMemcpyDeviceToHost, s), "D2H pre");
+    WV_CUDA(cudaStreamSynchronize(s), "decode");
+    WV_TRY(check_device_error(m->dev));
+  }
+  return Status::ok();
+}
+
+} // namespace wv

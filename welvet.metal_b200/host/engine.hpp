@@ -1,0 +1,173 @@
+// Host orchestration of the B200 MHA path (the role of the reference's
+// src/layers/mha/mha.cpp + src/layers/dense/dense.cpp + src/metal/*.mm):
+// configuration checks with the reference's defaults, resident weights in HBM,
+// the forward / prefill / decode sequences of kernel launches, the paged KV
+// cache and the NCCL communicator of a head shard.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdint>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/welvet_b200.h"
+#include "../csrc/kernels.h"
+
+namespace wv {
+
+struct Status {
+  int code = 0;  // welvet_status codes
+  std::string msg;
+  static Status ok() { return {}; }
+  static Status err(int c, std::string m) { return {c, std::move(m)}; }
+  explicit operator bool() const { return code == 0; }
+};
+
+welvet_status to_c(const Status& s);
+Status cuda_status(cudaError_t e, const char* what);
+
+#define WV_TRY(expr)                               \
+  do {                                             \
+    ::wv::Status _st = (expr);                     \
+    if (!_st) return _st;                          \
+  } while (0)
+#define WV_CUDA(expr, what)                                    \
+  do {                                                         \
+    cudaError_t _e = (expr);                                   \
+    if (_e != cudaSuccess) return ::wv::cuda_status(_e, what); \
+  } while (0)
+
+// Kernel launches issued by this library (benchmark accounting).
+extern std::atomic<int64_t> g_launches;
+inline void count_launch(int n = 1) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+// Live per-kernel timing: when enabled, the engine brackets each hot kernel with
+// CUDA events on the stream it launches on; profile_read() synchronises and
+// accumulates the durations per kernel id.
+enum ProfId : int {
+  kProfGemmQkv = 0,
+  kProfAttnPrefill = 1,
+  kProfGemmO = 2,
+  kProfAttnDecode = 3,
+  kProfGemmQkvDecode = 4,
+  kProfGemmODecode = 5,
+  kProfAllReduce = 6,
+  kProfOther = 7,
+  kProfCount = 8,
+};
+void prof_enable(bool on);
+bool prof_on();
+void prof_begin(int id, cudaStream_t s);
+void prof_end(int id, cudaStream_t s);
+void prof_read(double* ms, int64_t* counts, bool reset);
+
+// Owned device allocation, grown on demand (never shrunk).
+struct DevBuf {
+  void* p = nullptr;
+  size_t bytes = 0;
+  DevBuf() = default;
+  DevBuf(const DevBuf&) = delete;
+  DevBuf& operator=(const DevBuf&) = delete;
+  ~DevBuf() { release(); }
+  void release() {
+    if (p) cudaFree(p);
+    p = nullptr;
+    bytes = 0;
+  }
+  Status ensure(size_t n) {
+    if (n <= bytes && p) return Status::ok();
+    release();
+    cudaError_t e = cudaMalloc(&p, n ? n : 16);
+    if (e != cudaSuccess) {
+      p = nullptr;
+      return cuda_status(e, "cudaMalloc");
+    }
+    bytes = n;
+    return Status::ok();
+  }
+  template <class T> T* as() const { return static_cast<T*>(p); }
+};
+
+// Per-device state shared by every layer on that device.
+struct DeviceCtx {
+  int device = 0;
+  int sm_count = 148;
+  int cc_major = 0, cc_minor = 0;
+  std::string name;
+  uint32_t* err = nullptr;     // device error word
+  uint16_t* fp8_lut = nullptr; // E4M3 -> bf16 bits
+  float* scratch = nullptr;    // 4096 floats (reductions)
+  float* scalars = nullptr;    // 64 floats (per-tensor scales)
+};
+Status device_ctx(int device, DeviceCtx** out);  // device < 0: current
+Status check_device_error(DeviceCtx* d);         // sync + read/clear the error word
+
+// Resolved welvet::mha::Config (defaults of validate(),
+// src/layers/mha/mha.cpp:63-94) + execution choices.
+struct Cfg {
+  welvet_b200_mha_config c{};
+  int hd = 0, nk = 0, msl = 0, group = 0;
+  int qd = 0, kd = 0;
+  float scale = 0.f;
+  bool rope = false, alibi = false;
+};
+Status resolve_config(const welvet_b200_mha_config& in, Cfg* out);
+
+struct Kv;
+
+struct Mha {
+  Cfg cfg;
+  DeviceCtx* dev = nullptr;
+  int h0 = 0, hc = 0, kh0 = 0, khc = 0;  // head shard
+  int qd_l = 0, kd_l = 0, nqkv = 0;
+  int precision = 0, wfmt = 0;
+  // weights (layouts documented in engine.cpp)
+  DevBuf wqkv, wqkv_lo, wo, wo_lo, wqkv_scale, wo_scale;
+  // RoPE cos/sin table
+  DevBuf rope_tab;
+  int rope_max_pos = 0;
+  // workspaces
+  DevBuf x_io, pre_io, post_io, x_hi, x_lo, qkv, attn, attn_hi, attn_lo, post_tmp;
+  DevBuf positions, slots;
+  // communicator (head-sharded tensor parallelism)
+  void* comm = nullptr;
+  int nranks = 1, rank = 0;
+  std::mutex mu;  // one call at a time per layer (reference: per-session lock)
+  ~Mha();
+};
+
+Status mha_mount(const welvet_b200_mha_config& cfg, int dtype, const float* Q, const float* K,
+                 const float* V, const float* O, bool on_device, Mha** out);
+Status mha_forward(Mha* m, int batch, int seq, const void* x, void* pre, void* post,
+                   bool on_device, cudaStream_t s, Kv* kv = nullptr);
+
+struct Kv {
+  Mha* layer = nullptr;
+  int max_batch = 0, max_ctx = 0, pages_per_seq = 0;
+  DevBuf k_pool, v_pool, block_table, ctx_len, scratch;
+  std::vector<int> ctx_host;
+};
+Status kv_create(Mha* m, int max_batch, int max_ctx, Kv** out);
+Status kv_fill(Kv* kv, int batch, int ctx, const void* k, const void* v, bool on_device,
+               cudaStream_t s);
+Status mha_decode(Mha* m, Kv* kv, int batch, const void* x, void* pre, void* post,
+                  bool on_device, cudaStream_t s);
+
+// NCCL (comm.cpp)
+Status comm_unique_id(uint8_t id[128]);
+Status comm_attach(Mha* m, const uint8_t id[128], int nranks, int rank);
+Status comm_allreduce(Mha* m, void* buf, size_t count, bool bf16, cudaStream_t s);
+void comm_release(Mha* m);
+
+// small device helpers (engine_kernels.cu)
+cudaError_t make_prefill_slots(int* slots, int batch, int seq, int pages_per_seq, cudaStream_t s);
+cudaError_t make_decode_rows(int* ctx, int* positions, int* slots, int batch, int pages_per_seq,
+                             cudaStream_t s);
+cudaError_t set_ctx(int* ctx, int batch, int value, cudaStream_t s);
+cudaError_t make_block_table(int* bt, int batch, int pages_per_seq, cudaStream_t s);
+
+} // namespace wv
