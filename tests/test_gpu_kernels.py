@@ -61,8 +61,10 @@ def test_gemm_tf32x3_is_fp32_accurate(torch_cuda, M, N, K):
     torch.cuda.synchronize()
     W.device_check()
     ref = a.double() @ b.double().T
-    # the FP32 path's budget is 1e-4; 3xTF32 lands near FP32 rounding
-    assert rel_err(out.cpu().numpy(), ref.cpu().numpy()) < 2e-6
+    # The FP32 path's budget is 1e-4. 3xTF32 drops only lo*lo (2^-22 relative), but the
+    # tensor-core accumulator does not round each addition to nearest: measured
+    # ~8e-6 at K=1024 on B200, growing ~linearly with K.
+    assert rel_err(out.cpu().numpy(), ref.cpu().numpy()) < 1e-5 * max(1.0, K / 1024)
 
 
 def test_gemm_fp8_rowscale_weights(torch_cuda):
@@ -184,12 +186,16 @@ ATTN_CASES = [
     (dict(d_model=64, num_heads=4, seq_mode=1, mask=3, window=6, window_causal=0), 1, 50),
     (dict(d_model=64, num_heads=4, seq_mode=0, mask=4, prefix_len=9, max_seq_len=64), 2, 20),
     (dict(d_model=48, num_heads=4, seq_mode=1), 2, 19),                   # hd 12
+    (dict(d_model=1024, num_heads=8, seq_mode=1), 2, 1100),               # hd 128, 9 key blocks
+    (dict(d_model=512, num_heads=8, num_kv_heads=2, seq_mode=1), 1, 777),  # hd 64, GQA
+    (dict(d_model=256, num_heads=2, seq_mode=1, mask=2), 1, 300),         # bidirectional, hd 128
+    (dict(d_model=256, num_heads=4, seq_mode=1, mask=3, window=200, pos=2), 1, 700),
 ]
 
 
 @pytest.mark.parametrize("kw,B,T", ATTN_CASES)
-@pytest.mark.parametrize("precision", [0, 1])
-def test_attention_against_oracle(torch_cuda, kw, B, T, precision):
+@pytest.mark.parametrize("precision,impl", [(0, 1), (1, 1), (1, 2)])
+def test_attention_against_oracle(torch_cuda, kw, B, T, precision, impl):
     torch = torch_cuda
     kw = dict(kw)
     cfg = W.MhaConfig.make(kw.pop("d_model"), kw.pop("num_heads"), kw.pop("num_kv_heads", 0), precision=precision,
@@ -211,7 +217,12 @@ def test_attention_against_oracle(torch_cuda, kw, B, T, precision):
     ref = O.attention(oc, B, T, q, k, v)
     dt = torch.float32 if precision == 0 else torch.bfloat16
     out = torch.zeros(M, qd, device="cuda", dtype=dt)
-    W.attention(cfg, B, T, _dev(torch, q, dt), _dev(torch, k, dt), _dev(torch, v, dt), out)
+    try:
+        W.attention(cfg, B, T, _dev(torch, q, dt), _dev(torch, k, dt), _dev(torch, v, dt), out, impl=impl)
+    except W.WelvetError as e:
+        if impl == 2 and e.code == 2:
+            pytest.skip("tensor-core kernel does not cover this head_dim / mode")
+        raise
     torch.cuda.synchronize()
     W.device_check()
     tol = 1e-4 if precision == 0 else 2e-2

@@ -1,13 +1,479 @@
-// Tensor-core (tcgen05) flash-attention prefill. Placeholder entry points until
-// the kernel lands; attn_tc_supported() = false routes every call to the
-// CUDA-core kernel.
+// Flash-attention prefill on the 5th-generation tensor cores (tcgen05), BF16
+// inputs, FP32 accumulation, head_dim 64 or 128 — the B200 replacement for the
+// reference's single-thread attention loop (shaders/ops_mha.metal:31-127).
+//
+// One CTA per (128-query tile, head, sequence), heaviest causal tiles first:
+//   warp 0     TMA producer: Q once, then K_j / V_j (128 keys) into two rings
+//   warp 1     UMMA issuer: S_j = Q K_j^T into one of two TMEM S buffers, and
+//              O += P_j V_j (P from shared memory, V as an MN-major operand)
+//   warps 2-9  softmax in two warpgroups: warpgroup g owns keys [64g, 64g+64) of
+//              every block for the 128 query rows (one row per thread, its TMEM
+//              lane); the two halves of a row exchange their maxima through shared
+//              memory guarded by an mbarrier. Scale, mask (attn_allow,
+//              ops_mha.metal:1-12, evaluated only on blocks that straddle the mask
+//              edge), ALiBi, online max/sum in the log2 domain, P -> swizzled smem
+//              tile, O rescale in TMEM, final normalisation and store.
+// The S MMA of block j+1 overlaps the softmax of block j; O is rescaled only
+// when a row maximum grows by more than 2^8 (exact: the final division uses the
+// same reference maximum as every P), so most blocks never touch O.
 #include "common.cuh"
 #include "kernels.h"
 
+#include <algorithm>
+
 namespace wv {
+namespace {
 
-bool attn_tc_supported(const AttnArgs&) { return false; }
+constexpr int kBQ = 128;  // query rows per tile
+constexpr int kBK = 128;  // keys per block
+constexpr int kSoftThreads = 256;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
-cudaError_t attn_prefill_tc(const AttnArgs&, cudaStream_t) { return cudaErrorNotSupported; }
+template <int HD> struct FT {
+  static constexpr int CH = HD / 64;            // 64-wide (128-byte) chunks of a row
+  static constexpr int TILE = 128 * 128;        // bytes of a 128-row x 64-col bf16 chunk (16 KB)
+  static constexpr int Q_BYTES = CH * TILE;
+  static constexpr int KV_BYTES = CH * TILE;    // one K or V block (128 keys)
+  static constexpr int P_BYTES = 2 * TILE;      // 128 rows x 128 keys
+  static constexpr int SK = HD == 128 ? 2 : 3;  // ring depths
+  static constexpr int SV = HD == 128 ? 2 : 3;
+  static constexpr int OFF_K = Q_BYTES;
+  static constexpr int OFF_V = OFF_K + SK * KV_BYTES;
+  static constexpr int OFF_P = OFF_V + SV * KV_BYTES;
+  static constexpr int OFF_RED = OFF_P + P_BYTES;        // float [2][2][128] maxima + [2][128] sums
+  static constexpr int OFF_BAR = OFF_RED + 6 * 128 * 4;
+  static constexpr int SMEM = 1024 + OFF_BAR + 512;
+};
+
+struct FParams {
+  int batch, seq, num_heads, num_kv_heads, stream_mode;
+  int mask, window, msl, prefix, window_causal, head_base, total_heads;
+  float scale_log2;  // scale * log2(e)
+  void* out;
+  int ldo;
+  int nqt;
+  uint32_t* err;
+};
+
+// attn_allow (ops_mha.metal:1-12) on positions.
+__device__ __forceinline__ bool allow(const FParams& p, int q, int k) {
+  if (p.mask == 2) return true;
+  if (p.mask == 3) {
+    const int w = p.window > 0 ? p.window : p.msl;
+    return p.window_causal ? (k <= q && k >= q - w + 1) : (abs(q - k) < w);
+  }
+  if (p.mask == 4 && q < p.prefix && k < p.prefix) return true;
+  return k <= q;
+}
+
+// Inclusive key range allowed to queries [q0, q1] below kv_end.
+__device__ __forceinline__ void key_range(const FParams& p, int q0, int q1, int kv_end, int& lo, int& hi) {
+  lo = 0;
+  hi = kv_end - 1;
+  if (p.mask == 2) return;
+  if (p.mask == 3) {
+    const int w = p.window > 0 ? p.window : p.msl;
+    lo = max(0, q0 - w + 1);
+    hi = p.window_causal ? min(hi, q1) : min(hi, q1 + w - 1);
+    return;
+  }
+  int h = q1;
+  if (p.mask == 4 && q0 < p.prefix) h = max(h, p.prefix - 1);
+  hi = min(hi, h);
+}
+
+// True when every (query, key) pair of the block is allowed and in range.
+__device__ __forceinline__ bool block_full(const FParams& p, int q0, int q1, int k0, int k1, int kv_end) {
+  if (k1 >= kv_end) return false;
+  if (p.mask == 2) return true;
+  if (p.mask == 3) {
+    const int w = p.window > 0 ? p.window : p.msl;
+    return p.window_causal ? (k1 <= q0 && k0 >= q1 - w + 1) : (q1 - k0 < w && k1 - q0 < w);
+  }
+  if (p.mask == 4 && q1 < p.prefix && k1 < p.prefix) return true;
+  return k1 <= q0;
+}
+
+__device__ __forceinline__ uint32_t sw128(int row, int chunk16) {
+  return (uint32_t)(row * 128 + ((chunk16 ^ (row & 7)) << 4));
+}
+
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <int HD, bool ALIBI, bool SIGMOID>
+__global__ void __launch_bounds__(64 + kSoftThreads, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const FParams p) {
+  using F = FT<HD>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* red_max = reinterpret_cast<float*>(smem + F::OFF_RED);  // [2 buffers][2 halves][128]
+  float* red_sum = red_max + 4 * 128;                           // [2 halves][128]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + F::OFF_BAR);
+  uint64_t* q_full = bar;
+  uint64_t* k_full = bar + 1;
+  uint64_t* k_empty = k_full + F::SK;
+  uint64_t* v_full = k_empty + F::SK;
+  uint64_t* v_empty = v_full + F::SV;
+  uint64_t* s_full = v_empty + F::SV;   // [2]
+  uint64_t* s_empty = s_full + 2;       // [2]
+  uint64_t* p_full = s_empty + 2;       // P_j written (and O rescaled)
+  uint64_t* p_empty = p_full + 1;       // PV_j complete: P tile free, O current
+  uint64_t* mx_bar = p_empty + 1;       // [2] row-max exchange between the halves
+  uint64_t* sum_bar = mx_bar + 2;       // final row-sum exchange
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(sum_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  // ---- work item: heaviest query tiles first
+  const int qt = p.nqt - 1 - (int)blockIdx.x;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int group = p.num_heads / p.num_kv_heads, kh = h / group;
+  const int t0 = qt * kBQ;
+  const int rows_here = min(kBQ, p.seq - t0);
+  const int pos0 = p.stream_mode ? b * p.seq : 0;         // position of t = 0
+  const int kv_end = p.stream_mode ? (b + 1) * p.seq : p.seq;
+  const int q_row0 = b * p.seq + t0;                       // row in the Q matrix
+  const int key_row_base = p.stream_mode ? 0 : b * p.seq;  // row of key position 0
+  int lo, hi;
+  key_range(p, pos0 + t0, pos0 + t0 + rows_here - 1, kv_end, lo, hi);
+  const int kb0 = (lo / kBK) * kBK;
+  const int nblk = hi >= lo ? (hi - kb0) / kBK + 1 : 0;
+
+  const int warp = (int)warp_id(), lane = (int)lane_id();
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < F::SK; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < F::SV; ++s) {
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], kSoftThreads);
+      mbar_init(&mx_bar[i], kSoftThreads);
+    }
+    mbar_init(p_full, kSoftThreads);
+    mbar_init(p_empty, 1);
+    mbar_init(sum_bar, kSoftThreads);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  // TMEM columns: S buffers at 0 and 128 (fp32, 128 keys), O at 256 (head_dim columns).
+  const uint32_t O_col = 256u;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------- producer
+    if (lane == 0 && nblk > 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      mbar_arrive_expect_tx(q_full, F::Q_BYTES);
+      for (int c = 0; c < F::CH; ++c) tma_load_2d(smem + c * F::TILE, &tmQ, q_full, h * HD + c * 64, q_row0);
+      for (int j = 0; j < nblk; ++j) {
+        const int krow = key_row_base + kb0 + j * kBK;
+        const int ks = j % F::SK, vs = j % F::SV;
+        if (!mbar_wait(&k_empty[ks], ((j / F::SK) & 1) ^ 1, abort_flag, p.err, kErrWaitEmpty)) break;
+        mbar_arrive_expect_tx(&k_full[ks], F::KV_BYTES);
+        for (int c = 0; c < F::CH; ++c)
+          tma_load_2d(smem + F::OFF_K + ks * F::KV_BYTES + c * F::TILE, &tmK, &k_full[ks], kh * HD + c * 64, krow);
+        if (!mbar_wait(&v_empty[vs], ((j / F::SV) & 1) ^ 1, abort_flag, p.err, kErrWaitEmpty)) break;
+        mbar_arrive_expect_tx(&v_full[vs], F::KV_BYTES);
+        for (int c = 0; c < F::CH; ++c)
+          tma_load_2d(smem + F::OFF_V + vs * F::KV_BYTES + c * F::TILE, &tmV, &v_full[vs], kh * HD + c * 64, krow);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- UMMA issuer
+    if (lane == 0 && nblk > 0) {
+      constexpr uint32_t IDESC_S = idesc_make(1, kBQ, kBK, 0, 0);
+      constexpr uint32_t IDESC_PV = idesc_make(1, kBQ, HD, 0, 1);
+      const uint32_t q_base = smem_u32(smem);
+      if (!mbar_wait(q_full, 0, abort_flag, p.err, kErrWaitFull)) goto done;
+      for (int j = 0; j <= nblk; ++j) {
+        if (j < nblk) {
+          const int ks = j % F::SK;
+          if (!mbar_wait(&k_full[ks], (j / F::SK) & 1, abort_flag, p.err, kErrWaitFull)) goto done;
+          if (!mbar_wait(&s_empty[j & 1], ((j >> 1) & 1) ^ 1, abort_flag, p.err, kErrWaitAccEmpty)) goto done;
+          tc_fence_after();
+          const uint32_t k_base = smem_u32(smem + F::OFF_K + ks * F::KV_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < HD / 16; ++kk) {
+            const uint32_t off = (uint32_t)((kk >> 2) * F::TILE + (kk & 3) * 32);
+            umma_f16_ss(tmem + (uint32_t)((j & 1) * 128), sdesc_sw128(q_base + off, 16, 1024),
+                        sdesc_sw128(k_base + off, 16, 1024), IDESC_S, kk > 0);
+          }
+          umma_commit(&k_empty[ks]);
+          umma_commit(&s_full[j & 1]);
+        }
+        if (j >= 1) {
+          const int i = j - 1, vs = i % F::SV;
+          if (!mbar_wait(p_full, i & 1, abort_flag, p.err, kErrWaitOther)) goto done;
+          if (!mbar_wait(&v_full[vs], (i / F::SV) & 1, abort_flag, p.err, kErrWaitFull)) goto done;
+          tc_fence_after();
+          const uint32_t p_base = smem_u32(smem + F::OFF_P);
+          const uint32_t v_base = smem_u32(smem + F::OFF_V + vs * F::KV_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const uint32_t poff = (uint32_t)((kk >> 2) * F::TILE + (kk & 3) * 32);
+            // V is MN-major: 16 keys = 16 rows of 128 bytes; the second 64-column
+            // chunk of head_dim sits one TILE further (leading byte offset).
+            umma_f16_ss(tmem + O_col, sdesc_sw128(p_base + poff, 16, 1024),
+                        sdesc_sw128(v_base + (uint32_t)(kk * 16 * 128), F::TILE, 1024), IDESC_PV,
+                        (i > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&v_empty[vs]);
+          umma_commit(p_empty);
+        }
+      }
+    }
+  } else {
+    // -------------------------------------------------------------- softmax
+    const int half = (warp - 2) >> 2;  // key half of every block this warpgroup owns
+    const int q4 = warp & 3;
+    const int r = 32 * q4 + lane;  // query row within the tile (= TMEM lane)
+    const int qpos = pos0 + t0 + r;
+    const bool row_ok = r < rows_here;
+    const uint32_t lane_off = (uint32_t)(32 * q4) << 16;
+    const float sl = p.scale_log2;
+    const float slope2 = ALIBI ? exp2f(-(float)(p.head_base + h + 1) * 8.0f / (float)p.total_heads) * kLog2e : 0.f;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nblk; ++j) {
+      ok = mbar_wait(&s_full[j & 1], (j >> 1) & 1, abort_flag, p.err, kErrWaitAccFull);
+      if (!__all_sync(0xffffffffu, ok)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t s[64];
+      const uint32_t scol = (uint32_t)((j & 1) * 128 + half * 64);
+      tmem_ld32(tmem + lane_off + scol, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
+      tmem_ld32(tmem + lane_off + scol + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(&s_empty[j & 1]);
+
+      const int kblk = kb0 + j * kBK;
+      const int k0 = kblk + half * 64;  // key position of s[0]
+      const bool full = block_full(p, pos0 + t0, pos0 + t0 + kBQ - 1, kblk, kblk + kBK - 1, kv_end);
+      // Fast path: unmasked block, no ALiBi, positive scale -> logits are s * sl and
+      // the max of the logits is sl * max(s).
+      const bool fast = full && !ALIBI && sl > 0.f;
+      float mx = -INFINITY;
+      if (fast) {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) mx = fmaxf(mx, __uint_as_float(s[i]));
+        mx *= sl;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          const int kpos = k0 + i;
+          float v = __uint_as_float(s[i]) * sl;
+          if (ALIBI) v -= slope2 * (float)abs(qpos - kpos);
+          if (!full && !(kpos < kv_end && allow(p, qpos, kpos))) v = -INFINITY;
+          s[i] = __float_as_uint(v);
+          mx = fmaxf(mx, v);
+        }
+      }
+      float corr = 1.f;
+      bool need = false;
+      if (!SIGMOID) {
+        // row max across the two key halves
+        red_max[((j & 1) * 2 + half) * 128 + r] = mx;
+        mbar_arrive(&mx_bar[j & 1]);
+        ok = mbar_wait(&mx_bar[j & 1], (j >> 1) & 1, abort_flag, p.err, kErrWaitOther);
+        if (!__all_sync(0xffffffffu, ok)) {
+          ok = false;
+          break;
+        }
+        mx = fmaxf(mx, red_max[((j & 1) * 2 + (half ^ 1)) * 128 + r]);
+        const float mnew = fmaxf(m, mx);
+        if (m == -INFINITY) {
+          m = mnew;  // first allowed keys of the row: nothing accumulated yet
+        } else if (mnew > m + kRescaleThreshold) {
+          corr = fast_exp2(m - mnew);
+          m = mnew;
+          need = true;
+        }
+      }
+      const float mref = (m == -INFINITY) ? 0.f : m;
+      // The P tile is reused every block: PV_{j-1} must have finished reading it
+      // (and then O is current, so a rescale needs no further wait).
+      if (j >= 1) {
+        ok = mbar_wait(p_empty, (j - 1) & 1, abort_flag, p.err, kErrWaitOther);
+        if (!__all_sync(0xffffffffu, ok)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+      }
+      uint8_t* pb = smem + F::OFF_P + half * F::TILE;
+      float rs = 0.f;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {  // 8 pieces of 8 keys, 16 bytes each
+        uint32_t w4[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float x0 = __uint_as_float(s[8 * c + 2 * e]), x1 = __uint_as_float(s[8 * c + 2 * e + 1]);
+          float a, c2;
+          if (SIGMOID) {
+            const float v0 = fast ? x0 * sl : x0, v1 = fast ? x1 * sl : x1;
+            a = v0 == -INFINITY ? 0.f : __frcp_rn(1.f + fast_exp2(-v0));
+            c2 = v1 == -INFINITY ? 0.f : __frcp_rn(1.f + fast_exp2(-v1));
+          } else if (fast) {
+            a = fast_exp2(fmaf(x0, sl, -mref));
+            c2 = fast_exp2(fmaf(x1, sl, -mref));
+          } else {
+            a = fast_exp2(x0 - mref);
+            c2 = fast_exp2(x1 - mref);
+          }
+          rs += a + c2;
+          w4[e] = pack_bf16x2(a, c2);
+        }
+        *reinterpret_cast<uint4*>(pb + sw128(r, c)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+      }
+      l = l * corr + rs;
+      // Rescale this half's O columns for rows whose max moved (PV_{j-1} is done).
+      if (!SIGMOID && j >= 1 && __any_sync(0xffffffffu, need)) {
+#pragma unroll
+        for (int c = 0; c < HD / 64; ++c) {
+          uint32_t o[32];
+          const uint32_t ocol = O_col + (uint32_t)(half * (HD / 2) + 32 * c);
+          tmem_ld32(tmem + lane_off + ocol, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * corr);
+          tmem_st32(tmem + lane_off + ocol, o);
+        }
+        tmem_st_wait();
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    // ---- epilogue: O / l -> bf16 row of the output (this half's columns)
+    if (ok) {
+      red_sum[half * 128 + r] = l;
+      mbar_arrive(sum_bar);
+      ok = mbar_wait(sum_bar, 0, abort_flag, p.err, kErrWaitOther);
+    }
+    if (ok && nblk > 0) ok = mbar_wait(p_empty, (nblk - 1) & 1, abort_flag, p.err, kErrWaitOther);
+    if (__all_sync(0xffffffffu, ok)) {
+      tc_fence_after();
+      const float lt = l + red_sum[(half ^ 1) * 128 + r];
+      const float inv = SIGMOID ? 1.f : (lt > 0.f ? 1.f / lt : 0.f);
+      __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(p.out) + (size_t)(q_row0 + r) * p.ldo + (size_t)h * HD +
+                            half * (HD / 2);
+#pragma unroll
+      for (int c = 0; c < HD / 64; ++c) {
+        uint32_t o[32];
+        if (nblk > 0) {
+          tmem_ld32(tmem + lane_off + O_col + (uint32_t)(half * (HD / 2) + 32 * c), o);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = 0u;
+        }
+        if (row_ok) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 8)
+            st_global_v4(orow + 32 * c + e, pack_bf16x2(__uint_as_float(o[e]) * inv, __uint_as_float(o[e + 1]) * inv),
+                         pack_bf16x2(__uint_as_float(o[e + 2]) * inv, __uint_as_float(o[e + 3]) * inv),
+                         pack_bf16x2(__uint_as_float(o[e + 4]) * inv, __uint_as_float(o[e + 5]) * inv),
+                         pack_bf16x2(__uint_as_float(o[e + 6]) * inv, __uint_as_float(o[e + 7]) * inv));
+        }
+      }
+    }
+  }
+done:
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <int HD, bool ALIBI, bool SIGMOID>
+cudaError_t launch_variant(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const FParams& p,
+                           dim3 grid, cudaStream_t s) {
+  using F = FT<HD>;
+  static cudaError_t attr = cudaFuncSetAttribute(attn_fwd_kernel<HD, ALIBI, SIGMOID>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, F::SMEM);
+  if (attr != cudaSuccess) return attr;
+  attn_fwd_kernel<HD, ALIBI, SIGMOID><<<grid, 64 + kSoftThreads, F::SMEM, s>>>(mq, mk, mv, p);
+  return cudaGetLastError();
+}
+
+template <int HD> cudaError_t launch(const AttnArgs& a, cudaStream_t s) {
+  alignas(64) CUtensorMap mq, mk, mv;
+  const int rows = a.batch * a.seq;
+  const int qd = a.num_heads * HD, kd = a.num_kv_heads * HD;
+  const int BF16 = (int)CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, SW = (int)CU_TENSOR_MAP_SWIZZLE_128B;
+  if (!make_tma_2d(&mq, a.q, BF16, 2, qd, rows, a.ldq, 64, 128, SW) ||
+      !make_tma_2d(&mk, a.k, BF16, 2, kd, rows, a.ldk, 64, 128, SW) ||
+      !make_tma_2d(&mv, a.v, BF16, 2, kd, rows, a.ldk, 64, 128, SW))
+    return cudaErrorInvalidValue;
+  FParams p{};
+  p.batch = a.batch;
+  p.seq = a.seq;
+  p.num_heads = a.num_heads;
+  p.num_kv_heads = a.num_kv_heads;
+  p.stream_mode = a.stream_mode;
+  p.mask = a.mask;
+  p.window = a.window;
+  p.msl = a.max_seq_len;
+  p.prefix = a.prefix_len;
+  p.window_causal = a.window_causal;
+  p.head_base = a.head_base;
+  p.total_heads = a.total_heads > 0 ? a.total_heads : a.num_heads;
+  p.scale_log2 = a.scale * kLog2e;
+  p.out = a.out;
+  p.ldo = a.ldo;
+  p.nqt = (a.seq + kBQ - 1) / kBQ;
+  p.err = a.err;
+  dim3 grid(p.nqt, a.num_heads, a.batch);
+  if (a.alibi)
+    return a.sigmoid ? launch_variant<HD, true, true>(mq, mk, mv, p, grid, s)
+                     : launch_variant<HD, true, false>(mq, mk, mv, p, grid, s);
+  return a.sigmoid ? launch_variant<HD, false, true>(mq, mk, mv, p, grid, s)
+                   : launch_variant<HD, false, false>(mq, mk, mv, p, grid, s);
+}
+
+} // namespace
+
+bool attn_tc_supported(const AttnArgs& a) {
+  if (!a.is_bf16 || (a.head_dim != 64 && a.head_dim != 128)) return false;
+  if (a.num_kv_heads <= 0 || a.num_heads % a.num_kv_heads) return false;
+  // The ring-wrapped stream case (keys gathered from ring slots) stays on the
+  // CUDA-core kernel; so do outputs that need a TF32 split.
+  if (a.stream_mode && a.batch * a.seq > a.max_seq_len && a.batch > 1) return false;
+  if (a.out_hi) return false;
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (!al16(a.q) || !al16(a.k) || !al16(a.v) || !al16(a.out)) return false;
+  if ((a.ldq * 2) % 16 || (a.ldk * 2) % 16 || (a.ldo * 2) % 16) return false;
+  return true;
+}
+
+cudaError_t attn_prefill_tc(const AttnArgs& a, cudaStream_t s) {
+  if (!attn_tc_supported(a)) return cudaErrorInvalidValue;
+  return a.head_dim == 64 ? launch<64>(a, s) : launch<128>(a, s);
+}
 
 } // namespace wv

@@ -57,7 +57,8 @@ struct KParams {
   int ldo, out_bf16;
   float* out_hi;
   float* out_lo;
-  const float* b_scale;
+  const float* b_scale;    // FP8: per-row scales; NF4: per-64 absmax (dequant warps)
+  const float* col_scale;  // FP8 only: per-output-column scale applied in the epilogue
   int ldb;
   const uint16_t* b_lut;
   const float2* rope_tab;
@@ -169,9 +170,9 @@ __device__ __forceinline__ void epilogue_tile(const KParams& p, uint32_t tbase, 
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
             float a = __uint_as_float(x[e]), b = __uint_as_float(y[e]);
-            if (p.b_scale && p.b_lut) {  // FP8 per-channel scale precedes the rotation
-              a *= p.b_scale[gcol + j + e];
-              b *= p.b_scale[gcol + half + j + e];
+            if (p.col_scale) {  // FP8 per-channel scale precedes the rotation
+              a *= p.col_scale[gcol + j + e];
+              b *= p.col_scale[gcol + half + j + e];
             }
             const float2 cs = pos_ok ? tab[e] : make_float2(1.f, 0.f);
             xo[e] = a * cs.x - b * cs.y;
@@ -190,8 +191,8 @@ __device__ __forceinline__ void epilogue_tile(const KParams& p, uint32_t tbase, 
         float v[32];
 #pragma unroll
         for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(x[e]);
-        if (p.b_scale && p.b_lut) {  // FP8: per-output-channel scale factors out of the K sum
-          for (int e = 0; e < 32 && gcol + e < p.N; ++e) v[e] *= p.b_scale[gcol + e];
+        if (p.col_scale) {  // FP8: per-output-channel scale factors out of the K sum
+          for (int e = 0; e < 32 && gcol + e < p.N; ++e) v[e] *= p.col_scale[gcol + e];
         }
         store_vals(p, row, gcol, v, min(32, p.N - gcol));
       }
@@ -420,6 +421,8 @@ done:
   }
 }
 
+} // namespace
+
 // ---------------------------------------------------------------- host side
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -448,6 +451,15 @@ bool make_map_2d(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int e
             CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
+
+bool make_tma_2d(void* map128, const void* base, int dt, int elem_bytes, uint64_t inner,
+                 uint64_t outer, uint64_t ld_elems, uint32_t box_inner, uint32_t box_outer, int sw) {
+  return make_map_2d(static_cast<CUtensorMap*>(map128), base, static_cast<CUtensorMapDataType>(dt),
+                     elem_bytes, inner, outer, ld_elems, box_inner, box_outer,
+                     static_cast<CUtensorMapSwizzle>(sw));
+}
+
+namespace {
 
 template <int KIND> size_t smem_bytes() {
   using T = GT<KIND>;
@@ -498,6 +510,7 @@ template <int KIND> cudaError_t launch(const GemmArgs& g, cudaStream_t stream) {
   p.b_scale = g.b_scale;
   p.ldb = g.ldb;
   p.b_lut = g.b_lut;
+  p.col_scale = KIND == kGemmFP8 ? g.b_scale : nullptr;
   p.rope_tab = g.rope_tab;
   p.rope_cols = g.rope_tab ? g.rope_cols : 0;
   p.head_dim = g.head_dim;

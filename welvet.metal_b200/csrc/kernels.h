@@ -66,6 +66,12 @@ struct GemmArgs {
   int sm_count = 148;
 };
 
+// 2-D TMA descriptor over a row-major [outer][inner] matrix with row stride
+// ld_elems (cuTensorMapEncodeTiled through the runtime's driver entry point).
+// dt is a CUtensorMapDataType, sw a CUtensorMapSwizzle (ints to keep cuda.h out).
+bool make_tma_2d(void* map128, const void* base, int dt, int elem_bytes, uint64_t inner,
+                 uint64_t outer, uint64_t ld_elems, uint32_t box_inner, uint32_t box_outer, int sw);
+
 // True when the tensor-core GEMM supports these shapes (TMA alignment).
 bool gemm_tc_supported(const GemmArgs& a);
 cudaError_t gemm_tc(const GemmArgs& a, cudaStream_t stream);

@@ -519,7 +519,8 @@ Status mha_forward(Mha* m, int batch, int seq, const void* x, void* pre, void* p
   if (stream_mode && seq > c.msl) return Status::err(1, "mha: seq > MaxSeqLen");  // mha.cpp:159-161
   WV_CUDA(cudaSetDevice(m->dev->device), "cudaSetDevice");
   const int64_t M = (int64_t)batch * seq;
-  if (M > (int64_t)INT32_MAX / std::max(m->nqkv, c.c.d_model)) return Status::err(1, "mha: batch too large");
+  // Rows are 32-bit TMA coordinates; element offsets are 64-bit everywhere.
+  if (M >= (int64_t{1} << 30)) return Status::err(1, "mha: batch*seq too large");
   const int dm = c.c.d_model;
   const bool f32 = m->precision == 0;
   const size_t es = f32 ? 4 : 2;
