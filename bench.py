@@ -122,7 +122,7 @@ def cpu_sample(d, H, NK, T_s, threads=0):
     hd = d // H
     Ws = W.xavier_weights(d, H * hd, NK * hd, seed=0)
     x = W.synthetic(T_s * d, 1, 1, 1.0).reshape(T_s, d)
-    cfg = O.MhaCfg(d_model=d, num_heads=H, num_kv_heads=NK, per_sequence=1)
+    cfg = O.MhaCfg(d_model=d, num_heads=H, num_kv_heads=NK, max_seq_len=T_s, per_sequence=1)
     t0 = time.perf_counter()
     O.mha_forward(cfg, 1, T_s, *Ws, x, threads=threads)
     dt = time.perf_counter() - t0
@@ -366,6 +366,7 @@ def main():
                                                        "allreduce")}}}
         kv.close()
 
+    print(f"[bench] prefill {ms:.3f} ms/step, {tokps:.0f} tok/s; profile {prof}", file=sys.stderr, flush=True)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         dt, fl = cpu_sample(d, H, NK, args.cpu_tokens)

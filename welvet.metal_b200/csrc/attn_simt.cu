@@ -210,69 +210,91 @@ __global__ void __launch_bounds__(128) decode_kernel(DecodeArgs a, int splits, i
   const int k0 = split * chunk, k1 = min(L, k0 + chunk);
   
 
+  // Scores in the log2 domain: q is pre-scaled by scale*log2(e), m/l track exp2.
+  constexpr int U = 4;  // key groups in flight per warp iteration (memory-level parallelism)
   float q[MAXG][VEC];
   float o[MAXG][VEC];
   float m[MAXG], l[MAXG];
+  float slope2[MAXG];
   const T* Q = static_cast<const T*>(a.q);
+  const float qs = a.scale * 1.4426950408889634f;
+#pragma unroll
   for (int g = 0; g < MAXG; ++g) {
     m[g] = -INFINITY;
     l[g] = 0.f;
+    const int h = kh * G + g;
+    slope2[g] = a.alibi ? exp2f(-(float)(a.head_base + h + 1) * 8.0f / (float)a.total_heads) * 1.4426950408889634f
+                        : 0.f;
 #pragma unroll
     for (int e = 0; e < VEC; ++e) {
       o[g][e] = 0.f;
-      q[g][e] = 0.f;
-    }
-    if (g < G) {
-      const int h = kh * G + g;
-#pragma unroll
-      for (int e = 0; e < VEC; ++e) q[g][e] = ldf(Q, (size_t)b * a.ldq + (size_t)h * HD + sl * VEC + e) * a.scale;
+      q[g][e] = ldf(Q, (size_t)b * a.ldq + (size_t)h * HD + sl * VEC + e) * qs;
     }
   }
   const T* KP = static_cast<const T*>(a.k_pool);
   const T* VP = static_cast<const T*>(a.v_pool);
   const int* bt = a.block_table + (size_t)b * a.max_pages;
-  const int step = 4 * KPW;  // keys per block step
-  for (int base = k0 + warp * KPW; base < k1; base += step) {
-    const int p = base + sub;
-    const bool valid = p < k1;
-    float kf[VEC], vf[VEC];
-    if (valid) {
-      const int page = bt[p / kPageTokens];
-      const size_t off = (((size_t)page * NK + kh) * kPageTokens + (p % kPageTokens)) * HD + sl * VEC;
-      const uint4 kr = __ldg(reinterpret_cast<const uint4*>(KP + off));
-      const uint4 vr = __ldg(reinterpret_cast<const uint4*>(VP + off));
-      const T* kt = reinterpret_cast<const T*>(&kr);
-      const T* vt = reinterpret_cast<const T*>(&vr);
+  const int wstep = KPW * U;  // keys per warp iteration
+  for (int base = k0 + warp * wstep; base < k1; base += 4 * wstep) {
+    uint4 kr[U], vr[U];
+    bool valid[U];
+    int pos[U];
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) {
-        kf[e] = ldf(kt, e);
-        vf[e] = ldf(vt, e);
+    for (int u = 0; u < U; ++u) {
+      const int p = base + u * KPW + sub;
+      pos[u] = p;
+      valid[u] = p < k1;
+      if (valid[u]) {
+        const int page = bt[p / kPageTokens];
+        const size_t off = (((size_t)page * NK + kh) * kPageTokens + (p % kPageTokens)) * HD + sl * VEC;
+        kr[u] = __ldg(reinterpret_cast<const uint4*>(KP + off));
+        vr[u] = __ldg(reinterpret_cast<const uint4*>(VP + off));
+      } else {
+        kr[u] = vr[u] = make_uint4(0u, 0u, 0u, 0u);
       }
-    } else {
-#pragma unroll
-      for (int e = 0; e < VEC; ++e) kf[e] = vf[e] = 0.f;
     }
 #pragma unroll
     for (int g = 0; g < MAXG; ++g) {
-      if (g >= G) break;
-      float s = 0.f;
+      float s[U];
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) s = fmaf(q[g][e], kf[e], s);
+      for (int u = 0; u < U; ++u) {
+        const T* kt = reinterpret_cast<const T*>(&kr[u]);
+        float acc = 0.f;
 #pragma unroll
-      for (int off = LPK / 2; off; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-      if (a.alibi) s -= exp2f(-(float)(a.head_base + kh * G + g + 1) * 8.0f / (float)a.total_heads) * (float)abs((L - 1) - p);
-      if (a.sigmoid) {
-        const float pr = valid ? 1.f / (1.f + expf(-s)) : 0.f;
+        for (int e = 0; e < VEC; ++e) acc = fmaf(q[g][e], ldf(kt, e), acc);
 #pragma unroll
-        for (int e = 0; e < VEC; ++e) o[g][e] = fmaf(pr, vf[e], o[g][e]);
-      } else if (valid) {
-        const float mn = fmaxf(m[g], s);
-        const float corr = expf(m[g] - mn), pr = expf(s - mn);
-        l[g] = l[g] * corr + pr;
-#pragma unroll
-        for (int e = 0; e < VEC; ++e) o[g][e] = fmaf(pr, vf[e], o[g][e] * corr);
-        m[g] = mn;
+        for (int off = LPK / 2; off; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+        if (a.alibi) acc -= slope2[g] * (float)abs((L - 1) - pos[u]);
+        s[u] = acc;
       }
+      if (a.sigmoid) {
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const float pr = valid[u] ? 1.f / (1.f + exp2f(-s[u])) : 0.f;
+          const T* vt = reinterpret_cast<const T*>(&vr[u]);
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) o[g][e] = fmaf(pr, ldf(vt, e), o[g][e]);
+        }
+        continue;
+      }
+      float mx = m[g];
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (valid[u]) mx = fmaxf(mx, s[u]);
+      if (mx == -INFINITY) continue;  // no key of this group is valid
+      const float corr = exp2f(m[g] - mx);
+      l[g] *= corr;
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) o[g][e] *= corr;
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const float pr = valid[u] ? exp2f(s[u] - mx) : 0.f;
+        l[g] += pr;
+        const T* vt = reinterpret_cast<const T*>(&vr[u]);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) o[g][e] = fmaf(pr, ldf(vt, e), o[g][e]);
+      }
+      m[g] = mx;
     }
   }
   // Combine the KPW key slots of each warp, then the 4 warps, through smem.
@@ -291,7 +313,7 @@ __global__ void __launch_bounds__(128) decode_kernel(DecodeArgs a, int splits, i
     float mm = -INFINITY;
     for (int s2 = 0; s2 < 4 * KPW; ++s2) mm = fmaxf(mm, red_m[s2][g]);
     gm[g] = mm;
-    scl[g] = a.sigmoid ? 1.f : (m[g] == -INFINITY ? 0.f : expf(m[g] - mm));
+    scl[g] = a.sigmoid ? 1.f : (m[g] == -INFINITY ? 0.f : exp2f(m[g] - mm));
   }
   for (int i = threadIdx.x; i < G * HD; i += blockDim.x) red_o[i / HD][i % HD] = 0.f;
   __syncthreads();
@@ -307,7 +329,7 @@ __global__ void __launch_bounds__(128) decode_kernel(DecodeArgs a, int splits, i
     if (c == HD + 1) {
       for (int s2 = 0; s2 < 4 * KPW; ++s2) {
         const float ms = red_m[s2][g];
-        lsum += a.sigmoid ? red_l[s2][g] : (ms == -INFINITY ? 0.f : red_l[s2][g] * expf(ms - gm[g]));
+        lsum += a.sigmoid ? red_l[s2][g] : (ms == -INFINITY ? 0.f : red_l[s2][g] * exp2f(ms - gm[g]));
       }
     }
     const float val = c < HD ? red_o[g][c] : (c == HD ? gm[g] : lsum);
@@ -324,7 +346,7 @@ __global__ void decode_combine_kernel(DecodeArgs a, int splits) {
   float lsum = 0.f;
   for (int s = 0; s < splits; ++s) {
     const float ms = P[s * (hd + 2) + hd];
-    const float w = a.sigmoid ? 1.f : (ms == -INFINITY ? 0.f : expf(ms - mx));
+    const float w = a.sigmoid ? 1.f : (ms == -INFINITY ? 0.f : exp2f(ms - mx));
     lsum += w * P[s * (hd + 2) + hd + 1];
   }
   const float inv = a.sigmoid ? 1.f : (lsum > 0.f ? 1.f / lsum : 0.f);
@@ -332,7 +354,7 @@ __global__ void decode_combine_kernel(DecodeArgs a, int splits) {
     float acc = 0.f;
     for (int s = 0; s < splits; ++s) {
       const float ms = P[s * (hd + 2) + hd];
-      const float w = a.sigmoid ? 1.f : (ms == -INFINITY ? 0.f : expf(ms - mx));
+      const float w = a.sigmoid ? 1.f : (ms == -INFINITY ? 0.f : exp2f(ms - mx));
       acc += w * P[s * (hd + 2) + d];
     }
     const float val = acc * inv;

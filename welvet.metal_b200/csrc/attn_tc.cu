@@ -4,18 +4,20 @@
 //
 // One CTA per (128-query tile, head, sequence), heaviest causal tiles first:
 //   warp 0     TMA producer: Q once, then K_j / V_j (128 keys) into two rings
-//   warp 1     UMMA issuer: S_j = Q K_j^T into one of two TMEM S buffers, and
-//              O += P_j V_j (P from shared memory, V as an MN-major operand)
-//   warps 2-9  softmax in two warpgroups: warpgroup g owns keys [64g, 64g+64) of
-//              every block for the 128 query rows (one row per thread, its TMEM
-//              lane); the two halves of a row exchange their maxima through shared
-//              memory guarded by an mbarrier. Scale, mask (attn_allow,
-//              ops_mha.metal:1-12, evaluated only on blocks that straddle the mask
-//              edge), ALiBi, online max/sum in the log2 domain, P -> swizzled smem
-//              tile, O rescale in TMEM, final normalisation and store.
-// The S MMA of block j+1 overlaps the softmax of block j; O is rescaled only
-// when a row maximum grows by more than 2^8 (exact: the final division uses the
-// same reference maximum as every P), so most blocks never touch O.
+//   warp 1     UMMA issuer: S_j = Q K_j^T into TMEM buffer S_{j&1}, and
+//              O_{j&1} += P_j V_j (P from shared memory, V as an MN-major operand)
+//   warps 2-9  two softmax warpgroups; warpgroup g owns the key blocks j == g
+//              (mod 2) as an independent partial softmax (own running max, sum,
+//              P tile and O accumulator) — one query row per thread, its TMEM
+//              lane. The two partial results are merged once, at the end.
+// Per block a warpgroup scales, masks (attn_allow, ops_mha.metal:1-12, evaluated
+// only on blocks that straddle the mask edge), applies ALiBi, keeps an online
+// max/sum in the log2 domain and writes P to its swizzled smem tile. O is
+// rescaled only when a row maximum grows by more than 2^8 (exact: the final
+// division uses the same reference maximum as every P), and then without any
+// extra wait, since the last PV into that O is the one that freed the P tile.
+// While one warpgroup works on block j the tensor cores run S_{j+1} and PV_{j-1}
+// of the other, so the softmax of two blocks is always in flight.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -26,7 +28,16 @@ namespace {
 
 constexpr int kBQ = 128;  // query rows per tile
 constexpr int kBK = 128;  // keys per block
-constexpr int kSoftThreads = 256;
+constexpr int kSoftThreads = 256;  // warps 0-7: two softmax warpgroups
+constexpr int kThreads = 384;      // warps 8-11: TMA producer (8), UMMA issuer (9), idle (10, 11)
+// Register split by warpgroup (setmaxnreg): the launch gives every thread
+// kLaunchRegs; the producer warpgroup drops to kLowRegs and the softmax
+// warpgroups grow to kHighRegs. The host verifies the kernel's launch register
+// count before the first launch so the split always fits the block's pool.
+constexpr int kLaunchRegs = 168;
+constexpr int kLowRegs = 56;
+constexpr int kHighRegs = 224;
+static_assert(kLowRegs * 128 + kHighRegs * 256 <= kLaunchRegs * kThreads, "register split exceeds the pool");
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
@@ -40,9 +51,8 @@ template <int HD> struct FT {
   static constexpr int SV = HD == 128 ? 2 : 3;
   static constexpr int OFF_K = Q_BYTES;
   static constexpr int OFF_V = OFF_K + SK * KV_BYTES;
-  static constexpr int OFF_P = OFF_V + SV * KV_BYTES;
-  static constexpr int OFF_RED = OFF_P + P_BYTES;        // float [2][2][128] maxima + [2][128] sums
-  static constexpr int OFF_BAR = OFF_RED + 6 * 128 * 4;
+  static constexpr int OFF_P = OFF_V + SV * KV_BYTES;  // two P tiles, one per warpgroup
+  static constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
   static constexpr int SMEM = 1024 + OFF_BAR + 512;
 };
 
@@ -106,27 +116,24 @@ __device__ __forceinline__ float fast_exp2(float x) {
 }
 
 template <int HD, bool ALIBI, bool SIGMOID>
-__global__ void __launch_bounds__(64 + kSoftThreads, 1)
+__global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const FParams p) {
   using F = FT<HD>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  float* red_max = reinterpret_cast<float*>(smem + F::OFF_RED);  // [2 buffers][2 halves][128]
-  float* red_sum = red_max + 4 * 128;                           // [2 halves][128]
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + F::OFF_BAR);
   uint64_t* q_full = bar;
   uint64_t* k_full = bar + 1;
   uint64_t* k_empty = k_full + F::SK;
   uint64_t* v_full = k_empty + F::SK;
   uint64_t* v_empty = v_full + F::SV;
-  uint64_t* s_full = v_empty + F::SV;   // [2]
-  uint64_t* s_empty = s_full + 2;       // [2]
-  uint64_t* p_full = s_empty + 2;       // P_j written (and O rescaled)
-  uint64_t* p_empty = p_full + 1;       // PV_j complete: P tile free, O current
-  uint64_t* mx_bar = p_empty + 1;       // [2] row-max exchange between the halves
-  uint64_t* sum_bar = mx_bar + 2;       // final row-sum exchange
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(sum_bar + 1);
+  uint64_t* s_full = v_empty + F::SV;  // [2] per warpgroup
+  uint64_t* s_empty = s_full + 2;      // [2]
+  uint64_t* p_full = s_empty + 2;      // [2] P written (and O rescaled)
+  uint64_t* p_empty = p_full + 2;      // [2] PV complete: P tile free, O current
+  uint64_t* fin_bar = p_empty + 2;     // final (max, sum) exchange
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(fin_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   // ---- work item: heaviest query tiles first
@@ -157,16 +164,15 @@ __global__ void __launch_bounds__(64 + kSoftThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], kSoftThreads);
-      mbar_init(&mx_bar[i], kSoftThreads);
+      mbar_init(&s_empty[i], kSoftThreads / 2);
+      mbar_init(&p_full[i], kSoftThreads / 2);
+      mbar_init(&p_empty[i], 1);
     }
-    mbar_init(p_full, kSoftThreads);
-    mbar_init(p_empty, 1);
-    mbar_init(sum_bar, kSoftThreads);
+    mbar_init(fin_bar, kSoftThreads);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 1) {
+  if (warp == 9) {
     tmem_alloc(tmem_holder, 512);
     tmem_relinquish();
   }
@@ -174,10 +180,10 @@ __global__ void __launch_bounds__(64 + kSoftThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
-  // TMEM columns: S buffers at 0 and 128 (fp32, 128 keys), O at 256 (head_dim columns).
-  const uint32_t O_col = 256u;
+  // TMEM columns: S_g at 128*g (fp32, 128 keys); O_g at 256 + HD*g.
 
-  if (warp == 0) {
+  if (warp >= 8) regs_dec<kLowRegs>();  // whole warpgroup 2, before any role branch
+  if (warp == 8) {
     // ------------------------------------------------------------- producer
     if (lane == 0 && nblk > 0) {
       tma_prefetch_desc(&tmQ);
@@ -185,104 +191,131 @@ __global__ void __launch_bounds__(64 + kSoftThreads, 1)
       tma_prefetch_desc(&tmV);
       mbar_arrive_expect_tx(q_full, F::Q_BYTES);
       for (int c = 0; c < F::CH; ++c) tma_load_2d(smem + c * F::TILE, &tmQ, q_full, h * HD + c * 64, q_row0);
-      for (int j = 0; j < nblk; ++j) {
-        const int krow = key_row_base + kb0 + j * kBK;
-        const int ks = j % F::SK, vs = j % F::SV;
-        if (!mbar_wait(&k_empty[ks], ((j / F::SK) & 1) ^ 1, abort_flag, p.err, kErrWaitEmpty)) break;
-        mbar_arrive_expect_tx(&k_full[ks], F::KV_BYTES);
-        for (int c = 0; c < F::CH; ++c)
-          tma_load_2d(smem + F::OFF_K + ks * F::KV_BYTES + c * F::TILE, &tmK, &k_full[ks], kh * HD + c * 64, krow);
-        if (!mbar_wait(&v_empty[vs], ((j / F::SV) & 1) ^ 1, abort_flag, p.err, kErrWaitEmpty)) break;
-        mbar_arrive_expect_tx(&v_full[vs], F::KV_BYTES);
-        for (int c = 0; c < F::CH; ++c)
-          tma_load_2d(smem + F::OFF_V + vs * F::KV_BYTES + c * F::TILE, &tmV, &v_full[vs], kh * HD + c * 64, krow);
+      // K runs two blocks ahead of V, matching the issue order S_{i+2}, PV_i.
+      for (int j = 0; j < nblk + 2; ++j) {
+        if (j < nblk) {
+          const int ks = j % F::SK;
+          if (!mbar_wait(&k_empty[ks], ((j / F::SK) & 1) ^ 1, abort_flag, p.err, kErrWaitEmpty)) break;
+          mbar_arrive_expect_tx(&k_full[ks], F::KV_BYTES);
+          for (int c = 0; c < F::CH; ++c)
+            tma_load_2d(smem + F::OFF_K + ks * F::KV_BYTES + c * F::TILE, &tmK, &k_full[ks], kh * HD + c * 64,
+                        key_row_base + kb0 + j * kBK);
+        }
+        const int i = j - 2;
+        if (i >= 0 && i < nblk) {
+          const int vs = i % F::SV;
+          if (!mbar_wait(&v_empty[vs], ((i / F::SV) & 1) ^ 1, abort_flag, p.err, kErrWaitEmpty)) break;
+          mbar_arrive_expect_tx(&v_full[vs], F::KV_BYTES);
+          for (int c = 0; c < F::CH; ++c)
+            tma_load_2d(smem + F::OFF_V + vs * F::KV_BYTES + c * F::TILE, &tmV, &v_full[vs], kh * HD + c * 64,
+                        key_row_base + kb0 + i * kBK);
+        }
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == 9) {
     // ---------------------------------------------------------- UMMA issuer
     if (lane == 0 && nblk > 0) {
       constexpr uint32_t IDESC_S = idesc_make(1, kBQ, kBK, 0, 0);
       constexpr uint32_t IDESC_PV = idesc_make(1, kBQ, HD, 0, 1);
       const uint32_t q_base = smem_u32(smem);
       if (!mbar_wait(q_full, 0, abort_flag, p.err, kErrWaitFull)) goto done;
-      for (int j = 0; j <= nblk; ++j) {
-        if (j < nblk) {
-          const int ks = j % F::SK;
-          if (!mbar_wait(&k_full[ks], (j / F::SK) & 1, abort_flag, p.err, kErrWaitFull)) goto done;
-          if (!mbar_wait(&s_empty[j & 1], ((j >> 1) & 1) ^ 1, abort_flag, p.err, kErrWaitAccEmpty)) goto done;
-          tc_fence_after();
-          const uint32_t k_base = smem_u32(smem + F::OFF_K + ks * F::KV_BYTES);
+      // S_j into TMEM buffer j&1. Its warpgroup copies S into registers at the start
+      // of its block, so S_{j+2} can run while that warpgroup is still computing
+      // block j: issue order S_0, S_1, then per block i: S_{i+2}, PV_i.
+      auto issue_s = [&](int j) -> bool {
+        const int ks = j % F::SK, g = j & 1;
+        if (!mbar_wait(&k_full[ks], (j / F::SK) & 1, abort_flag, p.err, kErrWaitFull)) return false;
+        // S buffer g was last read by the warpgroup's copy of S_{j-2}
+        if (j >= 2 && !mbar_wait(&s_empty[g], ((j - 2) >> 1) & 1, abort_flag, p.err, kErrWaitAccEmpty))
+          return false;
+        tc_fence_after();
+        const uint32_t k_base = smem_u32(smem + F::OFF_K + ks * F::KV_BYTES);
 #pragma unroll
-          for (int kk = 0; kk < HD / 16; ++kk) {
-            const uint32_t off = (uint32_t)((kk >> 2) * F::TILE + (kk & 3) * 32);
-            umma_f16_ss(tmem + (uint32_t)((j & 1) * 128), sdesc_sw128(q_base + off, 16, 1024),
-                        sdesc_sw128(k_base + off, 16, 1024), IDESC_S, kk > 0);
-          }
-          umma_commit(&k_empty[ks]);
-          umma_commit(&s_full[j & 1]);
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off = (uint32_t)((kk >> 2) * F::TILE + (kk & 3) * 32);
+          umma_f16_ss(tmem + (uint32_t)(g * 128), sdesc_sw128(q_base + off, 16, 1024),
+                      sdesc_sw128(k_base + off, 16, 1024), IDESC_S, kk > 0);
         }
-        if (j >= 1) {
-          const int i = j - 1, vs = i % F::SV;
-          if (!mbar_wait(p_full, i & 1, abort_flag, p.err, kErrWaitOther)) goto done;
-          if (!mbar_wait(&v_full[vs], (i / F::SV) & 1, abort_flag, p.err, kErrWaitFull)) goto done;
-          tc_fence_after();
-          const uint32_t p_base = smem_u32(smem + F::OFF_P);
-          const uint32_t v_base = smem_u32(smem + F::OFF_V + vs * F::KV_BYTES);
+        umma_commit(&k_empty[ks]);
+        umma_commit(&s_full[g]);
+        return true;
+      };
+      auto issue_pv = [&](int i) -> bool {
+        const int vs = i % F::SV, g = i & 1;
+        if (!mbar_wait(&p_full[g], (i >> 1) & 1, abort_flag, p.err, kErrWaitOther)) return false;
+        if (!mbar_wait(&v_full[vs], (i / F::SV) & 1, abort_flag, p.err, kErrWaitFull)) return false;
+        tc_fence_after();
+        const uint32_t p_base = smem_u32(smem + F::OFF_P + g * F::P_BYTES);
+        const uint32_t v_base = smem_u32(smem + F::OFF_V + vs * F::KV_BYTES);
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk) {
-            const uint32_t poff = (uint32_t)((kk >> 2) * F::TILE + (kk & 3) * 32);
-            // V is MN-major: 16 keys = 16 rows of 128 bytes; the second 64-column
-            // chunk of head_dim sits one TILE further (leading byte offset).
-            umma_f16_ss(tmem + O_col, sdesc_sw128(p_base + poff, 16, 1024),
-                        sdesc_sw128(v_base + (uint32_t)(kk * 16 * 128), F::TILE, 1024), IDESC_PV,
-                        (i > 0 || kk > 0) ? 1u : 0u);
-          }
-          umma_commit(&v_empty[vs]);
-          umma_commit(p_empty);
+        for (int kk = 0; kk < kBK / 16; ++kk) {
+          const uint32_t poff = (uint32_t)((kk >> 2) * F::TILE + (kk & 3) * 32);
+          // V is MN-major: 16 keys = 16 rows of 128 bytes; the second 64-column
+          // chunk of head_dim sits one TILE further (leading byte offset).
+          umma_f16_ss(tmem + (uint32_t)(256 + HD * g), sdesc_sw128(p_base + poff, 16, 1024),
+                      sdesc_sw128(v_base + (uint32_t)(kk * 16 * 128), F::TILE, 1024), IDESC_PV,
+                      (i >= 2 || kk > 0) ? 1u : 0u);
         }
+        umma_commit(&v_empty[vs]);
+        umma_commit(&p_empty[g]);
+        return true;
+      };
+      for (int j = 0; j < min(2, nblk); ++j)
+        if (!issue_s(j)) goto done;
+      for (int i = 0; i < nblk; ++i) {
+        if (i + 2 < nblk && !issue_s(i + 2)) goto done;
+        if (!issue_pv(i)) goto done;
       }
     }
-  } else {
+  } else if (warp < 8) {
     // -------------------------------------------------------------- softmax
-    const int half = (warp - 2) >> 2;  // key half of every block this warpgroup owns
+    regs_inc<kHighRegs>();
+    const int g = warp >> 2;  // this warpgroup owns blocks j == g (mod 2)
     const int q4 = warp & 3;
-    const int r = 32 * q4 + lane;  // query row within the tile (= TMEM lane)
+    const int r = 32 * q4 + lane;   // query row within the tile (= TMEM lane)
     const int qpos = pos0 + t0 + r;
     const bool row_ok = r < rows_here;
     const uint32_t lane_off = (uint32_t)(32 * q4) << 16;
+    const uint32_t s_col = (uint32_t)(128 * g), o_col = (uint32_t)(256 + HD * g);
     const float sl = p.scale_log2;
     const float slope2 = ALIBI ? exp2f(-(float)(p.head_base + h + 1) * 8.0f / (float)p.total_heads) * kLog2e : 0.f;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < nblk; ++j) {
-      ok = mbar_wait(&s_full[j & 1], (j >> 1) & 1, abort_flag, p.err, kErrWaitAccFull);
+    int jl = -1;  // last block processed by this warpgroup
+    uint8_t* pt = smem + F::OFF_P + g * F::P_BYTES;
+    for (int j = g; j < nblk; j += 2) {
+      ok = mbar_wait(&s_full[g], (j >> 1) & 1, abort_flag, p.err, kErrWaitAccFull);
       if (!__all_sync(0xffffffffu, ok)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      uint32_t s[64];
-      const uint32_t scol = (uint32_t)((j & 1) * 128 + half * 64);
-      tmem_ld32(tmem + lane_off + scol, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
-      tmem_ld32(tmem + lane_off + scol + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
+      uint32_t s[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        tmem_ld32(tmem + lane_off + s_col + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&s[32 * c]));
       tmem_ld_wait();
       tc_fence_before();
-      mbar_arrive(&s_empty[j & 1]);
+      mbar_arrive(&s_empty[g]);
 
-      const int kblk = kb0 + j * kBK;
-      const int k0 = kblk + half * 64;  // key position of s[0]
-      const bool full = block_full(p, pos0 + t0, pos0 + t0 + kBQ - 1, kblk, kblk + kBK - 1, kv_end);
+      const int k0 = kb0 + j * kBK;
+      const bool full = block_full(p, pos0 + t0, pos0 + t0 + kBQ - 1, k0, k0 + kBK - 1, kv_end);
       // Fast path: unmasked block, no ALiBi, positive scale -> logits are s * sl and
       // the max of the logits is sl * max(s).
       const bool fast = full && !ALIBI && sl > 0.f;
       float mx = -INFINITY;
       if (fast) {
+        float m8[8];  // independent partial maxima (ILP)
 #pragma unroll
-        for (int i = 0; i < 64; ++i) mx = fmaxf(mx, __uint_as_float(s[i]));
+        for (int e = 0; e < 8; ++e) m8[e] = __uint_as_float(s[e]);
+#pragma unroll
+        for (int i = 8; i < 128; ++i) m8[i & 7] = fmaxf(m8[i & 7], __uint_as_float(s[i]));
+#pragma unroll
+        for (int e = 0; e < 8; ++e) mx = fmaxf(mx, m8[e]);
         mx *= sl;
       } else {
 #pragma unroll
-        for (int i = 0; i < 64; ++i) {
+        for (int i = 0; i < 128; ++i) {
           const int kpos = k0 + i;
           float v = __uint_as_float(s[i]) * sl;
           if (ALIBI) v -= slope2 * (float)abs(qpos - kpos);
@@ -294,15 +327,6 @@ __global__ void __launch_bounds__(64 + kSoftThreads, 1)
       float corr = 1.f;
       bool need = false;
       if (!SIGMOID) {
-        // row max across the two key halves
-        red_max[((j & 1) * 2 + half) * 128 + r] = mx;
-        mbar_arrive(&mx_bar[j & 1]);
-        ok = mbar_wait(&mx_bar[j & 1], (j >> 1) & 1, abort_flag, p.err, kErrWaitOther);
-        if (!__all_sync(0xffffffffu, ok)) {
-          ok = false;
-          break;
-        }
-        mx = fmaxf(mx, red_max[((j & 1) * 2 + (half ^ 1)) * 128 + r]);
         const float mnew = fmaxf(m, mx);
         if (m == -INFINITY) {
           m = mnew;  // first allowed keys of the row: nothing accumulated yet
@@ -313,20 +337,18 @@ __global__ void __launch_bounds__(64 + kSoftThreads, 1)
         }
       }
       const float mref = (m == -INFINITY) ? 0.f : m;
-      // The P tile is reused every block: PV_{j-1} must have finished reading it
-      // (and then O is current, so a rescale needs no further wait).
-      if (j >= 1) {
-        ok = mbar_wait(p_empty, (j - 1) & 1, abort_flag, p.err, kErrWaitOther);
+      // This warpgroup's P tile is free and its O current once PV_{j-2} is done.
+      if (j >= 2) {
+        ok = mbar_wait(&p_empty[g], ((j - 2) >> 1) & 1, abort_flag, p.err, kErrWaitOther);
         if (!__all_sync(0xffffffffu, ok)) {
           ok = false;
           break;
         }
         tc_fence_after();
       }
-      uint8_t* pb = smem + F::OFF_P + half * F::TILE;
-      float rs = 0.f;
+      float rs4[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial sums (ILP)
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {  // 8 pieces of 8 keys, 16 bytes each
+      for (int c = 0; c < 16; ++c) {  // 16 pieces of 8 keys, 16 bytes each
         uint32_t w4[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -343,60 +365,76 @@ __global__ void __launch_bounds__(64 + kSoftThreads, 1)
             a = fast_exp2(x0 - mref);
             c2 = fast_exp2(x1 - mref);
           }
-          rs += a + c2;
+          rs4[e] += a + c2;
           w4[e] = pack_bf16x2(a, c2);
         }
-        *reinterpret_cast<uint4*>(pb + sw128(r, c)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+        *reinterpret_cast<uint4*>(pt + (c >> 3) * F::TILE + sw128(r, c & 7)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
       }
-      l = l * corr + rs;
-      // Rescale this half's O columns for rows whose max moved (PV_{j-1} is done).
-      if (!SIGMOID && j >= 1 && __any_sync(0xffffffffu, need)) {
+      l = l * corr + ((rs4[0] + rs4[1]) + (rs4[2] + rs4[3]));
+      if (!SIGMOID && __any_sync(0xffffffffu, need)) {
 #pragma unroll
-        for (int c = 0; c < HD / 64; ++c) {
+        for (int c = 0; c < HD / 32; ++c) {
           uint32_t o[32];
-          const uint32_t ocol = O_col + (uint32_t)(half * (HD / 2) + 32 * c);
-          tmem_ld32(tmem + lane_off + ocol, o);
+          tmem_ld32(tmem + lane_off + o_col + 32 * c, o);
           tmem_ld_wait();
 #pragma unroll
           for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * corr);
-          tmem_st32(tmem + lane_off + ocol, o);
+          tmem_st32(tmem + lane_off + o_col + 32 * c, o);
         }
         tmem_st_wait();
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[g]);
+      jl = j;
     }
-    // ---- epilogue: O / l -> bf16 row of the output (this half's columns)
+    // ---- merge the two partial softmaxes; warpgroup g writes output columns
+    //      [g*HD/2, (g+1)*HD/2) of the row.
+    if (ok && jl >= 0) ok = mbar_wait(&p_empty[g], (jl >> 1) & 1, abort_flag, p.err, kErrWaitOther);
+    float* ex = reinterpret_cast<float*>(pt);  // this warpgroup's P tile is free now
     if (ok) {
-      red_sum[half * 128 + r] = l;
-      mbar_arrive(sum_bar);
-      ok = mbar_wait(sum_bar, 0, abort_flag, p.err, kErrWaitOther);
+      ex[r] = m;
+      ex[128 + r] = l;
+      // The other warpgroup reads O_g after this arrive; it orders after the
+      // p_empty[g] completion observed above (release/acquire through fin_bar).
+      tc_fence_before();
+      mbar_arrive(fin_bar);
+      ok = mbar_wait(fin_bar, 0, abort_flag, p.err, kErrWaitOther);
     }
-    if (ok && nblk > 0) ok = mbar_wait(p_empty, (nblk - 1) & 1, abort_flag, p.err, kErrWaitOther);
     if (__all_sync(0xffffffffu, ok)) {
       tc_fence_after();
-      const float lt = l + red_sum[(half ^ 1) * 128 + r];
-      const float inv = SIGMOID ? 1.f : (lt > 0.f ? 1.f / lt : 0.f);
-      __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(p.out) + (size_t)(q_row0 + r) * p.ldo + (size_t)h * HD +
-                            half * (HD / 2);
+      const float* exo = reinterpret_cast<const float*>(smem + F::OFF_P + (g ^ 1) * F::P_BYTES);
+      const float mA = g == 0 ? m : exo[r], lA = g == 0 ? l : exo[128 + r];
+      const float mB = g == 0 ? exo[r] : m, lB = g == 0 ? exo[128 + r] : l;
+      const int nbA = (nblk + 1) / 2, nbB = nblk / 2;
+      float wA = 1.f, wB = 1.f, inv = 1.f;
+      if (!SIGMOID) {
+        const float M = fmaxf(mA, mB);
+        wA = (mA == -INFINITY) ? 0.f : fast_exp2(mA - M);
+        wB = (mB == -INFINITY) ? 0.f : fast_exp2(mB - M);
+        const float L = lA * wA + lB * wB;
+        inv = L > 0.f ? 1.f / L : 0.f;
+      }
+      wA *= inv;
+      wB *= inv;
+      __nv_bfloat16* orow =
+          static_cast<__nv_bfloat16*>(p.out) + (size_t)(q_row0 + r) * p.ldo + (size_t)h * HD + g * (HD / 2);
 #pragma unroll
       for (int c = 0; c < HD / 64; ++c) {
-        uint32_t o[32];
-        if (nblk > 0) {
-          tmem_ld32(tmem + lane_off + O_col + (uint32_t)(half * (HD / 2) + 32 * c), o);
-          tmem_ld_wait();
-        } else {
+        const uint32_t col = (uint32_t)(g * (HD / 2) + 32 * c);
+        uint32_t oa[32], ob[32];
+        if (nbA > 0) tmem_ld32(tmem + lane_off + 256 + col, oa);
+        if (nbB > 0) tmem_ld32(tmem + lane_off + 256 + HD + col, ob);
+        tmem_ld_wait();
+        float v[32];
 #pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] = 0u;
-        }
+        for (int e = 0; e < 32; ++e)
+          v[e] = (nbA > 0 ? __uint_as_float(oa[e]) * wA : 0.f) + (nbB > 0 ? __uint_as_float(ob[e]) * wB : 0.f);
         if (row_ok) {
 #pragma unroll
           for (int e = 0; e < 32; e += 8)
-            st_global_v4(orow + 32 * c + e, pack_bf16x2(__uint_as_float(o[e]) * inv, __uint_as_float(o[e + 1]) * inv),
-                         pack_bf16x2(__uint_as_float(o[e + 2]) * inv, __uint_as_float(o[e + 3]) * inv),
-                         pack_bf16x2(__uint_as_float(o[e + 4]) * inv, __uint_as_float(o[e + 5]) * inv),
-                         pack_bf16x2(__uint_as_float(o[e + 6]) * inv, __uint_as_float(o[e + 7]) * inv));
+            st_global_v4(orow + 32 * c + e, pack_bf16x2(v[e], v[e + 1]), pack_bf16x2(v[e + 2], v[e + 3]),
+                         pack_bf16x2(v[e + 4], v[e + 5]), pack_bf16x2(v[e + 6], v[e + 7]));
         }
       }
     }
@@ -404,7 +442,7 @@ __global__ void __launch_bounds__(64 + kSoftThreads, 1)
 done:
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -414,10 +452,20 @@ template <int HD, bool ALIBI, bool SIGMOID>
 cudaError_t launch_variant(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const FParams& p,
                            dim3 grid, cudaStream_t s) {
   using F = FT<HD>;
-  static cudaError_t attr = cudaFuncSetAttribute(attn_fwd_kernel<HD, ALIBI, SIGMOID>,
-                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, F::SMEM);
-  if (attr != cudaSuccess) return attr;
-  attn_fwd_kernel<HD, ALIBI, SIGMOID><<<grid, 64 + kSoftThreads, F::SMEM, s>>>(mq, mk, mv, p);
+  static const cudaError_t ready = []() {
+    cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel<HD, ALIBI, SIGMOID>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, F::SMEM);
+    if (e != cudaSuccess) return e;
+    // setmaxnreg.inc waits until the block's register pool can serve it: refuse to
+    // launch unless the pool (launch registers x threads) covers the split.
+    cudaFuncAttributes fa{};
+    e = cudaFuncGetAttributes(&fa, attn_fwd_kernel<HD, ALIBI, SIGMOID>);
+    if (e != cudaSuccess) return e;
+    if (fa.numRegs * kThreads < kLowRegs * 128 + kHighRegs * 256) return cudaErrorNotSupported;
+    return cudaSuccess;
+  }();
+  if (ready != cudaSuccess) return ready;
+  attn_fwd_kernel<HD, ALIBI, SIGMOID><<<grid, kThreads, F::SMEM, s>>>(mq, mk, mv, p);
   return cudaGetLastError();
 }
 

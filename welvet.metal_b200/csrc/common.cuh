@@ -219,6 +219,10 @@ WV_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
 }
 WV_DEV void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// Warpgroup register reconfiguration (all 4 warps of the warpgroup execute it).
+template <int N> WV_DEV void regs_dec() { asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N)); }
+template <int N> WV_DEV void regs_inc() { asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N)); }
+
 // Shared-memory matrix descriptor (tcgen05 format): start address, leading and
 // stride byte offsets in 16-byte units, descriptor version 1 at bit 46, layout
 // type at bits 61-63 (2 = 128-byte swizzle). Tiles are 1024-byte aligned so the

@@ -499,11 +499,13 @@ AttnArgs attn_args(Mha* m, int batch, int seq, bool stream_mode) {
 
 Status run_attention(Mha* m, AttnArgs a, cudaStream_t s) {
   (void)m;
-  if (attn_tc_supported(a)) {
-    WV_CUDA(attn_prefill_tc(a, s), "attn_prefill_tc");
-  } else {
-    WV_CUDA(attn_prefill_simt(a, s), "attn_prefill_simt");
+  cudaError_t e = cudaErrorNotSupported;
+  if (attn_tc_supported(a)) e = attn_prefill_tc(a, s);
+  if (e == cudaErrorNotSupported) {  // shape/mode outside the tensor-core kernel, or its
+    cudaGetLastError();               // register split does not fit this build
+    e = attn_prefill_simt(a, s);
   }
+  WV_CUDA(e, "attention prefill");
   count_launch();
   return Status::ok();
 }
