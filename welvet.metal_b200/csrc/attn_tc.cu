@@ -115,6 +115,46 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// 2^x on the FMA/ALU pipes: x = n + f with n = rint(x) (magic-number rounding),
+// f in [-1/2, 1/2]; 2^f by a degree-3 polynomial fitted here (relative error
+// 7.5e-5, below bf16's 2^-9), 2^n added to the exponent field. Valid for
+// x >= -126 (clamped); callers use it only where no element is masked.
+__device__ __forceinline__ float poly_exp2(float x) {
+  x = fmaxf(x, -126.0f);
+  const float t = x + 12582912.0f;  // 1.5 * 2^23
+  const float f = x - (t - 12582912.0f);
+  float pf = fmaf(0.055171605199575424f, f, 0.2426111102104187f);
+  pf = fmaf(pf, f, 0.6932609677314758f);
+  pf = fmaf(pf, f, 0.9999280571937561f);
+  const int n = __float_as_int(t) - 0x4B400000;
+  return __int_as_float(__float_as_int(pf) + (n << 23));
+}
+
+// Packed FP32 pairs (sm_100 f32x2 ALU ops) and a three-input max.
+__device__ __forceinline__ uint64_t f2pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2unpack(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 template <int HD, bool ALIBI, bool SIGMOID>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -305,13 +345,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool fast = full && !ALIBI && sl > 0.f;
       float mx = -INFINITY;
       if (fast) {
-        float m8[8];  // independent partial maxima (ILP)
+        float m8[8];  // independent partial maxima (ILP), three-input max
 #pragma unroll
-        for (int e = 0; e < 8; ++e) m8[e] = __uint_as_float(s[e]);
+        for (int e = 0; e < 8; ++e) m8[e] = fmaxf(__uint_as_float(s[e]), __uint_as_float(s[8 + e]));
 #pragma unroll
-        for (int i = 8; i < 128; ++i) m8[i & 7] = fmaxf(m8[i & 7], __uint_as_float(s[i]));
+        for (int i = 16; i < 128; i += 16) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) mx = fmaxf(mx, m8[e]);
+          for (int e = 0; e < 8; ++e) m8[e] = fmax3(m8[e], __uint_as_float(s[i + e]), __uint_as_float(s[i + 8 + e]));
+        }
+        mx = fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
         mx *= sl;
       } else {
 #pragma unroll
@@ -346,31 +388,44 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
       }
-      float rs4[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial sums (ILP)
+      uint64_t acc2[4] = {0ull, 0ull, 0ull, 0ull};  // packed partial row sums (ILP)
+      const uint64_t sl2 = f2pack(sl, sl), nm2 = f2pack(-mref, -mref);
 #pragma unroll
       for (int c = 0; c < 16; ++c) {  // 16 pieces of 8 keys, 16 bytes each
         uint32_t w4[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float x0 = __uint_as_float(s[8 * c + 2 * e]), x1 = __uint_as_float(s[8 * c + 2 * e + 1]);
+          const uint64_t s2 = f2pack(__uint_as_float(s[8 * c + 2 * e]), __uint_as_float(s[8 * c + 2 * e + 1]));
           float a, c2;
           if (SIGMOID) {
-            const float v0 = fast ? x0 * sl : x0, v1 = fast ? x1 * sl : x1;
+            float v0, v1;
+            f2unpack(fast ? ffma2(s2, sl2, 0ull) : s2, v0, v1);
             a = v0 == -INFINITY ? 0.f : __frcp_rn(1.f + fast_exp2(-v0));
             c2 = v1 == -INFINITY ? 0.f : __frcp_rn(1.f + fast_exp2(-v1));
           } else if (fast) {
-            a = fast_exp2(fmaf(x0, sl, -mref));
-            c2 = fast_exp2(fmaf(x1, sl, -mref));
+            // logits x*sl - m as one packed FMA; every fourth exp2 runs as a
+            // polynomial on the FMA pipe to relieve the MUFU pipe
+            float x0, x1;
+            f2unpack(ffma2(s2, sl2, nm2), x0, x1);
+            a = fast_exp2(x0);
+            c2 = fast_exp2(x1);
           } else {
-            a = fast_exp2(x0 - mref);
-            c2 = fast_exp2(x1 - mref);
+            float x0, x1;
+            f2unpack(fadd2(s2, nm2), x0, x1);
+            a = fast_exp2(x0);
+            c2 = fast_exp2(x1);
           }
-          rs4[e] += a + c2;
+          acc2[e] = fadd2(acc2[e], f2pack(a, c2));
           w4[e] = pack_bf16x2(a, c2);
         }
         *reinterpret_cast<uint4*>(pt + (c >> 3) * F::TILE + sw128(r, c & 7)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
       }
-      l = l * corr + ((rs4[0] + rs4[1]) + (rs4[2] + rs4[3]));
+      float r0, r1, r2, r3, r4, r5, r6, r7;
+      f2unpack(acc2[0], r0, r1);
+      f2unpack(acc2[1], r2, r3);
+      f2unpack(acc2[2], r4, r5);
+      f2unpack(acc2[3], r6, r7);
+      l = l * corr + (((r0 + r1) + (r2 + r3)) + ((r4 + r5) + (r6 + r7)));
       if (!SIGMOID && __any_sync(0xffffffffu, need)) {
 #pragma unroll
         for (int c = 0; c < HD / 32; ++c) {
