@@ -167,6 +167,33 @@ WELVET_API int64_t welvet_b200_launch_count(int32_t reset);
 WELVET_API void welvet_b200_profile_enable(int32_t on);
 WELVET_API void welvet_b200_profile_read(double ms[8], int64_t counts[8], int32_t reset);
 
+/* ---- decode attention without allocation (no counterpart in the reference) ----
+ * Split-KV decode attention of one new query per sequence over a paged KV cache,
+ * the same kernels as the decode step of welvet_b200_mha_decode, with the split
+ * partials in a fixed per-device array of WELVET_B200_DECODE_STATIC_FLOATS floats
+ * (4 MiB) instead of allocated memory: for callers that may not allocate device
+ * memory while decoding (a pre-reserved HBM pool; a captured stream region).
+ * All buffers are device memory; asynchronous on `stream`.
+ *   cfg         heads, KV heads, head_dim, scale, ALiBi / sigmoid, precision
+ *               (1: BF16 buffers, 0: FP32), head shard; causal mask only.
+ *   q           [batch, ldq], RoPE applied, the shard's heads from column 0.
+ *   k_pool/v_pool [page][kv_heads][16][head_dim]; block_table [batch, max_pages]
+ *               int32 page ids; ctx_len [batch] int32 keys per sequence
+ *               (including the new one), each in [1, max_ctx].
+ *   out         [batch, ldo].
+ * Needs batch*heads*(head_dim+2) <= WELVET_B200_DECODE_STATIC_FLOATS (else code 1,
+ * nothing launched); fewer KV splits are used when the default count does not fit.
+ * The array need not start at zero. Calls on one device share it: calls that
+ * overlap in time race, so issue them on one stream. The first call on a device
+ * does the set-up (symbol lookup, module loading): make it before stream capture. */
+#define WELVET_B200_DECODE_STATIC_FLOATS (1 << 20)
+WELVET_API welvet_status welvet_b200_decode_attention_static(const welvet_b200_mha_config* cfg, int32_t batch,
+                                                             int32_t max_ctx, const void* q, int32_t ldq,
+                                                             const void* k_pool, const void* v_pool,
+                                                             const int32_t* block_table, int32_t max_pages,
+                                                             const int32_t* ctx_len, void* out, int32_t ldo,
+                                                             void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -32,7 +32,8 @@ EXT_SYMBOLS = ("welvet_b200_mha_config_default", "welvet_b200_mha_mount", "welve
                "welvet_b200_fp8_rowscale_encode", "welvet_b200_fp8_rowscale_decode",
                "welvet_b200_nf4_block_encode", "welvet_b200_nf4_block_decode",
                "welvet_b200_fill_synthetic", "welvet_b200_device_check", "welvet_b200_launch_count",
-               "welvet_b200_profile_enable", "welvet_b200_profile_read")
+               "welvet_b200_profile_enable", "welvet_b200_profile_read",
+               "welvet_b200_decode_attention_static")
 PROFILE_SLOTS = ("gemm_qkv", "attn_prefill", "gemm_o", "attn_decode", "gemm_qkv_decode", "gemm_o_decode",
                  "allreduce", "other")
 
@@ -127,6 +128,8 @@ def lib():
     L.welvet_b200_profile_enable.restype = None
     L.welvet_b200_profile_read.argtypes = [C.POINTER(C.c_double), C.POINTER(C.c_int64), C.c_int32]
     L.welvet_b200_profile_read.restype = None
+    L.welvet_b200_decode_attention_static.argtypes = [cfgp, C.c_int32, C.c_int32, _vp, C.c_int32, _vp, _vp, _vp,
+                                                      C.c_int32, _vp, _vp, C.c_int32, _vp]
     for name in ("welvet_b200_mha_mount", "welvet_b200_mha_forward", "welvet_b200_mha_check",
                  "welvet_b200_kv_create", "welvet_b200_kv_fill", "welvet_b200_mha_prefill",
                  "welvet_b200_mha_decode", "welvet_b200_comm_unique_id", "welvet_b200_comm_attach",
@@ -134,7 +137,8 @@ def lib():
                  "welvet_b200_codec_roundtrip", "welvet_b200_codec_encode", "welvet_b200_codec_decode",
                  "welvet_b200_fp8_rowscale_encode", "welvet_b200_fp8_rowscale_decode",
                  "welvet_b200_nf4_block_encode", "welvet_b200_nf4_block_decode",
-                 "welvet_b200_fill_synthetic", "welvet_b200_device_check"):
+                 "welvet_b200_fill_synthetic", "welvet_b200_device_check",
+                 "welvet_b200_decode_attention_static"):
         getattr(L, name).restype = Status
     _LIB = L
     return L
