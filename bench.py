@@ -217,10 +217,11 @@ def main():
     B = args.batch or B
     T = args.seq or T
     hd = d // H
-    if H % world:
-        raise SystemExit(f"{H} heads do not shard over {world} GPUs")
-    hc = H // world
-    cfg = W.MhaConfig.make(d, H, NK, precision=1, weight_format=wf, head_begin=rank * hc, head_count=hc,
+    try:
+        hb, hc = W.head_shard(H, NK, world, rank)
+    except ValueError as e:
+        raise SystemExit(str(e))
+    cfg = W.MhaConfig.make(d, H, NK, precision=1, weight_format=wf, head_begin=hb, head_count=hc,
                            device=local)
     # Full FP32 weights generated on the device (same stream on every rank), then mounted.
     shapes = [(H * hd, d), (NK * hd, d), (NK * hd, d), (d, H * hd)]

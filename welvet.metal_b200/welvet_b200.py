@@ -408,6 +408,22 @@ def synthetic(n: int, seed: int, kind: int, a: float, offset: int = 0) -> np.nda
     return v.astype(np.float32)
 
 
+def head_shard(num_heads: int, num_kv_heads: int, world: int, rank: int) -> tuple[int, int]:
+    """(head_begin, head_count) of `rank` when `world` GPUs split one layer by heads:
+    equal contiguous blocks of whole KV groups, as mha_mount requires. Each rank then
+    holds the Wq/Wk/Wv rows and the Wo columns of its heads; the per-rank outputs of
+    the O projection sum to the layer output (one all-reduce)."""
+    nk = num_kv_heads if num_kv_heads > 0 else num_heads
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError("head_shard: need 0 <= rank < world")
+    if num_heads % nk or num_heads % world:
+        raise ValueError(f"head_shard: {num_heads} heads do not split over {world} ranks")
+    hc = num_heads // world
+    if hc % (num_heads // nk):
+        raise ValueError(f"head_shard: {hc} heads per rank do not cover whole KV groups of {num_heads // nk}")
+    return rank * hc, hc
+
+
 def xavier_weights(d_model: int, q_dim: int, kv_dim: int, seed: int = 0):
     """Wq [qd,d], Wk/Wv [kd,d], Wo [d,qd], Xavier-uniform a = sqrt(6/(fan_in+fan_out)),
     drawn in this order from one counter stream (seed 0 by default)."""
