@@ -43,6 +43,21 @@ WORKLOADS = {
 }
 
 
+METRIC = "MHA prefill tok/s (BASELINE config 5; decode tok/s under 'decode')"
+
+
+def workload_config(args, world):
+    """The `config` object of the JSON line, the same for both arms."""
+    B, T, d, H, NK, wf = WORKLOADS[args.workload]
+    B = args.batch or B
+    T = args.seq or T
+    hd = d // H
+    return {"workload": f"{args.workload}: B={B} T={T} d={d} H={H}x{hd} NK={NK} causal RoPE"
+                        f"{' fp8 weights' if wf == 1 else ' nf4 weights' if wf == 2 else ''}",
+            "global_batch": B, "seq_len": T, "parallelism": f"tp{world} (heads {H // world}/GPU)",
+            "l2": "inputs larger than L2 (x is %.1f GB)" % (B * T * d * 2 / 1e9)}
+
+
 def peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -171,10 +186,10 @@ def run_reference(args):
     cores = os.cpu_count()
     sample = (f"1 sequence x {T_r} tokens of the {args.workload} layer (d={d}, {H}x{hd}) per step, FP32 "
               f"reference semantics; tok/s scaled by algorithmic FLOPs/token of the full workload")
-    line = {"impl": "reference", "metric": "MHA prefill tok/s", "value": value, "unit": "tok/s",
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64 (soft-double)",
-            "data": "synthetic", "config": {"workload": args.workload},
+            "data": "synthetic", "config": workload_config(args, args.gpus),
             "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": kind, "sample": sample},
             "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     del np
@@ -377,14 +392,11 @@ def main():
                          f"{dt:.1f} s; tok/s scaled by algorithmic FLOPs/token of the full workload"}
 
     if rank == 0:
-        line = {"metric": "MHA prefill tok/s (BASELINE config 5; decode tok/s under 'decode')",
+        line = {"metric": METRIC,
                 "value": tokps, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
                 "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
                 "dtype": "bf16", "data": "synthetic (SplitMix64 counter stream: Xavier weights seed 0, N(0,1) x seed 1)",
-                "config": {"workload": f"{args.workload}: B={B} T={T} d={d} H={H}x{hd} NK={NK} causal RoPE"
-                                       f"{' fp8 weights' if wf == 1 else ' nf4 weights' if wf == 2 else ''}",
-                           "global_batch": B, "seq_len": T, "parallelism": f"tp{world} (heads {hc}/GPU)",
-                           "l2": "inputs larger than L2 (x is %.1f GB)" % (M * d * 2 / 1e9)},
+                "config": workload_config(args, world),
                 "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "clocks": clk,
                 "decode": decode, "profile_ms": {k: v[0] / args.steps for k, v in prof.items() if v[1]}}
         print(json.dumps(line), flush=True)
