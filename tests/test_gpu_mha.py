@@ -206,3 +206,38 @@ def test_head_shards_sum_to_full_layer(torch_cuda):
         acc += p
     torch.cuda.synchronize()
     assert rel_err(acc.cpu().numpy(), post.cpu().numpy()) < 1e-5
+
+
+@pytest.mark.parametrize("precision", [0, 1])
+def test_chunked_forward_with_communicator(torch_cuda, precision):
+    """With a communicator attached (one rank here) the layer runs the batch in chunks
+    whose all-reduce overlaps the next chunk's compute. Every row is computed by the
+    same kernels over the same K loop, so the output equals the unchunked layer bit
+    for bit; the host-buffer path stages pre and post of every chunk."""
+    torch = torch_cuda
+    d, H, NK, B, T = 256, 4, 2, 6, 96
+    Ws = W.xavier_weights(d, d, NK * d // H, seed=0)
+    dt = torch.float32 if precision == 0 else torch.bfloat16
+    x = torch.from_numpy(W.synthetic(B * T * d, 1, 1, 1.0).reshape(B * T, d)).cuda().to(dt)
+    cfg = W.MhaConfig.make(d, H, NK, precision=precision)
+    plain = W.MhaLayer(cfg, *Ws)
+    chunked = W.MhaLayer(cfg, *Ws)
+    chunked.attach_comm(W.comm_unique_id(), 1, 0)
+    outs = []
+    for layer in (plain, chunked):
+        pre = torch.zeros(B * T, d, device="cuda", dtype=dt)
+        post = torch.zeros(B * T, d, device="cuda", dtype=dt)
+        layer.forward(B, T, x, pre, post)
+        torch.cuda.synchronize()
+        outs.append((pre.float().cpu().numpy(), post.float().cpu().numpy()))
+    assert np.array_equal(outs[0][0], outs[1][0])
+    assert np.array_equal(outs[0][1], outs[1][1])
+    xh = x.cpu()
+    pre_h = torch.zeros(B * T, d, dtype=dt)
+    post_h = torch.zeros(B * T, d, dtype=dt)
+    chunked.forward(B, T, xh, pre_h, post_h)
+    assert np.array_equal(pre_h.float().numpy(), outs[0][0])
+    assert np.array_equal(post_h.float().numpy(), outs[0][1])
+    chunked.check_device()
+    chunked.close()
+    plain.close()

@@ -76,6 +76,9 @@ Status comm_attach(Mha* m, const uint8_t id[128], int nranks, int rank) {
   m->comm = c;
   m->nranks = nranks;
   m->rank = rank;
+  WV_CUDA(cudaStreamCreateWithFlags(&m->comm_stream, cudaStreamNonBlocking), "comm stream");
+  for (auto& e : m->chunk_done) WV_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "chunk event");
+  WV_CUDA(cudaEventCreateWithFlags(&m->comm_done, cudaEventDisableTiming), "comm event");
   return Status::ok();
 }
 
@@ -88,12 +91,21 @@ Status comm_allreduce(Mha* m, void* buf, size_t count, bool bf16, cudaStream_t s
 }
 
 void comm_release(Mha* m) {
-  if (m && m->comm) {
+  if (!m) return;
+  if (m->comm) {
     if (nccl().ok) nccl().comm_destroy(static_cast<ncclComm_t>(m->comm));
     m->comm = nullptr;
     m->nranks = 1;
     m->rank = 0;
   }
+  for (auto& e : m->chunk_done) {
+    if (e) cudaEventDestroy(e);
+    e = nullptr;
+  }
+  if (m->comm_done) cudaEventDestroy(m->comm_done);
+  m->comm_done = nullptr;
+  if (m->comm_stream) cudaStreamDestroy(m->comm_stream);
+  m->comm_stream = nullptr;
 }
 
 } // namespace wv

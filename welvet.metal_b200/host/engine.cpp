@@ -538,100 +538,138 @@ Status mha_forward(Mha* m, int batch, int seq, const void* x, void* pre, void* p
     xd = m->x_io.p;
     postd = m->post_io.p;
     pred = nullptr;
+    if (pre) {  // attention output of every chunk lands here, copied back below
+      WV_TRY(m->pre_io.ensure(M * m->qd_l * es));
+      pred = m->pre_io.p;
+    }
   }
-  WV_TRY(m->qkv.ensure(M * m->nqkv * es));
-  void* attn = pred;
-  if (!attn) {
-    WV_TRY(m->attn.ensure(M * m->qd_l * es));
-    attn = m->attn.p;
+  // With a communicator attached and independent sequences (per-sequence mode, no
+  // KV prefill), the batch runs in chunks: the all-reduce of chunk i (comm_stream)
+  // overlaps the projections and attention of chunk i+1 (stream s).
+  const int chunks = (m->comm && !stream_mode && !kv) ? std::min(batch, Mha::kMaxChunks / 2) : 1;
+  const int bc_max = (batch + chunks - 1) / chunks;
+  const int64_t Mc_max = (int64_t)bc_max * seq;
+  WV_TRY(m->qkv.ensure(Mc_max * m->nqkv * es));
+  if (!pred) WV_TRY(m->attn.ensure(Mc_max * m->qd_l * es));
+  if (f32) {
+    WV_TRY(m->x_hi.ensure(Mc_max * dm * 4));
+    WV_TRY(m->x_lo.ensure(Mc_max * dm * 4));
+    WV_TRY(m->attn_hi.ensure(Mc_max * m->qd_l * 4));
+    WV_TRY(m->attn_lo.ensure(Mc_max * m->qd_l * 4));
   }
   // RoPE positions: stream mode -> row index (global position), else row % seq.
   const int max_pos = stream_mode ? (int)M : seq;
   WV_TRY(ensure_rope(m, max_pos, s));
 
-  Proj q;
-  q.M = (int)M;
-  q.K = dm;
-  q.lda = dm;
-  q.N = m->nqkv;
-  q.out = m->qkv.p;
-  q.ldo = m->nqkv;
-  q.rope_cols = m->qd_l + m->kd_l;
-  q.pos_mod = stream_mode ? 0 : seq;
-  q.w = m->wqkv.p;
-  q.w_lo = m->wqkv_lo.p;
-  q.w_scale = m->wqkv_scale.as<float>();
-  if (f32) {
-    WV_TRY(m->x_hi.ensure(M * dm * 4));
-    WV_TRY(m->x_lo.ensure(M * dm * 4));
-    WV_CUDA(split_tf32(static_cast<const float*>(xd), m->x_hi.as<float>(), m->x_lo.as<float>(), M * dm, s), "split x");
-    count_launch();
-    q.a = m->x_hi.p;
-    q.a_lo = m->x_lo.p;
-  } else {
-    q.a = xd;
-  }
-  prof_begin(kProfGemmQkv, s);
-  WV_TRY(run_proj(m, q, s));
-  prof_end(kProfGemmQkv, s);
+  // QKV projection, attention and O projection of sequences [b0, b0 + bc).
+  auto run_rows = [&](int b0, int bc) -> Status {
+    const int64_t r0 = (int64_t)b0 * seq, Mc = (int64_t)bc * seq;
+    const void* xc = static_cast<const char*>(xd) + r0 * dm * es;
+    void* attn = pred ? static_cast<void*>(static_cast<char*>(pred) + r0 * m->qd_l * es) : m->attn.p;
+    Proj q;
+    q.M = (int)Mc;
+    q.K = dm;
+    q.lda = dm;
+    q.N = m->nqkv;
+    q.out = m->qkv.p;
+    q.ldo = m->nqkv;
+    q.rope_cols = m->qd_l + m->kd_l;
+    q.pos_mod = stream_mode ? 0 : seq;
+    q.w = m->wqkv.p;
+    q.w_lo = m->wqkv_lo.p;
+    q.w_scale = m->wqkv_scale.as<float>();
+    if (f32) {
+      WV_CUDA(split_tf32(static_cast<const float*>(xc), m->x_hi.as<float>(), m->x_lo.as<float>(), Mc * dm, s),
+              "split x");
+      count_launch();
+      q.a = m->x_hi.p;
+      q.a_lo = m->x_lo.p;
+    } else {
+      q.a = xc;
+    }
+    prof_begin(kProfGemmQkv, s);
+    WV_TRY(run_proj(m, q, s));
+    prof_end(kProfGemmQkv, s);
 
-  if (kv) {  // prefill: K/V rows into the cache pages of each sequence
-    WV_TRY(m->slots.ensure(M * 4));
-    WV_CUDA(make_prefill_slots(m->slots.as<int>(), batch, seq, kv->pages_per_seq, s), "slots");
+    if (kv) {  // prefill: K/V rows into the cache pages of each sequence (single chunk)
+      WV_TRY(m->slots.ensure(M * 4));
+      WV_CUDA(make_prefill_slots(m->slots.as<int>(), batch, seq, kv->pages_per_seq, s), "slots");
+      const char* base = static_cast<const char*>(m->qkv.p);
+      WV_CUDA(kv_append(base + (size_t)m->qd_l * es, base + (size_t)(m->qd_l + m->kd_l) * es, m->nqkv, (int)M,
+                        m->kd_l, c.hd, f32 ? 0 : 1, m->slots.as<int>(), kv->k_pool.p, kv->v_pool.p, s),
+              "kv append");
+      WV_CUDA(set_ctx(kv->ctx_len.as<int>(), batch, seq, s), "ctx");
+      count_launch(3);
+      for (int b = 0; b < batch; ++b) kv->ctx_host[b] = seq;
+    }
+
+    AttnArgs a = attn_args(m, bc, seq, stream_mode);
     const char* base = static_cast<const char*>(m->qkv.p);
-    WV_CUDA(kv_append(base + (size_t)m->qd_l * es, base + (size_t)(m->qd_l + m->kd_l) * es, m->nqkv, (int)M,
-                      m->kd_l, c.hd, f32 ? 0 : 1, m->slots.as<int>(), kv->k_pool.p, kv->v_pool.p, s), "kv append");
-    WV_CUDA(set_ctx(kv->ctx_len.as<int>(), batch, seq, s), "ctx");
-    count_launch(3);
-    for (int b = 0; b < batch; ++b) kv->ctx_host[b] = seq;
-  }
+    a.q = base;
+    a.k = base + (size_t)m->qd_l * es;
+    a.v = base + (size_t)(m->qd_l + m->kd_l) * es;
+    a.ldq = a.ldk = m->nqkv;
+    a.out = attn;
+    a.ldo = m->qd_l;
+    if (f32) {
+      a.out_hi = m->attn_hi.as<float>();
+      a.out_lo = m->attn_lo.as<float>();
+    }
+    prof_begin(kProfAttnPrefill, s);
+    WV_TRY(run_attention(m, a, s));
+    prof_end(kProfAttnPrefill, s);
 
-  AttnArgs a = attn_args(m, batch, seq, stream_mode);
-  const char* base = static_cast<const char*>(m->qkv.p);
-  a.q = base;
-  a.k = base + (size_t)m->qd_l * es;
-  a.v = base + (size_t)(m->qd_l + m->kd_l) * es;
-  a.ldq = a.ldk = m->nqkv;
-  a.out = attn;
-  a.ldo = m->qd_l;
-  if (f32) {
-    WV_TRY(m->attn_hi.ensure(M * m->qd_l * 4));
-    WV_TRY(m->attn_lo.ensure(M * m->qd_l * 4));
-    a.out_hi = m->attn_hi.as<float>();
-    a.out_lo = m->attn_lo.as<float>();
-  }
-  prof_begin(kProfAttnPrefill, s);
-  WV_TRY(run_attention(m, a, s));
-  prof_end(kProfAttnPrefill, s);
+    Proj o;
+    o.M = (int)Mc;
+    o.K = m->qd_l;
+    o.lda = m->qd_l;
+    o.N = dm;
+    o.out = static_cast<char*>(postd) + r0 * dm * es;
+    o.ldo = dm;
+    o.w = m->wo.p;
+    o.w_lo = m->wo_lo.p;
+    o.w_scale = m->wo_scale.as<float>();
+    if (f32) {
+      o.a = m->attn_hi.p;
+      o.a_lo = m->attn_lo.p;
+    } else {
+      o.a = attn;
+    }
+    prof_begin(kProfGemmO, s);
+    WV_TRY(run_proj(m, o, s));
+    prof_end(kProfGemmO, s);
+    return Status::ok();
+  };
 
-  Proj o;
-  o.M = (int)M;
-  o.K = m->qd_l;
-  o.lda = m->qd_l;
-  o.N = dm;
-  o.out = postd;
-  o.ldo = dm;
-  o.w = m->wo.p;
-  o.w_lo = m->wo_lo.p;
-  o.w_scale = m->wo_scale.as<float>();
-  if (f32) {
-    o.a = m->attn_hi.p;
-    o.a_lo = m->attn_lo.p;
+  if (chunks == 1) {
+    WV_TRY(run_rows(0, batch));
+    if (m->comm) {
+      prof_begin(kProfAllReduce, s);
+      WV_TRY(comm_allreduce(m, postd, (size_t)M * dm, !f32, s));
+      prof_end(kProfAllReduce, s);
+    }
   } else {
-    o.a = attn;
-  }
-  prof_begin(kProfGemmO, s);
-  WV_TRY(run_proj(m, o, s));
-  prof_end(kProfGemmO, s);
-  if (m->comm) {
-    prof_begin(kProfAllReduce, s);
-    WV_TRY(comm_allreduce(m, postd, (size_t)M * dm, !f32, s));
-    prof_end(kProfAllReduce, s);
+    // The comm stream first waits for what s did before this call (H2D of x, the
+    // previous forward's readers of post).
+    WV_CUDA(cudaEventRecord(m->chunk_done[0], s), "event");
+    WV_CUDA(cudaStreamWaitEvent(m->comm_stream, m->chunk_done[0], 0), "wait");
+    for (int i = 0, b0 = 0; i < chunks && b0 < batch; ++i, b0 += bc_max) {
+      const int bc = std::min(bc_max, batch - b0);
+      WV_TRY(run_rows(b0, bc));
+      WV_CUDA(cudaEventRecord(m->chunk_done[i], s), "event");
+      WV_CUDA(cudaStreamWaitEvent(m->comm_stream, m->chunk_done[i], 0), "wait");
+      prof_begin(kProfAllReduce, m->comm_stream);
+      WV_TRY(comm_allreduce(m, static_cast<char*>(postd) + (int64_t)b0 * seq * dm * es, (size_t)bc * seq * dm,
+                            !f32, m->comm_stream));
+      prof_end(kProfAllReduce, m->comm_stream);
+    }
+    WV_CUDA(cudaEventRecord(m->comm_done, m->comm_stream), "event");
+    WV_CUDA(cudaStreamWaitEvent(s, m->comm_done, 0), "wait");
   }
 
   if (!on_device) {
     WV_CUDA(cudaMemcpyAsync(post, postd, M * dm * es, cudaMemcpyDeviceToHost, s), "D2H post");
-    if (pre) WV_CUDA(cudaMemcpyAsync(pre, attn, M * m->qd_l * es, cudaMemcpyDeviceToHost, s), "D2H pre");
+    if (pre) WV_CUDA(cudaMemcpyAsync(pre, pred, M * m->qd_l * es, cudaMemcpyDeviceToHost, s), "D2H pre");
     WV_CUDA(cudaStreamSynchronize(s), "forward");
     WV_TRY(check_device_error(m->dev));
   }

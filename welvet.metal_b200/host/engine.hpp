@@ -133,9 +133,14 @@ struct Mha {
   // workspaces
   DevBuf x_io, pre_io, post_io, x_hi, x_lo, qkv, attn, attn_hi, attn_lo, post_tmp;
   DevBuf positions, slots;
-  // communicator (head-sharded tensor parallelism)
+  // communicator (head-sharded tensor parallelism); the all-reduce of a forward
+  // chunk runs on comm_stream while the next chunk computes on the caller's stream
   void* comm = nullptr;
   int nranks = 1, rank = 0;
+  cudaStream_t comm_stream = nullptr;
+  static constexpr int kMaxChunks = 8;
+  cudaEvent_t chunk_done[kMaxChunks] = {};
+  cudaEvent_t comm_done = nullptr;
   std::mutex mu;  // one call at a time per layer (reference: per-session lock)
   ~Mha();
 };
