@@ -5,18 +5,23 @@ decode tok/s at 1/2/4/8 B200; % of roofline".
 Default workload = BASELINE config 5 (the metric's 1/2/4/8-GPU configuration):
 batch 32 x seq 8192, d_model 4096, 32 heads x 128, causal, RoPE, BF16 activations
 and weights, FP32 accumulation. Heads are sharded 32/N per GPU, the output
-projection is row-sharded and summed with one NCCL all-reduce. A step = one
-prefill forward over all 262144 tokens; value = whole-job prefill tok/s. After the
-timed prefill, 256 autoregressive decode steps run against the resulting KV cache
-and are reported under "decode".
+projection is row-sharded and summed with NCCL all-reduce. A step = one prefill
+forward over all 262144 tokens; value = whole-job prefill tok/s. After the timed
+prefill, 256 autoregressive decode steps run against the resulting KV cache and are
+reported under "decode".
+
+Other workloads (`--workload`): cfg2 (FP32 prefill, 3xTF32 projections), cfg3
+(decode only: 64 sequences over a 4096-token KV cache, GQA 32/8 x 64; a step = one
+decode step), cfg4-fp8 / cfg4-nf4 (quantised-weight prefill).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
   torchrun --nproc-per-node N bench.py --gpus N ...      (N > 1)
 
 Data is synthetic (no dataset is named by the baseline): the counter-based
 SplitMix64 stream of welvet_b200_fill_synthetic — Xavier-uniform weights (seed 0,
-order Wq, Wk, Wv, Wo), N(0,1) inputs (seed 1). Inputs (x: 2.1 GB) exceed L2
-(126 MB), so no explicit flush is needed between steps.
+order Wq, Wk, Wv, Wo; N(0, 0.02) for the quantised configs), N(0,1) inputs (seed 1),
+KV cache N(0,1)*0.5 (seed 2). Inputs (config 5 x: 2.1 GB; config 3 KV cache:
+1.1 GB) exceed L2 (126 MB), so no explicit flush is needed between steps.
 """
 from __future__ import annotations
 
@@ -34,28 +39,41 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "welvet.metal_b200"))
 sys.path.insert(0, os.path.join(ROOT, "oracle"))
 
+# B, T (sequence or cached context), d_model, heads, kv heads, weight format
+# (0 BF16/FP32, 1 FP8-E4M3 row scale, 2 NF4 block-64), precision (1 BF16, 0 FP32), kind
 WORKLOADS = {
-    # name: (batch, seq, d_model, heads, kv_heads, weight_format)
-    "cfg5": (32, 8192, 4096, 32, 32, 0),
-    "cfg4-fp8": (4, 4096, 4096, 32, 32, 1),
-    "cfg4-nf4": (4, 4096, 4096, 32, 32, 2),
-    "cfg2": (8, 2048, 1024, 16, 16, 0),
+    "cfg5": dict(B=32, T=8192, d=4096, H=32, NK=32, wf=0, prec=1, kind="prefill+decode"),
+    "cfg4-fp8": dict(B=4, T=4096, d=4096, H=32, NK=32, wf=1, prec=1, kind="prefill"),
+    "cfg4-nf4": dict(B=4, T=4096, d=4096, H=32, NK=32, wf=2, prec=1, kind="prefill"),
+    "cfg3": dict(B=64, T=4096, d=2048, H=32, NK=8, wf=0, prec=1, kind="decode"),
+    "cfg2": dict(B=8, T=2048, d=1024, H=16, NK=16, wf=0, prec=0, kind="prefill"),
 }
 
-
 METRIC = "MHA prefill tok/s (BASELINE config 5; decode tok/s under 'decode')"
+METRIC_DECODE = "MHA decode tok/s (BASELINE config 3)"
+
+
+def workload(args):
+    w = dict(WORKLOADS[args.workload])
+    w["B"] = args.batch or w["B"]
+    w["T"] = args.seq or w["T"]
+    w["hd"] = w["d"] // w["H"]
+    return w
 
 
 def workload_config(args, world):
     """The `config` object of the JSON line, the same for both arms."""
-    B, T, d, H, NK, wf = WORKLOADS[args.workload]
-    B = args.batch or B
-    T = args.seq or T
-    hd = d // H
-    return {"workload": f"{args.workload}: B={B} T={T} d={d} H={H}x{hd} NK={NK} causal RoPE"
-                        f"{' fp8 weights' if wf == 1 else ' nf4 weights' if wf == 2 else ''}",
+    w = workload(args)
+    B, T, d, H, NK, hd, wf = w["B"], w["T"], w["d"], w["H"], w["NK"], w["hd"], w["wf"]
+    fmt = " fp8 weights" if wf == 1 else " nf4 weights" if wf == 2 else ""
+    es = 2 if w["prec"] == 1 else 4
+    if w["kind"] == "decode":
+        return {"workload": f"{args.workload}: decode B={B} context {T} d={d} H={H}x{hd} NK={NK} RoPE{fmt}",
+                "global_batch": B, "seq_len": 1, "context": T, "parallelism": f"tp{world} (heads {H // world}/GPU)",
+                "l2": "KV cache larger than L2 (%.1f GB)" % (2 * B * T * NK * hd * es / 1e9)}
+    return {"workload": f"{args.workload}: B={B} T={T} d={d} H={H}x{hd} NK={NK} causal RoPE{fmt}",
             "global_batch": B, "seq_len": T, "parallelism": f"tp{world} (heads {H // world}/GPU)",
-            "l2": "inputs larger than L2 (x is %.1f GB)" % (B * T * d * 2 / 1e9)}
+            "l2": "inputs larger than L2 (x is %.1f GB)" % (B * T * d * es / 1e9)}
 
 
 def peaks():
@@ -127,14 +145,12 @@ def flops_prefill(B, T, d, H, NK, hd):
     return proj, attn
 
 
-def cpu_sample(d, H, NK, T_s, threads=0):
+def cpu_sample(w, T_s, threads=0):
     """Times the FP64 oracle (multithreaded C++) on one sequence of T_s tokens of the
     workload's layer shape; returns (seconds, flops)."""
-    import numpy as np
-
     import oracle_py as O
     import welvet_b200 as W
-    hd = d // H
+    d, H, NK, hd = w["d"], w["H"], w["NK"], w["hd"]
     Ws = W.xavier_weights(d, H * hd, NK * hd, seed=0)
     x = W.synthetic(T_s * d, 1, 1, 1.0).reshape(T_s, d)
     cfg = O.MhaCfg(d_model=d, num_heads=H, num_kv_heads=NK, max_seq_len=T_s, per_sequence=1)
@@ -142,8 +158,23 @@ def cpu_sample(d, H, NK, T_s, threads=0):
     O.mha_forward(cfg, 1, T_s, *Ws, x, threads=threads)
     dt = time.perf_counter() - t0
     pf, af = flops_prefill(1, T_s, d, H, NK, hd)
-    del np
     return dt, pf + af
+
+
+def cpu_sample_decode(w, B_s, threads=0):
+    """Times the FP64 oracle's decode step for B_s sequences over the workload's
+    context; returns seconds."""
+    import oracle_py as O
+    import welvet_b200 as W
+    d, H, NK, hd, T = w["d"], w["H"], w["NK"], w["hd"], w["T"]
+    Ws = W.xavier_weights(d, H * hd, NK * hd, seed=0)
+    kc = W.synthetic(B_s * T * NK * hd, 2, 1, 0.5).reshape(B_s, T, NK * hd)
+    vc = W.synthetic(B_s * T * NK * hd, 2, 1, 0.5, offset=B_s * T * NK * hd).reshape(B_s, T, NK * hd)
+    x = W.synthetic(B_s * d, 1, 1, 1.0).reshape(B_s, d)
+    cfg = O.MhaCfg(d_model=d, num_heads=H, num_kv_heads=NK, max_seq_len=T + 1, per_sequence=1)
+    t0 = time.perf_counter()
+    O.mha_decode(cfg, [T] * B_s, kc, vc, *Ws, x, threads=threads)
+    return time.perf_counter() - t0
 
 
 def run_reference(args):
@@ -153,12 +184,14 @@ def run_reference(args):
     bounded sample (1 sequence x T_r tokens of the workload's layer shape), scaled to the
     workload's tok/s by algorithmic FLOPs per token. Falls back to the FP64 port when
     oracle/_ref was not built."""
-    import numpy as np
-
     import oracle_py as O
     import welvet_b200 as W
-    B, T, d, H, NK, wf = WORKLOADS[args.workload]
-    hd = d // H
+    w = workload(args)
+    if w["kind"] == "decode":
+        print(json.dumps({"impl": "reference", "unavailable": "the reference MHA has no KV cache or decode step"}),
+              flush=True)
+        return
+    B, T, d, H, NK, hd = w["B"], w["T"], w["d"], w["H"], w["NK"], w["hd"]
     pf, af = flops_prefill(B, T, d, H, NK, hd)
     flops_per_tok = (pf + af) / (B * T)
     Ws = W.xavier_weights(d, H * hd, NK * hd, seed=0)
@@ -192,7 +225,6 @@ def run_reference(args):
             "data": "synthetic", "config": workload_config(args, args.gpus),
             "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": kind, "sample": sample},
             "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    del np
     print(json.dumps(line), flush=True)
 
 
@@ -204,7 +236,7 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--workload", default="cfg5", choices=sorted(WORKLOADS))
     ap.add_argument("--batch", type=int, default=0, help="override batch (small ncu cases)")
-    ap.add_argument("--seq", type=int, default=0, help="override seq")
+    ap.add_argument("--seq", type=int, default=0, help="override seq (decode workloads: context)")
     ap.add_argument("--decode-steps", type=int, default=256)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
@@ -233,15 +265,17 @@ def main():
         os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
-    B, T, d, H, NK, wf = WORKLOADS[args.workload]
-    B = args.batch or B
-    T = args.seq or T
-    hd = d // H
+    w = workload(args)
+    B, T, d, H, NK, hd, wf, prec = w["B"], w["T"], w["d"], w["H"], w["NK"], w["hd"], w["wf"], w["prec"]
+    decode_only = w["kind"] == "decode"
+    act = torch.bfloat16 if prec == 1 else torch.float32
+    es = 2 if prec == 1 else 4
     try:
         hb, hc = W.head_shard(H, NK, world, rank)
     except ValueError as e:
         raise SystemExit(str(e))
-    cfg = W.MhaConfig.make(d, H, NK, precision=1, weight_format=wf, head_begin=hb, head_count=hc,
+    kd_l = (hc // (H // NK)) * hd  # this rank's KV columns
+    cfg = W.MhaConfig.make(d, H, NK, precision=prec, weight_format=wf, head_begin=hb, head_count=hc,
                            device=local)
     # Full FP32 weights generated on the device (same stream on every rank), then mounted.
     shapes = [(H * hd, d), (NK * hd, d), (NK * hd, d), (d, H * hd)]
@@ -260,12 +294,8 @@ def main():
         uid = [W.comm_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
         layer.attach_comm(uid[0], world, rank)
-
-    M = B * T
-    x = torch.empty(M, d, device="cuda", dtype=torch.bfloat16)
-    W.fill_synthetic(x, 1, 1, 1.0)
-    post = torch.empty(M, d, device="cuda", dtype=torch.bfloat16)
     stream = torch.cuda.current_stream()
+    pk = peaks()
 
     def barrier():
         if world > 1:
@@ -279,134 +309,189 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    for _ in range(args.warmup):
-        layer.forward(B, T, x, None, post, stream=stream)
-    barrier()
-    layer.check_device()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    M = B * T
+    x = None
+    tokps = ms = None
+    roof = e2e = cpu = None
+    launches = 0
+    clk = {}
+    prof = {}
 
     # ------------------------------------------------------------ timed prefill
-    clocks = Clocks(local)
-    clocks.start()
-    W.profile_read(reset=True)
-    W.profile_enable(True)
-    W.launch_count(reset=True)
-    barrier()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev0.record(stream)
-    for _ in range(args.steps):
-        layer.forward(B, T, x, None, post, stream=stream)
-    ev1.record(stream)
-    barrier()
-    launches = W.launch_count(reset=True)
-    W.profile_enable(False)
-    prof = W.profile_read(reset=True)
-    clk = clocks.stop()
-    layer.check_device()
-    ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps)
-    tokps = M / (ms / 1e3)
-
-    pk = peaks()
-    pf, af = flops_prefill(B, T, d, H, NK, hd)
-    kd_l = (hc // (H // NK)) * hd  # this rank's KV columns
-    per_step = {"gemm_qkv": 2.0 * M * d * (hc * hd + 2 * kd_l),
-                "attn_prefill": 4.0 * hd * hc * B * T * (T + 1) / 2,
-                "gemm_o": 2.0 * M * hc * hd * d}
-    shares = {k: prof[k][0] for k in per_step}
-    dom = max(shares, key=shares.get)
-    tot, cnt = prof[dom]
-    avg_ms = tot / max(cnt, 1)
-    # with a communicator the batch runs in chunks: several launches per step
-    flops_launch = per_step[dom] * args.steps / max(cnt, 1)
-    achieved = flops_launch / (avg_ms / 1e3) / 1e12
-    roof = {"bound": "tensor", "kernel": dom, "achieved": achieved, "peak": pk["bf16_sus"], "unit": "TFLOP/s",
-            "frac": achieved / pk["bf16_sus"], "peak_kind": f"{pk['src']} sustained bf16 (of {pk['src']})",
-            "traffic": None, "flops_per_launch": flops_launch, "avg_launch_ms": avg_ms,
-            "launches_per_step": cnt / args.steps,
-            "kernel_ms_per_step": {k: prof[k][0] / args.steps for k in per_step},
-            "step_tflops": (pf + af) / world / (ms / 1e3) / 1e12}
-
-    # ---------------------------------------------------------------- e2e
-    e2e = None
-    if not args.no_e2e:
-        xh = x.cpu().pin_memory()
-        ph = torch.empty(M, d, dtype=torch.bfloat16).pin_memory()
-        layer.forward(B, T, xh, None, ph)  # warm the staging buffers
+    if not decode_only:
+        x = torch.empty(M, d, device="cuda", dtype=act)
+        W.fill_synthetic(x, 1, 1, 1.0)
+        post = torch.empty(M, d, device="cuda", dtype=act)
+        for _ in range(args.warmup):
+            layer.forward(B, T, x, None, post, stream=stream)
         barrier()
-        t0 = time.perf_counter()
-        ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        ea.record(stream)
-        n_e2e = max(1, min(args.steps, 3))
-        for _ in range(n_e2e):
-            layer.forward(B, T, xh, None, ph)  # H2D x, forward, D2H post, synchronise
-        eb.record(stream)
+        layer.check_device()
+
+        clocks = Clocks(local)
+        clocks.start()
+        W.profile_read(reset=True)
+        W.profile_enable(True)
+        W.launch_count(reset=True)
         barrier()
-        e_ms = max_over_ranks(max(ea.elapsed_time(eb), (time.perf_counter() - t0) * 1e3) / n_e2e)
-        e2e = {"value": M / (e_ms / 1e3), "unit": "tok/s", "ms_per_step": e_ms, "h2d_bytes_per_step": M * d * 2,
-               "d2h_bytes_per_step": M * d * 2, "api": "welvet_b200_mha_forward (host buffers, pinned)"}
-        del xh, ph
+        ev0.record(stream)
+        for _ in range(args.steps):
+            layer.forward(B, T, x, None, post, stream=stream)
+        ev1.record(stream)
+        barrier()
+        launches = W.launch_count(reset=True)
+        W.profile_enable(False)
+        prof = W.profile_read(reset=True)
+        clk = clocks.stop()
+        layer.check_device()
+        ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps)
+        tokps = M / (ms / 1e3)
+
+        pf, af = flops_prefill(B, T, d, H, NK, hd)
+        per_step = {"gemm_qkv": 2.0 * M * d * (hc * hd + 2 * kd_l),
+                    "attn_prefill": 4.0 * hd * hc * B * T * (T + 1) / 2,
+                    "gemm_o": 2.0 * M * hc * hd * d}
+        shares = {k: prof[k][0] for k in per_step}
+        dom = max(shares, key=shares.get)
+        tot, cnt = prof[dom]
+        avg_ms = tot / max(cnt, 1)
+        # with a communicator the batch runs in chunks: several launches per step
+        flops_launch = per_step[dom] * args.steps / max(cnt, 1)
+        achieved = flops_launch / (avg_ms / 1e3) / 1e12
+        if prec == 0 and dom == "attn_prefill":
+            # FP32 attention runs on the CUDA cores (FFMA): 148 SMs x 128 lanes x 2 x 1.965 GHz
+            peak, pkind = 148 * 128 * 2 * 1.965e9 / 1e12, "nominal FP32 FFMA peak (CUDA cores)"
+        else:
+            peak, pkind = pk["bf16_sus"], f"{pk['src']} sustained bf16 (of {pk['src']})"
+        roof = {"bound": "tensor" if peak == pk["bf16_sus"] else "fp32-fma", "kernel": dom, "achieved": achieved,
+                "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak, "peak_kind": pkind,
+                "traffic": None, "flops_per_launch": flops_launch, "avg_launch_ms": avg_ms,
+                "launches_per_step": cnt / args.steps,
+                "kernel_ms_per_step": {k: prof[k][0] / args.steps for k in per_step},
+                "step_tflops": (pf + af) / world / (ms / 1e3) / 1e12}
+
+        if not args.no_e2e:
+            xh = x.cpu().pin_memory()
+            ph = torch.empty(M, d, dtype=act).pin_memory()
+            layer.forward(B, T, xh, None, ph)  # warm the staging buffers
+            barrier()
+            t0 = time.perf_counter()
+            ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ea.record(stream)
+            n_e2e = max(1, min(args.steps, 3))
+            for _ in range(n_e2e):
+                layer.forward(B, T, xh, None, ph)  # H2D x, forward, D2H post, synchronise
+            eb.record(stream)
+            barrier()
+            e_ms = max_over_ranks(max(ea.elapsed_time(eb), (time.perf_counter() - t0) * 1e3) / n_e2e)
+            e2e = {"value": M / (e_ms / 1e3), "unit": "tok/s", "ms_per_step": e_ms,
+                   "h2d_bytes_per_step": M * d * es, "d2h_bytes_per_step": M * d * es,
+                   "api": "welvet_b200_mha_forward (host buffers, pinned)"}
+            del xh, ph
+        del post
+        torch.cuda.empty_cache()
+        print(f"[bench] prefill {ms:.3f} ms/step, {tokps:.0f} tok/s; profile {prof}", file=sys.stderr, flush=True)
+        if rank == 0 and world == 1 and not args.no_cpu:
+            dt, fl = cpu_sample(w, args.cpu_tokens)
+            cpu = {"value": fl / dt / ((pf + af) / M), "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+                   "sample": f"FP64 oracle, 1 sequence x {args.cpu_tokens} tokens of the layer (d={d}, {H}x{hd}), "
+                             f"{dt:.1f} s; tok/s scaled by algorithmic FLOPs/token of the full workload"}
 
     # --------------------------------------------------------------- decode
     decode = None
-    if args.decode_steps > 0:
-        del post
-        torch.cuda.empty_cache()
-        ctx_max = T + args.decode_steps + 16
-        kv = W.KvCache(layer, B, ctx_max)
-        post = torch.empty(M, d, device="cuda", dtype=torch.bfloat16)
-        layer.prefill(kv, B, T, x, None, post, stream=stream)
-        del post
-        xd = torch.empty(B, d, device="cuda", dtype=torch.bfloat16)
+    n_dec = args.steps if decode_only else args.decode_steps
+    if n_dec > 0 and w["kind"] != "prefill":
+        extra = n_dec + (args.warmup + (0 if args.no_e2e else 3) if decode_only else 0)
+        kv = W.KvCache(layer, B, T + extra + 16)
+        if decode_only:
+            # context: N(0,1)*0.5 keys/values (seed 2), as cached (after RoPE)
+            kc = torch.empty(B, T, kd_l, device="cuda", dtype=act)
+            vc = torch.empty(B, T, kd_l, device="cuda", dtype=act)
+            n = kc.numel()
+            W.fill_synthetic(kc, 2, 1, 0.5, offset=2 * rank * n)
+            W.fill_synthetic(vc, 2, 1, 0.5, offset=(2 * rank + 1) * n)
+            kv.fill(B, T, kc, vc, stream=stream)
+            torch.cuda.synchronize()
+            del kc, vc
+        else:
+            post = torch.empty(M, d, device="cuda", dtype=act)
+            layer.prefill(kv, B, T, x, None, post, stream=stream)
+            del post
+        xd = torch.empty(B, d, device="cuda", dtype=act)
         W.fill_synthetic(xd, 1, 1, 1.0, offset=M * d)
-        pd = torch.empty(B, d, device="cuda", dtype=torch.bfloat16)
+        pd = torch.empty(B, d, device="cuda", dtype=act)
+        if decode_only:
+            for _ in range(args.warmup):
+                layer.decode(kv, B, xd, None, pd, stream=stream)
+            clocks = Clocks(local)
+            clocks.start()
+            W.launch_count(reset=True)
         barrier()
+        ctx0 = T + (args.warmup if decode_only else 0)
         W.profile_read(reset=True)
         W.profile_enable(True)
         ev0.record(stream)
-        for _ in range(args.decode_steps):
+        for _ in range(n_dec):
             layer.decode(kv, B, xd, None, pd, stream=stream)
         ev1.record(stream)
         barrier()
         W.profile_enable(False)
         dprof = W.profile_read(reset=True)
+        if decode_only:
+            launches = W.launch_count(reset=True)
+            clk = clocks.stop()
         layer.check_device()
-        dms = max_over_ranks(ev0.elapsed_time(ev1) / args.decode_steps)
+        dms = max_over_ranks(ev0.elapsed_time(ev1) / n_dec)
         # algorithmic bytes of one decode-attention launch: the K and V rows of every
         # cached position (average context over the steps) + q and the output
-        avg_ctx = T + (args.decode_steps + 1) / 2.0
-        attn_bytes = B * avg_ctx * kd_l * 2 * 2 + 2 * B * hc * hd * 2
+        avg_ctx = ctx0 + (n_dec + 1) / 2.0
+        attn_bytes = B * avg_ctx * kd_l * es * 2 + 2 * B * hc * hd * es
         at, ac = dprof["attn_decode"]
         a_ms = at / max(ac, 1)
         gbs = attn_bytes / (a_ms / 1e3) / 1e9
-        wbytes = (d * (hc * hd + 2 * kd_l) + hc * hd * d) * 2
+        wbytes = (d * (hc * hd + 2 * kd_l) + hc * hd * d) * es
         step_bytes = attn_bytes + wbytes
-        decode = {"value": B / (dms / 1e3), "unit": "tok/s", "ms_per_step": dms, "steps": args.decode_steps,
-                  "context": f"{T}..{T + args.decode_steps}",
-                  "roofline": {"bound": "hbm", "kernel": "attn_decode", "achieved": gbs, "peak": pk["hbm"],
-                               "unit": "GB/s", "frac": gbs / pk["hbm"], "traffic": None,
-                               "bytes_per_launch": attn_bytes, "avg_launch_ms": a_ms,
-                               "step_bytes": step_bytes, "step_gbs": step_bytes / (dms / 1e3) / 1e9,
-                               "kernel_ms_per_step": {k: dprof[k][0] / args.decode_steps for k in
-                                                      ("gemm_qkv_decode", "attn_decode", "gemm_o_decode",
-                                                       "allreduce")}}}
+        droof = {"bound": "hbm", "kernel": "attn_decode", "achieved": gbs, "peak": pk["hbm"],
+                 "unit": "GB/s", "frac": gbs / pk["hbm"], "peak_kind": f"{pk['src']} HBM copy (of {pk['src']})",
+                 "traffic": None, "bytes_per_launch": attn_bytes, "avg_launch_ms": a_ms,
+                 "step_bytes": step_bytes, "step_gbs": step_bytes / (dms / 1e3) / 1e9,
+                 "kernel_ms_per_step": {k: dprof[k][0] / n_dec for k in
+                                        ("gemm_qkv_decode", "attn_decode", "gemm_o_decode", "allreduce")}}
+        decode = {"value": B / (dms / 1e3), "unit": "tok/s", "ms_per_step": dms, "steps": n_dec,
+                  "context": f"{ctx0}..{ctx0 + n_dec}", "roofline": droof}
+        if decode_only:
+            ms, tokps, roof, prof = dms, B / (dms / 1e3), droof, dprof
+            if not args.no_e2e:
+                xh = xd.cpu().pin_memory()
+                ph = torch.empty(B, d, dtype=act).pin_memory()
+                barrier()
+                t0 = time.perf_counter()
+                n_e2e = 3
+                for _ in range(n_e2e):
+                    layer.decode(kv, B, xh, None, ph)  # H2D x, decode step, D2H post, synchronise
+                barrier()
+                e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3 / n_e2e)
+                e2e = {"value": B / (e_ms / 1e3), "unit": "tok/s", "ms_per_step": e_ms,
+                       "h2d_bytes_per_step": B * d * es, "d2h_bytes_per_step": B * d * es,
+                       "api": "welvet_b200_mha_decode (host buffers, pinned)"}
+            if rank == 0 and world == 1 and not args.no_cpu:
+                B_s = 4
+                dt = cpu_sample_decode(w, B_s)
+                cpu = {"value": B_s / dt, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+                       "sample": f"FP64 oracle decode step, {B_s} sequences over {T} cached tokens "
+                                 f"(d={d}, {H}x{hd}, {NK} KV heads), {dt:.2f} s"}
         kv.close()
 
-    print(f"[bench] prefill {ms:.3f} ms/step, {tokps:.0f} tok/s; profile {prof}", file=sys.stderr, flush=True)
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu:
-        dt, fl = cpu_sample(d, H, NK, args.cpu_tokens)
-        per_tok = (pf + af) / M
-        cpu = {"value": fl / dt / per_tok, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
-               "sample": f"FP64 oracle, 1 sequence x {args.cpu_tokens} tokens of the layer (d={d}, {H}x{hd}), "
-                         f"{dt:.1f} s; tok/s scaled by algorithmic FLOPs/token of the full workload"}
-
     if rank == 0:
-        line = {"metric": METRIC,
+        line = {"metric": METRIC_DECODE if decode_only else METRIC,
                 "value": tokps, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
                 "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-                "dtype": "bf16", "data": "synthetic (SplitMix64 counter stream: Xavier weights seed 0, N(0,1) x seed 1)",
+                "dtype": "bf16" if prec == 1 else "f32 (3xTF32 projections)",
+                "data": "synthetic (SplitMix64 counter stream: weights seed 0, x seed 1, KV seed 2)",
                 "config": workload_config(args, world),
                 "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "clocks": clk,
-                "decode": decode, "profile_ms": {k: v[0] / args.steps for k, v in prof.items() if v[1]}}
+                "decode": None if decode_only else decode,
+                "profile_ms": {k: v[0] / args.steps for k, v in prof.items() if v[1]}}
         print(json.dumps(line), flush=True)
     layer.close()
     if world > 1:

@@ -108,8 +108,12 @@ WELVET_API welvet_status welvet_b200_comm_attach(welvet_b200_mha* layer, const u
 /* C[M,N] = A[M,K] B[N,K]^T (reference Dense MatVec, shaders/welvet_dense.metal:54-85).
  * kind 0: A,B bf16 -> out bf16 (out_bf16=1) or fp32; kind 1: 3xTF32 with A=(a,a_lo),
  * B=(b,b_lo) fp32 TF32 splits -> out fp32; kind 2: A bf16, B FP8-E4M3 codes with
- * per-row scale b_scale [N]; kind 3: A bf16, B NF4 packed [N, K/2] with b_scale
- * [N, K/64]. */
+ * per-row scale b_scale [N], decoded by the hardware E4M3 conversion: equal to the
+ * reference decoder except that subnormal codes give their IEEE value (the reference
+ * gives +-0; below 2^-6/448 of the row's absmax) and 0x7f/0xff are not accepted
+ * (neither encoder emits them); a mounted layer normalises its codes so that its
+ * dequantised weights equal the reference decoder's exactly; kind 3: A bf16, B NF4
+ * packed [N, K/2] with b_scale [N, K/64]. */
 WELVET_API welvet_status welvet_b200_gemm(int32_t kind, int32_t M, int32_t N, int32_t K,
                                           const void* a, const void* a_lo, const void* b,
                                           const void* b_lo, const float* b_scale, void* out,

@@ -163,11 +163,16 @@ __global__ void nf4_block_decode_kernel(const uint8_t* packed, const float* absm
   }
 }
 
-__global__ void fp8_lut_kernel(uint16_t* lut) {
-  const int i = threadIdx.x;
-  if (i < 256) {
-    // Every E4M3 value the reference decoder returns is exact in BF16.
-    lut[i] = (uint16_t)(__float_as_uint(e4m3_decode((uint8_t)i)) >> 16);
+// Codes whose reference decoding differs from IEEE-style E4M3 are rewritten to a
+// code with the same reference value: subnormal codes (exponent 0, mantissa != 0)
+// decode to +-0 in the reference, 0x7f/0xff decode to +-448 (= 0x7e/0xfe).
+__global__ void fp8_normalize_kernel(uint8_t* codes, int64_t n) {
+  GRID_STRIDE(i, n) {
+    const uint8_t c = codes[i];
+    if ((c & 0x78) == 0)
+      codes[i] = c & 0x80;
+    else if ((c & 0x7f) == 0x7f)
+      codes[i] = c - 1;
   }
 }
 
@@ -303,8 +308,8 @@ cudaError_t nf4_block_decode(const uint8_t* packed, const float* absmax, int64_t
   nf4_block_decode_kernel<<<grid_for(n), 256, 0, s>>>(packed, absmax, n, out, out_bf16);
   return cudaGetLastError();
 }
-cudaError_t fp8_lut_init(uint16_t* lut, cudaStream_t s) {
-  fp8_lut_kernel<<<1, 256, 0, s>>>(lut);
+cudaError_t fp8_normalize(uint8_t* codes, int64_t n, cudaStream_t s) {
+  fp8_normalize_kernel<<<grid_for(n), 256, 0, s>>>(codes, n);
   return cudaGetLastError();
 }
 cudaError_t split_tf32(const float* x, float* hi, float* lo, int64_t n, cudaStream_t s) {

@@ -16,6 +16,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <type_traits>
 #include <mutex>
 
 namespace wv {
@@ -60,7 +61,6 @@ struct KParams {
   const float* b_scale;    // FP8: per-row scales; NF4: per-64 absmax (dequant warps)
   const float* col_scale;  // FP8 only: per-output-column scale applied in the epilogue
   int ldb;
-  const uint16_t* b_lut;
   const float2* rope_tab;
   int rope_cols, head_dim, rope_max_pos;
   const int* positions;
@@ -230,8 +230,7 @@ __global__ void __launch_bounds__(GT<KIND>::THREADS, 1)
   uint64_t* acce = accf + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(acce + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
-  uint16_t* lut = reinterpret_cast<uint16_t*>(tmem_holder + 4);  // FP8: 256 bf16 decode table
-  float* nf4s = reinterpret_cast<float*>(tmem_holder + 4);        // NF4: 16 levels
+  float* nf4s = reinterpret_cast<float*>(tmem_holder + 4);  // NF4: 16 levels
 
   const int warp = (int)warp_id(), lane = (int)lane_id();
   if (threadIdx.x == 0) {
@@ -246,9 +245,6 @@ __global__ void __launch_bounds__(GT<KIND>::THREADS, 1)
     }
     *abort_flag = 0;
     fence_barrier_init();
-  }
-  if constexpr (KIND == kGemmFP8) {
-    for (int i = threadIdx.x; i < 256; i += blockDim.x) lut[i] = p.b_lut[i];
   }
   if constexpr (KIND == kGemmNF4) {
     if (threadIdx.x < 16) nf4s[threadIdx.x] = nf4_level(threadIdx.x);
@@ -362,46 +358,81 @@ __global__ void __launch_bounds__(GT<KIND>::THREADS, 1)
     }
   } else if constexpr (XFORM) {
     // --------------------------------------------- B dequantisation (FP8/NF4)
-    // 128 threads; each writes 16-byte (8 x bf16) chunks of the swizzled tile.
+    // 128 threads; thread xt writes 16-byte (8 x bf16) chunk ch = xt % 8 of rows
+    // xt / 8 + 16 j (j < BN / 16) of the swizzled tile.
     const int xt = threadIdx.x - 192;
+    const int ch = xt & 7, r0 = xt >> 3;
+    constexpr int RPT = BN / 16;  // rows per thread
     int stage = 0;
     uint32_t phase = 0;
     for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
       int mb, nb;
       tile_coords(t, p, mb, nb);
       for (int kb = 0; kb < p.k_blocks; ++kb) {
+        // NF4: the 64-code block of this k-block has one absmax per row; the loads
+        // are issued before the wait so their latency hides behind it.
+        float amax[KIND == kGemmNF4 ? RPT : 1];
+        if constexpr (KIND == kGemmNF4) {
+#pragma unroll
+          for (int j = 0; j < RPT; ++j) {
+            const int n = nb * BN + r0 + 16 * j;
+            amax[j] = n < p.N ? __ldg(p.b_scale + (size_t)n * (p.K / 64) + kb) : 0.f;
+          }
+        }
         bool ok = mbar_wait(&full[stage], phase, abort_flag, p.err, kErrWaitFull);
         if (!__all_sync(0xffffffffu, ok)) goto done;
         uint8_t* sb = smem + stage * STAGE_BYTES;
         uint8_t* btile = sb + T::NA * A_BYTES;
         const uint8_t* codes = btile + B_BYTES;
-        // BN rows x 8 chunks of 8 codes.
-        for (int i = xt; i < BN * 8; i += 128) {
-          const int row = i >> 3, ch = i & 7;
-          uint32_t w[4];
+        // All codes of this thread's rows are loaded before any converted chunk is
+        // stored: the stores may alias the loads as far as the compiler knows, so
+        // interleaving them would serialise every row on the shared-memory latency.
+        using CodeT = typename std::conditional<KIND == kGemmFP8, uint2, uint32_t>::type;
+        CodeT cw[RPT];
+#pragma unroll
+        for (int j = 0; j < RPT; ++j)
+          cw[j] = *reinterpret_cast<const CodeT*>(codes + (r0 + 16 * j) * (KIND == kGemmFP8 ? 64 : 32) +
+                                                  ch * (KIND == kGemmFP8 ? 8 : 4));
+        // Converted chunks are held in registers and stored after the last
+        // conversion, so the NF4 level lookups (shared memory) never wait behind
+        // a store either.
+        uint32_t w[RPT][4];
+#pragma unroll
+        for (int j = 0; j < RPT; ++j) {  // fully unrolled: cw[], amax[], w[] stay in registers
           if constexpr (KIND == kGemmFP8) {
-            const uint2 c8 = *reinterpret_cast<const uint2*>(codes + row * 64 + ch * 8);
+            // Codes are normalised E4M3 (no subnormal codes, no 0x7f/0xff: the
+            // mount maps them to the values the reference decoder gives, +-0 and
+            // +-448), so the hardware E4M3 -> F16 conversion is exact, as is F16 ->
+            // F32 -> BF16 for these 4-bit-mantissa values.
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              const uint32_t word = e < 2 ? c8.x : c8.y;
-              const int sh = (e & 1) * 16;
-              const uint32_t lo = lut[(word >> sh) & 0xff], hi = lut[(word >> (sh + 8)) & 0xff];
-              w[e] = lo | (hi << 16);
+              const uint32_t word = e < 2 ? cw[j].x : cw[j].y;
+              const uint16_t pair = (uint16_t)(word >> ((e & 1) * 16));
+              uint32_t h2;
+              float lo, hi;
+              asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"(pair));
+              asm("{.reg .f16 a, b;\n\tmov.b32 {a, b}, %2;\n\tcvt.f32.f16 %0, a;\n\tcvt.f32.f16 %1, b;\n\t}"
+                  : "=f"(lo), "=f"(hi) : "r"(h2));
+              w[j][e] = pack_bf16x2(lo, hi);
             }
           } else {
-            const uint32_t c4 = *reinterpret_cast<const uint32_t*>(codes + row * 32 + ch * 4);
-            const int n = nb * BN + row;
-            const int kidx = kb * BK + ch * 8;
-            const float amax = (n < p.N) ? p.b_scale[(size_t)n * (p.K / 64) + kidx / 64] : 0.f;
+            const float am = amax[j];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              const uint32_t byte = (c4 >> (8 * e)) & 0xff;
-              const float v0 = nf4s[byte & 0xf] * amax;
-              const float v1 = nf4s[byte >> 4] * amax;
-              w[e] = pack_bf16x2(v0, v1);
+              const uint32_t byte = (cw[j] >> (8 * e)) & 0xff;
+              w[j][e] = pack_bf16x2(nf4s[byte & 0xf] * am, nf4s[byte >> 4] * am);
             }
+            // NF4 stores each row as soon as it is converted: holding all rows
+            // bunches the 128 level lookups into one burst (measured slower).
+            *reinterpret_cast<uint4*>(btile + sw128_offset(r0 + 16 * j, ch)) =
+                make_uint4(w[j][0], w[j][1], w[j][2], w[j][3]);
           }
-          *reinterpret_cast<uint4*>(btile + sw128_offset(row, ch)) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+        if constexpr (KIND == kGemmFP8) {
+#pragma unroll
+          for (int j = 0; j < RPT; ++j)
+            *reinterpret_cast<uint4*>(btile + sw128_offset(r0 + 16 * j, ch)) =
+                make_uint4(w[j][0], w[j][1], w[j][2], w[j][3]);
         }
         fence_proxy_async_smem();
         mbar_arrive(&xfull[stage]);
@@ -509,7 +540,6 @@ template <int KIND> cudaError_t launch(const GemmArgs& g, cudaStream_t stream) {
   p.out_lo = g.out_lo;
   p.b_scale = g.b_scale;
   p.ldb = g.ldb;
-  p.b_lut = g.b_lut;
   p.col_scale = KIND == kGemmFP8 ? g.b_scale : nullptr;
   p.rope_tab = g.rope_tab;
   p.rope_cols = g.rope_tab ? g.rope_cols : 0;
@@ -545,7 +575,7 @@ bool gemm_tc_supported(const GemmArgs& g) {
   if (!al16(g.b)) return false;
   if (g.kind == kGemmFP8 || g.kind == kGemmNF4) {
     if (g.K % 64) return false;
-    if (g.kind == kGemmFP8 && (g.ldb % 16 || !g.b_lut || !g.b_scale)) return false;
+    if (g.kind == kGemmFP8 && (g.ldb % 16 || !g.b_scale)) return false;
     if (g.kind == kGemmNF4 && ((g.ldb / 2) % 16 || !g.b_scale)) return false;
   } else if (((size_t)g.ldb * ae) % 16) {
     return false;

@@ -42,7 +42,6 @@ struct GemmArgs {
   const void* b_lo = nullptr;
   int ldb = 0;              // elements (codes for fp8; bytes*2 for nf4 = K)
   const float* b_scale = nullptr;  // fp8: [N]; nf4: [N, K/64]
-  const uint16_t* b_lut = nullptr; // fp8: 256-entry bf16 decode table (device)
   // epilogue
   void* out = nullptr;      // [M, ldo]
   int ldo = 0;
@@ -101,8 +100,9 @@ cudaError_t nf4_block_encode(const float* w, int64_t n, uint8_t* packed, float* 
                              cudaStream_t s);
 cudaError_t nf4_block_decode(const uint8_t* packed, const float* absmax, int64_t n, void* out,
                              int out_bf16, cudaStream_t s);
-// The E4M3 decode table of the reference converter as bf16 bits (device, 256 entries).
-cudaError_t fp8_lut_init(uint16_t* lut, cudaStream_t s);
+// Rewrites E4M3 codes in place to codes with the same reference-decoded value that
+// the hardware E4M3 conversion decodes identically (no subnormal codes, no 0x7f/0xff).
+cudaError_t fp8_normalize(uint8_t* codes, int64_t n, cudaStream_t s);
 
 // ------------------------------------------------------------- elementwise
 cudaError_t split_tf32(const float* x, float* hi, float* lo, int64_t n, cudaStream_t s);

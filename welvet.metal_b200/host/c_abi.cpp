@@ -225,7 +225,6 @@ welvet_status welvet_b200_gemm(int32_t kind, int32_t M, int32_t N, int32_t K, co
   g.b_lo = b_lo;
   g.ldb = K;
   g.b_scale = b_scale;
-  g.b_lut = d->fp8_lut;
   g.out = out;
   g.ldo = N;
   g.out_bf16 = out_bf16;

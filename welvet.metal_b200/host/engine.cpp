@@ -144,9 +144,6 @@ Status device_ctx(int device, DeviceCtx** out) {
   d->name = prop.name;
   WV_CUDA(cudaMalloc(&d->err, 256), "cudaMalloc err");
   WV_CUDA(cudaMemset(d->err, 0, 256), "cudaMemset err");
-  WV_CUDA(cudaMalloc(&d->fp8_lut, 512), "cudaMalloc lut");
-  WV_CUDA(fp8_lut_init(d->fp8_lut, 0), "fp8 lut");
-  count_launch();
   WV_CUDA(cudaMalloc(&d->scratch, 4096 * sizeof(float)), "cudaMalloc scratch");
   WV_CUDA(cudaMalloc(&d->scalars, 64 * sizeof(float)), "cudaMalloc scalars");
   WV_CUDA(cudaDeviceSynchronize(), "init");
@@ -330,9 +327,12 @@ Status mha_mount(const welvet_b200_mha_config& cin, int dtype, const float* Q, c
       const int64_t n = (int64_t)rows * cols;
       WV_TRY(codes.ensure(fp8 ? n : n / 2));
       WV_TRY(sc.ensure(fp8 ? (size_t)rows * 4 : (size_t)(n / 64) * 4));
-      if (fp8)
+      if (fp8) {
         WV_CUDA(fp8_rowscale_encode(w.as<float>(), rows, cols, codes.as<uint8_t>(), sc.as<float>(), s), "fp8 enc");
-      else
+        // the dequantising GEMM decodes with the hardware E4M3 conversion
+        WV_CUDA(fp8_normalize(codes.as<uint8_t>(), n, s), "fp8 normalize");
+        count_launch();
+      } else
         WV_CUDA(nf4_block_encode(w.as<float>(), n, codes.as<uint8_t>(), sc.as<float>(), s), "nf4 enc");
       count_launch();
       return Status::ok();
@@ -430,7 +430,6 @@ Status run_proj(Mha* m, const Proj& pj, cudaStream_t s) {
   g.b_lo = pj.w_lo;
   g.ldb = pj.K;
   g.b_scale = pj.w_scale;
-  g.b_lut = m->dev->fp8_lut;
   g.out = pj.out;
   g.ldo = pj.ldo;
   g.out_bf16 = f32 ? 0 : 1;

@@ -99,7 +99,6 @@ struct DeviceCtx {
   int cc_major = 0, cc_minor = 0;
   std::string name;
   uint32_t* err = nullptr;     // device error word
-  uint16_t* fp8_lut = nullptr; // E4M3 -> bf16 bits
   float* scratch = nullptr;    // 4096 floats (reductions)
   float* scalars = nullptr;    // 64 floats (per-tensor scales)
 };
