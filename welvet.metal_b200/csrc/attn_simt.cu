@@ -417,6 +417,13 @@ cudaError_t attn_decode(const DecodeArgs& a, cudaStream_t s) {
   const int G = a.num_kv_heads > 0 ? a.num_heads / a.num_kv_heads : 0;
   if (G <= 0 || G > 8 || a.num_heads % a.num_kv_heads) return cudaErrorInvalidValue;
   const int splits = decode_splits(a);
+  if (decode_tc_supported(a)) {
+    cudaError_t e = attn_decode_tc(a, splits, s);
+    if (e != cudaSuccess) return e;
+    if (a.is_bf16)
+      decode_combine_kernel<__nv_bfloat16><<<dim3(a.num_heads, a.batch), 128, 0, s>>>(a, splits);
+    return cudaGetLastError();
+  }
   const int chunk = (a.max_ctx + splits - 1) / splits;
   dim3 grid(splits, a.num_kv_heads, a.batch);
 #define WV_DEC_G(T, HD)                                                                  \

@@ -168,12 +168,17 @@ struct DecodeArgs {
   int splits = 0;           // KV splits per (b, kv head); 0 = choose
   int max_ctx = 0;          // upper bound of ctx_len (split sizing)
   float* partial = nullptr; // scratch: [B, NH, splits, head_dim + 2]
-  uint32_t* err = nullptr;
+  uint32_t* err = nullptr;  // device error word (bounded waits); may be null
   int sm_count = 148;
+  int64_t pool_rows = 0;    // rows of the pools (pages * kv_heads * 16); 0 = unknown
 };
 int decode_splits(const DecodeArgs& a);
 size_t decode_scratch_floats(const DecodeArgs& a);
+// BF16 decode with TMA page loads and m16n8k16 MMAs (decode_tc.cu) when supported,
+// else the CUDA-core kernel; then the split combine.
 cudaError_t attn_decode(const DecodeArgs& a, cudaStream_t s);
+bool decode_tc_supported(const DecodeArgs& a);
+cudaError_t attn_decode_tc(const DecodeArgs& a, int splits, cudaStream_t s);
 // Append rows of k/v (token-major [rows, ld]) into the page pools at slot[row].
 // Pool layout: [page][kv_head][kPageTokens][head_dim]; slot = page*kPageTokens + row.
 cudaError_t kv_append(const void* k, const void* v, int ld, int rows, int kd, int head_dim,

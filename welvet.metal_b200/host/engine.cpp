@@ -822,6 +822,7 @@ Status mha_decode(Mha* m, Kv* kv, int batch, const void* x, void* pre, void* pos
   d.total_heads = c.c.num_heads;
   d.scale = c.scale;
   d.max_ctx = max_ctx + 1;
+  d.pool_rows = (int64_t)kv->max_batch * kv->pages_per_seq * m->khc * kPageTokens;
   d.err = m->dev->err;
   d.sm_count = m->dev->sm_count;
   WV_TRY(kv->scratch.ensure(decode_scratch_floats(d) * 4));
