@@ -235,9 +235,12 @@ def test_chunked_forward_with_communicator(torch_cuda, precision):
     xh = x.cpu()
     pre_h = torch.zeros(B * T, d, dtype=dt)
     post_h = torch.zeros(B * T, d, dtype=dt)
-    chunked.forward(B, T, xh, pre_h, post_h)
-    assert np.array_equal(pre_h.float().numpy(), outs[0][0])
-    assert np.array_equal(post_h.float().numpy(), outs[0][1])
+    for layer in (chunked, plain):  # host buffers: copies of chunk i+1 / i-1 overlap chunk i
+        pre_h.zero_()
+        post_h.zero_()
+        layer.forward(B, T, xh, pre_h, post_h)
+        assert np.array_equal(pre_h.float().numpy(), outs[0][0])
+        assert np.array_equal(post_h.float().numpy(), outs[0][1])
     chunked.check_device()
     chunked.close()
     plain.close()

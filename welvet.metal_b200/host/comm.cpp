@@ -77,7 +77,8 @@ Status comm_attach(Mha* m, const uint8_t id[128], int nranks, int rank) {
   m->nranks = nranks;
   m->rank = rank;
   WV_CUDA(cudaStreamCreateWithFlags(&m->comm_stream, cudaStreamNonBlocking), "comm stream");
-  for (auto& e : m->chunk_done) WV_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "chunk event");
+  for (auto& e : m->chunk_done)
+    if (!e) WV_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "chunk event");
   WV_CUDA(cudaEventCreateWithFlags(&m->comm_done, cudaEventDisableTiming), "comm event");
   return Status::ok();
 }

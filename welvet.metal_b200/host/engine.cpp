@@ -213,7 +213,13 @@ Status resolve_config(const welvet_b200_mha_config& in, Cfg* out) {
 }
 
 // -------------------------------------------------------------------- mount
-Mha::~Mha() { comm_release(this); }
+Mha::~Mha() {
+  comm_release(this);
+  for (auto& e : io_ev)
+    if (e) cudaEventDestroy(e);
+  if (io_in) cudaStreamDestroy(io_in);
+  if (io_out) cudaStreamDestroy(io_out);
+}
 
 namespace {
 
@@ -383,6 +389,17 @@ Status mha_mount(const welvet_b200_mha_config& cin, int dtype, const float* Q, c
 // ------------------------------------------------------------------ forward
 namespace {
 
+// Copy streams and events of the chunked host-buffer forward (created on first use).
+Status ensure_io_streams(Mha* m) {
+  if (m->io_in) return Status::ok();
+  WV_CUDA(cudaStreamCreateWithFlags(&m->io_in, cudaStreamNonBlocking), "io stream");
+  WV_CUDA(cudaStreamCreateWithFlags(&m->io_out, cudaStreamNonBlocking), "io stream");
+  for (auto& e : m->io_ev) WV_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "io event");
+  for (auto& e : m->chunk_done)  // shared with the communicator path
+    if (!e) WV_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "chunk event");
+  return Status::ok();
+}
+
 Status ensure_rope(Mha* m, int max_pos, cudaStream_t s) {
   if (!m->cfg.rope || m->cfg.hd < 2) return Status::ok();
   if (max_pos <= m->rope_max_pos) return Status::ok();
@@ -530,10 +547,18 @@ Status mha_forward(Mha* m, int batch, int seq, const void* x, void* pre, void* p
   const void* xd = x;
   void* pred = pre;
   void* postd = post;
+  // With a communicator attached, or with host buffers, and independent sequences
+  // (per-sequence mode, no KV prefill) the batch runs in chunks: the all-reduce of
+  // chunk i (comm_stream) and its device->host copy (io_out) overlap the next
+  // chunk's projections and attention (stream s), whose input copy (io_in) ran
+  // during the previous chunk.
+  const bool chunked = (m->comm || !on_device) && !stream_mode && !kv && batch > 1;
+  const int chunks = chunked ? std::min(batch, Mha::kMaxChunks / 2) : 1;
   if (!on_device) {
     WV_TRY(m->x_io.ensure(M * dm * es));
     WV_TRY(m->post_io.ensure(M * dm * es));
-    WV_CUDA(cudaMemcpyAsync(m->x_io.p, x, M * dm * es, cudaMemcpyHostToDevice, s), "H2D x");
+    if (!chunked) WV_CUDA(cudaMemcpyAsync(m->x_io.p, x, M * dm * es, cudaMemcpyHostToDevice, s), "H2D x");
+    else WV_TRY(ensure_io_streams(m));
     xd = m->x_io.p;
     postd = m->post_io.p;
     pred = nullptr;
@@ -542,10 +567,6 @@ Status mha_forward(Mha* m, int batch, int seq, const void* x, void* pre, void* p
       pred = m->pre_io.p;
     }
   }
-  // With a communicator attached and independent sequences (per-sequence mode, no
-  // KV prefill), the batch runs in chunks: the all-reduce of chunk i (comm_stream)
-  // overlaps the projections and attention of chunk i+1 (stream s).
-  const int chunks = (m->comm && !stream_mode && !kv) ? std::min(batch, Mha::kMaxChunks / 2) : 1;
   const int bc_max = (batch + chunks - 1) / chunks;
   const int64_t Mc_max = (int64_t)bc_max * seq;
   WV_TRY(m->qkv.ensure(Mc_max * m->nqkv * es));
@@ -648,27 +669,62 @@ Status mha_forward(Mha* m, int batch, int seq, const void* x, void* pre, void* p
       prof_end(kProfAllReduce, s);
     }
   } else {
-    // The comm stream first waits for what s did before this call (H2D of x, the
-    // previous forward's readers of post).
+    // The helper streams first wait for what s did before this call (the previous
+    // forward's readers of the staging buffers and of post).
+    const bool host = !on_device;
     WV_CUDA(cudaEventRecord(m->chunk_done[0], s), "event");
-    WV_CUDA(cudaStreamWaitEvent(m->comm_stream, m->chunk_done[0], 0), "wait");
+    if (m->comm) WV_CUDA(cudaStreamWaitEvent(m->comm_stream, m->chunk_done[0], 0), "wait");
+    if (host) {
+      WV_CUDA(cudaStreamWaitEvent(m->io_in, m->chunk_done[0], 0), "wait");
+      WV_CUDA(cudaStreamWaitEvent(m->io_out, m->chunk_done[0], 0), "wait");
+    }
     for (int i = 0, b0 = 0; i < chunks && b0 < batch; ++i, b0 += bc_max) {
       const int bc = std::min(bc_max, batch - b0);
+      const int64_t r0 = (int64_t)b0 * seq, rows = (int64_t)bc * seq;
+      if (host) {
+        WV_CUDA(cudaMemcpyAsync(static_cast<char*>(m->x_io.p) + r0 * dm * es, static_cast<const char*>(x) + r0 * dm * es,
+                                rows * dm * es, cudaMemcpyHostToDevice, m->io_in), "H2D x");
+        WV_CUDA(cudaEventRecord(m->io_ev[i], m->io_in), "event");
+        WV_CUDA(cudaStreamWaitEvent(s, m->io_ev[i], 0), "wait");
+      }
       WV_TRY(run_rows(b0, bc));
       WV_CUDA(cudaEventRecord(m->chunk_done[i], s), "event");
-      WV_CUDA(cudaStreamWaitEvent(m->comm_stream, m->chunk_done[i], 0), "wait");
-      prof_begin(kProfAllReduce, m->comm_stream);
-      WV_TRY(comm_allreduce(m, static_cast<char*>(postd) + (int64_t)b0 * seq * dm * es, (size_t)bc * seq * dm,
-                            !f32, m->comm_stream));
-      prof_end(kProfAllReduce, m->comm_stream);
+      cudaEvent_t out_ready = m->chunk_done[i];
+      if (m->comm) {
+        WV_CUDA(cudaStreamWaitEvent(m->comm_stream, m->chunk_done[i], 0), "wait");
+        prof_begin(kProfAllReduce, m->comm_stream);
+        WV_TRY(comm_allreduce(m, static_cast<char*>(postd) + r0 * dm * es, (size_t)rows * dm, !f32, m->comm_stream));
+        prof_end(kProfAllReduce, m->comm_stream);
+        if (host) {
+          WV_CUDA(cudaEventRecord(m->io_ev[Mha::kMaxChunks + i], m->comm_stream), "event");
+          out_ready = m->io_ev[Mha::kMaxChunks + i];
+        }
+      }
+      if (host) {
+        WV_CUDA(cudaStreamWaitEvent(m->io_out, out_ready, 0), "wait");
+        WV_CUDA(cudaMemcpyAsync(static_cast<char*>(post) + r0 * dm * es, static_cast<char*>(postd) + r0 * dm * es,
+                                rows * dm * es, cudaMemcpyDeviceToHost, m->io_out), "D2H post");
+        if (pre)
+          WV_CUDA(cudaMemcpyAsync(static_cast<char*>(pre) + r0 * m->qd_l * es,
+                                  static_cast<char*>(pred) + r0 * m->qd_l * es, rows * m->qd_l * es,
+                                  cudaMemcpyDeviceToHost, m->io_out), "D2H pre");
+      }
     }
-    WV_CUDA(cudaEventRecord(m->comm_done, m->comm_stream), "event");
-    WV_CUDA(cudaStreamWaitEvent(s, m->comm_done, 0), "wait");
+    if (m->comm) {
+      WV_CUDA(cudaEventRecord(m->comm_done, m->comm_stream), "event");
+      WV_CUDA(cudaStreamWaitEvent(s, m->comm_done, 0), "wait");
+    }
+    if (host) {
+      WV_CUDA(cudaEventRecord(m->io_ev[2 * Mha::kMaxChunks], m->io_out), "event");
+      WV_CUDA(cudaStreamWaitEvent(s, m->io_ev[2 * Mha::kMaxChunks], 0), "wait");
+    }
   }
 
   if (!on_device) {
-    WV_CUDA(cudaMemcpyAsync(post, postd, M * dm * es, cudaMemcpyDeviceToHost, s), "D2H post");
-    if (pre) WV_CUDA(cudaMemcpyAsync(pre, pred, M * m->qd_l * es, cudaMemcpyDeviceToHost, s), "D2H pre");
+    if (!chunked) {
+      WV_CUDA(cudaMemcpyAsync(post, postd, M * dm * es, cudaMemcpyDeviceToHost, s), "D2H post");
+      if (pre) WV_CUDA(cudaMemcpyAsync(pre, pred, M * m->qd_l * es, cudaMemcpyDeviceToHost, s), "D2H pre");
+    }
     WV_CUDA(cudaStreamSynchronize(s), "forward");
     WV_TRY(check_device_error(m->dev));
   }

@@ -140,6 +140,9 @@ struct Mha {
   static constexpr int kMaxChunks = 8;
   cudaEvent_t chunk_done[kMaxChunks] = {};
   cudaEvent_t comm_done = nullptr;
+  // host-buffer calls: input copies (io_in) and output copies (io_out) of the chunks
+  cudaStream_t io_in = nullptr, io_out = nullptr;
+  cudaEvent_t io_ev[2 * kMaxChunks + 1] = {};
   std::mutex mu;  // one call at a time per layer (reference: per-session lock)
   ~Mha();
 };
