@@ -390,35 +390,44 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       uint64_t acc2[4] = {0ull, 0ull, 0ull, 0ull};  // packed partial row sums (ILP)
       const uint64_t sl2 = f2pack(sl, sl), nm2 = f2pack(-mref, -mref);
+      // One loop per case (the case is uniform over the block): a per-pair branch
+      // inside the unrolled loop would cost a branch and its resolution per pair.
+      auto exp_loop = [&](auto pair_fn) {
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {  // 16 pieces of 8 keys, 16 bytes each
-        uint32_t w4[4];
+        for (int c = 0; c < 16; ++c) {  // 16 pieces of 8 keys, 16 bytes each
+          uint32_t w4[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const uint64_t s2 = f2pack(__uint_as_float(s[8 * c + 2 * e]), __uint_as_float(s[8 * c + 2 * e + 1]));
-          float a, c2;
-          if (SIGMOID) {
-            float v0, v1;
-            f2unpack(fast ? ffma2(s2, sl2, 0ull) : s2, v0, v1);
-            a = v0 == -INFINITY ? 0.f : __frcp_rn(1.f + fast_exp2(-v0));
-            c2 = v1 == -INFINITY ? 0.f : __frcp_rn(1.f + fast_exp2(-v1));
-          } else if (fast) {
-            // logits x*sl - m as one packed FMA; every fourth exp2 runs as a
-            // polynomial on the FMA pipe to relieve the MUFU pipe
-            float x0, x1;
-            f2unpack(ffma2(s2, sl2, nm2), x0, x1);
-            a = fast_exp2(x0);
-            c2 = fast_exp2(x1);
-          } else {
-            float x0, x1;
-            f2unpack(fadd2(s2, nm2), x0, x1);
-            a = fast_exp2(x0);
-            c2 = fast_exp2(x1);
+          for (int e = 0; e < 4; ++e) {
+            float a, c2;
+            pair_fn(__uint_as_float(s[8 * c + 2 * e]), __uint_as_float(s[8 * c + 2 * e + 1]), a, c2);
+            acc2[e] = fadd2(acc2[e], f2pack(a, c2));
+            w4[e] = pack_bf16x2(a, c2);
           }
-          acc2[e] = fadd2(acc2[e], f2pack(a, c2));
-          w4[e] = pack_bf16x2(a, c2);
+          *reinterpret_cast<uint4*>(pt + (c >> 3) * F::TILE + sw128(r, c & 7)) =
+              make_uint4(w4[0], w4[1], w4[2], w4[3]);
         }
-        *reinterpret_cast<uint4*>(pt + (c >> 3) * F::TILE + sw128(r, c & 7)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+      };
+      if (SIGMOID) {
+        const float k = fast ? sl : 1.f;  // masked logits are already scaled
+        exp_loop([&](float x0, float x1, float& a, float& c2) {
+          const float v0 = x0 * k, v1 = x1 * k;
+          a = v0 == -INFINITY ? 0.f : __frcp_rn(1.f + fast_exp2(-v0));
+          c2 = v1 == -INFINITY ? 0.f : __frcp_rn(1.f + fast_exp2(-v1));
+        });
+      } else if (fast) {
+        exp_loop([&](float x0, float x1, float& a, float& c2) {
+          float y0, y1;  // logits x*sl - m as one packed FMA
+          f2unpack(ffma2(f2pack(x0, x1), sl2, nm2), y0, y1);
+          a = fast_exp2(y0);
+          c2 = fast_exp2(y1);
+        });
+      } else {
+        exp_loop([&](float x0, float x1, float& a, float& c2) {
+          float y0, y1;
+          f2unpack(fadd2(f2pack(x0, x1), nm2), y0, y1);
+          a = fast_exp2(y0);
+          c2 = fast_exp2(y1);
+        });
       }
       float r0, r1, r2, r3, r4, r5, r6, r7;
       f2unpack(acc2[0], r0, r1);
