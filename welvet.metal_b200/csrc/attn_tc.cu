@@ -46,14 +46,14 @@ template <int HD> struct FT {
   static constexpr int TILE = 128 * 128;        // bytes of a 128-row x 64-col bf16 chunk (16 KB)
   static constexpr int Q_BYTES = CH * TILE;
   static constexpr int KV_BYTES = CH * TILE;    // one K or V block (128 keys)
-  static constexpr int P_BYTES = 2 * TILE;      // 128 rows x 128 keys
-  static constexpr int SK = HD == 128 ? 2 : 3;  // ring depths
-  static constexpr int SV = HD == 128 ? 2 : 3;
+  static constexpr int SK = HD == 128 ? 3 : 4;  // ring depths (K runs two blocks ahead of V)
+  static constexpr int SV = HD == 128 ? 2 : 4;
   static constexpr int OFF_K = Q_BYTES;
   static constexpr int OFF_V = OFF_K + SK * KV_BYTES;
-  static constexpr int OFF_P = OFF_V + SV * KV_BYTES;  // two P tiles, one per warpgroup
-  static constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
+  static constexpr int OFF_EX = OFF_V + SV * KV_BYTES;  // final (max, sum) exchange, 2 x 256 floats
+  static constexpr int OFF_BAR = OFF_EX + 2048;
   static constexpr int SMEM = 1024 + OFF_BAR + 512;
+  static_assert(SMEM <= 227 * 1024, "shared memory");
 };
 
 struct FParams {
@@ -105,29 +105,11 @@ __device__ __forceinline__ bool block_full(const FParams& p, int q0, int q1, int
   return k1 <= q0;
 }
 
-__device__ __forceinline__ uint32_t sw128(int row, int chunk16) {
-  return (uint32_t)(row * 128 + ((chunk16 ^ (row & 7)) << 4));
-}
 
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
-}
-
-// 2^x on the FMA/ALU pipes: x = n + f with n = rint(x) (magic-number rounding),
-// f in [-1/2, 1/2]; 2^f by a degree-3 polynomial fitted here (relative error
-// 7.5e-5, below bf16's 2^-9), 2^n added to the exponent field. Valid for
-// x >= -126 (clamped); callers use it only where no element is masked.
-__device__ __forceinline__ float poly_exp2(float x) {
-  x = fmaxf(x, -126.0f);
-  const float t = x + 12582912.0f;  // 1.5 * 2^23
-  const float f = x - (t - 12582912.0f);
-  float pf = fmaf(0.055171605199575424f, f, 0.2426111102104187f);
-  pf = fmaf(pf, f, 0.6932609677314758f);
-  pf = fmaf(pf, f, 0.9999280571937561f);
-  const int n = __float_as_int(t) - 0x4B400000;
-  return __int_as_float(__float_as_int(pf) + (n << 23));
 }
 
 // Packed FP32 pairs (sm_100 f32x2 ALU ops) and a three-input max.
@@ -169,9 +151,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* v_full = k_empty + F::SK;
   uint64_t* v_empty = v_full + F::SV;
   uint64_t* s_full = v_empty + F::SV;  // [2] per warpgroup
-  uint64_t* s_empty = s_full + 2;      // [2]
-  uint64_t* p_full = s_empty + 2;      // [2] P written (and O rescaled)
-  uint64_t* p_empty = p_full + 2;      // [2] PV complete: P tile free, O current
+  uint64_t* p_full = s_full + 2;       // [2] P written over S (and O rescaled)
+  uint64_t* p_empty = p_full + 2;      // [2] PV complete
   uint64_t* fin_bar = p_empty + 2;     // final (max, sum) exchange
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(fin_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
@@ -204,7 +185,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], kSoftThreads / 2);
       mbar_init(&p_full[i], kSoftThreads / 2);
       mbar_init(&p_empty[i], 1);
     }
@@ -262,12 +242,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       // S_j into TMEM buffer j&1. Its warpgroup copies S into registers at the start
       // of its block, so S_{j+2} can run while that warpgroup is still computing
       // block j: issue order S_0, S_1, then per block i: S_{i+2}, PV_i.
+      // S_j into TMEM buffer j&1 (columns 128*(j&1)); its warpgroup reads S_j into
+      // registers and writes P_j (bf16 pairs) over the first 64 columns, which the
+      // TS MMA of PV_j reads as its A operand. S_{j+2} reuses the buffer, so the
+      // issue order is S_0, S_1, then per block i: PV_i, S_{i+2} (MMAs of one thread
+      // execute in issue order).
       auto issue_s = [&](int j) -> bool {
         const int ks = j % F::SK, g = j & 1;
         if (!mbar_wait(&k_full[ks], (j / F::SK) & 1, abort_flag, p.err, kErrWaitFull)) return false;
-        // S buffer g was last read by the warpgroup's copy of S_{j-2}
-        if (j >= 2 && !mbar_wait(&s_empty[g], ((j - 2) >> 1) & 1, abort_flag, p.err, kErrWaitAccEmpty))
-          return false;
         tc_fence_after();
         const uint32_t k_base = smem_u32(smem + F::OFF_K + ks * F::KV_BYTES);
 #pragma unroll
@@ -285,14 +267,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(&p_full[g], (i >> 1) & 1, abort_flag, p.err, kErrWaitOther)) return false;
         if (!mbar_wait(&v_full[vs], (i / F::SV) & 1, abort_flag, p.err, kErrWaitFull)) return false;
         tc_fence_after();
-        const uint32_t p_base = smem_u32(smem + F::OFF_P + g * F::P_BYTES);
         const uint32_t v_base = smem_u32(smem + F::OFF_V + vs * F::KV_BYTES);
 #pragma unroll
         for (int kk = 0; kk < kBK / 16; ++kk) {
-          const uint32_t poff = (uint32_t)((kk >> 2) * F::TILE + (kk & 3) * 32);
-          // V is MN-major: 16 keys = 16 rows of 128 bytes; the second 64-column
-          // chunk of head_dim sits one TILE further (leading byte offset).
-          umma_f16_ss(tmem + (uint32_t)(256 + HD * g), sdesc_sw128(p_base + poff, 16, 1024),
+          // A = P from TMEM: 16 keys = 8 columns of bf16 pairs. V is MN-major: 16
+          // keys = 16 rows of 128 bytes; the second 64-column chunk of head_dim
+          // sits one TILE further (leading byte offset).
+          umma_f16_ts(tmem + (uint32_t)(256 + HD * g), tmem + (uint32_t)(g * 128 + kk * 8),
                       sdesc_sw128(v_base + (uint32_t)(kk * 16 * 128), F::TILE, 1024), IDESC_PV,
                       (i >= 2 || kk > 0) ? 1u : 0u);
         }
@@ -303,8 +284,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; j < min(2, nblk); ++j)
         if (!issue_s(j)) goto done;
       for (int i = 0; i < nblk; ++i) {
-        if (i + 2 < nblk && !issue_s(i + 2)) goto done;
         if (!issue_pv(i)) goto done;
+        if (i + 2 < nblk && !issue_s(i + 2)) goto done;
       }
     }
   } else if (warp < 8) {
@@ -322,7 +303,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     int jl = -1;  // last block processed by this warpgroup
-    uint8_t* pt = smem + F::OFF_P + g * F::P_BYTES;
     for (int j = g; j < nblk; j += 2) {
       ok = mbar_wait(&s_full[g], (j >> 1) & 1, abort_flag, p.err, kErrWaitAccFull);
       if (!__all_sync(0xffffffffu, ok)) {
@@ -335,8 +315,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < 4; ++c)
         tmem_ld32(tmem + lane_off + s_col + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&s[32 * c]));
       tmem_ld_wait();
-      tc_fence_before();
-      mbar_arrive(&s_empty[g]);
 
       const int k0 = kb0 + j * kBK;
       const bool full = block_full(p, pos0 + t0, pos0 + t0 + kBQ - 1, k0, k0 + kBK - 1, kv_end);
@@ -379,32 +357,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       const float mref = (m == -INFINITY) ? 0.f : m;
-      // This warpgroup's P tile is free and its O current once PV_{j-2} is done.
-      if (j >= 2) {
-        ok = mbar_wait(&p_empty[g], ((j - 2) >> 1) & 1, abort_flag, p.err, kErrWaitOther);
-        if (!__all_sync(0xffffffffu, ok)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-      }
+      // O_g is current: S_j completed after PV_{j-2} (issue order), and s_full(j)
+      // covers every MMA issued before it.
       uint64_t acc2[4] = {0ull, 0ull, 0ull, 0ull};  // packed partial row sums (ILP)
       const uint64_t sl2 = f2pack(sl, sl), nm2 = f2pack(-mref, -mref);
       // One loop per case (the case is uniform over the block): a per-pair branch
       // inside the unrolled loop would cost a branch and its resolution per pair.
+      // P as bf16 pairs over columns [0, 64) of S_g, 32 columns (64 keys) per store.
       auto exp_loop = [&](auto pair_fn) {
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {  // 16 pieces of 8 keys, 16 bytes each
-          uint32_t w4[4];
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t pk[32];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
+          for (int c = 0; c < 32; ++c) {
+            const int i = 64 * hh + 2 * c;
             float a, c2;
-            pair_fn(__uint_as_float(s[8 * c + 2 * e]), __uint_as_float(s[8 * c + 2 * e + 1]), a, c2);
-            acc2[e] = fadd2(acc2[e], f2pack(a, c2));
-            w4[e] = pack_bf16x2(a, c2);
+            pair_fn(__uint_as_float(s[i]), __uint_as_float(s[i + 1]), a, c2);
+            acc2[c & 3] = fadd2(acc2[c & 3], f2pack(a, c2));
+            pk[c] = pack_bf16x2(a, c2);
           }
-          *reinterpret_cast<uint4*>(pt + (c >> 3) * F::TILE + sw128(r, c & 7)) =
-              make_uint4(w4[0], w4[1], w4[2], w4[3]);
+          tmem_st32(tmem + lane_off + s_col + 32 * hh, pk);
         }
       };
       if (SIGMOID) {
@@ -445,9 +417,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * corr);
           tmem_st32(tmem + lane_off + o_col + 32 * c, o);
         }
-        tmem_st_wait();
       }
-      fence_proxy_async_smem();
+      tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&p_full[g]);
       jl = j;
@@ -455,7 +426,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---- merge the two partial softmaxes; warpgroup g writes output columns
     //      [g*HD/2, (g+1)*HD/2) of the row.
     if (ok && jl >= 0) ok = mbar_wait(&p_empty[g], (jl >> 1) & 1, abort_flag, p.err, kErrWaitOther);
-    float* ex = reinterpret_cast<float*>(pt);  // this warpgroup's P tile is free now
+    float* ex = reinterpret_cast<float*>(smem + F::OFF_EX) + g * 256;
     if (ok) {
       ex[r] = m;
       ex[128 + r] = l;
@@ -467,7 +438,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (__all_sync(0xffffffffu, ok)) {
       tc_fence_after();
-      const float* exo = reinterpret_cast<const float*>(smem + F::OFF_P + (g ^ 1) * F::P_BYTES);
+      const float* exo = reinterpret_cast<const float*>(smem + F::OFF_EX) + (g ^ 1) * 256;
       const float mA = g == 0 ? m : exo[r], lA = g == 0 ? l : exo[128 + r];
       const float mB = g == 0 ? exo[r] : m, lB = g == 0 ? exo[128 + r] : l;
       const int nbA = (nblk + 1) / 2, nbB = nblk / 2;
