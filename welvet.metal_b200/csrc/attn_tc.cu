@@ -29,7 +29,7 @@ namespace {
 constexpr int kBQ = 128;  // query rows per tile
 constexpr int kBK = 128;  // keys per block
 constexpr int kSoftThreads = 256;  // warps 0-7: two softmax warpgroups
-constexpr int kThreads = 384;      // warps 8-11: TMA producer (8), UMMA issuer (9), idle (10, 11)
+constexpr int kThreads = 384;      // warps 8-11: TMA Q/K (8), UMMA issuer (9), TMA V (10), idle (11)
 // Register split by warpgroup (setmaxnreg): the launch gives every thread
 // kLaunchRegs; the producer warpgroup drops to kLowRegs and the softmax
 // warpgroups grow to kHighRegs. The host verifies the kernel's launch register
@@ -46,12 +46,14 @@ template <int HD> struct FT {
   static constexpr int TILE = 128 * 128;        // bytes of a 128-row x 64-col bf16 chunk (16 KB)
   static constexpr int Q_BYTES = CH * TILE;
   static constexpr int KV_BYTES = CH * TILE;    // one K or V block (128 keys)
-  static constexpr int SK = HD == 128 ? 3 : 4;  // ring depths (K runs two blocks ahead of V)
-  static constexpr int SV = HD == 128 ? 2 : 4;
+  static constexpr int SK = HD == 128 ? 3 : 4;  // ring depths
+  static constexpr int SV = HD == 128 ? 3 : 4;
   static constexpr int OFF_K = Q_BYTES;
   static constexpr int OFF_V = OFF_K + SK * KV_BYTES;
-  static constexpr int OFF_EX = OFF_V + SV * KV_BYTES;  // final (max, sum) exchange, 2 x 256 floats
-  static constexpr int OFF_BAR = OFF_EX + 2048;
+  // Final (max, sum) exchange, 2 x 256 floats, in K stage 0: every S MMA (the last
+  // reader of K) has completed before the last PV, which the exchange waits for.
+  static constexpr int OFF_EX = OFF_K;
+  static constexpr int OFF_BAR = OFF_V + SV * KV_BYTES;
   static constexpr int SMEM = 1024 + OFF_BAR + 512;
   static_assert(SMEM <= 227 * 1024, "shared memory");
 };
@@ -204,32 +206,33 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp >= 8) regs_dec<kLowRegs>();  // whole warpgroup 2, before any role branch
   if (warp == 8) {
-    // ------------------------------------------------------------- producer
+    // ------------------------------------------------------- producer: Q, K
     if (lane == 0 && nblk > 0) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
-      tma_prefetch_desc(&tmV);
       mbar_arrive_expect_tx(q_full, F::Q_BYTES);
       for (int c = 0; c < F::CH; ++c) tma_load_2d(smem + c * F::TILE, &tmQ, q_full, h * HD + c * 64, q_row0);
-      // K runs two blocks ahead of V, matching the issue order S_{i+2}, PV_i.
-      for (int j = 0; j < nblk + 2; ++j) {
-        if (j < nblk) {
-          const int ks = j % F::SK;
-          if (!mbar_wait(&k_empty[ks], ((j / F::SK) & 1) ^ 1, abort_flag, p.err, kErrWaitEmpty)) break;
-          mbar_arrive_expect_tx(&k_full[ks], F::KV_BYTES);
-          for (int c = 0; c < F::CH; ++c)
-            tma_load_2d(smem + F::OFF_K + ks * F::KV_BYTES + c * F::TILE, &tmK, &k_full[ks], kh * HD + c * 64,
-                        key_row_base + kb0 + j * kBK);
-        }
-        const int i = j - 2;
-        if (i >= 0 && i < nblk) {
-          const int vs = i % F::SV;
-          if (!mbar_wait(&v_empty[vs], ((i / F::SV) & 1) ^ 1, abort_flag, p.err, kErrWaitEmpty)) break;
-          mbar_arrive_expect_tx(&v_full[vs], F::KV_BYTES);
-          for (int c = 0; c < F::CH; ++c)
-            tma_load_2d(smem + F::OFF_V + vs * F::KV_BYTES + c * F::TILE, &tmV, &v_full[vs], kh * HD + c * 64,
-                        key_row_base + kb0 + i * kBK);
-        }
+      for (int j = 0; j < nblk; ++j) {
+        const int ks = j % F::SK;
+        if (!mbar_wait(&k_empty[ks], ((j / F::SK) & 1) ^ 1, abort_flag, p.err, kErrWaitEmpty)) break;
+        mbar_arrive_expect_tx(&k_full[ks], F::KV_BYTES);
+        for (int c = 0; c < F::CH; ++c)
+          tma_load_2d(smem + F::OFF_K + ks * F::KV_BYTES + c * F::TILE, &tmK, &k_full[ks], kh * HD + c * 64,
+                      key_row_base + kb0 + j * kBK);
+      }
+    }
+  } else if (warp == 10) {
+    // ---------------------------------------------------------- producer: V
+    // (its own thread: a V load never waits behind a K slot and vice versa)
+    if (lane == 0 && nblk > 0) {
+      tma_prefetch_desc(&tmV);
+      for (int i = 0; i < nblk; ++i) {
+        const int vs = i % F::SV;
+        if (!mbar_wait(&v_empty[vs], ((i / F::SV) & 1) ^ 1, abort_flag, p.err, kErrWaitEmpty)) break;
+        mbar_arrive_expect_tx(&v_full[vs], F::KV_BYTES);
+        for (int c = 0; c < F::CH; ++c)
+          tma_load_2d(smem + F::OFF_V + vs * F::KV_BYTES + c * F::TILE, &tmV, &v_full[vs], kh * HD + c * 64,
+                      key_row_base + kb0 + i * kBK);
       }
     }
   } else if (warp == 9) {
@@ -239,9 +242,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t IDESC_PV = idesc_make(1, kBQ, HD, 0, 1);
       const uint32_t q_base = smem_u32(smem);
       if (!mbar_wait(q_full, 0, abort_flag, p.err, kErrWaitFull)) goto done;
-      // S_j into TMEM buffer j&1. Its warpgroup copies S into registers at the start
-      // of its block, so S_{j+2} can run while that warpgroup is still computing
-      // block j: issue order S_0, S_1, then per block i: S_{i+2}, PV_i.
       // S_j into TMEM buffer j&1 (columns 128*(j&1)); its warpgroup reads S_j into
       // registers and writes P_j (bf16 pairs) over the first 64 columns, which the
       // TS MMA of PV_j reads as its A operand. S_{j+2} reuses the buffer, so the
@@ -427,9 +427,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     //      [g*HD/2, (g+1)*HD/2) of the row.
     if (ok && jl >= 0) ok = mbar_wait(&p_empty[g], (jl >> 1) & 1, abort_flag, p.err, kErrWaitOther);
     float* ex = reinterpret_cast<float*>(smem + F::OFF_EX) + g * 256;
+    // A warpgroup without blocks (warpgroup 1 when nblk <= 1) writes nothing: the
+    // exchange lies in the K ring, which is only free once the last S has run.
+    const int nb_mine = g == 0 ? (nblk + 1) / 2 : nblk / 2, nb_other = g == 0 ? nblk / 2 : (nblk + 1) / 2;
     if (ok) {
-      ex[r] = m;
-      ex[128 + r] = l;
+      if (nb_mine > 0) {
+        ex[r] = m;
+        ex[128 + r] = l;
+      }
       // The other warpgroup reads O_g after this arrive; it orders after the
       // p_empty[g] completion observed above (release/acquire through fin_bar).
       tc_fence_before();
@@ -439,8 +444,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (__all_sync(0xffffffffu, ok)) {
       tc_fence_after();
       const float* exo = reinterpret_cast<const float*>(smem + F::OFF_EX) + (g ^ 1) * 256;
-      const float mA = g == 0 ? m : exo[r], lA = g == 0 ? l : exo[128 + r];
-      const float mB = g == 0 ? exo[r] : m, lB = g == 0 ? exo[128 + r] : l;
+      const float mo = nb_other > 0 ? exo[r] : -INFINITY, lo = nb_other > 0 ? exo[128 + r] : 0.f;
+      const float mA = g == 0 ? m : mo, lA = g == 0 ? l : lo;
+      const float mB = g == 0 ? mo : m, lB = g == 0 ? lo : l;
       const int nbA = (nblk + 1) / 2, nbB = nblk / 2;
       float wA = 1.f, wB = 1.f, inv = 1.f;
       if (!SIGMOID) {
