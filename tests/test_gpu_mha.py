@@ -244,3 +244,36 @@ def test_chunked_forward_with_communicator(torch_cuda, precision):
     chunked.check_device()
     chunked.close()
     plain.close()
+
+
+@pytest.mark.parametrize("H,NK,pos,softmax", [
+    (8, 2, 2, 0),   # GQA 4, head_dim 64, ALiBi
+    (8, 2, 0, 1),   # sigmoid scores, RoPE
+    (4, 4, 3, 0),   # MHA, head_dim 128, RoPE + ALiBi
+    (2, 1, 0, 0),   # GQA 2, head_dim 256
+])
+def test_decode_variants_against_oracle(torch_cuda, H, NK, pos, softmax):
+    """The paged decode kernel (TMA page rings + m16n8k16 MMAs) on the position
+    encodings and score functions of the reference, through the layer's decode."""
+    torch = torch_cuda
+    d, B, L = 512, 3, 150
+    cfg = W.MhaConfig.make(d, H, NK, precision=1, pos=pos, softmax=softmax)
+    hd, nk = cfg.resolved()
+    Ws = W.xavier_weights(d, H * hd, nk * hd, seed=0)
+    layer = W.MhaLayer(cfg, *Ws, dtype=1)
+    kv = W.KvCache(layer, B, 256)
+    n = B * L * nk * hd
+    kcb = torch.from_numpy(W.synthetic(n, 2, 1, 0.5).reshape(B, L, nk * hd)).cuda().to(torch.bfloat16)
+    vcb = torch.from_numpy(W.synthetic(n, 2, 1, 0.5, offset=n).reshape(B, L, nk * hd)).cuda().to(torch.bfloat16)
+    kv.fill(B, L, kcb, vcb)
+    x = torch.from_numpy(W.synthetic(B * d, 1, 1, 1.0).reshape(B, d)).cuda().to(torch.bfloat16)
+    post = torch.zeros(B, d, device="cuda", dtype=torch.bfloat16)
+    pre = torch.zeros(B, H * hd, device="cuda", dtype=torch.bfloat16)
+    layer.decode(kv, B, x, pre, post)
+    torch.cuda.synchronize()
+    layer.check_device()
+    oc = O.MhaCfg(d_model=d, num_heads=H, num_kv_heads=NK, pos=pos, softmax=softmax, per_sequence=1)
+    rpre, rpost, _, _ = O.mha_decode(oc, [L] * B, kcb.float().cpu().numpy(), vcb.float().cpu().numpy(),
+                                     *Ws, x.float().cpu().numpy())
+    assert rel_err(pre.float().cpu().numpy(), rpre) < LOW_TOL
+    assert rel_err(post.float().cpu().numpy(), rpost) < LOW_TOL
