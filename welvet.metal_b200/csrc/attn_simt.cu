@@ -387,6 +387,7 @@ __global__ void kv_append_kernel(const T* k, const T* v, int ld, int rows, int k
 cudaError_t attn_prefill_simt(const AttnArgs& a, cudaStream_t s) {
   if (a.head_dim <= 0 || a.head_dim > 256 || a.num_kv_heads <= 0 || a.num_heads % a.num_kv_heads)
     return cudaErrorInvalidValue;
+  if (attn_f32_supported(a)) return attn_prefill_f32(a, s);
   dim3 grid((a.seq + kRows - 1) / kRows, a.num_heads, a.batch);
   const size_t smem = sizeof(float) * (kRows * a.head_dim + 2 * kKeys * (a.head_dim + 1));
   MaskP mp{a.mask, a.window, a.max_seq_len, a.prefix_len, a.window_causal};

@@ -144,6 +144,9 @@ struct AttnArgs {
 bool attn_tc_supported(const AttnArgs& a);
 cudaError_t attn_prefill_tc(const AttnArgs& a, cudaStream_t s);
 cudaError_t attn_prefill_simt(const AttnArgs& a, cudaStream_t s);
+// FP32, head_dim 64/128, no ring wrap: register-tiled CUDA-core kernel (attn_f32.cu).
+bool attn_f32_supported(const AttnArgs& a);
+cudaError_t attn_prefill_f32(const AttnArgs& a, cudaStream_t s);
 
 // Split-KV decode over a paged cache. Pools hold pages of kPageTokens rows of
 // kd values (K and V separately, bf16 or fp32); block_table[b, j] names the
