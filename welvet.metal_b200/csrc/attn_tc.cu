@@ -3,21 +3,25 @@
 // reference's single-thread attention loop (shaders/ops_mha.metal:31-127).
 //
 // One CTA per (128-query tile, head, sequence), heaviest causal tiles first:
-//   warp 0     TMA producer: Q once, then K_j / V_j (128 keys) into two rings
-//   warp 1     UMMA issuer: S_j = Q K_j^T into TMEM buffer S_{j&1}, and
-//              O_{j&1} += P_j V_j (P from shared memory, V as an MN-major operand)
-//   warps 2-9  two softmax warpgroups; warpgroup g owns the key blocks j == g
-//              (mod 2) as an independent partial softmax (own running max, sum,
-//              P tile and O accumulator) — one query row per thread, its TMEM
-//              lane. The two partial results are merged once, at the end.
-// Per block a warpgroup scales, masks (attn_allow, ops_mha.metal:1-12, evaluated
-// only on blocks that straddle the mask edge), applies ALiBi, keeps an online
-// max/sum in the log2 domain and writes P to its swizzled smem tile. O is
-// rescaled only when a row maximum grows by more than 2^8 (exact: the final
-// division uses the same reference maximum as every P), and then without any
-// extra wait, since the last PV into that O is the one that freed the P tile.
-// While one warpgroup works on block j the tensor cores run S_{j+1} and PV_{j-1}
-// of the other, so the softmax of two blocks is always in flight.
+//   warps 0-7  two softmax warpgroups; warpgroup g owns the key blocks j == g
+//              (mod 2) as an independent partial softmax (own running max, sum
+//              and O accumulator) — one query row per thread, its TMEM lane. The
+//              two partial results are merged once, at the end.
+//   warp 8     TMA: Q once, then K_j (128 keys) into the K ring
+//   warp 9     UMMA issuer (one thread): S_j = Q K_j^T (SS) into TMEM buffer
+//              S_{j&1}; O_{j&1} += P_j V_j as a TS MMA whose A operand is P_j in
+//              TMEM (V an MN-major shared-memory operand)
+//   warp 10    TMA: V_j into the V ring
+// Per block a warpgroup copies S_j into registers, scales, masks (attn_allow,
+// ops_mha.metal:1-12, evaluated only on blocks that straddle the mask edge),
+// applies ALiBi, keeps an online max/sum in the log2 domain and writes P_j as bf16
+// pairs over the first 64 columns of S_j. Issue order S_0, S_1, then per block i:
+// PV_i, S_{i+2}; MMAs of one thread run in order, so S_{i+2} overwrites the buffer
+// only after PV_i has read P_i, and the arrival of S_{j+2} also tells the
+// warpgroup that PV_j is done, i.e. O is current. O is rescaled only when a row
+// maximum grows by more than 2^8 (exact: the final division uses the same
+// reference maximum as every P). While one warpgroup works on block j the tensor
+// core runs PV and S of the other's blocks.
 #include "common.cuh"
 #include "kernels.h"
 
