@@ -6,7 +6,10 @@
 // serial loop (F1 in the survey of the reference) is replaced by
 // (query-tile x head x sequence) parallelism.
 //
-// Also: split-KV decode over a paged KV cache and the KV append kernel.
+// FP32 inputs with head_dim 64/128 and no ring wrap go to the register-tiled
+// kernel of attn_f32.cu instead. Also here: the split-KV decode entry (BF16 shapes
+// go to decode_tc.cu, the rest to the CUDA-core decode_kernel below), the split
+// combine kernel and the KV append kernel.
 #include "common.cuh"
 #include "kernels.h"
 
