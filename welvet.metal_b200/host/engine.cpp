@@ -555,7 +555,7 @@ Status mha_forward(Mha* m, int batch, int seq, const void* x, void* pre, void* p
   const bool chunked = (m->comm || !on_device) && !stream_mode && !kv && batch > 1;
   // Host copies (about 40 ms per 2 GB each way on PCIe) want more, smaller chunks
   // than the all-reduce does.
-  const int chunks = chunked ? std::min(batch, on_device ? Mha::kMaxChunks / 2 : Mha::kMaxChunks) : 1;
+  const int chunks = chunked ? std::min(batch, on_device ? 4 : Mha::kMaxChunks) : 1;
   if (!on_device) {
     WV_TRY(m->x_io.ensure(M * dm * es));
     WV_TRY(m->post_io.ensure(M * dm * es));

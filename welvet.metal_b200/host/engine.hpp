@@ -137,7 +137,7 @@ struct Mha {
   void* comm = nullptr;
   int nranks = 1, rank = 0;
   cudaStream_t comm_stream = nullptr;
-  static constexpr int kMaxChunks = 8;
+  static constexpr int kMaxChunks = 16;
   cudaEvent_t chunk_done[kMaxChunks] = {};
   cudaEvent_t comm_done = nullptr;
   // host-buffer calls: input copies (io_in) and output copies (io_out) of the chunks
