@@ -47,14 +47,22 @@ WORKLOADS = {
     "cfg4-nf4": dict(B=4, T=4096, d=4096, H=32, NK=32, wf=2, prec=1, kind="prefill"),
     "cfg3": dict(B=64, T=4096, d=2048, H=32, NK=8, wf=0, prec=1, kind="decode"),
     "cfg2": dict(B=8, T=2048, d=1024, H=16, NK=16, wf=0, prec=0, kind="prefill"),
+    # FormatNone weight round trip (mount-time encode -> decode), all dtypes 0-33
+    "codec": dict(n=1 << 28, kind="codec"),
 }
+CODEC_DTYPES = range(34)
+CODEC_STATS_FREE = (0, 1, 2, 3, 4, 5, 16, 24, 25)  # dtypes without a per-tensor statistics pass
 
 METRIC = "MHA prefill tok/s (BASELINE config 5; decode tok/s under 'decode')"
 METRIC_DECODE = "MHA decode tok/s (BASELINE config 3)"
+METRIC_CODEC = "FormatNone weight round trip GB/s (decode(encode(w)), dtypes 0-33)"
 
 
 def workload(args):
     w = dict(WORKLOADS[args.workload])
+    if w["kind"] == "codec":
+        w["n"] = args.batch or w["n"]
+        return w
     w["B"] = args.batch or w["B"]
     w["T"] = args.seq or w["T"]
     w["hd"] = w["d"] // w["H"]
@@ -64,6 +72,10 @@ def workload(args):
 def workload_config(args, world):
     """The `config` object of the JSON line, the same for both arms."""
     w = workload(args)
+    if w["kind"] == "codec":
+        return {"workload": f"codec: decode(encode(w)) of {w['n']} FP32 weights, FormatNone dtypes 0-33",
+                "global_batch": w["n"], "seq_len": 1, "parallelism": f"replicas x{world}",
+                "l2": "tensor larger than L2 (%.2f GB)" % (w["n"] * 4 / 1e9)}
     B, T, d, H, NK, hd, wf = w["B"], w["T"], w["d"], w["H"], w["NK"], w["hd"], w["wf"]
     fmt = " fp8 weights" if wf == 1 else " nf4 weights" if wf == 2 else ""
     es = 2 if w["prec"] == 1 else 4
@@ -177,6 +189,32 @@ def cpu_sample_decode(w, B_s, threads=0):
     return time.perf_counter() - t0
 
 
+def codec_bytes(n, dtype):
+    """Algorithmic HBM bytes of one round trip: the statistics pass reads w once,
+    the element pass reads w and writes the result."""
+    return n * 4 * (2 if dtype in CODEC_STATS_FREE else 3)
+
+
+def codec_cpu_sample(n_s, use_ref):
+    """Times decode(encode(w)) of every dtype on n_s weights on one host core:
+    the reference's own WeightStore round trip (oracle/_ref) or the C port.
+    Returns (seconds, bytes in the GPU arm's accounting)."""
+    import oracle_py as O
+    import welvet_b200 as W
+    w = W.synthetic(n_s, 0, 1, 0.02)
+    wm = w.reshape(-1, 1024)
+    t0 = time.perf_counter()
+    for dt in CODEC_DTYPES:
+        if use_ref:
+            code, msg, _, _, _ = O.ref_weight_roundtrip(dt, wm)
+            if code:
+                raise RuntimeError(msg)
+        else:
+            O.roundtrip(dt, w)
+    dt_s = time.perf_counter() - t0
+    return dt_s, sum(codec_bytes(n_s, d) for d in CODEC_DTYPES)
+
+
 def run_reference(args):
     """Reference arm: the reference's own MHA code (mha.cpp + dense.cpp + soft-double
     shaders, oracle/_ref) on the host cores through its one-shot entry
@@ -190,6 +228,29 @@ def run_reference(args):
     if w["kind"] == "decode":
         print(json.dumps({"impl": "reference", "unavailable": "the reference MHA has no KV cache or decode step"}),
               flush=True)
+        return
+    if w["kind"] == "codec":
+        use_ref = O.ref_available()
+        n_s = 1 << 20
+        for _ in range(args.warmup):
+            codec_cpu_sample(1 << 16, use_ref)
+        tot_s = tot_b = 0.0
+        for _ in range(args.steps):
+            dt_s, b = codec_cpu_sample(n_s, use_ref)
+            tot_s += dt_s
+            tot_b += b
+        value = tot_b / tot_s / 1e9
+        kind = "reference" if use_ref else "port"
+        sample = f"{n_s} weights (1024-wide rows) x 34 dtypes per step, one core, WeightStore round trip"
+        print(json.dumps({"impl": "reference", "metric": METRIC_CODEC, "value": value, "unit": "GB/s",
+                          "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                          "ms_per_step": tot_s / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+                          "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                          "config": workload_config(args, args.gpus),
+                          "cpu_baseline": {"value": value, "unit": "GB/s", "cores": 1, "kind": kind,
+                                           "sample": sample},
+                          "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0,
+                                  "d2h_bytes_per_step": 0}}), flush=True)
         return
     B, T, d, H, NK, hd = w["B"], w["T"], w["d"], w["H"], w["NK"], w["hd"]
     pf, af = flops_prefill(B, T, d, H, NK, hd)
@@ -228,6 +289,112 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_codec(args, rank, world, local):
+    """FormatNone round trips (the mount-time weight codec) of one 1 GiB FP32 tensor
+    per GPU, every dtype in turn; a step = all 34 dtypes. Replicas only: each rank
+    converts its own tensor, no collective."""
+    import torch
+    import torch.distributed as dist
+    import welvet_b200 as W
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    n = workload(args)["n"]
+    w = torch.empty(n, device="cuda", dtype=torch.float32)
+    W.fill_synthetic(w, 0, 1, 0.02, offset=rank * n)
+    out = torch.empty_like(w)
+    stream = torch.cuda.current_stream()
+    pk = peaks()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        for dt in CODEC_DTYPES:
+            W.codec_roundtrip(dt, w, out, stream=stream)
+    barrier()
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(len(CODEC_DTYPES) + 1)]
+    clocks = Clocks(local)
+    clocks.start()
+    W.launch_count(reset=True)
+    barrier()
+    per = {dt: 0.0 for dt in CODEC_DTYPES}
+    t_all = 0.0
+    for _ in range(args.steps):
+        evs[0].record(stream)
+        for i, dt in enumerate(CODEC_DTYPES):
+            W.codec_roundtrip(dt, w, out, stream=stream)
+            evs[i + 1].record(stream)
+        stream.synchronize()
+        for i, dt in enumerate(CODEC_DTYPES):
+            per[dt] += evs[i].elapsed_time(evs[i + 1])
+        t_all += evs[0].elapsed_time(evs[-1])
+    barrier()
+    launches = W.launch_count(reset=True)
+    clk = clocks.stop()
+    W.device_check()
+    ms = max_over_ranks(t_all / args.steps)
+    step_bytes = sum(codec_bytes(n, dt) for dt in CODEC_DTYPES)
+    value = world * step_bytes / (ms / 1e3) / 1e9
+    per_dtype = {str(dt): {"ms": per[dt] / args.steps,
+                           "gbs": codec_bytes(n, dt) / (per[dt] / args.steps / 1e3) / 1e9} for dt in CODEC_DTYPES}
+    slow = min(per_dtype, key=lambda k: per_dtype[k]["gbs"])
+    achieved = step_bytes / (ms / 1e3) / 1e9
+    roof = {"bound": "hbm", "kernel": "roundtrip_kernel + stats_first (all dtypes)", "achieved": achieved,
+            "peak": pk["hbm"], "unit": "GB/s", "frac": achieved / pk["hbm"],
+            "peak_kind": f"{pk['src']} HBM copy (of {pk['src']})", "traffic": None,
+            "bytes_per_step": step_bytes, "slowest_dtype": {slow: per_dtype[slow]}}
+    # end to end: pinned host weights -> device, round trip, result back to the host
+    e2e = None
+    if not args.no_e2e:
+        n_e = min(n, 1 << 26)
+        wh = w[:n_e].cpu().pin_memory()
+        oh = torch.empty(n_e, dtype=torch.float32).pin_memory()
+        wd = torch.empty(n_e, device="cuda", dtype=torch.float32)
+        od = torch.empty_like(wd)
+        barrier()
+        ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0 = time.perf_counter()
+        ea.record(stream)
+        for dt in CODEC_DTYPES:
+            wd.copy_(wh, non_blocking=True)
+            W.codec_roundtrip(dt, wd, od, stream=stream)
+            oh.copy_(od, non_blocking=True)
+        eb.record(stream)
+        barrier()
+        e_ms = max_over_ranks(max(ea.elapsed_time(eb), (time.perf_counter() - t0) * 1e3))
+        e_bytes = sum(codec_bytes(n_e, dt) for dt in CODEC_DTYPES)
+        e2e = {"value": world * e_bytes / (e_ms / 1e3) / 1e9, "unit": "GB/s", "ms_per_step": e_ms,
+               "h2d_bytes_per_step": 34 * n_e * 4, "d2h_bytes_per_step": 34 * n_e * 4,
+               "api": "welvet_b200_codec_roundtrip between pinned host copies (%d weights)" % n_e}
+        del wh, oh, wd, od
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        dt_s, b = codec_cpu_sample(1 << 20, False)
+        cpu = {"value": b / dt_s / 1e9, "unit": "GB/s", "cores": 1, "kind": "port",
+               "sample": f"C port of the round trip, 1048576 weights x 34 dtypes, {dt_s:.2f} s"}
+    if rank == 0:
+        print(json.dumps({"metric": METRIC_CODEC, "value": value, "unit": "GB/s", "n_gpus": world,
+                          "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+                          "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                          "data": "synthetic (SplitMix64 normal(0, 0.02) weights)",
+                          "config": workload_config(args, world), "roofline": roof, "cpu_baseline": cpu,
+                          "e2e": e2e, "gpu_launches": launches, "clocks": clk, "per_dtype": per_dtype}),
+              flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -257,6 +424,8 @@ def main():
 
     import welvet_b200 as W
     torch.cuda.set_device(local)
+    if workload(args)["kind"] == "codec":
+        return run_codec(args, rank, world, local)
     if world > 1:
         # NVLS (in-switch reduction) is off unless the caller sets it: on this pool's
         # 8-GPU boxes the 256 KB decode all-reduce took 31 ms with NVLS and 0.05 ms

@@ -131,7 +131,9 @@ WELVET_API welvet_status welvet_b200_attention(const welvet_b200_mha_config* cfg
                                                void* stream);
 /* Codec kernels, bit-exact to the reference converters
  * (src/core/float_codecs.cpp, src/weights/native_codec.cpp:189-813):
- * roundtrip: out = decode(encode(w)) for FormatNone dtype; nf4 scale = absmax. */
+ * roundtrip: out = decode(encode(w)) for any FormatNone dtype 0-33 (per-tensor
+ * absmax / min / max computed on the device; out may equal w); encode/decode: the
+ * stored bytes of dtypes 0-5 and 26 (nf4 scale = absmax). */
 WELVET_API welvet_status welvet_b200_codec_roundtrip(int32_t dtype, const float* w, float* out,
                                                      int64_t n, void* stream);
 WELVET_API welvet_status welvet_b200_codec_encode(int32_t dtype, const float* w, void* codes,

@@ -9,8 +9,11 @@
 #include <cmath>
 #include <cstring>
 #include <limits>
+#include <vector>
 
 namespace {
+// FP4 (e2m1) grid of the reference converter, code order (float_codecs.cpp:184).
+constexpr float kFp4Grid[16] = {0, 0.5f, 1, 1.5f, 2, 3, 4, 6, -0.0f, -0.5f, -1, -1.5f, -2, -3, -4, -6};
 
 uint32_t bits(float f) {
   uint32_t u;
@@ -253,6 +256,157 @@ int32_t oracle_decode(int32_t dtype, const uint8_t* raw, int64_t n, float scale,
     for (int64_t i = 0; i < n; ++i) {
       const int code = (i % 2 == 0) ? (raw[i / 2] & 0xf) : (raw[i / 2] >> 4);
       out[i] = kNf4Levels[code] * s;
+    }
+    return 0;
+  }
+  default:
+    return -2;
+  }
+}
+
+// decode(encode(w)) for every FormatNone dtype of the reference
+// (pack_native, src/weights/native_codec.cpp:189-560, and weight_at /
+// decode_row_f64, :561-870), element by element in float arithmetic without
+// contraction. Per-tensor statistics: absmax (signed formats, Ternary, Binary,
+// NF4) or min/max (unsigned formats, stored minimum added back on decode).
+// Platform choices of the reference as built here (x86-64): Int and Uint are the
+// 64-bit forms, and a double at or above 2^31 converted to int32 (Int32's
+// positive absmax element, w/s*2147483648.0f) gives INT32_MIN.
+int32_t oracle_roundtrip(int32_t dtype, const float* w, int64_t n, float* out) {
+  if (n <= 0) return 0;
+  float amax = absmax(w, n), mn = w[0], mx = w[0];
+  for (int64_t i = 1; i < n; ++i) {
+    if (w[i] < mn) mn = w[i];
+    if (w[i] > mx) mx = w[i];
+  }
+  const float span = (mx - mn) == 0 ? 1.0f : (mx - mn);
+  auto rnd = [](double v) { return std::round(v); };
+  auto clampd = [](double v, double lo, double hi) { return v < lo ? lo : (v > hi ? hi : v); };
+  auto signed_nbit = [&](int bits) {
+    const int max_q = (1 << (bits - 1)) - 1, min_q = -(1 << (bits - 1));
+    float s = amax / (float)max_q;
+    if (s == 0) s = 1;
+    for (int64_t i = 0; i < n; ++i) {
+      int q = (int)std::round(w[i] / s);
+      q = q > max_q ? max_q : (q < min_q ? min_q : q);
+      out[i] = (float)q * s;
+    }
+  };
+  auto unsigned_q = [&](float maxq_f, double clamp_hi, bool as_u64) {
+    const float scale = span / maxq_f;
+    for (int64_t i = 0; i < n; ++i) {
+      const float qf = (w[i] - mn) / span * maxq_f;
+      const double q = clampd(rnd((double)qf), 0.0, clamp_hi);
+      const float fq = as_u64 ? (float)(uint64_t)q : (float)(uint32_t)q;
+      out[i] = fq * scale + mn;
+    }
+  };
+  switch (dtype) {
+  case 0: case 24: case 25:  // Float64, Complex64 / Complex128 (real part)
+    for (int64_t i = 0; i < n; ++i) out[i] = (float)(double)w[i];
+    return 0;
+  case 1:
+    std::memcpy(out, w, (size_t)n * 4);
+    return 0;
+  case 2: case 3: case 4: case 5: case 26: {
+    std::vector<uint8_t> raw((size_t)n * 8 + 8);
+    float scale = 1.0f;
+    if (oracle_encode(dtype, w, n, raw.data(), &scale) < 0) return -2;
+    return oracle_decode(dtype, raw.data(), n, scale, out);
+  }
+  case 6: case 21: {  // Int64, Int (64-bit host): w/s*1e6 rounded
+    const float s = amax == 0 ? 1.0f : amax, scale = s / 1e6f;
+    for (int64_t i = 0; i < n; ++i) {
+      const float qf = w[i] / s * 1e6f;
+      out[i] = (float)(int64_t)rnd((double)qf) * scale;
+    }
+    return 0;
+  }
+  case 7: {  // Int32
+    const float s = amax == 0 ? 1.0f : amax, scale = s / 2147483647.0f;
+    for (int64_t i = 0; i < n; ++i) {
+      const float qf = w[i] / s * 2147483647.0f;
+      const double r = rnd((double)qf);
+      const int32_t q = (r >= 2147483648.0 || r < -2147483648.0) ? INT32_MIN : (int32_t)r;
+      out[i] = (float)q * scale;
+    }
+    return 0;
+  }
+  case 8: {  // Int16
+    const float s = amax == 0 ? 1.0f : amax, scale = s / 32767.0f;
+    for (int64_t i = 0; i < n; ++i) {
+      const float qf = w[i] / s * 32767.0f;
+      out[i] = (float)(int)clampd(rnd((double)qf), -32768.0, 32767.0) * scale;
+    }
+    return 0;
+  }
+  case 9: {  // Int8
+    float s = amax / 127.0f;
+    if (s == 0) s = 1;
+    for (int64_t i = 0; i < n; ++i) out[i] = (float)(int)clampd(std::round(w[i] / s), -128.0, 127.0) * s;
+    return 0;
+  }
+  case 13: unsigned_q(255.0f, 255.0, false); return 0;                     // Uint8
+  case 12: unsigned_q(65535.0f, 65535.0, false); return 0;                 // Uint16
+  case 11: unsigned_q((float)4294967295u, 4294967295.0, false); return 0;  // Uint32
+  case 10: case 22: case 23: unsigned_q(1e15f, 1e15, true); return 0;      // Uint64, Uint, Uintptr
+  case 14: {  // Int4
+    float s = amax / 7.0f;
+    if (s == 0) s = 1;
+    for (int64_t i = 0; i < n; ++i) out[i] = (float)(int)clampd(std::round(w[i] / s), -8.0, 7.0) * s;
+    return 0;
+  }
+  case 15: unsigned_q(15.0f, 15.0, false); return 0;  // Uint4
+  case 16:  // FP4: nearest grid value, no scale
+    for (int64_t i = 0; i < n; ++i) {
+      int best = 0;
+      float best_err = std::numeric_limits<float>::max();
+      for (int c = 0; c < 16; ++c) {
+        const float e = std::fabs(w[i] - kFp4Grid[c]);
+        if (e < best_err) {
+          best_err = e;
+          best = c;
+        }
+      }
+      out[i] = kFp4Grid[best];
+    }
+    return 0;
+  case 17: {  // Int2
+    const float s = amax == 0 ? 1.0f : amax;
+    for (int64_t i = 0; i < n; ++i) out[i] = (float)(int)clampd(std::round(w[i] / s), -2.0, 1.0) * s;
+    return 0;
+  }
+  case 18: {  // Uint2: ((w-mn)/span) in float, times 3.0 in double
+    const float scale = span / 3.0f;
+    for (int64_t i = 0; i < n; ++i) {
+      const int q = (int)clampd(rnd((double)((w[i] - mn) / span) * 3.0), 0.0, 3.0);
+      out[i] = (float)q * scale + mn;
+    }
+    return 0;
+  }
+  case 19: {  // Ternary
+    const float s = amax == 0 ? 1.0f : amax;
+    for (int64_t i = 0; i < n; ++i) {
+      const float r = w[i] / s;
+      out[i] = r > 0.5f ? s : (r < -0.5f ? -s : 0.0f);
+    }
+    return 0;
+  }
+  case 20: {  // Binary
+    const float s = amax == 0 ? 1.0f : amax;
+    for (int64_t i = 0; i < n; ++i) out[i] = w[i] >= 0 ? s : -s;
+    return 0;
+  }
+  case 27: case 28: signed_nbit(6); return 0;  // FP6 (stored as signed 6-bit), Int6
+  case 30: signed_nbit(5); return 0;             // Int5
+  case 32: signed_nbit(3); return 0;             // Int3
+  case 29: case 31: case 33: {                   // Uint6, Uint5, Uint3
+    const int bits = dtype == 29 ? 6 : (dtype == 31 ? 5 : 3);
+    const int max_q = (1 << bits) - 1;
+    const float scale = span / (float)max_q;
+    for (int64_t i = 0; i < n; ++i) {
+      const int q = (int)clampd(std::round((w[i] - mn) / span * max_q), 0.0, (double)max_q);
+      out[i] = (float)q * scale + mn;
     }
     return 0;
   }

@@ -82,6 +82,8 @@ float oracle_nf4_level(int32_t code);  /* kNf4, native_codec.cpp:93-110 */
 int64_t oracle_encode(int32_t dtype, const float* w, int64_t n, uint8_t* out, float* scale);
 /* weight_at() decode of every element (native_codec.cpp:562-813). */
 int32_t oracle_decode(int32_t dtype, const uint8_t* raw, int64_t n, float scale, float* out);
+// decode(encode(w)) for every FormatNone dtype 0-33 (0 ok, -2 unsupported).
+int32_t oracle_roundtrip(int32_t dtype, const float* w, int64_t n, float* out);
 
 /* Extension formats (no reference counterpart; element codes use the reference
  * converters above):

@@ -100,6 +100,8 @@ def _load_oracle():
     lib.oracle_encode.argtypes = [C.c_int32, _f32p, C.c_int64, _u8p, C.POINTER(C.c_float)]
     lib.oracle_encode.restype = C.c_int64
     lib.oracle_decode.argtypes = [C.c_int32, _u8p, C.c_int64, C.c_float, _f32p]
+    lib.oracle_roundtrip.argtypes = [C.c_int32, _f32p, C.c_int64, _f32p]
+    lib.oracle_roundtrip.restype = C.c_int32
     lib.oracle_decode.restype = C.c_int32
     for name, a, r in (("oracle_bf16_encode", C.c_float, C.c_uint16), ("oracle_bf16_decode", C.c_uint16, C.c_float),
                        ("oracle_f16_encode", C.c_float, C.c_uint16), ("oracle_f16_decode", C.c_uint16, C.c_float),
@@ -270,6 +272,16 @@ def ref_mha_forward(cfg: MhaCfg, batch: int, seq: int, Wq, Wk, Wv, Wo, x, dtype:
                                  r.window_causal, r.rope_theta, r.scale_override, dtype,
                                  _f32(Wq), _f32(Wk), _f32(Wv), _f32(Wo), _f32(x), pre, post)
     return st.code, st.message.decode(), pre, post
+
+
+def roundtrip(dtype: int, w) -> np.ndarray:
+    """decode(encode(w)) of the oracle port for FormatNone dtypes 0-33."""
+    w = _f32(w)
+    out = np.empty_like(w)
+    st = oracle_lib().oracle_roundtrip(dtype, w, w.size, out)
+    if st:
+        raise ValueError(f"oracle_roundtrip: dtype {dtype} unsupported")
+    return out
 
 
 def ref_weight_roundtrip(dtype: int, w):

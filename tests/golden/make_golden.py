@@ -43,7 +43,42 @@ MHA_CASES = {
     "hd64_two_seq": (dict(d_model=128, num_heads=2, max_seq_len=64), 2, 32, 1),
     "hd128": (dict(d_model=256, num_heads=2, max_seq_len=64), 1, 24, 1),
     "hd64_gqa_window": (dict(d_model=256, num_heads=4, num_kv_heads=2, mask=3, window=7, max_seq_len=64), 1, 40, 1),
+    # integer / sub-byte FormatNone dtypes (native_codec.cpp:189-870)
+    "int64": (dict(d_model=64, num_heads=4), 1, 8, 6),
+    "int32": (dict(d_model=64, num_heads=4), 1, 8, 7),
+    "int8_gqa": (dict(d_model=64, num_heads=4, num_kv_heads=2), 2, 8, 9),
+    "uint8": (dict(d_model=64, num_heads=4), 1, 8, 13),
+    "uint64": (dict(d_model=64, num_heads=4), 1, 8, 10),
+    "int4": (dict(d_model=64, num_heads=4), 1, 8, 14),
+    "uint4": (dict(d_model=64, num_heads=4), 1, 8, 15),
+    "fp4": (dict(d_model=64, num_heads=4), 1, 8, 16),
+    "uint2_causal_window": (dict(d_model=64, num_heads=4, mask=3, window=4), 1, 12, 18),
+    "ternary": (dict(d_model=64, num_heads=4), 1, 8, 19),
+    "binary": (dict(d_model=64, num_heads=4), 1, 8, 20),
+    "fp6_bidir": (dict(d_model=64, num_heads=4, mask=2), 1, 8, 27),
+    "uint5": (dict(d_model=64, num_heads=4), 1, 8, 31),
+    "int3": (dict(d_model=64, num_heads=4), 1, 8, 32),
 }
+
+# Extra matrices for the all-dtype round trips: positive absmax (Int32's
+# out-of-range conversion), all zeros (absmax 0 and span 0), a constant.
+def codec_matrices(w):
+    wp = synthetic(8 * 64, 5, 0, 0.3).reshape(8, 64)
+    wp[3, 7] = 1.5
+    wp[5, 9] = -0.75
+    return {"w": w, "wpos": wp, "wzero": np.zeros((4, 16), np.float32),
+            "wconst": np.full((4, 16), 0.7, np.float32)}
+
+
+def _save(path, **arrays):
+    """Writes the npz only when its arrays changed, so a rerun leaves git clean."""
+    if os.path.exists(path):
+        old = dict(np.load(path))
+        if old.keys() == arrays.keys() and all(
+                old[k].dtype == np.asarray(v).dtype and old[k].shape == np.shape(v)
+                and old[k].tobytes() == np.asarray(v).tobytes() for k, v in arrays.items()):
+            return
+    np.savez_compressed(path, **arrays)
 
 
 def weights_for(cfg: O.MhaCfg):
@@ -70,7 +105,7 @@ def main():
         if code:
             raise SystemExit(f"{name}: reference returned {code} {msg}")
         out[name] = dict(cfg=kw, batch=B, seq=T, dtype=dtype, wsum=wsum((Wq, Wk, Wv, Wo)))
-        np.savez_compressed(os.path.join(HERE, f"mha_{name}.npz"), x=x, pre=pre, post=post)
+        _save(os.path.join(HERE, f"mha_{name}.npz"), x=x, pre=pre, post=post)
     with open(os.path.join(HERE, "mha_cases.json"), "w") as f:
         json.dump(out, f, indent=1, sort_keys=True)
 
@@ -100,8 +135,17 @@ def main():
         rt[f"native_{dt}"] = native
         rt[f"scale_{dt}"] = np.float32(scale)
         rt[f"dec_{dt}"] = dec
-    np.savez_compressed(os.path.join(HERE, "codecs.npz"), e4m3_dec=e4m3_dec, e5m2_dec=e5m2_dec, probes=probes,
-                        e4m3_enc=e4m3_enc, e5m2_enc=e5m2_enc, bf16_enc=bf16_enc, f16_enc=f16_enc, w=w, **rt)
+    # decode(encode(w)) of every FormatNone dtype 0-33 on each matrix.
+    mats = codec_matrices(w)
+    for mname, m in mats.items():
+        for dt in range(34):
+            code, msg, _, _, dec = O.ref_weight_roundtrip(dt, m)
+            if code:
+                raise SystemExit(f"roundtrip dtype {dt} on {mname}: {code} {msg}")
+            rt[f"rt_{mname}_{dt}"] = dec
+    mats.pop("w")
+    _save(os.path.join(HERE, "codecs.npz"), e4m3_dec=e4m3_dec, e5m2_dec=e5m2_dec, probes=probes,
+          e4m3_enc=e4m3_enc, e5m2_enc=e5m2_enc, bf16_enc=bf16_enc, f16_enc=f16_enc, w=w, **mats, **rt)
     print(f"wrote {len(MHA_CASES)} MHA cases and codecs.npz to {HERE}")
 
 

@@ -109,6 +109,75 @@ def test_codec_roundtrip_bitexact_against_reference(torch_cuda):
                                       err_msg=f"dtype {dt}")
 
 
+@pytest.mark.parametrize("dtype", range(34))
+def test_codec_roundtrip_all_dtypes_bitexact(torch_cuda, dtype):
+    """Device decode(encode(w)) of every FormatNone dtype against the reference's
+    own round trips (golden) and, on a 3M-element tensor that spans many blocks of
+    the statistics reduction, against the oracle port."""
+    torch = torch_cuda
+    g = dict(np.load(f"{GOLDEN}/codecs.npz"))
+    for m in ("w", "wpos", "wzero", "wconst"):
+        w = _dev(torch, g[m].ravel())
+        out = torch.empty_like(w)
+        W.codec_roundtrip(dtype, w, out)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(out.cpu().numpy().view(np.uint32), g[f"rt_{m}_{dtype}"].ravel().view(np.uint32),
+                                      err_msg=f"{m} dtype {dtype}")
+    big = W.synthetic(3 << 20, 11, 1, 0.05)
+    big[123457] = 0.9      # positive absmax, far from block 0
+    big[2999999] = -0.4    # minimum in the last block
+    w = _dev(torch, big)
+    out = torch.empty_like(w)
+    W.codec_roundtrip(dtype, w, out)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(out.cpu().numpy().view(np.uint32), O.roundtrip(dtype, big).view(np.uint32))
+
+
+def _nearest_value_edges():
+    """Values at and one ulp either side of every midpoint of the NF4 levels and
+    of the FP4 grid (where the reference's first-minimum scan breaks ties), plus
+    the extremes where the FP4 scan's rounded errors tie or reach FLT_MAX."""
+    nf4 = np.array([O.oracle_lib().oracle_nf4_level(c) for c in range(16)], np.float32)
+    fp4 = np.array([0, 0.5, 1, 1.5, 2, 3, 4, 6], np.float32)
+    vals = [0.0, -0.0, 1.0, -1.0]
+    for grid in (fp4, -fp4, nf4):
+        g = np.sort(grid)
+        mids = ((g[:-1] + g[1:]) / np.float32(2)).astype(np.float32)
+        for m in mids:
+            vals += [m, np.nextafter(m, np.float32(np.inf)), np.nextafter(m, np.float32(-np.inf))]
+    big = np.float32(3.4028235e38)
+    vals += [6.0, 6.5, 7.0, 1e7, 16777216.0, 16777220.0, 3e38, big, -big, np.nextafter(big, np.float32(0)),
+             1e-30, -1e-30, -6.5, -1e9]
+    return np.array(vals, np.float32)
+
+
+@pytest.mark.parametrize("dtype", [16, 26])
+def test_codec_nearest_value_ties(torch_cuda, dtype):
+    torch = torch_cuda
+    v = _nearest_value_edges()
+    if dtype == 26:
+        v = np.clip(v, -1, 1).astype(np.float32)  # absmax 1: r = w exactly
+    else:
+        v = np.concatenate([v, np.array([np.inf, -np.inf, np.nan], np.float32)])
+    v = np.tile(v, 5)  # vector body and tail
+    for off in (0, 1):  # 16-byte aligned and element-aligned (scalar) paths
+        w = torch.zeros(v.size + 1, dtype=torch.float32, device="cuda")
+        w[off:off + v.size] = torch.from_numpy(v).cuda()
+        out = torch.zeros_like(w)
+        W.codec_roundtrip(dtype, w[off:off + v.size], out[off:off + v.size])
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(out[off:off + v.size].cpu().numpy().view(np.uint32),
+                                      O.roundtrip(dtype, v).view(np.uint32), err_msg=f"offset {off}")
+    if dtype == 26:
+        w = _dev(torch, v)
+        packed = torch.empty((v.size + 1) // 2, dtype=torch.uint8, device="cuda")
+        amax = torch.empty((v.size + 63) // 64, dtype=torch.float32, device="cuda")
+        W.nf4_block_encode(w, packed, amax)
+        torch.cuda.synchronize()
+        p_o, a_o, _ = O.nf4_block(v, 64)
+        np.testing.assert_array_equal(packed.cpu().numpy(), p_o)
+
+
 def test_codec_encode_bytes_match_reference(torch_cuda):
     torch = torch_cuda
     g = dict(np.load(f"{GOLDEN}/codecs.npz"))

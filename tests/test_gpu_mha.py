@@ -70,8 +70,7 @@ def _oracle_weights(Ws, dtype, weight_format):
         elif weight_format == 2:
             out.append(O.nf4_block(w, 64)[2])
         else:
-            raw, s = O.encode(dtype, w)
-            out.append(O.decode(dtype, raw, w.size, s).reshape(w.shape))
+            out.append(O.roundtrip(dtype, w).reshape(w.shape))
     return out
 
 

@@ -3,7 +3,11 @@
 // multiple of the SM count, 16-byte accesses where the layout allows.
 #include "codec.cuh"
 #include "common.cuh"
+#include "formatnone.cuh"
 #include "kernels.h"
+
+#include <array>
+#include <utility>
 
 namespace wv {
 namespace {
@@ -19,37 +23,70 @@ inline int grid_for(int64_t n, int per_thread = 1) {
 #define GRID_STRIDE(i, n) \
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < (n); i += (int64_t)gridDim.x * blockDim.x)
 
-__device__ __forceinline__ float roundtrip(int dtype, float w, float nf4s) {
-  switch (dtype) {
-  case 0: return (float)(double)w;  // Float64 holds double(w) exactly
-  case 1: return w;
-  case 2: return f16_decode(f16_encode(w));
-  case 3: return bf16_decode(bf16_encode_trunc(w));
-  case 4: return e4m3_decode(e4m3_encode(w));
-  case 5: return e5m2_decode(e5m2_encode(w));
-  case 26: return nf4_level(nf4_nearest(__fdiv_rn(w, nf4s))) * nf4s;
-  default: return 0.f;
+template <int DT>
+__device__ __forceinline__ float4 rt_vec(float4 v, const RtStats& st, const float* t) {
+  return make_float4(rt_elem<DT>(v.x, st, t), rt_elem<DT>(v.y, st, t), rt_elem<DT>(v.z, st, t),
+                     rt_elem<DT>(v.w, st, t));
+}
+
+// One dtype per instantiation. stats = [absmax, min, max] of the tensor, or null
+// for dtypes that need none. With 16-byte aligned pointers each thread streams
+// two float4 per iteration (evict-first loads and stores; w may equal out, each
+// element is read and then written by the same thread), the n % 4 tail by block
+// 0; otherwise one element per thread.
+template <int DT>
+__global__ void __launch_bounds__(256) roundtrip_kernel(const float* w, float* out, int64_t n, const float* stats,
+                                                        int vec) {
+  __shared__ float t[17];
+  if (DT == 26) nf4_table_init(t);
+  RtStats st{1.f, 0.f, 1.f};
+  if (stats) {
+    st.amax = stats[0];
+    st.mn = stats[1];
+    const float span = __fsub_rn(stats[2], stats[1]);
+    st.span = span == 0.f ? 1.f : span;
+  }
+  if (DT == 26) __syncthreads();
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (!vec) {
+    for (; i < n; i += stride) out[i] = rt_elem<DT>(w[i], st, t);
+    return;
+  }
+  const int64_t n4 = n >> 2;
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  float4* o4 = reinterpret_cast<float4*>(out);
+  for (; i + stride < n4; i += 2 * stride) {
+    const float4 a = __ldcs(w4 + i), b = __ldcs(w4 + i + stride);
+    __stcs(o4 + i, rt_vec<DT>(a, st, t));
+    __stcs(o4 + i + stride, rt_vec<DT>(b, st, t));
+  }
+  if (i < n4) __stcs(o4 + i, rt_vec<DT>(__ldcs(w4 + i), st, t));
+  if (blockIdx.x == 0 && threadIdx.x < (n & 3)) {
+    const int64_t j = (n4 << 2) + threadIdx.x;
+    out[j] = rt_elem<DT>(w[j], st, t);
   }
 }
 
-__global__ void roundtrip_kernel(int dtype, const float* w, float* out, int64_t n, const float* nf4_scale) {
-  float s = 1.f;
-  if (dtype == 26) {
-    s = *nf4_scale;
-    if (s == 0.f) s = 1.f;
-  }
-  GRID_STRIDE(i, n) out[i] = roundtrip(dtype, w[i], s);
+using RoundtripFn = void (*)(const float*, float*, int64_t, const float*, int);
+template <int... D>
+constexpr std::array<RoundtripFn, sizeof...(D)> roundtrip_table(std::integer_sequence<int, D...>) {
+  return {&roundtrip_kernel<D>...};
 }
+constexpr auto kRoundtrip = roundtrip_table(std::make_integer_sequence<int, 34>{});
 
 __global__ void encode_kernel(int dtype, const float* w, void* codes, int64_t n, const float* nf4_scale) {
   if (dtype == 26) {
+    __shared__ float t[17];
+    nf4_table_init(t);
+    __syncthreads();
     float s = *nf4_scale;
     if (s == 0.f) s = 1.f;
     uint8_t* out = static_cast<uint8_t*>(codes);
     GRID_STRIDE(j, (n + 1) / 2) {
       const int64_t i = 2 * j;
-      const int lo = nf4_nearest(__fdiv_rn(w[i], s));
-      const int hi = (i + 1 < n) ? nf4_nearest(__fdiv_rn(w[i + 1], s)) : 0;
+      const int lo = nf4_nearest(__fdiv_rn(w[i], s), t);
+      const int hi = (i + 1 < n) ? nf4_nearest(__fdiv_rn(w[i + 1], s), t) : 0;
       out[j] = (uint8_t)(lo | (hi << 4));
     }
     return;
@@ -108,6 +145,83 @@ __global__ void absmax_partial(const float* w, int64_t n, float* partial) {
   }
 }
 
+// Block-level fold of (absmax, min, max); thread 0 writes out[blockIdx.x],
+// out[stride + blockIdx.x], out[2 * stride + blockIdx.x].
+__device__ __forceinline__ void stats_block_store(float m, float mn, float mx, float* out, int64_t out_stride) {
+  __shared__ float red[3][32];
+  for (int o = 16; o; o >>= 1) {
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  }
+  if ((threadIdx.x & 31) == 0) {
+    red[0][threadIdx.x >> 5] = m;
+    red[1][threadIdx.x >> 5] = mn;
+    red[2][threadIdx.x >> 5] = mx;
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const bool live = threadIdx.x < (blockDim.x >> 5);
+    m = live ? red[0][threadIdx.x] : 0.f;
+    mn = live ? red[1][threadIdx.x] : INFINITY;
+    mx = live ? red[2][threadIdx.x] : -INFINITY;
+    for (int o = 16; o; o >>= 1) {
+      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    }
+    if (threadIdx.x == 0) {
+      out[blockIdx.x] = m;
+      out[out_stride + blockIdx.x] = mn;
+      out[2 * out_stride + blockIdx.x] = mx;
+    }
+  }
+}
+
+// First pass of [absmax, min, max]: per-block partials into three arrays of
+// gridDim.x floats. 16-byte loads when w is aligned (four in flight per thread),
+// the n % 4 tail by block 0.
+__global__ void __launch_bounds__(256) stats_first(const float* w, int64_t n, float* out, int vec) {
+  float m = 0.f, mn = INFINITY, mx = -INFINITY;
+  auto acc = [&](float v) {
+    m = fmaxf(m, fabsf(v));
+    mn = fminf(mn, v);
+    mx = fmaxf(mx, v);
+  };
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (vec) {
+    const int64_t n4 = n >> 2;
+    const float4* w4 = reinterpret_cast<const float4*>(w);
+    for (; i + 3 * stride < n4; i += 4 * stride) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = __ldcs(w4 + i + u * stride);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) acc(v[u].x), acc(v[u].y), acc(v[u].z), acc(v[u].w);
+    }
+    for (; i < n4; i += stride) {
+      const float4 a = __ldcs(w4 + i);
+      acc(a.x), acc(a.y), acc(a.z), acc(a.w);
+    }
+    if (blockIdx.x == 0 && threadIdx.x < (n & 3)) acc(w[(n4 << 2) + threadIdx.x]);
+  } else {
+    for (; i < n; i += stride) acc(w[i]);
+  }
+  stats_block_store(m, mn, mx, out, gridDim.x);
+}
+
+// Second pass: one block folds the three partial arrays of length n.
+__global__ void stats_fold(const float* part, int64_t n, float* out3) {
+  float m = 0.f, mn = INFINITY, mx = -INFINITY;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+    m = fmaxf(m, part[i]);
+    mn = fminf(mn, part[n + i]);
+    mx = fmaxf(mx, part[2 * n + i]);
+  }
+  stats_block_store(m, mn, mx, out3, 1);
+}
+
 // One warp per row: absmax/448 (1 when 0), then E4M3 codes of w/scale.
 __global__ void fp8_rowscale_encode_kernel(const float* w, int rows, int cols, uint8_t* codes, float* scales) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
@@ -135,6 +249,9 @@ __global__ void fp8_rowscale_decode_kernel(const uint8_t* codes, const float* sc
 
 // One warp per block of 64 elements (two per lane).
 __global__ void nf4_block_encode_kernel(const float* w, int64_t n, uint8_t* packed, float* absmax) {
+  __shared__ float t[17];
+  nf4_table_init(t);
+  __syncthreads();
   const int64_t blk = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (blk * 64 >= n) return;
@@ -145,8 +262,8 @@ __global__ void nf4_block_encode_kernel(const float* w, int64_t n, uint8_t* pack
   if (m == 0.f) m = 1.f;
   if (lane == 0) absmax[blk] = m;
   if (i0 < n) {
-    const int lo = nf4_nearest(__fdiv_rn(a, m));
-    const int hi = i0 + 1 < n ? nf4_nearest(__fdiv_rn(b, m)) : 0;
+    const int lo = nf4_nearest(__fdiv_rn(a, m), t);
+    const int hi = i0 + 1 < n ? nf4_nearest(__fdiv_rn(b, m), t) : 0;
     packed[i0 / 2] = (uint8_t)(lo | (hi << 4));
   }
 }
@@ -266,9 +383,23 @@ __global__ void fill_kernel(void* dst, int is_bf16, int64_t n, uint64_t seed, ui
 
 } // namespace
 
-cudaError_t codec_roundtrip_f32(int dtype, const float* w, float* out, int64_t n, const float* nf4_scale,
+bool codec_dtype_supported(int dtype) { return dtype >= 0 && dtype <= 33; }
+bool codec_needs_stats(int dtype) { return formatnone_needs_stats(dtype); }
+cudaError_t codec_roundtrip_f32(int dtype, const float* w, float* out, int64_t n, const float* stats,
                                 cudaStream_t s) {
-  roundtrip_kernel<<<grid_for(n), 256, 0, s>>>(dtype, w, out, n, nf4_scale);
+  if (!codec_dtype_supported(dtype)) return cudaErrorInvalidValue;
+  if (n <= 0) return cudaSuccess;
+  const int vec = ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(out)) & 15) == 0;
+  const int grid = vec ? grid_for((n >> 2) + 1, 2) : grid_for(n);
+  kRoundtrip[dtype]<<<grid, 256, 0, s>>>(w, out, n, stats, vec);
+  return cudaGetLastError();
+}
+cudaError_t stats_f32(const float* w, int64_t n, float* out3, float* scratch, cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  const int vec = (reinterpret_cast<uintptr_t>(w) & 15) == 0;
+  const int g = std::min(vec ? grid_for((n >> 2) + 1, 4) : grid_for(n), 1024);
+  stats_first<<<g, 256, 0, s>>>(w, n, scratch, vec);
+  stats_fold<<<1, 1024, 0, s>>>(scratch, g, out3);
   return cudaGetLastError();
 }
 cudaError_t codec_encode(int dtype, const float* w, void* codes, int64_t n, const float* nf4_scale,

@@ -6,43 +6,13 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "formatnone.cuh"
+
 namespace wv {
 
-// kNf4 (src/weights/native_codec.cpp:93-110): the 16 NF4 levels.
-__host__ __device__ __forceinline__ float nf4_level(int c) {
-  switch (c & 15) {
-  case 0: return -1.0f;
-  case 1: return -0.6961928009986877f;
-  case 2: return -0.5250730514526367f;
-  case 3: return -0.39491748809814453f;
-  case 4: return -0.28444138169288635f;
-  case 5: return -0.18477343022823334f;
-  case 6: return -0.09105003625154495f;
-  case 7: return 0.0f;
-  case 8: return 0.07958029955625534f;
-  case 9: return 0.16093020141124725f;
-  case 10: return 0.24611230194568634f;
-  case 11: return 0.33791524171829224f;
-  case 12: return 0.44070982933044434f;
-  case 13: return 0.5626170039176941f;
-  case 14: return 0.7229568362236023f;
-  default: return 1.0f;
-  }
-}
-
-// Nearest level, first minimum wins (native_codec.cpp:524-533). r is w/absmax.
-__device__ __forceinline__ int nf4_nearest(float r) {
-  int best = 0;
-  float best_err = 3.402823466e38f;
-#pragma unroll
-  for (int c = 0; c < 16; ++c) {
-    const float e = fabsf(r - nf4_level(c));
-    if (e < best_err) {
-      best_err = e;
-      best = c;
-    }
-  }
-  return best;
+// Fills t[0..16] with the NF4 levels and the sentinel; callers sync before use.
+__device__ __forceinline__ void nf4_table_init(float* t) {
+  if (threadIdx.x < 17) t[threadIdx.x] = threadIdx.x < 16 ? nf4_level(threadIdx.x) : __int_as_float(0x7f800000);
 }
 
 // float_codecs.cpp:53 (truncating) / :55.

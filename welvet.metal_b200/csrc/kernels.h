@@ -79,10 +79,15 @@ cudaError_t gemm_tc(const GemmArgs& a, cudaStream_t stream);
 cudaError_t gemm_simt(const GemmArgs& a, cudaStream_t stream);
 
 // ----------------------------------------------------------------- codecs
-// decode(encode(w)) of a FormatNone dtype, elementwise, bit-exact to the
-// reference scalar codecs; NF4 (dtype 26) needs `nf4_scale` (per tensor).
+// decode(encode(w)) of FormatNone dtype 0-33, elementwise, bit-exact to the
+// reference scalar codecs. `stats` = [absmax, min, max] of w from stats_f32,
+// needed when codec_needs_stats(dtype), else may be null.
+bool codec_dtype_supported(int dtype);
+bool codec_needs_stats(int dtype);
 cudaError_t codec_roundtrip_f32(int dtype, const float* w, float* out, int64_t n,
-                                const float* nf4_scale, cudaStream_t s);
+                                const float* stats, cudaStream_t s);
+// [absmax, min, max] of w into out3 (device); scratch holds 3072 floats.
+cudaError_t stats_f32(const float* w, int64_t n, float* out3, float* scratch, cudaStream_t s);
 // Encoders/decoders of the stored byte formats.
 cudaError_t codec_encode(int dtype, const float* w, void* codes, int64_t n, const float* nf4_scale,
                          cudaStream_t s);

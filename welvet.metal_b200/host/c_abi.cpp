@@ -289,16 +289,18 @@ welvet_status welvet_b200_codec_roundtrip(int32_t dtype, const float* w, float* 
   wv::DeviceCtx* d = nullptr;
   Status st = wv::device_ctx(-1, &d);
   if (!st) return wv::to_c(st);
+  if (!wv::codec_dtype_supported(dtype) || n < 0 || (n > 0 && (!w || !out)))
+    return wv::to_c(Status::err(1, "codec_roundtrip: invalid argument"));
   cudaStream_t s = as_stream(stream);
-  const float* scale = nullptr;
-  if (dtype == 26) {
-    cudaError_t e = wv::absmax_f32(w, n, d->scalars, d->scratch, s);
-    if (e != cudaSuccess) return launch_status(e, "absmax");
-    scale = d->scalars;
+  const float* stats = nullptr;
+  if (wv::codec_needs_stats(dtype) && n > 0) {
+    cudaError_t e = wv::stats_f32(w, n, d->scalars, d->scratch, s);
+    if (e != cudaSuccess) return launch_status(e, "tensor stats");
+    stats = d->scalars;
     wv::count_launch(2);
   }
   wv::count_launch();
-  return launch_status(wv::codec_roundtrip_f32(dtype, w, out, n, scale, s), "codec_roundtrip");
+  return launch_status(wv::codec_roundtrip_f32(dtype, w, out, n, stats, s), "codec_roundtrip");
 }
 
 welvet_status welvet_b200_codec_encode(int32_t dtype, const float* w, void* codes, float* scale_out, int64_t n,

@@ -225,23 +225,19 @@ namespace {
 
 // Encode -> decode of one full FP32 matrix on the device (FormatNone dtype), in place.
 Status roundtrip_inplace(DeviceCtx* d, int dtype, float* w, int64_t n, cudaStream_t s) {
-  switch (dtype) {
-  case 0: case 1: case 2: case 3: case 4: case 5: case 26: break;
-  default: {
+  if (!codec_dtype_supported(dtype)) {
     char buf[128];
-    std::snprintf(buf, sizeof(buf),
-                  "mha: weight dtype %d is not implemented by the B200 path (supported: 0-5, 26)", dtype);
+    std::snprintf(buf, sizeof(buf), "mha: weight dtype %d is not a FormatNone dtype (0-33)", dtype);
     return Status::err(2, buf);
   }
-  }
   if (dtype == 1) return Status::ok();
-  const float* scale = nullptr;
-  if (dtype == 26) {
-    WV_CUDA(absmax_f32(w, n, d->scalars, d->scratch, s), "absmax");
+  const float* stats = nullptr;
+  if (codec_needs_stats(dtype)) {
+    WV_CUDA(stats_f32(w, n, d->scalars, d->scratch, s), "tensor stats");
     count_launch(2);
-    scale = d->scalars;
+    stats = d->scalars;
   }
-  WV_CUDA(codec_roundtrip_f32(dtype, w, w, n, scale, s), "codec roundtrip");
+  WV_CUDA(codec_roundtrip_f32(dtype, w, w, n, stats, s), "codec roundtrip");
   count_launch();
   return Status::ok();
 }
