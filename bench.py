@@ -35,6 +35,8 @@ import sys
 import threading
 import time
 
+import numpy as np
+
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "welvet.metal_b200"))
 sys.path.insert(0, os.path.join(ROOT, "oracle"))
@@ -49,19 +51,34 @@ WORKLOADS = {
     "cfg2": dict(B=8, T=2048, d=1024, H=16, NK=16, wf=0, prec=0, kind="prefill"),
     # FormatNone weight round trip (mount-time encode -> decode), all dtypes 0-33
     "codec": dict(n=1 << 28, kind="codec"),
+    # transformer-block forwards around the MHA, at the config-5 model width:
+    # SwiGLU d=4096 with the reference's default_ffn width (swiglu.cpp:59-65), BF16;
+    # RMSNorm / LayerNorm over 4096-wide rows, FP32 as the reference's entries;
+    # Embedding of a 128256 x 4096 FP32 table
+    "swiglu": dict(B=8, T=8192, d=4096, inter=10928, prec=1, kind="swiglu"),
+    "rmsnorm": dict(B=16, T=4096, d=4096, kind="rmsnorm"),
+    "layernorm": dict(B=16, T=4096, d=4096, kind="layernorm"),
+    "embedding": dict(B=16, T=4096, d=4096, vocab=128256, kind="embedding"),
 }
+BLOCK_KINDS = ("swiglu", "rmsnorm", "layernorm", "embedding")
 CODEC_DTYPES = range(34)
 CODEC_STATS_FREE = (0, 1, 2, 3, 4, 5, 16, 24, 25)  # dtypes without a per-tensor statistics pass
 
 METRIC = "MHA prefill tok/s (BASELINE config 5; decode tok/s under 'decode')"
 METRIC_DECODE = "MHA decode tok/s (BASELINE config 3)"
 METRIC_CODEC = "FormatNone weight round trip GB/s (decode(encode(w)), dtypes 0-33)"
+METRIC_BLOCK = {"swiglu": "SwiGLU forward tok/s", "rmsnorm": "RMSNorm forward tok/s",
+                "layernorm": "LayerNorm forward tok/s", "embedding": "Embedding forward tok/s"}
 
 
 def workload(args):
     w = dict(WORKLOADS[args.workload])
     if w["kind"] == "codec":
         w["n"] = args.batch or w["n"]
+        return w
+    if w["kind"] in BLOCK_KINDS:
+        w["B"] = args.batch or w["B"]
+        w["T"] = args.seq or w["T"]
         return w
     w["B"] = args.batch or w["B"]
     w["T"] = args.seq or w["T"]
@@ -76,6 +93,14 @@ def workload_config(args, world):
         return {"workload": f"codec: decode(encode(w)) of {w['n']} FP32 weights, FormatNone dtypes 0-33",
                 "global_batch": w["n"], "seq_len": 1, "parallelism": f"replicas x{world}",
                 "l2": "tensor larger than L2 (%.2f GB)" % (w["n"] * 4 / 1e9)}
+    if w["kind"] in BLOCK_KINDS:
+        B, T, d = w["B"], w["T"], w["d"]
+        desc = {"swiglu": f"SwiGLU d={d} inter={w.get('inter')} BF16",
+                "rmsnorm": f"RMSNorm dim={d} FP32", "layernorm": f"LayerNorm dim={d} FP32",
+                "embedding": f"Embedding vocab={w.get('vocab')} emb={d} FP32 table, Linear"}[w["kind"]]
+        return {"workload": f"{args.workload}: {desc}, B={B} T={T}", "global_batch": B, "seq_len": T,
+                "parallelism": f"replicas x{world}", "l2": "activations larger than L2 (x is %.2f GB)"
+                % (B * T * d * (2 if w["kind"] == "swiglu" else 4) / 1e9)}
     B, T, d, H, NK, hd, wf = w["B"], w["T"], w["d"], w["H"], w["NK"], w["hd"], w["wf"]
     fmt = " fp8 weights" if wf == 1 else " nf4 weights" if wf == 2 else ""
     es = 2 if w["prec"] == 1 else 4
@@ -229,6 +254,8 @@ def run_reference(args):
         print(json.dumps({"impl": "reference", "unavailable": "the reference MHA has no KV cache or decode step"}),
               flush=True)
         return
+    if w["kind"] in BLOCK_KINDS:
+        return run_block_reference(args, w)
     if w["kind"] == "codec":
         use_ref = O.ref_available()
         n_s = 1 << 20
@@ -287,6 +314,254 @@ def run_reference(args):
             "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": kind, "sample": sample},
             "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def block_sample(w, use_ref, tokens):
+    """One bounded CPU sample of a block workload: `tokens` tokens of the same layer
+    through the reference's own entry (oracle/_ref, when use_ref: weights encoded and
+    mounted per call, as its one-shot entry does) or the FP64 port on decoded weights.
+    Returns seconds."""
+    import oracle_py as O
+    import welvet_b200 as W
+    k, d = w["kind"], w["d"]
+    x = W.synthetic(tokens * d, 1, 1, 1.0)
+    if k == "swiglu":
+        h = w["inter"]
+        a = (6.0 / (d + h)) ** 0.5
+        G = W.synthetic(h * d, 0, 0, a).reshape(h, d)
+        U = W.synthetic(h * d, 0, 0, a, offset=h * d).reshape(h, d)
+        D = W.synthetic(d * h, 0, 0, a, offset=2 * h * d).reshape(d, h)
+        t0 = time.perf_counter()
+        if use_ref:
+            code, msg, _, _ = O.ref_swiglu_forward(1, tokens, G, U, D, x)
+            if code:
+                raise RuntimeError(msg)
+        else:
+            O.swiglu_forward(x.reshape(tokens, d), G, U, D)
+        return time.perf_counter() - t0
+    if k in ("rmsnorm", "layernorm"):
+        g = W.synthetic(d, 5, 1, 0.1) + np.float32(1)
+        b = W.synthetic(d, 6, 1, 0.1)
+        t0 = time.perf_counter()
+        if use_ref:
+            code, msg, _, _ = O.ref_norm_forward(k == "layernorm", 1, tokens, d, 0.0, g, x, beta=b)
+            if code:
+                raise RuntimeError(msg)
+        else:
+            O.norm_forward(k == "layernorm", x.reshape(tokens, d), g, b, 0.0)
+        return time.perf_counter() - t0
+    vocab = min(w["vocab"], 8192)  # the table is decoded per call: bounded here
+    Wt = W.synthetic(vocab * d, 7, 1, 1.0).reshape(vocab, d)
+    ids = np.floor(W.synthetic(tokens, 8, 0, float(vocab))).astype(np.float32)
+    t0 = time.perf_counter()
+    if use_ref:
+        code, msg, _, _ = O.ref_embedding_forward(1, vocab, d, tokens, 2, 1, -1, Wt, ids)
+        if code:
+            raise RuntimeError(msg)
+    else:
+        O.embedding_forward(ids, Wt, 1, -1)
+    return time.perf_counter() - t0
+
+
+BLOCK_CPU_TOKENS = {"swiglu": 8, "rmsnorm": 8192, "layernorm": 8192, "embedding": 8192}
+BLOCK_REF_TOKENS = {"swiglu": 2, "rmsnorm": 1024, "layernorm": 1024, "embedding": 1024}
+
+
+def run_block_reference(args, w):
+    """Reference arm of the block workloads: the reference's own layer code
+    (oracle/_ref; its one-shot entries encode and mount the weights on every call,
+    as timed here) on a bounded token sample per step, reported as tok/s; the FP64
+    port when oracle/_ref is absent."""
+    import oracle_py as O
+    use_ref = O.ref_available()
+    n = BLOCK_REF_TOKENS[w["kind"]]
+    for _ in range(args.warmup):
+        block_sample(w, use_ref, max(1, n // 4))
+    tot = sum(block_sample(w, use_ref, n) for _ in range(args.steps))
+    value = n * args.steps / tot
+    kind = "reference" if use_ref else "port"
+    sample = (f"{n} tokens of the {args.workload} layer per step through the reference's one-shot entry "
+              f"(weights encoded per call){', vocab bounded to 8192' if w['kind'] == 'embedding' else ''}")
+    print(json.dumps({"impl": "reference", "metric": METRIC_BLOCK[w["kind"]], "value": value, "unit": "tok/s",
+                      "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                      "ms_per_step": tot / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+                      "vs_baseline": None, "dtype": "f64 (soft-double)", "data": "synthetic",
+                      "config": workload_config(args, args.gpus),
+                      "cpu_baseline": {"value": value, "unit": "tok/s", "cores": os.cpu_count(), "kind": kind,
+                                       "sample": sample},
+                      "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+          flush=True)
+
+
+def run_block(args, rank, world, local):
+    """Transformer-block forwards (SwiGLU, RMSNorm, LayerNorm, Embedding) on one
+    GPU per rank; replicas only (each rank runs its own batch, no collective). A step
+    = one forward over B*T tokens with activations resident in HBM."""
+    import torch
+    import torch.distributed as dist
+    import welvet_b200 as W
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    w = workload(args)
+    k, B, T, d = w["kind"], w["B"], w["T"], w["d"]
+    M = B * T
+    pk = peaks()
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    host_args = None
+    if k == "swiglu":
+        h = w["inter"]
+        a = (6.0 / (d + h)) ** 0.5
+        ws = []
+        for i, (r, c) in enumerate(((h, d), (h, d), (d, h))):
+            t = torch.empty(r, c, device="cuda")
+            W.fill_synthetic(t, 0, 0, a, offset=i * h * d)
+            ws.append(t)
+        layer = W.SwigluLayer(*ws, dtype=1, precision=1)
+        del ws
+        x = torch.empty(M, d, device="cuda", dtype=torch.bfloat16)
+        W.fill_synthetic(x, 1, 1, 1.0, offset=rank * M * d)
+        pre = torch.empty(M, h, device="cuda", dtype=torch.bfloat16)
+        post = torch.empty(M, d, device="cuda", dtype=torch.bfloat16)
+        step = lambda: layer.forward(M, x, pre, post, stream=stream)  # noqa: E731
+        slots = ("gemm_gate_up", "gemm_down")
+        work = {"gemm_gate_up": 2.0 * M * d * 2 * h, "gemm_down": 2.0 * M * h * d}
+        unit, bound = "TFLOP/s", "tensor"
+        dtype = "bf16"
+    elif k in ("rmsnorm", "layernorm"):
+        x = torch.empty(M, d, device="cuda")
+        W.fill_synthetic(x, 1, 1, 1.0, offset=rank * M * d)
+        g = torch.empty(d, device="cuda")
+        b = torch.empty(d, device="cuda")
+        W.fill_synthetic(g, 5, 1, 0.1)
+        W.fill_synthetic(b, 6, 1, 0.1)
+        g += 1.0
+        pre = torch.empty_like(x)
+        post = torch.empty_like(x)
+        ln = k == "layernorm"
+        step = lambda: W.norm_forward(ln, M, d, 0.0, g, x, pre, post, beta=b, stream=stream)  # noqa: E731
+        slots = ("norm",)
+        work = {"norm": 3.0 * M * d * 4 + (2 if ln else 1) * d * 4}
+        unit, bound = "GB/s", "hbm"
+        dtype = "f32 (FP64 statistics)"
+    else:
+        vocab = w["vocab"]
+        Wt = torch.empty(vocab, d, device="cuda")
+        W.fill_synthetic(Wt, 7, 1, 1.0)
+        ids = torch.empty(M, device="cuda")
+        W.fill_synthetic(ids, 8, 0, float(vocab), offset=rank * M)
+        ids = ids.abs().floor()
+        out = torch.empty(M, d, device="cuda")
+        step = lambda: W.embedding_forward(M, vocab, d, 1, -1, Wt, ids, out, stream=stream)  # noqa: E731
+        slots = ("embedding",)
+        work = {"embedding": 2.0 * M * d * 4 + M * 4}
+        unit, bound = "GB/s", "hbm"
+        dtype = "f32"
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    W.device_check()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = Clocks(local)
+    clocks.start()
+    W.profile_read(reset=True)
+    W.profile_enable(True)
+    W.launch_count(reset=True)
+    barrier()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    barrier()
+    launches = W.launch_count(reset=True)
+    W.profile_enable(False)
+    prof = W.profile_read(reset=True)
+    clk = clocks.stop()
+    W.device_check()
+    ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps)
+    tokps = world * M / (ms / 1e3)
+    dom = max(slots, key=lambda s_: prof[s_][0])
+    tot, cnt = prof[dom]
+    avg_ms = tot / max(cnt, 1)
+    per_launch = work[dom] * args.steps / max(cnt, 1)
+    if bound == "tensor":
+        achieved = per_launch / (avg_ms / 1e3) / 1e12
+        peak, pkind = pk["bf16_sus"], f"{pk['src']} sustained bf16 (of {pk['src']})"
+    else:
+        achieved = per_launch / (avg_ms / 1e3) / 1e9
+        peak, pkind = pk["hbm"], f"{pk['src']} HBM copy (of {pk['src']})"
+    roof = {"bound": bound, "kernel": dom, "achieved": achieved, "peak": peak, "unit": unit,
+            "frac": achieved / peak, "peak_kind": pkind, "traffic": None,
+            ("flops_per_launch" if bound == "tensor" else "bytes_per_launch"): per_launch,
+            "avg_launch_ms": avg_ms, "kernel_ms_per_step": {s_: prof[s_][0] / args.steps for s_ in slots}}
+    e2e = None
+    if not args.no_e2e:
+        # the reference's one-shot entry over host buffers: weights encoded and
+        # mounted, x uploaded, outputs downloaded, per call (as the reference does)
+        n_e = min(M, 8192)
+        xh = W.synthetic(n_e * d, 1, 1, 1.0)
+        if k == "swiglu":
+            hh = w["inter"]
+            a = (6.0 / (d + hh)) ** 0.5
+            Wh = [W.synthetic(r * c, 0, 0, a, offset=i * hh * d).reshape(r, c)
+                  for i, (r, c) in enumerate(((hh, d), (hh, d), (d, hh)))]
+            call = lambda: W.swiglu_forward_f32(1, n_e, *Wh, xh)  # noqa: E731
+            hb, db = n_e * d * 4 + 3 * hh * d * 4, n_e * (d + hh) * 4
+        elif k in ("rmsnorm", "layernorm"):
+            gh = W.synthetic(d, 5, 1, 0.1) + np.float32(1)
+            bh = W.synthetic(d, 6, 1, 0.1)
+            call = lambda: W.norm_forward_f32(k == "layernorm", 1, n_e, d, 0.0, gh, xh, beta=bh)  # noqa: E731
+            hb, db = n_e * d * 4 + 2 * d * 4, 2 * n_e * d * 4
+        else:
+            vocab_e = min(w["vocab"], 32768)  # host table bounded to 0.5 GB
+            Wh = W.synthetic(vocab_e * d, 7, 1, 1.0).reshape(vocab_e, d)
+            idh = np.floor(W.synthetic(n_e, 8, 0, float(vocab_e))).astype(np.float32)
+            idh = np.abs(idh)
+            call = lambda: W.embedding_forward_f32(1, vocab_e, d, n_e, 2, 1, -1, Wh, idh)  # noqa: E731
+            hb, db = vocab_e * d * 4 + n_e * 4, 2 * n_e * d * 4
+        call()
+        barrier()
+        n_rep = 2
+        t0 = time.perf_counter()
+        for _ in range(n_rep):
+            call()
+        e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3 / n_rep)
+        e2e = {"value": world * n_e / (e_ms / 1e3), "unit": "tok/s", "ms_per_step": e_ms,
+               "h2d_bytes_per_step": hb, "d2h_bytes_per_step": db,
+               "api": f"welvet_{k}_forward_f32 (host buffers, weights encoded per call), {n_e} tokens"}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        n_c = BLOCK_CPU_TOKENS[k]
+        dt_c = block_sample(w, False, n_c)
+        cpu = {"value": n_c / dt_c, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+               "sample": f"FP64 oracle, {n_c} tokens of the layer, {dt_c:.2f} s"
+                         f"{' (vocab bounded to 8192)' if k == 'embedding' else ''}"}
+    if rank == 0:
+        print(json.dumps({"metric": METRIC_BLOCK[k], "value": tokps, "unit": "tok/s", "n_gpus": world,
+                          "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+                          "scaling": "weak", "vs_baseline": None, "dtype": dtype,
+                          "data": "synthetic (SplitMix64 counter stream)", "config": workload_config(args, world),
+                          "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
+                          "clocks": clk,
+                          "profile_ms": {s_: prof[s_][0] / args.steps for s_ in slots}}), flush=True)
+    if k == "swiglu":
+        layer.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def run_codec(args, rank, world, local):
@@ -426,6 +701,8 @@ def main():
     torch.cuda.set_device(local)
     if workload(args)["kind"] == "codec":
         return run_codec(args, rank, world, local)
+    if workload(args)["kind"] in BLOCK_KINDS:
+        return run_block(args, rank, world, local)
     if world > 1:
         # NVLS (in-switch reduction) is off unless the caller sets it: on this pool's
         # 8-GPU boxes the 256 KB decode all-reduce took 31 ms with NVLS and 0.05 ms

@@ -168,10 +168,11 @@ WELVET_API int64_t welvet_b200_launch_count(int32_t reset);
  * with steady_clock, tools/dense_fwd/main.cpp:198-216). When enabled, each hot kernel
  * of forward / decode is bracketed by CUDA events on its launch stream.
  * welvet_b200_profile_read synchronises and returns, per kernel id, the summed
- * milliseconds and launch counts (8 slots: 0 QKV GEMM, 1 prefill attention, 2 O GEMM,
- * 3 decode attention, 4 decode QKV GEMM, 5 decode O GEMM, 6 all-reduce, 7 other). */
+ * milliseconds and launch counts (12 slots: 0 QKV GEMM, 1 prefill attention, 2 O GEMM,
+ * 3 decode attention, 4 decode QKV GEMM, 5 decode O GEMM, 6 all-reduce, 7 other,
+ * 8 SwiGLU Gate|Up GEMM, 9 SwiGLU Down GEMM, 10 RMSNorm/LayerNorm, 11 embedding). */
 WELVET_API void welvet_b200_profile_enable(int32_t on);
-WELVET_API void welvet_b200_profile_read(double ms[8], int64_t counts[8], int32_t reset);
+WELVET_API void welvet_b200_profile_read(double ms[12], int64_t counts[12], int32_t reset);
 
 /* ---- decode attention without allocation (no counterpart in the reference) ----
  * Split-KV decode attention of one new query per sequence over a paged KV cache,
@@ -199,6 +200,46 @@ WELVET_API welvet_status welvet_b200_decode_attention_static(const welvet_b200_m
                                                              const int32_t* block_table, int32_t max_pages,
                                                              const int32_t* ctx_len, void* out, int32_t ldo,
                                                              void* stream);
+
+/* ---- transformer-block forwards around the MHA (extension; the reference's
+ * one-shot entries are in welvet_c.h) ----
+ * Resident SwiGLU feed-forward (src/layers/swiglu/swiglu.cpp:93-143): Gate/Up
+ * [intermediate_dim, input_dim] and Down [input_dim, intermediate_dim] FP32 inits
+ * decoded as FormatNone `dtype` (0-33) once, then packed for the tensor cores;
+ * precision 0 = FP32 (3xTF32 GEMMs), 1 = BF16 operands. forward: x [tokens,
+ * input_dim], pre = h = SiLU(x Gate^T) * (x Up^T) [tokens, intermediate_dim] (may
+ * be NULL), post = h Down^T [tokens, input_dim], device buffers of the layer's
+ * precision, asynchronous on `stream`; forward_host: FP32 host buffers,
+ * synchronous (FP32 layers). */
+typedef struct welvet_b200_swiglu welvet_b200_swiglu;
+WELVET_API welvet_status welvet_b200_swiglu_mount(int32_t input_dim, int32_t intermediate_dim,
+                                                  int32_t precision, int32_t device, int32_t dtype,
+                                                  const float* Gate, const float* Up,
+                                                  const float* Down, int32_t weights_on_device,
+                                                  welvet_b200_swiglu** out);
+WELVET_API welvet_status welvet_b200_swiglu_forward(welvet_b200_swiglu* layer, int64_t tokens,
+                                                    const void* x, void* pre, void* post,
+                                                    void* stream);
+WELVET_API welvet_status welvet_b200_swiglu_forward_host(welvet_b200_swiglu* layer, int64_t tokens,
+                                                         const float* x, float* pre, float* post);
+WELVET_API void welvet_b200_swiglu_release(welvet_b200_swiglu* layer);
+/* RMSNorm (layernorm = 0) / LayerNorm (1) forward over `rows` rows of `dim`
+ * (shaders/ops_norm.metal:2-26): pre = x-hat (may be NULL), post = x-hat * gamma
+ * (+ beta); gamma/beta are decoded FP32 weights in device memory
+ * (welvet_b200_codec_roundtrip); x/pre/post FP32, or BF16 when io_bf16; eps <= 0
+ * selects the reference default (1e-6 / 1e-5). Statistics in FP64. */
+WELVET_API welvet_status welvet_b200_norm_forward(int32_t layernorm, int64_t rows, int32_t dim,
+                                                  double eps, const float* gamma,
+                                                  const float* beta, const void* x, void* pre,
+                                                  void* post, int32_t io_bf16, void* stream);
+/* Embedding gather (shaders/ops_embedding.metal:1-8): out[t] = act(W[abs(int(x[t *
+ * in_last])) % vocab]) over decoded FP32 weights W [vocab, emb] (device); x holds the
+ * ids as floats; act is the reference's Activation id (-1 Linear, 0 ReLU, 1 SiLU,
+ * 2 GELU, 3 Tanh, 4 Sigmoid, 5 LeakyReLU, 6 ReLU2). */
+WELVET_API welvet_status welvet_b200_embedding_forward(int64_t tokens, int32_t vocab, int32_t emb,
+                                                       int32_t in_last, int32_t act, const float* W,
+                                                       const float* x, void* out, int32_t out_bf16,
+                                                       void* stream);
 
 #ifdef __cplusplus
 }

@@ -6,8 +6,10 @@
  * Every declaration below has the same name, signature, argument meaning and
  * status semantics as the reference header include/welvet_c.h of
  * openfluke/welvet.metal; the line of the reference each one replaces is cited.
- * The reference's other entry points (Dense/SwiGLU/norm/embedding families,
- * model sessions, training) are not part of this library. */
+ * Besides the MHA forward it serves the forward entries of the transformer block
+ * around it (SwiGLU, RMSNorm, LayerNorm, Embedding). The reference's other entry
+ * points (Dense/CNN/recurrent families, backward/NormalBP leaves, model sessions)
+ * are not part of this library. */
 
 #include <stddef.h>
 #include <stdint.h>
@@ -50,6 +52,40 @@ WELVET_API welvet_status welvet_mha_forward_f32(
     int32_t batch, int32_t seq, int32_t d_model, int32_t num_heads, int32_t num_kv_heads,
     int32_t head_dim, int32_t max_seq_len, int32_t mask, int32_t pos, int32_t dtype, int32_t backend,
     const float* Q, const float* K, const float* V, const float* O, const float* x, float* pre,
+    float* post);
+
+/* Reference include/welvet_c.h:105-109 (impl src/interop/c_abi.cpp:326-361).
+ * SwiGLU forward: Gate/Up [intermediate_dim, input_dim], Down [input_dim,
+ * intermediate_dim] FP32 inits encoded to `dtype`; x [batch*seq*input_dim];
+ * pre = h = SiLU(x Gate^T) * (x Up^T) [batch*seq*intermediate_dim], post = h Down^T
+ * [batch*seq*input_dim]. Host memory, synchronous, nothing retained. */
+WELVET_API welvet_status welvet_swiglu_forward_f32(
+    int32_t batch, int32_t seq, int32_t input_dim, int32_t intermediate_dim, int32_t dtype,
+    int32_t backend, const float* Gate, const float* Up, const float* Down, const float* x,
+    float* pre, float* post);
+
+/* Reference include/welvet_c.h:121-124 (impl c_abi.cpp:437-469). RMSNorm forward:
+ * gamma [dim] encoded to `dtype`; pre = x / rms(x), post = pre * gamma, each
+ * [batch*seq*dim]; eps <= 0 selects 1e-6. */
+WELVET_API welvet_status welvet_rmsnorm_forward_f32(int32_t batch, int32_t seq, int32_t dim,
+                                                    double eps, int32_t dtype, int32_t backend,
+                                                    const float* gamma, const float* x,
+                                                    float* pre, float* post);
+
+/* Reference include/welvet_c.h:135-138 (impl c_abi.cpp:543-577). LayerNorm forward:
+ * pre = (x - mean) / sqrt(var + eps), post = pre * gamma + beta; eps <= 0 selects 1e-5. */
+WELVET_API welvet_status welvet_layernorm_forward_f32(int32_t batch, int32_t seq, int32_t dim,
+                                                      double eps, int32_t dtype, int32_t backend,
+                                                      const float* gamma, const float* beta,
+                                                      const float* x, float* pre, float* post);
+
+/* Reference include/welvet_c.h:168-172 (impl c_abi.cpp:792-832). Embedding gather:
+ * W [vocab, emb] encoded to `dtype`; token t's id is abs(int(x[t*in_last])) % vocab
+ * (in_rank 1: seq_len tokens; 2: batch*seq_len; 3: batch*seq_len with in_last 1 or
+ * emb); pre = post = act(W[id]) [tokens*emb]. */
+WELVET_API welvet_status welvet_embedding_forward_f32(
+    int32_t batch, int32_t vocab, int32_t emb, int32_t seq_len, int32_t in_rank, int32_t in_last,
+    int32_t act, int32_t dtype, int32_t backend, const float* W, const float* x, float* pre,
     float* post);
 
 #ifdef __cplusplus

@@ -101,6 +101,25 @@ void oracle_nf4_block_encode(const float* w, int64_t n, int32_t block, uint8_t* 
 void oracle_nf4_block_decode(const uint8_t* packed, const float* absmax, int64_t n, int32_t block,
                              float* out);
 
+/* Transformer-block forwards (block_oracle.cpp), on decoded FP32 weights. */
+/* act_value of shaders/ops_common.metal:83-105 (Activation ids: -1 Linear, 0 ReLU,
+ * 1 Silu, 2 GELU, 3 Tanh, 4 Sigmoid, 5 LeakyReLU, 6 ReLU2). */
+float oracle_act_value(float v, int32_t act);
+/* RMSNorm (layernorm = 0) / LayerNorm (1) over rows of dim: pre = x-hat, post =
+ * x-hat * gamma (+ beta) (shaders/ops_norm.metal:2-26); eps <= 0 -> the validate()
+ * default (1e-6 / 1e-5). */
+int32_t oracle_norm_forward(int32_t layernorm, int64_t rows, int32_t dim, double eps,
+                            const float* gamma, const float* beta, const float* x, float* pre,
+                            float* post);
+/* SwiGLU (swiglu.cpp:93-143): pre = h = silu(x Gate^T) * (x Up^T), post = h Down^T. */
+int32_t oracle_swiglu_forward(int64_t tokens, int32_t in, int32_t inter, const float* Gate,
+                              const float* Up, const float* Down, const float* x, float* pre,
+                              float* post, int32_t threads);
+/* Embedding (ops_embedding.metal:1-8): row abs(int(x[t*in_last])) % vocab of W, act applied. */
+int32_t oracle_embedding_forward(int64_t tokens, int32_t vocab, int32_t emb, int32_t in_last,
+                                 int32_t act, const float* W, const float* x, float* pre,
+                                 float* post);
+
 #ifdef __cplusplus
 }
 #endif

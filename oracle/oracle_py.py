@@ -115,6 +115,16 @@ def _load_oracle():
     lib.oracle_fp8_rowscale_decode.argtypes = [_u8p, _f32p, C.c_int64, C.c_int64, _f32p]
     lib.oracle_nf4_block_encode.argtypes = [_f32p, C.c_int64, C.c_int32, _u8p, _f32p]
     lib.oracle_nf4_block_decode.argtypes = [_u8p, _f32p, C.c_int64, C.c_int32, _f32p]
+    lib.oracle_act_value.argtypes = [C.c_float, C.c_int32]
+    lib.oracle_act_value.restype = C.c_float
+    lib.oracle_norm_forward.argtypes = [C.c_int32, C.c_int64, C.c_int32, C.c_double, _f32p, _f32p, _f32p,
+                                        _f32p, _f32p]
+    lib.oracle_norm_forward.restype = C.c_int32
+    lib.oracle_swiglu_forward.argtypes = [C.c_int64, C.c_int32, C.c_int32] + [_f32p] * 6 + [C.c_int32]
+    lib.oracle_swiglu_forward.restype = C.c_int32
+    lib.oracle_embedding_forward.argtypes = [C.c_int64, C.c_int32, C.c_int32, C.c_int32, C.c_int32, _f32p,
+                                             _f32p, _f32p, _f32p]
+    lib.oracle_embedding_forward.restype = C.c_int32
     return lib
 
 
@@ -144,6 +154,14 @@ def ref_lib():
         lib.ref_weight_roundtrip.argtypes = [C.c_int32, C.c_int32, C.c_int32, _f32p, _u8p,
                                              C.POINTER(C.c_int64), C.POINTER(C.c_float), _f32p]
         lib.ref_weight_roundtrip.restype = RefStatusC
+        lib.ref_swiglu_forward_f32.argtypes = [C.c_int32] * 5 + [_f32p] * 6
+        lib.ref_swiglu_forward_f32.restype = RefStatusC
+        lib.ref_rmsnorm_forward_f32.argtypes = [C.c_int32] * 3 + [C.c_double, C.c_int32] + [_f32p] * 4
+        lib.ref_rmsnorm_forward_f32.restype = RefStatusC
+        lib.ref_layernorm_forward_f32.argtypes = [C.c_int32] * 3 + [C.c_double, C.c_int32] + [_f32p] * 5
+        lib.ref_layernorm_forward_f32.restype = RefStatusC
+        lib.ref_embedding_forward_f32.argtypes = [C.c_int32] * 8 + [_f32p] * 4
+        lib.ref_embedding_forward_f32.restype = RefStatusC
         for name, a, r in (("ref_fp8e4m3_encode", C.c_float, C.c_uint8), ("ref_fp8e4m3_decode", C.c_uint8, C.c_float),
                            ("ref_fp8e5m2_encode", C.c_float, C.c_uint8), ("ref_fp8e5m2_decode", C.c_uint8, C.c_float),
                            ("ref_bf16_encode", C.c_float, C.c_uint16), ("ref_bf16_decode", C.c_uint16, C.c_float),
@@ -293,3 +311,69 @@ def ref_weight_roundtrip(dtype: int, w):
     dec = np.empty_like(w)
     st = ref_lib().ref_weight_roundtrip(dtype, rows, cols, w, native, C.byref(cap), C.byref(s), dec)
     return st.code, st.message.decode(), native[:cap.value].copy(), s.value, dec
+
+
+# ------------------------------------------------------------ block forwards
+def norm_forward(layernorm: bool, x, gamma, beta=None, eps: float = 0.0):
+    """RMSNorm / LayerNorm forward of the oracle on decoded weights: (pre, post)."""
+    x = _f32(x)
+    dim = x.shape[-1]
+    rows = x.size // dim
+    pre = np.empty_like(x)
+    post = np.empty_like(x)
+    b = _f32(beta if beta is not None else np.zeros(dim, np.float32))
+    if oracle_lib().oracle_norm_forward(1 if layernorm else 0, rows, dim, eps, _f32(gamma), b, x, pre, post):
+        raise ValueError("oracle_norm_forward: bad shape")
+    return pre, post
+
+
+def swiglu_forward(x, Gate, Up, Down, threads: int = 0):
+    x = _f32(x)
+    inter, d = np.shape(Gate)
+    tokens = x.size // d
+    pre = np.empty((tokens, inter), np.float32)
+    post = np.empty((tokens, d), np.float32)
+    if oracle_lib().oracle_swiglu_forward(tokens, d, inter, _f32(Gate), _f32(Up), _f32(Down), x, pre, post,
+                                          threads):
+        raise ValueError("oracle_swiglu_forward: bad shape")
+    return pre, post
+
+
+def embedding_forward(x, W, in_last: int = 1, act: int = -1):
+    x = _f32(x)
+    vocab, emb = np.shape(W)
+    tokens = x.size // in_last
+    pre = np.empty((tokens, emb), np.float32)
+    post = np.empty((tokens, emb), np.float32)
+    if oracle_lib().oracle_embedding_forward(tokens, vocab, emb, in_last, act, _f32(W), x, pre, post):
+        raise ValueError("oracle_embedding_forward: bad shape")
+    return pre, post
+
+
+def ref_swiglu_forward(batch, seq, Gate, Up, Down, x, dtype=1):
+    inter, d = np.shape(Gate)
+    pre = np.zeros(batch * seq * inter, np.float32)
+    post = np.zeros(batch * seq * d, np.float32)
+    st = ref_lib().ref_swiglu_forward_f32(batch, seq, d, inter, dtype, _f32(Gate), _f32(Up), _f32(Down), _f32(x),
+                                          pre, post)
+    return st.code, st.message.decode(), pre, post
+
+
+def ref_norm_forward(layernorm, batch, seq, dim, eps, gamma, x, beta=None, dtype=1):
+    pre = np.zeros(batch * seq * dim, np.float32)
+    post = np.zeros(batch * seq * dim, np.float32)
+    if layernorm:
+        st = ref_lib().ref_layernorm_forward_f32(batch, seq, dim, eps, dtype, _f32(gamma), _f32(beta), _f32(x),
+                                                 pre, post)
+    else:
+        st = ref_lib().ref_rmsnorm_forward_f32(batch, seq, dim, eps, dtype, _f32(gamma), _f32(x), pre, post)
+    return st.code, st.message.decode(), pre, post
+
+
+def ref_embedding_forward(batch, vocab, emb, seq_len, in_rank, in_last, act, W, x, dtype=1):
+    n = batch * seq_len if in_rank > 1 else seq_len
+    pre = np.zeros(n * emb, np.float32)
+    post = np.zeros(n * emb, np.float32)
+    st = ref_lib().ref_embedding_forward_f32(batch, vocab, emb, seq_len, in_rank, in_last, act, dtype, _f32(W),
+                                             _f32(x), pre, post)
+    return st.code, st.message.decode(), pre, post

@@ -6,9 +6,16 @@
 //    mha::forward — running the reference shaders on the CPU executor.
 //  - ref_mha_forward_cfg: the same with every mha::Config field settable.
 //  - ref_weight_roundtrip: WeightStore::make + native bytes + export_f32.
+//  - ref_swiglu_forward_f32, ref_rmsnorm_forward_f32, ref_layernorm_forward_f32,
+//    ref_embedding_forward_f32: the bodies of the reference's block forward entries
+//    (src/interop/c_abi.cpp:326-361, 437-469, 543-577, 792-832).
 //  - the scalar converters of include/welvet/float_codecs.hpp.
+#include "welvet/embedding.hpp"
 #include "welvet/float_codecs.hpp"
+#include "welvet/layernorm.hpp"
 #include "welvet/mha.hpp"
+#include "welvet/rmsnorm.hpp"
+#include "welvet/swiglu.hpp"
 #include "welvet/weights.hpp"
 
 #include <cstdio>
@@ -108,6 +115,112 @@ ref_status ref_weight_roundtrip(int32_t dtype, int32_t rows, int32_t cols, const
   }
   *scale = s.scale;
   return to_status(s.export_f32(decoded));
+}
+
+
+static ref_status invalid(const char* msg) {
+  ref_status st{};
+  st.code = 1;
+  std::snprintf(st.message, sizeof(st.message), "%s", msg);
+  return st;
+}
+
+// [batch, dim] when seq == 1, else [batch, seq, dim], as the reference entries shape x.
+static welvet::TensorF32 block_input(int32_t batch, int32_t seq, int32_t dim, const float* x) {
+  welvet::TensorF32 input;
+  if (seq == 1)
+    input.shape = {batch, dim};
+  else
+    input.shape = {batch, seq, dim};
+  input.data.assign(x, x + static_cast<std::size_t>(batch) * seq * dim);
+  return input;
+}
+
+static ref_status copy_out(const welvet::TensorF32& pre_t, const welvet::TensorF32& post_t, float* pre,
+                           float* post) {
+  std::memcpy(pre, pre_t.data.data(), pre_t.data.size() * sizeof(float));
+  std::memcpy(post, post_t.data.data(), post_t.data.size() * sizeof(float));
+  return to_status(welvet::Status::Ok());
+}
+
+ref_status ref_swiglu_forward_f32(int32_t batch, int32_t seq, int32_t input_dim, int32_t intermediate_dim,
+                                  int32_t dtype, const float* Gate, const float* Up, const float* Down,
+                                  const float* x, float* pre, float* post) {
+  if (batch <= 0 || seq <= 0 || input_dim <= 0 || intermediate_dim <= 0 || !Gate || !Up || !Down || !x ||
+      !pre || !post)
+    return invalid("swiglu: invalid argument");
+  welvet::swiglu::Config cfg;
+  cfg.input_dim = input_dim;
+  cfg.intermediate_dim = intermediate_dim;
+  welvet::swiglu::Layer layer;
+  auto st = welvet::swiglu::new_configured(cfg, static_cast<welvet::DType>(dtype), Gate, Up, Down, &layer);
+  if (!st) return to_status(st);
+  welvet::TensorF32 pre_t, post_t;
+  st = welvet::swiglu::forward(layer, block_input(batch, seq, input_dim, x), &pre_t, &post_t);
+  if (!st) return to_status(st);
+  return copy_out(pre_t, post_t, pre, post);
+}
+
+ref_status ref_rmsnorm_forward_f32(int32_t batch, int32_t seq, int32_t dim, double eps, int32_t dtype,
+                                   const float* gamma, const float* x, float* pre, float* post) {
+  if (batch <= 0 || seq <= 0 || dim <= 0 || !gamma || !x || !pre || !post)
+    return invalid("rmsnorm: invalid argument");
+  welvet::rmsnorm::Config cfg;
+  cfg.dim = dim;
+  cfg.eps = eps;
+  welvet::rmsnorm::Layer layer;
+  auto st = welvet::rmsnorm::new_configured(cfg, static_cast<welvet::DType>(dtype), gamma, &layer);
+  if (!st) return to_status(st);
+  welvet::TensorF32 pre_t, post_t;
+  st = welvet::rmsnorm::forward(layer, block_input(batch, seq, dim, x), &pre_t, &post_t);
+  if (!st) return to_status(st);
+  return copy_out(pre_t, post_t, pre, post);
+}
+
+ref_status ref_layernorm_forward_f32(int32_t batch, int32_t seq, int32_t dim, double eps, int32_t dtype,
+                                     const float* gamma, const float* beta, const float* x, float* pre,
+                                     float* post) {
+  if (batch <= 0 || seq <= 0 || dim <= 0 || !gamma || !beta || !x || !pre || !post)
+    return invalid("layernorm: invalid argument");
+  welvet::layernorm::Config cfg;
+  cfg.dim = dim;
+  cfg.eps = eps;
+  welvet::layernorm::Layer layer;
+  auto st =
+      welvet::layernorm::new_configured(cfg, static_cast<welvet::DType>(dtype), gamma, beta, &layer);
+  if (!st) return to_status(st);
+  welvet::TensorF32 pre_t, post_t;
+  st = welvet::layernorm::forward(layer, block_input(batch, seq, dim, x), &pre_t, &post_t);
+  if (!st) return to_status(st);
+  return copy_out(pre_t, post_t, pre, post);
+}
+
+ref_status ref_embedding_forward_f32(int32_t batch, int32_t vocab, int32_t emb, int32_t seq_len,
+                                     int32_t in_rank, int32_t in_last, int32_t act, int32_t dtype,
+                                     const float* W, const float* x, float* pre, float* post) {
+  if (batch <= 0 || vocab <= 0 || emb <= 0 || seq_len <= 0 || in_last <= 0 || !W || !x || !pre || !post)
+    return invalid("embedding: invalid argument");
+  if (in_rank < 1 || in_rank > 3) return invalid("embedding: bad in_rank");
+  welvet::embedding::Config cfg;
+  cfg.vocab_size = vocab;
+  cfg.embedding_dim = emb;
+  cfg.seq_len = seq_len;
+  welvet::embedding::Layer layer;
+  auto st = welvet::embedding::new_configured(cfg, static_cast<welvet::DType>(dtype),
+                                              static_cast<welvet::Activation>(act), W, &layer);
+  if (!st) return to_status(st);
+  welvet::TensorF32 input;
+  if (in_rank == 1)
+    input.shape = {seq_len};
+  else if (in_rank == 2)
+    input.shape = {batch, seq_len};
+  else
+    input.shape = {batch, seq_len, in_last};
+  input.data.assign(x, x + static_cast<std::size_t>(batch) * seq_len * in_last);
+  welvet::TensorF32 pre_t, post_t;
+  st = welvet::embedding::forward(layer, input, &pre_t, &post_t);
+  if (!st) return to_status(st);
+  return copy_out(pre_t, post_t, pre, post);
 }
 
 uint8_t ref_fp8e4m3_encode(float f) { return welvet::float32_to_fp8e4m3(f); }

@@ -1,8 +1,8 @@
 // Test infrastructure (builds oracle/_ref only). A CPU executor that stands in
 // for the reference's Metal device layer (src/metal/ops.mm, src/metal/matvec.mm)
 // so that the reference's unmodified host code (src/layers/mha/mha.cpp,
-// src/layers/dense/dense.cpp, src/weights/*.cpp) runs its own shader kernels on
-// the CPU. Dispatch follows the reference: `run` copies every argument into a
+// src/layers/dense/dense.cpp, src/layers/{swiglu,rmsnorm,layernorm,embedding}/*.cpp,
+// src/weights/*.cpp) runs its own shader kernels on the CPU. Dispatch follows the reference: `run` copies every argument into a
 // fresh buffer, runs `threads` invocations and copies writable buffers back
 // (ops.mm:13-88); the resident Dense path runs matvec then bias_act over
 // batch*rows invocations (matvec.mm:332-400). Invocations of one dispatch are
@@ -68,11 +68,15 @@ Status run(const char* kernel, std::initializer_list<Arg> args, std::initializer
   std::copy(ints.begin(), ints.end(), ci);
   std::copy(reals.begin(), reals.end(), cr);
   if (std::string(kernel) == "op_attention") {
+    // one invocation does all the work (tid 0); the others return at once
     for (std::size_t t = 0; t < threads; ++t)
       refshader::op_attention_kernel(bufs, ci, cr, (uint32_t)t);
+  } else if (std::string(kernel) == "op_swiglu" || std::string(kernel) == "op_norm_forward" ||
+             std::string(kernel) == "op_embedding_forward") {
+    dispatch(threads, [&](uint32_t t) { refshader::op_kernel(kernel, bufs, ci, cr, t); });
   } else {
     return Status::Err(StatusCode::Unsupported,
-                       std::string("cpu executor: kernel not on the MHA path: ") + kernel);
+                       std::string("cpu executor: kernel not on the block forward paths: ") + kernel);
   }
   idx = 0;
   for (const auto& a : args) {

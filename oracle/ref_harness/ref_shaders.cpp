@@ -1,14 +1,19 @@
 // Test infrastructure (builds oracle/_ref only). Compiles the reference's own
-// soft-double shader sources — welvet_dense.metal, ops_common.metal and
-// ops_mha.metal, in the order the reference concatenates them
-// (CMakeLists.txt:118-129) — as host C++ through the MSL shim in
-// oracle/msl_shim, and exposes the kernels the MHA forward dispatches as plain
-// functions. The shader files are read where they lie; nothing is copied.
+// soft-double shader sources — welvet_dense.metal, then ops_common.metal,
+// ops_embedding.metal, ops_mha.metal and ops_norm.metal in the sorted order of the
+// reference's ops_*.metal glob (CMakeLists.txt:118-129) — as host C++ through the
+// MSL shim in oracle/msl_shim, and exposes the kernels that the MHA, SwiGLU,
+// RMSNorm/LayerNorm and Embedding forwards dispatch as plain functions. The
+// shader files are read where they lie; nothing is copied.
 #include <metal_stdlib>
+
+#include <cstring>
 
 #include "welvet_dense.metal"
 #include "ops_common.metal"
+#include "ops_embedding.metal"
 #include "ops_mha.metal"
+#include "ops_norm.metal"
 
 // Declared (not defined) by welvet_dense.metal; only the MSE-loss kernel uses it.
 namespace native_gpu {
@@ -42,6 +47,20 @@ void dense_bias_act(float* pre, float* post, const float* bias_xy, uint32_t out_
 
 void op_attention_kernel(float* const bufs[8], const int32_t* c, const float* r, uint32_t tid) {
   op_attention(bufs[0], bufs[1], bufs[2], bufs[3], bufs[4], bufs[5], bufs[6], bufs[7], c, r, tid);
+}
+
+bool op_kernel(const char* name, float* const bufs[8], const int32_t* c, const float* r, uint32_t tid) {
+#define WV_OP(k)                                                                                   \
+  if (std::strcmp(name, #k) == 0) {                                                                \
+    k(bufs[0], bufs[1], bufs[2], bufs[3], bufs[4], bufs[5], bufs[6], bufs[7], c, r, tid);          \
+    return true;                                                                                   \
+  }
+  WV_OP(op_attention)
+  WV_OP(op_swiglu)
+  WV_OP(op_norm_forward)
+  WV_OP(op_embedding_forward)
+#undef WV_OP
+  return false;
 }
 
 } // namespace refshader

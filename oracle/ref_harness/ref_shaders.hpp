@@ -12,4 +12,7 @@ void dense_bias_act(float* pre, float* post, const float* bias_xy, uint32_t out_
                     uint32_t batch, int32_t act, uint32_t bias_len, uint32_t gid);
 // op_attention (shaders/ops_mha.metal:31-176), one thread id; OP_ARGS buffers a..j.
 void op_attention_kernel(float* const bufs[8], const int32_t* c, const float* r, uint32_t tid);
+// One thread id of the OP_ARGS kernel `name` (op_attention, op_swiglu,
+// op_norm_forward, op_embedding_forward); false for any other name.
+bool op_kernel(const char* name, float* const bufs[8], const int32_t* c, const float* r, uint32_t tid);
 } // namespace refshader

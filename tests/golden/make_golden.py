@@ -60,6 +60,62 @@ MHA_CASES = {
     "int3": (dict(d_model=64, num_heads=4), 1, 8, 32),
 }
 
+# Transformer-block forwards (reference C entries welvet_{rmsnorm,layernorm,swiglu,
+# embedding}_forward_f32). name: (kind, params); inputs are stored with the outputs.
+BLOCK_CASES = {
+    "rms_d64_f32": ("rmsnorm", dict(batch=2, seq=8, dim=64, eps=0.0, dtype=1)),
+    "rms_d4096_bf16": ("rmsnorm", dict(batch=1, seq=4, dim=4096, eps=1e-5, dtype=3)),
+    "rms_seq1_int8": ("rmsnorm", dict(batch=3, seq=1, dim=96, eps=0.0, dtype=9)),
+    "ln_d64_f32": ("layernorm", dict(batch=2, seq=8, dim=64, eps=0.0, dtype=1)),
+    "ln_d1000_nf4": ("layernorm", dict(batch=1, seq=5, dim=1000, eps=1e-3, dtype=26)),
+    "ln_offset_mean": ("layernorm", dict(batch=1, seq=4, dim=256, eps=0.0, dtype=1, mean=100.0)),
+    "swiglu_f32": ("swiglu", dict(batch=2, seq=8, input_dim=64, intermediate_dim=176, dtype=1)),
+    "swiglu_seq1_fp8": ("swiglu", dict(batch=4, seq=1, input_dim=32, intermediate_dim=96, dtype=4)),
+    "swiglu_int4": ("swiglu", dict(batch=1, seq=6, input_dim=48, intermediate_dim=128, dtype=14)),
+    "emb_rank2_linear": ("embedding", dict(batch=2, vocab=50, emb=32, seq_len=6, in_rank=2, in_last=1, act=-1,
+                                           dtype=1)),
+    "emb_rank1_silu_int8": ("embedding", dict(batch=1, vocab=17, emb=24, seq_len=9, in_rank=1, in_last=1, act=1,
+                                              dtype=9)),
+    "emb_rank3_gelu": ("embedding", dict(batch=2, vocab=40, emb=16, seq_len=3, in_rank=3, in_last=16, act=2,
+                                         dtype=1)),
+    "emb_rank2_leaky_bf16": ("embedding", dict(batch=3, vocab=1000, emb=64, seq_len=5, in_rank=2, in_last=1, act=5,
+                                               dtype=3)),
+}
+
+
+def block_inputs(kind, p, seed):
+    """Deterministic inputs of a block case (counter-based stream, platform independent
+    up to libm in the normal transform; stored in the fixture)."""
+    if kind in ("rmsnorm", "layernorm"):
+        n = p["batch"] * p["seq"] * p["dim"]
+        x = synthetic(n, seed, 1, 1.0) + np.float32(p.get("mean", 0.0))
+        g = synthetic(p["dim"], seed + 1, 1, 0.1) + np.float32(1.0)
+        b = synthetic(p["dim"], seed + 2, 1, 0.1)
+        return dict(x=x.astype(np.float32), gamma=g.astype(np.float32), beta=b)
+    if kind == "swiglu":
+        d, h = p["input_dim"], p["intermediate_dim"]
+        a = (6.0 / (d + h)) ** 0.5
+        return dict(x=synthetic(p["batch"] * p["seq"] * d, seed, 1, 1.0),
+                    Gate=synthetic(h * d, seed + 1, 0, a).reshape(h, d),
+                    Up=synthetic(h * d, seed + 2, 0, a).reshape(h, d),
+                    Down=synthetic(d * h, seed + 3, 0, a).reshape(d, h))
+    tokens = p["batch"] * p["seq_len"] if p["in_rank"] > 1 else p["seq_len"]
+    ids = np.floor(synthetic(tokens * p["in_last"], seed, 0, 3.0 * p["vocab"])).astype(np.float32)
+    ids[::5] += np.float32(0.75)  # fractional ids truncate toward zero
+    return dict(x=ids, W=synthetic(p["vocab"] * p["emb"], seed + 1, 1, 1.0).reshape(p["vocab"], p["emb"]))
+
+
+def block_run(kind, p, inp):
+    if kind in ("rmsnorm", "layernorm"):
+        return O.ref_norm_forward(kind == "layernorm", p["batch"], p["seq"], p["dim"], p["eps"], inp["gamma"],
+                                  inp["x"], beta=inp["beta"], dtype=p["dtype"])
+    if kind == "swiglu":
+        return O.ref_swiglu_forward(p["batch"], p["seq"], inp["Gate"], inp["Up"], inp["Down"], inp["x"],
+                                    dtype=p["dtype"])
+    return O.ref_embedding_forward(p["batch"], p["vocab"], p["emb"], p["seq_len"], p["in_rank"], p["in_last"],
+                                   p["act"], inp["W"], inp["x"], dtype=p["dtype"])
+
+
 # Extra matrices for the all-dtype round trips: positive absmax (Int32's
 # out-of-range conversion), all zeros (absmax 0 and span 0), a constant.
 def codec_matrices(w):
@@ -109,6 +165,17 @@ def main():
     with open(os.path.join(HERE, "mha_cases.json"), "w") as f:
         json.dump(out, f, indent=1, sort_keys=True)
 
+    blocks = {}
+    for i, (name, (kind, p)) in enumerate(BLOCK_CASES.items()):
+        inp = block_inputs(kind, p, 100 + 10 * i)
+        code, msg, pre, post = block_run(kind, p, inp)
+        if code:
+            raise SystemExit(f"{name}: reference returned {code} {msg}")
+        blocks[name] = dict(kind=kind, **p)
+        _save(os.path.join(HERE, f"block_{name}.npz"), pre=pre, post=post, **inp)
+    with open(os.path.join(HERE, "block_cases.json"), "w") as f:
+        json.dump(blocks, f, indent=1, sort_keys=True)
+
     # Codec known answers straight from the reference converters.
     lib = O.ref_lib()
     codes = np.arange(256, dtype=np.uint8)
@@ -146,7 +213,7 @@ def main():
     mats.pop("w")
     _save(os.path.join(HERE, "codecs.npz"), e4m3_dec=e4m3_dec, e5m2_dec=e5m2_dec, probes=probes,
           e4m3_enc=e4m3_enc, e5m2_enc=e5m2_enc, bf16_enc=bf16_enc, f16_enc=f16_enc, w=w, **mats, **rt)
-    print(f"wrote {len(MHA_CASES)} MHA cases and codecs.npz to {HERE}")
+    print(f"wrote {len(MHA_CASES)} MHA cases, {len(BLOCK_CASES)} block cases and codecs.npz to {HERE}")
 
 
 if __name__ == "__main__":

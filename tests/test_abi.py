@@ -23,7 +23,8 @@ def declared_symbols():
 def test_headers_declare_the_reference_mha_entry_points():
     names = declared_symbols()
     for n in ("welvet_version", "welvet_runtime_identity", "welvet_metal_init", "welvet_metal_available",
-              "welvet_mha_forward_f32"):
+              "welvet_mha_forward_f32", "welvet_swiglu_forward_f32", "welvet_rmsnorm_forward_f32",
+              "welvet_layernorm_forward_f32", "welvet_embedding_forward_f32"):
         assert n in names
 
 
@@ -87,3 +88,41 @@ def test_synthetic_stream_is_deterministic():
     np.testing.assert_array_equal(a, b)
     n = W.synthetic(20000, 1, 1, 1.0)
     assert abs(n.mean()) < 0.05 and abs(n.std() - 1) < 0.05
+
+
+# ---------------------------------------------------------- block entries
+def test_block_entries_reject_bad_arguments_like_the_reference():
+    """Argument checks of src/interop/c_abi.cpp:326-361, 437-469, 543-577, 792-832
+    (code 1, '<layer>: invalid argument'); no device work is reached."""
+    z = np.zeros(64, np.float32)
+    lib = W.lib()
+    cases = [
+        (lib.welvet_swiglu_forward_f32(0, 1, 4, 4, 1, 0, *[W._ptr(z)] * 6), "swiglu"),
+        (lib.welvet_swiglu_forward_f32(1, 1, 4, 0, 1, 0, *[W._ptr(z)] * 6), "swiglu"),
+        (lib.welvet_rmsnorm_forward_f32(1, 1, 0, 0.0, 1, 0, *[W._ptr(z)] * 4), "rmsnorm"),
+        (lib.welvet_layernorm_forward_f32(1, 1, 4, 0.0, 1, 0, W._ptr(z), None, W._ptr(z), W._ptr(z), W._ptr(z)),
+         "layernorm"),
+        (lib.welvet_embedding_forward_f32(1, 0, 4, 2, 2, 1, -1, 1, 0, *[W._ptr(z)] * 4), "embedding"),
+    ]
+    for st, name in cases:
+        assert st.code == 1 and st.message.decode() == f"{name}: invalid argument"
+    st = lib.welvet_embedding_forward_f32(1, 4, 4, 2, 4, 1, -1, 1, 0, *[W._ptr(z)] * 4)
+    assert st.code == 1 and st.message.decode() == "embedding: bad in_rank"
+
+
+def test_block_entries_report_unknown_dtypes_with_the_reference_codes():
+    # reference: norms/embedding -> 3 "... gap? pack_native unknown" (WeightStore::make),
+    # SwiGLU -> 2 "swiglu Gate: dense ... FormatNone forward unsupported ..." (dense mount)
+    z = np.zeros(64, np.float32)
+    lib = W.lib()
+    st = lib.welvet_rmsnorm_forward_f32(1, 2, 8, 0.0, 34, 0, *[W._ptr(z)] * 4)
+    assert st.code == 3 and st.message.decode().startswith("rmsnorm gamma:")
+    st = lib.welvet_layernorm_forward_f32(1, 2, 8, 0.0, 40, 0, *[W._ptr(z)] * 5)
+    assert st.code == 3 and st.message.decode().startswith("layernorm gamma:")
+    st = lib.welvet_embedding_forward_f32(1, 4, 8, 2, 2, 1, -1, 34, 0, *[W._ptr(z)] * 4)
+    assert st.code == 3 and st.message.decode().startswith("embedding weights:")
+    st = lib.welvet_swiglu_forward_f32(2, 1, 8, 4, 34, 0, *[W._ptr(z)] * 6)
+    assert st.code == 2 and st.message.decode().startswith("swiglu Gate:")
+    # embedding rank 3 needs in_last 1 or emb
+    st = lib.welvet_embedding_forward_f32(1, 4, 8, 2, 3, 3, -1, 1, 0, *[W._ptr(z)] * 4)
+    assert st.code == 1 and "want 1 or emb" in st.message.decode()

@@ -69,6 +69,7 @@ struct KParams {
   void* kv_v;
   const int* kv_slot;
   int kv_col0, kv_dim;
+  int swiglu, swiglu_cols;
   uint32_t* err;
 };
 
@@ -144,6 +145,28 @@ __device__ __forceinline__ void store_vals(const KParams& p, int row, int col, c
 template <int BN>
 __device__ __forceinline__ void epilogue_tile(const KParams& p, uint32_t tbase, int row, int n0) {
   const bool row_ok = row < p.M;
+  if (p.swiglu) {
+    // 32 gate columns then the matching 32 up columns: h = SiLU(gate) * up with
+    // SiLU(g) = g / (1 + e^-g), the product rounded once (op_swiglu,
+    // shaders/ops_common.metal:27-38)
+    for (int c = 0; c < BN && n0 + c < p.N; c += 64) {
+      uint32_t g[32], u[32];
+      tmem_ld32(tbase + c, g);
+      tmem_ld32(tbase + c + 32, u);
+      tmem_ld_wait();
+      if (row_ok) {
+        float h[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const float gv = __uint_as_float(g[e]);
+          h[e] = __fdiv_rn(gv, 1.f + expf(-gv)) * __uint_as_float(u[e]);
+        }
+        const int hc = (n0 + c) / 2;
+        if (hc < p.swiglu_cols) store_vals(p, row, hc, h, min(32, p.swiglu_cols - hc));
+      }
+    }
+    return;
+  }
   const int hd = p.head_dim;
   const bool fuse_rope = p.rope_cols > 0 && (hd == 64 || hd == 128 || hd == 256) && (BN % hd) == 0;
   int pos = 0;
@@ -552,6 +575,8 @@ template <int KIND> cudaError_t launch(const GemmArgs& g, cudaStream_t stream) {
   p.kv_slot = g.kv_slot;
   p.kv_col0 = g.kv_col0;
   p.kv_dim = g.kv_dim;
+  p.swiglu = g.swiglu;
+  p.swiglu_cols = g.swiglu_cols > 0 ? g.swiglu_cols : g.N / 2;
   p.err = g.err;
 
   const size_t smem = smem_bytes<KIND>();
@@ -581,6 +606,7 @@ bool gemm_tc_supported(const GemmArgs& g) {
     return false;
   }
   if (g.kv_k && (g.kv_dim % 32 || g.kv_col0 % 32 || g.head_dim % 32)) return false;
+  if (g.swiglu && (g.N % 64 || g.rope_cols || g.kv_k || g.kind == kGemmFP8)) return false;
   return encode_fn() != nullptr;
 }
 

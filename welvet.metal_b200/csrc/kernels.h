@@ -61,6 +61,10 @@ struct GemmArgs {
   void* kv_v = nullptr;
   const int* kv_slot = nullptr;     // per row: destination row index in the pools
   int kv_col0 = 0, kv_dim = 0;
+  // SwiGLU: the N = 2 * inter_p columns alternate 32 gate / 32 up columns; the
+  // epilogue writes h = SiLU(gate) * up to column (n / 64) * 32 + (n % 32) of out
+  int swiglu = 0;
+  int swiglu_cols = 0;  // h columns written (>= the last chunk is clipped); 0: all
   uint32_t* err = nullptr;
   int sm_count = 148;
 };
@@ -191,5 +195,39 @@ cudaError_t attn_decode_tc(const DecodeArgs& a, int splits, cudaStream_t s);
 // Pool layout: [page][kv_head][kPageTokens][head_dim]; slot = page*kPageTokens + row.
 cudaError_t kv_append(const void* k, const void* v, int ld, int rows, int kd, int head_dim,
                       int is_bf16, const int* slot, void* k_pool, void* v_pool, cudaStream_t s);
+
+// ---- transformer-block kernels (block.cu)
+struct NormArgs {
+  int64_t rows = 0;
+  int dim = 0;
+  double eps = 1e-6;
+  const void* x = nullptr;     // [rows, dim] FP32, or BF16 when x_bf16
+  int x_bf16 = 0;
+  const float* gamma = nullptr;  // [dim] decoded weights
+  const float* beta = nullptr;   // [dim] (LayerNorm)
+  void* pre = nullptr;           // x-hat [rows, dim] (may be null)
+  void* post = nullptr;          // [rows, dim]
+  int out_bf16 = 0;
+  int vec4 = 0;                  // set by norm_forward
+};
+cudaError_t norm_forward(const NormArgs& a, int layernorm, cudaStream_t s);
+
+struct EmbedArgs {
+  int64_t tokens = 0;
+  int vocab = 0, emb = 0, in_last = 1, act = -1;
+  const float* W = nullptr;  // [vocab, emb] decoded weights
+  const float* x = nullptr;  // ids as floats, token t at x[t * in_last]
+  void* out = nullptr;       // [tokens, emb] FP32 or BF16
+  int out_bf16 = 0;
+  int vec4 = 0;              // set by embedding_forward
+};
+cudaError_t embedding_forward(const EmbedArgs& a, cudaStream_t s);
+
+cudaError_t swiglu_pack_gate_up(const float* gate, const float* up, float* out, int inter, int in,
+                                int inter_p, int in_p, cudaStream_t s);
+cudaError_t pad_cols(const float* src, float* dst, int64_t rows, int cols, int cols_p, cudaStream_t s);
+// x [rows, cols] -> zero-padded [rows, cols_p]: TF32 hi/lo pairs (hi != null) or BF16 (b)
+cudaError_t pad_operand(const void* x, int x_bf16, int64_t rows, int cols, int cols_p, float* hi,
+                        float* lo, void* b, cudaStream_t s);
 
 } // namespace wv

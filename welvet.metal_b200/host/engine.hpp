@@ -57,7 +57,11 @@ enum ProfId : int {
   kProfGemmODecode = 5,
   kProfAllReduce = 6,
   kProfOther = 7,
-  kProfCount = 8,
+  kProfGemmGateUp = 8,   // SwiGLU Gate|Up GEMM with the SiLU * up epilogue
+  kProfGemmDown = 9,     // SwiGLU Down GEMM
+  kProfNorm = 10,        // RMSNorm / LayerNorm
+  kProfEmbedding = 11,
+  kProfCount = 12,
 };
 void prof_enable(bool on);
 bool prof_on();

@@ -22,7 +22,8 @@ LIB_PATH = os.path.join(HERE, "lib", "libwelvet_b200.so")
 
 # Exported symbols declared in include/welvet_c.h and include/welvet_b200.h.
 C_ABI_SYMBOLS = ("welvet_version", "welvet_runtime_identity", "welvet_metal_init",
-                 "welvet_metal_available", "welvet_mha_forward_f32")
+                 "welvet_metal_available", "welvet_mha_forward_f32", "welvet_swiglu_forward_f32",
+                 "welvet_rmsnorm_forward_f32", "welvet_layernorm_forward_f32", "welvet_embedding_forward_f32")
 EXT_SYMBOLS = ("welvet_b200_mha_config_default", "welvet_b200_mha_mount", "welvet_b200_mha_release",
                "welvet_b200_mha_forward", "welvet_b200_mha_check", "welvet_b200_kv_create",
                "welvet_b200_kv_release", "welvet_b200_kv_fill", "welvet_b200_mha_prefill",
@@ -33,9 +34,11 @@ EXT_SYMBOLS = ("welvet_b200_mha_config_default", "welvet_b200_mha_mount", "welve
                "welvet_b200_nf4_block_encode", "welvet_b200_nf4_block_decode",
                "welvet_b200_fill_synthetic", "welvet_b200_device_check", "welvet_b200_launch_count",
                "welvet_b200_profile_enable", "welvet_b200_profile_read",
-               "welvet_b200_decode_attention_static")
+               "welvet_b200_decode_attention_static", "welvet_b200_swiglu_mount", "welvet_b200_swiglu_forward",
+               "welvet_b200_swiglu_forward_host", "welvet_b200_swiglu_release", "welvet_b200_norm_forward",
+               "welvet_b200_embedding_forward")
 PROFILE_SLOTS = ("gemm_qkv", "attn_prefill", "gemm_o", "attn_decode", "gemm_qkv_decode", "gemm_o_decode",
-                 "allreduce", "other")
+                 "allreduce", "other", "gemm_gate_up", "gemm_down", "norm", "embedding")
 
 DTYPES = {"float64": 0, "float32": 1, "float16": 2, "bfloat16": 3, "fp8e4m3": 4, "fp8e5m2": 5, "nf4": 26}
 
@@ -93,6 +96,24 @@ def lib():
     L.welvet_metal_init.restype = Status
     L.welvet_metal_available.restype = C.c_int32
     L.welvet_mha_forward_f32.argtypes = [C.c_int32] * 11 + [_vp] * 7
+    L.welvet_swiglu_forward_f32.argtypes = [C.c_int32] * 6 + [_vp] * 6
+    L.welvet_rmsnorm_forward_f32.argtypes = [C.c_int32] * 3 + [C.c_double, C.c_int32, C.c_int32] + [_vp] * 4
+    L.welvet_layernorm_forward_f32.argtypes = [C.c_int32] * 3 + [C.c_double, C.c_int32, C.c_int32] + [_vp] * 5
+    L.welvet_embedding_forward_f32.argtypes = [C.c_int32] * 9 + [_vp] * 4
+    for name in ("welvet_swiglu_forward_f32", "welvet_rmsnorm_forward_f32", "welvet_layernorm_forward_f32",
+                 "welvet_embedding_forward_f32"):
+        getattr(L, name).restype = Status
+    L.welvet_b200_swiglu_mount.argtypes = [C.c_int32] * 5 + [_vp] * 3 + [C.c_int32, C.POINTER(_vp)]
+    L.welvet_b200_swiglu_forward.argtypes = [_vp, C.c_int64, _vp, _vp, _vp, _vp]
+    L.welvet_b200_swiglu_forward_host.argtypes = [_vp, C.c_int64, _vp, _vp, _vp]
+    L.welvet_b200_swiglu_release.argtypes = [_vp]
+    L.welvet_b200_swiglu_release.restype = None
+    L.welvet_b200_norm_forward.argtypes = [C.c_int32, C.c_int64, C.c_int32, C.c_double, _vp, _vp, _vp, _vp, _vp,
+                                           C.c_int32, _vp]
+    L.welvet_b200_embedding_forward.argtypes = [C.c_int64] + [C.c_int32] * 4 + [_vp] * 3 + [C.c_int32, _vp]
+    for name in ("welvet_b200_swiglu_mount", "welvet_b200_swiglu_forward", "welvet_b200_swiglu_forward_host",
+                 "welvet_b200_norm_forward", "welvet_b200_embedding_forward"):
+        getattr(L, name).restype = Status
     L.welvet_mha_forward_f32.restype = Status
     cfgp = C.POINTER(MhaConfig)
     L.welvet_b200_mha_config_default.argtypes = [cfgp, C.c_int32, C.c_int32, C.c_int32]
@@ -218,7 +239,98 @@ def mha_forward_f32(batch, seq, d_model, num_heads, num_kv_heads, head_dim, max_
     return pre, post
 
 
+def swiglu_forward_f32(batch, seq, Gate, Up, Down, x, dtype=1, backend=0):
+    """welvet_swiglu_forward_f32 with numpy buffers: (pre [B*S*inter], post [B*S*in])."""
+    f = lambda a: np.ascontiguousarray(a, dtype=np.float32)  # noqa: E731
+    Gate, Up, Down, x = (f(a) for a in (Gate, Up, Down, x))
+    inter, d = Gate.shape
+    pre = np.zeros(max(1, batch * seq * inter), np.float32)
+    post = np.zeros(max(1, batch * seq * d), np.float32)
+    check(lib().welvet_swiglu_forward_f32(batch, seq, d, inter, dtype, backend, _ptr(Gate), _ptr(Up), _ptr(Down),
+                                          _ptr(x), _ptr(pre), _ptr(post)))
+    return pre, post
+
+
+def norm_forward_f32(layernorm, batch, seq, dim, eps, gamma, x, beta=None, dtype=1, backend=0):
+    """welvet_rmsnorm_forward_f32 / welvet_layernorm_forward_f32: (pre, post)."""
+    f = lambda a: np.ascontiguousarray(a, dtype=np.float32)  # noqa: E731
+    gamma, x = f(gamma), f(x)
+    n = max(1, batch * seq * dim)
+    pre = np.zeros(n, np.float32)
+    post = np.zeros(n, np.float32)
+    if layernorm:
+        beta = f(beta)
+        st = lib().welvet_layernorm_forward_f32(batch, seq, dim, eps, dtype, backend, _ptr(gamma), _ptr(beta),
+                                                _ptr(x), _ptr(pre), _ptr(post))
+    else:
+        st = lib().welvet_rmsnorm_forward_f32(batch, seq, dim, eps, dtype, backend, _ptr(gamma), _ptr(x),
+                                              _ptr(pre), _ptr(post))
+    check(st)
+    return pre, post
+
+
+def embedding_forward_f32(batch, vocab, emb, seq_len, in_rank, in_last, act, W, x, dtype=1, backend=0):
+    """welvet_embedding_forward_f32: (pre, post), each [tokens * emb]."""
+    W = np.ascontiguousarray(W, dtype=np.float32)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    tokens = seq_len if in_rank == 1 else batch * seq_len
+    pre = np.zeros(max(1, tokens * emb), np.float32)
+    post = np.zeros(max(1, tokens * emb), np.float32)
+    check(lib().welvet_embedding_forward_f32(batch, vocab, emb, seq_len, in_rank, in_last, act, dtype, backend,
+                                             _ptr(W), _ptr(x), _ptr(pre), _ptr(post)))
+    return pre, post
+
+
 # -------------------------------------------------------------- extension
+class SwigluLayer:
+    """Resident SwiGLU feed-forward (welvet_b200_swiglu_*). precision 0: FP32
+    tensors, 1: BF16 device tensors."""
+
+    def __init__(self, Gate, Up, Down, dtype: int = 1, precision: int = 0, device: int = -1):
+        self._h = _vp()
+        on_dev = _on_device(Gate, Up, Down)
+        if not on_dev:
+            Gate, Up, Down = (np.ascontiguousarray(a, dtype=np.float32) for a in (Gate, Up, Down))
+        self.inter, self.input_dim = Gate.shape
+        self.precision = precision
+        check(lib().welvet_b200_swiglu_mount(self.input_dim, self.inter, precision, device, dtype, _ptr(Gate),
+                                             _ptr(Up), _ptr(Down), on_dev, C.byref(self._h)))
+
+    def forward(self, tokens, x, pre, post, stream=None):
+        """Device tensors (torch); pre may be None."""
+        check(lib().welvet_b200_swiglu_forward(self._h, tokens, _ptr(x), _ptr(pre), _ptr(post), _stream(stream)))
+
+    def forward_host(self, tokens, x, pre=None, post=None):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        if post is None:
+            post = np.zeros(tokens * self.input_dim, np.float32)
+        check(lib().welvet_b200_swiglu_forward_host(self._h, tokens, _ptr(x), _ptr(pre), _ptr(post)))
+        return pre, post
+
+    def close(self):
+        if self._h:
+            lib().welvet_b200_swiglu_release(self._h)
+            self._h = _vp()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def norm_forward(layernorm, rows, dim, eps, gamma, x, pre, post, beta=None, io_bf16=0, stream=None):
+    """welvet_b200_norm_forward on device tensors (gamma/beta decoded FP32)."""
+    check(lib().welvet_b200_norm_forward(1 if layernorm else 0, rows, dim, eps, _ptr(gamma), _ptr(beta), _ptr(x),
+                                         _ptr(pre), _ptr(post), io_bf16, _stream(stream)))
+
+
+def embedding_forward(tokens, vocab, emb, in_last, act, W, x, out, out_bf16=0, stream=None):
+    """welvet_b200_embedding_forward on device tensors (W decoded FP32)."""
+    check(lib().welvet_b200_embedding_forward(tokens, vocab, emb, in_last, act, _ptr(W), _ptr(x), _ptr(out),
+                                              out_bf16, _stream(stream)))
+
+
 class MhaLayer:
     """Resident MHA layer (welvet_b200_mha_*)."""
 
@@ -371,8 +483,8 @@ def profile_enable(on: bool = True):
 
 def profile_read(reset: bool = True) -> dict:
     """{slot: (total_ms, launches)} of the live per-kernel event timing."""
-    ms = (C.c_double * 8)()
-    cnt = (C.c_int64 * 8)()
+    ms = (C.c_double * len(PROFILE_SLOTS))()
+    cnt = (C.c_int64 * len(PROFILE_SLOTS))()
     lib().welvet_b200_profile_read(ms, cnt, 1 if reset else 0)
     return {name: (ms[i], cnt[i]) for i, name in enumerate(PROFILE_SLOTS)}
 
