@@ -191,7 +191,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], kSoftThreads / 2);
+      mbar_init(&p_full[i], 4);  // one arrival per warp of the warpgroup
       mbar_init(&p_empty[i], 1);
     }
     mbar_init(fin_bar, kSoftThreads);
@@ -251,16 +251,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       // TS MMA of PV_j reads as its A operand. S_{j+2} reuses the buffer, so the
       // issue order is S_0, S_1, then per block i: PV_i, S_{i+2} (MMAs of one thread
       // execute in issue order).
+      // Descriptors as 32-bit halves, advanced by constant adds (a short issue path
+      // for the single issuing thread).
+      constexpr uint32_t DHI = sdesc_hi_sw128(1024);
+      const uint32_t q_lo = sdesc_lo(q_base, 16);
       auto issue_s = [&](int j) -> bool {
         const int ks = j % F::SK, g = j & 1;
         if (!mbar_wait(&k_full[ks], (j / F::SK) & 1, abort_flag, p.err, kErrWaitFull)) return false;
         tc_fence_after();
-        const uint32_t k_base = smem_u32(smem + F::OFF_K + ks * F::KV_BYTES);
+        const uint32_t k_lo = sdesc_lo(smem_u32(smem + F::OFF_K + ks * F::KV_BYTES), 16);
+        const uint32_t d = tmem + (uint32_t)(g * 128);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint32_t off = (uint32_t)((kk >> 2) * F::TILE + (kk & 3) * 32);
-          umma_f16_ss(tmem + (uint32_t)(g * 128), sdesc_sw128(q_base + off, 16, 1024),
-                      sdesc_sw128(k_base + off, 16, 1024), IDESC_S, kk > 0);
+          const uint32_t off = (uint32_t)(((kk >> 2) * F::TILE + (kk & 3) * 32) >> 4);
+          umma_f16_ss_lohi(d, q_lo + off, k_lo + off, DHI, IDESC_S, kk > 0);
         }
         umma_commit(&k_empty[ks]);
         umma_commit(&s_full[g]);
@@ -271,15 +275,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(&p_full[g], (i >> 1) & 1, abort_flag, p.err, kErrWaitOther)) return false;
         if (!mbar_wait(&v_full[vs], (i / F::SV) & 1, abort_flag, p.err, kErrWaitFull)) return false;
         tc_fence_after();
-        const uint32_t v_base = smem_u32(smem + F::OFF_V + vs * F::KV_BYTES);
+        const uint32_t v_lo = sdesc_lo(smem_u32(smem + F::OFF_V + vs * F::KV_BYTES), F::TILE);
+        const uint32_t d = tmem + (uint32_t)(256 + HD * g), pa = tmem + (uint32_t)(g * 128);
+        const uint32_t acc0 = i >= 2 ? 1u : 0u;
 #pragma unroll
         for (int kk = 0; kk < kBK / 16; ++kk) {
           // A = P from TMEM: 16 keys = 8 columns of bf16 pairs. V is MN-major: 16
           // keys = 16 rows of 128 bytes; the second 64-column chunk of head_dim
           // sits one TILE further (leading byte offset).
-          umma_f16_ts(tmem + (uint32_t)(256 + HD * g), tmem + (uint32_t)(g * 128 + kk * 8),
-                      sdesc_sw128(v_base + (uint32_t)(kk * 16 * 128), F::TILE, 1024), IDESC_PV,
-                      (i >= 2 || kk > 0) ? 1u : 0u);
+          umma_f16_ts_lohi(d, pa + (uint32_t)(kk * 8), v_lo + (uint32_t)((kk * 16 * 128) >> 4), DHI, IDESC_PV,
+                           kk > 0 ? 1u : acc0);
         }
         umma_commit(&v_empty[vs]);
         umma_commit(&p_empty[g]);
@@ -422,9 +427,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_st32(tmem + lane_off + o_col + 32 * c, o);
         }
       }
+      // Each thread's TMEM stores complete before its fence; the warp converges and
+      // one lane arrives (four arrivals per warpgroup instead of 128 on the MMA
+      // issuer's critical path).
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&p_full[g]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[g]);
       jl = j;
     }
     // ---- merge the two partial softmaxes; warpgroup g writes output columns
