@@ -101,6 +101,18 @@ void oracle_nf4_block_encode(const float* w, int64_t n, int32_t block, uint8_t* 
 void oracle_nf4_block_decode(const uint8_t* packed, const float* absmax, int64_t n, int32_t block,
                              float* out);
 
+/* welvet_mha_normalbp_f32 (src/interop/c_abi.cpp:249-325) on decoded FP32 weights,
+ * the reference's stream semantics: forward, MSE loss/gradient against
+ * grad_or_target (use_target) or grad_or_target as dL/dpost, mha::backward_f32
+ * (dense gradients, op_attention backward), SGD with rate lr for Float32 storage
+ * (sgd_f32 = 1; otherwise the step is not restated and 2 is returned when lr != 0),
+ * weight export. dW / W_after = concat(Q, K, V, O). */
+int32_t oracle_mha_normalbp(const oracle_mha_cfg* cfg, int32_t batch, int32_t seq, const float* Wq,
+                            const float* Wk, const float* Wv, const float* Wo, const float* x,
+                            const float* grad_or_target, int32_t use_target, double lr, int32_t sgd_f32,
+                            float* pre, float* post, float* dX, float* dW, float* W_after, double* loss,
+                            int32_t threads);
+
 /* Transformer-block forwards (block_oracle.cpp), on decoded FP32 weights. */
 /* act_value of shaders/ops_common.metal:83-105 (Activation ids: -1 Linear, 0 ReLU,
  * 1 Silu, 2 GELU, 3 Tanh, 4 Sigmoid, 5 LeakyReLU, 6 ReLU2). */

@@ -115,6 +115,9 @@ def _load_oracle():
     lib.oracle_fp8_rowscale_decode.argtypes = [_u8p, _f32p, C.c_int64, C.c_int64, _f32p]
     lib.oracle_nf4_block_encode.argtypes = [_f32p, C.c_int64, C.c_int32, _u8p, _f32p]
     lib.oracle_nf4_block_decode.argtypes = [_u8p, _f32p, C.c_int64, C.c_int32, _f32p]
+    lib.oracle_mha_normalbp.argtypes = [cfgp, C.c_int32, C.c_int32] + [_f32p] * 6 + [C.c_int32, C.c_double,
+                                        C.c_int32] + [_f32p] * 5 + [C.POINTER(C.c_double), C.c_int32]
+    lib.oracle_mha_normalbp.restype = C.c_int32
     lib.oracle_act_value.argtypes = [C.c_float, C.c_int32]
     lib.oracle_act_value.restype = C.c_float
     lib.oracle_norm_forward.argtypes = [C.c_int32, C.c_int64, C.c_int32, C.c_double, _f32p, _f32p, _f32p,
@@ -154,6 +157,9 @@ def ref_lib():
         lib.ref_weight_roundtrip.argtypes = [C.c_int32, C.c_int32, C.c_int32, _f32p, _u8p,
                                              C.POINTER(C.c_int64), C.POINTER(C.c_float), _f32p]
         lib.ref_weight_roundtrip.restype = RefStatusC
+        lib.ref_mha_normalbp_f32.argtypes = [C.c_int32] * 10 + [_f32p] * 6 + [C.c_int32, C.c_double] + \
+            [_f32p] * 5 + [C.POINTER(C.c_double)]
+        lib.ref_mha_normalbp_f32.restype = RefStatusC
         lib.ref_swiglu_forward_f32.argtypes = [C.c_int32] * 5 + [_f32p] * 6
         lib.ref_swiglu_forward_f32.restype = RefStatusC
         lib.ref_rmsnorm_forward_f32.argtypes = [C.c_int32] * 3 + [C.c_double, C.c_int32] + [_f32p] * 4
@@ -377,3 +383,42 @@ def ref_embedding_forward(batch, vocab, emb, seq_len, in_rank, in_last, act, W, 
     st = ref_lib().ref_embedding_forward_f32(batch, vocab, emb, seq_len, in_rank, in_last, act, dtype, _f32(W),
                                              _f32(x), pre, post)
     return st.code, st.message.decode(), pre, post
+
+
+def ref_mha_normalbp(cfg: MhaCfg, batch, seq, Wq, Wk, Wv, Wo, x, grad_or_target, use_target, lr, dtype=1):
+    """The reference's welvet_mha_normalbp_f32 (oracle/_ref): (code, msg, pre, post, dX, dW, W_after, loss)."""
+    r = cfg.resolved()
+    qd, kd, d = r.q_dim, r.kv_dim, r.d_model
+    M = batch * seq
+    pre = np.zeros(M * qd, np.float32)
+    post = np.zeros(M * d, np.float32)
+    dX = np.zeros(M * d, np.float32)
+    nw = qd * d + 2 * kd * d + d * qd
+    dW = np.zeros(nw, np.float32)
+    Wa = np.zeros(nw, np.float32)
+    loss = C.c_double(0.0)
+    st = ref_lib().ref_mha_normalbp_f32(batch, seq, cfg.d_model, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim,
+                                        cfg.max_seq_len, cfg.mask, cfg.pos, dtype, _f32(Wq), _f32(Wk), _f32(Wv),
+                                        _f32(Wo), _f32(x), _f32(grad_or_target), int(use_target), float(lr), pre,
+                                        post, dX, dW, Wa, C.byref(loss))
+    return st.code, st.message.decode(), pre, post, dX, dW, Wa, loss.value
+
+
+def mha_normalbp(cfg: MhaCfg, batch, seq, Wq, Wk, Wv, Wo, x, grad_or_target, use_target, lr, sgd_f32=True,
+                 threads=0):
+    """The oracle's welvet_mha_normalbp_f32 on decoded weights: (code, pre, post, dX, dW, W_after, loss)."""
+    r = cfg.resolved()
+    qd, kd, d = r.q_dim, r.kv_dim, r.d_model
+    M = batch * seq
+    pre = np.zeros(M * qd, np.float32)
+    post = np.zeros(M * d, np.float32)
+    dX = np.zeros(M * d, np.float32)
+    nw = qd * d + 2 * kd * d + d * qd
+    dW = np.zeros(nw, np.float32)
+    Wa = np.zeros(nw, np.float32)
+    loss = C.c_double(0.0)
+    c = cfg.to_c()
+    code = oracle_lib().oracle_mha_normalbp(C.byref(c), batch, seq, _f32(Wq), _f32(Wk), _f32(Wv), _f32(Wo),
+                                            _f32(x), _f32(grad_or_target), int(use_target), float(lr),
+                                            1 if sgd_f32 else 0, pre, post, dX, dW, Wa, C.byref(loss), threads)
+    return code, pre, post, dX, dW, Wa, loss.value

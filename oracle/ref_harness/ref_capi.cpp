@@ -6,6 +6,10 @@
 //    mha::forward — running the reference shaders on the CPU executor.
 //  - ref_mha_forward_cfg: the same with every mha::Config field settable.
 //  - ref_weight_roundtrip: WeightStore::make + native bytes + export_f32.
+//  - ref_mha_normalbp_f32: the body of welvet_mha_normalbp_f32
+//    (src/interop/c_abi.cpp:249-325) — forward, MSE or the given gradient,
+//    mha::backward_f32, SGD, weight export (MSE through metal::mse_f32 as
+//    src/runtime/training.cpp:43-57 does).
 //  - ref_swiglu_forward_f32, ref_rmsnorm_forward_f32, ref_layernorm_forward_f32,
 //    ref_embedding_forward_f32: the bodies of the reference's block forward entries
 //    (src/interop/c_abi.cpp:326-361, 437-469, 543-577, 792-832).
@@ -13,6 +17,7 @@
 #include "welvet/embedding.hpp"
 #include "welvet/float_codecs.hpp"
 #include "welvet/layernorm.hpp"
+#include "welvet/metal/training.hpp"
 #include "welvet/mha.hpp"
 #include "welvet/rmsnorm.hpp"
 #include "welvet/swiglu.hpp"
@@ -221,6 +226,63 @@ ref_status ref_embedding_forward_f32(int32_t batch, int32_t vocab, int32_t emb, 
   st = welvet::embedding::forward(layer, input, &pre_t, &post_t);
   if (!st) return to_status(st);
   return copy_out(pre_t, post_t, pre, post);
+}
+
+ref_status ref_mha_normalbp_f32(int32_t batch, int32_t seq, int32_t d_model, int32_t num_heads,
+                                int32_t num_kv_heads, int32_t head_dim, int32_t max_seq_len, int32_t mask,
+                                int32_t pos, int32_t dtype, const float* Q, const float* K, const float* V,
+                                const float* O, const float* x, const float* grad_or_target, int32_t use_target,
+                                double lr, float* pre, float* post, float* dX, float* dW, float* W_after,
+                                double* loss) {
+  if (batch <= 0 || seq <= 0 || d_model <= 0 || num_heads <= 0 || !Q || !K || !V || !O || !x ||
+      !grad_or_target || !pre || !post || !dX || !dW || !W_after || !loss)
+    return invalid("mha nbp: invalid argument");
+  welvet::mha::Config cfg;
+  cfg.d_model = d_model;
+  cfg.num_heads = num_heads;
+  cfg.num_kv_heads = num_kv_heads;
+  cfg.head_dim = head_dim;
+  cfg.max_seq_len = max_seq_len;
+  cfg.mask = static_cast<welvet::mha::MaskKind>(mask);
+  cfg.pos = static_cast<welvet::mha::PosKind>(pos);
+  cfg.mode = welvet::mha::AttnMode::Self;
+  cfg.causal = (cfg.mask == welvet::mha::MaskKind::Causal);
+  welvet::mha::Layer layer;
+  auto st = welvet::mha::new_configured(cfg, static_cast<welvet::DType>(dtype), Q, K, V, O, &layer);
+  if (!st) return to_status(st);
+  welvet::TensorF32 input;
+  input.shape = {batch, seq, d_model};
+  const std::size_t n = static_cast<std::size_t>(batch) * seq * d_model;
+  input.data.assign(x, x + n);
+  welvet::TensorF32 pre_t, post_t;
+  st = welvet::mha::forward(layer, input, &pre_t, &post_t);
+  if (!st) return to_status(st);
+  welvet::TensorF32 gy;
+  gy.shape = post_t.shape;
+  gy.data.assign(grad_or_target, grad_or_target + n);
+  *loss = 0.0;
+  if (use_target) {
+    st = welvet::metal::mse_f32(post_t.data.data(), gy.data.data(), n, loss, nullptr);
+    if (!st) return to_status(st);
+    welvet::TensorF32 g = post_t;
+    st = welvet::metal::mse_f32(post_t.data.data(), gy.data.data(), n, nullptr, g.data.data());
+    if (!st) return to_status(st);
+    gy = std::move(g);
+  }
+  welvet::TensorF32 dx_t, dw_t;
+  st = welvet::mha::backward_f32(layer, gy, input, pre_t, &dx_t, &dw_t);
+  if (!st) return to_status(st);
+  if (lr != 0.0) {
+    st = welvet::mha::apply_grad_sgd(&layer, dw_t, lr);
+    if (!st) return to_status(st);
+  }
+  st = welvet::mha::export_weights_f32(layer, W_after);
+  if (!st) return to_status(st);
+  std::memcpy(pre, pre_t.data.data(), pre_t.data.size() * sizeof(float));
+  std::memcpy(post, post_t.data.data(), post_t.data.size() * sizeof(float));
+  std::memcpy(dX, dx_t.data.data(), dx_t.data.size() * sizeof(float));
+  std::memcpy(dW, dw_t.data.data(), dw_t.data.size() * sizeof(float));
+  return to_status(welvet::Status::Ok());
 }
 
 uint8_t ref_fp8e4m3_encode(float f) { return welvet::float32_to_fp8e4m3(f); }

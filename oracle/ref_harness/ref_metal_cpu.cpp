@@ -14,6 +14,7 @@
 #include "ref_shaders.hpp"
 
 #include <algorithm>
+#include <cmath>
 #include <atomic>
 #include <cstring>
 #include <string>
@@ -72,7 +73,7 @@ Status run(const char* kernel, std::initializer_list<Arg> args, std::initializer
     for (std::size_t t = 0; t < threads; ++t)
       refshader::op_attention_kernel(bufs, ci, cr, (uint32_t)t);
   } else if (std::string(kernel) == "op_swiglu" || std::string(kernel) == "op_norm_forward" ||
-             std::string(kernel) == "op_embedding_forward") {
+             std::string(kernel) == "op_embedding_forward" || std::string(kernel) == "op_add3") {
     dispatch(threads, [&](uint32_t t) { refshader::op_kernel(kernel, bufs, ci, cr, t); });
   } else {
     return Status::Err(StatusCode::Unsupported,
@@ -138,9 +139,23 @@ Status resident_execute(ResidentDense* r, const float* x, float* pre, float* pos
   return Status::Ok();
 }
 
-Status resident_backward(ResidentDense*, const float*, const float*, const float*, float*, float*,
-                         bool) {
-  return Status::Err(StatusCode::Unsupported, "cpu executor: backward is not on the forward path");
+// matvec.mm:402-490: act' (Linear when `linear`), then gx = W^T d_pre and
+// dW = d_pre^T x, each kernel over its own grid.
+Status resident_backward(ResidentDense* r, const float* grad_out, const float* input, const float* pre,
+                         float* grad_in, float* grad_w, bool linear) {
+  if (!r || !r->buf_w || !grad_out || !input || !pre || !grad_in || !grad_w)
+    return Status::Err(StatusCode::InvalidArgument, "null resident backward");
+  auto* h = static_cast<HostResident*>(r->buf_w);
+  const uint32_t in = (uint32_t)r->cols, out = (uint32_t)r->rows, batch = (uint32_t)r->batch;
+  const int32_t act = linear ? (int32_t)Activation::Linear : (int32_t)r->act;
+  std::vector<float> d_pre((std::size_t)batch * out);
+  dispatch((std::size_t)batch * out,
+           [&](uint32_t gid) { refshader::dense_act_deriv(grad_out, pre, d_pre.data(), out, batch, act, gid); });
+  dispatch((std::size_t)batch * in,
+           [&](uint32_t gid) { refshader::dense_matvect(h->w_xy.data(), d_pre.data(), grad_in, in, out, batch, gid); });
+  dispatch((std::size_t)out * in,
+           [&](uint32_t gid) { refshader::dense_outer(d_pre.data(), input, grad_w, in, out, batch, gid); });
+  return Status::Ok();
 }
 
 void resident_release(ResidentDense* r) {
@@ -150,8 +165,33 @@ void resident_release(ResidentDense* r) {
   }
 }
 
-Status sgd_f32_f64_grad(float*, const double*, std::size_t, double) {
-  return Status::Err(StatusCode::Unsupported, "cpu executor: SGD is not on the forward path");
+// training.mm:75-128: gradients split to float2 pairs on the host, the update runs
+// in welvet_sgd_f32_f64_grad.
+Status sgd_f32_f64_grad(float* weights, const double* grad, std::size_t n, double lr) {
+  if (!weights || !grad || !n) return Status::Err(StatusCode::InvalidArgument, "Metal SGD: gradient size");
+  std::vector<float> xy(n * 2);
+  for (std::size_t i = 0; i < n; ++i) {
+    if (!std::isfinite(grad[i]) || std::abs(grad[i]) > 3.4028234663852886e38)
+      return Status::Err(StatusCode::Unsupported, "Metal SGD: gradient exceeds soft-double range");
+    split_double(grad[i], &xy[2 * i], &xy[2 * i + 1]);
+  }
+  float rate[2];
+  split_double(lr, &rate[0], &rate[1]);
+  dispatch(n, [&](uint32_t gid) { refshader::sgd_f32_f64_grad(weights, xy.data(), rate, (uint32_t)n, gid); });
+  return Status::Ok();
+}
+
+// training.mm:130-180: the loss kernel (one thread, serial order) and the gradient.
+Status mse_f32(const float* pred, const float* target, std::size_t n, double* loss, float* grad) {
+  if (!pred || !target || (!loss && !grad) || !n)
+    return Status::Err(StatusCode::InvalidArgument, "Metal MSE: invalid arguments");
+  if (loss) {
+    float l2[2] = {0.f, 0.f};
+    refshader::mse_loss(pred, target, l2, (uint32_t)n);
+    std::memcpy(loss, l2, sizeof(double));
+  }
+  if (grad) dispatch(n, [&](uint32_t gid) { refshader::mse_grad(pred, target, grad, (uint32_t)n, gid); });
+  return Status::Ok();
 }
 
 } // namespace welvet::metal

@@ -83,6 +83,21 @@ BLOCK_CASES = {
 }
 
 
+# MHA NormalBP leaf (reference welvet_mha_normalbp_f32): name: (config kwargs, batch,
+# seq, dtype, use_target, lr). Weights from the Xavier stream (seed 0); x, the target
+# / gradient and every output are stored.
+NBP_CASES = {
+    "nbp_tiny_sgd": (dict(d_model=16, num_heads=2), 1, 8, 1, 1, 0.01),
+    "nbp_stream2_sgd": (dict(d_model=16, num_heads=2), 2, 6, 1, 1, 0.01),
+    "nbp_gqa_gradout": (dict(d_model=32, num_heads=4, num_kv_heads=2), 2, 5, 1, 0, 0.0),
+    "nbp_alibi_sgd": (dict(d_model=16, num_heads=2, pos=2), 2, 4, 1, 1, 0.02),
+    "nbp_ropealibi_bidir": (dict(d_model=16, num_heads=2, pos=3, mask=2), 2, 4, 1, 1, 0.0),
+    "nbp_ring_wrap_sgd": (dict(d_model=16, num_heads=2, max_seq_len=8), 3, 6, 1, 1, 0.01),
+    "nbp_window_bf16": (dict(d_model=24, num_heads=2, mask=3), 2, 7, 3, 1, 0.0),
+    "nbp_prefix_nopos_int8": (dict(d_model=16, num_heads=2, mask=4, pos=1), 2, 5, 9, 0, 0.0),
+}
+
+
 def block_inputs(kind, p, seed):
     """Deterministic inputs of a block case (counter-based stream, platform independent
     up to libm in the normal transform; stored in the fixture)."""
@@ -164,6 +179,22 @@ def main():
         _save(os.path.join(HERE, f"mha_{name}.npz"), x=x, pre=pre, post=post)
     with open(os.path.join(HERE, "mha_cases.json"), "w") as f:
         json.dump(out, f, indent=1, sort_keys=True)
+
+    nbp = {}
+    for name, (kw, B, T, dt, ut, lr) in NBP_CASES.items():
+        cfg = O.MhaCfg(**kw)
+        Wq, Wk, Wv, Wo = weights_for(cfg)
+        x = synthetic(B * T * cfg.d_model, 1, 1, 1.0)
+        tgt = synthetic(B * T * cfg.d_model, 2, 1, 1.0)
+        code, msg, pre, post, dX, dW, Wa, loss = O.ref_mha_normalbp(cfg, B, T, Wq, Wk, Wv, Wo, x, tgt, ut, lr,
+                                                                    dtype=dt)
+        if code:
+            raise SystemExit(f"{name}: reference returned {code} {msg}")
+        nbp[name] = dict(cfg=kw, batch=B, seq=T, dtype=dt, use_target=ut, lr=lr, wsum=wsum((Wq, Wk, Wv, Wo)))
+        _save(os.path.join(HERE, f"{name}.npz"), x=x, target=tgt, pre=pre, post=post, dX=dX, dW=dW, W_after=Wa,
+              loss=np.float64(loss))
+    with open(os.path.join(HERE, "nbp_cases.json"), "w") as f:
+        json.dump(nbp, f, indent=1, sort_keys=True)
 
     blocks = {}
     for i, (name, (kind, p)) in enumerate(BLOCK_CASES.items()):
