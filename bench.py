@@ -59,6 +59,9 @@ WORKLOADS = {
     "rmsnorm": dict(B=16, T=4096, d=4096, kind="rmsnorm"),
     "layernorm": dict(B=16, T=4096, d=4096, kind="layernorm"),
     "embedding": dict(B=16, T=4096, d=4096, vocab=128256, kind="embedding"),
+    # MHA NormalBP leaf (welvet_mha_normalbp_f32): forward + MSE + backward + SGD, FP32,
+    # the reference's stream semantics, one call per step from host buffers
+    "mha-nbp": dict(B=4, T=512, d=1024, H=16, kind="nbp"),
 }
 BLOCK_KINDS = ("swiglu", "rmsnorm", "layernorm", "embedding")
 CODEC_DTYPES = range(34)
@@ -67,6 +70,7 @@ CODEC_STATS_FREE = (0, 1, 2, 3, 4, 5, 16, 24, 25)  # dtypes without a per-tensor
 METRIC = "MHA prefill tok/s (BASELINE config 5; decode tok/s under 'decode')"
 METRIC_DECODE = "MHA decode tok/s (BASELINE config 3)"
 METRIC_CODEC = "FormatNone weight round trip GB/s (decode(encode(w)), dtypes 0-33)"
+METRIC_NBP = "MHA NormalBP tok/s (forward + backward + SGD)"
 METRIC_BLOCK = {"swiglu": "SwiGLU forward tok/s", "rmsnorm": "RMSNorm forward tok/s",
                 "layernorm": "LayerNorm forward tok/s", "embedding": "Embedding forward tok/s"}
 
@@ -76,7 +80,7 @@ def workload(args):
     if w["kind"] == "codec":
         w["n"] = args.batch or w["n"]
         return w
-    if w["kind"] in BLOCK_KINDS:
+    if w["kind"] in BLOCK_KINDS or w["kind"] == "nbp":
         w["B"] = args.batch or w["B"]
         w["T"] = args.seq or w["T"]
         return w
@@ -93,6 +97,11 @@ def workload_config(args, world):
         return {"workload": f"codec: decode(encode(w)) of {w['n']} FP32 weights, FormatNone dtypes 0-33",
                 "global_batch": w["n"], "seq_len": 1, "parallelism": f"replicas x{world}",
                 "l2": "tensor larger than L2 (%.2f GB)" % (w["n"] * 4 / 1e9)}
+    if w["kind"] == "nbp":
+        return {"workload": f"mha-nbp: NormalBP leaf (forward, MSE, backward, SGD) B={w['B']} T={w['T']} "
+                            f"d={w['d']} H={w['H']}x{w['d'] // w['H']} causal RoPE FP32, stream semantics",
+                "global_batch": w["B"], "seq_len": w["T"], "parallelism": f"replicas x{world}",
+                "l2": "one call per step from host buffers (the reference entry's contract)"}
     if w["kind"] in BLOCK_KINDS:
         B, T, d = w["B"], w["T"], w["d"]
         desc = {"swiglu": f"SwiGLU d={d} inter={w.get('inter')} BF16",
@@ -256,6 +265,8 @@ def run_reference(args):
         return
     if w["kind"] in BLOCK_KINDS:
         return run_block_reference(args, w)
+    if w["kind"] == "nbp":
+        return run_nbp_reference(args, w)
     if w["kind"] == "codec":
         use_ref = O.ref_available()
         n_s = 1 << 20
@@ -564,6 +575,132 @@ def run_block(args, rank, world, local):
         dist.destroy_process_group()
 
 
+def nbp_inputs(d, H, M, seed=0):
+    import welvet_b200 as W
+    Ws = W.xavier_weights(d, d, d, seed=seed)
+    x = W.synthetic(M * d, 1, 1, 1.0)
+    tgt = W.synthetic(M * d, 2, 1, 1.0)
+    return Ws, x, tgt
+
+
+def nbp_sample(w, use_ref, B, T):
+    """One NormalBP call of B x T tokens of the workload's layer on the host: the
+    reference's own entry (oracle/_ref) or the FP64 port. Returns seconds."""
+    import oracle_py as O
+    d, H = w["d"], w["H"]
+    Ws, x, tgt = nbp_inputs(d, H, B * T)
+    cfg = O.MhaCfg(d_model=d, num_heads=H, max_seq_len=max(512, T))
+    t0 = time.perf_counter()
+    if use_ref:
+        code, msg, *_ = O.ref_mha_normalbp(cfg, B, T, *Ws, x, tgt, 1, 0.01)
+        if code:
+            raise RuntimeError(msg)
+    else:
+        code, *_ = O.mha_normalbp(cfg, B, T, *Ws, x, tgt, 1, 0.01)
+        if code:
+            raise RuntimeError(f"oracle {code}")
+    return time.perf_counter() - t0
+
+
+def run_nbp_reference(args, w):
+    import oracle_py as O
+    use_ref = O.ref_available()
+    T_s = 16
+    for _ in range(args.warmup):
+        nbp_sample(w, use_ref, 1, 4)
+    tot = sum(nbp_sample(w, use_ref, 1, T_s) for _ in range(args.steps))
+    value = T_s * args.steps / tot
+    kind = "reference" if use_ref else "port"
+    sample = f"1 x {T_s} tokens of the mha-nbp layer per step through the reference's welvet_mha_normalbp_f32 body"
+    print(json.dumps({"impl": "reference", "metric": METRIC_NBP, "value": value, "unit": "tok/s",
+                      "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                      "ms_per_step": tot / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+                      "vs_baseline": None, "dtype": "f64 (soft-double)", "data": "synthetic",
+                      "config": workload_config(args, args.gpus),
+                      "cpu_baseline": {"value": value, "unit": "tok/s", "cores": os.cpu_count(), "kind": kind,
+                                       "sample": sample},
+                      "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+          flush=True)
+
+
+def run_nbp(args, rank, world, local):
+    """The NormalBP leaf: a step is one welvet_mha_normalbp_f32 call (host buffers in
+    and out, weights encoded per call, as the reference entry), so `value` and `e2e`
+    are the same measurement; the live per-kernel event profile splits it."""
+    import torch
+    import torch.distributed as dist
+    import welvet_b200 as W
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    w = workload(args)
+    B, T, d, H = w["B"], w["T"], w["d"], w["H"]
+    M = B * T
+    Ws, x, tgt = nbp_inputs(d, H, M, seed=rank)
+
+    def step():
+        return W.mha_normalbp_f32(B, T, d, H, 0, 0, max(512, T), 1, 0, 1, *Ws, x, tgt, 1, 0.01)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = Clocks(local)
+    clocks.start()
+    W.profile_read(reset=True)
+    W.profile_enable(True)
+    W.launch_count(reset=True)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    el = (time.perf_counter() - t0) / args.steps * 1e3
+    launches = W.launch_count(reset=True)
+    W.profile_enable(False)
+    prof = W.profile_read(reset=True)
+    clk = clocks.stop()
+    if world > 1:
+        t = torch.tensor([el], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        el = float(t.item())
+    value = world * M / (el / 1e3)
+    hd = d // H
+    # algorithmic FP64 work of the attention backward: per (head, query, allowed key)
+    # the score dot, dw dot, gv / gk / gq updates ~ 5 x 2 hd FLOPs; keys = all earlier
+    # positions of the stream (causal)
+    keys = sum(T * b * T + T * (T + 1) / 2 for b in range(B))
+    attn_flops = H * keys * 10.0 * hd
+    gemm_flops = 2.0 * M * d * d * (4 + 4)  # QKV recompute, dX, dWqkv (3 d x d each) + O grads
+    a_ms = prof["attn_bwd"][0] / args.steps
+    g_ms = prof["gemm_grad"][0] / args.steps
+    roof = {"bound": "fp64-atomics", "kernel": "attn_bwd_query_kernel", "achieved": attn_flops / (a_ms / 1e3) / 1e12,
+            "peak": None, "unit": "TFLOP/s", "frac": None,
+            "peak_kind": "no measured FP64 peak on this pool; FP64 CUDA-core kernel with FP64 atomics into the key ring",
+            "traffic": None, "kernel_ms_per_step": {"attn_bwd": a_ms, "gemm_grad": g_ms},
+            "gemm_grad_tflops": gemm_flops / (g_ms / 1e3) / 1e12 if g_ms > 0 else None}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        T_c = 64
+        dt = nbp_sample(w, False, 1, T_c)
+        cpu = {"value": T_c / dt, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+               "sample": f"FP64 oracle, 1 x {T_c} tokens of the layer, {dt:.2f} s"}
+    if rank == 0:
+        print(json.dumps({"metric": METRIC_NBP, "value": value, "unit": "tok/s", "n_gpus": world,
+                          "steps": args.steps, "warmup": args.warmup, "ms_per_step": el, "higher_is_better": True,
+                          "scaling": "weak", "vs_baseline": None, "dtype": "f32 (FP64 attention backward)",
+                          "data": "synthetic", "config": workload_config(args, world), "roofline": roof,
+                          "cpu_baseline": cpu,
+                          "e2e": {"value": value, "unit": "tok/s", "ms_per_step": el,
+                                  "h2d_bytes_per_step": 4 * (4 * d * d + 2 * M * d),
+                                  "d2h_bytes_per_step": 4 * (M * d * 3 + 8 * d * d),
+                                  "api": "welvet_mha_normalbp_f32 (host buffers)"},
+                          "gpu_launches": launches, "clocks": clk,
+                          "profile_ms": {k: v[0] / args.steps for k, v in prof.items() if v[1]}}), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def run_codec(args, rank, world, local):
     """FormatNone round trips (the mount-time weight codec) of one 1 GiB FP32 tensor
     per GPU, every dtype in turn; a step = all 34 dtypes. Replicas only: each rank
@@ -703,6 +840,8 @@ def main():
         return run_codec(args, rank, world, local)
     if workload(args)["kind"] in BLOCK_KINDS:
         return run_block(args, rank, world, local)
+    if workload(args)["kind"] == "nbp":
+        return run_nbp(args, rank, world, local)
     if world > 1:
         # NVLS (in-switch reduction) is off unless the caller sets it: on this pool's
         # 8-GPU boxes the 256 KB decode all-reduce took 31 ms with NVLS and 0.05 ms

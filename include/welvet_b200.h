@@ -168,11 +168,12 @@ WELVET_API int64_t welvet_b200_launch_count(int32_t reset);
  * with steady_clock, tools/dense_fwd/main.cpp:198-216). When enabled, each hot kernel
  * of forward / decode is bracketed by CUDA events on its launch stream.
  * welvet_b200_profile_read synchronises and returns, per kernel id, the summed
- * milliseconds and launch counts (12 slots: 0 QKV GEMM, 1 prefill attention, 2 O GEMM,
+ * milliseconds and launch counts (14 slots: 0 QKV GEMM, 1 prefill attention, 2 O GEMM,
  * 3 decode attention, 4 decode QKV GEMM, 5 decode O GEMM, 6 all-reduce, 7 other,
- * 8 SwiGLU Gate|Up GEMM, 9 SwiGLU Down GEMM, 10 RMSNorm/LayerNorm, 11 embedding). */
+ * 8 SwiGLU Gate|Up GEMM, 9 SwiGLU Down GEMM, 10 RMSNorm/LayerNorm, 11 embedding,
+ * 12 NormalBP attention backward, 13 NormalBP gradient GEMMs). */
 WELVET_API void welvet_b200_profile_enable(int32_t on);
-WELVET_API void welvet_b200_profile_read(double ms[12], int64_t counts[12], int32_t reset);
+WELVET_API void welvet_b200_profile_read(double ms[14], int64_t counts[14], int32_t reset);
 
 /* ---- decode attention without allocation (no counterpart in the reference) ----
  * Split-KV decode attention of one new query per sequence over a paged KV cache,

@@ -6,10 +6,10 @@
  * Every declaration below has the same name, signature, argument meaning and
  * status semantics as the reference header include/welvet_c.h of
  * openfluke/welvet.metal; the line of the reference each one replaces is cited.
- * Besides the MHA forward it serves the forward entries of the transformer block
- * around it (SwiGLU, RMSNorm, LayerNorm, Embedding). The reference's other entry
- * points (Dense/CNN/recurrent families, backward/NormalBP leaves, model sessions)
- * are not part of this library. */
+ * Besides the MHA forward it serves the MHA NormalBP leaf and the forward entries
+ * of the transformer block around it (SwiGLU, RMSNorm, LayerNorm, Embedding). The
+ * reference's other entry points (Dense/CNN/recurrent families, the other NormalBP
+ * leaves, model sessions) are not part of this library. */
 
 #include <stddef.h>
 #include <stdint.h>
@@ -53,6 +53,20 @@ WELVET_API welvet_status welvet_mha_forward_f32(
     int32_t head_dim, int32_t max_seq_len, int32_t mask, int32_t pos, int32_t dtype, int32_t backend,
     const float* Q, const float* K, const float* V, const float* O, const float* x, float* pre,
     float* post);
+
+/* Reference include/welvet_c.h:94-103 (impl src/interop/c_abi.cpp:249-325). MHA NormalBP
+ * leaf: forward, then dL/dpost = MSE gradient against grad_or_target (use_target = 1,
+ * *loss = the MSE) or grad_or_target itself (use_target = 0, *loss = 0), the backward
+ * with the reference's stream semantics, SGD with rate lr (Float32 storage; other
+ * dtypes need lr = 0 here, status 2 otherwise), the weight export. Outputs pre
+ * [batch*seq*q_dim], post and dX [batch*seq*d_model], dW and W_after = concat(Q, K,
+ * V, O). Host memory, synchronous, nothing retained. */
+WELVET_API welvet_status welvet_mha_normalbp_f32(
+    int32_t batch, int32_t seq, int32_t d_model, int32_t num_heads, int32_t num_kv_heads,
+    int32_t head_dim, int32_t max_seq_len, int32_t mask, int32_t pos, int32_t dtype, int32_t backend,
+    const float* Q, const float* K, const float* V, const float* O, const float* x,
+    const float* grad_or_target, int32_t use_target, double lr, float* pre, float* post, float* dX,
+    float* dW, float* W_after, double* loss);
 
 /* Reference include/welvet_c.h:105-109 (impl src/interop/c_abi.cpp:326-361).
  * SwiGLU forward: Gate/Up [intermediate_dim, input_dim], Down [input_dim,

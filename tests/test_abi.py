@@ -23,7 +23,8 @@ def declared_symbols():
 def test_headers_declare_the_reference_mha_entry_points():
     names = declared_symbols()
     for n in ("welvet_version", "welvet_runtime_identity", "welvet_metal_init", "welvet_metal_available",
-              "welvet_mha_forward_f32", "welvet_swiglu_forward_f32", "welvet_rmsnorm_forward_f32",
+              "welvet_mha_forward_f32", "welvet_mha_normalbp_f32", "welvet_swiglu_forward_f32",
+              "welvet_rmsnorm_forward_f32",
               "welvet_layernorm_forward_f32", "welvet_embedding_forward_f32"):
         assert n in names
 
@@ -126,3 +127,20 @@ def test_block_entries_report_unknown_dtypes_with_the_reference_codes():
     # embedding rank 3 needs in_last 1 or emb
     st = lib.welvet_embedding_forward_f32(1, 4, 8, 2, 3, 3, -1, 1, 0, *[W._ptr(z)] * 4)
     assert st.code == 1 and "want 1 or emb" in st.message.decode()
+
+
+def test_normalbp_rejects_bad_arguments_and_dtypes_like_the_reference():
+    """c_abi.cpp:249-268: null / non-positive arguments -> 1 "mha nbp: invalid
+    argument"; dtype outside 0-33 -> 1 "mha nbp: bad dtype"; SGD of non-FP32 storage
+    is the documented gap (status 2). No device work is reached."""
+    z = np.zeros(4096, np.float32)
+    lib = W.lib()
+    loss = W.C.c_double(0.0)
+    args = lambda b, dt, lr: (b, 4, 16, 2, 0, 0, 0, 1, 0, dt, 0, *[W._ptr(z)] * 6, 1, lr, *[W._ptr(z)] * 5,  # noqa
+                              W.C.byref(loss))
+    st = lib.welvet_mha_normalbp_f32(*args(0, 1, 0.0))
+    assert st.code == 1 and st.message.decode() == "mha nbp: invalid argument"
+    st = lib.welvet_mha_normalbp_f32(*args(1, 34, 0.0))
+    assert st.code == 1 and st.message.decode() == "mha nbp: bad dtype 34"
+    st = lib.welvet_mha_normalbp_f32(*args(1, 9, 0.01))
+    assert st.code == 2 and "Float32 only" in st.message.decode()

@@ -230,4 +230,39 @@ cudaError_t pad_cols(const float* src, float* dst, int64_t rows, int cols, int c
 cudaError_t pad_operand(const void* x, int x_bf16, int64_t rows, int cols, int cols_p, float* hi,
                         float* lo, void* b, cudaStream_t s);
 
+// ---- MHA NormalBP leaf (mha_bwd.cu)
+struct BwdArgs {
+  int B = 0, T = 0;
+  int64_t M = 0;
+  int nh = 0, nk = 0, hd = 0, qd = 0, kd = 0, msl = 0;
+  int mask = 1, window = 0, window_causal = 1, prefix = 0;
+  int rope = 0, alibi = 0, sigmoid = 0;
+  double theta = 10000.0, scale = 1.0;
+  int shift = 0;                    // 64 when every attention gradient is below 1e-20
+  const float* qkv = nullptr;       // [M, ld_qkv]: q | k | v projections (no RoPE)
+  int ld_qkv = 0;
+  const float* grad_attn = nullptr; // [M, qd]
+  double* ck = nullptr;             // [msl, kd] key ring (rotated)
+  double* cv = nullptr;             // [msl, kd]
+  double* qb = nullptr;             // [T, qd] the batch's rotated q rows
+  double* gq = nullptr;             // [T, qd]
+  double* gk = nullptr;             // [msl, kd] key-gradient ring (kept across batches)
+  double* gv = nullptr;             // [msl, kd]
+  double* scratch = nullptr;        // [T * nh, 2 * kvmax]
+  int kvmax = 0;
+  float* g_q = nullptr;             // outputs, rows of stride ld_g
+  float* g_k = nullptr;
+  float* g_v = nullptr;
+  int ld_g = 0;
+};
+cudaError_t attn_backward(const BwdArgs& a, cudaStream_t s);
+// src [rows, cols] -> [cols, rows_p] transposed, as TF32 hi/lo pairs, zero rows past `rows`
+cudaError_t transpose_split(const float* src, int64_t rows, int cols, int64_t rows_p, float* hi, float* lo,
+                            cudaStream_t s);
+int mse_grid(int64_t n);
+// grad = fl32(2 (pred - target) / n); partial[mse_grid(n)] = sums of squared differences
+cudaError_t mse_grad(const float* pred, const float* target, float* grad, double* partial, int64_t n,
+                     cudaStream_t s);
+cudaError_t sgd_f32(const float* w, const float* g, float* out, int64_t n, double lr, cudaStream_t s);
+
 } // namespace wv

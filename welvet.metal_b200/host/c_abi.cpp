@@ -366,7 +366,7 @@ int64_t welvet_b200_launch_count(int32_t reset) {
 
 void welvet_b200_profile_enable(int32_t on) { wv::prof_enable(on != 0); }
 
-void welvet_b200_profile_read(double ms[12], int64_t counts[12], int32_t reset) {
+void welvet_b200_profile_read(double ms[14], int64_t counts[14], int32_t reset) {
   wv::prof_read(ms, counts, reset != 0);
 }
 

@@ -61,7 +61,9 @@ enum ProfId : int {
   kProfGemmDown = 9,     // SwiGLU Down GEMM
   kProfNorm = 10,        // RMSNorm / LayerNorm
   kProfEmbedding = 11,
-  kProfCount = 12,
+  kProfAttnBwd = 12,     // NormalBP attention backward
+  kProfGemmGrad = 13,    // NormalBP gradient GEMMs
+  kProfCount = 14,
 };
 void prof_enable(bool on);
 bool prof_on();

@@ -22,7 +22,8 @@ LIB_PATH = os.path.join(HERE, "lib", "libwelvet_b200.so")
 
 # Exported symbols declared in include/welvet_c.h and include/welvet_b200.h.
 C_ABI_SYMBOLS = ("welvet_version", "welvet_runtime_identity", "welvet_metal_init",
-                 "welvet_metal_available", "welvet_mha_forward_f32", "welvet_swiglu_forward_f32",
+                 "welvet_metal_available", "welvet_mha_forward_f32", "welvet_mha_normalbp_f32",
+                 "welvet_swiglu_forward_f32",
                  "welvet_rmsnorm_forward_f32", "welvet_layernorm_forward_f32", "welvet_embedding_forward_f32")
 EXT_SYMBOLS = ("welvet_b200_mha_config_default", "welvet_b200_mha_mount", "welvet_b200_mha_release",
                "welvet_b200_mha_forward", "welvet_b200_mha_check", "welvet_b200_kv_create",
@@ -38,7 +39,7 @@ EXT_SYMBOLS = ("welvet_b200_mha_config_default", "welvet_b200_mha_mount", "welve
                "welvet_b200_swiglu_forward_host", "welvet_b200_swiglu_release", "welvet_b200_norm_forward",
                "welvet_b200_embedding_forward")
 PROFILE_SLOTS = ("gemm_qkv", "attn_prefill", "gemm_o", "attn_decode", "gemm_qkv_decode", "gemm_o_decode",
-                 "allreduce", "other", "gemm_gate_up", "gemm_down", "norm", "embedding")
+                 "allreduce", "other", "gemm_gate_up", "gemm_down", "norm", "embedding", "attn_bwd", "gemm_grad")
 
 DTYPES = {"float64": 0, "float32": 1, "float16": 2, "bfloat16": 3, "fp8e4m3": 4, "fp8e5m2": 5, "nf4": 26}
 
@@ -96,6 +97,9 @@ def lib():
     L.welvet_metal_init.restype = Status
     L.welvet_metal_available.restype = C.c_int32
     L.welvet_mha_forward_f32.argtypes = [C.c_int32] * 11 + [_vp] * 7
+    L.welvet_mha_normalbp_f32.argtypes = [C.c_int32] * 11 + [_vp] * 6 + [C.c_int32, C.c_double] + [_vp] * 5 + \
+        [C.POINTER(C.c_double)]
+    L.welvet_mha_normalbp_f32.restype = Status
     L.welvet_swiglu_forward_f32.argtypes = [C.c_int32] * 6 + [_vp] * 6
     L.welvet_rmsnorm_forward_f32.argtypes = [C.c_int32] * 3 + [C.c_double, C.c_int32, C.c_int32] + [_vp] * 4
     L.welvet_layernorm_forward_f32.argtypes = [C.c_int32] * 3 + [C.c_double, C.c_int32, C.c_int32] + [_vp] * 5
@@ -237,6 +241,27 @@ def mha_forward_f32(batch, seq, d_model, num_heads, num_kv_heads, head_dim, max_
                                       _ptr(pre), _ptr(post))
     check(st)
     return pre, post
+
+
+def mha_normalbp_f32(batch, seq, d_model, num_heads, num_kv_heads, head_dim, max_seq_len, mask, pos, dtype,
+                     Q, K, V, O, x, grad_or_target, use_target, lr, backend=0):
+    """welvet_mha_normalbp_f32 with numpy buffers: (pre, post, dX, dW, W_after, loss)."""
+    f = lambda a: np.ascontiguousarray(a, dtype=np.float32)  # noqa: E731
+    Q, K, V, O, x, g = (f(a) for a in (Q, K, V, O, x, grad_or_target))
+    M = batch * seq
+    qd, kdim = Q.shape[0], K.shape[0]
+    pre = np.zeros(max(1, M * qd), np.float32)
+    post = np.zeros(max(1, M * d_model), np.float32)
+    dX = np.zeros(max(1, M * d_model), np.float32)
+    nw = Q.size + K.size + V.size + O.size
+    dW = np.zeros(nw, np.float32)
+    Wa = np.zeros(nw, np.float32)
+    loss = C.c_double(0.0)
+    check(lib().welvet_mha_normalbp_f32(batch, seq, d_model, num_heads, num_kv_heads, head_dim, max_seq_len, mask,
+                                        pos, dtype, backend, _ptr(Q), _ptr(K), _ptr(V), _ptr(O), _ptr(x), _ptr(g),
+                                        int(use_target), float(lr), _ptr(pre), _ptr(post), _ptr(dX), _ptr(dW),
+                                        _ptr(Wa), C.byref(loss)))
+    return pre, post, dX, dW, Wa, loss.value
 
 
 def swiglu_forward_f32(batch, seq, Gate, Up, Down, x, dtype=1, backend=0):
