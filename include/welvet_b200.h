@@ -179,8 +179,9 @@ WELVET_API void welvet_b200_profile_read(double ms[14], int64_t counts[14], int3
  * Split-KV decode attention of one new query per sequence over a paged KV cache,
  * the same kernels as the decode step of welvet_b200_mha_decode, with the split
  * partials in a fixed per-device array of WELVET_B200_DECODE_STATIC_FLOATS floats
- * (4 MiB) instead of allocated memory: for callers that may not allocate device
- * memory while decoding (a pre-reserved HBM pool; a captured stream region).
+ * (4 MiB) instead of allocated memory: for callers that may not let a library
+ * allocate device memory while decoding (HBM reserved up front by their own pool;
+ * a framework whose caching allocator accounts for all device memory).
  * All buffers are device memory; asynchronous on `stream`.
  *   cfg         heads, KV heads, head_dim, scale, ALiBi / sigmoid, precision
  *               (1: BF16 buffers, 0: FP32), head shard; causal mask only.

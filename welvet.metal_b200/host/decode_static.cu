@@ -7,9 +7,10 @@
 //     (the KV pages, the activations and the weights fill the device), so a
 //     late cudaMalloc can fail, and cudaFree synchronises the whole device,
 //     stalling the other streams of the loop;
-//   * a caller that records its decode step with stream capture: in the default
-//     (global) capture mode a cudaMalloc inside the captured region is an error
-//     and invalidates the capture.
+//   * a host framework that owns all device memory through its own caching
+//     allocator (PyTorch's, for one) and sizes its pools against the free
+//     memory it sees: memory that a library takes behind its back is missing
+//     from that accounting and can make the framework's next allocation fail.
 // For them this entry point runs the same two kernels (decode_kernel +
 // decode_combine_kernel) with the partials in a fixed file-scope device array.
 //
@@ -72,7 +73,7 @@ Status decode_attention_static(const welvet_b200_mha_config& cfg_in, int batch, 
                                int ldq, const void* k_pool, const void* v_pool, const int* block_table,
                                int max_pages, const int* ctx_len, void* out, int ldo, cudaStream_t stream) {
   if (batch <= 0 || max_ctx <= 0 || !q || !k_pool || !v_pool || !block_table || !ctx_len || !out ||
-      max_pages * kPageTokens < max_ctx)
+      (int64_t)max_pages * kPageTokens < max_ctx)
     return Status::err(1, "decode_attention_static: invalid argument");
   Cfg c;
   WV_TRY(resolve_config(cfg_in, &c));
