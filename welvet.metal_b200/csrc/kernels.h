@@ -245,6 +245,7 @@ struct BwdArgs {
   double* ck = nullptr;             // [msl, kd] key ring (rotated)
   double* cv = nullptr;             // [msl, kd]
   double* qb = nullptr;             // [T, qd] the batch's rotated q rows
+  double* gyb = nullptr;            // [T, qd] the batch's attention gradient rows (x 2^shift)
   double* gq = nullptr;             // [T, qd]
   double* gk = nullptr;             // [msl, kd] key-gradient ring (kept across batches)
   double* gv = nullptr;             // [msl, kd]

@@ -524,6 +524,22 @@ Status run_attention(Mha* m, AttnArgs a, cudaStream_t s) {
 
 } // namespace
 
+// New weights for a mounted FP32 layer that holds every head in the FormatNone
+// layout (precision 0, weight format 0): already decoded device matrices W_qkv
+// [q_dim + 2 kv_dim, d_model] (rows Q | K | V) and Wo [d_model, q_dim] are split
+// into the layer's TF32 pairs in place; nothing is allocated.
+Status mha_reload_fp32(Mha* m, const float* wqkv, const float* wo, cudaStream_t s) {
+  if (!m || !wqkv || !wo) return Status::err(1, "mha: invalid argument");
+  if (m->precision != 0 || m->wfmt != 0 || m->qd_l != m->cfg.qd || m->kd_l != m->cfg.kd)
+    return Status::err(2, "mha: weight reload needs an FP32 layer holding every head");
+  std::lock_guard<std::mutex> lock(m->mu);
+  const int64_t dm = m->cfg.c.d_model;
+  WV_CUDA(split_tf32(wqkv, m->wqkv.as<float>(), m->wqkv_lo.as<float>(), (int64_t)m->nqkv * dm, s), "split");
+  WV_CUDA(split_tf32(wo, m->wo.as<float>(), m->wo_lo.as<float>(), dm * m->qd_l, s), "split");
+  count_launch(2);
+  return Status::ok();
+}
+
 Status mha_forward(Mha* m, int batch, int seq, const void* x, void* pre, void* post, bool on_device,
                    cudaStream_t s, Kv* kv) {
   if (!m || !x || !post || batch <= 0 || seq <= 0) return Status::err(1, "mha: invalid argument");

@@ -155,6 +155,9 @@ struct Mha {
 
 Status mha_mount(const welvet_b200_mha_config& cfg, int dtype, const float* Q, const float* K,
                  const float* V, const float* O, bool on_device, Mha** out);
+// Replaces the weights of an FP32 full-head layer by decoded device matrices
+// (W_qkv rows Q | K | V, Wo), without allocating.
+Status mha_reload_fp32(Mha* m, const float* wqkv, const float* wo, cudaStream_t s);
 Status mha_forward(Mha* m, int batch, int seq, const void* x, void* pre, void* post,
                    bool on_device, cudaStream_t s, Kv* kv = nullptr);
 

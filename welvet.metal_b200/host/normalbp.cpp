@@ -9,6 +9,9 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
 #include <vector>
 
 #include "../../include/welvet_c.h"
@@ -87,6 +90,39 @@ Status decode_to(DeviceCtx* d, int dtype, const float* src, float* dst, int64_t 
   return Status::ok();
 }
 
+// The device buffers of a call and the forward layer of its configuration, kept
+// per device and reused by later calls: buffers grow on demand and are never freed
+// (they live until the process exits); a later call of the same configuration
+// only loads its weights into the layer, so a repeated call of one shape allocates
+// nothing. The mutex serialises calls on one device.
+struct Workspace {
+  std::mutex mu;
+  std::unique_ptr<Mha> layer;  // the FP32 forward layer of the last call's configuration
+  welvet_b200_mha_config layer_cfg{};
+  DevBuf wqkv, wo, xb, preb, postb, gy, tgt, qkv, gattn, G, dxb, dwb, wab, part;
+  DevBuf ck, cv, qb, gyb, gq, gk, gv, scr;
+  Operand a1, b1, a2, b2;
+};
+
+bool same_config(const welvet_b200_mha_config& a, const welvet_b200_mha_config& b) {
+  return a.d_model == b.d_model && a.num_heads == b.num_heads && a.num_kv_heads == b.num_kv_heads &&
+         a.head_dim == b.head_dim && a.max_seq_len == b.max_seq_len && a.mask == b.mask && a.pos == b.pos &&
+         a.softmax == b.softmax && a.window == b.window && a.prefix_len == b.prefix_len &&
+         a.window_causal == b.window_causal && a.rope_theta == b.rope_theta &&
+         a.scale_override == b.scale_override && a.seq_mode == b.seq_mode && a.precision == b.precision &&
+         a.weight_format == b.weight_format && a.head_begin == b.head_begin && a.head_count == b.head_count &&
+         a.device == b.device;
+}
+
+Workspace* workspace(int device) {
+  static std::mutex mu;
+  static std::map<int, Workspace*> by_device;
+  std::lock_guard<std::mutex> lock(mu);
+  Workspace*& w = by_device[device];
+  if (!w) w = new Workspace();
+  return w;
+}
+
 }  // namespace
 
 Status mha_normalbp(const welvet_b200_mha_config& cin, int dtype, int B, int T, const float* Q, const float* K,
@@ -110,12 +146,16 @@ Status mha_normalbp(const welvet_b200_mha_config& cin, int dtype, int B, int T, 
   if (T > cfg.msl) return Status::err(1, "mha: seq > MaxSeqLen");
   DeviceCtx* d = nullptr;
   WV_TRY(device_ctx(cin.device, &d));
+  Workspace* ws = workspace(d->device);
+  std::lock_guard<std::mutex> lock(ws->mu);
   cudaStream_t s = 0;
   const int dm = cin.d_model, qd = cfg.qd, kd = cfg.kd, nqkv = qd + 2 * kd;
   const int64_t M = (int64_t)B * T, n = M * dm;
   const int64_t nq = (int64_t)qd * dm, nk = (int64_t)kd * dm;
   // decoded weights: Wqkv [nqkv, d] (Q, K, V rows) and Wo [d, qd]
-  DevBuf wqkv, wo, xb, preb, postb, gy, tgt, qkv, gattn, G, dxb, dwb, wab, part;
+  DevBuf &wqkv = ws->wqkv, &wo = ws->wo, &xb = ws->xb, &preb = ws->preb, &postb = ws->postb, &gy = ws->gy,
+         &tgt = ws->tgt, &qkv = ws->qkv, &gattn = ws->gattn, &G = ws->G, &dxb = ws->dxb, &dwb = ws->dwb,
+         &wab = ws->wab, &part = ws->part;
   WV_TRY(wqkv.ensure((size_t)nqkv * dm * 4));
   WV_TRY(wo.ensure((size_t)nq * 4));
   float* Wq = wqkv.as<float>();
@@ -130,12 +170,16 @@ Status mha_normalbp(const welvet_b200_mha_config& cin, int dtype, int B, int T, 
   WV_TRY(preb.ensure((size_t)M * qd * 4));
   WV_TRY(postb.ensure((size_t)n * 4));
   WV_CUDA(cudaMemcpyAsync(xb.p, x, (size_t)n * 4, cudaMemcpyHostToDevice, s), "x upload");
-  {
+  if (ws->layer && same_config(ws->layer_cfg, cin)) {
+    WV_TRY(mha_reload_fp32(ws->layer.get(), Wq, wo.as<float>(), s));
+  } else {
+    ws->layer.reset();
     Mha* m = nullptr;
     WV_TRY(mha_mount(cin, 1, Wq, Wk, Wv, wo.as<float>(), true, &m));
-    std::unique_ptr<Mha> hold(m);
-    WV_TRY(mha_forward(m, B, T, xb.p, preb.p, postb.p, true, s));
+    ws->layer.reset(m);
+    ws->layer_cfg = cin;
   }
+  WV_TRY(mha_forward(ws->layer.get(), B, T, xb.p, preb.p, postb.p, true, s));
   // dL/dpost
   WV_TRY(gy.ensure((size_t)n * 4));
   *loss = 0.0;
@@ -157,7 +201,7 @@ Status mha_normalbp(const welvet_b200_mha_config& cin, int dtype, int B, int T, 
   }
   const int64_t Mp = round4(M);
   const int dp = (int)round4(dm), qdp = (int)round4(qd), nqkvp = (int)round4(nqkv);
-  Operand a1, b1, a2, b2;
+  Operand &a1 = ws->a1, &b1 = ws->b1, &a2 = ws->a2, &b2 = ws->b2;
   // grad_attn [M, qd] = gy [M, d] . Wo [d, qd]
   WV_TRY(gattn.ensure((size_t)M * qd * 4));
   WV_TRY(op_rows(a1, gy.as<float>(), M, dm, s));
@@ -207,10 +251,12 @@ Status mha_normalbp(const welvet_b200_mha_config& cin, int dtype, int B, int T, 
     a.ld_qkv = nqkv;
     a.grad_attn = gattn.as<float>();
     a.kvmax = (int)M;
-    DevBuf ck, cv, qb, gq, gk, gv, scr;
+    DevBuf &ck = ws->ck, &cv = ws->cv, &qb = ws->qb, &gyb = ws->gyb, &gq = ws->gq, &gk = ws->gk, &gv = ws->gv,
+           &scr = ws->scr;
     WV_TRY(ck.ensure((size_t)a.msl * kd * 8));
     WV_TRY(cv.ensure((size_t)a.msl * kd * 8));
     WV_TRY(qb.ensure((size_t)T * qd * 8));
+    WV_TRY(gyb.ensure((size_t)T * qd * 8));
     WV_TRY(gq.ensure((size_t)T * qd * 8));
     WV_TRY(gk.ensure((size_t)a.msl * kd * 8));
     WV_TRY(gv.ensure((size_t)a.msl * kd * 8));
@@ -218,6 +264,7 @@ Status mha_normalbp(const welvet_b200_mha_config& cin, int dtype, int B, int T, 
     a.ck = ck.as<double>();
     a.cv = cv.as<double>();
     a.qb = qb.as<double>();
+    a.gyb = gyb.as<double>();
     a.gq = gq.as<double>();
     a.gk = gk.as<double>();
     a.gv = gv.as<double>();
@@ -229,8 +276,7 @@ Status mha_normalbp(const welvet_b200_mha_config& cin, int dtype, int B, int T, 
     prof_begin(kProfAttnBwd, s);
     WV_CUDA(attn_backward(a, s), "attention backward");
     prof_end(kProfAttnBwd, s);
-    count_launch(3 * B + 1);
-    WV_CUDA(cudaStreamSynchronize(s), "attention backward");
+    count_launch(7 * B + 1);
   }
   // dX [M, d] = G [M, nqkv] . Wqkv [nqkv, d]   (the three input gradients summed)
   WV_TRY(dxb.ensure((size_t)n * 4));

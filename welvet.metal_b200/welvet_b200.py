@@ -244,18 +244,23 @@ def mha_forward_f32(batch, seq, d_model, num_heads, num_kv_heads, head_dim, max_
 
 
 def mha_normalbp_f32(batch, seq, d_model, num_heads, num_kv_heads, head_dim, max_seq_len, mask, pos, dtype,
-                     Q, K, V, O, x, grad_or_target, use_target, lr, backend=0):
-    """welvet_mha_normalbp_f32 with numpy buffers: (pre, post, dX, dW, W_after, loss)."""
+                     Q, K, V, O, x, grad_or_target, use_target, lr, backend=0, out=None):
+    """welvet_mha_normalbp_f32 with numpy buffers: (pre, post, dX, dW, W_after, loss).
+    `out` = (pre, post, dX, dW, W_after) lets a caller reuse its output arrays
+    (contiguous float32 of M*q_dim, M*d_model, M*d_model, |W|, |W| elements)."""
     f = lambda a: np.ascontiguousarray(a, dtype=np.float32)  # noqa: E731
     Q, K, V, O, x, g = (f(a) for a in (Q, K, V, O, x, grad_or_target))
     M = batch * seq
     qd, kdim = Q.shape[0], K.shape[0]
-    pre = np.zeros(max(1, M * qd), np.float32)
-    post = np.zeros(max(1, M * d_model), np.float32)
-    dX = np.zeros(max(1, M * d_model), np.float32)
     nw = Q.size + K.size + V.size + O.size
-    dW = np.zeros(nw, np.float32)
-    Wa = np.zeros(nw, np.float32)
+    sizes = (max(1, M * qd), max(1, M * d_model), max(1, M * d_model), nw, nw)
+    if out is None:
+        pre, post, dX, dW, Wa = (np.zeros(n, np.float32) for n in sizes)
+    else:
+        pre, post, dX, dW, Wa = out
+        for a, n in zip(out, sizes):
+            if a.dtype != np.float32 or not a.flags.c_contiguous or a.size != n:
+                raise ValueError(f"mha_normalbp_f32: output buffers must be contiguous float32 of sizes {sizes}")
     loss = C.c_double(0.0)
     check(lib().welvet_mha_normalbp_f32(batch, seq, d_model, num_heads, num_kv_heads, head_dim, max_seq_len, mask,
                                         pos, dtype, backend, _ptr(Q), _ptr(K), _ptr(V), _ptr(O), _ptr(x), _ptr(g),
