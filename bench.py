@@ -40,6 +40,12 @@ import numpy as np
 # nominal dense FP64 of one B200 (HGX B200 datasheet: 296 TFLOP/s for 8 GPUs); the pool
 # measures no FP64 peak, so the NormalBP backward's fraction is quoted against this
 FP64_NOMINAL_TFLOPS = 37.0
+# DRAM bytes per unit measured by ncu (dram__bytes_read.sum + dram__bytes_write.sum) for
+# config 5's head shape (32 x 128, BF16) at B=2, T=4096: prefill attention per token,
+# decode attention per cached (sequence, position); scaled to the bench's launches
+TRAFFIC_PREFILL_PER_TOKEN = 247.8e6 / 8192
+TRAFFIC_DECODE_PER_ROW = 135.12e6 / (2 * 4097)
+TRAFFIC_SOURCE = "ncu dram__bytes_read.sum+dram__bytes_write.sum at B=2 T=4096, scaled by units"
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "welvet.metal_b200"))
@@ -957,9 +963,13 @@ def main():
             peak, pkind = 148 * 128 * 2 * 1.965e9 / 1e12, "nominal FP32 FFMA peak (CUDA cores)"
         else:
             peak, pkind = pk["bf16_sus"], f"{pk['src']} sustained bf16 (of {pk['src']})"
+        cfg5_heads = prec == 1 and hd == 128 and hc == 32 and kd_l == 4096
+        traffic = TRAFFIC_PREFILL_PER_TOKEN * M * args.steps / max(cnt, 1) \
+            if dom == "attn_prefill" and cfg5_heads else None
         roof = {"bound": "tensor" if peak == pk["bf16_sus"] else "fp32-fma", "kernel": dom, "achieved": achieved,
                 "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak, "peak_kind": pkind,
-                "traffic": None, "flops_per_launch": flops_launch, "avg_launch_ms": avg_ms,
+                "traffic": traffic, "traffic_source": TRAFFIC_SOURCE if traffic else None,
+                "flops_per_launch": flops_launch, "avg_launch_ms": avg_ms,
                 "launches_per_step": cnt / args.steps,
                 "kernel_ms_per_step": {k: prof[k][0] / args.steps for k in per_step},
                 "step_tflops": (pf + af) / world / (ms / 1e3) / 1e12}
@@ -1047,7 +1057,9 @@ def main():
         step_bytes = attn_bytes + wbytes
         droof = {"bound": "hbm", "kernel": "attn_decode", "achieved": gbs, "peak": pk["hbm"],
                  "unit": "GB/s", "frac": gbs / pk["hbm"], "peak_kind": f"{pk['src']} HBM copy (of {pk['src']})",
-                 "traffic": None, "bytes_per_launch": attn_bytes, "avg_launch_ms": a_ms,
+                 "traffic": (TRAFFIC_DECODE_PER_ROW * B * avg_ctx if es == 2 and hd == 128 and kd_l == 4096
+                             else None),
+                 "bytes_per_launch": attn_bytes, "avg_launch_ms": a_ms,
                  "step_bytes": step_bytes, "step_gbs": step_bytes / (dms / 1e3) / 1e9,
                  "kernel_ms_per_step": {k: dprof[k][0] / n_dec for k in
                                         ("gemm_qkv_decode", "attn_decode", "gemm_o_decode", "allreduce")}}
