@@ -45,6 +45,9 @@ def test_normalbp_matches_reference_golden(torch_cuda, name):
     (dict(d_model=256, num_heads=2, max_seq_len=96), 2, 80, 1, 0.01),
     # odd head_dim with RoPE: the last element of each head is not rotated
     (dict(d_model=42, num_heads=2), 2, 9, 1, 0.0),
+    # 300 queries (the key/value reduction split over query rows), 600 keys in batch 1
+    # (the q-gradient GEMM split over keys), the stream wrapping a 400-slot ring
+    (dict(d_model=128, num_heads=2, max_seq_len=400), 2, 300, 1, 0.01),
 ])
 def test_normalbp_against_oracle(torch_cuda, kw, B, T, use_target, lr):
     cfg = O.MhaCfg(**kw)

@@ -250,13 +250,17 @@ struct BwdArgs {
   double* gk = nullptr;             // [msl, kd] key-gradient ring (kept across batches)
   double* gv = nullptr;             // [msl, kd]
   double* scratch = nullptr;        // [T * nh, 2 * kvmax]
+  double* part_q = nullptr;         // [kMaxSplit, T, qd] q-gradient partials
+  double* part_kv = nullptr;        // [2 * kMaxSplit, msl, kd] value / key gradient partials
   int kvmax = 0;
   float* g_q = nullptr;             // outputs, rows of stride ld_g
   float* g_k = nullptr;
   float* g_v = nullptr;
   int ld_g = 0;
 };
+constexpr int kMaxSplit = 4;       // reduction splits of the attention backward
 cudaError_t attn_backward(const BwdArgs& a, cudaStream_t s);
+int attn_backward_launches(const BwdArgs& a);  // kernels attn_backward launches
 // src [rows, cols] -> [cols, rows_p] transposed, as TF32 hi/lo pairs, zero rows past `rows`
 cudaError_t transpose_split(const float* src, int64_t rows, int cols, int64_t rows_p, float* hi, float* lo,
                             cudaStream_t s);

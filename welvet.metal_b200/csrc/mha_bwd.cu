@@ -158,7 +158,7 @@ __device__ __forceinline__ double block_max(double v, double* red) {
   return t;
 }
 
-// FP64 tiled GEMM, one query head per blockIdx.z:
+// FP64 tiled GEMM, one (query head, k split) per blockIdx.z:
 //   C_h[m, n] = sum_k A_h[m, k] * B_h(k, n)
 // A_h[m, k] = a[h * a_hs + m * lda + k]; B's rows are ring slots taken modulo `mod`
 // (key positions past the ring wrap onto it): with B_NK, B_h(k, n) =
@@ -167,6 +167,8 @@ __device__ __forceinline__ double block_max(double v, double* red) {
 // outputs; operands outside M / N / K read as zero.
 struct DgemmArgs {
   int M = 0, N = 0, K = 0, mod = 1, group = 1;
+  int heads = 1, ksplit = 1;  // blockIdx.z = head + heads * split; split s sums k in its chunk
+  int64_t c_split = 0;        // output offset of split s: s * c_split
   const double* a = nullptr;
   int64_t lda = 0, a_hs = 0;
   const double* b = nullptr;
@@ -177,10 +179,12 @@ struct DgemmArgs {
 template <bool B_NK>
 __global__ void __launch_bounds__(256) dgemm_kernel(DgemmArgs g) {
   __shared__ double As[16][65], Bs[16][65];
-  const int h = blockIdx.z;
+  const int h = blockIdx.z % g.heads, split = blockIdx.z / g.heads;
   const double* A = g.a + (int64_t)h * g.a_hs;
   const double* B = g.b + (int64_t)(h / g.group) * g.b_hs;
-  double* C = g.c + (int64_t)h * g.c_hs;
+  double* C = g.c + (int64_t)h * g.c_hs + (int64_t)split * g.c_split;
+  const int kchunk = (g.K + g.ksplit * 16 - 1) / (g.ksplit * 16) * 16;
+  const int kbeg = split * kchunk, kend = min(g.K, kbeg + kchunk);
   const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
   double acc[4][4];
@@ -188,18 +192,18 @@ __global__ void __launch_bounds__(256) dgemm_kernel(DgemmArgs g) {
   for (int i = 0; i < 4; ++i)
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[i][j] = 0.0;
-  for (int k0 = 0; k0 < g.K; k0 += 16) {
+  for (int k0 = kbeg; k0 < kend; k0 += 16) {
 #pragma unroll
     for (int l = 0; l < 4; ++l) {
       const int idx = tid + 256 * l;
       const int r = idx >> 4, kk = idx & 15, m = m0 + r, k = k0 + kk;
-      As[kk][r] = (m < g.M && k < g.K) ? A[(int64_t)m * g.lda + k] : 0.0;
+      As[kk][r] = (m < g.M && k < kend) ? A[(int64_t)m * g.lda + k] : 0.0;
       if (B_NK) {
         const int n = n0 + r;
-        Bs[kk][r] = (n < g.N && k < g.K) ? B[(int64_t)(n % g.mod) * g.ldb + k] : 0.0;
+        Bs[kk][r] = (n < g.N && k < kend) ? B[(int64_t)(n % g.mod) * g.ldb + k] : 0.0;
       } else {
         const int kb = idx >> 6, n = n0 + (idx & 63), kr = k0 + kb;
-        Bs[kb][idx & 63] = (kr < g.K && n < g.N) ? B[(int64_t)(kr % g.mod) * g.ldb + n] : 0.0;
+        Bs[kb][idx & 63] = (kr < kend && n < g.N) ? B[(int64_t)(kr % g.mod) * g.ldb + n] : 0.0;
       }
     }
     __syncthreads();
@@ -307,19 +311,22 @@ __global__ void __launch_bounds__(256) kv_grad_kernel(BwdArgs a, int b) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int rows = G * a.T;  // row r: query t = r / G, head kh * G + r % G
   const size_t ldr = 2 * (size_t)a.kvmax;
+  // split blockIdx.z of gridDim.z takes rows [r_lo, r_hi) (whole 16-row chunks)
+  const int per = (rows + (int)gridDim.z * kKvRows - 1) / ((int)gridDim.z * kKvRows) * kKvRows;
+  const int r_lo = (int)blockIdx.z * per, r_hi = min(rows, r_lo + per);
   for (int z0 = 0; z0 < a.hd; z0 += kKvDims) {
     double av[8], ak[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) av[i] = ak[i] = 0.0;
     for (int k0 = s0; k0 < kvlen; k0 += a.msl) {
-      int r_begin = 0;
-      if (a.mask == 1) r_begin = max(0, k0 - base) * G / kKvRows * kKvRows;
-      for (int r0 = r_begin; r0 < rows; r0 += kKvRows) {
+      int r_begin = r_lo;
+      if (a.mask == 1) r_begin = max(r_lo, max(0, k0 - base) * G / kKvRows * kKvRows);
+      for (int r0 = r_begin; r0 < r_hi; r0 += kKvRows) {
         __syncthreads();
         for (int i = threadIdx.x; i < kKvRows * kKvSlots; i += blockDim.x) {
           const int rr = i / kKvSlots, j = i % kKvSlots, r = r0 + rr, k = k0 + j;
           double pv = 0.0, dv = 0.0;
-          if (r < rows && k < kvlen && s0 + j < a.msl) {
+          if (r < r_hi && k < kvlen && s0 + j < a.msl) {
             const int t = r / G, h = kh * G + r % G;
             const double* row = a.scratch + ((size_t)t * a.nh + h) * ldr;
             pv = row[k];
@@ -331,7 +338,7 @@ __global__ void __launch_bounds__(256) kv_grad_kernel(BwdArgs a, int b) {
         for (int i = threadIdx.x; i < kKvRows * kKvDims; i += blockDim.x) {
           const int rr = i / kKvDims, zz = i % kKvDims, r = r0 + rr, z = z0 + zz;
           double gv = 0.0, qv = 0.0;
-          if (r < rows && z < a.hd) {
+          if (r < r_hi && z < a.hd) {
             const int t = r / G, h = kh * G + r % G;
             gv = a.gyb[(size_t)t * a.qd + (size_t)h * a.hd + z];
             qv = a.qb[(size_t)t * a.qd + (size_t)h * a.hd + z];
@@ -353,16 +360,46 @@ __global__ void __launch_bounds__(256) kv_grad_kernel(BwdArgs a, int b) {
     }
     const int s = s0 + lane;
     if (s < a.msl && s < kvlen) {
-      double* gvr = a.gv + (size_t)s * a.kd + (size_t)kh * a.hd;
-      double* gkr = a.gk + (size_t)s * a.kd + (size_t)kh * a.hd;
+      // one split: add into the ring; several: this split's partial sums, which
+      // sum_parts_kernel adds into the ring in split order
+      const size_t ring = (size_t)a.msl * a.kd, off = (size_t)s * a.kd + (size_t)kh * a.hd;
+      double* gvr = gridDim.z == 1 ? a.gv + off : a.part_kv + (2 * (size_t)blockIdx.z) * ring + off;
+      double* gkr = gridDim.z == 1 ? a.gk + off : a.part_kv + (2 * (size_t)blockIdx.z + 1) * ring + off;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const int z = z0 + warp + 8 * i;
         if (z < a.hd) {
-          gvr[z] += av[i];
-          gkr[z] += ak[i];
+          if (gridDim.z == 1) {
+            gvr[z] += av[i];
+            gkr[z] += ak[i];
+          } else {
+            gvr[z] = av[i];
+            gkr[z] = ak[i];
+          }
         }
       }
+    }
+  }
+}
+
+// out[i] (+)= sum over p < nparts of part[p * stride + i], in order p = 0, 1, ...
+// (accumulate: add to out; else overwrite). With the key/value partials the parts
+// alternate v, k: out2 receives the odd parts.
+__global__ void sum_parts_kernel(const double* part, int nparts, int64_t stride, int64_t n, double* out,
+                                 double* out2, bool accumulate) {
+  GSTRIDE(i, n) {
+    if (out2) {
+      double v = 0.0, k = 0.0;
+      for (int p = 0; p < nparts; ++p) {
+        v += part[(2 * (int64_t)p) * stride + i];
+        k += part[(2 * (int64_t)p + 1) * stride + i];
+      }
+      out[i] += v;
+      out2[i] += k;
+    } else {
+      double v = 0.0;
+      for (int p = 0; p < nparts; ++p) v += part[(int64_t)p * stride + i];
+      out[i] = accumulate ? out[i] + v : v;
     }
   }
 }
@@ -445,6 +482,15 @@ cudaError_t transpose_split(const float* src, int64_t rows, int cols, int64_t ro
   return cudaGetLastError();
 }
 
+int attn_backward_launches(const BwdArgs& a) {
+  int n = 1;  // final_kv_kernel
+  for (int b = 0; b < a.B; ++b) {
+    const int kvlen = (b + 1) * a.T;
+    n += 7 + ((kvlen + 511) / 512 > 1 ? 1 : 0) + (a.nh / a.nk * a.T >= 256 ? 1 : 0);
+  }
+  return n;
+}
+
 cudaError_t attn_backward(const BwdArgs& a, cudaStream_t s) {
   if (a.T > 65535 || a.nh > 65535 || a.nk <= 0 || a.nh % a.nk) return cudaErrorInvalidValue;
   cudaError_t e = cudaMemsetAsync(a.gk, 0, (size_t)a.msl * a.kd * sizeof(double), s);
@@ -469,6 +515,7 @@ cudaError_t attn_backward(const BwdArgs& a, cudaStream_t s) {
     g.b_hs = a.hd;
     g.ldc = (int64_t)a.nh * ldr;
     g.c_hs = ldr;
+    g.heads = a.nh;
     const dim3 grid_s((kvlen + 63) / 64, (a.T + 63) / 64, a.nh);
     g.a = a.qb;
     g.b = a.ck;
@@ -479,7 +526,8 @@ cudaError_t attn_backward(const BwdArgs& a, cudaStream_t s) {
     g.c = a.scratch + a.kvmax;
     dgemm_kernel<true><<<grid_s, 256, 0, s>>>(g);
     attn_bwd_row_kernel<<<dim3(a.nh, a.T), 256, 0, s>>>(a, b);
-    // gq = delta k
+    // gq = delta k, the keys split into chunks of up to 512 (partials summed in order)
+    const int qsplit = std::min(kMaxSplit, (kvlen + 511) / 512);
     DgemmArgs q;
     q.M = a.T;
     q.N = a.hd;
@@ -492,12 +540,22 @@ cudaError_t attn_backward(const BwdArgs& a, cudaStream_t s) {
     q.b = a.ck;
     q.ldb = a.kd;
     q.b_hs = a.hd;
-    q.c = a.gq;
+    q.c = qsplit > 1 ? a.part_q : a.gq;
     q.ldc = a.qd;
     q.c_hs = a.hd;
-    dgemm_kernel<false><<<dim3((a.hd + 63) / 64, (a.T + 63) / 64, a.nh), 256, 0, s>>>(q);
+    q.heads = a.nh;
+    q.ksplit = qsplit;
+    q.c_split = (int64_t)a.T * a.qd;
+    dgemm_kernel<false><<<dim3((a.hd + 63) / 64, (a.T + 63) / 64, a.nh * qsplit), 256, 0, s>>>(q);
+    if (qsplit > 1)
+      sum_parts_kernel<<<grid_n((int64_t)a.T * a.qd), 256, 0, s>>>(a.part_q, qsplit, (int64_t)a.T * a.qd,
+                                                                  (int64_t)a.T * a.qd, a.gq, nullptr, false);
     const int nslot = std::min(a.msl, kvlen);
-    kv_grad_kernel<<<dim3((nslot + kKvSlots - 1) / kKvSlots, a.nk), 256, 0, s>>>(a, b);
+    const int kvsplit = a.nh / a.nk * a.T >= 256 ? kMaxSplit : 1;
+    kv_grad_kernel<<<dim3((nslot + kKvSlots - 1) / kKvSlots, a.nk, kvsplit), 256, 0, s>>>(a, b);
+    if (kvsplit > 1)
+      sum_parts_kernel<<<grid_n((int64_t)nslot * a.kd), 256, 0, s>>>(a.part_kv, kvsplit, (int64_t)a.msl * a.kd,
+                                                                    (int64_t)nslot * a.kd, a.gv, a.gk, true);
     batch_end_kernel<<<grid_n((int64_t)(a.T * a.nh + a.msl * a.nk) * P), 256, 0, s>>>(a, b);
   }
   final_kv_kernel<<<grid_n(a.M * a.kd), 256, 0, s>>>(a);

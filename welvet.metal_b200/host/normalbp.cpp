@@ -100,7 +100,7 @@ struct Workspace {
   std::unique_ptr<Mha> layer;  // the FP32 forward layer of the last call's configuration
   welvet_b200_mha_config layer_cfg{};
   DevBuf wqkv, wo, xb, preb, postb, gy, tgt, qkv, gattn, G, dxb, dwb, wab, part;
-  DevBuf ck, cv, qb, gyb, gq, gk, gv, scr;
+  DevBuf ck, cv, qb, gyb, gq, gk, gv, scr, pq, pkv;
   Operand a1, b1, a2, b2;
 };
 
@@ -252,11 +252,13 @@ Status mha_normalbp(const welvet_b200_mha_config& cin, int dtype, int B, int T, 
     a.grad_attn = gattn.as<float>();
     a.kvmax = (int)M;
     DevBuf &ck = ws->ck, &cv = ws->cv, &qb = ws->qb, &gyb = ws->gyb, &gq = ws->gq, &gk = ws->gk, &gv = ws->gv,
-           &scr = ws->scr;
+           &scr = ws->scr, &pq = ws->pq, &pkv = ws->pkv;
     WV_TRY(ck.ensure((size_t)a.msl * kd * 8));
     WV_TRY(cv.ensure((size_t)a.msl * kd * 8));
     WV_TRY(qb.ensure((size_t)T * qd * 8));
     WV_TRY(gyb.ensure((size_t)T * qd * 8));
+    WV_TRY(pq.ensure((size_t)kMaxSplit * T * qd * 8));
+    WV_TRY(pkv.ensure((size_t)2 * kMaxSplit * a.msl * kd * 8));
     WV_TRY(gq.ensure((size_t)T * qd * 8));
     WV_TRY(gk.ensure((size_t)a.msl * kd * 8));
     WV_TRY(gv.ensure((size_t)a.msl * kd * 8));
@@ -265,6 +267,8 @@ Status mha_normalbp(const welvet_b200_mha_config& cin, int dtype, int B, int T, 
     a.cv = cv.as<double>();
     a.qb = qb.as<double>();
     a.gyb = gyb.as<double>();
+    a.part_q = pq.as<double>();
+    a.part_kv = pkv.as<double>();
     a.gq = gq.as<double>();
     a.gk = gk.as<double>();
     a.gv = gv.as<double>();
@@ -276,7 +280,7 @@ Status mha_normalbp(const welvet_b200_mha_config& cin, int dtype, int B, int T, 
     prof_begin(kProfAttnBwd, s);
     WV_CUDA(attn_backward(a, s), "attention backward");
     prof_end(kProfAttnBwd, s);
-    count_launch(7 * B + 1);
+    count_launch(attn_backward_launches(a));
   }
   // dX [M, d] = G [M, nqkv] . Wqkv [nqkv, d]   (the three input gradients summed)
   WV_TRY(dxb.ensure((size_t)n * 4));
