@@ -975,22 +975,35 @@ def main():
                 "step_tflops": (pf + af) / world / (ms / 1e3) / 1e12}
 
         if not args.no_e2e:
-            xh = x.cpu().pin_memory()
-            ph = torch.empty(M, d, dtype=act).pin_memory()
-            layer.forward(B, T, xh, None, ph)  # warm the staging buffers
+            # With N ranks each holds its B/N sequences in host memory and receives the
+            # summed output of those rows (welvet_b200_mha_forward_rows: all-gather in,
+            # reduce-scatter out over NVLink); one rank uses the host-buffer forward.
+            rows_io = world > 1 and B % world == 0
+            bl = B // world if rows_io else B
+            xh = x[rank * bl * T:(rank + 1) * bl * T].cpu().pin_memory() if rows_io else x.cpu().pin_memory()
+            ph = torch.empty(bl * T, d, dtype=act).pin_memory()
+
+            def e2e_step():  # H2D x, forward, D2H post, synchronise
+                if rows_io:
+                    layer.forward_rows(bl, T, xh, ph)
+                else:
+                    layer.forward(B, T, xh, None, ph)
+            e2e_step()  # warm the staging buffers
             barrier()
             t0 = time.perf_counter()
             ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             ea.record(stream)
             n_e2e = max(1, min(args.steps, 3))
             for _ in range(n_e2e):
-                layer.forward(B, T, xh, None, ph)  # H2D x, forward, D2H post, synchronise
+                e2e_step()
             eb.record(stream)
             barrier()
             e_ms = max_over_ranks(max(ea.elapsed_time(eb), (time.perf_counter() - t0) * 1e3) / n_e2e)
             e2e = {"value": M / (e_ms / 1e3), "unit": "tok/s", "ms_per_step": e_ms,
                    "h2d_bytes_per_step": M * d * es, "d2h_bytes_per_step": M * d * es,
-                   "api": "welvet_b200_mha_forward (host buffers, pinned)"}
+                   "bytes_scope": "whole job (each rank copies its B/N sequences)" if rows_io else "one GPU",
+                   "api": ("welvet_b200_mha_forward_rows (host buffers, pinned, row-sharded)" if rows_io
+                           else "welvet_b200_mha_forward (host buffers, pinned)")}
             del xh, ph
         del post
         torch.cuda.empty_cache()

@@ -63,6 +63,19 @@ WELVET_API welvet_status welvet_b200_mha_forward(welvet_b200_mha* layer, int32_t
                                                  int32_t seq, const void* x, void* pre, void* post,
                                                  int32_t on_device, void* stream);
 
+/* Forward with row-sharded host buffers (no reference counterpart: the reference
+ * is single-device). For a head-sharded layer with a communicator of N ranks in
+ * per-sequence mode: every rank passes its own batch_local sequences (rank r holds
+ * sequences [r * batch_local, (r + 1) * batch_local) of the whole batch of
+ * N * batch_local), x [batch_local*seq, d_model] in and post [batch_local*seq,
+ * d_model] out, host memory (pinned for full speed), synchronous. post receives the
+ * sum over ranks of those rows, as welvet_b200_mha_forward would give for them. The
+ * layer all-gathers the input rows and reduce-scatters the output rows over NVLink,
+ * so each GPU moves 1/N of x and post over PCIe. Without a communicator (or with
+ * one rank) it is the host-buffer forward of batch_local sequences. */
+WELVET_API welvet_status welvet_b200_mha_forward_rows(welvet_b200_mha* layer, int32_t batch_local,
+                                                      int32_t seq, const void* x, void* post);
+
 /* Reads and clears the device error word of the layer's device after a
  * synchronisation; code 4 with the kernel's reason when a device-side bounded wait
  * expired or a bound check failed. No reference counterpart. */

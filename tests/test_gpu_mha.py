@@ -276,3 +276,23 @@ def test_decode_variants_against_oracle(torch_cuda, H, NK, pos, softmax):
                                      *Ws, x.float().cpu().numpy())
     assert rel_err(pre.float().cpu().numpy(), rpre) < LOW_TOL
     assert rel_err(post.float().cpu().numpy(), rpost) < LOW_TOL
+
+
+@pytest.mark.parametrize("precision", [0, 1])
+def test_forward_rows_one_rank_equals_host_forward(torch_cuda, precision):
+    """welvet_b200_mha_forward_rows with a communicator of one rank is the host-buffer
+    forward of the caller's sequences: same chunks, same kernels, equal bit for bit."""
+    torch = torch_cuda
+    d, H, NK, B, T = 256, 4, 2, 6, 96
+    Ws = W.xavier_weights(d, d, NK * d // H, seed=0)
+    dt = torch.float32 if precision == 0 else torch.bfloat16
+    x = torch.from_numpy(W.synthetic(B * T * d, 1, 1, 1.0).reshape(B * T, d)).to(dt).pin_memory()
+    cfg = W.MhaConfig.make(d, H, NK, precision=precision)
+    plain = W.MhaLayer(cfg, *Ws)
+    rows = W.MhaLayer(cfg, *Ws)
+    rows.attach_comm(W.comm_unique_id(), 1, 0)
+    want = torch.zeros(B * T, d, dtype=dt).pin_memory()
+    got = torch.zeros(B * T, d, dtype=dt).pin_memory()
+    plain.forward(B, T, x, None, want)
+    rows.forward_rows(B, T, x, got)
+    assert torch.equal(want, got)

@@ -1,0 +1,66 @@
+"""Two ranks on two GPUs (skipped with fewer): head-sharded layers with an NCCL
+communicator, the row-sharded host-buffer forward (welvet_b200_mha_forward_rows)
+against one unsharded layer on the whole batch. Each rank passes only its half of
+the sequences and receives the summed output rows of that half."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, out_dir, precision):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import welvet_b200 as W
+    torch.cuda.set_device(rank)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    d, H, NK, B, T = 512, 8, 4, 8, 128
+    dt = torch.float32 if precision == 0 else torch.bfloat16
+    Ws = W.xavier_weights(d, d, NK * d // H, seed=0)
+    x = torch.from_numpy(W.synthetic(B * T * d, 1, 1, 1.0).reshape(B * T, d)).to(dt)
+    hb, hc = W.head_shard(H, NK, world, rank)
+    layer = W.MhaLayer(W.MhaConfig.make(d, H, NK, precision=precision, head_begin=hb, head_count=hc), *Ws)
+    uid = [W.comm_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(uid, src=0)
+    layer.attach_comm(uid[0], world, rank)
+    bl = B // world
+    xl = x[rank * bl * T:(rank + 1) * bl * T].contiguous().pin_memory()
+    post = torch.zeros(bl * T, d, dtype=dt).pin_memory()
+    for _ in range(2):  # the second call reuses the staging buffers and events
+        layer.forward_rows(bl, T, xl, post)
+    np.save(os.path.join(out_dir, f"rows{rank}.npy"), post.float().numpy())
+    if rank == 0:
+        full = W.MhaLayer(W.MhaConfig.make(d, H, NK, precision=precision), *Ws)
+        ref = torch.zeros(B * T, d, dtype=dt).pin_memory()
+        full.forward(B, T, x.pin_memory(), None, ref)
+        np.save(os.path.join(out_dir, "full.npy"), ref.float().numpy())
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("precision", [0, 1])
+def test_forward_rows_two_ranks(tmp_path, precision):
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    mp.start_processes(_worker, args=(2, _free_port(), str(tmp_path), precision), nprocs=2, join=True,
+                       start_method="spawn")
+    full = np.load(tmp_path / "full.npy")
+    got = np.concatenate([np.load(tmp_path / f"rows{r}.npy") for r in range(2)])
+    tol = 1e-5 if precision == 0 else 2e-2  # the two head shards' partial sums add in another order
+    err = np.abs(got - full).max() / np.abs(full).max()
+    assert err < tol, err

@@ -1,5 +1,6 @@
 // extern "C" entry points: the welvet_c.h MHA subset (drop-in for the
 // reference's src/interop/c_abi.cpp MHA entries) and the welvet_b200.h extension.
+#include <climits>
 #include <cstdio>
 #include <cstring>
 #include <memory>
@@ -153,6 +154,17 @@ welvet_status welvet_b200_mha_forward(welvet_b200_mha* layer, int32_t batch, int
                                       void* pre, void* post, int32_t on_device, void* stream) {
   if (!layer) return wv::to_c(Status::err(1, "mha: nil layer"));
   return wv::to_c(wv::mha_forward(layer->m, batch, seq, x, pre, post, on_device != 0, as_stream(stream)));
+}
+
+welvet_status welvet_b200_mha_forward_rows(welvet_b200_mha* layer, int32_t batch_local, int32_t seq, const void* x,
+                                           void* post) {
+  if (!layer) return wv::to_c(Status::err(1, "mha: nil layer"));
+  wv::Mha* m = layer->m;
+  const bool sharded = m->comm && m->nranks > 1;
+  if (batch_local <= 0 || (sharded && (int64_t)batch_local * m->nranks > INT32_MAX))
+    return wv::to_c(Status::err(1, "mha: invalid argument"));
+  const int batch = sharded ? batch_local * m->nranks : batch_local;
+  return wv::to_c(wv::mha_forward(m, batch, seq, x, nullptr, post, false, nullptr, nullptr, sharded));
 }
 
 welvet_status welvet_b200_mha_check(welvet_b200_mha* layer) {

@@ -1,5 +1,7 @@
 // NCCL communicator of a head-sharded layer: one all-reduce (sum) of the
-// row-sharded output projection per forward / decode step, over NVLink.
+// row-sharded output projection per forward / decode step, over NVLink; with
+// row-sharded host I/O an all-gather of the input rows and a reduce-scatter of the
+// output rows instead.
 // The reference is single-device and has no counterpart.
 //
 // libnccl is opened with dlopen when a communicator is first needed, not linked:
@@ -20,6 +22,8 @@ struct NcclApi {
   decltype(&ncclGetUniqueId) get_unique_id = nullptr;
   decltype(&ncclCommInitRank) comm_init_rank = nullptr;
   decltype(&ncclAllReduce) all_reduce = nullptr;
+  decltype(&ncclAllGather) all_gather = nullptr;
+  decltype(&ncclReduceScatter) reduce_scatter = nullptr;
   decltype(&ncclCommDestroy) comm_destroy = nullptr;
   decltype(&ncclGetErrorString) error_string = nullptr;
   bool ok = false;
@@ -39,9 +43,12 @@ const NcclApi& nccl() {
     api.get_unique_id = reinterpret_cast<decltype(api.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
     api.comm_init_rank = reinterpret_cast<decltype(api.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
     api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(dlsym(h, "ncclAllReduce"));
+    api.all_gather = reinterpret_cast<decltype(api.all_gather)>(dlsym(h, "ncclAllGather"));
+    api.reduce_scatter = reinterpret_cast<decltype(api.reduce_scatter)>(dlsym(h, "ncclReduceScatter"));
     api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
     api.error_string = reinterpret_cast<decltype(api.error_string)>(dlsym(h, "ncclGetErrorString"));
-    api.ok = api.get_unique_id && api.comm_init_rank && api.all_reduce && api.comm_destroy && api.error_string;
+    api.ok = api.get_unique_id && api.comm_init_rank && api.all_reduce && api.all_gather && api.reduce_scatter &&
+             api.comm_destroy && api.error_string;
     if (!api.ok) api.why = "libnccl.so.2 lacks an entry point";
   });
   return api;
@@ -88,6 +95,25 @@ Status comm_allreduce(Mha* m, void* buf, size_t count, bool bf16, cudaStream_t s
   ncclResult_t r = nccl().all_reduce(buf, buf, count, bf16 ? ncclBfloat16 : ncclFloat32, ncclSum,
                                      static_cast<ncclComm_t>(m->comm), s);
   if (r != ncclSuccess) return nccl_status(r, "ncclAllReduce");
+  return Status::ok();
+}
+
+// In place over buf [nranks * count]: rank r's part starts at r * count elements.
+Status comm_allgather(Mha* m, void* buf, size_t count, bool bf16, cudaStream_t s) {
+  if (!m->comm || m->nranks == 1) return Status::ok();
+  const size_t es = bf16 ? 2 : 4;
+  ncclResult_t r = nccl().all_gather(static_cast<char*>(buf) + (size_t)m->rank * count * es, buf, count,
+                                     bf16 ? ncclBfloat16 : ncclFloat32, static_cast<ncclComm_t>(m->comm), s);
+  if (r != ncclSuccess) return nccl_status(r, "ncclAllGather");
+  return Status::ok();
+}
+Status comm_reducescatter(Mha* m, void* buf, size_t count, bool bf16, cudaStream_t s) {
+  if (!m->comm || m->nranks == 1) return Status::ok();
+  const size_t es = bf16 ? 2 : 4;
+  ncclResult_t r = nccl().reduce_scatter(buf, static_cast<char*>(buf) + (size_t)m->rank * count * es, count,
+                                         bf16 ? ncclBfloat16 : ncclFloat32, ncclSum,
+                                         static_cast<ncclComm_t>(m->comm), s);
+  if (r != ncclSuccess) return nccl_status(r, "ncclReduceScatter");
   return Status::ok();
 }
 

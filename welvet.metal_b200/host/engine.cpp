@@ -217,6 +217,8 @@ Mha::~Mha() {
   comm_release(this);
   for (auto& e : io_ev)
     if (e) cudaEventDestroy(e);
+  for (auto& e : gather_ev)
+    if (e) cudaEventDestroy(e);
   if (io_in) cudaStreamDestroy(io_in);
   if (io_out) cudaStreamDestroy(io_out);
 }
@@ -391,6 +393,7 @@ Status ensure_io_streams(Mha* m) {
   WV_CUDA(cudaStreamCreateWithFlags(&m->io_in, cudaStreamNonBlocking), "io stream");
   WV_CUDA(cudaStreamCreateWithFlags(&m->io_out, cudaStreamNonBlocking), "io stream");
   for (auto& e : m->io_ev) WV_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "io event");
+  for (auto& e : m->gather_ev) WV_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "io event");
   for (auto& e : m->chunk_done)  // shared with the communicator path
     if (!e) WV_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "chunk event");
   return Status::ok();
@@ -541,11 +544,18 @@ Status mha_reload_fp32(Mha* m, const float* wqkv, const float* wo, cudaStream_t 
 }
 
 Status mha_forward(Mha* m, int batch, int seq, const void* x, void* pre, void* post, bool on_device,
-                   cudaStream_t s, Kv* kv) {
+                   cudaStream_t s, Kv* kv, bool rows) {
   if (!m || !x || !post || batch <= 0 || seq <= 0) return Status::err(1, "mha: invalid argument");
   std::lock_guard<std::mutex> lock(m->mu);
   const auto& c = m->cfg;
   const bool stream_mode = c.c.seq_mode == 0;
+  // Row-sharded host I/O: rank r's sequences are [r * batch / N, (r + 1) * batch / N).
+  const bool rows_io = rows && m->comm && m->nranks > 1;
+  if (rows_io) {
+    if (on_device || stream_mode || kv || pre)
+      return Status::err(2, "mha: row-sharded I/O needs host buffers, per-sequence mode and no pre");
+    if (batch % m->nranks) return Status::err(1, "mha: batch not divisible by the ranks");
+  }
   if (stream_mode && seq > c.msl) return Status::err(1, "mha: seq > MaxSeqLen");  // mha.cpp:159-161
   WV_CUDA(cudaSetDevice(m->dev->device), "cudaSetDevice");
   const int64_t M = (int64_t)batch * seq;
@@ -567,7 +577,12 @@ Status mha_forward(Mha* m, int batch, int seq, const void* x, void* pre, void* p
   const bool chunked = (m->comm || !on_device) && !stream_mode && !kv && batch > 1;
   // Host copies (about 40 ms per 2 GB each way on PCIe) want more, smaller chunks
   // than the all-reduce does.
-  const int chunks = chunked ? std::min(batch, on_device ? 4 : Mha::kMaxChunks) : 1;
+  int chunks = chunked ? std::min(batch, on_device ? 4 : Mha::kMaxChunks) : 1;
+  // rows_io: chunk i takes bcl sequences of every rank (rank-major), bcl of this rank
+  const int nr = rows_io ? m->nranks : 1, b_local = batch / nr;
+  const int bcl = rows_io ? (b_local + std::min(b_local, Mha::kMaxChunks) - 1) / std::min(b_local, Mha::kMaxChunks)
+                          : 0;
+  if (rows_io) chunks = (b_local + bcl - 1) / bcl;
   if (!on_device) {
     WV_TRY(m->x_io.ensure(M * dm * es));
     WV_TRY(m->post_io.ensure(M * dm * es));
@@ -581,7 +596,7 @@ Status mha_forward(Mha* m, int batch, int seq, const void* x, void* pre, void* p
       pred = m->pre_io.p;
     }
   }
-  const int bc_max = (batch + chunks - 1) / chunks;
+  const int bc_max = rows_io ? bcl * nr : (batch + chunks - 1) / chunks;
   const int64_t Mc_max = (int64_t)bc_max * seq;
   WV_TRY(m->qkv.ensure(Mc_max * m->nqkv * es));
   if (!pred) WV_TRY(m->attn.ensure(Mc_max * m->qd_l * es));
@@ -692,9 +707,44 @@ Status mha_forward(Mha* m, int batch, int seq, const void* x, void* pre, void* p
       WV_CUDA(cudaStreamWaitEvent(m->io_in, m->chunk_done[0], 0), "wait");
       WV_CUDA(cudaStreamWaitEvent(m->io_out, m->chunk_done[0], 0), "wait");
     }
+    // rows_io: this rank's rows of chunk i go up and are all-gathered (comm_stream)
+    // one chunk ahead of the compute, so that the gather of chunk i + 1 runs
+    // during chunk i and precedes chunk i's reduce-scatter on comm_stream.
+    auto gather_chunk = [&](int i) -> Status {
+      const int b0 = i * bc_max, bc = std::min(bc_max, batch - b0);
+      const int64_t r0 = (int64_t)b0 * seq, own = (int64_t)(bc / nr) * seq;
+      WV_CUDA(cudaMemcpyAsync(static_cast<char*>(m->x_io.p) + (r0 + m->rank * own) * dm * es,
+                              static_cast<const char*>(x) + (int64_t)i * bcl * seq * dm * es, own * dm * es,
+                              cudaMemcpyHostToDevice, m->io_in), "H2D x rows");
+      WV_CUDA(cudaEventRecord(m->io_ev[i], m->io_in), "event");
+      WV_CUDA(cudaStreamWaitEvent(m->comm_stream, m->io_ev[i], 0), "wait");
+      WV_TRY(comm_allgather(m, static_cast<char*>(m->x_io.p) + r0 * dm * es, (size_t)own * dm, !f32,
+                            m->comm_stream));
+      WV_CUDA(cudaEventRecord(m->gather_ev[i], m->comm_stream), "event");
+      return Status::ok();
+    };
+    if (rows_io) WV_TRY(gather_chunk(0));
     for (int i = 0, b0 = 0; i < chunks && b0 < batch; ++i, b0 += bc_max) {
       const int bc = std::min(bc_max, batch - b0);
       const int64_t r0 = (int64_t)b0 * seq, rows = (int64_t)bc * seq;
+      if (rows_io) {
+        const int64_t own = rows / nr;
+        WV_CUDA(cudaStreamWaitEvent(s, m->gather_ev[i], 0), "wait");
+        WV_TRY(run_rows(b0, bc));
+        WV_CUDA(cudaEventRecord(m->chunk_done[i], s), "event");
+        if (i + 1 < chunks) WV_TRY(gather_chunk(i + 1));
+        WV_CUDA(cudaStreamWaitEvent(m->comm_stream, m->chunk_done[i], 0), "wait");
+        prof_begin(kProfAllReduce, m->comm_stream);
+        WV_TRY(comm_reducescatter(m, static_cast<char*>(postd) + r0 * dm * es, (size_t)own * dm, !f32,
+                                  m->comm_stream));
+        prof_end(kProfAllReduce, m->comm_stream);
+        WV_CUDA(cudaEventRecord(m->io_ev[Mha::kMaxChunks + i], m->comm_stream), "event");
+        WV_CUDA(cudaStreamWaitEvent(m->io_out, m->io_ev[Mha::kMaxChunks + i], 0), "wait");
+        WV_CUDA(cudaMemcpyAsync(static_cast<char*>(post) + (int64_t)i * bcl * seq * dm * es,
+                                static_cast<char*>(postd) + (r0 + m->rank * own) * dm * es, own * dm * es,
+                                cudaMemcpyDeviceToHost, m->io_out), "D2H post rows");
+        continue;
+      }
       if (host) {
         WV_CUDA(cudaMemcpyAsync(static_cast<char*>(m->x_io.p) + r0 * dm * es, static_cast<const char*>(x) + r0 * dm * es,
                                 rows * dm * es, cudaMemcpyHostToDevice, m->io_in), "H2D x");

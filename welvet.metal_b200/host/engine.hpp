@@ -149,6 +149,7 @@ struct Mha {
   // host-buffer calls: input copies (io_in) and output copies (io_out) of the chunks
   cudaStream_t io_in = nullptr, io_out = nullptr;
   cudaEvent_t io_ev[2 * kMaxChunks + 1] = {};
+  cudaEvent_t gather_ev[kMaxChunks] = {};  // row-sharded host I/O: chunk all-gathered
   std::mutex mu;  // one call at a time per layer (reference: per-session lock)
   ~Mha();
 };
@@ -159,7 +160,11 @@ Status mha_mount(const welvet_b200_mha_config& cfg, int dtype, const float* Q, c
 // (W_qkv rows Q | K | V, Wo), without allocating.
 Status mha_reload_fp32(Mha* m, const float* wqkv, const float* wo, cudaStream_t s);
 Status mha_forward(Mha* m, int batch, int seq, const void* x, void* pre, void* post,
-                   bool on_device, cudaStream_t s, Kv* kv = nullptr);
+                   bool on_device, cudaStream_t s, Kv* kv = nullptr, bool rows = false);
+// rows = true (host buffers, communicator of N ranks, per-sequence mode, no pre):
+// batch is the whole batch, x / post hold this rank's batch / N sequences
+// (ranks in order); the input rows are all-gathered and the output rows
+// reduce-scattered over NVLink, so each GPU copies 1/N of them over PCIe.
 
 struct Kv {
   Mha* layer = nullptr;
@@ -177,6 +182,9 @@ Status mha_decode(Mha* m, Kv* kv, int batch, const void* x, void* pre, void* pos
 Status comm_unique_id(uint8_t id[128]);
 Status comm_attach(Mha* m, const uint8_t id[128], int nranks, int rank);
 Status comm_allreduce(Mha* m, void* buf, size_t count, bool bf16, cudaStream_t s);
+// in place over buf [nranks * count]; rank r's part at r * count elements
+Status comm_allgather(Mha* m, void* buf, size_t count, bool bf16, cudaStream_t s);
+Status comm_reducescatter(Mha* m, void* buf, size_t count, bool bf16, cudaStream_t s);
 void comm_release(Mha* m);
 
 // small device helpers (engine_kernels.cu)

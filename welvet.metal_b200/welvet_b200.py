@@ -26,7 +26,8 @@ C_ABI_SYMBOLS = ("welvet_version", "welvet_runtime_identity", "welvet_metal_init
                  "welvet_swiglu_forward_f32",
                  "welvet_rmsnorm_forward_f32", "welvet_layernorm_forward_f32", "welvet_embedding_forward_f32")
 EXT_SYMBOLS = ("welvet_b200_mha_config_default", "welvet_b200_mha_mount", "welvet_b200_mha_release",
-               "welvet_b200_mha_forward", "welvet_b200_mha_check", "welvet_b200_kv_create",
+               "welvet_b200_mha_forward", "welvet_b200_mha_forward_rows", "welvet_b200_mha_check",
+               "welvet_b200_kv_create",
                "welvet_b200_kv_release", "welvet_b200_kv_fill", "welvet_b200_mha_prefill",
                "welvet_b200_mha_decode", "welvet_b200_comm_unique_id", "welvet_b200_comm_attach",
                "welvet_b200_gemm", "welvet_b200_split_tf32", "welvet_b200_attention",
@@ -126,6 +127,7 @@ def lib():
     L.welvet_b200_mha_release.argtypes = [_vp]
     L.welvet_b200_mha_release.restype = None
     L.welvet_b200_mha_forward.argtypes = [_vp, C.c_int32, C.c_int32, _vp, _vp, _vp, C.c_int32, _vp]
+    L.welvet_b200_mha_forward_rows.argtypes = [_vp, C.c_int32, C.c_int32, _vp, _vp]
     L.welvet_b200_mha_check.argtypes = [_vp]
     L.welvet_b200_kv_create.argtypes = [_vp, C.c_int32, C.c_int32, C.POINTER(_vp)]
     L.welvet_b200_kv_release.argtypes = [_vp]
@@ -155,7 +157,8 @@ def lib():
     L.welvet_b200_profile_read.restype = None
     L.welvet_b200_decode_attention_static.argtypes = [cfgp, C.c_int32, C.c_int32, _vp, C.c_int32, _vp, _vp, _vp,
                                                       C.c_int32, _vp, _vp, C.c_int32, _vp]
-    for name in ("welvet_b200_mha_mount", "welvet_b200_mha_forward", "welvet_b200_mha_check",
+    for name in ("welvet_b200_mha_mount", "welvet_b200_mha_forward", "welvet_b200_mha_forward_rows",
+                 "welvet_b200_mha_check",
                  "welvet_b200_kv_create", "welvet_b200_kv_fill", "welvet_b200_mha_prefill",
                  "welvet_b200_mha_decode", "welvet_b200_comm_unique_id", "welvet_b200_comm_attach",
                  "welvet_b200_gemm", "welvet_b200_split_tf32", "welvet_b200_attention",
@@ -398,6 +401,11 @@ class MhaLayer:
     def forward(self, batch, seq, x, pre, post, stream=None):
         check(lib().welvet_b200_mha_forward(self._h, batch, seq, _ptr(x), _ptr(pre), _ptr(post),
                                             _on_device(x, pre, post), _stream(stream)))
+
+    def forward_rows(self, batch_local, seq, x, post):
+        """Row-sharded host I/O: this rank's batch_local sequences of x in, the same
+        sequences of post (summed over ranks) out; host tensors / arrays."""
+        check(lib().welvet_b200_mha_forward_rows(self._h, batch_local, seq, _ptr(x), _ptr(post)))
 
     def check_device(self):
         check(lib().welvet_b200_mha_check(self._h))
