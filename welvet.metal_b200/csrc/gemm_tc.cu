@@ -253,7 +253,6 @@ __global__ void __launch_bounds__(GT<KIND>::THREADS, 1)
   uint64_t* acce = accf + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(acce + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
-  float* nf4s = reinterpret_cast<float*>(tmem_holder + 4);  // NF4: 16 levels
 
   const int warp = (int)warp_id(), lane = (int)lane_id();
   if (threadIdx.x == 0) {
@@ -268,9 +267,6 @@ __global__ void __launch_bounds__(GT<KIND>::THREADS, 1)
     }
     *abort_flag = 0;
     fence_barrier_init();
-  }
-  if constexpr (KIND == kGemmNF4) {
-    if (threadIdx.x < 16) nf4s[threadIdx.x] = nf4_level(threadIdx.x);
   }
   if (warp == 1) {
     tmem_alloc(tmem_holder, TMEM_COLS);
@@ -386,6 +382,18 @@ __global__ void __launch_bounds__(GT<KIND>::THREADS, 1)
     const int xt = threadIdx.x - 192;
     const int ch = xt & 7, r0 = xt >> 3;
     constexpr int RPT = BN / 16;  // rows per thread
+    // NF4: the 16 levels as BF16, held in registers as two byte planes (low and
+    // high bytes, four levels per register), so a level lookup is a byte permute
+    // instead of a shared-memory load.
+    uint32_t lvl_lo[4] = {0, 0, 0, 0}, lvl_hi[4] = {0, 0, 0, 0};
+    if constexpr (KIND == kGemmNF4) {
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        const uint32_t h = pack_bf16x2(nf4_level(c), 0.f) & 0xffffu;
+        lvl_lo[c >> 2] |= (h & 0xffu) << (8 * (c & 3));
+        lvl_hi[c >> 2] |= (h >> 8) << (8 * (c & 3));
+      }
+    }
     int stage = 0;
     uint32_t phase = 0;
     for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
@@ -417,8 +425,8 @@ __global__ void __launch_bounds__(GT<KIND>::THREADS, 1)
           cw[j] = *reinterpret_cast<const CodeT*>(codes + (r0 + 16 * j) * (KIND == kGemmFP8 ? 64 : 32) +
                                                   ch * (KIND == kGemmFP8 ? 8 : 4));
         // Converted chunks are held in registers and stored after the last
-        // conversion, so the NF4 level lookups (shared memory) never wait behind
-        // a store either.
+        // conversion: both conversions are register-only (no shared-memory loads),
+        // so the stores leave as one burst.
         uint32_t w[RPT][4];
 #pragma unroll
         for (int j = 0; j < RPT; ++j) {  // fully unrolled: cw[], amax[], w[] stay in registers
@@ -439,24 +447,37 @@ __global__ void __launch_bounds__(GT<KIND>::THREADS, 1)
               w[j][e] = pack_bf16x2(lo, hi);
             }
           } else {
-            const float am = amax[j];
+            // Nibble k of the code word is element k (low nibble first). Each
+            // nibble's low three bits select a byte from a register pair (levels
+            // 0-7 or 8-15; __byte_perm reads three bits per selector nibble), and
+            // bit 3 picks the pair through a byte mask (byte 0 or 1 of 0xff00).
+            // The two planes are then interleaved into BF16 pairs and scaled by
+            // the block absmax with one BF16x2 multiply: bf16(bf16(level) *
+            // bf16(absmax)).
+            const __nv_bfloat162 am2 = __float2bfloat162_rn(amax[j]);
+            const uint32_t sel = cw[j] & 0x77777777u;
+            const uint32_t msel = (cw[j] >> 3) & 0x11111111u;
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const uint32_t byte = (cw[j] >> (8 * e)) & 0xff;
-              w[j][e] = pack_bf16x2(nf4s[byte & 0xf] * am, nf4s[byte >> 4] * am);
+            for (int h = 0; h < 2; ++h) {
+              const uint32_t s4 = sel >> (16 * h), m4 = msel >> (16 * h);
+              const uint32_t hi8 = __byte_perm(0x0000ff00u, 0u, m4);
+              const uint32_t lo = (__byte_perm(lvl_lo[0], lvl_lo[1], s4) & ~hi8) |
+                                  (__byte_perm(lvl_lo[2], lvl_lo[3], s4) & hi8);
+              const uint32_t hi = (__byte_perm(lvl_hi[0], lvl_hi[1], s4) & ~hi8) |
+                                  (__byte_perm(lvl_hi[2], lvl_hi[3], s4) & hi8);
+#pragma unroll
+              for (int q = 0; q < 2; ++q) {
+                uint32_t v = __byte_perm(lo, hi, q ? 0x7362u : 0x5140u);
+                __nv_bfloat162 r = __hmul2(*reinterpret_cast<__nv_bfloat162*>(&v), am2);
+                w[j][2 * h + q] = *reinterpret_cast<uint32_t*>(&r);
+              }
             }
-            // NF4 stores each row as soon as it is converted: holding all rows
-            // bunches the 128 level lookups into one burst (measured slower).
-            *reinterpret_cast<uint4*>(btile + sw128_offset(r0 + 16 * j, ch)) =
-                make_uint4(w[j][0], w[j][1], w[j][2], w[j][3]);
           }
         }
-        if constexpr (KIND == kGemmFP8) {
 #pragma unroll
-          for (int j = 0; j < RPT; ++j)
-            *reinterpret_cast<uint4*>(btile + sw128_offset(r0 + 16 * j, ch)) =
-                make_uint4(w[j][0], w[j][1], w[j][2], w[j][3]);
-        }
+        for (int j = 0; j < RPT; ++j)
+          *reinterpret_cast<uint4*>(btile + sw128_offset(r0 + 16 * j, ch)) =
+              make_uint4(w[j][0], w[j][1], w[j][2], w[j][3]);
         fence_proxy_async_smem();
         mbar_arrive(&xfull[stage]);
         if (++stage == S) {
