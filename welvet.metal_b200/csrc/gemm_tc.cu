@@ -5,7 +5,7 @@
 //   warp 0      TMA producer (one elected thread) filling a ring of smem stages
 //   warp 1      UMMA issuer (one thread); owns the TMEM allocation
 //   warps 2-5   epilogue: TMEM -> registers -> (RoPE) -> global, one row per thread
-//   warps 6-9   (FP8/NF4 only) dequantise B codes into a BF16 smem tile per stage
+//   warps 6-13  (FP8/NF4 only) dequantise B codes into a BF16 smem tile per stage
 // Accumulators are double-buffered in TMEM so the epilogue of tile i overlaps the
 // mainloop of tile i+1. Tiles: 128 x BN, K-blocks of 128 bytes per operand row
 // (128-byte swizzle, the canonical K-major UMMA layout).
@@ -38,18 +38,18 @@ template <> struct GT<kGemmTF32x3> {
   static constexpr int THREADS = 192;
 };
 // FP8 / NF4 weights: TMA brings the codes (BN x 64 codes) into a staging buffer,
-// warps 6-9 write the BF16 tile that UMMA reads.
+// warps 6-13 write the BF16 tile that UMMA reads.
 template <> struct GT<kGemmFP8> {
   static constexpr int BN = 256, BK = 64, STAGES = 3, UK = 16, NA = 1, NB = 1, ELEM = 2;
   static constexpr uint32_t FMT = 1;
   static constexpr int CODE_BYTES = 256 * 64;  // one byte per code
-  static constexpr int THREADS = 320;
+  static constexpr int THREADS = 448;
 };
 template <> struct GT<kGemmNF4> {
   static constexpr int BN = 256, BK = 64, STAGES = 3, UK = 16, NA = 1, NB = 1, ELEM = 2;
   static constexpr uint32_t FMT = 1;
   static constexpr int CODE_BYTES = 256 * 32;  // two codes per byte
-  static constexpr int THREADS = 320;
+  static constexpr int THREADS = 448;
 };
 
 struct KParams {
@@ -259,7 +259,7 @@ __global__ void __launch_bounds__(GT<KIND>::THREADS, 1)
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
-      mbar_init(&xfull[s], 128);
+      mbar_init(&xfull[s], T::THREADS - 192);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&accf[a], 1);
@@ -377,11 +377,14 @@ __global__ void __launch_bounds__(GT<KIND>::THREADS, 1)
     }
   } else if constexpr (XFORM) {
     // --------------------------------------------- B dequantisation (FP8/NF4)
-    // 128 threads; thread xt writes 16-byte (8 x bf16) chunk ch = xt % 8 of rows
-    // xt / 8 + 16 j (j < BN / 16) of the swizzled tile.
+    // XT = 256 threads; thread xt writes 16-byte (8 x bf16) chunk ch = xt % 8 of
+    // rows xt / 8 + RS j (j < BN / RS, RS = XT / 8) of the swizzled tile. Each
+    // warp's conversions are dependent chains per row, so more warps (not more
+    // rows per warp) keep the conversion pipes busy.
+    constexpr int XT = T::THREADS - 192, RS = XT / 8;
     const int xt = threadIdx.x - 192;
     const int ch = xt & 7, r0 = xt >> 3;
-    constexpr int RPT = BN / 16;  // rows per thread
+    constexpr int RPT = BN / RS;  // rows per thread
     // NF4: the 16 levels as BF16, held in registers as two byte planes (low and
     // high bytes, four levels per register), so a level lookup is a byte permute
     // instead of a shared-memory load.
@@ -406,7 +409,7 @@ __global__ void __launch_bounds__(GT<KIND>::THREADS, 1)
         if constexpr (KIND == kGemmNF4) {
 #pragma unroll
           for (int j = 0; j < RPT; ++j) {
-            const int n = nb * BN + r0 + 16 * j;
+            const int n = nb * BN + r0 + RS * j;
             amax[j] = n < p.N ? __ldg(p.b_scale + (size_t)n * (p.K / 64) + kb) : 0.f;
           }
         }
@@ -422,7 +425,7 @@ __global__ void __launch_bounds__(GT<KIND>::THREADS, 1)
         CodeT cw[RPT];
 #pragma unroll
         for (int j = 0; j < RPT; ++j)
-          cw[j] = *reinterpret_cast<const CodeT*>(codes + (r0 + 16 * j) * (KIND == kGemmFP8 ? 64 : 32) +
+          cw[j] = *reinterpret_cast<const CodeT*>(codes + (r0 + RS * j) * (KIND == kGemmFP8 ? 64 : 32) +
                                                   ch * (KIND == kGemmFP8 ? 8 : 4));
         // Converted chunks are held in registers and stored after the last
         // conversion: both conversions are register-only (no shared-memory loads),
@@ -476,7 +479,7 @@ __global__ void __launch_bounds__(GT<KIND>::THREADS, 1)
         }
 #pragma unroll
         for (int j = 0; j < RPT; ++j)
-          *reinterpret_cast<uint4*>(btile + sw128_offset(r0 + 16 * j, ch)) =
+          *reinterpret_cast<uint4*>(btile + sw128_offset(r0 + RS * j, ch)) =
               make_uint4(w[j][0], w[j][1], w[j][2], w[j][3]);
         fence_proxy_async_smem();
         mbar_arrive(&xfull[stage]);
