@@ -49,6 +49,7 @@ def test_gemm_bf16_output_bf16(torch_cuda):
 @pytest.mark.parametrize("M,N,K", [(128, 128, 32), (333, 384, 1024), (2048, 1024, 1024)])
 def test_gemm_tf32x3_is_fp32_accurate(torch_cuda, M, N, K):
     torch = torch_cuda
+    torch.manual_seed(M * 7919 + N * 31 + K)  # inputs independent of the tests run before
     a = torch.randn(M, K, device="cuda", dtype=torch.float32)
     b = torch.randn(N, K, device="cuda", dtype=torch.float32)
     ah, al, bh, bl = (torch.empty_like(t) for t in (a, a, b, b))
@@ -63,8 +64,10 @@ def test_gemm_tf32x3_is_fp32_accurate(torch_cuda, M, N, K):
     ref = a.double() @ b.double().T
     # The FP32 path's budget is 1e-4. 3xTF32 drops only lo*lo (2^-22 relative), but the
     # tensor-core accumulator does not round each addition to nearest: measured
-    # ~8e-6 at K=1024 on B200, growing ~linearly with K.
-    assert rel_err(out.cpu().numpy(), ref.cpu().numpy()) < 1e-5 * max(1.0, K / 1024)
+    # 8e-6 to 1.02e-5 at K=1024 on B200 over different random draws, growing
+    # ~linearly with K. The bound keeps a 2x margin and stays 5x inside the 1e-4
+    # budget of the FP32 path.
+    assert rel_err(out.cpu().numpy(), ref.cpu().numpy()) < 2e-5 * max(1.0, K / 1024)
 
 
 def test_gemm_fp8_rowscale_weights(torch_cuda):

@@ -5,7 +5,7 @@
 //   warp 0      TMA producer (one elected thread) filling a ring of smem stages
 //   warp 1      UMMA issuer (one thread); owns the TMEM allocation
 //   warps 2-5   epilogue: TMEM -> registers -> (RoPE) -> global, one row per thread
-//   warps 6-13  (FP8/NF4 only) dequantise B codes into a BF16 smem tile per stage
+//   warps 6..   (FP8: 8 warps, NF4: 16) dequantise B codes into a BF16 smem tile per stage
 // Accumulators are double-buffered in TMEM so the epilogue of tile i overlaps the
 // mainloop of tile i+1. Tiles: 128 x BN, K-blocks of 128 bytes per operand row
 // (128-byte swizzle, the canonical K-major UMMA layout).
@@ -38,18 +38,18 @@ template <> struct GT<kGemmTF32x3> {
   static constexpr int THREADS = 192;
 };
 // FP8 / NF4 weights: TMA brings the codes (BN x 64 codes) into a staging buffer,
-// warps 6-13 write the BF16 tile that UMMA reads.
+// warps 6.. (8 for FP8, 16 for NF4) write the BF16 tile that UMMA reads.
 template <> struct GT<kGemmFP8> {
   static constexpr int BN = 256, BK = 64, STAGES = 3, UK = 16, NA = 1, NB = 1, ELEM = 2;
   static constexpr uint32_t FMT = 1;
   static constexpr int CODE_BYTES = 256 * 64;  // one byte per code
-  static constexpr int THREADS = 448;
+  static constexpr int THREADS = 448;  // 8 dequantisation warps
 };
 template <> struct GT<kGemmNF4> {
   static constexpr int BN = 256, BK = 64, STAGES = 3, UK = 16, NA = 1, NB = 1, ELEM = 2;
   static constexpr uint32_t FMT = 1;
   static constexpr int CODE_BYTES = 256 * 32;  // two codes per byte
-  static constexpr int THREADS = 448;
+  static constexpr int THREADS = 704;  // 16 dequantisation warps (NF4 conversion is longer)
 };
 
 struct KParams {
@@ -377,7 +377,7 @@ __global__ void __launch_bounds__(GT<KIND>::THREADS, 1)
     }
   } else if constexpr (XFORM) {
     // --------------------------------------------- B dequantisation (FP8/NF4)
-    // XT = 256 threads; thread xt writes 16-byte (8 x bf16) chunk ch = xt % 8 of
+    // XT threads; thread xt writes 16-byte (8 x bf16) chunk ch = xt % 8 of
     // rows xt / 8 + RS j (j < BN / RS, RS = XT / 8) of the swizzled tile. Each
     // warp's conversions are dependent chains per row, so more warps (not more
     // rows per warp) keep the conversion pipes busy.
