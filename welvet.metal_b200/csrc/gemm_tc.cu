@@ -452,22 +452,21 @@ __global__ void __launch_bounds__(GT<KIND>::THREADS, 1)
           } else {
             // Nibble k of the code word is element k (low nibble first). Each
             // nibble's low three bits select a byte from a register pair (levels
-            // 0-7 or 8-15; __byte_perm reads three bits per selector nibble), and
-            // bit 3 picks the pair through a byte mask (byte 0 or 1 of 0xff00).
-            // The two planes are then interleaved into BF16 pairs and scaled by
-            // the block absmax with one BF16x2 multiply: bf16(bf16(level) *
-            // bf16(absmax)).
+            // 0-7 or 8-15; __byte_perm reads three bits per selector nibble and
+            // the low 16 bits of the selector). A second permute picks, per byte,
+            // the pair that bit 3 names (selector nibble j + 4 * bit3). The two
+            // planes are then interleaved into BF16 pairs and scaled by the block
+            // absmax with one BF16x2 multiply: bf16(bf16(level) * bf16(absmax)).
             const __nv_bfloat162 am2 = __float2bfloat162_rn(amax[j]);
-            const uint32_t sel = cw[j] & 0x77777777u;
-            const uint32_t msel = (cw[j] >> 3) & 0x11111111u;
+            const uint32_t code = cw[j];
+            const uint32_t pick = ((code >> 1) & 0x44444444u) | 0x32103210u;
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-              const uint32_t s4 = sel >> (16 * h), m4 = msel >> (16 * h);
-              const uint32_t hi8 = __byte_perm(0x0000ff00u, 0u, m4);
-              const uint32_t lo = (__byte_perm(lvl_lo[0], lvl_lo[1], s4) & ~hi8) |
-                                  (__byte_perm(lvl_lo[2], lvl_lo[3], s4) & hi8);
-              const uint32_t hi = (__byte_perm(lvl_hi[0], lvl_hi[1], s4) & ~hi8) |
-                                  (__byte_perm(lvl_hi[2], lvl_hi[3], s4) & hi8);
+              const uint32_t s4 = code >> (16 * h), p4 = pick >> (16 * h);
+              const uint32_t lo = __byte_perm(__byte_perm(lvl_lo[0], lvl_lo[1], s4),
+                                              __byte_perm(lvl_lo[2], lvl_lo[3], s4), p4);
+              const uint32_t hi = __byte_perm(__byte_perm(lvl_hi[0], lvl_hi[1], s4),
+                                              __byte_perm(lvl_hi[2], lvl_hi[3], s4), p4);
 #pragma unroll
               for (int q = 0; q < 2; ++q) {
                 uint32_t v = __byte_perm(lo, hi, q ? 0x7362u : 0x5140u);
