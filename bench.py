@@ -1,18 +1,23 @@
 #!/usr/bin/env python
-"""Benchmark of the B200 MHA forward path — BASELINE metric "MHA prefill tok/s +
-decode tok/s at 1/2/4/8 B200; % of roofline".
+"""Benchmark of the B200 MHA forward path — metric "MHA prefill tok/s + decode tok/s
+at 1/2/4/8 B200; % of roofline".
 
-Default workload = BASELINE config 5 (the metric's 1/2/4/8-GPU configuration):
-batch 32 x seq 8192, d_model 4096, 32 heads x 128, causal, RoPE, BF16 activations
-and weights, FP32 accumulation. Heads are sharded 32/N per GPU, the output
-projection is row-sharded and summed with NCCL all-reduce. A step = one prefill
-forward over all 262144 tokens; value = whole-job prefill tok/s. After the timed
-prefill, 256 autoregressive decode steps run against the resulting KV cache and are
-reported under "decode".
+Default workload (cfg5, the metric's 1/2/4/8-GPU configuration): batch 32 x seq
+8192, d_model 4096, 32 heads x 128, causal, RoPE, BF16 activations and weights,
+FP32 accumulation. Heads are sharded 32/N per GPU, the output projection is
+row-sharded and summed with NCCL all-reduce. A step = one prefill forward over all
+262144 tokens; value = whole-job prefill tok/s. After the timed prefill, 256
+autoregressive decode steps run against the resulting KV cache and are reported
+under "decode". The line's "parity" compares rows of the timed forward's output
+with the FP64 oracle (oracle/, test infrastructure: the checker, never the thing
+measured).
 
-Other workloads (`--workload`): cfg2 (FP32 prefill, 3xTF32 projections), cfg3
-(decode only: 64 sequences over a 4096-token KV cache, GQA 32/8 x 64; a step = one
-decode step), cfg4-fp8 / cfg4-nf4 (quantised-weight prefill).
+On one GPU the default line also carries "configs": the other configurations of
+the metric, each with its own roofline and parity — cfg2 (FP32 prefill B=8
+T=2048 d=1024 16x64), cfg3 (decode of 64 sequences over a 4096-token KV cache,
+GQA 32/8 x 64), cfg4-fp8 / cfg4-nf4 (prefill B=4 T=4096 d=4096 32x128 with FP8
+row-scale / NF4 block-64 weights) — and "dequant" (FP8 / NF4 -> BF16 GB/s).
+Each is also selectable on its own with --workload.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
   torchrun --nproc-per-node N bench.py --gpus N ...      (N > 1)
@@ -20,8 +25,8 @@ decode step), cfg4-fp8 / cfg4-nf4 (quantised-weight prefill).
 Data is synthetic (no dataset is named by the baseline): the counter-based
 SplitMix64 stream of welvet_b200_fill_synthetic — Xavier-uniform weights (seed 0,
 order Wq, Wk, Wv, Wo; N(0, 0.02) for the quantised configs), N(0,1) inputs (seed 1),
-KV cache N(0,1)*0.5 (seed 2). Inputs (config 5 x: 2.1 GB; config 3 KV cache:
-1.1 GB) exceed L2 (126 MB), so no explicit flush is needed between steps.
+KV cache N(0,1)*0.5 (seed 2). Inputs (cfg5 x: 2.1 GB; cfg3 KV cache: 1.1 GB) exceed
+L2 (126 MB), so no explicit flush is needed between steps.
 """
 from __future__ import annotations
 
@@ -41,7 +46,7 @@ import numpy as np
 # measures no FP64 peak, so the NormalBP backward's fraction is quoted against this
 FP64_NOMINAL_TFLOPS = 37.0
 # DRAM bytes per unit measured by ncu (dram__bytes_read.sum + dram__bytes_write.sum) for
-# config 5's head shape (32 x 128, BF16) at B=2, T=4096: prefill attention per token,
+# the cfg5 head shape (32 x 128, BF16) at B=2, T=4096: prefill attention per token,
 # decode attention per cached (sequence, position); scaled to the bench's launches
 TRAFFIC_PREFILL_PER_TOKEN = 247.8e6 / 8192
 TRAFFIC_DECODE_PER_ROW = 135.12e6 / (2 * 4097)
@@ -77,32 +82,40 @@ BLOCK_KINDS = ("swiglu", "rmsnorm", "layernorm", "embedding")
 CODEC_DTYPES = range(34)
 CODEC_STATS_FREE = (0, 1, 2, 3, 4, 5, 16, 24, 25)  # dtypes without a per-tensor statistics pass
 
-METRIC = "MHA prefill tok/s (BASELINE config 5; decode tok/s under 'decode')"
-METRIC_DECODE = "MHA decode tok/s (BASELINE config 3)"
+METRIC = "MHA prefill tok/s (decode tok/s under 'decode'); % of roofline"
+METRIC_DECODE = "MHA decode tok/s; % of HBM roofline"
+SUB_WORKLOADS = ("cfg2", "cfg3", "cfg4-fp8", "cfg4-nf4")
+DEQUANT_WEIGHTS = 1 << 30  # per format: 1 GiB of FP8 codes, 0.5 GiB of NF4 codes, 2 GiB of BF16 out
+# FP32 prefill attention runs on the CUDA cores (attn_f32_kernel): its roofline is the FFMA peak
+FP32_ATTENTION_ON_TENSOR_CORES = False
 METRIC_CODEC = "FormatNone weight round trip GB/s (decode(encode(w)), dtypes 0-33)"
 METRIC_NBP = "MHA NormalBP tok/s (forward + backward + SGD)"
 METRIC_BLOCK = {"swiglu": "SwiGLU forward tok/s", "rmsnorm": "RMSNorm forward tok/s",
                 "layernorm": "LayerNorm forward tok/s", "embedding": "Embedding forward tok/s"}
 
 
-def workload(args):
-    w = dict(WORKLOADS[args.workload])
+def workload_of(wname, args):
+    """Shape of workload `wname`; --batch / --seq override the selected workload only."""
+    w = dict(WORKLOADS[wname])
+    own = wname == args.workload
     if w["kind"] == "codec":
-        w["n"] = args.batch or w["n"]
+        w["n"] = (args.batch if own else 0) or w["n"]
         return w
+    w["B"] = (args.batch if own else 0) or w["B"]
+    w["T"] = (args.seq if own else 0) or w["T"]
     if w["kind"] in BLOCK_KINDS or w["kind"] == "nbp":
-        w["B"] = args.batch or w["B"]
-        w["T"] = args.seq or w["T"]
         return w
-    w["B"] = args.batch or w["B"]
-    w["T"] = args.seq or w["T"]
     w["hd"] = w["d"] // w["H"]
     return w
 
 
-def workload_config(args, world):
-    """The `config` object of the JSON line, the same for both arms."""
-    w = workload(args)
+def workload(args):
+    return workload_of(args.workload, args)
+
+
+def workload_config_of(wname, args, world):
+    """The `config` object of a JSON line, the same for both arms."""
+    w = workload_of(wname, args)
     if w["kind"] == "codec":
         return {"workload": f"codec: decode(encode(w)) of {w['n']} FP32 weights, FormatNone dtypes 0-33",
                 "global_batch": w["n"], "seq_len": 1, "parallelism": f"replicas x{world}",
@@ -117,19 +130,24 @@ def workload_config(args, world):
         desc = {"swiglu": f"SwiGLU d={d} inter={w.get('inter')} BF16",
                 "rmsnorm": f"RMSNorm dim={d} FP32", "layernorm": f"LayerNorm dim={d} FP32",
                 "embedding": f"Embedding vocab={w.get('vocab')} emb={d} FP32 table, Linear"}[w["kind"]]
-        return {"workload": f"{args.workload}: {desc}, B={B} T={T}", "global_batch": B, "seq_len": T,
+        return {"workload": f"{wname}: {desc}, B={B} T={T}", "global_batch": B, "seq_len": T,
                 "parallelism": f"replicas x{world}", "l2": "activations larger than L2 (x is %.2f GB)"
                 % (B * T * d * (2 if w["kind"] == "swiglu" else 4) / 1e9)}
     B, T, d, H, NK, hd, wf = w["B"], w["T"], w["d"], w["H"], w["NK"], w["hd"], w["wf"]
     fmt = " fp8 weights" if wf == 1 else " nf4 weights" if wf == 2 else ""
     es = 2 if w["prec"] == 1 else 4
+    prec = " BF16" if w["prec"] == 1 else " FP32"
     if w["kind"] == "decode":
-        return {"workload": f"{args.workload}: decode B={B} context {T} d={d} H={H}x{hd} NK={NK} RoPE{fmt}",
+        return {"workload": f"{wname}: decode B={B} context {T} d={d} H={H}x{hd} NK={NK} RoPE{prec}{fmt}",
                 "global_batch": B, "seq_len": 1, "context": T, "parallelism": f"tp{world} (heads {H // world}/GPU)",
                 "l2": "KV cache larger than L2 (%.1f GB)" % (2 * B * T * NK * hd * es / 1e9)}
-    return {"workload": f"{args.workload}: B={B} T={T} d={d} H={H}x{hd} NK={NK} causal RoPE{fmt}",
+    return {"workload": f"{wname}: B={B} T={T} d={d} H={H}x{hd} NK={NK} causal RoPE{prec}{fmt}",
             "global_batch": B, "seq_len": T, "parallelism": f"tp{world} (heads {H // world}/GPU)",
             "l2": "inputs larger than L2 (x is %.1f GB)" % (B * T * d * es / 1e9)}
+
+
+def workload_config(args, world):
+    return workload_config_of(args.workload, args, world)
 
 
 def peaks():
@@ -201,22 +219,6 @@ def flops_prefill(B, T, d, H, NK, hd):
     return proj, attn
 
 
-def cpu_sample(w, T_s, threads=0):
-    """Times the FP64 oracle (multithreaded C++) on one sequence of T_s tokens of the
-    workload's layer shape; returns (seconds, flops)."""
-    import oracle_py as O
-    import welvet_b200 as W
-    d, H, NK, hd = w["d"], w["H"], w["NK"], w["hd"]
-    Ws = W.xavier_weights(d, H * hd, NK * hd, seed=0)
-    x = W.synthetic(T_s * d, 1, 1, 1.0).reshape(T_s, d)
-    cfg = O.MhaCfg(d_model=d, num_heads=H, num_kv_heads=NK, max_seq_len=T_s, per_sequence=1)
-    t0 = time.perf_counter()
-    O.mha_forward(cfg, 1, T_s, *Ws, x, threads=threads)
-    dt = time.perf_counter() - t0
-    pf, af = flops_prefill(1, T_s, d, H, NK, hd)
-    return dt, pf + af
-
-
 def cpu_sample_decode(w, B_s, threads=0):
     """Times the FP64 oracle's decode step for B_s sequences over the workload's
     context; returns seconds."""
@@ -262,10 +264,9 @@ def codec_cpu_sample(n_s, use_ref):
 def run_reference(args):
     """Reference arm: the reference's own MHA code (mha.cpp + dense.cpp + soft-double
     shaders, oracle/_ref) on the host cores through its one-shot entry
-    (welvet_mha_forward_f32 semantics: encode + mount + forward per call), each step a
-    bounded sample (1 sequence x T_r tokens of the workload's layer shape), scaled to the
-    workload's tok/s by algorithmic FLOPs per token. Falls back to the FP64 port when
-    oracle/_ref was not built."""
+    (welvet_mha_forward_f32 semantics: encode + mount + forward per call). Falls back
+    to the FP64 port when oracle/_ref was not built. Prefill workloads: see
+    reference_prefill_sample for how each step's samples become the workload's tok/s."""
     import oracle_py as O
     import welvet_b200 as W
     w = workload(args)
@@ -300,38 +301,81 @@ def run_reference(args):
                           "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0,
                                   "d2h_bytes_per_step": 0}}), flush=True)
         return
-    B, T, d, H, NK, hd = w["B"], w["T"], w["d"], w["H"], w["NK"], w["hd"]
-    pf, af = flops_prefill(B, T, d, H, NK, hd)
-    flops_per_tok = (pf + af) / (B * T)
-    Ws = W.xavier_weights(d, H * hd, NK * hd, seed=0)
-    kind = "reference" if O.ref_available() else "port"
-    T_r = args.ref_tokens
-    x = W.synthetic(T_r * d, 1, 1, 1.0).reshape(T_r, d)
-    cfg = O.MhaCfg(d_model=d, num_heads=H, num_kv_heads=NK, max_seq_len=max(512, T_r))
+    return run_reference_prefill(args, w)
 
-    def step():
+
+def reference_prefill_sample(O, W, w, kind):
+    """One step of the prefill reference arm: four bounded calls of the reference's
+    one-shot forward (stream semantics, one sequence), timed separately:
+      A1, A16: the workload's layer (d, H x hd) on 1 and 16 tokens. Their difference is
+               15 tokens of projections (soft-double matvec, spread over all host
+               threads by the CPU executor) -> seconds per token p; A1 - p is the
+               per-call mount (encode + decode of the four weight matrices) c.
+      B256, B512: a one-head layer with the workload's head_dim (d = hd) on 256 and
+               512 tokens: time = a T + b T^2, so b = (B512 - 2 B256) / (512^2 - 2 256^2)
+               and one (query, key) pair of one head costs r = 2 b seconds (the
+               reference's attention runs on one thread, shaders/ops_mha.metal:32-33).
+    The workload's time is modelled as c + M p + r H B T (T + 1) / 2: the mount once,
+    projections per token, attention per causal pair and head."""
+    d, H, NK, hd = w["d"], w["H"], w["NK"], w["hd"]
+    Ws = W.xavier_weights(d, H * hd, NK * hd, seed=0)
+    W1 = W.xavier_weights(hd, hd, hd, seed=0)
+
+    def call(cfg, T, Wt, dd):
+        x = W.synthetic(T * dd, 1, 1, 1.0).reshape(T, dd)
+        t0 = time.perf_counter()
         if kind == "reference":
-            code, msg, _, _ = O.ref_mha_forward(cfg, 1, T_r, *Ws, x, 1)
+            code, msg, _, _ = O.ref_mha_forward(cfg, 1, T, *Wt, x, 1)
             if code:
                 raise RuntimeError(msg)
         else:
-            O.mha_forward(cfg, 1, T_r, *Ws, x)
+            O.mha_forward(cfg, 1, T, *Wt, x)
+        return time.perf_counter() - t0
 
+    big = O.MhaCfg(d_model=d, num_heads=H, num_kv_heads=NK, max_seq_len=512)
+    one = O.MhaCfg(d_model=hd, num_heads=1, num_kv_heads=1, max_seq_len=512)
+    tA1 = call(big, 1, Ws, d)
+    tA16 = call(big, 16, Ws, d)
+    tB256 = call(one, 256, W1, hd)
+    tB512 = call(one, 512, W1, hd)
+    p = max((tA16 - tA1) / 15.0, 1e-9)
+    c = max(tA1 - p, 0.0)
+    b = (tB512 - 2.0 * tB256) / (512.0 ** 2 - 2.0 * 256.0 ** 2)
+    if b <= 0:  # timing noise: bound the pair cost by the whole 512-token call
+        b = tB512 / 512.0 ** 2
+    return {"mount_s": c, "proj_s_per_token": p, "attn_s_per_pair_head": 2.0 * b,
+            "sample_s": tA1 + tA16 + tB256 + tB512}
+
+
+def run_reference_prefill(args, w):
+    import oracle_py as O
+    import welvet_b200 as W
+    B, T, d, H, NK, hd = w["B"], w["T"], w["d"], w["H"], w["NK"], w["hd"]
+    M = B * T
+    kind = "reference" if O.ref_available() else "port"
+    small = dict(w, d=hd, H=1, NK=1)
     for _ in range(args.warmup):
-        step()
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        step()
-    dt = (time.perf_counter() - t0) / args.steps
-    pf_s, af_s = flops_prefill(1, T_r, d, H, NK, hd)
-    value = (pf_s + af_s) / dt / flops_per_tok
+        reference_prefill_sample(O, W, small, kind)
+    samples = [reference_prefill_sample(O, W, w, kind) for _ in range(args.steps)]
+    med = {k: statistics.median(s_[k] for s_ in samples) for k in samples[0]}
+    pairs = H * B * T * (T + 1) / 2.0
+    est_s = med["mount_s"] + M * med["proj_s_per_token"] + pairs * med["attn_s_per_pair_head"]
+    value = M / est_s
+    step_s = sum(s_["sample_s"] for s_ in samples) / len(samples)
     cores = os.cpu_count()
-    sample = (f"1 sequence x {T_r} tokens of the {args.workload} layer (d={d}, {H}x{hd}) per step, FP32 "
-              f"reference semantics; tok/s scaled by algorithmic FLOPs/token of the full workload")
+    sample = (f"per step: the reference's one-shot forward on 1 and 16 tokens of the {args.workload} layer "
+              f"(d={d}, {H}x{hd}) and on 256 and 512 tokens of a one-head layer with head_dim {hd}; the workload "
+              f"time is modelled as mount + M x projection s/token + H B T(T+1)/2 x attention s/pair (medians "
+              f"over the steps): mount {med['mount_s']:.2f} s, {med['proj_s_per_token'] * 1e3:.1f} ms/token, "
+              f"{med['attn_s_per_pair_head'] * 1e6:.2f} us/pair/head -> {est_s / 3600:.1f} h per step "
+              f"(attention {pairs * med['attn_s_per_pair_head'] / est_s * 100:.0f} %)")
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s",
-            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64 (soft-double)",
             "data": "synthetic", "config": workload_config(args, args.gpus),
+            "method": "projection and attention timed separately on the reference's own code, each scaled by "
+                      "its own unit count (tokens, causal pairs x heads)",
+            "model_s_per_workload_step": est_s,
             "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": kind, "sample": sample},
             "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -822,61 +866,62 @@ def run_codec(args, rank, world, local):
         dist.destroy_process_group()
 
 
-def main():
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5)
-    ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--workload", default="cfg5", choices=sorted(WORKLOADS))
-    ap.add_argument("--batch", type=int, default=0, help="override batch (small ncu cases)")
-    ap.add_argument("--seq", type=int, default=0, help="override seq (decode workloads: context)")
-    ap.add_argument("--decode-steps", type=int, default=256)
-    ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--cpu-tokens", type=int, default=1024)
-    ap.add_argument("--ref-tokens", type=int, default=16)
-    args = ap.parse_args()
+def bf16_round(a):
+    """float32 -> the nearest bfloat16 (round to nearest even) as float32: the value a
+    BF16 device buffer holds after __float2bfloat16_rn of the same float."""
+    a = np.ascontiguousarray(a, np.float32)
+    u = a.view(np.uint32).astype(np.uint64)
+    r = ((u + np.uint64(0x7FFF) + ((u >> np.uint64(16)) & np.uint64(1))) >> np.uint64(16)) << np.uint64(16)
+    return r.astype(np.uint32).view(np.float32).reshape(a.shape)
 
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if args.impl == "reference":
-        if rank == 0:
-            run_reference(args)
-        return
 
+def oracle_weights(O, host_ws, wf, prec):
+    """The dequantised weights the device layer computes with (the parity checker's
+    inputs): FP32 as given (3xTF32 splits are exact), BF16 rounded, FP8 row-scale or
+    NF4 block-64 decoded by the oracle's codecs."""
+    if wf == 1:
+        return [O.fp8_rowscale(w)[2] for w in host_ws]
+    if wf == 2:
+        return [O.nf4_block(w, 64)[2] for w in host_ws]
+    return [bf16_round(w) for w in host_ws] if prec == 1 else list(host_ws)
+
+
+def parity_record(got, want, tol, rows):
+    """max|y - ŷ| / max|ŷ| of each output tensor against the FP64 oracle."""
+    out = {"metric": "max|y-yhat|/max|yhat| vs the FP64 oracle on the same (dequantised) weights and inputs",
+           "rows": rows, "tol": tol}
+    ok = True
+    for name, (g, r) in {k: (got[k], want[k]) for k in got}.items():
+        g = np.asarray(g, np.float64)
+        r = np.asarray(r, np.float64)
+        e = float(np.abs(g - r).max() / max(np.abs(r).max(), 1e-30))
+        out[name] = e
+        ok = ok and bool(np.isfinite(g).all()) and e <= tol
+    out["ok"] = ok
+    return out
+
+
+def run_mha(args, wname, rank, world, local, primary=True):
+    """One MHA workload on this rank's head shard; returns the JSON record (rank 0)
+    or None. A step = one prefill forward over B x T tokens (prefill workloads) or
+    one decode step of B sequences (decode workloads), device-resident inputs.
+    primary: the headline line (clocks, e2e through the host-buffer API, CPU
+    baseline); sub-records carry their own roofline, parity and clocks."""
     import torch
     import torch.distributed as dist
-
     import welvet_b200 as W
-    torch.cuda.set_device(local)
-    if workload(args)["kind"] == "codec":
-        return run_codec(args, rank, world, local)
-    if workload(args)["kind"] in BLOCK_KINDS:
-        return run_block(args, rank, world, local)
-    if workload(args)["kind"] == "nbp":
-        return run_nbp(args, rank, world, local)
-    if world > 1:
-        # NVLS (in-switch reduction) is off unless the caller sets it: on this pool's
-        # 8-GPU boxes the 256 KB decode all-reduce took 31 ms with NVLS and 0.05 ms
-        # without, while the 0.5 GB prefill chunks lost only 4 %. NCCL reads the
-        # variable once, at the first communicator, so it is set before any.
-        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
-    w = workload(args)
+    wall0 = time.perf_counter()
+    w = workload_of(wname, args)
     B, T, d, H, NK, hd, wf, prec = w["B"], w["T"], w["d"], w["H"], w["NK"], w["hd"], w["wf"], w["prec"]
     decode_only = w["kind"] == "decode"
     act = torch.bfloat16 if prec == 1 else torch.float32
     es = 2 if prec == 1 else 4
-    try:
-        hb, hc = W.head_shard(H, NK, world, rank)
-    except ValueError as e:
-        raise SystemExit(str(e))
+    steps, warmup = args.steps, args.warmup
+    hb, hc = W.head_shard(H, NK, world, rank)
     kd_l = (hc // (H // NK)) * hd  # this rank's KV columns
     cfg = W.MhaConfig.make(d, H, NK, precision=prec, weight_format=wf, head_begin=hb, head_count=hc,
                            device=local)
+    check_parity = not args.no_parity and rank == 0
     # Full FP32 weights generated on the device (same stream on every rank), then mounted.
     shapes = [(H * hd, d), (NK * hd, d), (NK * hd, d), (d, H * hd)]
     ws, off = [], 0
@@ -887,6 +932,7 @@ def main():
         off += r * c
         ws.append(t)
     torch.cuda.synchronize()
+    host_ws = [t.cpu().numpy() for t in ws] if (check_parity or (primary and not args.no_cpu)) else None
     layer = W.MhaLayer(cfg, *ws, dtype=1)
     del ws
     torch.cuda.empty_cache()
@@ -913,17 +959,19 @@ def main():
     M = B * T
     x = None
     tokps = ms = None
-    roof = e2e = cpu = None
+    roof = e2e = cpu = parity = None
     launches = 0
     clk = {}
     prof = {}
+    dparity = None
+    n_oracle = min(args.parity_tokens, T)
 
     # ------------------------------------------------------------ timed prefill
     if not decode_only:
         x = torch.empty(M, d, device="cuda", dtype=act)
         W.fill_synthetic(x, 1, 1, 1.0)
         post = torch.empty(M, d, device="cuda", dtype=act)
-        for _ in range(args.warmup):
+        for _ in range(warmup):
             layer.forward(B, T, x, None, post, stream=stream)
         barrier()
         layer.check_device()
@@ -935,7 +983,7 @@ def main():
         W.launch_count(reset=True)
         barrier()
         ev0.record(stream)
-        for _ in range(args.steps):
+        for _ in range(steps):
             layer.forward(B, T, x, None, post, stream=stream)
         ev1.record(stream)
         barrier()
@@ -944,7 +992,7 @@ def main():
         prof = W.profile_read(reset=True)
         clk = clocks.stop()
         layer.check_device()
-        ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps)
+        ms = max_over_ranks(ev0.elapsed_time(ev1) / steps)
         tokps = M / (ms / 1e3)
 
         pf, af = flops_prefill(B, T, d, H, NK, hd)
@@ -956,25 +1004,25 @@ def main():
         tot, cnt = prof[dom]
         avg_ms = tot / max(cnt, 1)
         # with a communicator the batch runs in chunks: several launches per step
-        flops_launch = per_step[dom] * args.steps / max(cnt, 1)
+        flops_launch = per_step[dom] * steps / max(cnt, 1)
         achieved = flops_launch / (avg_ms / 1e3) / 1e12
-        if prec == 0 and dom == "attn_prefill":
-            # FP32 attention runs on the CUDA cores (FFMA): 148 SMs x 128 lanes x 2 x 1.965 GHz
-            peak, pkind = 148 * 128 * 2 * 1.965e9 / 1e12, "nominal FP32 FFMA peak (CUDA cores)"
+        if prec == 0 and dom == "attn_prefill" and not FP32_ATTENTION_ON_TENSOR_CORES:
+            # FP32 attention on the CUDA cores (FFMA): 148 SMs x 128 lanes x 2 x 1.965 GHz
+            peak, pkind, bound = 148 * 128 * 2 * 1.965e9 / 1e12, "nominal FP32 FFMA peak (CUDA cores)", "fp32-fma"
         else:
-            peak, pkind = pk["bf16_sus"], f"{pk['src']} sustained bf16 (of {pk['src']})"
+            peak, pkind, bound = pk["bf16_sus"], f"{pk['src']} sustained bf16 (of {pk['src']})", "tensor"
         cfg5_heads = prec == 1 and hd == 128 and hc == 32 and kd_l == 4096
-        traffic = TRAFFIC_PREFILL_PER_TOKEN * M * args.steps / max(cnt, 1) \
+        traffic = TRAFFIC_PREFILL_PER_TOKEN * M * steps / max(cnt, 1) \
             if dom == "attn_prefill" and cfg5_heads else None
-        roof = {"bound": "tensor" if peak == pk["bf16_sus"] else "fp32-fma", "kernel": dom, "achieved": achieved,
+        roof = {"bound": bound, "kernel": dom, "achieved": achieved,
                 "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak, "peak_kind": pkind,
                 "traffic": traffic, "traffic_source": TRAFFIC_SOURCE if traffic else None,
                 "flops_per_launch": flops_launch, "avg_launch_ms": avg_ms,
-                "launches_per_step": cnt / args.steps,
-                "kernel_ms_per_step": {k: prof[k][0] / args.steps for k in per_step},
+                "launches_per_step": cnt / steps,
+                "kernel_ms_per_step": {k: prof[k][0] / steps for k in per_step},
                 "step_tflops": (pf + af) / world / (ms / 1e3) / 1e12}
 
-        if not args.no_e2e:
+        if primary and not args.no_e2e:
             # With N ranks each holds its B/N sequences in host memory and receives the
             # summed output of those rows (welvet_b200_mha_forward_rows: all-gather in,
             # reduce-scatter out over NVLink); one rank uses the host-buffer forward.
@@ -993,33 +1041,63 @@ def main():
             t0 = time.perf_counter()
             ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             ea.record(stream)
-            n_e2e = max(1, min(args.steps, 3))
-            for _ in range(n_e2e):
+            for _ in range(steps):
                 e2e_step()
             eb.record(stream)
             barrier()
-            e_ms = max_over_ranks(max(ea.elapsed_time(eb), (time.perf_counter() - t0) * 1e3) / n_e2e)
-            e2e = {"value": M / (e_ms / 1e3), "unit": "tok/s", "ms_per_step": e_ms,
+            e_ms = max_over_ranks(max(ea.elapsed_time(eb), (time.perf_counter() - t0) * 1e3) / steps)
+            e2e = {"value": M / (e_ms / 1e3), "unit": "tok/s", "ms_per_step": e_ms, "steps": steps,
                    "h2d_bytes_per_step": M * d * es, "d2h_bytes_per_step": M * d * es,
                    "bytes_scope": "whole job (each rank copies its B/N sequences)" if rows_io else "one GPU",
                    "api": ("welvet_b200_mha_forward_rows (host buffers, pinned, row-sharded)" if rows_io
                            else "welvet_b200_mha_forward (host buffers, pinned)")}
             del xh, ph
+
+        # parity of the timed configuration: one more forward of the same inputs, then
+        # rows [0, n_oracle) of sequence 0 against the FP64 oracle (causal: they depend
+        # on those tokens only); with a communicator post is the sum over ranks
+        pre = torch.empty(M, hc * hd, device="cuda", dtype=act) if world == 1 else None
+        layer.forward(B, T, x, pre, post, stream=stream)
+        barrier()
+        got = {"post": post[:n_oracle].float().cpu().numpy()}
+        if pre is not None:
+            got["pre"] = pre[:n_oracle].float().cpu().numpy()
+            del pre
+        x_rows = x[:n_oracle].float().cpu().numpy()
         del post
         torch.cuda.empty_cache()
-        print(f"[bench] prefill {ms:.3f} ms/step, {tokps:.0f} tok/s; profile {prof}", file=sys.stderr, flush=True)
-        if rank == 0 and world == 1 and not args.no_cpu:
-            dt, fl = cpu_sample(w, args.cpu_tokens)
-            cpu = {"value": fl / dt / ((pf + af) / M), "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
-                   "sample": f"FP64 oracle, 1 sequence x {args.cpu_tokens} tokens of the layer (d={d}, {H}x{hd}), "
-                             f"{dt:.1f} s; tok/s scaled by algorithmic FLOPs/token of the full workload"}
+        if check_parity or (primary and rank == 0 and world == 1 and not args.no_cpu):
+            import oracle_py as O
+            oc = O.MhaCfg(d_model=d, num_heads=H, num_kv_heads=NK, max_seq_len=n_oracle, per_sequence=1)
+            t0 = time.perf_counter()
+            rpre, rpost = O.mha_forward(oc, 1, n_oracle, *oracle_weights(O, host_ws, wf, prec), x_rows)
+            dt = time.perf_counter() - t0
+            if check_parity:
+                want = {"post": rpost}
+                if "pre" in got:
+                    want["pre"] = rpre
+                parity = parity_record(got, want, 1e-4 if prec == 0 else 2e-2,
+                                       f"sequence 0, tokens 0..{n_oracle - 1} of the timed B={B} T={T} forward")
+            if primary and world == 1 and not args.no_cpu:
+                # the same oracle run is the CPU baseline (FP64, all host threads)
+                fl_s = sum(flops_prefill(1, n_oracle, d, H, NK, hd))
+                cpu = {"value": fl_s / dt / ((pf + af) / M), "unit": "tok/s",
+                       "cores": os.cpu_count(), "kind": "port",
+                       "sample": f"FP64 oracle, 1 sequence x {n_oracle} tokens of the layer (d={d}, {H}x{hd}), "
+                                 f"{dt:.1f} s; tok/s scaled by algorithmic FLOPs/token of the full workload"}
+        barrier()
+        print(f"[bench] {wname} prefill {ms:.3f} ms/step, {tokps:.0f} tok/s; parity {parity}", file=sys.stderr,
+              flush=True)
 
     # --------------------------------------------------------------- decode
     decode = None
-    n_dec = args.steps if decode_only else args.decode_steps
+    n_dec = steps if decode_only else (args.decode_steps if primary else 0)
     if n_dec > 0 and w["kind"] != "prefill":
-        extra = n_dec + args.warmup + (3 if decode_only and not args.no_e2e else 0)
+        extra = n_dec + warmup + 1 + (steps if decode_only and primary and not args.no_e2e else 0)
         kv = W.KvCache(layer, B, T + extra + 16)
+        xd = torch.empty(B, d, device="cuda", dtype=act)
+        W.fill_synthetic(xd, 1, 1, 1.0, offset=M * d)
+        pd = torch.empty(B, d, device="cuda", dtype=act)
         if decode_only:
             # context: N(0,1)*0.5 keys/values (seed 2), as cached (after RoPE)
             kc = torch.empty(B, T, kd_l, device="cuda", dtype=act)
@@ -1029,22 +1107,36 @@ def main():
             W.fill_synthetic(vc, 2, 1, 0.5, offset=(2 * rank + 1) * n)
             kv.fill(B, T, kc, vc, stream=stream)
             torch.cuda.synchronize()
+            if world == 1:
+                # parity: one decode step at context T against the oracle's decode for
+                # a few sequences; then the cached lengths go back to T
+                layer.decode(kv, B, xd, None, pd, stream=stream)
+                torch.cuda.synchronize()
+                if check_parity:
+                    import oracle_py as O
+                    sel = [0, B // 2, B - 1]
+                    oc = O.MhaCfg(d_model=d, num_heads=H, num_kv_heads=NK, max_seq_len=T + 1, per_sequence=1)
+                    _, rpost, _, _ = O.mha_decode(oc, [T] * len(sel), kc[sel].float().cpu().numpy(),
+                                                  vc[sel].float().cpu().numpy(),
+                                                  *oracle_weights(O, host_ws, wf, prec),
+                                                  xd[sel].float().cpu().numpy())
+                    dparity = parity_record({"post": pd[sel].float().cpu().numpy()}, {"post": rpost},
+                                            1e-4 if prec == 0 else 2e-2,
+                                            f"sequences {sel}: one decode step over {T} cached tokens")
+                kv.fill(B, T, None, None, stream=stream)
             del kc, vc
         else:
             post = torch.empty(M, d, device="cuda", dtype=act)
             layer.prefill(kv, B, T, x, None, post, stream=stream)
             del post
-        xd = torch.empty(B, d, device="cuda", dtype=act)
-        W.fill_synthetic(xd, 1, 1, 1.0, offset=M * d)
-        pd = torch.empty(B, d, device="cuda", dtype=act)
-        for _ in range(args.warmup):  # first launches load the decode kernels' module
+        for _ in range(warmup):  # first launches load the decode kernels' module
             layer.decode(kv, B, xd, None, pd, stream=stream)
         if decode_only:
             clocks = Clocks(local)
             clocks.start()
             W.launch_count(reset=True)
         barrier()
-        ctx0 = T + args.warmup
+        ctx0 = T + warmup
         W.profile_read(reset=True)
         W.profile_enable(True)
         ev0.record(stream)
@@ -1079,40 +1171,185 @@ def main():
         decode = {"value": B / (dms / 1e3), "unit": "tok/s", "ms_per_step": dms, "steps": n_dec,
                   "context": f"{ctx0}..{ctx0 + n_dec}", "roofline": droof}
         if decode_only:
-            ms, tokps, roof, prof = dms, B / (dms / 1e3), droof, dprof
-            if not args.no_e2e:
+            ms, tokps, roof, prof, parity = dms, B / (dms / 1e3), droof, dprof, dparity
+            if primary and not args.no_e2e:
                 xh = xd.cpu().pin_memory()
                 ph = torch.empty(B, d, dtype=act).pin_memory()
                 barrier()
                 t0 = time.perf_counter()
-                n_e2e = 3
-                for _ in range(n_e2e):
+                for _ in range(steps):
                     layer.decode(kv, B, xh, None, ph)  # H2D x, decode step, D2H post, synchronise
                 barrier()
-                e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3 / n_e2e)
-                e2e = {"value": B / (e_ms / 1e3), "unit": "tok/s", "ms_per_step": e_ms,
+                e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3 / steps)
+                e2e = {"value": B / (e_ms / 1e3), "unit": "tok/s", "ms_per_step": e_ms, "steps": steps,
                        "h2d_bytes_per_step": B * d * es, "d2h_bytes_per_step": B * d * es,
                        "api": "welvet_b200_mha_decode (host buffers, pinned)"}
-            if rank == 0 and world == 1 and not args.no_cpu:
+            if primary and rank == 0 and world == 1 and not args.no_cpu:
                 B_s = 4
                 dt = cpu_sample_decode(w, B_s)
                 cpu = {"value": B_s / dt, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
                        "sample": f"FP64 oracle decode step, {B_s} sequences over {T} cached tokens "
                                  f"(d={d}, {H}x{hd}, {NK} KV heads), {dt:.2f} s"}
         kv.close()
-
-    if rank == 0:
-        line = {"metric": METRIC_DECODE if decode_only else METRIC,
-                "value": tokps, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-                "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-                "dtype": "bf16" if prec == 1 else "f32 (3xTF32 projections)",
-                "data": "synthetic (SplitMix64 counter stream: weights seed 0, x seed 1, KV seed 2)",
-                "config": workload_config(args, world),
-                "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "clocks": clk,
-                "decode": None if decode_only else decode,
-                "profile_ms": {k: v[0] / args.steps for k, v in prof.items() if v[1]}}
-        print(json.dumps(line), flush=True)
     layer.close()
+    del x
+    torch.cuda.empty_cache()
+    if rank != 0:
+        return None
+    return {"metric": METRIC_DECODE if decode_only else METRIC,
+            "value": tokps, "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": warmup,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16" if prec == 1 else "f32 (3xTF32 tensor cores)",
+            "data": "synthetic (SplitMix64 counter stream: weights seed 0, x seed 1, KV seed 2)",
+            "config": workload_config_of(wname, args, world),
+            "roofline": roof, "parity": parity, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
+            "clocks": clk, "decode": None if decode_only else decode,
+            "profile_ms": {k: v[0] / steps for k, v in prof.items() if v[1]},
+            "wall_s": time.perf_counter() - wall0}
+
+
+def run_dequant(args, rank, world, local):
+    """Standalone dequantisation of the extension weight formats to BF16 (the
+    in-mainloop dequant's data path as a kernel of its own): FP8-E4M3 codes with one
+    FP32 scale per row, and NF4 codes (two per byte) with one FP32 absmax per 64
+    weights, over DEQUANT_WEIGHTS weights each (inputs and outputs larger than L2).
+    HBM-bound: bytes = codes + scales read + BF16 written. Parity: the FP32 decode
+    of the first 2^20 weights equals the oracle's decode bit for bit."""
+    import torch
+    import welvet_b200 as W
+    wall0 = time.perf_counter()
+    n = DEQUANT_WEIGHTS
+    cols = 4096
+    rows = n // cols
+    pk = peaks()
+    stream = torch.cuda.current_stream()
+    w = torch.empty(n, device="cuda", dtype=torch.float32)
+    W.fill_synthetic(w, 0, 1, 0.02, offset=rank * n)
+    codes = torch.empty(n, device="cuda", dtype=torch.uint8)
+    # (the encoders below are set-up, outside the timed region)
+    scales = torch.empty(rows, device="cuda", dtype=torch.float32)
+    W.fp8_rowscale_encode(w.view(rows, cols), codes, scales, stream=stream)
+    packed = torch.empty(n // 2, device="cuda", dtype=torch.uint8)
+    absmax = torch.empty(n // 64, device="cuda", dtype=torch.float32)
+    W.nf4_block_encode(w, packed, absmax, stream=stream)
+    out = torch.empty(n, device="cuda", dtype=torch.bfloat16)
+    kinds = {
+        "fp8_rowscale": (lambda: W.fp8_rowscale_decode(codes.view(rows, cols), scales, out, out_bf16=1,
+                                                       stream=stream),
+                         n + rows * 4 + 2 * n),
+        "nf4_block64": (lambda: W.nf4_block_decode(packed, absmax, out, out_bf16=1, stream=stream),
+                        n // 2 + (n // 64) * 4 + 2 * n),
+    }
+    res = {}
+    for name, (fn, nbytes) in kinds.items():
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        clocks = Clocks(local)
+        clocks.start()
+        ea.record(stream)
+        for _ in range(args.steps):
+            fn()
+        eb.record(stream)
+        torch.cuda.synchronize()
+        clk = clocks.stop()
+        ms = ea.elapsed_time(eb) / args.steps
+        gbs = nbytes / (ms / 1e3) / 1e9
+        res[name] = {"value": gbs, "unit": "GB/s", "ms_per_launch": ms, "bytes_per_launch": nbytes,
+                     "roofline": {"bound": "hbm", "achieved": gbs, "peak": pk["hbm"], "unit": "GB/s",
+                                  "frac": gbs / pk["hbm"], "peak_kind": f"{pk['src']} HBM copy (of {pk['src']})",
+                                  "traffic": None},
+                     "clocks": clk}
+    # parity (checker): FP32 decode of the first 2^20 weights vs the oracle, bit for bit
+    parity = None
+    if not args.no_parity and rank == 0:
+        import oracle_py as O
+        ns = 1 << 20
+        wh = w[:ns].cpu().numpy()
+        of = torch.empty(ns, device="cuda", dtype=torch.float32)
+        W.fp8_rowscale_decode(codes[:ns].view(ns // cols, cols), scales[:ns // cols], of, out_bf16=0, stream=stream)
+        got8 = of.cpu().numpy()
+        W.nf4_block_decode(packed[:ns // 2], absmax[:ns // 64], of, out_bf16=0, stream=stream)
+        torch.cuda.synchronize()
+        got4 = of.cpu().numpy()
+        want8 = O.fp8_rowscale(wh.reshape(-1, cols))[2].reshape(-1)
+        want4 = O.nf4_block(wh, 64)[2].reshape(-1)
+        mis8 = int((got8.view(np.uint32) != want8.view(np.uint32)).sum())
+        mis4 = int((got4.view(np.uint32) != want4.view(np.uint32)).sum())
+        parity = {"metric": "bit-exact FP32 decode vs the oracle's decode", "weights": ns,
+                  "fp8_rowscale_mismatches": mis8, "nf4_block64_mismatches": mis4, "ok": mis8 == 0 and mis4 == 0}
+    del w, codes, scales, packed, absmax, out
+    torch.cuda.empty_cache()
+    return {"metric": "FP8 row-scale / NF4 block-64 -> BF16 dequant GB/s", "weights": n,
+            "kernels": res, "parity": parity, "wall_s": time.perf_counter() - wall0}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--workload", default="cfg5", choices=sorted(WORKLOADS))
+    ap.add_argument("--batch", type=int, default=0, help="override batch (small ncu cases)")
+    ap.add_argument("--seq", type=int, default=0, help="override seq (decode workloads: context)")
+    ap.add_argument("--decode-steps", type=int, default=256)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-parity", action="store_true")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the cfg2/cfg3/cfg4/dequant sub-records of the default one-GPU line")
+    ap.add_argument("--parity-tokens", type=int, default=1024)
+    args = ap.parse_args()
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        if rank == 0:
+            run_reference(args)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    if workload(args)["kind"] == "codec":
+        return run_codec(args, rank, world, local)
+    if workload(args)["kind"] in BLOCK_KINDS:
+        return run_block(args, rank, world, local)
+    if workload(args)["kind"] == "nbp":
+        return run_nbp(args, rank, world, local)
+    if world > 1:
+        # NVLS (in-switch reduction) is off unless the caller sets it: on this pool's
+        # 8-GPU boxes the 256 KB decode all-reduce took 31 ms with NVLS and 0.05 ms
+        # without, while the 0.5 GB prefill chunks lost only 4 %. NCCL reads the
+        # variable once, at the first communicator, so it is set before any.
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+    import welvet_b200 as W
+    w = workload(args)
+    try:
+        W.head_shard(w["H"], w["NK"], world, rank)
+    except ValueError as e:
+        raise SystemExit(str(e))
+    t_all = time.perf_counter()
+    line = run_mha(args, args.workload, rank, world, local, primary=True)
+    if world == 1 and args.workload == "cfg5" and not args.no_configs and not (args.batch or args.seq):
+        # the other configurations of the metric, each with its roofline and parity
+        subs = {}
+        for wname in SUB_WORKLOADS:
+            subs[wname] = run_mha(args, wname, rank, world, local, primary=False)
+        subs["dequant"] = run_dequant(args, rank, world, local)
+        total = time.perf_counter() - t_all
+        for r in subs.values():
+            r["share_of_run"] = r["wall_s"] / total
+        line["configs"] = subs
+        line["wall_s_total"] = total
+    if rank == 0:
+        print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -174,6 +174,15 @@ WELVET_API welvet_status welvet_b200_fill_synthetic(void* dst, int32_t is_bf16, 
                                                     double a, void* stream);
 /* Reads and clears the current device's error word (synchronises the device). */
 WELVET_API welvet_status welvet_b200_device_check(void);
+/* Bounded-wait probe (no reference counterpart; the reference reports failures as
+ * status codes, include/welvet/status.hpp:8-30, and this checks the device side of
+ * that contract): launches one kernel whose thread waits on an mbarrier that
+ * nothing arrives at, through the bounded wait every pipeline kernel here uses,
+ * with limit_ns (1 ns .. 10 s) instead of the library's 4 s. The wait runs out,
+ * the kernel records "device wait timeout" in the current device's error word and
+ * returns without trapping; welvet_b200_device_check then returns code 4 and the
+ * device stays usable. Code 1 for a limit out of range. */
+WELVET_API welvet_status welvet_b200_wait_probe(uint64_t limit_ns, void* stream);
 /* Number of kernel launches this library issued since the last reset
  * (benchmark accounting). No reference counterpart. */
 WELVET_API int64_t welvet_b200_launch_count(int32_t reset);

@@ -32,6 +32,15 @@ def rel_err(got, ref):
     return float(np.abs(got - ref).max() / denom)
 
 
+def bf16_round(a):
+    """float32 -> nearest bfloat16 (round to nearest even) as float32: what a BF16
+    device buffer holds after __float2bfloat16_rn of the same value."""
+    a = np.ascontiguousarray(a, np.float32)
+    u = a.view(np.uint32).astype(np.uint64)
+    r = ((u + np.uint64(0x7FFF) + ((u >> np.uint64(16)) & np.uint64(1))) >> np.uint64(16)) << np.uint64(16)
+    return r.astype(np.uint32).view(np.float32).reshape(a.shape)
+
+
 @pytest.fixture(scope="session")
 def torch_cuda():
     import torch

@@ -161,7 +161,7 @@ def test_prefill_then_decode_against_oracle(torch_cuda, precision):
 
 
 def test_decode_gqa_against_oracle_decode(torch_cuda):
-    """Decode with a cache filled directly (BASELINE config 3 shape class)."""
+    """Decode with a cache filled directly (GQA decode shape class: 32/8 heads x 64)."""
     torch = torch_cuda
     d, H, NK, B, L = 512, 8, 2, 6, 333
     cfg = W.MhaConfig.make(d, H, NK, precision=1)

@@ -75,8 +75,9 @@ WV_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Waits for the phase of `bar` with the given parity. Gives up when `abort`
 // (a shared flag) becomes non-zero or after WV_WAIT_LIMIT_NS, recording `code`
 // in *err and setting *abort so the other roles of the CTA unwind too.
-WV_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, uint32_t* err,
-                      uint32_t code) {
+// mbar_wait_for takes the limit as an argument (the wait probe uses a short one).
+WV_DEV bool mbar_wait_for(uint64_t* bar, uint32_t parity, volatile int* abort, uint32_t* err,
+                          uint32_t code, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (true) {
@@ -84,12 +85,16 @@ WV_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, uint3
     for (int i = 0; i < 32; ++i)
       if (mbar_try_wait(bar, parity)) return true;
     if (*abort) return false;
-    if (globaltimer() - t0 > WV_WAIT_LIMIT_NS) {
+    if (globaltimer() - t0 > limit_ns) {
       atomicCAS(err, 0u, code);
       *abort = 1;
       return false;
     }
   }
+}
+WV_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, uint32_t* err,
+                      uint32_t code) {
+  return mbar_wait_for(bar, parity, abort, err, code, WV_WAIT_LIMIT_NS);
 }
 
 // ----------------------------------------------------------------------- TMA

@@ -230,6 +230,10 @@ cudaError_t pad_cols(const float* src, float* dst, int64_t rows, int cols, int c
 cudaError_t pad_operand(const void* x, int x_bf16, int64_t rows, int cols, int cols_p, float* hi,
                         float* lo, void* b, cudaStream_t s);
 
+// ---- bounded-wait probe (wait_probe.cu): one mbarrier wait that runs out after
+// limit_ns and records kErrWaitOther in err
+cudaError_t wait_probe(uint32_t* err, uint64_t limit_ns, cudaStream_t s);
+
 // ---- MHA NormalBP leaf (mha_bwd.cu)
 struct BwdArgs {
   int B = 0, T = 0;

@@ -310,6 +310,7 @@ struct welvet_b200_swiglu {
 welvet_status welvet_swiglu_forward_f32(int32_t batch, int32_t seq, int32_t input_dim, int32_t intermediate_dim,
                                         int32_t dtype, int32_t /*backend*/, const float* Gate, const float* Up,
                                         const float* Down, const float* x, float* pre, float* post) {
+  wv::DeviceRestore restore_device;
   if (batch <= 0 || seq <= 0 || input_dim <= 0 || intermediate_dim <= 0 || !Gate || !Up || !Down || !x || !pre ||
       !post)
     return wv::status_c(1, "swiglu: invalid argument");
@@ -354,6 +355,7 @@ welvet_status welvet_embedding_forward_f32(int32_t batch, int32_t vocab, int32_t
 welvet_status welvet_b200_swiglu_mount(int32_t input_dim, int32_t intermediate_dim, int32_t precision,
                                        int32_t device, int32_t dtype, const float* Gate, const float* Up,
                                        const float* Down, int32_t weights_on_device, welvet_b200_swiglu** out) {
+  wv::DeviceRestore restore_device;
   if (!out) return wv::status_c(1, "swiglu: invalid argument");
   wv::Swiglu* L = nullptr;
   Status st = wv::swiglu_mount(input_dim, intermediate_dim, precision, device, dtype, Gate, Up, Down,
@@ -365,18 +367,21 @@ welvet_status welvet_b200_swiglu_mount(int32_t input_dim, int32_t intermediate_d
 
 welvet_status welvet_b200_swiglu_forward(welvet_b200_swiglu* layer, int64_t tokens, const void* x, void* pre,
                                          void* post, void* stream) {
+  wv::DeviceRestore restore_device;
   if (!layer) return wv::status_c(1, "swiglu: invalid argument");
   return wv::to_c(wv::swiglu_forward(layer->impl, tokens, x, pre, post, false, static_cast<cudaStream_t>(stream)));
 }
 
 welvet_status welvet_b200_swiglu_forward_host(welvet_b200_swiglu* layer, int64_t tokens, const float* x,
                                               float* pre, float* post) {
+  wv::DeviceRestore restore_device;
   if (!layer) return wv::status_c(1, "swiglu: invalid argument");
   if (layer->impl->precision != 0) return wv::status_c(2, "swiglu: host buffers need the FP32 layer");
   return wv::to_c(wv::swiglu_forward(layer->impl, tokens, x, pre, post, true, 0));
 }
 
 void welvet_b200_swiglu_release(welvet_b200_swiglu* layer) {
+  wv::DeviceRestore restore_device;
   if (!layer) return;
   cudaDeviceSynchronize();
   wv::swiglu_release(layer->impl);

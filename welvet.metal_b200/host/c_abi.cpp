@@ -77,6 +77,7 @@ welvet_status welvet_mha_forward_f32(int32_t batch, int32_t seq, int32_t d_model
                                      int32_t mask, int32_t pos, int32_t dtype, int32_t /*backend*/,
                                      const float* Q, const float* K, const float* V, const float* O,
                                      const float* x, float* pre, float* post) {
+  wv::DeviceRestore restore_device;
   if (batch <= 0 || seq <= 0 || d_model <= 0 || num_heads <= 0 || !Q || !K || !V || !O || !x || !pre ||
       !post) {
     welvet_status st{};
@@ -136,6 +137,7 @@ void welvet_b200_mha_config_default(welvet_b200_mha_config* cfg, int32_t d_model
 welvet_status welvet_b200_mha_mount(const welvet_b200_mha_config* cfg, int32_t dtype, const float* Q,
                                     const float* K, const float* V, const float* O, int32_t weights_on_device,
                                     welvet_b200_mha** out) {
+  wv::DeviceRestore restore_device;
   if (!cfg || !out) return wv::to_c(Status::err(1, "mha: invalid argument"));
   wv::Mha* m = nullptr;
   Status st = wv::mha_mount(*cfg, dtype, Q, K, V, O, weights_on_device != 0, &m);
@@ -145,6 +147,7 @@ welvet_status welvet_b200_mha_mount(const welvet_b200_mha_config* cfg, int32_t d
 }
 
 void welvet_b200_mha_release(welvet_b200_mha* layer) {
+  wv::DeviceRestore restore_device;
   if (!layer) return;
   delete layer->m;
   delete layer;
@@ -152,12 +155,14 @@ void welvet_b200_mha_release(welvet_b200_mha* layer) {
 
 welvet_status welvet_b200_mha_forward(welvet_b200_mha* layer, int32_t batch, int32_t seq, const void* x,
                                       void* pre, void* post, int32_t on_device, void* stream) {
+  wv::DeviceRestore restore_device;
   if (!layer) return wv::to_c(Status::err(1, "mha: nil layer"));
   return wv::to_c(wv::mha_forward(layer->m, batch, seq, x, pre, post, on_device != 0, as_stream(stream)));
 }
 
 welvet_status welvet_b200_mha_forward_rows(welvet_b200_mha* layer, int32_t batch_local, int32_t seq, const void* x,
                                            void* post) {
+  wv::DeviceRestore restore_device;
   if (!layer) return wv::to_c(Status::err(1, "mha: nil layer"));
   wv::Mha* m = layer->m;
   const bool sharded = m->comm && m->nranks > 1;
@@ -168,12 +173,16 @@ welvet_status welvet_b200_mha_forward_rows(welvet_b200_mha* layer, int32_t batch
 }
 
 welvet_status welvet_b200_mha_check(welvet_b200_mha* layer) {
+  wv::DeviceRestore restore_device;
   if (!layer) return wv::to_c(Status::err(1, "mha: nil layer"));
-  return wv::to_c(wv::check_device_error(layer->m->dev));
+  Status st = wv::check_device_error(layer->m->dev);
+  if (!st) return wv::to_c(st);
+  return wv::to_c(wv::comm_poll(layer->m));
 }
 
 welvet_status welvet_b200_kv_create(welvet_b200_mha* layer, int32_t max_batch, int32_t max_ctx,
                                     welvet_b200_kv** out) {
+  wv::DeviceRestore restore_device;
   if (!layer || !out) return wv::to_c(Status::err(1, "kv: invalid argument"));
   wv::Kv* kv = nullptr;
   Status st = wv::kv_create(layer->m, max_batch, max_ctx, &kv);
@@ -183,6 +192,7 @@ welvet_status welvet_b200_kv_create(welvet_b200_mha* layer, int32_t max_batch, i
 }
 
 void welvet_b200_kv_release(welvet_b200_kv* kv) {
+  wv::DeviceRestore restore_device;
   if (!kv) return;
   delete kv->kv;
   delete kv;
@@ -190,12 +200,14 @@ void welvet_b200_kv_release(welvet_b200_kv* kv) {
 
 welvet_status welvet_b200_kv_fill(welvet_b200_kv* kv, int32_t batch, int32_t ctx_len, const void* k,
                                   const void* v, int32_t on_device, void* stream) {
+  wv::DeviceRestore restore_device;
   if (!kv) return wv::to_c(Status::err(1, "kv: nil cache"));
   return wv::to_c(wv::kv_fill(kv->kv, batch, ctx_len, k, v, on_device != 0, as_stream(stream)));
 }
 
 welvet_status welvet_b200_mha_prefill(welvet_b200_mha* layer, welvet_b200_kv* kv, int32_t batch, int32_t seq,
                                       const void* x, void* pre, void* post, int32_t on_device, void* stream) {
+  wv::DeviceRestore restore_device;
   if (!layer || !kv) return wv::to_c(Status::err(1, "mha prefill: invalid argument"));
   if (layer->m->cfg.c.seq_mode != 1)
     return wv::to_c(Status::err(1, "mha prefill: needs seq_mode 1 (per-sequence positions)"));
@@ -206,6 +218,7 @@ welvet_status welvet_b200_mha_prefill(welvet_b200_mha* layer, welvet_b200_kv* kv
 
 welvet_status welvet_b200_mha_decode(welvet_b200_mha* layer, welvet_b200_kv* kv, int32_t batch, const void* x_new,
                                      void* pre, void* post, int32_t on_device, void* stream) {
+  wv::DeviceRestore restore_device;
   if (!layer || !kv) return wv::to_c(Status::err(1, "mha decode: invalid argument"));
   return wv::to_c(wv::mha_decode(layer->m, kv->kv, batch, x_new, pre, post, on_device != 0, as_stream(stream)));
 }
@@ -214,6 +227,7 @@ welvet_status welvet_b200_comm_unique_id(uint8_t id[128]) { return wv::to_c(wv::
 
 welvet_status welvet_b200_comm_attach(welvet_b200_mha* layer, const uint8_t id[128], int32_t nranks,
                                       int32_t rank) {
+  wv::DeviceRestore restore_device;
   if (!layer) return wv::to_c(Status::err(1, "comm: nil layer"));
   return wv::to_c(wv::comm_attach(layer->m, id, nranks, rank));
 }
@@ -254,6 +268,7 @@ welvet_status welvet_b200_split_tf32(const float* x, float* hi, float* lo, int64
 
 welvet_status welvet_b200_attention(const welvet_b200_mha_config* cfgp, int32_t batch, int32_t seq, const void* q,
                                     const void* k, const void* v, void* out, int32_t impl, void* stream) {
+  wv::DeviceRestore restore_device;
   if (!cfgp || !q || !k || !v || !out || batch <= 0 || seq <= 0)
     return wv::to_c(Status::err(1, "attention: invalid argument"));
   wv::Cfg c;
@@ -369,6 +384,15 @@ welvet_status welvet_b200_device_check(void) {
   Status st = wv::device_ctx(-1, &d);
   if (!st) return wv::to_c(st);
   return wv::to_c(wv::check_device_error(d));
+}
+
+welvet_status welvet_b200_wait_probe(uint64_t limit_ns, void* stream) {
+  if (limit_ns == 0 || limit_ns > 10000000000ull) return wv::to_c(Status::err(1, "wait probe: limit out of range"));
+  wv::DeviceCtx* d = nullptr;
+  Status st = wv::device_ctx(-1, &d);
+  if (!st) return wv::to_c(st);
+  wv::count_launch();
+  return launch_status(wv::wait_probe(d->err, limit_ns, as_stream(stream)), "wait_probe");
 }
 
 int64_t welvet_b200_launch_count(int32_t reset) {

@@ -7,11 +7,25 @@
 // libnccl is opened with dlopen when a communicator is first needed, not linked:
 // in a process that already loaded NCCL (e.g. through torch) the same library is
 // reused, so two NCCL versions never meet in one process.
+//
+// Failures end in a status, never a hang (the reference's contract,
+// include/welvet/status.hpp:8-30). The communicator is created non-blocking and
+// the host polls ncclCommGetAsyncError until it is ready, for at most the comm
+// timeout: a rank that never joins makes every other rank's attach abort the
+// communicator (ncclCommAbort) and return code 4. Synchronous calls wait for
+// their stream the same way (comm_wait): a collective that does not finish
+// within the timeout, or an asynchronous NCCL error, aborts the communicator,
+// which ends the NCCL kernels still waiting for a peer, and returns code 4; the
+// layer then has no communicator until it is attached again. The timeout is
+// WELVET_B200_COMM_TIMEOUT_MS (default 300000 ms), read at each attach.
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <chrono>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <thread>
 
 #include "engine.hpp"
 
@@ -20,7 +34,9 @@ namespace {
 
 struct NcclApi {
   decltype(&ncclGetUniqueId) get_unique_id = nullptr;
-  decltype(&ncclCommInitRank) comm_init_rank = nullptr;
+  decltype(&ncclCommInitRankConfig) comm_init_rank_config = nullptr;
+  decltype(&ncclCommGetAsyncError) async_error = nullptr;
+  decltype(&ncclCommAbort) comm_abort = nullptr;
   decltype(&ncclAllReduce) all_reduce = nullptr;
   decltype(&ncclAllGather) all_gather = nullptr;
   decltype(&ncclReduceScatter) reduce_scatter = nullptr;
@@ -41,14 +57,17 @@ const NcclApi& nccl() {
       return;
     }
     api.get_unique_id = reinterpret_cast<decltype(api.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
-    api.comm_init_rank = reinterpret_cast<decltype(api.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
+    api.comm_init_rank_config =
+        reinterpret_cast<decltype(api.comm_init_rank_config)>(dlsym(h, "ncclCommInitRankConfig"));
+    api.async_error = reinterpret_cast<decltype(api.async_error)>(dlsym(h, "ncclCommGetAsyncError"));
+    api.comm_abort = reinterpret_cast<decltype(api.comm_abort)>(dlsym(h, "ncclCommAbort"));
     api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(dlsym(h, "ncclAllReduce"));
     api.all_gather = reinterpret_cast<decltype(api.all_gather)>(dlsym(h, "ncclAllGather"));
     api.reduce_scatter = reinterpret_cast<decltype(api.reduce_scatter)>(dlsym(h, "ncclReduceScatter"));
     api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
     api.error_string = reinterpret_cast<decltype(api.error_string)>(dlsym(h, "ncclGetErrorString"));
-    api.ok = api.get_unique_id && api.comm_init_rank && api.all_reduce && api.all_gather && api.reduce_scatter &&
-             api.comm_destroy && api.error_string;
+    api.ok = api.get_unique_id && api.comm_init_rank_config && api.async_error && api.comm_abort &&
+             api.all_reduce && api.all_gather && api.reduce_scatter && api.comm_destroy && api.error_string;
     if (!api.ok) api.why = "libnccl.so.2 lacks an entry point";
   });
   return api;
@@ -56,6 +75,25 @@ const NcclApi& nccl() {
 
 Status nccl_status(ncclResult_t r, const char* what) {
   return Status::err(4, std::string("nccl: ") + what + ": " + nccl().error_string(r));
+}
+
+int64_t comm_timeout_ms() {
+  const char* v = std::getenv("WELVET_B200_COMM_TIMEOUT_MS");
+  if (v && *v) {
+    const long long t = std::atoll(v);
+    if (t > 0) return t;
+  }
+  return 300000;
+}
+
+// Aborts the layer's communicator after a failure and drops it (the layer runs
+// without one until it is attached again). Returns `why`.
+Status abort_comm(Mha* m, Status why) {
+  if (m->comm && nccl().ok) nccl().comm_abort(static_cast<ncclComm_t>(m->comm));
+  m->comm = nullptr;
+  m->nranks = 1;
+  m->rank = 0;
+  return why;
 }
 
 } // namespace
@@ -78,8 +116,29 @@ Status comm_attach(Mha* m, const uint8_t id[128], int nranks, int rank) {
   ncclUniqueId u;
   std::memcpy(&u, id, 128);
   ncclComm_t c = nullptr;
-  ncclResult_t r = nccl().comm_init_rank(&c, nranks, u, rank);
-  if (r != ncclSuccess) return nccl_status(r, "ncclCommInitRank");
+  ncclConfig_t config = NCCL_CONFIG_INITIALIZER;
+  config.blocking = 0;
+  m->comm_timeout_ms = comm_timeout_ms();
+  ncclResult_t r = nccl().comm_init_rank_config(&c, nranks, u, rank, &config);
+  if (r != ncclSuccess && r != ncclInProgress) return nccl_status(r, "ncclCommInitRankConfig");
+  // Every rank must join within the timeout.
+  const auto t0 = std::chrono::steady_clock::now();
+  ncclResult_t state = ncclInProgress;
+  while (true) {
+    if (nccl().async_error(c, &state) != ncclSuccess) state = ncclInternalError;
+    if (state != ncclInProgress) break;
+    const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0);
+    if (ms.count() > m->comm_timeout_ms) {
+      nccl().comm_abort(c);
+      return Status::err(4, "comm: communicator init timed out after " + std::to_string(m->comm_timeout_ms) +
+                                " ms (a rank did not join); aborted");
+    }
+    std::this_thread::sleep_for(std::chrono::milliseconds(1));
+  }
+  if (state != ncclSuccess) {
+    nccl().comm_abort(c);
+    return nccl_status(state, "ncclCommInitRankConfig (asynchronous)");
+  }
   m->comm = c;
   m->nranks = nranks;
   m->rank = rank;
@@ -90,12 +149,32 @@ Status comm_attach(Mha* m, const uint8_t id[128], int nranks, int rank) {
   return Status::ok();
 }
 
+namespace {
+// A non-blocking communicator may answer an enqueue with ncclInProgress; the
+// operation is then complete once the asynchronous state leaves ncclInProgress.
+Status enqueued(Mha* m, ncclResult_t r, const char* what) {
+  if (r == ncclSuccess) return Status::ok();
+  if (r != ncclInProgress) return abort_comm(m, nccl_status(r, what));
+  const auto t0 = std::chrono::steady_clock::now();
+  ncclResult_t state = ncclInProgress;
+  while (true) {
+    if (nccl().async_error(static_cast<ncclComm_t>(m->comm), &state) != ncclSuccess) state = ncclInternalError;
+    if (state != ncclInProgress) break;
+    const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0);
+    if (ms.count() > m->comm_timeout_ms)
+      return abort_comm(m, Status::err(4, std::string("comm: ") + what + " enqueue timed out; communicator aborted"));
+    std::this_thread::yield();
+  }
+  if (state != ncclSuccess) return abort_comm(m, nccl_status(state, what));
+  return Status::ok();
+}
+}  // namespace
+
 Status comm_allreduce(Mha* m, void* buf, size_t count, bool bf16, cudaStream_t s) {
   if (!m->comm || m->nranks == 1) return Status::ok();
   ncclResult_t r = nccl().all_reduce(buf, buf, count, bf16 ? ncclBfloat16 : ncclFloat32, ncclSum,
                                      static_cast<ncclComm_t>(m->comm), s);
-  if (r != ncclSuccess) return nccl_status(r, "ncclAllReduce");
-  return Status::ok();
+  return enqueued(m, r, "ncclAllReduce");
 }
 
 // In place over buf [nranks * count]: rank r's part starts at r * count elements.
@@ -104,8 +183,7 @@ Status comm_allgather(Mha* m, void* buf, size_t count, bool bf16, cudaStream_t s
   const size_t es = bf16 ? 2 : 4;
   ncclResult_t r = nccl().all_gather(static_cast<char*>(buf) + (size_t)m->rank * count * es, buf, count,
                                      bf16 ? ncclBfloat16 : ncclFloat32, static_cast<ncclComm_t>(m->comm), s);
-  if (r != ncclSuccess) return nccl_status(r, "ncclAllGather");
-  return Status::ok();
+  return enqueued(m, r, "ncclAllGather");
 }
 Status comm_reducescatter(Mha* m, void* buf, size_t count, bool bf16, cudaStream_t s) {
   if (!m->comm || m->nranks == 1) return Status::ok();
@@ -113,8 +191,43 @@ Status comm_reducescatter(Mha* m, void* buf, size_t count, bool bf16, cudaStream
   ncclResult_t r = nccl().reduce_scatter(buf, static_cast<char*>(buf) + (size_t)m->rank * count * es, count,
                                          bf16 ? ncclBfloat16 : ncclFloat32, ncclSum,
                                          static_cast<ncclComm_t>(m->comm), s);
-  if (r != ncclSuccess) return nccl_status(r, "ncclReduceScatter");
+  return enqueued(m, r, "ncclReduceScatter");
+}
+
+Status comm_poll(Mha* m) {
+  if (!m->comm || !nccl().ok) return Status::ok();
+  ncclResult_t state = ncclSuccess;
+  ncclResult_t r = nccl().async_error(static_cast<ncclComm_t>(m->comm), &state);
+  if (r != ncclSuccess) return abort_comm(m, nccl_status(r, "ncclCommGetAsyncError"));
+  if (state != ncclSuccess && state != ncclInProgress)
+    return abort_comm(m, nccl_status(state, "asynchronous communicator error; communicator aborted"));
   return Status::ok();
+}
+
+Status comm_wait(Mha* m, cudaStream_t s, const char* what) {
+  if (!m->comm || m->nranks == 1) {
+    WV_CUDA(cudaStreamSynchronize(s), what);
+    return Status::ok();
+  }
+  const auto t0 = std::chrono::steady_clock::now();
+  while (true) {
+    cudaError_t e = cudaStreamQuery(s);
+    if (e == cudaSuccess) return comm_poll(m);
+    if (e != cudaErrorNotReady) return cuda_status(e, what);
+    WV_TRY(comm_poll(m));
+    if (!m->comm) return Status::err(4, "comm: communicator aborted");
+    const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0);
+    if (ms.count() > m->comm_timeout_ms) {
+      Status st = abort_comm(m, Status::err(4, std::string("comm: ") + what + " did not finish within " +
+                                                   std::to_string(m->comm_timeout_ms) +
+                                                   " ms (a peer rank stopped); communicator aborted"));
+      // the abort ends the NCCL kernels that waited for the peer; drain the stream
+      cudaStreamSynchronize(s);
+      cudaGetLastError();
+      return st;
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(200));
+  }
 }
 
 void comm_release(Mha* m) {

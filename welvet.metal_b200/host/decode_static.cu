@@ -11,8 +11,10 @@
 //     allocator (PyTorch's, for one) and sizes its pools against the free
 //     memory it sees: memory that a library takes behind its back is missing
 //     from that accounting and can make the framework's next allocation fail.
-// For them this entry point runs the same two kernels (decode_kernel +
-// decode_combine_kernel) with the partials in a fixed file-scope device array.
+// For them this entry point runs the same kernels as the layer's decode step
+// (attn_decode: decode_tc_kernel for BF16 head_dim 64/128 with aligned rows, else
+// the CUDA-core decode_kernel, then decode_combine_kernel) with the partials in a
+// fixed file-scope device array.
 //
 // Contract:
 //   * The scratch holds kStaticDecodeFloats floats (4 MiB) per device. A call
@@ -25,6 +27,16 @@
 //   * One scratch per device is shared by every call on that device: calls that
 //     overlap in time (different streams, or different host threads with their
 //     own streams) race on it. Issue them on one stream, one after another.
+//   * Errors found on the device (a bounded wait of decode_tc_kernel that ran
+//     out) go to a second file-scope word, g_decode_err, found the same way, so
+//     that no error buffer has to be allocated either. welvet_b200_device_check
+//     reads and clears it together with the library's per-device error word
+//     (that call allocates the library's small per-device state on its first
+//     call on a device, so callers that cannot allocate later make it once
+//     during their set-up).
+//   * Page ids in block_table must name pages of k_pool/v_pool: the entry point
+//     does not know the pools' size, so it cannot check them.
+//   * The caller's current device is restored before the call returns.
 //   * The first call on a device performs the set-up: the symbol lookup below
 //     (which can load this module and its 4 MiB array) and the first launches of
 //     the decode kernels (which load their module). Make that first call before
@@ -42,9 +54,11 @@ constexpr size_t kStaticDecodeFloats = WELVET_B200_DECODE_STATIC_FLOATS;
 constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) float g_decode_partial[kStaticDecodeFloats];
+static __device__ uint32_t g_decode_err;
 
 struct StaticSlot {
   float* partial = nullptr;
+  uint32_t* err = nullptr;
   int sm_count = 0;
 };
 StaticSlot g_slots[kMaxDevices];
@@ -59,10 +73,14 @@ Status static_slot(int device, StaticSlot* out) {
     void* p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_decode_partial);
     if (e != cudaSuccess) return cuda_status(e, "decode_attention_static: cudaGetSymbolAddress");
+    void* pe = nullptr;
+    e = cudaGetSymbolAddress(&pe, g_decode_err);
+    if (e != cudaSuccess) return cuda_status(e, "decode_attention_static: cudaGetSymbolAddress (error word)");
     int sms = 0;
     e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
     if (e != cudaSuccess) return cuda_status(e, "decode_attention_static: SM count");
     s.sm_count = sms;
+    s.err = static_cast<uint32_t*>(pe);
     s.partial = static_cast<float*>(p);
   }
   *out = s;
@@ -98,6 +116,7 @@ Status decode_attention_static(const welvet_b200_mha_config& cfg_in, int batch, 
   if (device < 0 && cudaGetDevice(&device) != cudaSuccess)
     return Status::err(4, "decode_attention_static: no current device");
   if (device >= kMaxDevices) return Status::err(1, "decode_attention_static: device ordinal too large");
+  DeviceRestore restore_device;
   int cur = -1;
   WV_CUDA(cudaGetDevice(&cur), "cudaGetDevice");
   if (cur != device) WV_CUDA(cudaSetDevice(device), "cudaSetDevice");
@@ -127,6 +146,7 @@ Status decode_attention_static(const welvet_b200_mha_config& cfg_in, int batch, 
   d.max_ctx = max_ctx;
   d.sm_count = slot.sm_count;
   d.partial = slot.partial;
+  d.err = slot.err;
   const int want = decode_splits(d);
   d.splits = (int)std::min<size_t>((size_t)want, kStaticDecodeFloats / per_split);
   WV_CUDA(attn_decode(d, stream), "decode_attention_static");
@@ -135,6 +155,26 @@ Status decode_attention_static(const welvet_b200_mha_config& cfg_in, int batch, 
 }
 
 }  // namespace
+
+// Reads and clears g_decode_err of the current device when this entry point has
+// run on it (no allocation: the word is this module's own variable).
+Status take_static_decode_error(uint32_t* code) {
+  *code = 0;
+  int device = -1;
+  WV_CUDA(cudaGetDevice(&device), "cudaGetDevice");
+  if (device < 0 || device >= kMaxDevices) return Status::ok();
+  {
+    std::lock_guard<std::mutex> lock(g_slots_mu);
+    if (!g_slots[device].err) return Status::ok();
+  }
+  WV_CUDA(cudaMemcpyFromSymbol(code, g_decode_err, sizeof(uint32_t)), "read static decode error word");
+  if (*code) {
+    const uint32_t zero = 0;
+    WV_CUDA(cudaMemcpyToSymbol(g_decode_err, &zero, sizeof(uint32_t)), "clear static decode error word");
+  }
+  return Status::ok();
+}
+
 }  // namespace wv
 
 // No counterpart in the reference; declared in include/welvet_b200.h.

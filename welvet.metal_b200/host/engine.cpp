@@ -105,6 +105,36 @@ Status cuda_status(cudaError_t e, const char* what) {
   return Status::err(4, std::string("cuda: ") + what + ": " + cudaGetErrorString(e));
 }
 
+namespace {
+using PrimaryCtxStateFn = int (*)(int dev, unsigned int* flags, int* active);
+PrimaryCtxStateFn primary_ctx_state_fn() {
+  static PrimaryCtxStateFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuDevicePrimaryCtxGetState", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      return reinterpret_cast<PrimaryCtxStateFn>(p);
+    return static_cast<PrimaryCtxStateFn>(nullptr);
+  }();
+  return fn;
+}
+}  // namespace
+
+DeviceRestore::DeviceRestore() {
+  if (cudaGetDevice(&dev_) != cudaSuccess) dev_ = -1;
+}
+
+DeviceRestore::~DeviceRestore() {
+  if (dev_ < 0) return;
+  int now = -1;
+  if (cudaGetDevice(&now) != cudaSuccess || now == dev_) return;
+  unsigned int flags = 0;
+  int active = 0;
+  PrimaryCtxStateFn fn = primary_ctx_state_fn();
+  if (!fn || fn(dev_, &flags, &active) != 0 || !active) return;
+  cudaSetDevice(dev_);
+}
+
 // ------------------------------------------------------------------ devices
 namespace {
 std::mutex g_dev_mu;
@@ -157,6 +187,9 @@ Status check_device_error(DeviceCtx* d) {
   WV_CUDA(cudaDeviceSynchronize(), "synchronize");
   uint32_t code = 0;
   WV_CUDA(cudaMemcpy(&code, d->err, 4, cudaMemcpyDeviceToHost), "read error word");
+  uint32_t static_code = 0;
+  WV_TRY(take_static_decode_error(&static_code));
+  if (!code) code = static_code;
   if (code) {
     cudaMemset(d->err, 0, 4);
     char buf[96];
@@ -789,7 +822,7 @@ Status mha_forward(Mha* m, int batch, int seq, const void* x, void* pre, void* p
       WV_CUDA(cudaMemcpyAsync(post, postd, M * dm * es, cudaMemcpyDeviceToHost, s), "D2H post");
       if (pre) WV_CUDA(cudaMemcpyAsync(pre, pred, M * m->qd_l * es, cudaMemcpyDeviceToHost, s), "D2H pre");
     }
-    WV_CUDA(cudaStreamSynchronize(s), "forward");
+    WV_TRY(comm_wait(m, s, "forward"));
     WV_TRY(check_device_error(m->dev));
   }
   return Status::ok();
@@ -985,7 +1018,7 @@ Status mha_decode(Mha* m, Kv* kv, int batch, const void* x, void* pre, void* pos
   if (!on_device) {
     WV_CUDA(cudaMemcpyAsync(post, postd, (size_t)batch * dm * es, cudaMemcpyDeviceToHost, s), "D2H post");
     if (pre) WV_CUDA(cudaMemcpyAsync(pre, attn, (size_t)batch * m->qd_l * es, cudaMemcpyDeviceToHost, s), "D2H pre");
-    WV_CUDA(cudaStreamSynchronize(s), "decode");
+    WV_TRY(comm_wait(m, s, "decode"));
     WV_TRY(check_device_error(m->dev));
   }
   return Status::ok();

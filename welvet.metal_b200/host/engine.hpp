@@ -30,6 +30,23 @@ struct Status {
 welvet_status to_c(const Status& s);
 Status cuda_status(cudaError_t e, const char* what);
 
+// Keeps the calling thread's current CUDA device across an entry point: the
+// engine switches to the device of the layer it runs, and the destructor
+// switches back. When the caller's device has no active primary context (the
+// thread never used CUDA on it), switching back would create one on that device
+// (cudaSetDevice initialises it), so the thread is then left on the device the
+// call used.
+class DeviceRestore {
+ public:
+  DeviceRestore();
+  ~DeviceRestore();
+  DeviceRestore(const DeviceRestore&) = delete;
+  DeviceRestore& operator=(const DeviceRestore&) = delete;
+
+ private:
+  int dev_ = -1;
+};
+
 #define WV_TRY(expr)                               \
   do {                                             \
     ::wv::Status _st = (expr);                     \
@@ -110,6 +127,9 @@ struct DeviceCtx {
 };
 Status device_ctx(int device, DeviceCtx** out);  // device < 0: current
 Status check_device_error(DeviceCtx* d);         // sync + read/clear the error word
+// Reads and clears the error word of welvet_b200_decode_attention_static on the
+// current device (decode_static.cu; 0 when that entry point has not run there).
+Status take_static_decode_error(uint32_t* code);
 
 // Resolved welvet::mha::Config (defaults of validate(),
 // src/layers/mha/mha.cpp:63-94) + execution choices.
@@ -142,6 +162,7 @@ struct Mha {
   // chunk runs on comm_stream while the next chunk computes on the caller's stream
   void* comm = nullptr;
   int nranks = 1, rank = 0;
+  int64_t comm_timeout_ms = 300000;  // bound of init, enqueue and synchronous waits
   cudaStream_t comm_stream = nullptr;
   static constexpr int kMaxChunks = 16;
   cudaEvent_t chunk_done[kMaxChunks] = {};
@@ -185,6 +206,13 @@ Status comm_allreduce(Mha* m, void* buf, size_t count, bool bf16, cudaStream_t s
 // in place over buf [nranks * count]; rank r's part at r * count elements
 Status comm_allgather(Mha* m, void* buf, size_t count, bool bf16, cudaStream_t s);
 Status comm_reducescatter(Mha* m, void* buf, size_t count, bool bf16, cudaStream_t s);
+// Asynchronous NCCL error check; on an error the communicator is aborted and
+// dropped, code 4.
+Status comm_poll(Mha* m);
+// cudaStreamSynchronize for synchronous calls of a layer with a communicator:
+// polls the stream and the communicator, aborts the communicator after
+// comm_timeout_ms, code 4 on either failure.
+Status comm_wait(Mha* m, cudaStream_t s, const char* what);
 void comm_release(Mha* m);
 
 // small device helpers (engine_kernels.cu)

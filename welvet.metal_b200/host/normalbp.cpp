@@ -321,6 +321,7 @@ welvet_status welvet_mha_normalbp_f32(int32_t batch, int32_t seq, int32_t d_mode
                                       const float* K, const float* V, const float* O, const float* x,
                                       const float* grad_or_target, int32_t use_target, double lr, float* pre,
                                       float* post, float* dX, float* dW, float* W_after, double* loss) {
+  wv::DeviceRestore restore_device;
   if (batch <= 0 || seq <= 0 || d_model <= 0 || num_heads <= 0 || !Q || !K || !V || !O || !x ||
       !grad_or_target || !pre || !post || !dX || !dW || !W_after || !loss) {
     welvet_status st{};

@@ -38,7 +38,7 @@ EXT_SYMBOLS = ("welvet_b200_mha_config_default", "welvet_b200_mha_mount", "welve
                "welvet_b200_profile_enable", "welvet_b200_profile_read",
                "welvet_b200_decode_attention_static", "welvet_b200_swiglu_mount", "welvet_b200_swiglu_forward",
                "welvet_b200_swiglu_forward_host", "welvet_b200_swiglu_release", "welvet_b200_norm_forward",
-               "welvet_b200_embedding_forward")
+               "welvet_b200_embedding_forward", "welvet_b200_wait_probe")
 PROFILE_SLOTS = ("gemm_qkv", "attn_prefill", "gemm_o", "attn_decode", "gemm_qkv_decode", "gemm_o_decode",
                  "allreduce", "other", "gemm_gate_up", "gemm_down", "norm", "embedding", "attn_bwd", "gemm_grad")
 
@@ -157,7 +157,9 @@ def lib():
     L.welvet_b200_profile_read.restype = None
     L.welvet_b200_decode_attention_static.argtypes = [cfgp, C.c_int32, C.c_int32, _vp, C.c_int32, _vp, _vp, _vp,
                                                       C.c_int32, _vp, _vp, C.c_int32, _vp]
-    for name in ("welvet_b200_mha_mount", "welvet_b200_mha_forward", "welvet_b200_mha_forward_rows",
+    L.welvet_b200_wait_probe.argtypes = [C.c_uint64, _vp]
+    for name in ("welvet_b200_wait_probe",
+"welvet_b200_mha_mount", "welvet_b200_mha_forward", "welvet_b200_mha_forward_rows",
                  "welvet_b200_mha_check",
                  "welvet_b200_kv_create", "welvet_b200_kv_fill", "welvet_b200_mha_prefill",
                  "welvet_b200_mha_decode", "welvet_b200_comm_unique_id", "welvet_b200_comm_attach",
@@ -509,6 +511,12 @@ def fill_synthetic(dst, seed, kind, a, offset=0, stream=None):
 
 def device_check():
     check(lib().welvet_b200_device_check())
+
+
+def wait_probe(limit_ns: int, stream=None):
+    """Launches the bounded-wait probe (a wait nothing satisfies, given up after
+    limit_ns); the timeout is reported by the next device_check()."""
+    check(lib().welvet_b200_wait_probe(limit_ns, _stream(stream)))
 
 
 def launch_count(reset: bool = False) -> int:
