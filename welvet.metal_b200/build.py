@@ -16,6 +16,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "lib", "libwelvet_b200.so")
+# the MHA wire tool (WVM1 / WMV1 readers, tools/welvet_dense_fwd.cpp), linked to LIB
+TOOL = os.path.join(HERE, "lib", "welvet_dense_fwd")
+TOOL_SRC = os.path.join(HERE, "tools", "welvet_dense_fwd.cpp")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC,-fvisibility=hidden",
@@ -36,6 +39,8 @@ def _headers():
         for ext in ("*.h", "*.hpp", "*.cuh"):
             hs += glob.glob(os.path.join(HERE, sub, ext))
     hs += glob.glob(os.path.join(ROOT, "include", "*.h"))
+    hs += glob.glob(os.path.join(ROOT, "include", "welvet", "*.hpp"))
+    hs += glob.glob(os.path.join(ROOT, "include", "welvet", "runtime", "*.hpp"))
     return hs
 
 
@@ -75,6 +80,13 @@ def build(verbose: bool = False, jobs: int | None = None) -> str:
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+    if not os.path.exists(TOOL) or os.path.getmtime(TOOL) < max(os.path.getmtime(LIB), os.path.getmtime(TOOL_SRC),
+                                                                newest_header):
+        cmd = [os.environ.get("CXX", "g++"), "-std=c++17", "-O2", f"-I{os.path.join(ROOT, 'include')}", TOOL_SRC,
+               "-o", TOOL, f"-L{os.path.dirname(LIB)}", "-lwelvet_b200", "-Wl,-rpath,$ORIGIN"]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"tool build failed:\n{r.stdout}\n{r.stderr}")
     return LIB
 
 
