@@ -74,6 +74,8 @@ WORKLOADS = {
     "rmsnorm": dict(B=16, T=4096, d=4096, kind="rmsnorm"),
     "layernorm": dict(B=16, T=4096, d=4096, kind="layernorm"),
     "embedding": dict(B=16, T=4096, d=4096, vocab=128256, kind="embedding"),
+    # FP8 row-scale / NF4 block-64 -> BF16 dequantisation (the extension weight formats)
+    "dequant": dict(n=1 << 30, kind="dequant"),
     # MHA NormalBP leaf (welvet_mha_normalbp_f32): forward + MSE + backward + SGD, FP32,
     # the reference's stream semantics, one call per step from host buffers
     "mha-nbp": dict(B=4, T=512, d=1024, H=16, kind="nbp"),
@@ -85,7 +87,6 @@ CODEC_STATS_FREE = (0, 1, 2, 3, 4, 5, 16, 24, 25)  # dtypes without a per-tensor
 METRIC = "MHA prefill tok/s (decode tok/s under 'decode'); % of roofline"
 METRIC_DECODE = "MHA decode tok/s; % of HBM roofline"
 SUB_WORKLOADS = ("cfg2", "cfg3", "cfg4-fp8", "cfg4-nf4")
-DEQUANT_WEIGHTS = 1 << 30  # per format: 1 GiB of FP8 codes, 0.5 GiB of NF4 codes, 2 GiB of BF16 out
 # FP32 prefill attention runs on the CUDA cores (attn_f32_kernel): its roofline is the FFMA peak
 FP32_ATTENTION_ON_TENSOR_CORES = False
 METRIC_CODEC = "FormatNone weight round trip GB/s (decode(encode(w)), dtypes 0-33)"
@@ -98,7 +99,7 @@ def workload_of(wname, args):
     """Shape of workload `wname`; --batch / --seq override the selected workload only."""
     w = dict(WORKLOADS[wname])
     own = wname == args.workload
-    if w["kind"] == "codec":
+    if w["kind"] in ("codec", "dequant"):
         w["n"] = (args.batch if own else 0) or w["n"]
         return w
     w["B"] = (args.batch if own else 0) or w["B"]
@@ -116,6 +117,10 @@ def workload(args):
 def workload_config_of(wname, args, world):
     """The `config` object of a JSON line, the same for both arms."""
     w = workload_of(wname, args)
+    if w["kind"] == "dequant":
+        return {"workload": f"dequant: FP8 row-scale and NF4 block-64 -> BF16 of {w['n']} weights each",
+                "global_batch": w["n"], "seq_len": 1, "parallelism": f"replicas x{world}",
+                "l2": "codes and outputs larger than L2"}
     if w["kind"] == "codec":
         return {"workload": f"codec: decode(encode(w)) of {w['n']} FP32 weights, FormatNone dtypes 0-33",
                 "global_batch": w["n"], "seq_len": 1, "parallelism": f"replicas x{world}",
@@ -141,8 +146,10 @@ def workload_config_of(wname, args, world):
         return {"workload": f"{wname}: decode B={B} context {T} d={d} H={H}x{hd} NK={NK} RoPE{prec}{fmt}",
                 "global_batch": B, "seq_len": 1, "context": T, "parallelism": f"tp{world} (heads {H // world}/GPU)",
                 "l2": "KV cache larger than L2 (%.1f GB)" % (2 * B * T * NK * hd * es / 1e9)}
+    out = "" if world == 1 else (", reduce-scatter output (rank r keeps its row slice of each chunk)"
+                                 if args.output == "reducescatter" else ", all-reduce output")
     return {"workload": f"{wname}: B={B} T={T} d={d} H={H}x{hd} NK={NK} causal RoPE{prec}{fmt}",
-            "global_batch": B, "seq_len": T, "parallelism": f"tp{world} (heads {H // world}/GPU)",
+            "global_batch": B, "seq_len": T, "parallelism": f"tp{world} (heads {H // world}/GPU){out}",
             "l2": "inputs larger than L2 (x is %.1f GB)" % (B * T * d * es / 1e9)}
 
 
@@ -940,6 +947,10 @@ def run_mha(args, wname, rank, world, local, primary=True):
         uid = [W.comm_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
         layer.attach_comm(uid[0], world, rank)
+        # output collective of the device-timed prefill: reduce-scatter (rank r keeps
+        # the r-th row slice of each chunk summed; half the NVLink bytes) unless
+        # --output allreduce; decode and the host-buffer e2e path all-reduce
+        layer.set_output_mode(1 if args.output == "reducescatter" else 0)
     stream = torch.cuda.current_stream()
     pk = peaks()
 
@@ -1020,7 +1031,22 @@ def run_mha(args, wname, rank, world, local, primary=True):
                 "flops_per_launch": flops_launch, "avg_launch_ms": avg_ms,
                 "launches_per_step": cnt / steps,
                 "kernel_ms_per_step": {k: prof[k][0] / steps for k in per_step},
+                "collective_ms_per_step": prof["allreduce"][0] / steps if world > 1 else 0.0,
+                "collective": ("reduce-scatter" if args.output == "reducescatter" else "all-reduce")
+                              if world > 1 else None,
                 "step_tflops": (pf + af) / world / (ms / 1e3) / 1e12}
+        if world > 1 and args.output == "reducescatter":
+            # the same step with the all-reduce output, for comparison (3 steps)
+            layer.set_output_mode(0)
+            layer.forward(B, T, x, None, post, stream=stream)
+            barrier()
+            ev0.record(stream)
+            for _ in range(3):
+                layer.forward(B, T, x, None, post, stream=stream)
+            ev1.record(stream)
+            barrier()
+            roof["allreduce_output_ms_per_step"] = max_over_ranks(ev0.elapsed_time(ev1) / 3)
+            layer.set_output_mode(1)
 
         if primary and not args.no_e2e:
             # With N ranks each holds its B/N sequences in host memory and receives the
@@ -1212,13 +1238,13 @@ def run_dequant(args, rank, world, local):
     """Standalone dequantisation of the extension weight formats to BF16 (the
     in-mainloop dequant's data path as a kernel of its own): FP8-E4M3 codes with one
     FP32 scale per row, and NF4 codes (two per byte) with one FP32 absmax per 64
-    weights, over DEQUANT_WEIGHTS weights each (inputs and outputs larger than L2).
+    weights, over 2^30 weights each by default (inputs and outputs larger than L2).
     HBM-bound: bytes = codes + scales read + BF16 written. Parity: the FP32 decode
     of the first 2^20 weights equals the oracle's decode bit for bit."""
     import torch
     import welvet_b200 as W
     wall0 = time.perf_counter()
-    n = DEQUANT_WEIGHTS
+    n = workload_of("dequant", args)["n"]
     cols = 4096
     rows = n // cols
     pk = peaks()
@@ -1301,6 +1327,8 @@ def main():
     ap.add_argument("--no-configs", action="store_true",
                     help="skip the cfg2/cfg3/cfg4/dequant sub-records of the default one-GPU line")
     ap.add_argument("--parity-tokens", type=int, default=1024)
+    ap.add_argument("--output", default="reducescatter", choices=["reducescatter", "allreduce"],
+                    help="output collective of the device-timed prefill at N > 1")
     args = ap.parse_args()
 
     rank = int(os.environ.get("RANK", "0"))
@@ -1321,6 +1349,16 @@ def main():
         return run_block(args, rank, world, local)
     if workload(args)["kind"] == "nbp":
         return run_nbp(args, rank, world, local)
+    if workload(args)["kind"] == "dequant":
+        rec = run_dequant(args, rank, world, local)
+        if rank == 0:
+            k8 = rec["kernels"]["fp8_rowscale"]
+            print(json.dumps(dict(rec, value=k8["value"], unit="GB/s", n_gpus=world, steps=args.steps,
+                                  warmup=args.warmup, ms_per_step=k8["ms_per_launch"], higher_is_better=True,
+                                  scaling="weak", vs_baseline=None, dtype="u8 codes -> bf16", data="synthetic",
+                                  config=workload_config(args, world), roofline=k8["roofline"],
+                                  gpu_launches=2 * args.steps, cpu_baseline=None, e2e=None)), flush=True)
+        return
     if world > 1:
         # NVLS (in-switch reduction) is off unless the caller sets it: on this pool's
         # 8-GPU boxes the 256 KB decode all-reduce took 31 ms with NVLS and 0.05 ms

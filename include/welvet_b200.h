@@ -76,6 +76,19 @@ WELVET_API welvet_status welvet_b200_mha_forward(welvet_b200_mha* layer, int32_t
 WELVET_API welvet_status welvet_b200_mha_forward_rows(welvet_b200_mha* layer, int32_t batch_local,
                                                       int32_t seq, const void* x, void* post);
 
+/* Output collective of welvet_b200_mha_forward with device buffers and a
+ * communicator of N ranks (no reference counterpart: the reference is
+ * single-device). mode 0 (default): all-reduce, every rank's post holds every
+ * summed row. mode 1: reduce-scatter, half the NVLink bytes: the forward runs the
+ * batch in chunks of whole sequences (4 chunks of ceil(batch/4) sequences when
+ * batch > 1 in per-sequence mode, else one chunk of all rows), each chunk's rows
+ * must divide by N, and rank r's post holds the summed rows [c0 + r*n/N,
+ * c0 + (r+1)*n/N) of each chunk (c0 its first row, n its rows); the other rows hold
+ * this rank's partial sums (a sequence-sharded output, as a sequence-parallel
+ * next layer consumes it). Host-buffer forwards and decode always all-reduce.
+ * Code 1 for another mode. */
+WELVET_API welvet_status welvet_b200_mha_set_output_mode(welvet_b200_mha* layer, int32_t mode);
+
 /* Reads and clears the device error word of the layer's device after a
  * synchronisation; code 4 with the kernel's reason when a device-side bounded wait
  * expired or a bound check failed. No reference counterpart. */

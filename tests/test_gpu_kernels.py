@@ -217,9 +217,10 @@ def test_codec_probe_values(torch_cuda):
         np.testing.assert_array_equal(out.cpu().numpy().view(np.uint32), g[key].view(np.uint32))
 
 
-def test_extension_formats_bitexact_against_oracle(torch_cuda):
+@pytest.mark.parametrize("rows,cols", [(96, 320), (7, 100), (64, 4096)])
+def test_extension_formats_bitexact_against_oracle(torch_cuda, rows, cols):
+    """(96, 320), (64, 4096): the vectorised decodes; (7, 100): the scalar ones."""
     torch = torch_cuda
-    rows, cols = 96, 320
     w = W.synthetic(rows * cols, 13, 1, 0.02).reshape(rows, cols)
     w[3, :] = 0.0  # all-zero row -> scale 1
     codes_o, scales_o, dec_o = O.fp8_rowscale(w)
@@ -234,8 +235,8 @@ def test_extension_formats_bitexact_against_oracle(torch_cuda):
     np.testing.assert_array_equal(scales.cpu().numpy(), scales_o)
     np.testing.assert_array_equal(dec.cpu().numpy(), dec_o)
     packed_o, amax_o, ndec_o = O.nf4_block(w, 64)
-    packed = torch.empty(w.size // 2, dtype=torch.uint8, device="cuda")
-    amax = torch.empty(w.size // 64, dtype=torch.float32, device="cuda")
+    packed = torch.empty((w.size + 1) // 2, dtype=torch.uint8, device="cuda")
+    amax = torch.empty((w.size + 63) // 64, dtype=torch.float32, device="cuda")
     W.nf4_block_encode(wd, packed, amax)
     ndec = torch.empty(w.size, dtype=torch.float32, device="cuda")
     W.nf4_block_decode(packed, amax, ndec)
@@ -243,6 +244,16 @@ def test_extension_formats_bitexact_against_oracle(torch_cuda):
     np.testing.assert_array_equal(packed.cpu().numpy(), packed_o)
     np.testing.assert_array_equal(amax.cpu().numpy(), amax_o)
     np.testing.assert_array_equal(ndec.cpu().numpy().reshape(rows, cols), ndec_o)
+    # BF16 outputs: each FP32 value rounded to nearest even
+    from conftest import bf16_round
+    db = torch.empty(rows, cols, dtype=torch.bfloat16, device="cuda")
+    W.fp8_rowscale_decode(codes, scales, db, out_bf16=1)
+    nb = torch.empty(w.size, dtype=torch.bfloat16, device="cuda")
+    W.nf4_block_decode(packed, amax, nb, out_bf16=1)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(db.float().cpu().numpy().view(np.uint32), bf16_round(dec_o).view(np.uint32))
+    np.testing.assert_array_equal(nb.float().cpu().numpy().reshape(rows, cols).view(np.uint32),
+                                  bf16_round(ndec_o).view(np.uint32))
 
 
 # ---------------------------------------------------------------- attention

@@ -43,6 +43,17 @@ def _worker(rank, world, port, out_dir, precision):
     for _ in range(2):  # the second call reuses the staging buffers and events
         layer.forward_rows(bl, T, xl, post)
     np.save(os.path.join(out_dir, f"rows{rank}.npy"), post.float().numpy())
+    # device buffers, reduce-scatter output: the batch runs in 4 chunks of 2
+    # sequences (256 rows); rank r keeps rows [c0 + 128 r, c0 + 128 (r + 1)) summed
+    layer.set_output_mode(1)
+    xd = x.cuda()
+    pd = torch.zeros(B * T, d, device="cuda", dtype=dt)
+    layer.forward(B, T, xd, None, pd)
+    torch.cuda.synchronize()
+    layer.check_device()
+    own = np.concatenate([pd[c0 + rank * 128:c0 + (rank + 1) * 128].float().cpu().numpy()
+                          for c0 in range(0, B * T, 256)])
+    np.save(os.path.join(out_dir, f"rs{rank}.npy"), own)
     if rank == 0:
         np.save(os.path.join(out_dir, "x.npy"), x.float().numpy())
     layer.close()
@@ -71,3 +82,7 @@ def test_forward_rows_two_ranks(tmp_path, precision):
     got = np.concatenate([np.load(tmp_path / f"rows{r}.npy") for r in range(2)])
     tol = 1e-4 if precision == 0 else 2e-2
     assert rel_err(got, want) < tol, rel_err(got, want)
+    for r in range(2):  # reduce-scatter output: each rank's row slices of each chunk
+        rows = np.concatenate([np.arange(c0 + r * 128, c0 + (r + 1) * 128) for c0 in range(0, B * T, 256)])
+        rs = np.load(tmp_path / f"rs{r}.npy")
+        assert rel_err(rs, want[rows]) < tol, (r, rel_err(rs, want[rows]))

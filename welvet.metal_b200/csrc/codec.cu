@@ -268,6 +268,82 @@ __global__ void nf4_block_encode_kernel(const float* w, int64_t n, uint8_t* pack
   }
 }
 
+// Vectorised decodes for the aligned shapes (FP8: cols % 16 == 0; NF4: n % 32 ==
+// 0): each step loads 16 code bytes (16 FP8 / 32 NF4 codes) with one scale, and
+// stores the decoded values as 16-byte vectors; loads and stores are streaming
+// (evict-first), two steps in flight per thread. Values are those of the scalar
+// kernels (the same products, each rounded to BF16 alone).
+__device__ __forceinline__ void store_decoded(void* out, int64_t first, const float* v, int count, bool bf16) {
+  if (bf16) {
+    uint4* o = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(out) + first);
+    for (int q = 0; q < count / 8; ++q) {
+      uint32_t w[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const __nv_bfloat162 h = __floats2bfloat162_rn(v[8 * q + 2 * j], v[8 * q + 2 * j + 1]);
+        w[j] = *reinterpret_cast<const uint32_t*>(&h);
+      }
+      __stcs(o + q, make_uint4(w[0], w[1], w[2], w[3]));
+    }
+  } else {
+    float4* o = reinterpret_cast<float4*>(static_cast<float*>(out) + first);
+    for (int q = 0; q < count / 4; ++q) __stcs(o + q, make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]));
+  }
+}
+
+template <bool BF16>
+__global__ void __launch_bounds__(256) fp8_rowscale_decode_vec_kernel(const uint4* codes, const float* scales,
+                                                                      uint32_t n16, uint32_t cols16, void* out) {
+  const uint32_t stride = gridDim.x * blockDim.x;
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += 2 * stride) {
+    const bool two = i + stride < n16;
+    const uint4 c0 = __ldcs(codes + i);
+    const uint4 c1 = two ? __ldcs(codes + i + stride) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      if (h == 1 && !two) break;
+      const uint32_t idx = h ? i + stride : i;
+      const uint4 c = h ? c1 : c0;
+      const float sc = __ldg(scales + idx / cols16);
+      const uint32_t w[4] = {c.x, c.y, c.z, c.w};
+      float v[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[j] = __fmul_rn(e4m3_decode((uint8_t)(w[j >> 2] >> (8 * (j & 3)))), sc);
+      store_decoded(out, (int64_t)idx * 16, v, 16, BF16);
+    }
+  }
+}
+
+template <bool BF16>
+__global__ void __launch_bounds__(256) nf4_block_decode_vec_kernel(const uint4* packed, const float* absmax,
+                                                                   uint32_t n32, void* out) {
+  __shared__ float lv[16];
+  if (threadIdx.x < 16) lv[threadIdx.x] = nf4_level(threadIdx.x);
+  __syncthreads();
+  const uint32_t stride = gridDim.x * blockDim.x;
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n32; i += 2 * stride) {
+    const bool two = i + stride < n32;
+    const uint4 c0 = __ldcs(packed + i);
+    const uint4 c1 = two ? __ldcs(packed + i + stride) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      if (h == 1 && !two) break;
+      const uint32_t idx = h ? i + stride : i;
+      const uint4 c = h ? c1 : c0;
+      const float am = __ldg(absmax + idx / 2);  // 32 codes of one 64-weight block
+      const uint32_t w[4] = {c.x, c.y, c.z, c.w};
+      float v[32];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {  // byte j: low nibble = even weight, high = odd
+        const uint32_t b = (w[j >> 2] >> (8 * (j & 3))) & 0xffu;
+        v[2 * j] = __fmul_rn(lv[b & 0xf], am);
+        v[2 * j + 1] = __fmul_rn(lv[b >> 4], am);
+      }
+      store_decoded(out, (int64_t)idx * 32, v, 32, BF16);
+    }
+  }
+}
+
 __global__ void nf4_block_decode_kernel(const uint8_t* packed, const float* absmax, int64_t n, void* out,
                                         int out_bf16) {
   GRID_STRIDE(i, n) {
@@ -425,6 +501,18 @@ cudaError_t fp8_rowscale_encode(const float* w, int rows, int cols, uint8_t* cod
 }
 cudaError_t fp8_rowscale_decode(const uint8_t* codes, const float* scales, int rows, int cols, void* out,
                                 int out_bf16, cudaStream_t s) {
+  const int64_t n = (int64_t)rows * cols;
+  if (cols % 16 == 0 && n / 16 < (int64_t{1} << 31) && reinterpret_cast<uintptr_t>(codes) % 16 == 0 &&
+      reinterpret_cast<uintptr_t>(out) % 16 == 0) {
+    const uint32_t n16 = (uint32_t)(n / 16);
+    if (out_bf16)
+      fp8_rowscale_decode_vec_kernel<true><<<grid_for(n16), 256, 0, s>>>(reinterpret_cast<const uint4*>(codes),
+                                                                          scales, n16, cols / 16, out);
+    else
+      fp8_rowscale_decode_vec_kernel<false><<<grid_for(n16), 256, 0, s>>>(reinterpret_cast<const uint4*>(codes),
+                                                                           scales, n16, cols / 16, out);
+    return cudaGetLastError();
+  }
   fp8_rowscale_decode_kernel<<<grid_for((int64_t)rows * cols), 256, 0, s>>>(codes, scales, rows, cols, out,
                                                                              out_bf16);
   return cudaGetLastError();
@@ -436,6 +524,17 @@ cudaError_t nf4_block_encode(const float* w, int64_t n, uint8_t* packed, float* 
 }
 cudaError_t nf4_block_decode(const uint8_t* packed, const float* absmax, int64_t n, void* out, int out_bf16,
                              cudaStream_t s) {
+  if (n % 32 == 0 && n / 32 < (int64_t{1} << 31) && reinterpret_cast<uintptr_t>(packed) % 16 == 0 &&
+      reinterpret_cast<uintptr_t>(out) % 16 == 0) {
+    const uint32_t n32 = (uint32_t)(n / 32);
+    if (out_bf16)
+      nf4_block_decode_vec_kernel<true><<<grid_for(n32), 256, 0, s>>>(reinterpret_cast<const uint4*>(packed),
+                                                                       absmax, n32, out);
+    else
+      nf4_block_decode_vec_kernel<false><<<grid_for(n32), 256, 0, s>>>(reinterpret_cast<const uint4*>(packed),
+                                                                        absmax, n32, out);
+    return cudaGetLastError();
+  }
   nf4_block_decode_kernel<<<grid_for(n), 256, 0, s>>>(packed, absmax, n, out, out_bf16);
   return cudaGetLastError();
 }

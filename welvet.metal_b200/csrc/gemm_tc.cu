@@ -54,6 +54,7 @@ template <> struct GT<kGemmNF4> {
 
 struct KParams {
   int M, N, K, m_tiles, n_tiles, num_tiles, k_blocks;
+  int gn;  // N-tiles per raster group (see tile_coords)
   void* out;
   int ldo, out_bf16;
   float* out_hi;
@@ -73,16 +74,19 @@ struct KParams {
   uint32_t* err;
 };
 
-// Grouped rasterisation: 8 M-tiles advance together across N so the A rows and
-// B columns a wave of CTAs touches stay L2-resident.
+// Grouped rasterisation over N: a panel of gn N-tiles of B (the weights: at most
+// ~48 MB, chosen on the host) is swept by every M-tile before the next panel, N
+// fastest within the panel. The panel stays L2-resident, so B is read from HBM once
+// and A once per panel (n_tiles / gn times); the CTAs of one wave share their A
+// tiles too. (Grouping 8 M-tiles across all of N instead re-read the whole weight
+// matrix once per 8 M-tiles: 3.2x the algorithmic bytes at the QKV shape.)
 __device__ __forceinline__ void tile_coords(int t, const KParams& p, int& mb, int& nb) {
-  constexpr int GM = 8;
-  const int group = GM * p.n_tiles;
+  const int group = p.gn * p.m_tiles;
   const int g = t / group, r = t % group;
-  const int first = g * GM;
-  const int gm = min(GM, p.m_tiles - first);
-  mb = first + r % gm;
-  nb = r / gm;
+  const int first = g * p.gn;
+  const int gn = min(p.gn, p.n_tiles - first);
+  nb = first + r % gn;
+  mb = r / gn;
 }
 
 __device__ __forceinline__ void store_vals(const KParams& p, int row, int col, const float* v,
@@ -579,6 +583,13 @@ template <int KIND> cudaError_t launch(const GemmArgs& g, cudaStream_t stream) {
   p.n_tiles = (g.N + T::BN - 1) / T::BN;
   p.num_tiles = p.m_tiles * p.n_tiles;
   p.k_blocks = (g.K + T::BK - 1) / T::BK;
+  {
+    // B bytes of one N-tile as stored in HBM (codes for FP8 / NF4, both TF32 parts)
+    const double b_elem = KIND == kGemmFP8 ? 1.0 : KIND == kGemmNF4 ? 0.5 : (double)(T::ELEM * T::NB);
+    const double panel = (double)T::BN * g.K * b_elem;
+    const int gn = (int)std::max(1.0, std::floor(48.0e6 / std::max(panel, 1.0)));
+    p.gn = std::min(p.n_tiles, gn);
+  }
   p.out = g.out;
   p.ldo = g.ldo;
   p.out_bf16 = g.out_bf16;

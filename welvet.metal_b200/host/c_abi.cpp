@@ -4,6 +4,7 @@
 #include <cstdio>
 #include <cstring>
 #include <memory>
+#include <mutex>
 #include <string>
 
 #include "engine.hpp"
@@ -170,6 +171,13 @@ welvet_status welvet_b200_mha_forward_rows(welvet_b200_mha* layer, int32_t batch
     return wv::to_c(Status::err(1, "mha: invalid argument"));
   const int batch = sharded ? batch_local * m->nranks : batch_local;
   return wv::to_c(wv::mha_forward(m, batch, seq, x, nullptr, post, false, nullptr, nullptr, sharded));
+}
+
+welvet_status welvet_b200_mha_set_output_mode(welvet_b200_mha* layer, int32_t mode) {
+  if (!layer || (mode != 0 && mode != 1)) return wv::to_c(Status::err(1, "mha: invalid output mode"));
+  std::lock_guard<std::mutex> lock(layer->m->mu);
+  layer->m->out_mode = mode;
+  return ok_status();
 }
 
 welvet_status welvet_b200_mha_check(welvet_b200_mha* layer) {

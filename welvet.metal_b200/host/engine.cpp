@@ -723,11 +723,21 @@ Status mha_forward(Mha* m, int batch, int seq, const void* x, void* pre, void* p
     return Status::ok();
   };
 
+  // Reduce-scatter output (device buffers): chunk rows split evenly over the ranks,
+  // rank r keeps the r-th slice of each chunk summed; other rows hold its partial.
+  const bool rs_out = m->comm && m->nranks > 1 && m->out_mode == 1 && on_device && !rows_io;
+  if (rs_out && ((int64_t)bc_max * seq % m->nranks || M % m->nranks ||
+                 (int64_t)(batch - (int64_t)(chunks - 1) * bc_max) * seq % m->nranks))
+    return Status::err(1, "mha: reduce-scatter output needs every chunk's rows divisible by the ranks");
+  auto reduce_out = [&](char* base, int64_t rows, cudaStream_t st) -> Status {
+    if (rs_out) return comm_reducescatter(m, base, (size_t)(rows / m->nranks) * dm, !f32, st);
+    return comm_allreduce(m, base, (size_t)rows * dm, !f32, st);
+  };
   if (chunks == 1) {
     WV_TRY(run_rows(0, batch));
     if (m->comm) {
       prof_begin(kProfAllReduce, s);
-      WV_TRY(comm_allreduce(m, postd, (size_t)M * dm, !f32, s));
+      WV_TRY(reduce_out(static_cast<char*>(postd), M, s));
       prof_end(kProfAllReduce, s);
     }
   } else {
@@ -790,7 +800,7 @@ Status mha_forward(Mha* m, int batch, int seq, const void* x, void* pre, void* p
       if (m->comm) {
         WV_CUDA(cudaStreamWaitEvent(m->comm_stream, m->chunk_done[i], 0), "wait");
         prof_begin(kProfAllReduce, m->comm_stream);
-        WV_TRY(comm_allreduce(m, static_cast<char*>(postd) + r0 * dm * es, (size_t)rows * dm, !f32, m->comm_stream));
+        WV_TRY(reduce_out(static_cast<char*>(postd) + r0 * dm * es, rows, m->comm_stream));
         prof_end(kProfAllReduce, m->comm_stream);
         if (host) {
           WV_CUDA(cudaEventRecord(m->io_ev[Mha::kMaxChunks + i], m->comm_stream), "event");

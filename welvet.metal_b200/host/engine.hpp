@@ -163,6 +163,9 @@ struct Mha {
   void* comm = nullptr;
   int nranks = 1, rank = 0;
   int64_t comm_timeout_ms = 300000;  // bound of init, enqueue and synchronous waits
+  // Output collective of a device-buffer forward with a communicator: 0 all-reduce
+  // (every rank holds every summed row), 1 reduce-scatter (see welvet_b200.h).
+  int out_mode = 0;
   cudaStream_t comm_stream = nullptr;
   static constexpr int kMaxChunks = 16;
   cudaEvent_t chunk_done[kMaxChunks] = {};

@@ -38,7 +38,7 @@ EXT_SYMBOLS = ("welvet_b200_mha_config_default", "welvet_b200_mha_mount", "welve
                "welvet_b200_profile_enable", "welvet_b200_profile_read",
                "welvet_b200_decode_attention_static", "welvet_b200_swiglu_mount", "welvet_b200_swiglu_forward",
                "welvet_b200_swiglu_forward_host", "welvet_b200_swiglu_release", "welvet_b200_norm_forward",
-               "welvet_b200_embedding_forward", "welvet_b200_wait_probe")
+               "welvet_b200_embedding_forward", "welvet_b200_wait_probe", "welvet_b200_mha_set_output_mode")
 PROFILE_SLOTS = ("gemm_qkv", "attn_prefill", "gemm_o", "attn_decode", "gemm_qkv_decode", "gemm_o_decode",
                  "allreduce", "other", "gemm_gate_up", "gemm_down", "norm", "embedding", "attn_bwd", "gemm_grad")
 
@@ -158,7 +158,8 @@ def lib():
     L.welvet_b200_decode_attention_static.argtypes = [cfgp, C.c_int32, C.c_int32, _vp, C.c_int32, _vp, _vp, _vp,
                                                       C.c_int32, _vp, _vp, C.c_int32, _vp]
     L.welvet_b200_wait_probe.argtypes = [C.c_uint64, _vp]
-    for name in ("welvet_b200_wait_probe",
+    L.welvet_b200_mha_set_output_mode.argtypes = [_vp, C.c_int32]
+    for name in ("welvet_b200_wait_probe", "welvet_b200_mha_set_output_mode",
 "welvet_b200_mha_mount", "welvet_b200_mha_forward", "welvet_b200_mha_forward_rows",
                  "welvet_b200_mha_check",
                  "welvet_b200_kv_create", "welvet_b200_kv_fill", "welvet_b200_mha_prefill",
@@ -419,6 +420,11 @@ class MhaLayer:
     def decode(self, kv: "KvCache", batch, x, pre, post, stream=None):
         check(lib().welvet_b200_mha_decode(self._h, kv.handle, batch, _ptr(x), _ptr(pre), _ptr(post),
                                            _on_device(x, pre, post), _stream(stream)))
+
+    def set_output_mode(self, mode: int):
+        """0: all-reduce output (default); 1: reduce-scatter, rank r keeps the r-th
+        row slice of each chunk summed (welvet_b200_mha_set_output_mode)."""
+        check(lib().welvet_b200_mha_set_output_mode(self._h, mode))
 
     def attach_comm(self, uid: bytes, nranks: int, rank: int):
         check(lib().welvet_b200_comm_attach(self._h, uid, nranks, rank))
