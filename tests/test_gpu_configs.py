@@ -120,7 +120,8 @@ def test_cfg4_quantised_full_shape(torch_cuda, weight_format):
     layer.close()
 
 
-def test_cfg5_heads_tensor_core_attention_at_8192(torch_cuda):
+@pytest.mark.parametrize("impl", [2, 3])  # single CTAs; CTA pairs (M = 256 UMMAs)
+def test_cfg5_heads_tensor_core_attention_at_8192(torch_cuda, impl):
     torch = torch_cuda
     T, H, hd = 8192, 2, 128
     cfg = W.MhaConfig.make(H * hd, H, H, precision=1, pos=1, seq_mode=1, max_seq_len=T)
@@ -129,7 +130,7 @@ def test_cfg5_heads_tensor_core_attention_at_8192(torch_cuda):
     k = torch.randn(T, H * hd, device="cuda", generator=g).to(torch.bfloat16)
     v = torch.randn(T, H * hd, device="cuda", generator=g).to(torch.bfloat16)
     out = torch.empty_like(q)
-    W.attention(cfg, 1, T, q, k, v, out, impl=2)
+    W.attention(cfg, 1, T, q, k, v, out, impl=impl)
     torch.cuda.synchronize()
     W.device_check()
     oc = O.MhaCfg(d_model=H * hd, num_heads=H, max_seq_len=T, pos=1, per_sequence=1)

@@ -310,3 +310,45 @@ def test_attention_against_oracle(torch_cuda, kw, B, T, precision, impl):
     W.device_check()
     tol = 1e-4 if precision == 0 else 2e-2
     assert rel_err(out.float().cpu().numpy(), ref) < tol
+
+
+# CTA-pair tensor-core attention (impl 3: clusters of two CTAs, M = 256 UMMAs;
+# head_dim 128, sequences of whole 256-query tile pairs): the masks, position
+# biases and score functions of the reference, GQA, stream semantics, against the
+# oracle on the same bf16-rounded inputs.
+PAIR_CASES = [
+    (dict(d_model=256, num_heads=2, seq_mode=1), 2, 512),                  # causal, 4 key blocks
+    (dict(d_model=1024, num_heads=8, num_kv_heads=2, seq_mode=1), 1, 1280),  # GQA, 10 key blocks
+    (dict(d_model=256, num_heads=2, seq_mode=1, mask=2), 1, 512),          # bidirectional
+    (dict(d_model=256, num_heads=2, seq_mode=1, mask=3, window=200, pos=2), 1, 768),  # window + ALiBi
+    (dict(d_model=256, num_heads=2, seq_mode=1, mask=3, window=130, window_causal=0, softmax=1), 1, 512),
+    (dict(d_model=256, num_heads=2, seq_mode=0, max_seq_len=1024, mask=4, prefix_len=300), 2, 256),  # stream
+    (dict(d_model=256, num_heads=2, seq_mode=1), 3, 256),                  # one pair per sequence
+]
+
+
+@pytest.mark.parametrize("kw,B,T", PAIR_CASES)
+def test_attention_cta_pairs_against_oracle(torch_cuda, kw, B, T):
+    torch = torch_cuda
+    kw = dict(kw)
+    cfg = W.MhaConfig.make(kw.pop("d_model"), kw.pop("num_heads"), kw.pop("num_kv_heads", 0), precision=1, **kw)
+    hd, nk = cfg.resolved()
+    assert hd == 128 and T % 256 == 0
+    qd, kd = cfg.num_heads * hd, nk * hd
+    M = B * T
+    q, k, v = (torch.from_numpy(W.synthetic(M * n, s, 1, 1.0).reshape(M, n)).to(torch.bfloat16)
+               for n, s in ((qd, 31), (kd, 32), (kd, 33)))
+    oc = O.MhaCfg(d_model=cfg.d_model, num_heads=cfg.num_heads, num_kv_heads=nk, head_dim=hd,
+                  max_seq_len=cfg.max_seq_len, mask=cfg.mask, pos=1 if cfg.pos == 0 else cfg.pos,
+                  softmax=cfg.softmax, window=cfg.window, prefix_len=cfg.prefix_len,
+                  window_causal=cfg.window_causal, per_sequence=cfg.seq_mode)
+    cfg.pos = oc.pos
+    ref = O.attention(oc, B, T, q.float().numpy(), k.float().numpy(), v.float().numpy())
+    out = torch.zeros(M, qd, device="cuda", dtype=torch.bfloat16)
+    W.attention(cfg, B, T, q.cuda(), k.cuda(), v.cuda(), out, impl=3)
+    torch.cuda.synchronize()
+    W.device_check()
+    got = out.float().cpu().numpy()
+    assert rel_err(got, ref) < 2e-2
+    # both CTAs of every pair: rows of the even and the odd query tiles
+    assert rel_err(got[:128], ref[:128]) < 2e-2 and rel_err(got[128:256], ref[128:256]) < 2e-2

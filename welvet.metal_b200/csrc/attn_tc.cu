@@ -26,6 +26,7 @@
 #include "kernels.h"
 
 #include <algorithm>
+#include <climits>
 
 namespace wv {
 namespace {
@@ -44,22 +45,33 @@ constexpr int kHighRegs = 224;
 static_assert(kLowRegs * 128 + kHighRegs * 256 <= kLaunchRegs * kThreads, "register split exceeds the pool");
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
+// Whether AttnArgs::pair = -1 (auto) picks the CTA-pair kernel where it applies.
+constexpr bool kPairDefault = false;
 
-template <int HD> struct FT {
+// PAIR: a cluster of two CTAs (head_dim 128) shares each 128-key block: every
+// UMMA is M = 256 (both CTAs' query tiles), issued by the leader CTA; CTA r holds
+// keys [64 r, 64 r + 64) of the K block and head-dim columns [64 r, 64 r + 64) of
+// the V block, so each SM stages and streams half of every K and V operand.
+template <int HD, bool PAIR = false> struct FT {
+  static_assert(!PAIR || HD == 128, "CTA pairs split head_dim into 128-byte halves");
   static constexpr int CH = HD / 64;            // 64-wide (128-byte) chunks of a row
   static constexpr int TILE = 128 * 128;        // bytes of a 128-row x 64-col bf16 chunk (16 KB)
   static constexpr int Q_BYTES = CH * TILE;
-  static constexpr int KV_BYTES = CH * TILE;    // one K or V block (128 keys)
-  static constexpr int SK = HD == 128 ? 3 : 4;  // ring depths
-  static constexpr int SV = HD == 128 ? 3 : 4;
+  static constexpr int K_ROWS = PAIR ? 64 : 128;   // keys of a K block held by this CTA
+  static constexpr int K_CHUNK = K_ROWS * 128;     // bytes of one 64-column chunk of them
+  static constexpr int K_BYTES = CH * K_CHUNK;
+  static constexpr int V_BYTES = PAIR ? TILE : CH * TILE;  // 128 keys x (head_dim / 2 in a pair)
+  static constexpr int SK = PAIR ? 4 : (HD == 128 ? 3 : 4);  // ring depths
+  static constexpr int SV = PAIR ? 4 : (HD == 128 ? 3 : 4);
   static constexpr int OFF_K = Q_BYTES;
-  static constexpr int OFF_V = OFF_K + SK * KV_BYTES;
+  static constexpr int OFF_V = OFF_K + SK * K_BYTES;
   // Final (max, sum) exchange, 2 x 256 floats, in K stage 0: every S MMA (the last
   // reader of K) has completed before the last PV, which the exchange waits for.
   static constexpr int OFF_EX = OFF_K;
-  static constexpr int OFF_BAR = OFF_V + SV * KV_BYTES;
+  static constexpr int OFF_BAR = OFF_V + SV * V_BYTES;
   static constexpr int SMEM = 1024 + OFF_BAR + 512;
   static_assert(SMEM <= 227 * 1024, "shared memory");
+  static_assert(K_BYTES >= 2048, "exchange area");
 };
 
 struct FParams {
@@ -143,11 +155,11 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
-template <int HD, bool ALIBI, bool SIGMOID>
+template <int HD, bool ALIBI, bool SIGMOID, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const FParams p) {
-  using F = FT<HD>;
+  using F = FT<HD, PAIR>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + F::OFF_BAR);
@@ -174,7 +186,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int q_row0 = b * p.seq + t0;                       // row in the Q matrix
   const int key_row_base = p.stream_mode ? 0 : b * p.seq;  // row of key position 0
   int lo, hi;
-  key_range(p, pos0 + t0, pos0 + t0 + rows_here - 1, kv_end, lo, hi);
+  // A pair runs the union of its two tiles' key ranges (tiles qt and qt - 1, leader
+  // first); keys outside a CTA's own range are masked in its softmax.
+  const bool leader = !PAIR || cluster_rank() == 0;
+  const int rank_in_pair = PAIR && !leader ? 1 : 0;
+  if (PAIR) {
+    const int qt_lead = p.nqt - 1 - (int)(blockIdx.x & ~1u);
+    key_range(p, pos0 + (qt_lead - 1) * kBQ, pos0 + min(p.seq, (qt_lead + 1) * kBQ) - 1, kv_end, lo, hi);
+  } else {
+    key_range(p, pos0 + t0, pos0 + t0 + rows_here - 1, kv_end, lo, hi);
+  }
   const int kb0 = (lo / kBK) * kBK;
   const int nblk = hi >= lo ? (hi - kb0) / kBK + 1 : 0;
 
@@ -191,7 +212,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 4);  // one arrival per warp of the warpgroup
+      // one arrival per warp of the warpgroup (in a pair: of both CTAs' warpgroups,
+      // on the leader's barrier)
+      mbar_init(&p_full[i], PAIR ? 8 : 4);
       mbar_init(&p_empty[i], 1);
     }
     mbar_init(fin_bar, kSoftThreads);
@@ -199,11 +222,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_barrier_init();
   }
   if (warp == 9) {
-    tmem_alloc(tmem_holder, 512);
-    tmem_relinquish();
+    if (PAIR) {
+      tmem_alloc_pair(tmem_holder, 512);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_holder, 512);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  // In a pair the other CTA's loads and arrivals target this CTA's barriers: both
+  // CTAs' barriers are initialised before either proceeds.
+  if (PAIR) cluster_sync();
+  else __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
   // TMEM columns: S_g at 128*g (fp32, 128 keys); O_g at 256 + HD*g.
@@ -214,15 +245,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0 && nblk > 0) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
-      mbar_arrive_expect_tx(q_full, F::Q_BYTES);
-      for (int c = 0; c < F::CH; ++c) tma_load_2d(smem + c * F::TILE, &tmQ, q_full, h * HD + c * 64, q_row0);
+      // In a pair the leader arms its barrier with both CTAs' bytes and both CTAs'
+      // loads complete on it.
+      if (leader) mbar_arrive_expect_tx(q_full, (PAIR ? 2 : 1) * F::Q_BYTES);
+      for (int c = 0; c < F::CH; ++c) {
+        if (PAIR) tma_load_2d_pair(smem + c * F::TILE, &tmQ, q_full, h * HD + c * 64, q_row0);
+        else tma_load_2d(smem + c * F::TILE, &tmQ, q_full, h * HD + c * 64, q_row0);
+      }
       for (int j = 0; j < nblk; ++j) {
         const int ks = j % F::SK;
         if (!mbar_wait(&k_empty[ks], ((j / F::SK) & 1) ^ 1, abort_flag, p.err, kErrWaitEmpty)) break;
-        mbar_arrive_expect_tx(&k_full[ks], F::KV_BYTES);
-        for (int c = 0; c < F::CH; ++c)
-          tma_load_2d(smem + F::OFF_K + ks * F::KV_BYTES + c * F::TILE, &tmK, &k_full[ks], kh * HD + c * 64,
-                      key_row_base + kb0 + j * kBK);
+        if (leader) mbar_arrive_expect_tx(&k_full[ks], (PAIR ? 2 : 1) * F::K_BYTES);
+        const int krow = key_row_base + kb0 + j * kBK + rank_in_pair * F::K_ROWS;
+        for (int c = 0; c < F::CH; ++c) {
+          uint8_t* dst = smem + F::OFF_K + ks * F::K_BYTES + c * F::K_CHUNK;
+          if (PAIR) tma_load_2d_pair(dst, &tmK, &k_full[ks], kh * HD + c * 64, krow);
+          else tma_load_2d(dst, &tmK, &k_full[ks], kh * HD + c * 64, krow);
+        }
       }
     }
   } else if (warp == 10) {
@@ -233,17 +272,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int i = 0; i < nblk; ++i) {
         const int vs = i % F::SV;
         if (!mbar_wait(&v_empty[vs], ((i / F::SV) & 1) ^ 1, abort_flag, p.err, kErrWaitEmpty)) break;
-        mbar_arrive_expect_tx(&v_full[vs], F::KV_BYTES);
-        for (int c = 0; c < F::CH; ++c)
-          tma_load_2d(smem + F::OFF_V + vs * F::KV_BYTES + c * F::TILE, &tmV, &v_full[vs], kh * HD + c * 64,
-                      key_row_base + kb0 + i * kBK);
+        if (leader) mbar_arrive_expect_tx(&v_full[vs], (PAIR ? 2 : 1) * F::V_BYTES);
+        uint8_t* dst = smem + F::OFF_V + vs * F::V_BYTES;
+        if (PAIR) {  // head-dim columns [64 r, 64 r + 64) of the block
+          tma_load_2d_pair(dst, &tmV, &v_full[vs], kh * HD + 64 * rank_in_pair, key_row_base + kb0 + i * kBK);
+        } else {
+          for (int c = 0; c < F::CH; ++c)
+            tma_load_2d(dst + c * F::TILE, &tmV, &v_full[vs], kh * HD + c * 64, key_row_base + kb0 + i * kBK);
+        }
       }
     }
   } else if (warp == 9) {
     // ---------------------------------------------------------- UMMA issuer
-    if (lane == 0 && nblk > 0) {
-      constexpr uint32_t IDESC_S = idesc_make(1, kBQ, kBK, 0, 0);
-      constexpr uint32_t IDESC_PV = idesc_make(1, kBQ, HD, 0, 1);
+    if (lane == 0 && nblk > 0 && leader) {
+      constexpr int MM = PAIR ? 2 * kBQ : kBQ;  // rows of one UMMA (both CTAs' tiles in a pair)
+      constexpr uint32_t IDESC_S = idesc_make(1, MM, kBK, 0, 0);
+      constexpr uint32_t IDESC_PV = idesc_make(1, MM, HD, 0, 1);
       const uint32_t q_base = smem_u32(smem);
       if (!mbar_wait(q_full, 0, abort_flag, p.err, kErrWaitFull)) goto done;
       // S_j into TMEM buffer j&1 (columns 128*(j&1)); its warpgroup reads S_j into
@@ -259,15 +303,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int ks = j % F::SK, g = j & 1;
         if (!mbar_wait(&k_full[ks], (j / F::SK) & 1, abort_flag, p.err, kErrWaitFull)) return false;
         tc_fence_after();
-        const uint32_t k_lo = sdesc_lo(smem_u32(smem + F::OFF_K + ks * F::KV_BYTES), 16);
+        const uint32_t k_lo = sdesc_lo(smem_u32(smem + F::OFF_K + ks * F::K_BYTES), 16);
         const uint32_t d = tmem + (uint32_t)(g * 128);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint32_t off = (uint32_t)(((kk >> 2) * F::TILE + (kk & 3) * 32) >> 4);
-          umma_f16_ss_lohi(d, q_lo + off, k_lo + off, DHI, IDESC_S, kk > 0);
+          const uint32_t a_off = (uint32_t)(((kk >> 2) * F::TILE + (kk & 3) * 32) >> 4);
+          const uint32_t b_off = (uint32_t)(((kk >> 2) * F::K_CHUNK + (kk & 3) * 32) >> 4);
+          if (PAIR) umma2_f16_ss_lohi(d, q_lo + a_off, k_lo + b_off, DHI, IDESC_S, kk > 0);
+          else umma_f16_ss_lohi(d, q_lo + a_off, k_lo + b_off, DHI, IDESC_S, kk > 0);
         }
-        umma_commit(&k_empty[ks]);
-        umma_commit(&s_full[g]);
+        if (PAIR) {
+          umma2_commit_both(&k_empty[ks]);
+          umma2_commit_both(&s_full[g]);
+        } else {
+          umma_commit(&k_empty[ks]);
+          umma_commit(&s_full[g]);
+        }
         return true;
       };
       auto issue_pv = [&](int i) -> bool {
@@ -275,19 +326,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(&p_full[g], (i >> 1) & 1, abort_flag, p.err, kErrWaitOther)) return false;
         if (!mbar_wait(&v_full[vs], (i / F::SV) & 1, abort_flag, p.err, kErrWaitFull)) return false;
         tc_fence_after();
-        const uint32_t v_lo = sdesc_lo(smem_u32(smem + F::OFF_V + vs * F::KV_BYTES), F::TILE);
+        const uint32_t v_lo = sdesc_lo(smem_u32(smem + F::OFF_V + vs * F::V_BYTES), F::TILE);
         const uint32_t d = tmem + (uint32_t)(256 + HD * g), pa = tmem + (uint32_t)(g * 128);
         const uint32_t acc0 = i >= 2 ? 1u : 0u;
 #pragma unroll
         for (int kk = 0; kk < kBK / 16; ++kk) {
           // A = P from TMEM: 16 keys = 8 columns of bf16 pairs. V is MN-major: 16
           // keys = 16 rows of 128 bytes; the second 64-column chunk of head_dim
-          // sits one TILE further (leading byte offset).
-          umma_f16_ts_lohi(d, pa + (uint32_t)(kk * 8), v_lo + (uint32_t)((kk * 16 * 128) >> 4), DHI, IDESC_PV,
-                           kk > 0 ? 1u : acc0);
+          // sits one TILE further (leading byte offset; in a pair each CTA holds
+          // one 64-column chunk, the other CTA's half of N).
+          const uint32_t b = v_lo + (uint32_t)((kk * 16 * 128) >> 4);
+          if (PAIR) umma2_f16_ts_lohi(d, pa + (uint32_t)(kk * 8), b, DHI, IDESC_PV, kk > 0 ? 1u : acc0);
+          else umma_f16_ts_lohi(d, pa + (uint32_t)(kk * 8), b, DHI, IDESC_PV, kk > 0 ? 1u : acc0);
         }
-        umma_commit(&v_empty[vs]);
-        umma_commit(&p_empty[g]);
+        if (PAIR) {
+          umma2_commit_both(&v_empty[vs]);
+          umma2_commit_both(&p_empty[g]);
+        } else {
+          umma_commit(&v_empty[vs]);
+          umma_commit(&p_empty[g]);
+        }
         return true;
       };
       for (int j = 0; j < min(2, nblk); ++j)
@@ -309,6 +367,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t s_col = (uint32_t)(128 * g), o_col = (uint32_t)(256 + HD * g);
     const float sl = p.scale_log2;
     const float slope2 = ALIBI ? exp2f(-(float)(p.head_base + h + 1) * 8.0f / (float)p.total_heads) * kLog2e : 0.f;
+    // The keys attn_allow admits for this row form one interval [row_lo, row_hi]
+    // (causal: [0, q]; sliding window: [q-w+1, q] or (q-w, q+w); prefix-LM:
+    // [0, max(q, prefix-1)] inside the prefix), cut at the end of the keys.
+    int row_lo = 0, row_hi = qpos;
+    if (p.mask == 2) {
+      row_hi = INT_MAX;
+    } else if (p.mask == 3) {
+      const int w = p.window > 0 ? p.window : p.msl;
+      row_lo = qpos - w + 1;
+      row_hi = p.window_causal ? qpos : qpos + w - 1;
+    } else if (p.mask == 4 && qpos < p.prefix) {
+      row_hi = max(qpos, p.prefix - 1);
+    }
+    row_hi = min(row_hi, kv_end - 1);
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     int jl = -1;  // last block processed by this warpgroup
@@ -327,9 +399,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 
       const int k0 = kb0 + j * kBK;
       const bool full = block_full(p, pos0 + t0, pos0 + t0 + kBQ - 1, k0, k0 + kBK - 1, kv_end);
-      // Fast path: unmasked block, no ALiBi, positive scale -> logits are s * sl and
-      // the max of the logits is sl * max(s).
-      const bool fast = full && !ALIBI && sl > 0.f;
+      // Fast path (no ALiBi, positive scale): logits are s * sl and the max of the
+      // logits is sl * max(s). A block that straddles the mask edge first sets the
+      // raw scores outside the row's interval to -inf (one compare and select per
+      // score; -inf * sl stays -inf) and then takes the same code as an unmasked
+      // block: a separate masked variant of the loops ran once per tile and paid
+      // for its instruction fetches every time (about 25k cycles against 2.3k).
+      const bool fast = !ALIBI && sl > 0.f;
+      if (fast && !full) {
+        const int lo_rel = row_lo - k0, hi_rel = row_hi - k0;
+#pragma unroll
+        for (int i = 0; i < 128; ++i)
+          if (i < lo_rel || i > hi_rel) s[i] = 0xff800000u;  // -inf
+      }
       float mx = -INFINITY;
       if (fast) {
         float m8[8];  // independent partial maxima (ILP), three-input max
@@ -433,7 +515,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[g]);
+      if (lane == 0) {
+        // the leader's issuer waits for P in both CTAs' TMEM
+        if (PAIR) mbar_arrive_leader(&p_full[g]);
+        else mbar_arrive(&p_full[g]);
+      }
       jl = j;
     }
     // ---- merge the two partial softmaxes; warpgroup g writes output columns
@@ -495,41 +581,61 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 done:
   tc_fence_before();
-  __syncthreads();
+  // In a pair neither CTA leaves (and frees shared memory or TMEM the leader's
+  // MMAs or the other CTA's loads and arrivals use) before both are done.
+  if (PAIR) cluster_sync();
+  else __syncthreads();
   if (warp == 9) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    if (PAIR) tmem_dealloc_pair(tmem, 512);
+    else tmem_dealloc(tmem, 512);
   }
 }
 
-template <int HD, bool ALIBI, bool SIGMOID>
+template <int HD, bool ALIBI, bool SIGMOID, bool PAIR>
 cudaError_t launch_variant(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const FParams& p,
                            dim3 grid, cudaStream_t s) {
-  using F = FT<HD>;
-  static const cudaError_t ready = []() {
-    cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel<HD, ALIBI, SIGMOID>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, F::SMEM);
+  using F = FT<HD, PAIR>;
+  auto kern = attn_fwd_kernel<HD, ALIBI, SIGMOID, PAIR>;
+  static const cudaError_t ready = [kern]() {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, F::SMEM);
     if (e != cudaSuccess) return e;
     // setmaxnreg.inc waits until the block's register pool can serve it: refuse to
     // launch unless the pool (launch registers x threads) covers the split.
     cudaFuncAttributes fa{};
-    e = cudaFuncGetAttributes(&fa, attn_fwd_kernel<HD, ALIBI, SIGMOID>);
+    e = cudaFuncGetAttributes(&fa, kern);
     if (e != cudaSuccess) return e;
     if (fa.numRegs * kThreads < kLowRegs * 128 + kHighRegs * 256) return cudaErrorNotSupported;
     return cudaSuccess;
   }();
   if (ready != cudaSuccess) return ready;
-  attn_fwd_kernel<HD, ALIBI, SIGMOID><<<grid, kThreads, F::SMEM, s>>>(mq, mk, mv, p);
-  return cudaGetLastError();
+  if (!PAIR) {
+    kern<<<grid, kThreads, F::SMEM, s>>>(mq, mk, mv, p);
+    return cudaGetLastError();
+  }
+  // CTA pairs: clusters of two consecutive query tiles of one (head, sequence)
+  cudaLaunchConfig_t lc{};
+  lc.gridDim = grid;
+  lc.blockDim = dim3(kThreads, 1, 1);
+  lc.dynamicSmemBytes = F::SMEM;
+  lc.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  lc.attrs = at;
+  lc.numAttrs = 1;
+  return cudaLaunchKernelEx(&lc, kern, mq, mk, mv, p);
 }
 
-template <int HD> cudaError_t launch(const AttnArgs& a, cudaStream_t s) {
+template <int HD, bool PAIR> cudaError_t launch(const AttnArgs& a, cudaStream_t s) {
   alignas(64) CUtensorMap mq, mk, mv;
   const int rows = a.batch * a.seq;
   const int qd = a.num_heads * HD, kd = a.num_kv_heads * HD;
   const int BF16 = (int)CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, SW = (int)CU_TENSOR_MAP_SWIZZLE_128B;
   if (!make_tma_2d(&mq, a.q, BF16, 2, qd, rows, a.ldq, 64, 128, SW) ||
-      !make_tma_2d(&mk, a.k, BF16, 2, kd, rows, a.ldk, 64, 128, SW) ||
+      !make_tma_2d(&mk, a.k, BF16, 2, kd, rows, a.ldk, 64, FT<HD, PAIR>::K_ROWS, SW) ||
       !make_tma_2d(&mv, a.v, BF16, 2, kd, rows, a.ldk, 64, 128, SW))
     return cudaErrorInvalidValue;
   FParams p{};
@@ -552,10 +658,10 @@ template <int HD> cudaError_t launch(const AttnArgs& a, cudaStream_t s) {
   p.err = a.err;
   dim3 grid(p.nqt, a.num_heads, a.batch);
   if (a.alibi)
-    return a.sigmoid ? launch_variant<HD, true, true>(mq, mk, mv, p, grid, s)
-                     : launch_variant<HD, true, false>(mq, mk, mv, p, grid, s);
-  return a.sigmoid ? launch_variant<HD, false, true>(mq, mk, mv, p, grid, s)
-                   : launch_variant<HD, false, false>(mq, mk, mv, p, grid, s);
+    return a.sigmoid ? launch_variant<HD, true, true, PAIR>(mq, mk, mv, p, grid, s)
+                     : launch_variant<HD, true, false, PAIR>(mq, mk, mv, p, grid, s);
+  return a.sigmoid ? launch_variant<HD, false, true, PAIR>(mq, mk, mv, p, grid, s)
+                   : launch_variant<HD, false, false, PAIR>(mq, mk, mv, p, grid, s);
 }
 
 } // namespace
@@ -573,9 +679,20 @@ bool attn_tc_supported(const AttnArgs& a) {
   return true;
 }
 
+bool attn_tc_pair_supported(const AttnArgs& a) {
+  // head_dim 128 (each CTA holds a 128-byte half of V's rows) and whole pairs of
+  // 128-query tiles per sequence
+  return attn_tc_supported(a) && a.head_dim == 128 && a.seq % (2 * kBQ) == 0;
+}
+
 cudaError_t attn_prefill_tc(const AttnArgs& a, cudaStream_t s) {
   if (!attn_tc_supported(a)) return cudaErrorInvalidValue;
-  return a.head_dim == 64 ? launch<64>(a, s) : launch<128>(a, s);
+  const bool pair = a.pair > 0 || (a.pair < 0 && kPairDefault && attn_tc_pair_supported(a));
+  if (pair) {
+    if (!attn_tc_pair_supported(a)) return cudaErrorInvalidValue;
+    return launch<128, true>(a, s);
+  }
+  return a.head_dim == 64 ? launch<64, false>(a, s) : launch<128, false>(a, s);
 }
 
 } // namespace wv

@@ -149,8 +149,10 @@ struct AttnArgs {
   float* out_lo = nullptr;
   uint32_t* err = nullptr;
   int sm_count = 148;
+  int pair = -1;                   // tensor-core kernel: 1 CTA pairs (M = 256 UMMAs), 0 single CTAs, -1 auto
 };
 bool attn_tc_supported(const AttnArgs& a);
+bool attn_tc_pair_supported(const AttnArgs& a);
 cudaError_t attn_prefill_tc(const AttnArgs& a, cudaStream_t s);
 cudaError_t attn_prefill_simt(const AttnArgs& a, cudaStream_t s);
 // FP32, head_dim 64/128, no ring wrap: register-tiled CUDA-core kernel (attn_f32.cu).

@@ -313,8 +313,15 @@ welvet_status welvet_b200_attention(const welvet_b200_mha_config* cfgp, int32_t 
   a.err = d->err;
   a.sm_count = d->sm_count;
   wv::count_launch();
+  if (impl == 3) {  // tensor-core kernel on CTA pairs (M = 256 UMMAs)
+    if (!wv::attn_tc_pair_supported(a))
+      return wv::to_c(Status::err(2, "attention: CTA-pair tensor-core kernel unsupported here"));
+    a.pair = 1;
+    return launch_status(wv::attn_prefill_tc(a, as_stream(stream)), "attn_prefill_tc (pairs)");
+  }
   if (impl == 2 || (impl == 0 && wv::attn_tc_supported(a))) {
     if (!wv::attn_tc_supported(a)) return wv::to_c(Status::err(2, "attention: tensor-core kernel unsupported here"));
+    if (impl == 2) a.pair = 0;
     return launch_status(wv::attn_prefill_tc(a, as_stream(stream)), "attn_prefill_tc");
   }
   return launch_status(wv::attn_prefill_simt(a, as_stream(stream)), "attn_prefill_simt");
