@@ -62,6 +62,9 @@ WORKLOADS = {
     "cfg5": dict(B=32, T=8192, d=4096, H=32, NK=32, wf=0, prec=1, kind="prefill+decode"),
     "cfg4-fp8": dict(B=4, T=4096, d=4096, H=32, NK=32, wf=1, prec=1, kind="prefill"),
     "cfg4-nf4": dict(B=4, T=4096, d=4096, H=32, NK=32, wf=2, prec=1, kind="prefill"),
+    # the reference's own FormatNone Int4 codes (per-tensor scale) kept resident and
+    # dequantised inside the GEMM mainloop (weight_format 3, dtype 14)
+    "cfg4-int4": dict(B=4, T=4096, d=4096, H=32, NK=32, wf=3, dt=14, prec=1, kind="prefill"),
     "cfg3": dict(B=64, T=4096, d=2048, H=32, NK=8, wf=0, prec=1, kind="decode"),
     "cfg2": dict(B=8, T=2048, d=1024, H=16, NK=16, wf=0, prec=0, kind="prefill"),
     # FormatNone weight round trip (mount-time encode -> decode), all dtypes 0-33
@@ -86,7 +89,7 @@ CODEC_STATS_FREE = (0, 1, 2, 3, 4, 5, 16, 24, 25)  # dtypes without a per-tensor
 
 METRIC = "MHA prefill tok/s (decode tok/s under 'decode'); % of roofline"
 METRIC_DECODE = "MHA decode tok/s; % of HBM roofline"
-SUB_WORKLOADS = ("cfg2", "cfg3", "cfg4-fp8", "cfg4-nf4")
+SUB_WORKLOADS = ("cfg2", "cfg3", "cfg4-fp8", "cfg4-nf4", "cfg4-int4")
 # FP32 prefill attention runs on the CUDA cores (attn_f32_kernel): its roofline is the FFMA peak
 FP32_ATTENTION_ON_TENSOR_CORES = False
 METRIC_CODEC = "FormatNone weight round trip GB/s (decode(encode(w)), dtypes 0-33)"
@@ -139,7 +142,7 @@ def workload_config_of(wname, args, world):
                 "parallelism": f"replicas x{world}", "l2": "activations larger than L2 (x is %.2f GB)"
                 % (B * T * d * (2 if w["kind"] == "swiglu" else 4) / 1e9)}
     B, T, d, H, NK, hd, wf = w["B"], w["T"], w["d"], w["H"], w["NK"], w["hd"], w["wf"]
-    fmt = " fp8 weights" if wf == 1 else " nf4 weights" if wf == 2 else ""
+    fmt = {1: " fp8 weights", 2: " nf4 weights", 3: f" FormatNone dtype {w.get('dt')} code weights"}.get(wf, "")
     es = 2 if w["prec"] == 1 else 4
     prec = " BF16" if w["prec"] == 1 else " FP32"
     if w["kind"] == "decode":
@@ -882,10 +885,13 @@ def bf16_round(a):
     return r.astype(np.uint32).view(np.float32).reshape(a.shape)
 
 
-def oracle_weights(O, host_ws, wf, prec):
+def oracle_weights(O, host_ws, wf, prec, dt=1):
     """The dequantised weights the device layer computes with (the parity checker's
     inputs): FP32 as given (3xTF32 splits are exact), BF16 rounded, FP8 row-scale or
-    NF4 block-64 decoded by the oracle's codecs."""
+    NF4 block-64 decoded by the oracle's codecs, or the FormatNone decode(encode)
+    of dtype dt (weight_format 3)."""
+    if wf == 3:
+        return [O.roundtrip(dt, w).reshape(w.shape) for w in host_ws]
     if wf == 1:
         return [O.fp8_rowscale(w)[2] for w in host_ws]
     if wf == 2:
@@ -940,7 +946,7 @@ def run_mha(args, wname, rank, world, local, primary=True):
         ws.append(t)
     torch.cuda.synchronize()
     host_ws = [t.cpu().numpy() for t in ws] if (check_parity or (primary and not args.no_cpu)) else None
-    layer = W.MhaLayer(cfg, *ws, dtype=1)
+    layer = W.MhaLayer(cfg, *ws, dtype=w.get("dt", 1))
     del ws
     torch.cuda.empty_cache()
     if world > 1:
@@ -1096,7 +1102,7 @@ def run_mha(args, wname, rank, world, local, primary=True):
             import oracle_py as O
             oc = O.MhaCfg(d_model=d, num_heads=H, num_kv_heads=NK, max_seq_len=n_oracle, per_sequence=1)
             t0 = time.perf_counter()
-            rpre, rpost = O.mha_forward(oc, 1, n_oracle, *oracle_weights(O, host_ws, wf, prec), x_rows)
+            rpre, rpost = O.mha_forward(oc, 1, n_oracle, *oracle_weights(O, host_ws, wf, prec, w.get("dt", 1)), x_rows)
             dt = time.perf_counter() - t0
             if check_parity:
                 want = {"post": rpost}
@@ -1144,7 +1150,7 @@ def run_mha(args, wname, rank, world, local, primary=True):
                     oc = O.MhaCfg(d_model=d, num_heads=H, num_kv_heads=NK, max_seq_len=T + 1, per_sequence=1)
                     _, rpost, _, _ = O.mha_decode(oc, [T] * len(sel), kc[sel].float().cpu().numpy(),
                                                   vc[sel].float().cpu().numpy(),
-                                                  *oracle_weights(O, host_ws, wf, prec),
+                                                  *oracle_weights(O, host_ws, wf, prec, w.get("dt", 1)),
                                                   xd[sel].float().cpu().numpy())
                     dparity = parity_record({"post": pd[sel].float().cpu().numpy()}, {"post": rpost},
                                             1e-4 if prec == 0 else 2e-2,

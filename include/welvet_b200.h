@@ -30,7 +30,9 @@ typedef struct welvet_b200_mha_config {
   int32_t precision;     /* 0 FP32 activations (3xTF32 tensor cores), 1 BF16 */
   int32_t weight_format; /* precision 1 only: 0 BF16 (from the decoded dtype), 1 FP8-E4M3 with
                             one FP32 scale per output channel, 2 NF4 with one FP32 absmax per
-                            64 weights */
+                            64 weights, 3 the reference's FormatNone codes of the mount's dtype
+                            kept resident (Int8 9, Int4 14 or FP4 16; per-tensor scale) and
+                            dequantised inside the GEMM mainloop */
   int32_t head_begin, head_count; /* this rank's query heads; head_count 0 = all heads */
   int32_t device;                 /* CUDA ordinal; -1 = current device */
 } welvet_b200_mha_config;
@@ -139,7 +141,11 @@ WELVET_API welvet_status welvet_b200_comm_attach(welvet_b200_mha* layer, const u
  * gives +-0; below 2^-6/448 of the row's absmax) and 0x7f/0xff are not accepted
  * (neither encoder emits them); a mounted layer normalises its codes so that its
  * dequantised weights equal the reference decoder's exactly; kind 3: A bf16, B NF4
- * packed [N, K/2] with b_scale [N, K/64]. */
+ * packed [N, K/2] with b_scale [N, K/64]; kinds 4 / 5 / 6: A bf16, B the
+ * reference's FormatNone Int8 codes [N, K] / Int4 codes [N, K/2] / FP4 (E2M1) codes
+ * [N, K/2] (src/weights/native_codec.cpp pack_native, two per byte low nibble first)
+ * dequantised in shared memory inside the mainloop, b_scale [N] the per-row scale
+ * applied in the epilogue (may be NULL for FP4). */
 WELVET_API welvet_status welvet_b200_gemm(int32_t kind, int32_t M, int32_t N, int32_t K,
                                           const void* a, const void* a_lo, const void* b,
                                           const void* b_lo, const float* b_scale, void* out,
@@ -159,7 +165,8 @@ WELVET_API welvet_status welvet_b200_attention(const welvet_b200_mha_config* cfg
  * (src/core/float_codecs.cpp, src/weights/native_codec.cpp:189-813):
  * roundtrip: out = decode(encode(w)) for any FormatNone dtype 0-33 (per-tensor
  * absmax / min / max computed on the device; out may equal w); encode/decode: the
- * stored bytes of dtypes 0-5 and 26 (nf4 scale = absmax). */
+ * stored bytes of dtypes 0-5 and 26 (nf4 scale = absmax); encode also dtypes 9, 14
+ * and 16 (Int8 / Int4 / FP4 bytes, the per-tensor scale to scale_out[0]). */
 WELVET_API welvet_status welvet_b200_codec_roundtrip(int32_t dtype, const float* w, float* out,
                                                      int64_t n, void* stream);
 WELVET_API welvet_status welvet_b200_codec_encode(int32_t dtype, const float* w, void* codes,

@@ -352,3 +352,59 @@ def test_attention_cta_pairs_against_oracle(torch_cuda, kw, B, T):
     assert rel_err(got, ref) < 2e-2
     # both CTAs of every pair: rows of the even and the odd query tiles
     assert rel_err(got[:128], ref[:128]) < 2e-2 and rel_err(got[128:256], ref[128:256]) < 2e-2
+
+
+# FormatNone codes dequantised inside the GEMM mainloop (kinds 4 Int8, 5 Int4, 6 FP4):
+# every code value, two's-complement Int4 nibbles and the E2M1 levels of the
+# reference's kFp4 table (float_codecs.cpp:184), low nibble first, with a per-row
+# epilogue scale, against an FP64 product of the decoded weights.
+FP4_LEVELS = np.array([0, 0.5, 1, 1.5, 2, 3, 4, 6, -0.0, -0.5, -1, -1.5, -2, -3, -4, -6], np.float32)
+
+
+@pytest.mark.parametrize("kind", [4, 5, 6])
+def test_gemm_formatnone_code_weights(torch_cuda, kind):
+    torch = torch_cuda
+    M, N, K = 700, 512, 1024
+    rng = np.random.default_rng(kind)
+    scale = (rng.random(N).astype(np.float32) + 0.5) * np.float32(0.01)
+    if kind == 4:
+        q = rng.integers(-128, 128, size=(N, K)).astype(np.int8)
+        codes, dec = q.view(np.uint8), q.astype(np.float32) * scale[:, None]
+    else:
+        nib = rng.integers(0, 16, size=(N, K)).astype(np.uint8)
+        codes = (nib[:, 0::2] | (nib[:, 1::2] << 4)).astype(np.uint8)
+        lv = np.where(nib < 8, nib, nib.astype(np.int16) - 16).astype(np.float32) if kind == 5 else FP4_LEVELS[nib]
+        if kind == 6:
+            scale[:] = 1.0
+        dec = lv * scale[:, None]
+    x = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+    out = torch.empty(M, N, device="cuda", dtype=torch.float32)
+    W.gemm(kind, M, N, K, x, _dev(torch, np.ascontiguousarray(codes)), out, b_scale=_dev(torch, scale))
+    torch.cuda.synchronize()
+    W.device_check()
+    ref = x.double() @ _dev(torch, dec.astype(np.float32)).double().T
+    # codes are exact in BF16 and the scale is applied once in FP32
+    assert rel_err(out.cpu().numpy(), ref.cpu().numpy()) < 1e-5
+
+
+@pytest.mark.parametrize("dtype", [9, 14, 16])
+def test_formatnone_code_encoder_bitexact_against_reference(torch_cuda, dtype):
+    """The device encoder of the resident Int8 / Int4 / FP4 codes gives the
+    reference's own pack_native bytes and scale (oracle/_ref, the reference's
+    WeightStore compiled for the CPU), on a tensor with ties, zeros and extremes."""
+    torch = torch_cuda
+    if not O.ref_available():
+        pytest.skip("oracle/_ref (the reference compiled for the CPU) not built")
+    rows, cols = 64, 1000
+    w = W.synthetic(rows * cols, 15, 1, 0.7 if dtype == 16 else 0.02).reshape(rows, cols)
+    w[0, :8] = [0.0, -0.0, 1e-9, -1e-9, 0.25, -0.75, 7.0, -9.0]  # zeros, FP4 midpoints and clamps
+    code, msg, native, scale, _ = O.ref_weight_roundtrip(dtype, w)
+    assert code == 0, msg
+    n = w.size
+    codes = torch.empty(n if dtype == 9 else (n + 1) // 2, device="cuda", dtype=torch.uint8)
+    sc = torch.empty(1, device="cuda", dtype=torch.float32)
+    W.codec_encode(dtype, _dev(torch, w.reshape(-1)), codes, sc)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(codes.cpu().numpy(), native[:codes.numel()])
+    if dtype != 16:
+        assert sc.item() == np.float32(scale)

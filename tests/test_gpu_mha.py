@@ -296,3 +296,34 @@ def test_forward_rows_one_rank_equals_host_forward(torch_cuda, precision):
     plain.forward(B, T, x, None, want)
     rows.forward_rows(B, T, x, got)
     assert torch.equal(want, got)
+
+
+@pytest.mark.parametrize("dtype", [9, 14, 16])  # Int8, Int4, FP4 codes resident (weight_format 3)
+def test_resident_formatnone_code_layer(torch_cuda, dtype):
+    """The reference's FormatNone codes kept resident and dequantised inside the
+    GEMM mainloop, against the oracle on the reference-decoded weights of the same
+    dtype (decode(encode(w)), per tensor) and the same bf16 inputs; GQA head shard."""
+    torch = torch_cuda
+    d, H, NK, B, T = 512, 8, 2, 2, 160
+    cfg = W.MhaConfig.make(d, H, NK, precision=1, weight_format=3, seq_mode=1)
+    hd, nk = cfg.resolved()
+    Ws = W.xavier_weights(d, H * hd, nk * hd, seed=0)
+    if dtype == 16:
+        Ws = [w * np.float32(8.0) for w in Ws]  # FP4 has no scale: use its range
+    layer = W.MhaLayer(cfg, *Ws, dtype=dtype)
+    # (FP4 weights are 8x larger: the input is 8x smaller so that the logits, and
+    # with them the softmax's sensitivity to the BF16 rounding of q and k, stay as
+    # for the other dtypes)
+    x = W.synthetic(B * T * d, 1, 1, 0.125 if dtype == 16 else 1.0).reshape(B * T, d)
+    xb = torch.from_numpy(x).cuda().to(torch.bfloat16)
+    pre = torch.zeros(B * T, H * hd, device="cuda", dtype=torch.bfloat16)
+    post = torch.zeros(B * T, d, device="cuda", dtype=torch.bfloat16)
+    layer.forward(B, T, xb, pre, post)
+    torch.cuda.synchronize()
+    layer.check_device()
+    oc = O.MhaCfg(d_model=d, num_heads=H, num_kv_heads=nk, per_sequence=1)
+    deq = [O.roundtrip(dtype, w).reshape(w.shape) for w in Ws]
+    rpre, rpost = O.mha_forward(oc, B, T, *deq, xb.float().cpu().numpy())
+    assert rel_err(pre.float().cpu().numpy(), rpre) < LOW_TOL
+    assert rel_err(post.float().cpu().numpy(), rpost) < LOW_TOL
+    layer.close()

@@ -517,6 +517,56 @@ cudaError_t fp8_rowscale_decode(const uint8_t* codes, const float* scales, int r
                                                                              out_bf16);
   return cudaGetLastError();
 }
+// FormatNone codes of the reference quantisers kept resident for the dequantising
+// GEMM (native_codec.cpp pack_native :189-560): Int8 (one byte, q = clamp(round(w /
+// s), -128, 127), s = absmax / 127), Int4 (two per byte, low nibble first, s =
+// absmax / 7, q in [-8, 7]) and FP4 (E2M1 code of fp4_roundtrip's value, no scale);
+// the same float arithmetic as rt_signed / fp4_roundtrip, so code * scale is the
+// reference's decoded weight. row_scale[r] = s for each of the n / cols rows (1 for
+// FP4). stats = [absmax, min, max] of w (stats_f32).
+__global__ void fn_codes_kernel(int dtype, const float* w, int64_t n, int cols, const float* stats, uint8_t* codes,
+                                float* row_scale) {
+  const int max_q = dtype == 9 ? 127 : 7;
+  float sc = 1.f;
+  if (dtype != 16) {
+    sc = rn_div(stats[0], (float)max_q);
+    if (sc == 0.f) sc = 1.f;
+  }
+  auto code_of = [&](float x) -> uint32_t {
+    if (dtype == 16) {
+      const float r = fp4_roundtrip(x);
+      const float m = fabsf(r);
+      const uint32_t c = m < 0.25f ? 0u : m < 0.75f ? 1u : m < 1.25f ? 2u : m < 1.75f ? 3u
+                       : m < 2.5f ? 4u : m < 3.5f ? 5u : m < 5.f ? 6u : 7u;
+      return (r < 0.f ? 8u : 0u) | c;
+    }
+    int q = (int)roundf(rn_div(x, sc));
+    q = q > max_q ? max_q : (q < -max_q - 1 ? -max_q - 1 : q);
+    return (uint32_t)q & (dtype == 9 ? 0xffu : 0xfu);
+  };
+  const int64_t nb = dtype == 9 ? n : (n + 1) / 2;  // code bytes
+  GRID_STRIDE(i, nb) {
+    if (dtype == 9) {
+      codes[i] = (uint8_t)code_of(w[i]);
+    } else {
+      const uint32_t lo = code_of(w[2 * i]);
+      const uint32_t hi = 2 * i + 1 < n ? code_of(w[2 * i + 1]) : 0u;
+      codes[i] = (uint8_t)(lo | (hi << 4));
+    }
+    const int64_t e0 = dtype == 9 ? i : 2 * i;
+    if (e0 % cols == 0) row_scale[e0 / cols] = sc;
+    if (dtype != 9 && (e0 + 1) % cols == 0 && e0 + 1 < n) row_scale[(e0 + 1) / cols] = sc;
+  }
+}
+
+cudaError_t formatnone_codes_encode(int dtype, const float* w, int64_t n, int cols, const float* stats,
+                                    uint8_t* codes, float* row_scale, cudaStream_t s) {
+  if (dtype != 9 && dtype != 14 && dtype != 16) return cudaErrorInvalidValue;
+  fn_codes_kernel<<<grid_for(dtype == 9 ? n : (n + 1) / 2), 256, 0, s>>>(dtype, w, n, cols, stats, codes,
+                                                                       row_scale);
+  return cudaGetLastError();
+}
+
 cudaError_t nf4_block_encode(const float* w, int64_t n, uint8_t* packed, float* absmax, cudaStream_t s) {
   const int64_t blocks = (n + 63) / 64;
   nf4_block_encode_kernel<<<(int)((blocks + 7) / 8), 256, 0, s>>>(w, n, packed, absmax);

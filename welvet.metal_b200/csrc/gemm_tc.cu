@@ -51,6 +51,21 @@ template <> struct GT<kGemmNF4> {
   static constexpr int CODE_BYTES = 256 * 32;  // two codes per byte
   static constexpr int THREADS = 704;  // 16 dequantisation warps (NF4 conversion is longer)
 };
+// FormatNone Int8 codes take FP8's layout and warp count; Int4 / FP4 take NF4's.
+template <> struct GT<kGemmI8> : GT<kGemmFP8> {};
+template <> struct GT<kGemmI4> : GT<kGemmNF4> {};
+template <> struct GT<kGemmFP4> : GT<kGemmNF4> {};
+template <int KIND> __host__ __device__ constexpr bool byte_codes() { return KIND == kGemmFP8 || KIND == kGemmI8; }
+template <int KIND> __host__ __device__ constexpr bool nibble_codes() { return KIND == kGemmNF4 || KIND == kGemmI4 || KIND == kGemmFP4; }
+// The 16 BF16-exact values a nibble code stands for (before the epilogue scale).
+__device__ __forceinline__ float nibble_level(int kind, int c) {
+  if (kind == kGemmI4) return (float)(c < 8 ? c : c - 16);                // Int4: two's complement
+  if (kind == kGemmFP4) {                                                // FP4 E2M1 (float_codecs.cpp:184)
+    const float mag[8] = {0.f, 0.5f, 1.f, 1.5f, 2.f, 3.f, 4.f, 6.f};
+    return c < 8 ? mag[c] : -mag[c - 8];
+  }
+  return nf4_level(c);
+}
 
 struct KParams {
   int M, N, K, m_tiles, n_tiles, num_tiles, k_blocks;
@@ -301,7 +316,7 @@ __global__ void __launch_bounds__(GT<KIND>::THREADS, 1)
           if constexpr (T::NA == 2) tma_load_2d(sb + A_BYTES, &tmA2, &full[stage], kb * BK, mb * kBM);
           if constexpr (XFORM) {
             // Codes for (BN rows) x (64 k): fp8 64 bytes/row, nf4 32 bytes/row.
-            constexpr int kx = (KIND == kGemmFP8) ? BK : BK / 2;
+            constexpr int kx = byte_codes<KIND>() ? BK : BK / 2;
             tma_load_2d(sb + T::NA * A_BYTES + B_BYTES, &tmB, &full[stage], kb * kx, nb * BN);
           } else {
             tma_load_2d(sb + T::NA * A_BYTES, &tmB, &full[stage], kb * BK, nb * BN);
@@ -393,10 +408,10 @@ __global__ void __launch_bounds__(GT<KIND>::THREADS, 1)
     // high bytes, four levels per register), so a level lookup is a byte permute
     // instead of a shared-memory load.
     uint32_t lvl_lo[4] = {0, 0, 0, 0}, lvl_hi[4] = {0, 0, 0, 0};
-    if constexpr (KIND == kGemmNF4) {
+    if constexpr (nibble_codes<KIND>()) {
 #pragma unroll
       for (int c = 0; c < 16; ++c) {
-        const uint32_t h = pack_bf16x2(nf4_level(c), 0.f) & 0xffffu;
+        const uint32_t h = pack_bf16x2(nibble_level(KIND, c), 0.f) & 0xffffu;
         lvl_lo[c >> 2] |= (h & 0xffu) << (8 * (c & 3));
         lvl_hi[c >> 2] |= (h >> 8) << (8 * (c & 3));
       }
@@ -425,12 +440,12 @@ __global__ void __launch_bounds__(GT<KIND>::THREADS, 1)
         // All codes of this thread's rows are loaded before any converted chunk is
         // stored: the stores may alias the loads as far as the compiler knows, so
         // interleaving them would serialise every row on the shared-memory latency.
-        using CodeT = typename std::conditional<KIND == kGemmFP8, uint2, uint32_t>::type;
+        using CodeT = typename std::conditional<byte_codes<KIND>(), uint2, uint32_t>::type;
         CodeT cw[RPT];
 #pragma unroll
         for (int j = 0; j < RPT; ++j)
-          cw[j] = *reinterpret_cast<const CodeT*>(codes + (r0 + RS * j) * (KIND == kGemmFP8 ? 64 : 32) +
-                                                  ch * (KIND == kGemmFP8 ? 8 : 4));
+          cw[j] = *reinterpret_cast<const CodeT*>(codes + (r0 + RS * j) * (byte_codes<KIND>() ? 64 : 32) +
+                                                  ch * (byte_codes<KIND>() ? 8 : 4));
         // Converted chunks are held in registers and stored after the last
         // conversion: both conversions are register-only (no shared-memory loads),
         // so the stores leave as one burst.
@@ -453,6 +468,18 @@ __global__ void __launch_bounds__(GT<KIND>::THREADS, 1)
                   : "=f"(lo), "=f"(hi) : "r"(h2));
               w[j][e] = pack_bf16x2(lo, hi);
             }
+          } else if constexpr (KIND == kGemmI8) {
+            // Int8 codes are exact in BF16: each byte becomes the float 2^23 + (b ^
+            // 0x80) by a byte permute under the exponent of 2^23, minus 2^23 + 128
+            // (one packed f32x2 add per pair), then one RN pack (exact) per pair.
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const uint32_t word = (e < 2 ? cw[j].x : cw[j].y) ^ 0x80808080u;
+              const int b0 = 2 * (e & 1);
+              const float lo = __uint_as_float(__byte_perm(word, 0x4B000000u, 0x7540u + b0)) - 8388736.0f;
+              const float hi = __uint_as_float(__byte_perm(word, 0x4B000000u, 0x7541u + b0)) - 8388736.0f;
+              w[j][e] = pack_bf16x2(lo, hi);
+            }
           } else {
             // Nibble k of the code word is element k (low nibble first). Each
             // nibble's low three bits select a byte from a register pair (levels
@@ -461,7 +488,7 @@ __global__ void __launch_bounds__(GT<KIND>::THREADS, 1)
             // the pair that bit 3 names (selector nibble j + 4 * bit3). The two
             // planes are then interleaved into BF16 pairs and scaled by the block
             // absmax with one BF16x2 multiply: bf16(bf16(level) * bf16(absmax)).
-            const __nv_bfloat162 am2 = __float2bfloat162_rn(amax[j]);
+            const __nv_bfloat162 am2 = __float2bfloat162_rn(KIND == kGemmNF4 ? amax[j] : 1.f);
             const uint32_t code = cw[j];
             const uint32_t pick = ((code >> 1) & 0x44444444u) | 0x32103210u;
 #pragma unroll
@@ -474,8 +501,11 @@ __global__ void __launch_bounds__(GT<KIND>::THREADS, 1)
 #pragma unroll
               for (int q = 0; q < 2; ++q) {
                 uint32_t v = __byte_perm(lo, hi, q ? 0x7362u : 0x5140u);
-                __nv_bfloat162 r = __hmul2(*reinterpret_cast<__nv_bfloat162*>(&v), am2);
-                w[j][2 * h + q] = *reinterpret_cast<uint32_t*>(&r);
+                if constexpr (KIND == kGemmNF4) {
+                  __nv_bfloat162 r = __hmul2(*reinterpret_cast<__nv_bfloat162*>(&v), am2);
+                  v = *reinterpret_cast<uint32_t*>(&r);
+                }
+                w[j][2 * h + q] = v;
               }
             }
           }
@@ -559,11 +589,11 @@ template <int KIND> cudaError_t launch(const GemmArgs& g, cudaStream_t stream) {
   ta2 = ta;
   if (f32 && !make_map_2d(&ta2, g.a_lo, adt, ae, g.K, g.M, g.lda, T::BK, kBM, CU_TENSOR_MAP_SWIZZLE_128B))
     return cudaErrorInvalidValue;
-  if (KIND == kGemmFP8) {
+  if (byte_codes<KIND>()) {
     if (!make_map_2d(&tb, g.b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.K, g.N, g.ldb, 64, T::BN,
                      CU_TENSOR_MAP_SWIZZLE_NONE))
       return cudaErrorInvalidValue;
-  } else if (KIND == kGemmNF4) {
+  } else if (nibble_codes<KIND>()) {
     if (!make_map_2d(&tb, g.b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.K / 2, g.N, g.ldb / 2, 32, T::BN,
                      CU_TENSOR_MAP_SWIZZLE_NONE))
       return cudaErrorInvalidValue;
@@ -585,7 +615,7 @@ template <int KIND> cudaError_t launch(const GemmArgs& g, cudaStream_t stream) {
   p.k_blocks = (g.K + T::BK - 1) / T::BK;
   {
     // B bytes of one N-tile as stored in HBM (codes for FP8 / NF4, both TF32 parts)
-    const double b_elem = KIND == kGemmFP8 ? 1.0 : KIND == kGemmNF4 ? 0.5 : (double)(T::ELEM * T::NB);
+    const double b_elem = byte_codes<KIND>() ? 1.0 : nibble_codes<KIND>() ? 0.5 : (double)(T::ELEM * T::NB);
     const double panel = (double)T::BN * g.K * b_elem;
     const int gn = (int)std::max(1.0, std::floor(48.0e6 / std::max(panel, 1.0)));
     p.gn = std::min(p.n_tiles, gn);
@@ -597,7 +627,7 @@ template <int KIND> cudaError_t launch(const GemmArgs& g, cudaStream_t stream) {
   p.out_lo = g.out_lo;
   p.b_scale = g.b_scale;
   p.ldb = g.ldb;
-  p.col_scale = KIND == kGemmFP8 ? g.b_scale : nullptr;
+  p.col_scale = (KIND == kGemmFP8 || KIND == kGemmI8 || KIND == kGemmI4 || KIND == kGemmFP4) ? g.b_scale : nullptr;
   p.rope_tab = g.rope_tab;
   p.rope_cols = g.rope_tab ? g.rope_cols : 0;
   p.head_dim = g.head_dim;
@@ -632,15 +662,19 @@ bool gemm_tc_supported(const GemmArgs& g) {
   if (!al16(g.a) || ((size_t)g.lda * ae) % 16) return false;
   if (g.kind == kGemmTF32x3 && (!al16(g.a_lo) || !al16(g.b_lo))) return false;
   if (!al16(g.b)) return false;
-  if (g.kind == kGemmFP8 || g.kind == kGemmNF4) {
+  const bool bytes = g.kind == kGemmFP8 || g.kind == kGemmI8;
+  const bool nibbles = g.kind == kGemmNF4 || g.kind == kGemmI4 || g.kind == kGemmFP4;
+  if (g.kind < kGemmBF16 || g.kind > kGemmFP4) return false;
+  if (bytes || nibbles) {
     if (g.K % 64) return false;
-    if (g.kind == kGemmFP8 && (g.ldb % 16 || !g.b_scale)) return false;
-    if (g.kind == kGemmNF4 && ((g.ldb / 2) % 16 || !g.b_scale)) return false;
+    if (bytes && g.ldb % 16) return false;
+    if (nibbles && (g.ldb / 2) % 16) return false;
+    if (g.kind != kGemmFP4 && !g.b_scale) return false;
   } else if (((size_t)g.ldb * ae) % 16) {
     return false;
   }
   if (g.kv_k && (g.kv_dim % 32 || g.kv_col0 % 32 || g.head_dim % 32)) return false;
-  if (g.swiglu && (g.N % 64 || g.rope_cols || g.kv_k || g.kind == kGemmFP8)) return false;
+  if (g.swiglu && (g.N % 64 || g.rope_cols || g.kv_k || (g.kind != kGemmBF16 && g.kind != kGemmTF32x3))) return false;
   return encode_fn() != nullptr;
 }
 
@@ -651,6 +685,9 @@ cudaError_t gemm_tc(const GemmArgs& g, cudaStream_t stream) {
   case kGemmTF32x3: return launch<kGemmTF32x3>(g, stream);
   case kGemmFP8: return launch<kGemmFP8>(g, stream);
   case kGemmNF4: return launch<kGemmNF4>(g, stream);
+  case kGemmI8: return launch<kGemmI8>(g, stream);
+  case kGemmI4: return launch<kGemmI4>(g, stream);
+  case kGemmFP4: return launch<kGemmFP4>(g, stream);
   default: return cudaErrorInvalidValue;
   }
 }

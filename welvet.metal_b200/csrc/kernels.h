@@ -30,6 +30,13 @@ enum GemmKind : int {
                    // three TF32 products per k (hi*hi + hi*lo + lo*hi), ~FP32 accuracy
   kGemmFP8 = 2,    // A bf16, B FP8-E4M3 codes (+ one FP32 scale per B row, epilogue)
   kGemmNF4 = 3,    // A bf16, B NF4 codes two per byte (+ FP32 absmax per 64 codes)
+  // FormatNone codes of the reference's own quantisers (src/weights/native_codec.cpp),
+  // dequantised in shared memory inside the mainloop; b_scale [N] holds the
+  // per-output-row scale, applied in the epilogue (the per-tensor scale of the
+  // matrix each row belongs to):
+  kGemmI8 = 4,     // A bf16, B Int8 codes (one byte each; weight = code * scale)
+  kGemmI4 = 5,     // A bf16, B Int4 codes two per byte, low nibble first (weight = q * scale)
+  kGemmFP4 = 6,    // A bf16, B FP4 (E2M1) codes two per byte (weight = level; b_scale may be null)
 };
 
 struct GemmArgs {
@@ -109,6 +116,11 @@ cudaError_t nf4_block_encode(const float* w, int64_t n, uint8_t* packed, float* 
                              cudaStream_t s);
 cudaError_t nf4_block_decode(const uint8_t* packed, const float* absmax, int64_t n, void* out,
                              int out_bf16, cudaStream_t s);
+// FormatNone Int8 (dtype 9), Int4 (14) or FP4 (16) codes of the reference quantisers
+// for the dequantising GEMM kinds kGemmI8 / kGemmI4 / kGemmFP4, the per-tensor
+// scale written once per row (n / cols rows; 1 for FP4). stats = [absmax, min, max].
+cudaError_t formatnone_codes_encode(int dtype, const float* w, int64_t n, int cols, const float* stats,
+                                    uint8_t* codes, float* row_scale, cudaStream_t s);
 // Rewrites E4M3 codes in place to codes with the same reference-decoded value that
 // the hardware E4M3 conversion decodes identically (no subnormal codes, no 0x7f/0xff).
 cudaError_t fp8_normalize(uint8_t* codes, int64_t n, cudaStream_t s);

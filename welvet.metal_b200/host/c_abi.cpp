@@ -351,6 +351,17 @@ welvet_status welvet_b200_codec_encode(int32_t dtype, const float* w, void* code
   Status st = wv::device_ctx(-1, &d);
   if (!st) return wv::to_c(st);
   cudaStream_t s = as_stream(stream);
+  if (dtype == 9 || dtype == 14 || dtype == 16) {
+    // Int8 / Int4 / FP4 bytes of pack_native with the per-tensor scale (the codes the
+    // dequantising GEMM keeps resident); scale_out receives the scale (n / 1 row)
+    if (!scale_out || n <= 0 || n > INT32_MAX) return wv::to_c(Status::err(1, "codec: invalid argument"));
+    cudaError_t e = wv::stats_f32(w, n, d->scalars, d->scratch, s);
+    if (e != cudaSuccess) return launch_status(e, "stats");
+    wv::count_launch(3);
+    return launch_status(wv::formatnone_codes_encode(dtype, w, n, (int)n, d->scalars,
+                                                     static_cast<uint8_t*>(codes), scale_out, s),
+                         "formatnone codes");
+  }
   if (dtype == 26) {
     if (!scale_out) return wv::to_c(Status::err(1, "codec: nf4 needs scale_out"));
     cudaError_t e = wv::absmax_f32(w, n, scale_out, d->scratch, s);

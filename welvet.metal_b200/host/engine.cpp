@@ -135,6 +135,19 @@ DeviceRestore::~DeviceRestore() {
   cudaSetDevice(dev_);
 }
 
+// True for host memory the device copies from or to asynchronously (page-locked);
+// false for pageable memory, whose device-to-host copies hold the calling thread
+// until the copy has run.
+bool host_pinned(const void* p) {
+  if (!p) return true;
+  cudaPointerAttributes a{};
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return a.type == cudaMemoryTypeHost;
+}
+
 // ------------------------------------------------------------------ devices
 namespace {
 std::mutex g_dev_mu;
@@ -219,8 +232,8 @@ Status resolve_config(const welvet_b200_mha_config& in, Cfg* out) {
   if (c.rope_theta <= 0) c.rope_theta = 10000;
   if (c.softmax != 0 && c.softmax != 1) return Status::err(1, "mha: unknown Softmax");
   if (c.precision != 0 && c.precision != 1) return Status::err(1, "mha: precision must be 0 or 1");
-  if (c.weight_format < 0 || c.weight_format > 2 || (c.precision == 0 && c.weight_format != 0))
-    return Status::err(1, "mha: weight_format 1/2 need precision 1 (BF16)");
+  if (c.weight_format < 0 || c.weight_format > 3 || (c.precision == 0 && c.weight_format != 0))
+    return Status::err(1, "mha: weight_format 1/2/3 need precision 1 (BF16)");
   r.hd = c.head_dim;
   r.nk = c.num_kv_heads;
   r.msl = c.max_seq_len;
@@ -356,15 +369,26 @@ Status mha_mount(const welvet_b200_mha_config& cin, int dtype, const float* Q, c
   } else {
     // Extension formats encode the FP32 inits directly. Scales are computed on the
     // full matrices, then the shard's slice of codes and scales is kept.
-    const bool fp8 = m->wfmt == 1;
+    // weight_format 3 keeps the reference's own FormatNone codes of `dtype` (Int8,
+    // Int4 or FP4) with the per-tensor scale of each matrix as a per-row scale.
+    if (m->wfmt == 3 && dtype != 9 && dtype != 14 && dtype != 16)
+      return Status::err(2, "mha: weight_format 3 keeps Int8 (9), Int4 (14) or FP4 (16) codes");
+    m->wdtype = dtype;
+    const bool fp8 = m->wfmt == 1 || (m->wfmt == 3 && dtype == 9);  // one byte per code
+    const bool rowscale = m->wfmt != 2;                               // one scale per row
     if (dm % 64 || cfg.qd % 64 || (m->qd_l % 64))
-      return Status::err(2, "mha: FP8/NF4 weight formats need d_model and head slices % 64 == 0");
+      return Status::err(2, "mha: FP8/NF4/FormatNone-code weight formats need d_model and head slices % 64 == 0");
     DevBuf cq, ck, cv, co, sq, sk, sv, so;
     auto enc = [&](const DevBuf& w, int rows, int cols, DevBuf& codes, DevBuf& sc) -> Status {
       const int64_t n = (int64_t)rows * cols;
       WV_TRY(codes.ensure(fp8 ? n : n / 2));
-      WV_TRY(sc.ensure(fp8 ? (size_t)rows * 4 : (size_t)(n / 64) * 4));
-      if (fp8) {
+      WV_TRY(sc.ensure(rowscale ? (size_t)rows * 4 : (size_t)(n / 64) * 4));
+      if (m->wfmt == 3) {
+        WV_CUDA(stats_f32(w.as<float>(), n, d->scalars, d->scratch, s), "stats");
+        WV_CUDA(formatnone_codes_encode(dtype, w.as<float>(), n, cols, d->scalars, codes.as<uint8_t>(),
+                                        sc.as<float>(), s), "formatnone codes");
+        count_launch(2);
+      } else if (fp8) {
         WV_CUDA(fp8_rowscale_encode(w.as<float>(), rows, cols, codes.as<uint8_t>(), sc.as<float>(), s), "fp8 enc");
         // the dequantising GEMM decodes with the hardware E4M3 conversion
         WV_CUDA(fp8_normalize(codes.as<uint8_t>(), n, s), "fp8 normalize");
@@ -379,7 +403,7 @@ Status mha_mount(const welvet_b200_mha_config& cin, int dtype, const float* Q, c
     WV_TRY(enc(fv, cfg.kd, dm, cv, sv));
     WV_TRY(enc(fo, dm, cfg.qd, co, so));
     const size_t rb = fp8 ? (size_t)dm : (size_t)dm / 2;   // code bytes per W_qkv row
-    const size_t srow = fp8 ? 1 : (size_t)dm / 64;         // scales per W_qkv row
+    const size_t srow = rowscale ? 1 : (size_t)dm / 64;    // scales per W_qkv row
     WV_TRY(m->wqkv.ensure((size_t)m->nqkv * rb));
     WV_TRY(m->wqkv_scale.ensure((size_t)m->nqkv * srow * 4));
     auto cp = [&](void* dstp, const void* srcp, size_t bytes) -> Status {
@@ -401,7 +425,7 @@ Status mha_mount(const welvet_b200_mha_config& cin, int dtype, const float* Q, c
     WV_TRY(m->wo.ensure((size_t)dm * ob_l));
     WV_CUDA(cudaMemcpy2DAsync(m->wo.p, ob_l, co.as<uint8_t>() + oc0, ob, ob_l, dm,
                               cudaMemcpyDeviceToDevice, s), "slice Wo codes");
-    if (fp8) {
+    if (rowscale) {
       WV_TRY(m->wo_scale.ensure((size_t)dm * 4));
       WV_TRY(cp(m->wo_scale.p, so.p, (size_t)dm * 4));
     } else {
@@ -468,7 +492,11 @@ struct Proj {
 Status run_proj(Mha* m, const Proj& pj, cudaStream_t s) {
   const bool f32 = m->precision == 0;
   GemmArgs g;
-  g.kind = f32 ? kGemmTF32x3 : (m->wfmt == 1 ? kGemmFP8 : (m->wfmt == 2 ? kGemmNF4 : kGemmBF16));
+  g.kind = f32 ? kGemmTF32x3
+              : m->wfmt == 1 ? kGemmFP8
+              : m->wfmt == 2 ? kGemmNF4
+              : m->wfmt == 3 ? (m->wdtype == 9 ? kGemmI8 : m->wdtype == 14 ? kGemmI4 : kGemmFP4)
+                             : kGemmBF16;
   g.M = pj.M;
   g.N = pj.N;
   g.K = pj.K;
@@ -608,6 +636,11 @@ Status mha_forward(Mha* m, int batch, int seq, const void* x, void* pre, void* p
   // chunk's projections and attention (stream s), whose input copy (io_in) ran
   // during the previous chunk.
   const bool chunked = (m->comm || !on_device) && !stream_mode && !kv && batch > 1;
+  // Pageable host outputs with a communicator: a device-to-host copy queued behind a
+  // collective would hold this thread until the collective ends, i.e. forever if a
+  // peer rank stopped. Their copies wait until the bounded wait (comm_wait) has seen
+  // the collectives finish.
+  const bool defer_d2h = !on_device && m->comm && m->nranks > 1 && (!host_pinned(post) || !host_pinned(pre));
   // Host copies (about 40 ms per 2 GB each way on PCIe) want more, smaller chunks
   // than the all-reduce does.
   int chunks = chunked ? std::min(batch, on_device ? 4 : Mha::kMaxChunks) : 1;
@@ -781,11 +814,13 @@ Status mha_forward(Mha* m, int batch, int seq, const void* x, void* pre, void* p
         WV_TRY(comm_reducescatter(m, static_cast<char*>(postd) + r0 * dm * es, (size_t)own * dm, !f32,
                                   m->comm_stream));
         prof_end(kProfAllReduce, m->comm_stream);
-        WV_CUDA(cudaEventRecord(m->io_ev[Mha::kMaxChunks + i], m->comm_stream), "event");
-        WV_CUDA(cudaStreamWaitEvent(m->io_out, m->io_ev[Mha::kMaxChunks + i], 0), "wait");
-        WV_CUDA(cudaMemcpyAsync(static_cast<char*>(post) + (int64_t)i * bcl * seq * dm * es,
-                                static_cast<char*>(postd) + (r0 + m->rank * own) * dm * es, own * dm * es,
-                                cudaMemcpyDeviceToHost, m->io_out), "D2H post rows");
+        if (!defer_d2h) {
+          WV_CUDA(cudaEventRecord(m->io_ev[Mha::kMaxChunks + i], m->comm_stream), "event");
+          WV_CUDA(cudaStreamWaitEvent(m->io_out, m->io_ev[Mha::kMaxChunks + i], 0), "wait");
+          WV_CUDA(cudaMemcpyAsync(static_cast<char*>(post) + (int64_t)i * bcl * seq * dm * es,
+                                  static_cast<char*>(postd) + (r0 + m->rank * own) * dm * es, own * dm * es,
+                                  cudaMemcpyDeviceToHost, m->io_out), "D2H post rows");
+        }
         continue;
       }
       if (host) {
@@ -807,7 +842,7 @@ Status mha_forward(Mha* m, int batch, int seq, const void* x, void* pre, void* p
           out_ready = m->io_ev[Mha::kMaxChunks + i];
         }
       }
-      if (host) {
+      if (host && !defer_d2h) {
         WV_CUDA(cudaStreamWaitEvent(m->io_out, out_ready, 0), "wait");
         WV_CUDA(cudaMemcpyAsync(static_cast<char*>(post) + r0 * dm * es, static_cast<char*>(postd) + r0 * dm * es,
                                 rows * dm * es, cudaMemcpyDeviceToHost, m->io_out), "D2H post");
@@ -828,11 +863,26 @@ Status mha_forward(Mha* m, int batch, int seq, const void* x, void* pre, void* p
   }
 
   if (!on_device) {
-    if (!chunked) {
-      WV_CUDA(cudaMemcpyAsync(post, postd, M * dm * es, cudaMemcpyDeviceToHost, s), "D2H post");
-      if (pre) WV_CUDA(cudaMemcpyAsync(pre, pred, M * m->qd_l * es, cudaMemcpyDeviceToHost, s), "D2H pre");
+    if (defer_d2h) {
+      WV_TRY(comm_wait(m, s, "forward"));  // every collective finished (or code 4)
+      if (rows_io) {
+        for (int i = 0, b0 = 0; i < chunks && b0 < batch; ++i, b0 += bc_max) {
+          const int64_t r0 = (int64_t)b0 * seq, own = (int64_t)(std::min(bc_max, batch - b0) / nr) * seq;
+          WV_CUDA(cudaMemcpy(static_cast<char*>(post) + (int64_t)i * bcl * seq * dm * es,
+                             static_cast<char*>(postd) + (r0 + m->rank * own) * dm * es, own * dm * es,
+                             cudaMemcpyDeviceToHost), "D2H post rows");
+        }
+      } else {
+        WV_CUDA(cudaMemcpy(post, postd, M * dm * es, cudaMemcpyDeviceToHost), "D2H post");
+        if (pre) WV_CUDA(cudaMemcpy(pre, pred, M * m->qd_l * es, cudaMemcpyDeviceToHost), "D2H pre");
+      }
+    } else {
+      if (!chunked) {
+        WV_CUDA(cudaMemcpyAsync(post, postd, M * dm * es, cudaMemcpyDeviceToHost, s), "D2H post");
+        if (pre) WV_CUDA(cudaMemcpyAsync(pre, pred, M * m->qd_l * es, cudaMemcpyDeviceToHost, s), "D2H pre");
+      }
+      WV_TRY(comm_wait(m, s, "forward"));
     }
-    WV_TRY(comm_wait(m, s, "forward"));
     WV_TRY(check_device_error(m->dev));
   }
   return Status::ok();
@@ -1026,6 +1076,10 @@ Status mha_decode(Mha* m, Kv* kv, int batch, const void* x, void* pre, void* pos
   }
   for (int b = 0; b < batch; ++b) kv->ctx_host[b] += 1;
   if (!on_device) {
+    // pageable outputs with a communicator: copy only after the bounded wait (see
+    // mha_forward)
+    const bool defer_d2h = m->comm && m->nranks > 1 && (!host_pinned(post) || !host_pinned(pre));
+    if (defer_d2h) WV_TRY(comm_wait(m, s, "decode"));
     WV_CUDA(cudaMemcpyAsync(post, postd, (size_t)batch * dm * es, cudaMemcpyDeviceToHost, s), "D2H post");
     if (pre) WV_CUDA(cudaMemcpyAsync(pre, attn, (size_t)batch * m->qd_l * es, cudaMemcpyDeviceToHost, s), "D2H pre");
     WV_TRY(comm_wait(m, s, "decode"));

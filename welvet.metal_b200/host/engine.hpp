@@ -150,6 +150,7 @@ struct Mha {
   int h0 = 0, hc = 0, kh0 = 0, khc = 0;  // head shard
   int qd_l = 0, kd_l = 0, nqkv = 0;
   int precision = 0, wfmt = 0;
+  int wdtype = 1;  // FormatNone dtype of resident codes (weight_format 3)
   // weights (layouts documented in engine.cpp)
   DevBuf wqkv, wqkv_lo, wo, wo_lo, wqkv_scale, wo_scale;
   // RoPE cos/sin table
