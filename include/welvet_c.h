@@ -9,7 +9,8 @@
  * Besides the MHA forward it serves the MHA NormalBP leaf and the forward entries
  * of the transformer block around it (SwiGLU, RMSNorm, LayerNorm, Embedding). The
  * reference's other entry points (Dense/CNN/recurrent families, the other NormalBP
- * leaves, model sessions) are not part of this library. */
+ * leaves) are not part of this library. Model sessions (WMN1) are served for models
+ * whose layers are MHA cells; their training entry points answer code 2. */
 
 #include <stddef.h>
 #include <stdint.h>
@@ -101,6 +102,32 @@ WELVET_API welvet_status welvet_embedding_forward_f32(
     int32_t batch, int32_t vocab, int32_t emb, int32_t seq_len, int32_t in_rank, int32_t in_last,
     int32_t act, int32_t dtype, int32_t backend, const float* W, const float* x, float* pre,
     float* post);
+
+/* Versioned model sessions (reference include/welvet_c.h:36-56, impl
+ * src/interop/model_session.cpp:319-576). welvet_model_mount reads a WMN1
+ * descriptor (root Stack = 0 or Grid = 2, MHA and nested-Stack children,
+ * Cameral controls, native Store snapshots, grid cell metadata; the byte layout of
+ * the reference's model_wire.hpp / child_wire.hpp) and mounts every MHA child as a
+ * resident B200 layer whose weights are the snapshots' stores (Q, K, V, O). Inputs
+ * and outputs are the reference's tensor wires (rank, dims, FP32 values; outputs
+ * add the element count). Buffers are copied during calls; one call at a time per
+ * session (a per-session lock). Root Parallel, other layer kinds, and the training
+ * / proxy / sync entry points answer code 2. */
+typedef struct welvet_model_session welvet_model_session;
+typedef struct welvet_metal_blob { uint8_t* data; size_t size; } welvet_metal_blob;
+WELVET_API int32_t welvet_model_abi_version(void);
+WELVET_API welvet_status welvet_model_mount(const uint8_t*, size_t, welvet_model_session**);
+WELVET_API welvet_status welvet_model_forward(welvet_model_session*, const uint8_t*, size_t, welvet_metal_blob*);
+WELVET_API welvet_status welvet_model_train_credit(welvet_model_session*, int32_t, double, const uint8_t*, size_t);
+WELVET_API welvet_status welvet_model_dense_proxy(welvet_model_session*, int32_t, const uint8_t*, size_t, welvet_metal_blob*);
+WELVET_API welvet_status welvet_model_forward_pair(welvet_model_session*, const uint8_t*, size_t, welvet_metal_blob*);
+WELVET_API welvet_status welvet_model_backward(welvet_model_session*, const uint8_t*, size_t, welvet_metal_blob*);
+WELVET_API welvet_status welvet_model_apply_sgd(welvet_model_session*, double, const uint8_t*, size_t);
+WELVET_API welvet_status welvet_model_train_mse(welvet_model_session*, int32_t mode, double lr, int32_t ticks, const uint8_t*, size_t, double* loss);
+WELVET_API welvet_status welvet_model_export_weights(welvet_model_session*, welvet_metal_blob*);
+WELVET_API welvet_status welvet_model_sync(welvet_model_session*, int32_t event);
+WELVET_API void welvet_model_release(welvet_model_session*);
+WELVET_API void welvet_metal_blob_free(welvet_metal_blob*);
 
 #ifdef __cplusplus
 }
