@@ -24,7 +24,12 @@ LIB_PATH = os.path.join(HERE, "lib", "libwelvet_b200.so")
 C_ABI_SYMBOLS = ("welvet_version", "welvet_runtime_identity", "welvet_metal_init",
                  "welvet_metal_available", "welvet_mha_forward_f32", "welvet_mha_normalbp_f32",
                  "welvet_swiglu_forward_f32",
-                 "welvet_rmsnorm_forward_f32", "welvet_layernorm_forward_f32", "welvet_embedding_forward_f32")
+                 "welvet_rmsnorm_forward_f32", "welvet_layernorm_forward_f32", "welvet_embedding_forward_f32",
+                 "welvet_model_abi_version", "welvet_model_mount", "welvet_model_forward",
+                 "welvet_model_train_credit", "welvet_model_dense_proxy", "welvet_model_forward_pair",
+                 "welvet_model_backward", "welvet_model_apply_sgd", "welvet_model_train_mse",
+                 "welvet_model_export_weights", "welvet_model_sync", "welvet_model_release",
+                 "welvet_metal_blob_free")
 EXT_SYMBOLS = ("welvet_b200_mha_config_default", "welvet_b200_mha_mount", "welvet_b200_mha_release",
                "welvet_b200_mha_forward", "welvet_b200_mha_forward_rows", "welvet_b200_mha_check",
                "welvet_b200_kv_create",
