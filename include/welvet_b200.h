@@ -156,11 +156,22 @@ WELVET_API welvet_status welvet_b200_split_tf32(const float* x, float* hi, float
 /* Attention forward over token-major q [*, q_dim], k/v [*, kv_dim] (RoPE already
  * applied) -> out [*, q_dim] (reference op_attention forward,
  * shaders/ops_mha.metal:31-127). impl 0 = best available, 1 = CUDA-core kernel,
- * 2 = tensor-core kernel (fails when unsupported). */
+ * 2 = tensor-core kernel (fails when unsupported), 3 = tensor-core kernel on CTA
+ * pairs (head_dim 128, seq a multiple of 256). */
 WELVET_API welvet_status welvet_b200_attention(const welvet_b200_mha_config* cfg, int32_t batch,
                                                int32_t seq, const void* q, const void* k,
                                                const void* v, void* out, int32_t impl,
                                                void* stream);
+/* The same forward for an FP32 configuration on the tensor cores (3xTF32, head_dim
+ * 64): q/k/v given as their TF32 split (hi, lo from welvet_b200_split_tf32, same
+ * layouts as above); out FP32, and its TF32 split into out_hi / out_lo when both
+ * are given. Code 2 when the configuration is outside the kernel (head_dim,
+ * stream ring wrap, alignment). Reference: shaders/ops_mha.metal:31-127. */
+WELVET_API welvet_status welvet_b200_attention_tf32(const welvet_b200_mha_config* cfg, int32_t batch,
+                                                    int32_t seq, const float* q_hi, const float* q_lo,
+                                                    const float* k_hi, const float* k_lo,
+                                                    const float* v_hi, const float* v_lo, float* out,
+                                                    float* out_hi, float* out_lo, void* stream);
 /* Codec kernels, bit-exact to the reference converters
  * (src/core/float_codecs.cpp, src/weights/native_codec.cpp:189-813):
  * roundtrip: out = decode(encode(w)) for any FormatNone dtype 0-33 (per-tensor

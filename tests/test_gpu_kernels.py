@@ -312,6 +312,55 @@ def test_attention_against_oracle(torch_cuda, kw, B, T, precision, impl):
     assert rel_err(out.float().cpu().numpy(), ref) < tol
 
 
+# FP32 attention on the tensor cores (3xTF32, head_dim 64) from the TF32 split of
+# q, k, v: every case above that the kernel takes, plus long causal sequences
+# (many 64-key blocks, lazy rescale and the two partial softmaxes merged), GQA,
+# ALiBi with sigmoid scores, against the FP64 oracle within the FP32 budget 1e-4.
+TF32_CASES = ATTN_CASES + [
+    (dict(d_model=1024, num_heads=16, seq_mode=1), 1, 2048),               # the cfg2 head shape
+    (dict(d_model=512, num_heads=8, num_kv_heads=2, seq_mode=1, pos=2, softmax=1), 2, 333),
+    (dict(d_model=256, num_heads=4, seq_mode=1, mask=4, prefix_len=100), 1, 260),
+]
+
+
+@pytest.mark.parametrize("kw,B,T", TF32_CASES)
+def test_attention_tf32_against_oracle(torch_cuda, kw, B, T):
+    torch = torch_cuda
+    kw = dict(kw)
+    cfg = W.MhaConfig.make(kw.pop("d_model"), kw.pop("num_heads"), kw.pop("num_kv_heads", 0), precision=0, **kw)
+    hd, nk = cfg.resolved()
+    qd, kd = cfg.num_heads * hd, nk * hd
+    M = B * T
+    q = W.synthetic(M * qd, 21, 1, 1.0).reshape(M, qd)
+    k = W.synthetic(M * kd, 22, 1, 1.0).reshape(M, kd)
+    v = W.synthetic(M * kd, 23, 1, 1.0).reshape(M, kd)
+    oc = O.MhaCfg(d_model=cfg.d_model, num_heads=cfg.num_heads, num_kv_heads=nk, head_dim=hd,
+                  max_seq_len=cfg.max_seq_len, mask=cfg.mask, pos=1 if cfg.pos == 0 else cfg.pos,
+                  softmax=cfg.softmax, window=cfg.window, prefix_len=cfg.prefix_len,
+                  window_causal=cfg.window_causal, per_sequence=cfg.seq_mode)
+    cfg.pos = oc.pos
+    parts = []
+    for a in (q, k, v):
+        t = _dev(torch, a)
+        hi, lo = torch.empty_like(t), torch.empty_like(t)
+        W.split_tf32(t, hi, lo)
+        parts += [hi, lo]
+    out = torch.zeros(M, qd, device="cuda")
+    oh, ol = torch.zeros_like(out), torch.zeros_like(out)
+    try:
+        W.attention_tf32(cfg, B, T, *parts, out, oh, ol)
+    except W.WelvetError as e:
+        if e.code == 2 and (hd != 64 or (cfg.seq_mode == 0 and B * T > cfg.max_seq_len)):
+            pytest.skip("3xTF32 kernel: head_dim 64 without the stream ring wrap")
+        raise
+    torch.cuda.synchronize()
+    W.device_check()
+    ref = O.attention(oc, B, T, q, k, v)
+    assert rel_err(out.cpu().numpy(), ref) < 1e-4
+    assert torch.equal(oh + ol, out)
+    assert not torch.any(oh.view(torch.int32) & 0x1FFF)
+
+
 # CTA-pair tensor-core attention (impl 3: clusters of two CTAs, M = 256 UMMAs;
 # head_dim 128, sequences of whole 256-query tile pairs): the masks, position
 # biases and score functions of the reference, GQA, stream semantics, against the

@@ -327,3 +327,34 @@ def test_resident_formatnone_code_layer(torch_cuda, dtype):
     assert rel_err(pre.float().cpu().numpy(), rpre) < LOW_TOL
     assert rel_err(post.float().cpu().numpy(), rpost) < LOW_TOL
     layer.close()
+
+
+@pytest.mark.parametrize("weight_format,dtype", [(0, 1), (1, 1), (2, 1), (3, 9), (3, 14)])
+def test_decode_split_k_weight_formats(torch_cuda, weight_format, dtype):
+    """Decode projections at few rows split their K range over the SMs (FP32 partials
+    summed in split order, then scale, RoPE and the BF16 store); every resident weight
+    format, against the oracle's decode on the decoded weights."""
+    torch = torch_cuda
+    d, H, NK, B, L = 1024, 16, 4, 5, 70
+    cfg = W.MhaConfig.make(d, H, NK, precision=1, weight_format=weight_format)
+    hd, nk = cfg.resolved()
+    Ws = W.xavier_weights(d, H * hd, nk * hd, seed=3)
+    layer = W.MhaLayer(cfg, *Ws, dtype=dtype)
+    kv = W.KvCache(layer, B, 128)
+    kc = W.synthetic(B * L * nk * hd, 2, 1, 0.5).reshape(B, L, nk * hd)
+    vc = W.synthetic(B * L * nk * hd, 2, 1, 0.5, offset=B * L * nk * hd).reshape(B, L, nk * hd)
+    kcb = torch.from_numpy(kc).cuda().to(torch.bfloat16)
+    vcb = torch.from_numpy(vc).cuda().to(torch.bfloat16)
+    kv.fill(B, L, kcb, vcb)
+    x = torch.from_numpy(W.synthetic(B * d, 1, 1, 1.0).reshape(B, d)).cuda().to(torch.bfloat16)
+    post = torch.zeros(B, d, device="cuda", dtype=torch.bfloat16)
+    pre = torch.zeros(B, H * hd, device="cuda", dtype=torch.bfloat16)
+    layer.decode(kv, B, x, pre, post)
+    torch.cuda.synchronize()
+    layer.check_device()
+    oc = O.MhaCfg(d_model=d, num_heads=H, num_kv_heads=NK, per_sequence=1)
+    rpre, rpost, _, _ = O.mha_decode(oc, [L] * B, kcb.float().cpu().numpy(), vcb.float().cpu().numpy(),
+                                     *_oracle_weights(Ws, dtype, weight_format), x.float().cpu().numpy())
+    assert rel_err(pre.float().cpu().numpy(), rpre) < LOW_TOL
+    assert rel_err(post.float().cpu().numpy(), rpost) < LOW_TOL
+    layer.close()

@@ -61,7 +61,7 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(GemmArgs g) {
       if (g.out_bf16) {
         static_cast<__nv_bfloat16*>(g.out)[off] = __float2bfloat16_rn(v);
       } else {
-        static_cast<float*>(g.out)[off] = v;
+        if (!(g.split_only && g.out_hi)) static_cast<float*>(g.out)[off] = v;
         if (g.out_hi) {
           const float h = to_tf32(v);
           g.out_hi[off] = h;

@@ -70,10 +70,17 @@ __device__ __forceinline__ float nibble_level(int kind, int c) {
 struct KParams {
   int M, N, K, m_tiles, n_tiles, num_tiles, k_blocks;
   int gn;  // N-tiles per raster group (see tile_coords)
+  // Split-K (few output tiles, e.g. a decode step's M <= 128 rows): tile t covers
+  // k-blocks [sk * kb_per, (sk + 1) * kb_per) of output tile t / ksplit (sk = t %
+  // ksplit); its epilogue writes the raw FP32 sums to ws [ksplit, M, N] and
+  // splitk_finish_kernel adds the splits in order and applies the epilogue.
+  int ksplit, kb_per;
+  float* ws;
   void* out;
   int ldo, out_bf16;
   float* out_hi;
   float* out_lo;
+  int split_only;  // FP32 output: only out_hi / out_lo are written
   const float* b_scale;    // FP8: per-row scales; NF4: per-64 absmax (dequant warps)
   const float* col_scale;  // FP8 only: per-output-column scale applied in the epilogue
   int ldb;
@@ -102,6 +109,14 @@ __device__ __forceinline__ void tile_coords(int t, const KParams& p, int& mb, in
   const int gn = min(p.gn, p.n_tiles - first);
   nb = first + r % gn;
   mb = r / gn;
+}
+
+// Work of persistent tile index t: output tile (mb, nb) and k-blocks [kb0, kb1).
+__device__ __forceinline__ void tile_work(int t, const KParams& p, int& mb, int& nb, int& kb0, int& kb1, int& sk) {
+  sk = t % p.ksplit;
+  tile_coords(t / p.ksplit, p, mb, nb);
+  kb0 = sk * p.kb_per;
+  kb1 = min(p.k_blocks, kb0 + p.kb_per);
 }
 
 __device__ __forceinline__ void store_vals(const KParams& p, int row, int col, const float* v,
@@ -141,22 +156,34 @@ __device__ __forceinline__ void store_vals(const KParams& p, int row, int col, c
     }
     return;
   }
-  float* d = static_cast<float*>(p.out) + off;
-  if (nvalid == 32 && (off % 4) == 0) {
+  if (!p.split_only) {
+    float* d = static_cast<float*>(p.out) + off;
+    if (nvalid == 32 && (off % 4) == 0) {
 #pragma unroll
-    for (int e = 0; e < 32; e += 4)
-      st_global_v4(d + e, __float_as_uint(v[e]), __float_as_uint(v[e + 1]),
-                   __float_as_uint(v[e + 2]), __float_as_uint(v[e + 3]));
-  } else {
-    for (int e = 0; e < nvalid; ++e) d[e] = v[e];
+      for (int e = 0; e < 32; e += 4)
+        st_global_v4(d + e, __float_as_uint(v[e]), __float_as_uint(v[e + 1]),
+                     __float_as_uint(v[e + 2]), __float_as_uint(v[e + 3]));
+    } else {
+      for (int e = 0; e < nvalid; ++e) d[e] = v[e];
+    }
   }
   if (p.out_hi) {
     float* h = p.out_hi + off;
     float* l = p.out_lo + off;
-    for (int e = 0; e < nvalid; ++e) {
-      const float hv = to_tf32(v[e]);
-      h[e] = hv;
-      l[e] = v[e] - hv;
+    if (nvalid == 32 && ((reinterpret_cast<uintptr_t>(h) | reinterpret_cast<uintptr_t>(l)) & 15) == 0) {
+#pragma unroll
+      for (int e = 0; e < 32; e += 4) {
+        const float h0 = to_tf32(v[e]), h1 = to_tf32(v[e + 1]), h2 = to_tf32(v[e + 2]), h3 = to_tf32(v[e + 3]);
+        st_global_v4(h + e, __float_as_uint(h0), __float_as_uint(h1), __float_as_uint(h2), __float_as_uint(h3));
+        st_global_v4(l + e, __float_as_uint(v[e] - h0), __float_as_uint(v[e + 1] - h1),
+                     __float_as_uint(v[e + 2] - h2), __float_as_uint(v[e + 3] - h3));
+      }
+    } else {
+      for (int e = 0; e < nvalid; ++e) {
+        const float hv = to_tf32(v[e]);
+        h[e] = hv;
+        l[e] = v[e] - hv;
+      }
     }
   }
 }
@@ -243,6 +270,65 @@ __device__ __forceinline__ void epilogue_tile(const KParams& p, uint32_t tbase, 
   }
 }
 
+// Split-K epilogue: the tile's raw FP32 sums into the split's slice of ws.
+template <int BN>
+__device__ __forceinline__ void epilogue_partial(const KParams& p, uint32_t tbase, int row, int n0, int sk) {
+  const bool row_ok = row < p.M;
+  float* dst = p.ws + ((size_t)sk * p.M + (row_ok ? row : 0)) * p.N;
+  for (int c = 0; c < BN && n0 + c < p.N; c += 32) {
+    uint32_t x[32];
+    tmem_ld32(tbase + c, x);
+    tmem_ld_wait();
+    if (!row_ok) continue;
+    const int gcol = n0 + c;
+    if (gcol + 32 <= p.N && (((size_t)sk * p.M + row) * p.N + gcol) % 4 == 0) {
+#pragma unroll
+      for (int e = 0; e < 32; e += 4) st_global_v4(dst + gcol + e, x[e], x[e + 1], x[e + 2], x[e + 3]);
+    } else {
+      for (int e = 0; e < 32 && gcol + e < p.N; ++e) dst[gcol + e] = __uint_as_float(x[e]);
+    }
+  }
+}
+
+// Sum of the split-K partials of (row, col), in split order.
+__device__ __forceinline__ float splitk_sum(const KParams& p, int row, int col) {
+  float v = 0.f;
+  for (int s_ = 0; s_ < p.ksplit; ++s_) v += __ldg(p.ws + ((size_t)s_ * p.M + row) * p.N + col);
+  if (p.col_scale) v *= p.col_scale[col];
+  return v;
+}
+
+// The epilogue of split-K GEMMs (per-row scale, RoPE on the first rope_cols
+// columns, output type), one output element per thread; a RoPE element reads its
+// pair partner's sums too. RoPE is applied where epilogue_tile<BN> would fuse it.
+template <int BN>
+__global__ void splitk_finish_kernel(const KParams p) {
+  const int hd = p.head_dim;
+  const bool fuse_rope = p.rope_cols > 0 && (hd == 64 || hd == 128 || hd == 256) && (BN % hd) == 0;
+  const int64_t total = (int64_t)p.M * p.N;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int row = (int)(i / p.N), col = (int)(i % p.N);
+    float v = splitk_sum(p, row, col);
+    if (fuse_rope && col < p.rope_cols) {
+      const int half = hd >> 1, in_head = col % hd;
+      const int pos = p.positions ? p.positions[row] : (p.pos_mod > 0 ? row % p.pos_mod : row);
+      const bool pos_ok = pos >= 0 && pos < p.rope_max_pos;
+      if (!pos_ok) atomicCAS(p.err, 0u, 0x100u);
+      const float2 cs = pos_ok ? p.rope_tab[(size_t)pos * half + (in_head % half)] : make_float2(1.f, 0.f);
+      if (in_head < half) {
+        const float b = splitk_sum(p, row, col + half);
+        v = v * cs.x - b * cs.y;
+      } else {
+        const float a = splitk_sum(p, row, col - half);
+        v = a * cs.y + v * cs.x;
+      }
+    }
+    const size_t off = (size_t)row * p.ldo + col;
+    if (p.out_bf16) static_cast<__nv_bfloat16*>(p.out)[off] = __float2bfloat16_rn(v);
+    else static_cast<float*>(p.out)[off] = v;
+  }
+}
+
 // 16 bytes of a 128-byte-swizzled K-major row: chunk index XOR (row mod 8).
 __device__ __forceinline__ uint32_t sw128_offset(int row, int chunk16) {
   return (uint32_t)(row * 128 + ((chunk16 ^ (row & 7)) << 4));
@@ -306,9 +392,9 @@ __global__ void __launch_bounds__(GT<KIND>::THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
-        int mb, nb;
-        tile_coords(t, p, mb, nb);
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        int mb, nb, kb0, kb1, sk;
+        tile_work(t, p, mb, nb, kb0, kb1, sk);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.err, kErrWaitEmpty)) goto done;
           uint8_t* sb = smem + stage * STAGE_BYTES;
           mbar_arrive_expect_tx(&full[stage], STAGE_BYTES - (XFORM ? B_BYTES : 0));
@@ -341,7 +427,9 @@ __global__ void __launch_bounds__(GT<KIND>::THREADS, 1)
         if (!mbar_wait(&acce[acc], acc_phase ^ 1, abort_flag, p.err, kErrWaitAccEmpty)) goto done;
         tc_fence_after();
         const uint32_t d = tmem_base + (uint32_t)(acc * BN);
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        int mb, nb, kb0, kb1, sk;
+        tile_work(t, p, mb, nb, kb0, kb1, sk);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, p.err, kErrWaitFull)) goto done;
           if constexpr (XFORM) {
             if (!mbar_wait(&xfull[stage], phase, abort_flag, p.err, kErrWaitFull)) goto done;
@@ -356,7 +444,7 @@ __global__ void __launch_bounds__(GT<KIND>::THREADS, 1)
             const uint32_t off = (uint32_t)(ks * T::UK * T::ELEM);
             const uint64_t ad = sdesc_sw128(a0 + off, 16, 1024);
             const uint64_t bd = sdesc_sw128(b0 + off, 16, 1024);
-            const uint32_t accum = (kb | ks) != 0;
+            const uint32_t accum = (kb != kb0 || ks != 0) ? 1u : 0u;
             if constexpr (KIND == kGemmTF32x3) {
               umma_tf32_ss(d, sdesc_sw128(a1 + off, 16, 1024), bd, IDESC, accum);
               umma_tf32_ss(d, ad, sdesc_sw128(b1 + off, 16, 1024), IDESC, 1);
@@ -382,13 +470,14 @@ __global__ void __launch_bounds__(GT<KIND>::THREADS, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
-      int mb, nb;
-      tile_coords(t, p, mb, nb);
+      int mb, nb, kb0, kb1, sk;
+      tile_work(t, p, mb, nb, kb0, kb1, sk);
       bool ok = mbar_wait(&accf[acc], acc_phase, abort_flag, p.err, kErrWaitAccFull);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * BN);
-      epilogue_tile<BN>(p, tbase, mb * kBM + 32 * q + lane, nb * BN);
+      if (p.ksplit > 1) epilogue_partial<BN>(p, tbase, mb * kBM + 32 * q + lane, nb * BN, sk);
+      else epilogue_tile<BN>(p, tbase, mb * kBM + 32 * q + lane, nb * BN);
       tc_fence_before();
       mbar_arrive(&acce[acc]);
       acc ^= 1;
@@ -419,9 +508,9 @@ __global__ void __launch_bounds__(GT<KIND>::THREADS, 1)
     int stage = 0;
     uint32_t phase = 0;
     for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
-      int mb, nb;
-      tile_coords(t, p, mb, nb);
-      for (int kb = 0; kb < p.k_blocks; ++kb) {
+      int mb, nb, kb0, kb1, sk;
+      tile_work(t, p, mb, nb, kb0, kb1, sk);
+      for (int kb = kb0; kb < kb1; ++kb) {
         // NF4: the 64-code block of this k-block has one absmax per row; the loads
         // are issued before the wait so their latency hides behind it.
         float amax[KIND == kGemmNF4 ? RPT : 1];
@@ -572,6 +661,26 @@ bool make_tma_2d(void* map128, const void* base, int dt, int elem_bytes, uint64_
 
 namespace {
 
+// Split-K factor of a GEMM: when its output tiles fill under half of the SMs (a
+// decode step's few rows), the K range is split so that about one tile per SM runs;
+// needs the caller's FP32 workspace (splitk_ws, ksplit * M * N floats) and the plain
+// epilogue (no SwiGLU, KV scatter or TF32 output split).
+// (query: the factor an unlimited workspace would allow).
+int splitk_count(const GemmArgs& g, int spatial, int k_blocks, int* kb_per, bool query = false) {
+  *kb_per = k_blocks;
+  if ((!g.splitk_ws && !query) || g.swiglu || g.kv_k || g.out_hi || spatial * 2 > g.sm_count || k_blocks < 2)
+    return 1;
+  const int want = std::max(1, g.sm_count / spatial);
+  int per = (k_blocks + want - 1) / want;
+  int ks = (k_blocks + per - 1) / per;
+  while (!query && ks > 1 && (size_t)ks * g.M * g.N > g.splitk_ws_floats) {  // fit the workspace
+    ++per;
+    ks = (k_blocks + per - 1) / per;
+  }
+  *kb_per = ks > 1 ? per : k_blocks;
+  return ks;
+}
+
 template <int KIND> size_t smem_bytes() {
   using T = GT<KIND>;
   const size_t stage = T::NA * kBM * T::BK * T::ELEM + T::NB * T::BN * T::BK * T::ELEM + T::CODE_BYTES;
@@ -611,8 +720,10 @@ template <int KIND> cudaError_t launch(const GemmArgs& g, cudaStream_t stream) {
   p.K = g.K;
   p.m_tiles = (g.M + kBM - 1) / kBM;
   p.n_tiles = (g.N + T::BN - 1) / T::BN;
-  p.num_tiles = p.m_tiles * p.n_tiles;
   p.k_blocks = (g.K + T::BK - 1) / T::BK;
+  p.ksplit = splitk_count(g, p.m_tiles * p.n_tiles, p.k_blocks, &p.kb_per);
+  p.ws = p.ksplit > 1 ? g.splitk_ws : nullptr;
+  p.num_tiles = p.m_tiles * p.n_tiles * p.ksplit;
   {
     // B bytes of one N-tile as stored in HBM (codes for FP8 / NF4, both TF32 parts)
     const double b_elem = byte_codes<KIND>() ? 1.0 : nibble_codes<KIND>() ? 0.5 : (double)(T::ELEM * T::NB);
@@ -625,6 +736,7 @@ template <int KIND> cudaError_t launch(const GemmArgs& g, cudaStream_t stream) {
   p.out_bf16 = g.out_bf16;
   p.out_hi = g.out_hi;
   p.out_lo = g.out_lo;
+  p.split_only = g.split_only && g.out_hi ? 1 : 0;
   p.b_scale = g.b_scale;
   p.ldb = g.ldb;
   p.col_scale = (KIND == kGemmFP8 || KIND == kGemmI8 || KIND == kGemmI4 || KIND == kGemmFP4) ? g.b_scale : nullptr;
@@ -649,6 +761,13 @@ template <int KIND> cudaError_t launch(const GemmArgs& g, cudaStream_t stream) {
   if (attr != cudaSuccess) return attr;
   const int grid = std::max(1, std::min(p.num_tiles, g.sm_count));
   gemm_tc_kernel<KIND><<<grid, T::THREADS, smem, stream>>>(ta, ta2, tb, tb2, p);
+  if (p.ksplit > 1) {
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    const int64_t total = (int64_t)g.M * g.N;
+    const int blocks = (int)std::min<int64_t>((total + 255) / 256, (int64_t)g.sm_count * 8);
+    splitk_finish_kernel<T::BN><<<blocks, 256, 0, stream>>>(p);
+  }
   return cudaGetLastError();
 }
 
@@ -677,6 +796,23 @@ bool gemm_tc_supported(const GemmArgs& g) {
   if (g.swiglu && (g.N % 64 || g.rope_cols || g.kv_k || (g.kind != kGemmBF16 && g.kind != kGemmTF32x3))) return false;
   return encode_fn() != nullptr;
 }
+
+namespace {
+int splitk_of(const GemmArgs& g, bool query) {
+  const int bn = g.kind == kGemmTF32x3 ? GT<kGemmTF32x3>::BN : GT<kGemmBF16>::BN;
+  const int bk = g.kind == kGemmTF32x3 ? GT<kGemmTF32x3>::BK : GT<kGemmBF16>::BK;
+  int kb_per = 0;
+  const int spatial = ((g.M + kBM - 1) / kBM) * ((g.N + bn - 1) / bn);
+  return splitk_count(g, spatial, (g.K + bk - 1) / bk, &kb_per, query);
+}
+}  // namespace
+
+size_t gemm_tc_splitk_floats(const GemmArgs& g) {
+  const int ks = splitk_of(g, true);
+  return ks > 1 ? (size_t)ks * g.M * g.N : 0;
+}
+
+int gemm_tc_launches(const GemmArgs& g) { return splitk_of(g, false) > 1 ? 2 : 1; }
 
 cudaError_t gemm_tc(const GemmArgs& g, cudaStream_t stream) {
   if (!gemm_tc_supported(g)) return cudaErrorInvalidValue;

@@ -55,6 +55,7 @@ struct GemmArgs {
   int out_bf16 = 0;         // 1: bf16 output, 0: fp32
   float* out_hi = nullptr;  // optional TF32 split of the output (fp32 outputs only)
   float* out_lo = nullptr;
+  int split_only = 0;       // with out_hi: write only the split, not out
   // RoPE fused on columns [0, rope_cols), heads of head_dim columns, pairs (i, i+hd/2)
   const float2* rope_tab = nullptr; // [max_pos, head_dim/2] (cos, sin)
   int rope_cols = 0;
@@ -74,7 +75,16 @@ struct GemmArgs {
   int swiglu_cols = 0;  // h columns written (>= the last chunk is clipped); 0: all
   uint32_t* err = nullptr;
   int sm_count = 148;
+  // Split-K workspace (FP32, splitk_ws_floats floats): when given and the output
+  // has few tiles (M <= 128 decode rows), the K range is split over the SMs and a
+  // second kernel adds the partials in order and applies the epilogue.
+  float* splitk_ws = nullptr;
+  size_t splitk_ws_floats = 0;
 };
+// Launches gemm_tc makes for these arguments (2 with split-K), and the split-K
+// workspace (floats) the arguments' shape would use, 0 when it is not split.
+int gemm_tc_launches(const GemmArgs& a);
+size_t gemm_tc_splitk_floats(const GemmArgs& a);
 
 // 2-D TMA descriptor over a row-major [outer][inner] matrix with row stride
 // ld_elems (cuTensorMapEncodeTiled through the runtime's driver entry point).
@@ -162,11 +172,20 @@ struct AttnArgs {
   uint32_t* err = nullptr;
   int sm_count = 148;
   int pair = -1;                   // tensor-core kernel: 1 CTA pairs (M = 256 UMMAs), 0 single CTAs, -1 auto
+  // FP32 3xTF32 kernel: q/k/v are the TF32 hi parts, these the FP32 remainders
+  // (same row strides).
+  const void* q_lo = nullptr;
+  const void* k_lo = nullptr;
+  const void* v_lo = nullptr;
 };
 bool attn_tc_supported(const AttnArgs& a);
 bool attn_tc_pair_supported(const AttnArgs& a);
 cudaError_t attn_prefill_tc(const AttnArgs& a, cudaStream_t s);
 cudaError_t attn_prefill_simt(const AttnArgs& a, cudaStream_t s);
+// FP32 on the tensor cores (attn_tf32.cu): 3xTF32 flash attention, head_dim 64, no
+// ring wrap; needs the hi / lo split of Q, K and V.
+bool attn_tf32_supported(const AttnArgs& a);
+cudaError_t attn_prefill_tf32(const AttnArgs& a, cudaStream_t s);
 // FP32, head_dim 64/128, no ring wrap: register-tiled CUDA-core kernel (attn_f32.cu).
 bool attn_f32_supported(const AttnArgs& a);
 cudaError_t attn_prefill_f32(const AttnArgs& a, cudaStream_t s);

@@ -274,18 +274,19 @@ welvet_status welvet_b200_split_tf32(const float* x, float* hi, float* lo, int64
   return launch_status(wv::split_tf32(x, hi, lo, n, as_stream(stream)), "split_tf32");
 }
 
-welvet_status welvet_b200_attention(const welvet_b200_mha_config* cfgp, int32_t batch, int32_t seq, const void* q,
-                                    const void* k, const void* v, void* out, int32_t impl, void* stream) {
-  wv::DeviceRestore restore_device;
-  if (!cfgp || !q || !k || !v || !out || batch <= 0 || seq <= 0)
-    return wv::to_c(Status::err(1, "attention: invalid argument"));
+namespace {
+// Attention arguments of a kernel-level call: q/k/v/out token-major with the
+// configuration's natural row strides.
+Status attention_args(const welvet_b200_mha_config* cfgp, int32_t batch, int32_t seq, const void* q, const void* k,
+                      const void* v, void* out, wv::AttnArgs* out_args) {
+  if (!cfgp || !q || !k || !v || !out || batch <= 0 || seq <= 0) return Status::err(1, "attention: invalid argument");
   wv::Cfg c;
   Status st = wv::resolve_config(*cfgp, &c);
-  if (!st) return wv::to_c(st);
+  if (!st) return st;
   wv::DeviceCtx* d = nullptr;
   st = wv::device_ctx(c.c.device, &d);
-  if (!st) return wv::to_c(st);
-  wv::AttnArgs a;
+  if (!st) return st;
+  wv::AttnArgs& a = *out_args;
   a.q = q;
   a.k = k;
   a.v = v;
@@ -312,6 +313,16 @@ welvet_status welvet_b200_attention(const welvet_b200_mha_config* cfgp, int32_t 
   a.scale = c.scale;
   a.err = d->err;
   a.sm_count = d->sm_count;
+  return Status::ok();
+}
+}  // namespace
+
+welvet_status welvet_b200_attention(const welvet_b200_mha_config* cfgp, int32_t batch, int32_t seq, const void* q,
+                                    const void* k, const void* v, void* out, int32_t impl, void* stream) {
+  wv::DeviceRestore restore_device;
+  wv::AttnArgs a;
+  Status st = attention_args(cfgp, batch, seq, q, k, v, out, &a);
+  if (!st) return wv::to_c(st);
   wv::count_launch();
   if (impl == 3) {  // tensor-core kernel on CTA pairs (M = 256 UMMAs)
     if (!wv::attn_tc_pair_supported(a))
@@ -325,6 +336,26 @@ welvet_status welvet_b200_attention(const welvet_b200_mha_config* cfgp, int32_t 
     return launch_status(wv::attn_prefill_tc(a, as_stream(stream)), "attn_prefill_tc");
   }
   return launch_status(wv::attn_prefill_simt(a, as_stream(stream)), "attn_prefill_simt");
+}
+
+welvet_status welvet_b200_attention_tf32(const welvet_b200_mha_config* cfgp, int32_t batch, int32_t seq,
+                                         const float* q_hi, const float* q_lo, const float* k_hi, const float* k_lo,
+                                         const float* v_hi, const float* v_lo, float* out, float* out_hi,
+                                         float* out_lo, void* stream) {
+  wv::DeviceRestore restore_device;
+  wv::AttnArgs a;
+  Status st = attention_args(cfgp, batch, seq, q_hi, k_hi, v_hi, out, &a);
+  if (!st) return wv::to_c(st);
+  if (!q_lo || !k_lo || !v_lo || (out_hi == nullptr) != (out_lo == nullptr))
+    return wv::to_c(Status::err(1, "attention: invalid argument"));
+  a.q_lo = q_lo;
+  a.k_lo = k_lo;
+  a.v_lo = v_lo;
+  a.out_hi = out_hi;
+  a.out_lo = out_lo;
+  if (!wv::attn_tf32_supported(a)) return wv::to_c(Status::err(2, "attention: 3xTF32 kernel unsupported here"));
+  wv::count_launch();
+  return launch_status(wv::attn_prefill_tf32(a, as_stream(stream)), "attn_prefill_tf32");
 }
 
 welvet_status welvet_b200_codec_roundtrip(int32_t dtype, const float* w, float* out, int64_t n, void* stream) {

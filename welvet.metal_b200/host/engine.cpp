@@ -487,6 +487,8 @@ struct Proj {
   int rope_cols = 0;
   const int* positions = nullptr;
   int pos_mod = 0;
+  bool splitk = false;  // few rows (decode): split K over the SMs through m->splitk_ws
+  bool split_only = false;  // with out_hi: out is not needed (written only if RoPE is unfused)
 };
 
 Status run_proj(Mha* m, const Proj& pj, cudaStream_t s) {
@@ -513,6 +515,7 @@ Status run_proj(Mha* m, const Proj& pj, cudaStream_t s) {
   g.out_hi = pj.out_hi;
   g.out_lo = pj.out_lo;
   g.err = m->dev->err;
+  g.split_only = pj.split_only ? 1 : 0;
   g.sm_count = m->dev->sm_count;
   const bool rope = pj.rope_cols > 0 && m->cfg.rope;
   if (rope) {
@@ -526,9 +529,18 @@ Status run_proj(Mha* m, const Proj& pj, cudaStream_t s) {
   const int hd = m->cfg.hd;
   const int bn = f32 ? 128 : 256;
   const bool fused_rope = rope && (hd == 64 || hd == 128 || hd == 256) && bn % hd == 0;
+  if (rope && !fused_rope) g.split_only = 0;  // rope_apply rotates out, then re-splits it
   if (gemm_tc_supported(g)) {
+    if (pj.splitk) {
+      const size_t floats = gemm_tc_splitk_floats(g);
+      if (floats) {
+        WV_TRY(m->splitk_ws.ensure(floats * sizeof(float)));
+        g.splitk_ws = m->splitk_ws.as<float>();
+        g.splitk_ws_floats = floats;
+      }
+    }
     WV_CUDA(gemm_tc(g, s), "gemm_tc");
-    count_launch();
+    count_launch(gemm_tc_launches(g));
   } else {
     if (g.kind == kGemmFP8 || g.kind == kGemmNF4)
       return Status::err(2, "mha: quantised weight GEMM needs TMA-aligned shapes");
@@ -576,7 +588,8 @@ AttnArgs attn_args(Mha* m, int batch, int seq, bool stream_mode) {
 Status run_attention(Mha* m, AttnArgs a, cudaStream_t s) {
   (void)m;
   cudaError_t e = cudaErrorNotSupported;
-  if (attn_tc_supported(a)) e = attn_prefill_tc(a, s);
+  if (attn_tf32_supported(a)) e = attn_prefill_tf32(a, s);
+  else if (attn_tc_supported(a)) e = attn_prefill_tc(a, s);
   if (e == cudaErrorNotSupported) {  // shape/mode outside the tensor-core kernel, or its
     cudaGetLastError();               // register split does not fit this build
     e = attn_prefill_simt(a, s);
@@ -672,6 +685,23 @@ Status mha_forward(Mha* m, int batch, int seq, const void* x, void* pre, void* p
     WV_TRY(m->attn_hi.ensure(Mc_max * m->qd_l * 4));
     WV_TRY(m->attn_lo.ensure(Mc_max * m->qd_l * 4));
   }
+  // FP32 attention on the tensor cores (3xTF32) reads the TF32 split of Q, K and
+  // V, written by the QKV projection's epilogue.
+  bool tf32_attn = false;
+  if (f32) {
+    AttnArgs t = attn_args(m, bc_max, seq, stream_mode);
+    t.q = t.k = t.v = t.q_lo = t.k_lo = t.v_lo = m->qkv.p;  // alignment stand-ins
+    t.ldq = t.ldk = m->nqkv;
+    t.out = pred ? pred : m->attn.p;
+    t.ldo = m->qd_l;
+    t.out_hi = m->attn_hi.as<float>();
+    t.out_lo = m->attn_lo.as<float>();
+    tf32_attn = attn_tf32_supported(t);
+    if (tf32_attn) {
+      WV_TRY(m->qkv_hi.ensure(Mc_max * m->nqkv * 4));
+      WV_TRY(m->qkv_lo.ensure(Mc_max * m->nqkv * 4));
+    }
+  }
   // RoPE positions: stream mode -> row index (global position), else row % seq.
   const int max_pos = stream_mode ? (int)M : seq;
   WV_TRY(ensure_rope(m, max_pos, s));
@@ -693,6 +723,11 @@ Status mha_forward(Mha* m, int batch, int seq, const void* x, void* pre, void* p
     q.w = m->wqkv.p;
     q.w_lo = m->wqkv_lo.p;
     q.w_scale = m->wqkv_scale.as<float>();
+    if (tf32_attn) {
+      q.out_hi = m->qkv_hi.as<float>();
+      q.out_lo = m->qkv_lo.as<float>();
+      q.split_only = kv == nullptr;  // the KV cache takes the FP32 rows
+    }
     if (f32) {
       WV_CUDA(split_tf32(static_cast<const float*>(xc), m->x_hi.as<float>(), m->x_lo.as<float>(), Mc * dm, s),
               "split x");
@@ -729,6 +764,17 @@ Status mha_forward(Mha* m, int batch, int seq, const void* x, void* pre, void* p
     if (f32) {
       a.out_hi = m->attn_hi.as<float>();
       a.out_lo = m->attn_lo.as<float>();
+    }
+    if (tf32_attn) {  // (every chunk qualifies when the largest one does)
+      const char* hb = static_cast<const char*>(m->qkv_hi.p);
+      const char* lb = static_cast<const char*>(m->qkv_lo.p);
+      a.q = hb;
+      a.k = hb + (size_t)m->qd_l * es;
+      a.v = hb + (size_t)(m->qd_l + m->kd_l) * es;
+      a.q_lo = lb;
+      a.k_lo = lb + (size_t)m->qd_l * es;
+      a.v_lo = lb + (size_t)(m->qd_l + m->kd_l) * es;
+      if (!attn_tf32_supported(a)) return Status::err(4, "mha: 3xTF32 attention refused a chunk");
     }
     prof_begin(kProfAttnPrefill, s);
     WV_TRY(run_attention(m, a, s));
@@ -987,6 +1033,7 @@ Status mha_decode(Mha* m, Kv* kv, int batch, const void* x, void* pre, void* pos
   q.ldo = m->nqkv;
   q.rope_cols = m->qd_l + m->kd_l;
   q.positions = m->positions.as<int>();
+  q.splitk = true;
   q.w = m->wqkv.p;
   q.w_lo = m->wqkv_lo.p;
   q.w_scale = m->wqkv_scale.as<float>();
@@ -1055,6 +1102,7 @@ Status mha_decode(Mha* m, Kv* kv, int batch, const void* x, void* pre, void* pos
   o.w = m->wo.p;
   o.w_lo = m->wo_lo.p;
   o.w_scale = m->wo_scale.as<float>();
+  o.splitk = true;
   if (f32) {
     WV_TRY(m->attn_hi.ensure((size_t)batch * m->qd_l * 4));
     WV_TRY(m->attn_lo.ensure((size_t)batch * m->qd_l * 4));

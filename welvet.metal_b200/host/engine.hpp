@@ -159,6 +159,8 @@ struct Mha {
   // workspaces
   DevBuf x_io, pre_io, post_io, x_hi, x_lo, qkv, attn, attn_hi, attn_lo, post_tmp;
   DevBuf positions, slots;
+  DevBuf splitk_ws;  // split-K partial sums of the decode projections
+  DevBuf qkv_hi, qkv_lo;  // FP32 path: TF32 split of q/k/v for the 3xTF32 attention
   // communicator (head-sharded tensor parallelism); the all-reduce of a forward
   // chunk runs on comm_stream while the next chunk computes on the caller's stream
   void* comm = nullptr;

@@ -43,7 +43,8 @@ EXT_SYMBOLS = ("welvet_b200_mha_config_default", "welvet_b200_mha_mount", "welve
                "welvet_b200_profile_enable", "welvet_b200_profile_read",
                "welvet_b200_decode_attention_static", "welvet_b200_swiglu_mount", "welvet_b200_swiglu_forward",
                "welvet_b200_swiglu_forward_host", "welvet_b200_swiglu_release", "welvet_b200_norm_forward",
-               "welvet_b200_embedding_forward", "welvet_b200_wait_probe", "welvet_b200_mha_set_output_mode")
+               "welvet_b200_embedding_forward", "welvet_b200_wait_probe", "welvet_b200_mha_set_output_mode",
+               "welvet_b200_attention_tf32")
 PROFILE_SLOTS = ("gemm_qkv", "attn_prefill", "gemm_o", "attn_decode", "gemm_qkv_decode", "gemm_o_decode",
                  "allreduce", "other", "gemm_gate_up", "gemm_down", "norm", "embedding", "attn_bwd", "gemm_grad")
 
@@ -164,7 +165,8 @@ def lib():
                                                       C.c_int32, _vp, _vp, C.c_int32, _vp]
     L.welvet_b200_wait_probe.argtypes = [C.c_uint64, _vp]
     L.welvet_b200_mha_set_output_mode.argtypes = [_vp, C.c_int32]
-    for name in ("welvet_b200_wait_probe", "welvet_b200_mha_set_output_mode",
+    L.welvet_b200_attention_tf32.argtypes = [cfgp, C.c_int32, C.c_int32] + [_vp] * 9 + [_vp]
+    for name in ("welvet_b200_wait_probe", "welvet_b200_mha_set_output_mode", "welvet_b200_attention_tf32",
 "welvet_b200_mha_mount", "welvet_b200_mha_forward", "welvet_b200_mha_forward_rows",
                  "welvet_b200_mha_check",
                  "welvet_b200_kv_create", "welvet_b200_kv_fill", "welvet_b200_mha_prefill",
@@ -480,6 +482,14 @@ def split_tf32(x, hi, lo, stream=None):
 def attention(cfg: MhaConfig, batch, seq, q, k, v, out, impl=0, stream=None):
     check(lib().welvet_b200_attention(C.byref(cfg), batch, seq, _ptr(q), _ptr(k), _ptr(v), _ptr(out), impl,
                                       _stream(stream)))
+
+
+def attention_tf32(cfg: MhaConfig, batch, seq, q, q_lo, k, k_lo, v, v_lo, out, out_hi=None, out_lo=None,
+                   stream=None):
+    """FP32 attention on the tensor cores from the TF32 split of q, k, v."""
+    check(lib().welvet_b200_attention_tf32(C.byref(cfg), batch, seq, _ptr(q), _ptr(q_lo), _ptr(k), _ptr(k_lo),
+                                           _ptr(v), _ptr(v_lo), _ptr(out), _ptr(out_hi), _ptr(out_lo),
+                                           _stream(stream)))
 
 
 def codec_roundtrip(dtype, w, out, stream=None):
