@@ -90,8 +90,12 @@ CODEC_STATS_FREE = (0, 1, 2, 3, 4, 5, 16, 24, 25)  # dtypes without a per-tensor
 METRIC = "MHA prefill tok/s (decode tok/s under 'decode'); % of roofline"
 METRIC_DECODE = "MHA decode tok/s; % of HBM roofline"
 SUB_WORKLOADS = ("cfg2", "cfg3", "cfg4-fp8", "cfg4-nf4", "cfg4-int4")
-# FP32 prefill attention runs on the CUDA cores (attn_f32_kernel): its roofline is the FFMA peak
-FP32_ATTENTION_ON_TENSOR_CORES = False
+# FP32 kernels (cfg2) run as 3xTF32 on the tensor cores: kind::tf32 issues at half
+# the kind::f16 rate (1.1 against 2.25 PFLOP/s dense, nominal) and every FP32 product
+# is three TF32 products, so their ceiling is the measured sustained BF16 rate / 6.
+# FP32 attention with a head_dim other than 64 runs on the CUDA cores
+# (attn_f32_kernel): its roofline is the FFMA peak.
+TF32X3_PER_BF16 = 1.0 / 6.0
 METRIC_CODEC = "FormatNone weight round trip GB/s (decode(encode(w)), dtypes 0-33)"
 METRIC_NBP = "MHA NormalBP tok/s (forward + backward + SGD)"
 METRIC_BLOCK = {"swiglu": "SwiGLU forward tok/s", "rmsnorm": "RMSNorm forward tok/s",
@@ -1023,9 +1027,14 @@ def run_mha(args, wname, rank, world, local, primary=True):
         # with a communicator the batch runs in chunks: several launches per step
         flops_launch = per_step[dom] * steps / max(cnt, 1)
         achieved = flops_launch / (avg_ms / 1e3) / 1e12
-        if prec == 0 and dom == "attn_prefill" and not FP32_ATTENTION_ON_TENSOR_CORES:
+        if prec == 0 and dom == "attn_prefill" and hd != 64:
             # FP32 attention on the CUDA cores (FFMA): 148 SMs x 128 lanes x 2 x 1.965 GHz
             peak, pkind, bound = 148 * 128 * 2 * 1.965e9 / 1e12, "nominal FP32 FFMA peak (CUDA cores)", "fp32-fma"
+        elif prec == 0:
+            peak = pk["bf16_sus"] * TF32X3_PER_BF16
+            pkind = (f"3xTF32 ceiling: {pk['src']} sustained bf16 / 2 (kind::tf32 rate) / 3 (TF32 products "
+                     f"per FP32 product) (derived from {pk['src']})")
+            bound = "tensor"
         else:
             peak, pkind, bound = pk["bf16_sus"], f"{pk['src']} sustained bf16 (of {pk['src']})", "tensor"
         cfg5_heads = prec == 1 and hd == 128 and hc == 32 and kd_l == 4096

@@ -15,7 +15,9 @@
 //   warp 9     UMMA issuer (one thread): S_j = Qh Kh^T + Qh Kl^T + Ql Kh^T (SS,
 //              kind::tf32) into TMEM buffer S_{j&1}; O_{j&1} += Ph V_h + Ph V_l +
 //              Pl V_h as TS MMAs whose A operand is P in TMEM (Ph over S_j, Pl in
-//              its own columns) and V an MN-major shared-memory operand
+//              its own columns) and V an MN-major shared-memory operand (TMA
+//              writes V in the 32-byte-atom 128-byte swizzle: MN-major TF32
+//              operands take no other swizzled layout)
 //   warp 10    TMA: V_j (hi, lo) into the V ring
 // The softmax is the BF16 kernel's (attn_tc.cu): log2-domain online max and sum,
 // masks evaluated only on blocks that straddle the mask edge (scores outside the
@@ -179,6 +181,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t IDESC_S = idesc_make(2, kBQ, kBK, 0, 0);
       constexpr uint32_t IDESC_PV = idesc_make(2, kBQ, kHD, 0, 1);
       constexpr uint32_t DHI = sdesc_hi_sw128(1024);
+      constexpr uint32_t DHI_V = sdesc_hi_sw128_32b(4 * 128);
       if (!mbar_wait(q_full, 0, abort_flag, p.err, kErrWaitFull)) goto done;
       const uint32_t qh = sdesc_lo(smem_u32(smem), 16);
       const uint32_t ql = qh + (uint32_t)((2 * kQChunk) >> 4);
@@ -203,9 +206,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         umma_commit(&s_full[g]);
         return true;
       };
-      // PV_i: A = P from TMEM (a k-step is 8 keys = 8 columns), B = V MN-major: a
-      // k-step is 8 key rows of 128 bytes (one 1024-byte swizzle atom), the second
-      // 32-column chunk of head_dim one chunk further (leading byte offset).
+      // PV_i: A = P from TMEM (a k-step is 8 keys = 8 columns), B = V MN-major in
+      // the 32-byte-atom 128-byte swizzle: a k-step is 8 key rows of 128 bytes (two
+      // 4-row swizzle groups, 512 bytes apart), the second 32-column chunk of
+      // head_dim one chunk further (leading byte offset).
       auto issue_pv = [&](int i) -> bool {
         const int vs = i % kSV, g = i & 1;
         if (!mbar_wait(&p_full[g], (i >> 1) & 1, abort_flag, p.err, kErrWaitOther)) return false;
@@ -219,9 +223,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int kk = 0; kk < kBK / 8; ++kk) {
           const uint32_t b_off = (uint32_t)((kk * 8 * 128) >> 4);
-          umma_tf32_ts_lohi(d, pl + (uint32_t)(kk * 8), vh + b_off, DHI, IDESC_PV, kk > 0 ? 1u : acc0);
-          umma_tf32_ts_lohi(d, ph + (uint32_t)(kk * 8), vl + b_off, DHI, IDESC_PV, 1u);
-          umma_tf32_ts_lohi(d, ph + (uint32_t)(kk * 8), vh + b_off, DHI, IDESC_PV, 1u);
+          umma_tf32_ts_lohi(d, pl + (uint32_t)(kk * 8), vh + b_off, DHI_V, IDESC_PV, kk > 0 ? 1u : acc0);
+          umma_tf32_ts_lohi(d, ph + (uint32_t)(kk * 8), vl + b_off, DHI_V, IDESC_PV, 1u);
+          umma_tf32_ts_lohi(d, ph + (uint32_t)(kk * 8), vh + b_off, DHI_V, IDESC_PV, 1u);
         }
         umma_commit(&v_empty[vs]);
         umma_commit(&p_empty[g]);
@@ -496,12 +500,13 @@ cudaError_t attn_prefill_tf32(const AttnArgs& a, cudaStream_t s) {
   const int rows = a.batch * a.seq;
   const int qd = a.num_heads * kHD, kd = a.num_kv_heads * kHD;
   const int F32 = (int)CU_TENSOR_MAP_DATA_TYPE_FLOAT32, SW = (int)CU_TENSOR_MAP_SWIZZLE_128B;
+  const int SWV = (int)CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;  // V is the MN-major operand
   if (!make_tma_2d(&maps[0], a.q, F32, 4, qd, rows, a.ldq, 32, kBQ, SW) ||
       !make_tma_2d(&maps[1], a.q_lo, F32, 4, qd, rows, a.ldq, 32, kBQ, SW) ||
       !make_tma_2d(&maps[2], a.k, F32, 4, kd, rows, a.ldk, 32, kBK, SW) ||
       !make_tma_2d(&maps[3], a.k_lo, F32, 4, kd, rows, a.ldk, 32, kBK, SW) ||
-      !make_tma_2d(&maps[4], a.v, F32, 4, kd, rows, a.ldk, 32, kBK, SW) ||
-      !make_tma_2d(&maps[5], a.v_lo, F32, 4, kd, rows, a.ldk, 32, kBK, SW))
+      !make_tma_2d(&maps[4], a.v, F32, 4, kd, rows, a.ldk, 32, kBK, SWV) ||
+      !make_tma_2d(&maps[5], a.v_lo, F32, 4, kd, rows, a.ldk, 32, kBK, SWV))
     return cudaErrorInvalidValue;
   TParams p{};
   FParams& f = p.f;

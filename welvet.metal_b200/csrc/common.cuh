@@ -221,6 +221,14 @@ WV_DEV void umma_tf32_ts_lohi(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, u
 WV_DEV uint32_t sdesc_lo(uint32_t saddr, uint32_t lbo_bytes) {
   return ((saddr & 0x3FFFFu) >> 4) | (((lbo_bytes >> 4) & 0x3FFFu) << 16);
 }
+// High word for an MN-major 32-bit (TF32) operand: layout type 1, the 128-byte
+// swizzle of 32-byte atoms that TMA writes with CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+// (the only swizzled layout the MMA takes for MN-major TF32). Its pattern repeats
+// every 4 rows of 128 bytes, so the stride byte offset is the stride of those
+// 4-row groups along K.
+__host__ __device__ constexpr uint32_t sdesc_hi_sw128_32b(uint32_t sbo_bytes) {
+  return ((sbo_bytes >> 4) & 0x3FFFu) | (1u << 14) | (1u << 29);
+}
 __host__ __device__ constexpr uint32_t sdesc_hi_sw128(uint32_t sbo_bytes) {
   return ((sbo_bytes >> 4) & 0x3FFFu) | (1u << 14) | (2u << 29);
 }
