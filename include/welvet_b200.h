@@ -156,8 +156,11 @@ WELVET_API welvet_status welvet_b200_split_tf32(const float* x, float* hi, float
 /* Attention forward over token-major q [*, q_dim], k/v [*, kv_dim] (RoPE already
  * applied) -> out [*, q_dim] (reference op_attention forward,
  * shaders/ops_mha.metal:31-127). impl 0 = best available, 1 = CUDA-core kernel,
- * 2 = tensor-core kernel (fails when unsupported), 3 = tensor-core kernel on CTA
- * pairs (head_dim 128, seq a multiple of 256). */
+ * 2 = tensor-core kernel (fails when unsupported; the persistent form, one CTA per
+ * SM looping over query tiles), 3 = tensor-core kernel on CTA pairs (head_dim 128,
+ * seq a multiple of 256), 4 = tensor-core kernel with one CTA per query tile. The
+ * persistent form counts its tiles in one per-device word: calls of impl 0/2 on
+ * one device must not overlap in time (one stream, or ordered streams). */
 WELVET_API welvet_status welvet_b200_attention(const welvet_b200_mha_config* cfg, int32_t batch,
                                                int32_t seq, const void* q, const void* k,
                                                const void* v, void* out, int32_t impl,

@@ -120,7 +120,7 @@ def test_cfg4_quantised_full_shape(torch_cuda, weight_format):
     layer.close()
 
 
-@pytest.mark.parametrize("impl", [2, 3])  # single CTAs; CTA pairs (M = 256 UMMAs)
+@pytest.mark.parametrize("impl", [2, 3, 4])  # persistent; CTA pairs (M = 256 UMMAs); one CTA per tile
 def test_cfg5_heads_tensor_core_attention_at_8192(torch_cuda, impl):
     torch = torch_cuda
     T, H, hd = 8192, 2, 128

@@ -606,6 +606,7 @@ bool attn_tc_pair_supported(const AttnArgs& a) {
 cudaError_t attn_prefill_tc(const AttnArgs& a, cudaStream_t s) {
   if (!attn_tc_supported(a)) return cudaErrorInvalidValue;
   const bool pair = a.pair > 0 || (a.pair < 0 && kPairDefault && attn_tc_pair_supported(a));
+  if (!pair && a.tile_ctr) return attn_prefill_persist(a, s);
   if (pair) {
     if (!attn_tc_pair_supported(a)) return cudaErrorInvalidValue;
     return launch<128, true>(a, s);

@@ -120,6 +120,18 @@ WV_DEV void tma_load_3d(void* dst, const void* map, uint64_t* bar, int32_t x, in
 WV_DEV void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
+// TMA tile store from shared memory (the map's box at (x, y); x a multiple of 16
+// bytes, y >= 0), tracked as a bulk group of the issuing thread.
+WV_DEV void tma_store_2d(const void* map, const void* src, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+WV_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// The issuing thread's bulk groups have finished reading shared memory.
+WV_DEV void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// ... and their global writes are complete.
+WV_DEV void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // ------------------------------------------------------------------- tcgen05
 WV_DEV void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
@@ -406,6 +418,10 @@ WV_DEV float to_tf32(float x) {
   return __uint_as_float(r & 0xFFFFE000u);
 }
 
+WV_DEV void st_shared_v4(void* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(p)), "r"(a), "r"(b), "r"(c), "r"(d)
+               : "memory");
+}
 WV_DEV void st_global_v4(void* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.global.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(a), "r"(b), "r"(c),
                "r"(d)

@@ -95,6 +95,13 @@ bool make_tma_2d(void* map128, const void* base, int dt, int elem_bytes, uint64_
 // True when the tensor-core GEMM supports these shapes (TMA alignment).
 bool gemm_tc_supported(const GemmArgs& a);
 cudaError_t gemm_tc(const GemmArgs& a, cudaStream_t stream);
+// Few-row BF16 projection (decode steps, M <= 64): streams the weights once at HBM
+// rate on m16n8k16 MMAs, K split over a cluster of CTAs and reduced through
+// distributed shared memory; RoPE and the KV page scatter in the epilogue
+// (gemv_decode.cu). Uses a, lda, b (ldb == K), M, N, K, out (bf16), ldo, the RoPE
+// and KV fields, err, sm_count.
+bool gemv_decode_supported(const GemmArgs& a);
+cudaError_t gemv_decode(const GemmArgs& a, cudaStream_t stream);
 // CUDA-core fallback for shapes the TMA path cannot address (FP32 and BF16
 // operands only; same epilogue semantics, RoPE excluded).
 cudaError_t gemm_simt(const GemmArgs& a, cudaStream_t stream);
@@ -172,6 +179,10 @@ struct AttnArgs {
   uint32_t* err = nullptr;
   int sm_count = 148;
   int pair = -1;                   // tensor-core kernel: 1 CTA pairs (M = 256 UMMAs), 0 single CTAs, -1 auto
+  // Tile counter of the persistent tensor-core kernel (one device int, zeroed by
+  // each launch on its stream; launches that share it must not overlap in time).
+  // Null: one CTA per query tile.
+  int* tile_ctr = nullptr;
   // FP32 3xTF32 kernel: q/k/v are the TF32 hi parts, these the FP32 remainders
   // (same row strides).
   const void* q_lo = nullptr;
@@ -181,6 +192,9 @@ struct AttnArgs {
 bool attn_tc_supported(const AttnArgs& a);
 bool attn_tc_pair_supported(const AttnArgs& a);
 cudaError_t attn_prefill_tc(const AttnArgs& a, cudaStream_t s);
+// Persistent form of the BF16 tensor-core kernel (attn_persist.cu): needs tile_ctr.
+bool attn_persist_supported(const AttnArgs& a);
+cudaError_t attn_prefill_persist(const AttnArgs& a, cudaStream_t s);
 cudaError_t attn_prefill_simt(const AttnArgs& a, cudaStream_t s);
 // FP32 on the tensor cores (attn_tf32.cu): 3xTF32 flash attention, head_dim 64, no
 // ring wrap; needs the hi / lo split of Q, K and V.

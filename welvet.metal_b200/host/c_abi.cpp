@@ -313,6 +313,7 @@ Status attention_args(const welvet_b200_mha_config* cfgp, int32_t batch, int32_t
   a.scale = c.scale;
   a.err = d->err;
   a.sm_count = d->sm_count;
+  a.tile_ctr = d->tile_ctr;
   return Status::ok();
 }
 }  // namespace
@@ -330,9 +331,10 @@ welvet_status welvet_b200_attention(const welvet_b200_mha_config* cfgp, int32_t 
     a.pair = 1;
     return launch_status(wv::attn_prefill_tc(a, as_stream(stream)), "attn_prefill_tc (pairs)");
   }
-  if (impl == 2 || (impl == 0 && wv::attn_tc_supported(a))) {
+  if (impl == 2 || impl == 4 || (impl == 0 && wv::attn_tc_supported(a))) {
     if (!wv::attn_tc_supported(a)) return wv::to_c(Status::err(2, "attention: tensor-core kernel unsupported here"));
-    if (impl == 2) a.pair = 0;
+    if (impl == 2 || impl == 4) a.pair = 0;
+    if (impl == 4) a.tile_ctr = nullptr;  // one CTA per query tile
     return launch_status(wv::attn_prefill_tc(a, as_stream(stream)), "attn_prefill_tc");
   }
   return launch_status(wv::attn_prefill_simt(a, as_stream(stream)), "attn_prefill_simt");

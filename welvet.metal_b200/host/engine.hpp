@@ -124,6 +124,7 @@ struct DeviceCtx {
   uint32_t* err = nullptr;     // device error word
   float* scratch = nullptr;    // 4096 floats (reductions)
   float* scalars = nullptr;    // 64 floats (per-tensor scales)
+  int* tile_ctr = nullptr;     // tile counter of the standalone persistent attention entry
 };
 Status device_ctx(int device, DeviceCtx** out);  // device < 0: current
 Status check_device_error(DeviceCtx* d);         // sync + read/clear the error word
@@ -161,6 +162,7 @@ struct Mha {
   DevBuf positions, slots;
   DevBuf splitk_ws;  // split-K partial sums of the decode projections
   DevBuf qkv_hi, qkv_lo;  // FP32 path: TF32 split of q/k/v for the 3xTF32 attention
+  DevBuf attn_ctr;        // tile counter of the persistent prefill attention (one int)
   // communicator (head-sharded tensor parallelism); the all-reduce of a forward
   // chunk runs on comm_stream while the next chunk computes on the caller's stream
   void* comm = nullptr;
