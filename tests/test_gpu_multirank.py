@@ -2,7 +2,9 @@
 communicator, the row-sharded host-buffer forward (welvet_b200_mha_forward_rows)
 against the FP64 oracle's forward of the whole batch (per-sequence semantics, the
 same FP32 or BF16-rounded weights and inputs). Each rank passes only its half of
-the sequences and receives the summed output rows of that half."""
+the sequences and receives the summed output rows of that half. Then two decode
+steps over each rank's KV heads, their outputs summed through the NVLink
+peer-memory all-reduce, against the oracle's decode of the whole layer."""
 import os
 import socket
 
@@ -56,6 +58,30 @@ def _worker(rank, world, port, out_dir, precision):
     np.save(os.path.join(out_dir, f"rs{rank}.npy"), own)
     if rank == 0:
         np.save(os.path.join(out_dir, "x.npy"), x.float().numpy())
+    # decode: two steps over a paged KV cache holding this rank's KV heads; the
+    # batch x d_model output is all-reduced over NVLink peer memory (one kernel),
+    # the second step on the other parity of the peer workspace
+    hd, L = d // H, 64
+    kdf = NK * hd
+    kc = torch.from_numpy(W.synthetic(B * L * kdf, 2, 1, 0.5).reshape(B, L, kdf)).to(dt)
+    vc = torch.from_numpy(W.synthetic(B * L * kdf, 2, 1, 0.5, offset=B * L * kdf).reshape(B, L, kdf)).to(dt)
+    kh0, khc = hb // (H // NK), hc // (H // NK)
+    kv = W.KvCache(layer, B, L + 16)
+    kv.fill(B, L, kc[:, :, kh0 * hd:(kh0 + khc) * hd].contiguous().cuda(),
+            vc[:, :, kh0 * hd:(kh0 + khc) * hd].contiguous().cuda())
+    for step in range(2):
+        xs = torch.from_numpy(W.synthetic(B * d, 30 + step, 1, 1.0).reshape(B, d)).to(dt)
+        pre_d = torch.zeros(B, hc * hd, device="cuda", dtype=dt)
+        post_d = torch.zeros(B, d, device="cuda", dtype=dt)
+        layer.decode(kv, B, xs.cuda(), pre_d, post_d)
+        torch.cuda.synchronize()
+        layer.check_device()
+        np.save(os.path.join(out_dir, f"dec{rank}_{step}.npy"), post_d.float().cpu().numpy())
+        if rank == 0:
+            np.save(os.path.join(out_dir, f"decx{step}.npy"), xs.float().numpy())
+    if rank == 0:
+        np.save(os.path.join(out_dir, "kc.npy"), kc.float().numpy())
+        np.save(os.path.join(out_dir, "vc.npy"), vc.float().numpy())
     layer.close()
     dist.barrier()
     dist.destroy_process_group()
@@ -86,3 +112,16 @@ def test_forward_rows_two_ranks(tmp_path, precision):
         rows = np.concatenate([np.arange(c0 + r * 128, c0 + (r + 1) * 128) for c0 in range(0, B * T, 256)])
         rs = np.load(tmp_path / f"rs{r}.npy")
         assert rel_err(rs, want[rows]) < tol, (r, rel_err(rs, want[rows]))
+    # decode steps: every rank holds the whole summed output
+    kc, vc = np.load(tmp_path / "kc.npy"), np.load(tmp_path / "vc.npy")
+    L = kc.shape[1]
+    for step in range(2):
+        xs = np.load(tmp_path / f"decx{step}.npy")
+        _, want_d, kn, vn = O.mha_decode(oc, [L + step] * B, kc, vc, *Ws, xs)
+        for r in range(2):
+            got_d = np.load(tmp_path / f"dec{r}_{step}.npy")
+            assert rel_err(got_d, want_d) < tol, (step, r, rel_err(got_d, want_d))
+        if precision == 1:  # the cache holds the new rows in bf16
+            kn, vn = bf16_round(kn), bf16_round(vn)
+        kc = np.concatenate([kc, kn[:, None, :]], axis=1)
+        vc = np.concatenate([vc, vn[:, None, :]], axis=1)

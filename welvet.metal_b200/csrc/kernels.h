@@ -18,6 +18,7 @@ enum : uint32_t {
   kErrWaitAccFull = 3,
   kErrWaitAccEmpty = 4,
   kErrWaitOther = 5,
+  kErrPeerWait = 6,   // a peer rank's data did not arrive (peer-memory all-reduce)
 };
 
 // --------------------------------------------------------------------- GEMM
@@ -102,6 +103,29 @@ cudaError_t gemm_tc(const GemmArgs& a, cudaStream_t stream);
 // and KV fields, err, sm_count.
 bool gemv_decode_supported(const GemmArgs& a);
 cudaError_t gemv_decode(const GemmArgs& a, cudaStream_t stream);
+// One-shot all-reduce (sum) of a small vector over NVLink peer memory (peer.cu):
+// every rank's receive area (slot [parity][sender] of slot_bytes, then the flags
+// [parity][sender][kPeerCtas] uint32) mapped into this process; epoch = the call
+// number (from 1, the same on every rank), parity = epoch & 1. count * element size
+// must be a multiple of 16 bytes and at most slot_bytes; in/out 16-byte aligned,
+// out may equal in.
+constexpr int kPeerMaxRanks = 8;
+constexpr int kPeerCtas = 32;
+struct PeerArgs {
+  const void* in = nullptr;
+  void* out = nullptr;
+  size_t count = 0;
+  int bf16 = 1;
+  int nranks = 0, rank = 0;
+  void* areas[kPeerMaxRanks] = {};
+  size_t slot_bytes = 0;
+  size_t flags_off = 0;
+  uint32_t epoch = 0;
+  uint64_t wait_ns = 0;
+  uint32_t* err = nullptr;
+};
+cudaError_t peer_allreduce(const PeerArgs& a, cudaStream_t s);
+
 // CUDA-core fallback for shapes the TMA path cannot address (FP32 and BF16
 // operands only; same epilogue semantics, RoPE excluded).
 cudaError_t gemm_simt(const GemmArgs& a, cudaStream_t stream);

@@ -1,0 +1,124 @@
+// One-shot all-reduce of a small vector over NVLink peer memory (the output of a
+// head-sharded decode step: batch x d_model partial sums per rank), in place of an
+// NCCL all-reduce whose fixed latency (tens of microseconds at 8 ranks) is several
+// times the transfer. The reference is single-device and has no counterpart.
+//
+// Every rank owns a receive area with one slot per sender and two parities, mapped
+// into every other rank's address space (CUDA IPC). One launch per call, kPeerCtas
+// CTAs, CTA c owning a contiguous piece of the vector:
+//   1. push: CTA c writes its piece of the local partial into slot[rank] of every
+//      rank's area (NVLink stores to the peers, plain stores to itself);
+//   2. publish: after a system-scope fence, a release store of the call's epoch into
+//      flag[parity][rank][c] of every rank;
+//   3. wait: CTA c waits (bounded by time) until flag[parity][q][c] of its own area
+//      holds the epoch for every sender q;
+//   4. reduce: out = sum over q = 0 .. n-1 of slot[q], in rank order, so every rank
+//      computes bit-identical sums.
+// Epochs increase by one per call on every rank (all ranks call in the same order),
+// and the parity alternates, so a slot is rewritten two calls later at the earliest:
+// by then its reader has finished (the writer has seen the reader's flags of the
+// call in between, which the reader publishes only after its previous call ended).
+// A wait that runs out records kErrPeerWait in the error word and the CTA skips its
+// reduction; nothing traps.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace wv {
+namespace {
+
+constexpr int kThreads = 512;
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+template <bool BF16>
+__global__ void __launch_bounds__(kThreads) peer_allreduce_kernel(const PeerArgs a) {
+  const int n = a.nranks, par = (int)(a.epoch & 1u), cta = blockIdx.x;
+  // 16-byte units of the vector, split over the CTAs
+  const size_t units = (a.count * (BF16 ? 2 : 4) + 15) / 16;
+  const size_t per = (units + gridDim.x - 1) / gridDim.x;
+  const size_t u0 = (size_t)cta * per, u1 = min(units, u0 + per);
+  const uint4* src = static_cast<const uint4*>(a.in);
+  // 1. push this CTA's piece into slot[par][rank] of every rank
+  for (int p = 0; p < n; ++p) {
+    uint4* dst = reinterpret_cast<uint4*>(static_cast<char*>(a.areas[p]) +
+                                          ((size_t)par * n + a.rank) * a.slot_bytes);
+    for (size_t u = u0 + threadIdx.x; u < u1; u += kThreads) dst[u] = src[u];
+  }
+  __syncthreads();
+  // 2. publish: flag[par][rank][cta] = epoch on every rank. The barrier orders the
+  // CTA's stores before the flag writers' system-scope fence and release stores.
+  if (threadIdx.x < (unsigned)n) {
+    __threadfence_system();
+    uint32_t* f = reinterpret_cast<uint32_t*>(static_cast<char*>(a.areas[threadIdx.x]) + a.flags_off);
+    st_release_sys(f + ((size_t)par * n + a.rank) * gridDim.x + cta, a.epoch);
+  }
+  // 3. wait for every sender's piece of this CTA
+  __shared__ int ok_all;
+  if (threadIdx.x == 0) ok_all = 1;
+  __syncthreads();
+  if (threadIdx.x < (unsigned)n) {
+    const uint32_t* f = reinterpret_cast<const uint32_t*>(static_cast<const char*>(a.areas[a.rank]) + a.flags_off) +
+                        ((size_t)par * n + threadIdx.x) * gridDim.x + cta;
+    const uint64_t t0 = globaltimer();
+    while (ld_acquire_sys(f) != a.epoch) {
+      if (globaltimer() - t0 > a.wait_ns) {
+        atomicCAS(a.err, 0u, (uint32_t)kErrPeerWait);
+        ok_all = 0;
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  if (!ok_all) return;
+  // 4. reduce in rank order
+  const char* own = static_cast<const char*>(a.areas[a.rank]) + (size_t)par * n * a.slot_bytes;
+  uint4* out = static_cast<uint4*>(a.out);
+  for (size_t u = u0 + threadIdx.x; u < u1; u += kThreads) {
+    float acc[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+    for (int q = 0; q < n; ++q) {
+      const uint4 v = reinterpret_cast<const uint4*>(own + (size_t)q * a.slot_bytes)[u];
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+      if (BF16) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          acc[2 * e] += __uint_as_float(w[e] << 16);
+          acc[2 * e + 1] += __uint_as_float(w[e] & 0xFFFF0000u);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[e] += __uint_as_float(w[e]);
+      }
+    }
+    if (BF16) {
+      out[u] = make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]), pack_bf16x2(acc[4], acc[5]),
+                          pack_bf16x2(acc[6], acc[7]));
+    } else {
+      out[u] = make_uint4(__float_as_uint(acc[0]), __float_as_uint(acc[1]), __float_as_uint(acc[2]),
+                          __float_as_uint(acc[3]));
+    }
+  }
+}
+
+}  // namespace
+
+cudaError_t peer_allreduce(const PeerArgs& a, cudaStream_t s) {
+  if (a.nranks < 1 || a.nranks > kPeerMaxRanks || a.rank < 0 || a.rank >= a.nranks || !a.in || !a.out ||
+      (reinterpret_cast<uintptr_t>(a.in) & 15) || (reinterpret_cast<uintptr_t>(a.out) & 15))
+    return cudaErrorInvalidValue;
+  const size_t bytes = a.count * (a.bf16 ? 2 : 4);
+  if (bytes % 16 || bytes > a.slot_bytes) return cudaErrorInvalidValue;
+  if (a.bf16) peer_allreduce_kernel<true><<<kPeerCtas, kThreads, 0, s>>>(a);
+  else peer_allreduce_kernel<false><<<kPeerCtas, kThreads, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace wv

@@ -26,6 +26,8 @@
 #include <cstring>
 #include <mutex>
 #include <thread>
+#include <vector>
+#include <algorithm>
 
 #include "engine.hpp"
 
@@ -194,6 +196,98 @@ Status comm_reducescatter(Mha* m, void* buf, size_t count, bool bf16, cudaStream
   return enqueued(m, r, "ncclReduceScatter");
 }
 
+// ------------------------------------------------------- NVLink peer workspace
+namespace {
+void peer_release(Mha* m) {
+  for (int p = 0; p < kPeerMaxRanks; ++p) {
+    if (m->peer_areas[p] && m->peer_areas[p] != m->peer_area) cudaIpcCloseMemHandle(m->peer_areas[p]);
+    m->peer_areas[p] = nullptr;
+  }
+  if (m->peer_area) cudaFree(m->peer_area);
+  m->peer_area = nullptr;
+  m->peer_slot_bytes = m->peer_flags_off = 0;
+  m->peer_epoch = 0;
+}
+
+bool peer_disabled() {
+  static const bool off = [] {
+    const char* v = std::getenv("WELVET_B200_PEER_ALLREDUCE");
+    return v && v[0] == '0';
+  }();
+  return off;
+}
+
+// Every rank allocates its receive area (2 parities x n senders x slot bytes, then
+// the flags), zeroes it, and the CUDA IPC handles are all-gathered over NCCL; each
+// rank opens the others' areas. Collective (same slot size on every rank).
+Status peer_setup(Mha* m, size_t bytes, cudaStream_t s) {
+  if (m->peer_area && m->peer_slot_bytes >= bytes) return Status::ok();
+  peer_release(m);
+  const int n = m->nranks;
+  const size_t slot = (bytes + 255) / 256 * 256;
+  const size_t flags_off = 2 * (size_t)n * slot;
+  const size_t total = flags_off + 2 * (size_t)n * kPeerCtas * sizeof(uint32_t);
+  WV_CUDA(cudaMalloc(&m->peer_area, total), "peer workspace");
+  WV_CUDA(cudaMemsetAsync(m->peer_area, 0, total, s), "peer workspace clear");
+  cudaIpcMemHandle_t own;
+  WV_CUDA(cudaIpcGetMemHandle(&own, m->peer_area), "cudaIpcGetMemHandle");
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+  DevBuf handles;
+  WV_TRY(handles.ensure((size_t)n * 64));
+  WV_CUDA(cudaMemcpyAsync(static_cast<char*>(handles.p) + (size_t)m->rank * 64, &own, 64, cudaMemcpyHostToDevice, s),
+          "peer handle");
+  WV_TRY(comm_allgather(m, handles.p, 16, false, s));  // 64 bytes = 16 floats per rank
+  WV_TRY(comm_wait(m, s, "peer handle exchange"));
+  std::vector<cudaIpcMemHandle_t> all(n);
+  WV_CUDA(cudaMemcpy(all.data(), handles.p, (size_t)n * 64, cudaMemcpyDeviceToHost), "peer handles");
+  for (int p = 0; p < n; ++p) {
+    if (p == m->rank) {
+      m->peer_areas[p] = m->peer_area;
+      continue;
+    }
+    void* ptr = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&ptr, all[p], cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      peer_release(m);
+      return cuda_status(e, "cudaIpcOpenMemHandle (peer workspace)");
+    }
+    m->peer_areas[p] = ptr;
+  }
+  m->peer_slot_bytes = slot;
+  m->peer_flags_off = flags_off;
+  m->peer_epoch = 0;
+  return Status::ok();
+}
+}  // namespace
+
+bool comm_peer_ok(const Mha* m, size_t bytes) {
+  return m->comm && m->nranks > 1 && m->nranks <= kPeerMaxRanks && bytes > 0 && bytes % 16 == 0 &&
+         bytes <= kPeerMaxBytes && !peer_disabled();
+}
+
+Status comm_peer_allreduce(Mha* m, void* buf, size_t count, bool bf16, cudaStream_t s) {
+  const size_t bytes = count * (bf16 ? 2 : 4);
+  if (!comm_peer_ok(m, bytes)) return Status::err(2, "comm: peer all-reduce not available here");
+  WV_TRY(peer_setup(m, bytes, s));
+  PeerArgs a;
+  a.in = buf;
+  a.out = buf;
+  a.count = count;
+  a.bf16 = bf16 ? 1 : 0;
+  a.nranks = m->nranks;
+  a.rank = m->rank;
+  for (int p = 0; p < m->nranks; ++p) a.areas[p] = m->peer_areas[p];
+  a.slot_bytes = m->peer_slot_bytes;
+  a.flags_off = m->peer_flags_off;
+  a.epoch = ++m->peer_epoch;
+  // The device wait is bounded like the host's collective waits (capped at 60 s).
+  a.wait_ns = (uint64_t)std::min<int64_t>(m->comm_timeout_ms, 60000) * 1000000ull;
+  a.err = m->dev->err;
+  WV_CUDA(peer_allreduce(a, s), "peer_allreduce");
+  count_launch();
+  return Status::ok();
+}
+
 Status comm_poll(Mha* m) {
   if (!m->comm || !nccl().ok) return Status::ok();
   ncclResult_t state = ncclSuccess;
@@ -232,6 +326,7 @@ Status comm_wait(Mha* m, cudaStream_t s, const char* what) {
 
 void comm_release(Mha* m) {
   if (!m) return;
+  peer_release(m);
   if (m->comm) {
     if (nccl().ok) nccl().comm_destroy(static_cast<ncclComm_t>(m->comm));
     m->comm = nullptr;

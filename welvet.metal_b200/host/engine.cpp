@@ -12,6 +12,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 
@@ -160,6 +161,7 @@ const char* err_reason(uint32_t code) {
   case kErrWaitAccFull: return "device wait timeout (accumulator full)";
   case kErrWaitAccEmpty: return "device wait timeout (accumulator empty)";
   case kErrWaitOther: return "device wait timeout";
+  case kErrPeerWait: return "peer rank's data did not arrive (peer-memory all-reduce)";
   case 0x100: return "RoPE position outside the table";
   default: return "device error";
   }
@@ -189,6 +191,7 @@ Status device_ctx(int device, DeviceCtx** out) {
   WV_CUDA(cudaMemset(d->err, 0, 256), "cudaMemset err");
   WV_CUDA(cudaMalloc(&d->scratch, 4096 * sizeof(float)), "cudaMalloc scratch");
   WV_CUDA(cudaMalloc(&d->scalars, 64 * sizeof(float)), "cudaMalloc scalars");
+  WV_CUDA(cudaMalloc(&d->tile_ctr, 256), "cudaMalloc tile counter");
   WV_CUDA(cudaDeviceSynchronize(), "init");
   g_devs[device] = d;
   *out = d;
@@ -489,9 +492,27 @@ struct Proj {
   int pos_mod = 0;
   bool splitk = false;  // few rows (decode): split K over the SMs through m->splitk_ws
   bool split_only = false;  // with out_hi: out is not needed (written only if RoPE is unfused)
+  // Decode: the K and V column ranges [kv_col0, kv_col0 + 2 kv_dim) may go straight
+  // to the KV page pools (row b to slot kv_slot[b]) when the kernel can scatter them.
+  void* kv_k = nullptr;
+  void* kv_v = nullptr;
+  const int* kv_slot = nullptr;
+  int kv_col0 = 0, kv_dim = 0;
 };
 
-Status run_proj(Mha* m, const Proj& pj, cudaStream_t s) {
+// Few-row BF16 projections (decode) run as a GEMV streaming the weights at HBM rate
+// unless WELVET_B200_DECODE_GEMV=0 selects the split-K tensor-core GEMM.
+bool decode_gemv_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("WELVET_B200_DECODE_GEMV");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
+// *kv_done (optional) tells whether the K/V columns went to the page pools.
+Status run_proj(Mha* m, const Proj& pj, cudaStream_t s, bool* kv_done = nullptr) {
+  if (kv_done) *kv_done = false;
   const bool f32 = m->precision == 0;
   GemmArgs g;
   g.kind = f32 ? kGemmTF32x3
@@ -527,6 +548,21 @@ Status run_proj(Mha* m, const Proj& pj, cudaStream_t s) {
     g.pos_mod = pj.pos_mod;
   }
   const int hd = m->cfg.hd;
+  if (pj.splitk && !f32 && decode_gemv_enabled()) {
+    GemmArgs v = g;
+    v.head_dim = hd;
+    v.kv_k = pj.kv_k;
+    v.kv_v = pj.kv_v;
+    v.kv_slot = pj.kv_slot;
+    v.kv_col0 = pj.kv_col0;
+    v.kv_dim = pj.kv_dim;
+    if (gemv_decode_supported(v)) {
+      WV_CUDA(gemv_decode(v, s), "gemv_decode");
+      count_launch();
+      if (kv_done) *kv_done = pj.kv_k != nullptr;
+      return Status::ok();
+    }
+  }
   const int bn = f32 ? 128 : 256;
   const bool fused_rope = rope && (hd == 64 || hd == 128 || hd == 256) && bn % hd == 0;
   if (rope && !fused_rope) g.split_only = 0;  // rope_apply rotates out, then re-splits it
@@ -582,6 +618,7 @@ AttnArgs attn_args(Mha* m, int batch, int seq, bool stream_mode) {
   a.is_bf16 = m->precision == 1;
   a.err = m->dev->err;
   a.sm_count = m->dev->sm_count;
+  a.tile_ctr = m->attn_ctr.as<int>();  // null until mha_forward sized it
   return a;
 }
 
@@ -702,6 +739,7 @@ Status mha_forward(Mha* m, int batch, int seq, const void* x, void* pre, void* p
       WV_TRY(m->qkv_lo.ensure(Mc_max * m->nqkv * 4));
     }
   }
+  if (!f32) WV_TRY(m->attn_ctr.ensure(256));  // the persistent attention's tile counter
   // RoPE positions: stream mode -> row index (global position), else row % seq.
   const int max_pos = stream_mode ? (int)M : seq;
   WV_TRY(ensure_rope(m, max_pos, s));
@@ -1048,13 +1086,22 @@ Status mha_decode(Mha* m, Kv* kv, int batch, const void* x, void* pre, void* pos
   } else {
     q.a = xd;
   }
+  q.kv_k = kv->k_pool.p;
+  q.kv_v = kv->v_pool.p;
+  q.kv_slot = m->slots.as<int>();
+  q.kv_col0 = m->qd_l;
+  q.kv_dim = m->kd_l;
+  bool kv_done = false;
   prof_begin(kProfGemmQkvDecode, s);
-  WV_TRY(run_proj(m, q, s));
+  WV_TRY(run_proj(m, q, s, &kv_done));
   prof_end(kProfGemmQkvDecode, s);
-  const char* base = static_cast<const char*>(m->qkv.p);
-  WV_CUDA(kv_append(base + (size_t)m->qd_l * es, base + (size_t)(m->qd_l + m->kd_l) * es, m->nqkv, batch,
-                    m->kd_l, c.hd, f32 ? 0 : 1, m->slots.as<int>(), kv->k_pool.p, kv->v_pool.p, s), "kv append");
-  count_launch();
+  if (!kv_done) {
+    const char* base = static_cast<const char*>(m->qkv.p);
+    WV_CUDA(kv_append(base + (size_t)m->qd_l * es, base + (size_t)(m->qd_l + m->kd_l) * es, m->nqkv, batch,
+                      m->kd_l, c.hd, f32 ? 0 : 1, m->slots.as<int>(), kv->k_pool.p, kv->v_pool.p, s),
+            "kv append");
+    count_launch();
+  }
 
   void* attn = pre;
   if (!attn || !on_device) {
@@ -1118,8 +1165,12 @@ Status mha_decode(Mha* m, Kv* kv, int batch, const void* x, void* pre, void* pos
   WV_TRY(run_proj(m, o, s));
   prof_end(kProfGemmODecode, s);
   if (m->comm) {
+    // The decode output (batch x d_model) is small: one peer-memory kernel over
+    // NVLink instead of NCCL when the layer can take it.
+    const size_t count = (size_t)batch * dm;
     prof_begin(kProfAllReduce, s);
-    WV_TRY(comm_allreduce(m, postd, (size_t)batch * dm, !f32, s));
+    if (comm_peer_ok(m, count * es)) WV_TRY(comm_peer_allreduce(m, postd, count, !f32, s));
+    else WV_TRY(comm_allreduce(m, postd, count, !f32, s));
     prof_end(kProfAllReduce, s);
   }
   for (int b = 0; b < batch; ++b) kv->ctx_host[b] += 1;

@@ -172,6 +172,13 @@ struct Mha {
   // (every rank holds every summed row), 1 reduce-scatter (see welvet_b200.h).
   int out_mode = 0;
   cudaStream_t comm_stream = nullptr;
+  // NVLink peer workspace of the peer-memory all-reduce (decode outputs): this
+  // rank's receive area and every rank's area opened through CUDA IPC (index =
+  // rank). Created collectively by the first call that needs it (comm.cpp).
+  void* peer_area = nullptr;
+  void* peer_areas[8] = {};
+  size_t peer_slot_bytes = 0, peer_flags_off = 0;
+  uint32_t peer_epoch = 0;
   static constexpr int kMaxChunks = 16;
   cudaEvent_t chunk_done[kMaxChunks] = {};
   cudaEvent_t comm_done = nullptr;
@@ -214,6 +221,13 @@ Status comm_allreduce(Mha* m, void* buf, size_t count, bool bf16, cudaStream_t s
 // in place over buf [nranks * count]; rank r's part at r * count elements
 Status comm_allgather(Mha* m, void* buf, size_t count, bool bf16, cudaStream_t s);
 Status comm_reducescatter(Mha* m, void* buf, size_t count, bool bf16, cudaStream_t s);
+// All-reduce of a small vector through the NVLink peer workspace (one kernel, no
+// NCCL): true when this layer can take it (2-8 ranks, at most kPeerMaxBytes, 16-byte
+// multiple, not switched off by WELVET_B200_PEER_ALLREDUCE=0). Collective: every
+// rank makes the same calls; the first one (and any larger one) sets the workspace up.
+constexpr size_t kPeerMaxBytes = 4u << 20;
+bool comm_peer_ok(const Mha* m, size_t bytes);
+Status comm_peer_allreduce(Mha* m, void* buf, size_t count, bool bf16, cudaStream_t s);
 // Asynchronous NCCL error check; on an error the communicator is aborted and
 // dropped, code 4.
 Status comm_poll(Mha* m);
