@@ -2,27 +2,27 @@
 // token per sequence), the Dense forward of the reference's decode path
 // (shaders/welvet_dense.metal:54-85 per output, src/layers/mha/mha.cpp:138-205 for
 // the q/k/v and output projections), written for what bounds it on the B200: the
-// weight matrix is streamed from HBM once, so the kernel is a GEMV at HBM rate with
-// the M rows riding along on m16n8k16 tensor-core MMAs.
+// weight matrix is read from HBM once, and at these sizes (a few to a hundred MB)
+// the time is one memory round trip plus the transfer, so every load is issued up
+// front and the M rows ride along on m16n8k16 tensor-core MMAs.
 //
-// Work split: a CTA (8 warps) owns 128 output columns, warp w the 16 columns
-// [16w, 16w + 16) as two n8 tiles, over a K slice; a thread-block cluster of ks
-// CTAs along K covers the whole K range, one CTA per SM. The slice streams through a
-// four-stage cp.async ring of 128-wide k steps (three steps, 96 KB of W, in flight
-// per SM): per 32-wide k chunk a thread fetches 16 bytes of each of its two W rows
-// (n = lane / 4, k = 8 (lane % 4) .. + 8: four threads read 64 contiguous bytes of a
-// row) into its own slots, and the step's x rows go to a shared part of the stage.
-// A chunk is consumed by two k16 MMAs under a fixed permutation of k inside the
-// chunk (logical k pairs {2c, 2c+1} / {2c+8, 2c+9} of MMA m are physical
-// 8c + 4m + {0,1} / {2,3}); x and W use the same permutation, so the dot products
-// are unchanged.
+// Work split: a CTA (16 warps) owns 128 output columns over a 512-wide K slice;
+// warp w owns the n8 tile of columns [8w, 8w + 8); a thread-block cluster of
+// ks = K / 512 CTAs (at most 8) along K covers the whole K range. A thread issues
+// its sixteen 16-byte W loads at once (row n = lane / 4, k = 32 q + 8 (lane % 4):
+// four threads read 64 contiguous bytes of a row), while the CTA stages the x rows
+// of its slice in shared memory. Each 32-wide k chunk is consumed by two k16 MMAs
+// under a fixed permutation of k inside the chunk (logical k pairs {2c, 2c+1} /
+// {2c+8, 2c+9} of MMA m are physical 8c + 4m + {0,1} / {2,3}); x and W use the
+// same permutation, so the dot products are unchanged.
 //
 // Epilogue: each CTA writes its FP32 partial tile to shared memory; after a
 // cluster barrier CTA r sums the partials of rows [r R, (r+1) R) from every CTA of
-// the cluster in cluster-rank order (distributed shared memory; deterministic) and
-// applies RoPE (rotate-half pairs inside a head: a head lies inside one 128-column
-// tile for head_dim 32/64/128), then stores bf16 rows, with the K and V column
-// ranges scattered into the KV page pools (the cache append) when kv_k is given.
+// the cluster in cluster-rank order (distributed shared memory, four columns per
+// load; deterministic) and applies RoPE (rotate-half pairs inside a head: a head
+// lies inside one 128-column tile for head_dim 32/64/128), then stores bf16 rows,
+// with the K and V column ranges scattered into the KV page pools (the cache
+// append) when kv_k is given.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -31,10 +31,12 @@
 namespace wv {
 namespace {
 
-constexpr int kThreads = 256;
-constexpr int kNC = 128;   // output columns per CTA
-constexpr int kKU = 128;   // k per unrolled iteration (four 32-wide chunks)
+constexpr int kThreads = 512;
+constexpr int kNC = 128;         // output columns per CTA
+constexpr int kSlice = 512;      // K per CTA
+constexpr int kChunks = kSlice / 32;
 constexpr int kRedLd = kNC + 4;  // padded row of the partial tile (floats)
+constexpr int kXRow = kSlice * 2 + 16;  // bytes of a staged x row (pad: conflict-free fragment reads)
 constexpr int kMaxCluster = 8;
 
 struct VParams {
@@ -76,20 +78,12 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint3
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
-// (ordered by the cluster barriers around the reads; no clobber, so the loads of
-// one sum are in flight together)
-__device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr));
+// Four floats of another CTA's shared memory (ordered by the cluster barriers
+// around the reads; no clobber, so the loads of one sum are in flight together).
+__device__ __forceinline__ float4 ld_dsmem_v4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
   return v;
-}
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool pred) {
-  const uint32_t n = pred ? 16u : 0u;  // 0 source bytes: the 16 bytes are zero-filled
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem)), "l"(gmem), "r"(n) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N> __device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 __device__ __forceinline__ uint32_t dsmem_addr(const void* local, uint32_t rank) {
   uint32_t r;
@@ -97,174 +91,158 @@ __device__ __forceinline__ uint32_t dsmem_addr(const void* local, uint32_t rank)
   return r;
 }
 
-// Stage s of the ring: each thread's eight 16-byte W fragments (four k chunks x two
-// rows) at [q][j][thread] (a warp's reads hit consecutive 16-byte words), then the
-// x rows of the step, [16 MT][128 k] with a 16-byte pad per row.
-constexpr int kStages = 4;
-constexpr int kWStage = 8 * kThreads * 16;  // 32 KB
-constexpr int kXRow = kKU * 2 + 16;         // bytes of a staged x row
-template <int MT> __host__ __device__ constexpr int stage_bytes() { return kWStage + MT * 16 * kXRow; }
-
 template <int MT>
 __global__ void __launch_bounds__(kThreads, 1) gemv_decode_kernel(const VParams p) {
   extern __shared__ __align__(16) float vsm[];
-  uint8_t* ring = reinterpret_cast<uint8_t*>(vsm);
+  uint8_t* xs = reinterpret_cast<uint8_t*>(vsm);  // [16 MT][kXRow] x rows of the slice
   const int ks = p.ks;
   const int rank = ks > 1 ? (int)cluster_rank() : 0;
   const int tile = blockIdx.x / ks;
   const int n0 = tile * kNC;
-  const int kslice = p.K / ks, kbeg = rank * kslice;
-  const int steps = kslice / kKU;
+  const int kbeg = rank * kSlice;
   const int warp = (int)warp_id(), lane = (int)lane_id(), tid = (int)threadIdx.x;
   const int g = lane >> 2, c = lane & 3;
+  const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
 
-  // This thread's two W rows (one per n8 tile) from column kbeg + 8c.
-  const __nv_bfloat16* wr[2];
-  bool wok[2];
+  // Every W load of this thread, issued before anything waits.
+  const int n = n0 + 8 * warp + g;
+  const bool wok = n < p.N;
+  const __nv_bfloat16* wr = p.w + (size_t)(wok ? n : 0) * p.K + kbeg + 8 * c;
+  uint4 wv[kChunks];
 #pragma unroll
-  for (int j = 0; j < 2; ++j) {
-    const int n = n0 + 16 * warp + 8 * j + g;
-    wok[j] = n < p.N;
-    wr[j] = p.w + (size_t)(wok[j] ? n : 0) * p.K + kbeg + 8 * c;
-  }
-  // Step i into its stage: this thread's W fragments and its share of the x rows.
-  auto issue = [&](int i) {
-    uint8_t* st = ring + (i % kStages) * stage_bytes<MT>();
-    const int k0 = i * kKU;
+  for (int q = 0; q < kChunks; ++q) wv[q] = wok ? ldg_stream_v4(wr + 32 * q) : zero;
+  // The x rows of the slice into shared memory (rows past M as zeros).
+  {
+    constexpr int kUnits = MT * 16 * (kSlice / 8);  // 16-byte units
+    uint4 xv[kUnits / kThreads];
 #pragma unroll
-    for (int q = 0; q < 4; ++q)
-#pragma unroll
-      for (int j = 0; j < 2; ++j) cp_async16(st + ((q * 2 + j) * kThreads + tid) * 16, wr[j] + k0 + 32 * q, wok[j]);
-    uint8_t* xs = st + kWStage;
-#pragma unroll
-    for (int u = tid; u < MT * 16 * 16; u += kThreads) {  // 16 units of 16 bytes per row
-      const int row = u >> 4, cu = u & 15;
-      const bool ok = row < p.M;
-      cp_async16(xs + row * kXRow + 16 * cu, p.x + (size_t)(ok ? row : 0) * p.ldx + kbeg + k0 + 8 * cu, ok);
+    for (int i = 0; i < kUnits / kThreads; ++i) {
+      const int u = tid + i * kThreads, row = u / (kSlice / 8), cu = u % (kSlice / 8);
+      xv[i] = row < p.M ? ldg_nc_v4(p.x + (size_t)row * p.ldx + kbeg + 8 * cu) : zero;
     }
-  };
 #pragma unroll
-  for (int i = 0; i < kStages - 1; ++i) {
-    if (i < steps) issue(i);
-    cp_async_commit();
+    for (int i = 0; i < kUnits / kThreads; ++i) {
+      const int u = tid + i * kThreads, row = u / (kSlice / 8), cu = u % (kSlice / 8);
+      *reinterpret_cast<uint4*>(xs + row * kXRow + 16 * cu) = xv[i];
+    }
   }
-  float acc[MT][2][4];
+  __syncthreads();
+  float acc[MT][4];
 #pragma unroll
   for (int i = 0; i < MT; ++i)
 #pragma unroll
-    for (int j = 0; j < 2; ++j)
+    for (int e = 0; e < 4; ++e) acc[i][e] = 0.f;
+  const uint8_t* xth = xs + g * kXRow + 16 * c;
 #pragma unroll
-      for (int e = 0; e < 4; ++e) acc[i][j][e] = 0.f;
-
-  for (int i = 0; i < steps; ++i) {
-    cp_async_wait<kStages - 2>();  // this thread's copies of step i are complete
-    __syncthreads();               // ... and every thread's (x rows); step i - 1 is consumed
-    if (i + kStages - 1 < steps) issue(i + kStages - 1);
-    cp_async_commit();
-    const uint8_t* st = ring + (i % kStages) * stage_bytes<MT>();
-    const uint8_t* xth = st + kWStage + g * kXRow + 16 * c;
+  for (int q = 0; q < kChunks; ++q) {
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      uint4 wv[2];
-#pragma unroll
-      for (int j = 0; j < 2; ++j) wv[j] = *reinterpret_cast<const uint4*>(st + ((q * 2 + j) * kThreads + tid) * 16);
-#pragma unroll
-      for (int mi = 0; mi < MT; ++mi) {
-        const uint8_t* xa_p = xth + (16 * mi) * kXRow + 64 * q;
-        const uint4 xa = *reinterpret_cast<const uint4*>(xa_p);
-        const uint4 xb = *reinterpret_cast<const uint4*>(xa_p + 8 * kXRow);
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          mma_bf16_16816(acc[mi][j], xa.x, xb.x, xa.y, xb.y, wv[j].x, wv[j].y);
-          mma_bf16_16816(acc[mi][j], xa.z, xb.z, xa.w, xb.w, wv[j].z, wv[j].w);
-        }
-      }
+    for (int mi = 0; mi < MT; ++mi) {
+      const uint8_t* xa_p = xth + (16 * mi) * kXRow + 64 * q;
+      const uint4 xa = *reinterpret_cast<const uint4*>(xa_p);
+      const uint4 xb = *reinterpret_cast<const uint4*>(xa_p + 8 * kXRow);
+      mma_bf16_16816(acc[mi], xa.x, xb.x, xa.y, xb.y, wv[q].x, wv[q].y);
+      mma_bf16_16816(acc[mi], xa.z, xb.z, xa.w, xb.w, wv[q].z, wv[q].w);
     }
   }
-  cp_async_wait<0>();
   __syncthreads();  // the x area becomes the partial tiles
-  float* red = vsm;                        // [MT*16][kRedLd] this CTA's partial tile
-  float* fin = vsm + MT * 16 * kRedLd;     // [MT*16][kRedLd] the summed rows of this CTA's slice
-  // Partial tile: rows 16 i + g (+8), columns 16 warp + 8 j + 2 c (+1).
+  float* red = vsm;                     // [MT*16][kRedLd] this CTA's partial tile
+  float* fin = vsm + MT * 16 * kRedLd;  // [MT*16][kRedLd] the summed rows of this CTA's slice
+  // Partial tile: rows 16 mi + g (+8), columns 8 warp + 2 c (+1).
 #pragma unroll
-  for (int i = 0; i < MT; ++i) {
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const int col = 16 * warp + 8 * j + 2 * c;
-      float* r0 = red + (16 * i + g) * kRedLd + col;
-      float* r1 = r0 + 8 * kRedLd;
-      r0[0] = acc[i][j][0];
-      r0[1] = acc[i][j][1];
-      r1[0] = acc[i][j][2];
-      r1[1] = acc[i][j][3];
-    }
+  for (int mi = 0; mi < MT; ++mi) {
+    float* r0 = red + (16 * mi + g) * kRedLd + 8 * warp + 2 * c;
+    *reinterpret_cast<float2*>(r0) = make_float2(acc[mi][0], acc[mi][1]);
+    *reinterpret_cast<float2*>(r0 + 8 * kRedLd) = make_float2(acc[mi][2], acc[mi][3]);
   }
-  // Rows of this CTA's slice, summed over the cluster in rank order.
+  // Rows of this CTA's slice, summed over the cluster in rank order. A thread
+  // handles columns [4 (tid % 32), + 4) of rows tid / 32 + 16 it.
   const int rows = MT * 16;
   const int rpr = (rows + ks - 1) / ks;
   const int r0 = rank * rpr, r1 = min(rows, r0 + rpr);
+  const int col = 4 * (tid % 32), rsub = tid / 32;
   if (ks > 1) {
     cluster_sync();  // every CTA's partial tile is written and visible
-    for (int e = threadIdx.x; e < (r1 - r0) * kNC; e += kThreads) {
-      const int row = r0 + e / kNC, col = e % kNC;
-      const float* loc = red + row * kRedLd + col;
-      float v[kMaxCluster];
+    uint32_t base[kMaxCluster];
 #pragma unroll
-      for (int q = 0; q < kMaxCluster; ++q) v[q] = q < ks ? ld_dsmem_f32(dsmem_addr(loc, (uint32_t)q)) : 0.f;
-      float s = 0.f;
+    for (int q = 0; q < kMaxCluster; ++q) base[q] = q < ks ? dsmem_addr(red, (uint32_t)q) : 0u;
 #pragma unroll
-      for (int q = 0; q < kMaxCluster; ++q) s += v[q];  // rank order (absent ranks add 0)
-      fin[row * kRedLd + col] = s;
+    for (int it = 0; it < MT; ++it) {
+      const int row = rsub + 16 * it;
+      if (row < r0 || row >= r1) continue;
+      const uint32_t off = (uint32_t)((row * kRedLd + col) * 4);
+      float4 v[kMaxCluster];
+#pragma unroll
+      for (int q = 0; q < kMaxCluster; ++q) v[q] = q < ks ? ld_dsmem_v4(base[q] + off) : make_float4(0.f, 0.f, 0.f, 0.f);
+      float4 sm = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int q = 0; q < kMaxCluster; ++q) {  // rank order (absent ranks add 0)
+        sm.x += v[q].x;
+        sm.y += v[q].y;
+        sm.z += v[q].z;
+        sm.w += v[q].w;
+      }
+      *reinterpret_cast<float4*>(fin + row * kRedLd + col) = sm;
     }
     cluster_sync();  // the other CTAs are done reading this CTA's partial tile
   } else {
     __syncthreads();
-    for (int e = threadIdx.x; e < rows * kNC; e += kThreads) {
-      const int row = e / kNC, col = e % kNC;
-      fin[row * kRedLd + col] = red[row * kRedLd + col];
+#pragma unroll
+    for (int it = 0; it < MT; ++it) {
+      const int row = rsub + 16 * it;
+      *reinterpret_cast<float4*>(fin + row * kRedLd + col) = *reinterpret_cast<const float4*>(red + row * kRedLd + col);
     }
     __syncthreads();
   }
-  // RoPE, then bf16 stores (q columns) or the KV page scatter (k, v columns).
+  // RoPE, then bf16 stores (q columns) or the KV page scatter (k, v columns); four
+  // columns per thread stay inside one head (head_dim is a multiple of 4).
   const int hd = p.head_dim, half = hd >> 1;
-  for (int e = threadIdx.x; e < (r1 - r0) * kNC; e += kThreads) {
-    const int row = r0 + e / kNC, col = e % kNC, gc = n0 + col;
-    if (row >= p.M || gc >= p.N) continue;
-    float v = fin[row * kRedLd + col];
-    if (gc < p.rope_cols) {
-      const int in_head = gc % hd;
+  const int gc = n0 + col;
+  if (gc >= p.N) return;
+  const bool roped = gc < p.rope_cols;
+  const int in_head = gc % hd;
+  const bool to_kv = p.kv_k && gc >= p.kv_col0;
+  int rel = gc - p.kv_col0;
+  const bool is_v = to_kv && rel >= p.kv_dim;
+  if (is_v) rel -= p.kv_dim;
+  const int nk = p.kv_dim > 0 ? p.kv_dim / hd : 1;
+  __nv_bfloat16* kv_base = is_v ? p.kv_v : p.kv_k;
+  const int pcol = in_head < half ? col + half : col - half;  // rotate-half partner
+#pragma unroll
+  for (int it = 0; it < MT; ++it) {
+    const int row = rsub + 16 * it;
+    if (row < r0 || row >= r1 || row >= p.M) continue;
+    float4 v = *reinterpret_cast<const float4*>(fin + row * kRedLd + col);
+    if (roped) {
       const int pos = p.positions ? p.positions[row] : (p.pos_mod > 0 ? row % p.pos_mod : row);
       const bool pos_ok = pos >= 0 && pos < p.rope_max_pos;
       if (!pos_ok) atomicCAS(p.err, 0u, 0x100u);
-      const float2 cs = pos_ok ? p.rope_tab[(size_t)pos * half + (in_head % half)] : make_float2(1.f, 0.f);
-      if (in_head < half) {
-        const float b = fin[row * kRedLd + col + half];
-        v = v * cs.x - b * cs.y;
-      } else {
-        const float a = fin[row * kRedLd + col - half];
-        v = a * cs.y + v * cs.x;
+      const float4 o = *reinterpret_cast<const float4*>(fin + row * kRedLd + pcol);
+      float vv[4] = {v.x, v.y, v.z, v.w};
+      const float ov[4] = {o.x, o.y, o.z, o.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 cs = pos_ok ? p.rope_tab[(size_t)pos * half + ((in_head + e) % half)] : make_float2(1.f, 0.f);
+        vv[e] = in_head < half ? vv[e] * cs.x - ov[e] * cs.y : ov[e] * cs.y + vv[e] * cs.x;
       }
+      v = make_float4(vv[0], vv[1], vv[2], vv[3]);
     }
-    if (p.kv_k && gc >= p.kv_col0) {
-      int rel = gc - p.kv_col0;
-      const bool is_v = rel >= p.kv_dim;
-      if (is_v) rel -= p.kv_dim;
+    const uint2 pk = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+    if (to_kv) {
       const int slot = p.kv_slot[row];
       if (slot < 0) continue;
       // pool layout [page][kv_head][kPageTokens][head_dim]
-      const int nk = p.kv_dim / hd;
       const size_t off =
           (((size_t)(slot / kPageTokens) * nk + rel / hd) * kPageTokens + slot % kPageTokens) * hd + rel % hd;
-      (is_v ? p.kv_v : p.kv_k)[off] = __float2bfloat16_rn(v);
+      *reinterpret_cast<uint2*>(kv_base + off) = pk;
     } else {
-      p.out[(size_t)row * p.ldo + gc] = __float2bfloat16_rn(v);
+      *reinterpret_cast<uint2*>(p.out + (size_t)row * p.ldo + gc) = pk;
     }
   }
 }
 
-// Shared memory: the ring, later the partial and summed tiles.
+// Shared memory: the staged x rows, later the partial and summed tiles.
 template <int MT> constexpr int smem_bytes() {
-  return std::max(kStages * stage_bytes<MT>(), 2 * MT * 16 * kRedLd * (int)sizeof(float));
+  return std::max(MT * 16 * kXRow, 2 * MT * 16 * kRedLd * (int)sizeof(float));
 }
 
 template <int MT>
@@ -288,30 +266,23 @@ cudaError_t launch(const VParams& p, int tiles, cudaStream_t s) {
   return cudaLaunchKernelEx(&lc, kern, p);
 }
 
-// Cluster size along K: the largest that keeps the grid within one CTA per SM
-// (one wave), the K slice a whole number of 128-wide steps.
-int cluster_size(int tiles, int K, int sm_count) {
-  int best = 1;
-  for (int ks = 2; ks <= kMaxCluster; ks *= 2) {
-    if (K % (kKU * ks) || tiles * ks > sm_count) break;
-    best = ks;
-  }
-  return best;
-}
-
 }  // namespace
 
 bool gemv_decode_supported(const GemmArgs& a) {
   if (a.kind != kGemmBF16 || !a.out_bf16 || a.a_lo || a.b_lo || a.out_hi || a.swiglu) return false;
-  if (a.M < 1 || a.M > 64 || a.N < 1 || a.K < kKU || a.K % kKU) return false;
-  if (a.ldb != a.K || a.lda < a.K || a.lda % 8) return false;
+  // K in whole 512-wide slices, at most kMaxCluster of them (one cluster along K)
+  if (a.M < 1 || a.M > 64 || a.N < 4 || a.N % 4 || a.K < kSlice || a.K % kSlice || a.K / kSlice > kMaxCluster)
+    return false;
+  if (a.ldb != a.K || a.lda < a.K || a.lda % 8 || a.ldo % 4) return false;
   auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
-  if (!al16(a.a) || !al16(a.b)) return false;
+  if (!al16(a.a) || !al16(a.b) || (reinterpret_cast<uintptr_t>(a.out) & 7)) return false;
   if (a.rope_cols > 0) {
     // a head lies inside one 128-column tile
     if (!a.rope_tab || !(a.head_dim == 32 || a.head_dim == 64 || a.head_dim == 128)) return false;
   }
-  if (a.kv_k && (!a.kv_v || !a.kv_slot || a.head_dim <= 0 || a.kv_dim % a.head_dim)) return false;
+  if (a.kv_k && (!a.kv_v || !a.kv_slot || a.head_dim <= 0 || a.head_dim % 4 || a.kv_dim % a.head_dim ||
+                 (reinterpret_cast<uintptr_t>(a.kv_k) & 7) || (reinterpret_cast<uintptr_t>(a.kv_v) & 7)))
+    return false;
   return true;
 }
 
@@ -338,8 +309,8 @@ cudaError_t gemv_decode(const GemmArgs& a, cudaStream_t s) {
   p.kv_col0 = a.kv_col0;
   p.kv_dim = a.kv_dim;
   p.err = a.err;
+  p.ks = a.K / kSlice;
   const int tiles = (a.N + kNC - 1) / kNC;
-  p.ks = cluster_size(tiles, a.K, a.sm_count);
   switch ((a.M + 15) / 16) {
     case 1: return launch<1>(p, tiles, s);
     case 2: return launch<2>(p, tiles, s);
