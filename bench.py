@@ -175,18 +175,50 @@ def peaks():
 
 
 class Clocks:
-    """nvidia-smi sampling during the timed region (SM clock, throttle reasons)."""
+    """SM clock and throttle reasons sampled during the timed region: through NVML
+    (pynvml) every 10 ms in a thread, so that a timed region of a few hundred ms
+    (8 GPUs) still gets its own record; nvidia-smi (200 ms) when NVML is missing."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
+    # NVML clocks-event reason bits (nvml.h): sw power cap, hw slowdown, sw thermal,
+    # hw thermal
+    BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40}
 
     def __init__(self, index: int):
         self.index = index
         self.proc = None
         self.lines = []
         self.thread = None
+        self.nvml = None
+        self.samples = []  # (sm_mhz, reason bits)
+        self.max_mhz = None
+        self.stop_evt = threading.Event()
 
     def start(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+            self.nvml = pynvml
+
+            def loop():
+                while not self.stop_evt.is_set():
+                    try:
+                        self.samples.append((float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)),
+                                             int(reasons(h))))
+                    except pynvml.NVMLError:
+                        pass
+                    self.stop_evt.wait(0.01)
+
+            self.thread = threading.Thread(target=loop, daemon=True)
+            self.thread.start()
+            return
+        except Exception:
+            self.nvml = None
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
                                           "--format=csv,noheader,nounits", "-lms", "200"],
@@ -201,6 +233,13 @@ class Clocks:
             self.lines.append(line.strip())
 
     def stop(self):
+        if self.nvml is not None:
+            self.stop_evt.set()
+            self.thread.join(timeout=5)
+            sm = [c for c, _ in self.samples]
+            reasons = sorted({n for _, bits in self.samples for n, b in self.BITS.items() if bits & b})
+            return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz,
+                    "samples": len(sm), "reasons": reasons, "source": "nvml 10 ms"}
         if not self.proc:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
@@ -223,7 +262,7 @@ class Clocks:
                 if v.lower().startswith("active"):
                     reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "samples": len(sm),
-                "reasons": sorted(reasons)}
+                "reasons": sorted(reasons), "source": "nvidia-smi 200 ms"}
 
 
 def flops_prefill(B, T, d, H, NK, hd):
@@ -1326,6 +1365,24 @@ def run_dequant(args, rank, world, local):
             "kernels": res, "parity": parity, "wall_s": time.perf_counter() - wall0}
 
 
+def bind_local_cpus(index: int):
+    """Pins this rank's process to the CPUs NVML names as local to its GPU, so that its
+    pinned host buffers (first touched here) sit on the GPU's own NUMA node: with 8
+    ranks the host-buffer end-to-end copies are otherwise limited by cross-socket
+    memory traffic. Nothing changes when NVML or the affinity call is unavailable."""
+    try:
+        import pynvml
+        pynvml.nvmlInit()
+        h = pynvml.nvmlDeviceGetHandleByIndex(index)
+        words = pynvml.nvmlDeviceGetCpuAffinity(h, (os.cpu_count() + 63) // 64)
+        cpus = {64 * i + b for i, w in enumerate(words) for b in range(64) if (w >> b) & 1}
+        cpus &= set(range(os.cpu_count()))
+        if cpus:
+            os.sched_setaffinity(0, cpus)
+    except Exception:
+        pass
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1357,6 +1414,8 @@ def main():
     import torch
     import torch.distributed as dist
 
+    if world > 1:
+        bind_local_cpus(local)
     torch.cuda.set_device(local)
     if workload(args)["kind"] == "codec":
         return run_codec(args, rank, world, local)

@@ -9,7 +9,7 @@ import pytest
 
 import oracle_py as O
 import welvet_b200 as W
-from conftest import golden_cases, load_golden, rel_err
+from conftest import bf16_round, golden_cases, load_golden, rel_err
 
 pytestmark = pytest.mark.gpu
 
@@ -357,4 +357,40 @@ def test_decode_split_k_weight_formats(torch_cuda, weight_format, dtype):
                                      *_oracle_weights(Ws, dtype, weight_format), x.float().cpu().numpy())
     assert rel_err(pre.float().cpu().numpy(), rpre) < LOW_TOL
     assert rel_err(post.float().cpu().numpy(), rpost) < LOW_TOL
+    layer.close()
+
+
+@pytest.mark.parametrize("d,H,NK,B", [(2048, 16, 4, 20), (1536, 12, 12, 33), (512, 8, 2, 64)])
+def test_decode_gemv_shapes(torch_cuda, d, H, NK, B):
+    """BF16 decode projections through the weight-streaming GEMV (K a multiple of
+    512): head_dim 128 and 64 RoPE pairs inside the 128-column tiles, batch rows
+    padded to the MMA's N (32, 48, 64), K split over clusters of 4, 3... 1 CTAs, the
+    K/V rows appended to the cache pages in the epilogue; against the oracle's
+    decode, two steps (the second reads the first step's appended rows)."""
+    torch = torch_cuda
+    L = 40
+    cfg = W.MhaConfig.make(d, H, NK, precision=1)
+    hd, nk = cfg.resolved()
+    Ws = W.xavier_weights(d, H * hd, nk * hd, seed=5)
+    layer = W.MhaLayer(cfg, *Ws, dtype=1)
+    kv = W.KvCache(layer, B, 64)
+    n = B * L * nk * hd
+    kc = torch.from_numpy(W.synthetic(n, 2, 1, 0.5).reshape(B, L, nk * hd)).cuda().to(torch.bfloat16)
+    vc = torch.from_numpy(W.synthetic(n, 2, 1, 0.5, offset=n).reshape(B, L, nk * hd)).cuda().to(torch.bfloat16)
+    kv.fill(B, L, kc, vc)
+    oc = O.MhaCfg(d_model=d, num_heads=H, num_kv_heads=NK, per_sequence=1)
+    kcn, vcn = kc.float().cpu().numpy(), vc.float().cpu().numpy()
+    Wb = _oracle_weights(Ws, 1, 0)
+    for step in range(2):
+        x = torch.from_numpy(W.synthetic(B * d, 40 + step, 1, 1.0).reshape(B, d)).cuda().to(torch.bfloat16)
+        post = torch.zeros(B, d, device="cuda", dtype=torch.bfloat16)
+        pre = torch.zeros(B, H * hd, device="cuda", dtype=torch.bfloat16)
+        layer.decode(kv, B, x, pre, post)
+        torch.cuda.synchronize()
+        layer.check_device()
+        rpre, rpost, kn, vn = O.mha_decode(oc, [L + step] * B, kcn, vcn, *Wb, x.float().cpu().numpy())
+        assert rel_err(pre.float().cpu().numpy(), rpre) < LOW_TOL, step
+        assert rel_err(post.float().cpu().numpy(), rpost) < LOW_TOL, step
+        kcn = np.concatenate([kcn, bf16_round(kn)[:, None, :]], axis=1)
+        vcn = np.concatenate([vcn, bf16_round(vn)[:, None, :]], axis=1)
     layer.close()

@@ -6,15 +6,16 @@
 // the time is one memory round trip plus the transfer, so every load is issued up
 // front and the M rows ride along on m16n8k16 tensor-core MMAs.
 //
-// Work split: a CTA (16 warps) owns 128 output columns over a 512-wide K slice;
-// warp w owns the n8 tile of columns [8w, 8w + 8); a thread-block cluster of
-// ks = K / 512 CTAs (at most 8) along K covers the whole K range. A thread issues
-// its sixteen 16-byte W loads at once (row n = lane / 4, k = 32 q + 8 (lane % 4):
-// four threads read 64 contiguous bytes of a row), while the CTA stages the x rows
-// of its slice in shared memory. Each 32-wide k chunk is consumed by two k16 MMAs
-// under a fixed permutation of k inside the chunk (logical k pairs {2c, 2c+1} /
-// {2c+8, 2c+9} of MMA m are physical 8c + 4m + {0,1} / {2,3}); x and W use the
-// same permutation, so the dot products are unchanged.
+// Work split (weights as the A operand, "swap AB"): a CTA owns 128 output columns
+// (128 weight rows = the M = 128 rows of a tcgen05 MMA) over a 512-wide K slice,
+// the batch rows are the MMA's N (a multiple of 16, zero-filled past M by TMA); a
+// thread-block cluster of ks = K / 512 CTAs (at most 8) along K covers the whole K
+// range. A TMA thread streams the slice's eight 64-wide k blocks of W (16 KB) and x
+// through a four-stage ring, one thread issues 4 UMMAs (K = 16) per block into a
+// TMEM accumulator [128 lanes = output columns][N columns = batch rows], and four
+// warps read it back. Each weight byte crosses shared memory once (an mma.sync
+// form re-read the x fragments once per 8 output columns: ~1 MB of shared-memory
+// traffic per CTA, 10 us of a 15 us kernel).
 //
 // Epilogue: each CTA writes its FP32 partial tile to shared memory; after a
 // cluster barrier CTA r sums the partials of rows [r R, (r+1) R) from every CTA of
@@ -31,19 +32,23 @@
 namespace wv {
 namespace {
 
-constexpr int kThreads = 512;
-constexpr int kNC = 128;         // output columns per CTA
+constexpr int kThreads = 192;    // warp 0 TMA, warp 1 MMA + TMEM, warps 2-5 epilogue
+constexpr int kNC = 128;         // output columns per CTA (the MMA's M)
 constexpr int kSlice = 512;      // K per CTA
-constexpr int kChunks = kSlice / 32;
+constexpr int kBK = 64;          // k per block (one 128-byte swizzled row)
+constexpr int kBlocks = kSlice / kBK;
+constexpr int kStages = 4;
+constexpr int kNBMax = 64;       // batch rows (MMA N) at most
+constexpr int kWBytes = kNC * kBK * 2;      // 16 KB
+constexpr int kXBytes = kNBMax * kBK * 2;   // 8 KB
+constexpr int kStageBytes = kWBytes + kXBytes;
 constexpr int kRedLd = kNC + 4;  // padded row of the partial tile (floats)
-constexpr int kXRow = kSlice * 2 + 16;  // bytes of a staged x row (pad: conflict-free fragment reads)
 constexpr int kMaxCluster = 8;
+constexpr int kSmem = 1024 + kStages * kStageBytes + 256;
+static_assert(2 * kNBMax * kRedLd * 4 <= kStages * kStageBytes, "partial tiles fit in the ring");
 
 struct VParams {
-  const __nv_bfloat16* x;
-  int ldx;
-  const __nv_bfloat16* w;
-  int M, N, K, ks;
+  int M, N, K, ks, nb;  // nb: batch rows rounded up to 16 (the MMA's N)
   __nv_bfloat16* out;
   int ldo;
   const float2* rope_tab;
@@ -57,27 +62,6 @@ struct VParams {
   uint32_t* err;
 };
 
-__device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
-  uint4 r;
-  asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
-  return r;
-}
-// Weights are read once: no L1 allocation.
-__device__ __forceinline__ uint4 ldg_stream_v4(const void* p) {
-  uint4 r;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-               : "l"(p));
-  return r;
-}
-__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                               uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-      "{%0, %1, %2, %3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
 // Four floats of another CTA's shared memory (ordered by the cluster barriers
 // around the reads; no clobber, so the loads of one sum are in flight together).
 __device__ __forceinline__ float4 ld_dsmem_v4(uint32_t addr) {
@@ -91,108 +75,136 @@ __device__ __forceinline__ uint32_t dsmem_addr(const void* local, uint32_t rank)
   return r;
 }
 
-template <int MT>
-__global__ void __launch_bounds__(kThreads, 1) gemv_decode_kernel(const VParams p) {
-  extern __shared__ __align__(16) float vsm[];
-  uint8_t* xs = reinterpret_cast<uint8_t*>(vsm);  // [16 MT][kXRow] x rows of the slice
+__global__ void __launch_bounds__(kThreads, 1)
+    gemv_decode_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+                       const VParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  uint64_t* empty = full + kStages;
+  uint64_t* acc_full = empty + kStages;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(acc_full + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   const int ks = p.ks;
   const int rank = ks > 1 ? (int)cluster_rank() : 0;
   const int tile = blockIdx.x / ks;
   const int n0 = tile * kNC;
   const int kbeg = rank * kSlice;
   const int warp = (int)warp_id(), lane = (int)lane_id(), tid = (int)threadIdx.x;
-  const int g = lane >> 2, c = lane & 3;
-  const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
 
-  // Every W load of this thread, issued before anything waits.
-  const int n = n0 + 8 * warp + g;
-  const bool wok = n < p.N;
-  const __nv_bfloat16* wr = p.w + (size_t)(wok ? n : 0) * p.K + kbeg + 8 * c;
-  uint4 wv[kChunks];
-#pragma unroll
-  for (int q = 0; q < kChunks; ++q) wv[q] = wok ? ldg_stream_v4(wr + 32 * q) : zero;
-  // The x rows of the slice into shared memory (rows past M as zeros).
-  {
-    constexpr int kUnits = MT * 16 * (kSlice / 8);  // 16-byte units
-    uint4 xv[kUnits / kThreads];
-#pragma unroll
-    for (int i = 0; i < kUnits / kThreads; ++i) {
-      const int u = tid + i * kThreads, row = u / (kSlice / 8), cu = u % (kSlice / 8);
-      xv[i] = row < p.M ? ldg_nc_v4(p.x + (size_t)row * p.ldx + kbeg + 8 * cu) : zero;
+  if (tid == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
     }
-#pragma unroll
-    for (int i = 0; i < kUnits / kThreads; ++i) {
-      const int u = tid + i * kThreads, row = u / (kSlice / 8), cu = u % (kSlice / 8);
-      *reinterpret_cast<uint4*>(xs + row * kXRow + 16 * cu) = xv[i];
-    }
+    mbar_init(acc_full, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
   }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, kNBMax);
+    tmem_relinquish();
+  }
+  tc_fence_before();
   __syncthreads();
-  float acc[MT][4];
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    // ------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmW);
+      tma_prefetch_desc(&tmX);
+      const uint32_t bytes = (uint32_t)(kWBytes + p.nb * kBK * 2);
+      for (int b = 0; b < kBlocks; ++b) {
+        const int s = b % kStages;
+        if (!mbar_wait(&empty[s], ((b / kStages) & 1) ^ 1, abort_flag, p.err, kErrWaitEmpty)) break;
+        uint8_t* st = smem + s * kStageBytes;
+        mbar_arrive_expect_tx(&full[s], bytes);
+        tma_load_2d(st, &tmW, &full[s], kbeg + b * kBK, n0);
+        tma_load_2d(st + kWBytes, &tmX, &full[s], kbeg + b * kBK, 0);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------ UMMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_make(1, kNC, p.nb, 0, 0);
+      for (int b = 0; b < kBlocks; ++b) {
+        const int s = b % kStages;
+        if (!mbar_wait(&full[s], (b / kStages) & 1, abort_flag, p.err, kErrWaitFull)) break;
+        tc_fence_after();
+        const uint32_t wa = smem_u32(smem + s * kStageBytes), xa = wa + kWBytes;
 #pragma unroll
-  for (int i = 0; i < MT; ++i)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) acc[i][e] = 0.f;
-  const uint8_t* xth = xs + g * kXRow + 16 * c;
-#pragma unroll
-  for (int q = 0; q < kChunks; ++q) {
-#pragma unroll
-    for (int mi = 0; mi < MT; ++mi) {
-      const uint8_t* xa_p = xth + (16 * mi) * kXRow + 64 * q;
-      const uint4 xa = *reinterpret_cast<const uint4*>(xa_p);
-      const uint4 xb = *reinterpret_cast<const uint4*>(xa_p + 8 * kXRow);
-      mma_bf16_16816(acc[mi], xa.x, xb.x, xa.y, xb.y, wv[q].x, wv[q].y);
-      mma_bf16_16816(acc[mi], xa.z, xb.z, xa.w, xb.w, wv[q].z, wv[q].w);
+        for (int kk = 0; kk < kBK / 16; ++kk)
+          umma_f16_ss(tmem, sdesc_sw128(wa + 32 * kk, 16, 1024), sdesc_sw128(xa + 32 * kk, 16, 1024), idesc,
+                      (b > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&empty[s]);
+      }
+      umma_commit(acc_full);
     }
   }
-  __syncthreads();  // the x area becomes the partial tiles
-  float* red = vsm;                     // [MT*16][kRedLd] this CTA's partial tile
-  float* fin = vsm + MT * 16 * kRedLd;  // [MT*16][kRedLd] the summed rows of this CTA's slice
-  // Partial tile: rows 16 mi + g (+8), columns 8 warp + 2 c (+1).
+  // -------------------------------------------------- accumulator -> smem
+  // (warps 2-5: TMEM lane quadrant warp % 4 = output columns, columns = batch rows)
+  float* red = reinterpret_cast<float*>(smem);  // [nb][kRedLd] partial tile (the ring is free)
+  float* fin = red + kNBMax * kRedLd;          // [nb][kRedLd] summed rows of this CTA's slice
+  bool ok = true;
+  if (warp >= 2) {
+    ok = mbar_wait(acc_full, 0, abort_flag, p.err, kErrWaitAccFull);
+    if (__all_sync(0xffffffffu, ok)) {
+      tc_fence_after();
+      const int qd = warp & 3, col = 32 * qd + lane;
+      for (int c0 = 0; c0 < p.nb; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld32(tmem + ((uint32_t)(32 * qd) << 16) + (uint32_t)c0, v);
+        tmem_ld_wait();
 #pragma unroll
-  for (int mi = 0; mi < MT; ++mi) {
-    float* r0 = red + (16 * mi + g) * kRedLd + 8 * warp + 2 * c;
-    *reinterpret_cast<float2*>(r0) = make_float2(acc[mi][0], acc[mi][1]);
-    *reinterpret_cast<float2*>(r0 + 8 * kRedLd) = make_float2(acc[mi][2], acc[mi][3]);
+        for (int e = 0; e < 32; ++e)
+          if (c0 + e < p.nb) red[(c0 + e) * kRedLd + col] = __uint_as_float(v[e]);
+      }
+    }
   }
-  // Rows of this CTA's slice, summed over the cluster in rank order. A thread
-  // handles columns [4 (tid % 32), + 4) of rows tid / 32 + 16 it.
-  const int rows = MT * 16;
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kNBMax);
+  }
+  // Rows of this CTA's slice, summed over the cluster in rank order. Epilogue thread
+  // t handles columns [4 (t % 32), + 4) of rows t / 32 + 4 it. (A CTA whose waits
+  // ran out still takes part in the cluster barriers; its error is recorded.)
+  const int rows = p.nb;
   const int rpr = (rows + ks - 1) / ks;
   const int r0 = rank * rpr, r1 = min(rows, r0 + rpr);
-  const int col = 4 * (tid % 32), rsub = tid / 32;
+  const int t = tid - 64;
+  const int col = 4 * (t & 31), rsub = t >> 5;
   if (ks > 1) {
     cluster_sync();  // every CTA's partial tile is written and visible
-    uint32_t base[kMaxCluster];
+    if (t >= 0) {
+      uint32_t base[kMaxCluster];
 #pragma unroll
-    for (int q = 0; q < kMaxCluster; ++q) base[q] = q < ks ? dsmem_addr(red, (uint32_t)q) : 0u;
+      for (int q = 0; q < kMaxCluster; ++q) base[q] = q < ks ? dsmem_addr(red, (uint32_t)q) : 0u;
+      for (int row = r0 + rsub; row < r1; row += 4) {
+        const uint32_t off = (uint32_t)((row * kRedLd + col) * 4);
+        float4 v[kMaxCluster];
 #pragma unroll
-    for (int it = 0; it < MT; ++it) {
-      const int row = rsub + 16 * it;
-      if (row < r0 || row >= r1) continue;
-      const uint32_t off = (uint32_t)((row * kRedLd + col) * 4);
-      float4 v[kMaxCluster];
+        for (int q = 0; q < kMaxCluster; ++q)
+          v[q] = q < ks ? ld_dsmem_v4(base[q] + off) : make_float4(0.f, 0.f, 0.f, 0.f);
+        float4 sm = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-      for (int q = 0; q < kMaxCluster; ++q) v[q] = q < ks ? ld_dsmem_v4(base[q] + off) : make_float4(0.f, 0.f, 0.f, 0.f);
-      float4 sm = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-      for (int q = 0; q < kMaxCluster; ++q) {  // rank order (absent ranks add 0)
-        sm.x += v[q].x;
-        sm.y += v[q].y;
-        sm.z += v[q].z;
-        sm.w += v[q].w;
+        for (int q = 0; q < kMaxCluster; ++q) {  // rank order (absent ranks add 0)
+          sm.x += v[q].x;
+          sm.y += v[q].y;
+          sm.z += v[q].z;
+          sm.w += v[q].w;
+        }
+        *reinterpret_cast<float4*>(fin + row * kRedLd + col) = sm;
       }
-      *reinterpret_cast<float4*>(fin + row * kRedLd + col) = sm;
     }
     cluster_sync();  // the other CTAs are done reading this CTA's partial tile
   } else {
-    __syncthreads();
-#pragma unroll
-    for (int it = 0; it < MT; ++it) {
-      const int row = rsub + 16 * it;
-      *reinterpret_cast<float4*>(fin + row * kRedLd + col) = *reinterpret_cast<const float4*>(red + row * kRedLd + col);
-    }
-    __syncthreads();
+    fin = red;
   }
+  if (t < 0 || !ok) return;
   // RoPE, then bf16 stores (q columns) or the KV page scatter (k, v columns); four
   // columns per thread stay inside one head (head_dim is a multiple of 4).
   const int hd = p.head_dim, half = hd >> 1;
@@ -207,10 +219,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_decode_kernel(const VParams 
   const int nk = p.kv_dim > 0 ? p.kv_dim / hd : 1;
   __nv_bfloat16* kv_base = is_v ? p.kv_v : p.kv_k;
   const int pcol = in_head < half ? col + half : col - half;  // rotate-half partner
-#pragma unroll
-  for (int it = 0; it < MT; ++it) {
-    const int row = rsub + 16 * it;
-    if (row < r0 || row >= r1 || row >= p.M) continue;
+  for (int row = r0 + rsub; row < min(r1, p.M); row += 4) {
     float4 v = *reinterpret_cast<const float4*>(fin + row * kRedLd + col);
     if (roped) {
       const int pos = p.positions ? p.positions[row] : (p.pos_mod > 0 ? row % p.pos_mod : row);
@@ -240,21 +249,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_decode_kernel(const VParams 
   }
 }
 
-// Shared memory: the staged x rows, later the partial and summed tiles.
-template <int MT> constexpr int smem_bytes() {
-  return std::max(MT * 16 * kXRow, 2 * MT * 16 * kRedLd * (int)sizeof(float));
-}
-
-template <int MT>
-cudaError_t launch(const VParams& p, int tiles, cudaStream_t s) {
-  auto kern = gemv_decode_kernel<MT>;
-  constexpr int smem = smem_bytes<MT>();
-  static const cudaError_t ready = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+cudaError_t launch(const CUtensorMap* maps, const VParams& p, int tiles, cudaStream_t s) {
+  static const cudaError_t ready =
+      cudaFuncSetAttribute(gemv_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
   if (ready != cudaSuccess) return ready;
   cudaLaunchConfig_t lc{};
   lc.gridDim = dim3(tiles * p.ks, 1, 1);
   lc.blockDim = dim3(kThreads, 1, 1);
-  lc.dynamicSmemBytes = smem;
+  lc.dynamicSmemBytes = kSmem;
   lc.stream = s;
   cudaLaunchAttribute at[1];
   at[0].id = cudaLaunchAttributeClusterDimension;
@@ -263,7 +265,7 @@ cudaError_t launch(const VParams& p, int tiles, cudaStream_t s) {
   at[0].val.clusterDim.z = 1;
   lc.attrs = at;
   lc.numAttrs = 1;
-  return cudaLaunchKernelEx(&lc, kern, p);
+  return cudaLaunchKernelEx(&lc, gemv_decode_kernel, maps[0], maps[1], p);
 }
 
 }  // namespace
@@ -289,12 +291,10 @@ bool gemv_decode_supported(const GemmArgs& a) {
 cudaError_t gemv_decode(const GemmArgs& a, cudaStream_t s) {
   if (!gemv_decode_supported(a)) return cudaErrorInvalidValue;
   VParams p{};
-  p.x = static_cast<const __nv_bfloat16*>(a.a);
-  p.ldx = a.lda;
-  p.w = static_cast<const __nv_bfloat16*>(a.b);
   p.M = a.M;
   p.N = a.N;
   p.K = a.K;
+  p.nb = (a.M + 15) / 16 * 16;
   p.out = static_cast<__nv_bfloat16*>(a.out);
   p.ldo = a.ldo;
   p.rope_tab = a.rope_tab;
@@ -310,13 +310,14 @@ cudaError_t gemv_decode(const GemmArgs& a, cudaStream_t s) {
   p.kv_dim = a.kv_dim;
   p.err = a.err;
   p.ks = a.K / kSlice;
-  const int tiles = (a.N + kNC - 1) / kNC;
-  switch ((a.M + 15) / 16) {
-    case 1: return launch<1>(p, tiles, s);
-    case 2: return launch<2>(p, tiles, s);
-    case 3: return launch<3>(p, tiles, s);
-    default: return launch<4>(p, tiles, s);
-  }
+  alignas(64) CUtensorMap maps[2];
+  const int BF16 = (int)CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, SW = (int)CU_TENSOR_MAP_SWIZZLE_128B;
+  // W [N rows][K]: 128-row boxes; x [M rows][K]: boxes of nb rows, rows past M
+  // zero-filled
+  if (!make_tma_2d(&maps[0], a.b, BF16, 2, a.K, a.N, a.ldb, kBK, kNC, SW) ||
+      !make_tma_2d(&maps[1], a.a, BF16, 2, a.K, a.M, a.lda, kBK, p.nb, SW))
+    return cudaErrorInvalidValue;
+  return launch(maps, p, (a.N + kNC - 1) / kNC, s);
 }
 
 }  // namespace wv

@@ -125,6 +125,23 @@ struct PeerArgs {
   uint32_t* err = nullptr;
 };
 cudaError_t peer_allreduce(const PeerArgs& a, cudaStream_t s);
+// Owner side of a copy-engine reduce-scatter (peer.cu): slots[q] (q != rank, slot_bytes
+// apart) hold the peers' partial of this rank's count elements, flags[q] becomes
+// epoch once slot q has arrived; own (this rank's partial) is overwritten by the sum
+// over ranks in rank order.
+struct PeerRsArgs {
+  void* own = nullptr;
+  const void* slots = nullptr;
+  const uint32_t* flags = nullptr;
+  size_t count = 0;
+  size_t slot_bytes = 0;
+  int bf16 = 1;
+  int nranks = 0, rank = 0;
+  uint32_t epoch = 0;
+  uint64_t wait_ns = 0;
+  uint32_t* err = nullptr;
+};
+cudaError_t peer_rs_sum(const PeerRsArgs& a, int grid, cudaStream_t s);
 
 // CUDA-core fallback for shapes the TMA path cannot address (FP32 and BF16
 // operands only; same epilogue semantics, RoPE excluded).

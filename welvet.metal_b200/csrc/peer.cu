@@ -20,6 +20,10 @@
 // call in between, which the reader publishes only after its previous call ended).
 // A wait that runs out records kErrPeerWait in the error word and the CTA skips its
 // reduction; nothing traps.
+//
+// peer_rs_sum is the owner's half of the prefill output's reduce-scatter, whose
+// transfers are copy-engine copies (host/comm.cpp): it waits for the peers' epoch
+// flags and sums the slices.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -108,7 +112,73 @@ __global__ void __launch_bounds__(kThreads) peer_allreduce_kernel(const PeerArgs
   }
 }
 
+// Owner side of the chunked reduce-scatter: the N - 1 peers' slices of this rank's
+// rows arrive by copy-engine transfers, each followed by a 4-byte epoch write into
+// flag[q]; once every flag holds the epoch the rows are summed in rank order (this
+// rank's own partial in place) and written over the own partial.
+template <bool BF16>
+__global__ void __launch_bounds__(256) peer_rs_sum_kernel(const PeerRsArgs a) {
+  __shared__ int ok_all;
+  if (threadIdx.x == 0) {
+    ok_all = 1;
+    const uint64_t t0 = globaltimer();
+    for (int q = 0; q < a.nranks && ok_all; ++q) {
+      if (q == a.rank) continue;
+      while (ld_acquire_sys(a.flags + q) != a.epoch) {
+        if (globaltimer() - t0 > a.wait_ns) {
+          atomicCAS(a.err, 0u, (uint32_t)kErrPeerWait);
+          ok_all = 0;
+          break;
+        }
+        __nanosleep(2000);
+      }
+    }
+  }
+  __syncthreads();
+  if (!ok_all) return;
+  const size_t units = a.count * (BF16 ? 2 : 4) / 16;
+  uint4* own = static_cast<uint4*>(a.own);
+  for (size_t u = blockIdx.x * (size_t)blockDim.x + threadIdx.x; u < units; u += (size_t)gridDim.x * blockDim.x) {
+    float acc[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+    for (int q = 0; q < a.nranks; ++q) {
+      const uint4 v = q == a.rank ? own[u]
+                                  : reinterpret_cast<const uint4*>(static_cast<const char*>(a.slots) +
+                                                                   (size_t)q * a.slot_bytes)[u];
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+      if (BF16) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          acc[2 * e] += __uint_as_float(w[e] << 16);
+          acc[2 * e + 1] += __uint_as_float(w[e] & 0xFFFF0000u);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[e] += __uint_as_float(w[e]);
+      }
+    }
+    if (BF16) {
+      own[u] = make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]), pack_bf16x2(acc[4], acc[5]),
+                          pack_bf16x2(acc[6], acc[7]));
+    } else {
+      own[u] = make_uint4(__float_as_uint(acc[0]), __float_as_uint(acc[1]), __float_as_uint(acc[2]),
+                          __float_as_uint(acc[3]));
+    }
+  }
+}
+
 }  // namespace
+
+cudaError_t peer_rs_sum(const PeerRsArgs& a, int grid, cudaStream_t s) {
+  if (a.nranks < 2 || a.nranks > kPeerMaxRanks || a.rank < 0 || a.rank >= a.nranks || !a.own || !a.slots ||
+      !a.flags || (reinterpret_cast<uintptr_t>(a.own) & 15) || (reinterpret_cast<uintptr_t>(a.slots) & 15) ||
+      (a.count * (a.bf16 ? 2 : 4)) % 16 || a.count * (a.bf16 ? 2 : 4) > a.slot_bytes || grid < 1)
+    return cudaErrorInvalidValue;
+  if (a.bf16) peer_rs_sum_kernel<true><<<grid, 256, 0, s>>>(a);
+  else peer_rs_sum_kernel<false><<<grid, 256, 0, s>>>(a);
+  return cudaGetLastError();
+}
 
 cudaError_t peer_allreduce(const PeerArgs& a, cudaStream_t s) {
   if (a.nranks < 1 || a.nranks > kPeerMaxRanks || a.rank < 0 || a.rank >= a.nranks || !a.in || !a.out ||

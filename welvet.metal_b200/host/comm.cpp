@@ -217,6 +217,33 @@ bool peer_disabled() {
   return off;
 }
 
+// All-gathers the CUDA IPC handle of every rank's `own` allocation over NCCL and
+// opens the others' (areas[p]; areas[rank] = own). Collective.
+Status ipc_exchange(Mha* m, void* own, void** areas, cudaStream_t s) {
+  const int n = m->nranks;
+  cudaIpcMemHandle_t h;
+  WV_CUDA(cudaIpcGetMemHandle(&h, own), "cudaIpcGetMemHandle");
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+  DevBuf handles;
+  WV_TRY(handles.ensure((size_t)n * 64));
+  WV_CUDA(cudaMemcpyAsync(static_cast<char*>(handles.p) + (size_t)m->rank * 64, &h, 64, cudaMemcpyHostToDevice, s),
+          "peer handle");
+  WV_TRY(comm_allgather(m, handles.p, 16, false, s));  // 64 bytes = 16 floats per rank
+  WV_TRY(comm_wait(m, s, "peer handle exchange"));
+  std::vector<cudaIpcMemHandle_t> all(n);
+  WV_CUDA(cudaMemcpy(all.data(), handles.p, (size_t)n * 64, cudaMemcpyDeviceToHost), "peer handles");
+  for (int p = 0; p < n; ++p) {
+    if (p == m->rank) {
+      areas[p] = own;
+      continue;
+    }
+    void* ptr = nullptr;
+    WV_CUDA(cudaIpcOpenMemHandle(&ptr, all[p], cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+    areas[p] = ptr;
+  }
+  return Status::ok();
+}
+
 // Every rank allocates its receive area (2 parities x n senders x slot bytes, then
 // the flags), zeroes it, and the CUDA IPC handles are all-gathered over NCCL; each
 // rank opens the others' areas. Collective (same slot size on every rank).
@@ -229,36 +256,131 @@ Status peer_setup(Mha* m, size_t bytes, cudaStream_t s) {
   const size_t total = flags_off + 2 * (size_t)n * kPeerCtas * sizeof(uint32_t);
   WV_CUDA(cudaMalloc(&m->peer_area, total), "peer workspace");
   WV_CUDA(cudaMemsetAsync(m->peer_area, 0, total, s), "peer workspace clear");
-  cudaIpcMemHandle_t own;
-  WV_CUDA(cudaIpcGetMemHandle(&own, m->peer_area), "cudaIpcGetMemHandle");
-  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
-  DevBuf handles;
-  WV_TRY(handles.ensure((size_t)n * 64));
-  WV_CUDA(cudaMemcpyAsync(static_cast<char*>(handles.p) + (size_t)m->rank * 64, &own, 64, cudaMemcpyHostToDevice, s),
-          "peer handle");
-  WV_TRY(comm_allgather(m, handles.p, 16, false, s));  // 64 bytes = 16 floats per rank
-  WV_TRY(comm_wait(m, s, "peer handle exchange"));
-  std::vector<cudaIpcMemHandle_t> all(n);
-  WV_CUDA(cudaMemcpy(all.data(), handles.p, (size_t)n * 64, cudaMemcpyDeviceToHost), "peer handles");
-  for (int p = 0; p < n; ++p) {
-    if (p == m->rank) {
-      m->peer_areas[p] = m->peer_area;
-      continue;
-    }
-    void* ptr = nullptr;
-    cudaError_t e = cudaIpcOpenMemHandle(&ptr, all[p], cudaIpcMemLazyEnablePeerAccess);
-    if (e != cudaSuccess) {
-      peer_release(m);
-      return cuda_status(e, "cudaIpcOpenMemHandle (peer workspace)");
-    }
-    m->peer_areas[p] = ptr;
+  Status st = ipc_exchange(m, m->peer_area, m->peer_areas, s);
+  if (!st) {
+    peer_release(m);
+    return st;
   }
   m->peer_slot_bytes = slot;
   m->peer_flags_off = flags_off;
   m->peer_epoch = 0;
   return Status::ok();
 }
+
+void rs_release(Mha* m) {
+  for (int p = 0; p < kPeerMaxRanks; ++p) {
+    if (m->rs_areas[p] && m->rs_areas[p] != m->rs_area) cudaIpcCloseMemHandle(m->rs_areas[p]);
+    m->rs_areas[p] = nullptr;
+    if (m->rs_cs[p]) cudaStreamDestroy(m->rs_cs[p]);
+    m->rs_cs[p] = nullptr;
+    if (m->rs_done[p]) cudaEventDestroy(m->rs_done[p]);
+    m->rs_done[p] = nullptr;
+  }
+  if (m->rs_area) cudaFree(m->rs_area);
+  m->rs_area = nullptr;
+  if (m->rs_epoch_tab) cudaFree(m->rs_epoch_tab);
+  m->rs_epoch_tab = nullptr;
+  m->rs_slice_bytes = m->rs_flags_off = 0;
+  m->rs_chunks = 0;
+  m->rs_epoch = m->rs_calls = 0;
+}
+
+constexpr uint32_t kEpochs = 4096;  // flag values 1 .. kEpochs - 1, reused cyclically
+
+// Collective (the same chunks and slice size on every rank).
+Status rs_setup(Mha* m, int chunks, size_t slice_bytes, cudaStream_t s) {
+  if (m->rs_area && m->rs_chunks >= chunks && m->rs_slice_bytes >= slice_bytes) return Status::ok();
+  rs_release(m);
+  const int n = m->nranks;
+  const size_t slice = (slice_bytes + 255) / 256 * 256;
+  const size_t flags_off = 2 * (size_t)chunks * n * slice;
+  const size_t total = flags_off + 2 * (size_t)chunks * n * sizeof(uint32_t);
+  WV_CUDA(cudaMalloc(&m->rs_area, total), "reduce-scatter workspace");
+  WV_CUDA(cudaMemsetAsync(static_cast<char*>(m->rs_area) + flags_off, 0, total - flags_off, s), "flags clear");
+  std::vector<uint32_t> tab(kEpochs);
+  for (uint32_t i = 0; i < kEpochs; ++i) tab[i] = i;
+  WV_CUDA(cudaMalloc(&m->rs_epoch_tab, kEpochs * sizeof(uint32_t)), "epoch table");
+  WV_CUDA(cudaMemcpyAsync(m->rs_epoch_tab, tab.data(), kEpochs * sizeof(uint32_t), cudaMemcpyHostToDevice, s),
+          "epoch table");
+  Status st = ipc_exchange(m, m->rs_area, m->rs_areas, s);  // (its comm_wait also completes the copy above)
+  if (!st) {
+    rs_release(m);
+    return st;
+  }
+  for (int p = 0; p < n; ++p) {
+    if (p == m->rank) continue;
+    WV_CUDA(cudaStreamCreateWithFlags(&m->rs_cs[p], cudaStreamNonBlocking), "copy stream");
+    WV_CUDA(cudaEventCreateWithFlags(&m->rs_done[p], cudaEventDisableTiming), "copy event");
+  }
+  m->rs_slice_bytes = slice;
+  m->rs_flags_off = flags_off;
+  m->rs_chunks = chunks;
+  return Status::ok();
+}
+
+bool rs_disabled() {
+  static const bool off = [] {
+    const char* v = std::getenv("WELVET_B200_PEER_RS");
+    return v && v[0] == '0';
+  }();
+  return off;
+}
 }  // namespace
+
+bool comm_peer_rs_ok(const Mha* m) {
+  return m->comm && m->nranks > 1 && m->nranks <= kPeerMaxRanks && !rs_disabled();
+}
+
+Status comm_peer_rs_chunk(Mha* m, char* base, int64_t rows, int64_t max_rows, int dm, bool bf16, int chunk,
+                          int chunks, cudaEvent_t ready, cudaStream_t st) {
+  const int n = m->nranks;
+  const size_t es = bf16 ? 2 : 4;
+  if (!comm_peer_rs_ok(m) || rows % n || max_rows % n || chunk < 0 || chunk >= chunks)
+    return Status::err(2, "comm: peer reduce-scatter not available here");
+  const size_t slice = (size_t)(rows / n) * dm * es;
+  if (slice % 16) return Status::err(2, "comm: peer reduce-scatter needs 16-byte slices");
+  WV_TRY(rs_setup(m, chunks, (size_t)(max_rows / n) * dm * es, st));
+  if (chunk == 0) ++m->rs_calls;
+  const size_t cp = m->rs_calls & 1;
+  const uint32_t epoch = m->rs_epoch++ % (kEpochs - 1) + 1;
+  const size_t slot0 = (cp * m->rs_chunks + chunk) * n;  // first slot of this (call parity, chunk)
+  for (int p = 0; p < n; ++p) {
+    if (p == m->rank) continue;
+    char* area = static_cast<char*>(m->rs_areas[p]);
+    WV_CUDA(cudaStreamWaitEvent(m->rs_cs[p], ready, 0), "wait");
+    WV_CUDA(cudaMemcpyAsync(area + (slot0 + m->rank) * m->rs_slice_bytes, base + (size_t)p * slice, slice,
+                            cudaMemcpyDeviceToDevice, m->rs_cs[p]),
+            "slice to peer");
+    // issued after the slice on the same stream: written once the slice has landed
+    WV_CUDA(cudaMemcpyAsync(area + m->rs_flags_off + (slot0 + m->rank) * sizeof(uint32_t), m->rs_epoch_tab + epoch,
+                            sizeof(uint32_t), cudaMemcpyDeviceToDevice, m->rs_cs[p]),
+            "flag to peer");
+  }
+  PeerRsArgs a;
+  a.own = base + (size_t)m->rank * slice;
+  a.slots = static_cast<char*>(m->rs_area) + slot0 * m->rs_slice_bytes;
+  a.flags = reinterpret_cast<const uint32_t*>(static_cast<char*>(m->rs_area) + m->rs_flags_off) + slot0;
+  a.count = (size_t)(rows / n) * dm;
+  a.slot_bytes = m->rs_slice_bytes;
+  a.bf16 = bf16 ? 1 : 0;
+  a.nranks = n;
+  a.rank = m->rank;
+  a.epoch = epoch;
+  a.wait_ns = (uint64_t)std::min<int64_t>(m->comm_timeout_ms, 60000) * 1000000ull;
+  a.err = m->dev->err;
+  WV_CUDA(peer_rs_sum(a, 2 * m->dev->sm_count, st), "peer_rs_sum");
+  count_launch();
+  return Status::ok();
+}
+
+Status comm_peer_rs_finish(Mha* m, cudaStream_t s) {
+  for (int p = 0; p < m->nranks; ++p) {
+    if (p == m->rank || !m->rs_cs[p]) continue;
+    WV_CUDA(cudaEventRecord(m->rs_done[p], m->rs_cs[p]), "event");
+    WV_CUDA(cudaStreamWaitEvent(s, m->rs_done[p], 0), "wait");
+  }
+  return Status::ok();
+}
 
 bool comm_peer_ok(const Mha* m, size_t bytes) {
   return m->comm && m->nranks > 1 && m->nranks <= kPeerMaxRanks && bytes > 0 && bytes % 16 == 0 &&
@@ -327,6 +449,7 @@ Status comm_wait(Mha* m, cudaStream_t s, const char* what) {
 void comm_release(Mha* m) {
   if (!m) return;
   peer_release(m);
+  rs_release(m);
   if (m->comm) {
     if (nccl().ok) nccl().comm_destroy(static_cast<ncclComm_t>(m->comm));
     m->comm = nullptr;

@@ -846,6 +846,10 @@ Status mha_forward(Mha* m, int batch, int seq, const void* x, void* pre, void* p
   if (rs_out && ((int64_t)bc_max * seq % m->nranks || M % m->nranks ||
                  (int64_t)(batch - (int64_t)(chunks - 1) * bc_max) * seq % m->nranks))
     return Status::err(1, "mha: reduce-scatter output needs every chunk's rows divisible by the ranks");
+  // Reduce-scatter through copy engines and peer memory when the layer can take it
+  // (chunked calls), else NCCL's.
+  const bool peer_rs = rs_out && chunks > 1 && comm_peer_rs_ok(m) &&
+                       ((int64_t)bc_max * seq / m->nranks) * dm * (int64_t)es % 16 == 0;
   auto reduce_out = [&](char* base, int64_t rows, cudaStream_t st) -> Status {
     if (rs_out) return comm_reducescatter(m, base, (size_t)(rows / m->nranks) * dm, !f32, st);
     return comm_allreduce(m, base, (size_t)rows * dm, !f32, st);
@@ -919,7 +923,12 @@ Status mha_forward(Mha* m, int batch, int seq, const void* x, void* pre, void* p
       if (m->comm) {
         WV_CUDA(cudaStreamWaitEvent(m->comm_stream, m->chunk_done[i], 0), "wait");
         prof_begin(kProfAllReduce, m->comm_stream);
-        WV_TRY(reduce_out(static_cast<char*>(postd) + r0 * dm * es, rows, m->comm_stream));
+        if (peer_rs) {
+          WV_TRY(comm_peer_rs_chunk(m, static_cast<char*>(postd) + r0 * dm * es, rows, (int64_t)bc_max * seq, dm,
+                                    !f32, i, chunks, m->chunk_done[i], m->comm_stream));
+        } else {
+          WV_TRY(reduce_out(static_cast<char*>(postd) + r0 * dm * es, rows, m->comm_stream));
+        }
         prof_end(kProfAllReduce, m->comm_stream);
         if (host) {
           WV_CUDA(cudaEventRecord(m->io_ev[Mha::kMaxChunks + i], m->comm_stream), "event");
@@ -940,6 +949,7 @@ Status mha_forward(Mha* m, int batch, int seq, const void* x, void* pre, void* p
       WV_CUDA(cudaEventRecord(m->comm_done, m->comm_stream), "event");
       WV_CUDA(cudaStreamWaitEvent(s, m->comm_done, 0), "wait");
     }
+    if (peer_rs) WV_TRY(comm_peer_rs_finish(m, s));  // the copies have read every chunk's rows
     if (host) {
       WV_CUDA(cudaEventRecord(m->io_ev[2 * Mha::kMaxChunks], m->io_out), "event");
       WV_CUDA(cudaStreamWaitEvent(s, m->io_ev[2 * Mha::kMaxChunks], 0), "wait");

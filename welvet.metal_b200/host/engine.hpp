@@ -179,6 +179,18 @@ struct Mha {
   void* peer_areas[8] = {};
   size_t peer_slot_bytes = 0, peer_flags_off = 0;
   uint32_t peer_epoch = 0;
+  // Copy-engine reduce-scatter of the chunked prefill output (device buffers, output
+  // mode 1): receive area [2 call parities][chunks][N senders][slice] then flags
+  // [2][chunks][N], every rank's area opened through CUDA IPC, one copy stream per
+  // peer, and a device table of epoch values for the flag writes.
+  void* rs_area = nullptr;
+  void* rs_areas[8] = {};
+  size_t rs_slice_bytes = 0, rs_flags_off = 0;
+  int rs_chunks = 0;
+  cudaStream_t rs_cs[8] = {};
+  cudaEvent_t rs_done[8] = {};
+  uint32_t* rs_epoch_tab = nullptr;
+  uint32_t rs_epoch = 0, rs_calls = 0;
   static constexpr int kMaxChunks = 16;
   cudaEvent_t chunk_done[kMaxChunks] = {};
   cudaEvent_t comm_done = nullptr;
@@ -228,6 +240,18 @@ Status comm_reducescatter(Mha* m, void* buf, size_t count, bool bf16, cudaStream
 constexpr size_t kPeerMaxBytes = 4u << 20;
 bool comm_peer_ok(const Mha* m, size_t bytes);
 Status comm_peer_allreduce(Mha* m, void* buf, size_t count, bool bf16, cudaStream_t s);
+// Reduce-scatter of one chunk of a device-buffer forward's output through copy
+// engines and peer memory (no NCCL kernels on the SMs): the chunk's rows [base,
+// base + rows) (rows divisible by the ranks; the first chunk of a call has chunk 0)
+// are sent slice by slice to their owners once `ready` (recorded on the compute
+// stream after the chunk's output projection) has passed, and this rank's slice is
+// summed in place by a kernel on st. Collective, like NCCL; true from comm_peer_rs_ok
+// when the layer can take it (2-8 ranks; WELVET_B200_PEER_RS=0 keeps NCCL).
+bool comm_peer_rs_ok(const Mha* m);
+Status comm_peer_rs_chunk(Mha* m, char* base, int64_t rows, int64_t max_rows, int dm, bool bf16, int chunk,
+                          int chunks, cudaEvent_t ready, cudaStream_t st);
+// s waits until every copy of the call has read the output rows.
+Status comm_peer_rs_finish(Mha* m, cudaStream_t s);
 // Asynchronous NCCL error check; on an error the communicator is aborted and
 // dropped, code 4.
 Status comm_poll(Mha* m);
