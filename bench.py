@@ -66,6 +66,9 @@ WORKLOADS = {
     # dequantised inside the GEMM mainloop (weight_format 3, dtype 14)
     "cfg4-int4": dict(B=4, T=4096, d=4096, H=32, NK=32, wf=3, dt=14, prec=1, kind="prefill"),
     "cfg3": dict(B=64, T=4096, d=2048, H=32, NK=8, wf=0, prec=1, kind="decode"),
+    # diagnostic: one GPU's share of cfg5 at 8 GPUs (4 of the 32 heads: q/k/v
+    # projection N = 1536, output projection K = 512), without the collective
+    "cfg5-shard8": dict(B=32, T=8192, d=4096, H=4, NK=4, hd=128, wf=0, prec=1, kind="prefill+decode"),
     "cfg2": dict(B=8, T=2048, d=1024, H=16, NK=16, wf=0, prec=0, kind="prefill"),
     # FormatNone weight round trip (mount-time encode -> decode), all dtypes 0-33
     "codec": dict(n=1 << 28, kind="codec"),
@@ -113,7 +116,7 @@ def workload_of(wname, args):
     w["T"] = (args.seq if own else 0) or w["T"]
     if w["kind"] in BLOCK_KINDS or w["kind"] == "nbp":
         return w
-    w["hd"] = w["d"] // w["H"]
+    w["hd"] = w.get("hd") or w["d"] // w["H"]
     return w
 
 
@@ -976,7 +979,7 @@ def run_mha(args, wname, rank, world, local, primary=True):
     hb, hc = W.head_shard(H, NK, world, rank)
     kd_l = (hc // (H // NK)) * hd  # this rank's KV columns
     cfg = W.MhaConfig.make(d, H, NK, precision=prec, weight_format=wf, head_begin=hb, head_count=hc,
-                           device=local)
+                           device=local, head_dim=hd)
     check_parity = not args.no_parity and rank == 0
     # Full FP32 weights generated on the device (same stream on every rank), then mounted.
     shapes = [(H * hd, d), (NK * hd, d), (NK * hd, d), (d, H * hd)]
@@ -1148,7 +1151,7 @@ def run_mha(args, wname, rank, world, local, primary=True):
         torch.cuda.empty_cache()
         if check_parity or (primary and rank == 0 and world == 1 and not args.no_cpu):
             import oracle_py as O
-            oc = O.MhaCfg(d_model=d, num_heads=H, num_kv_heads=NK, max_seq_len=n_oracle, per_sequence=1)
+            oc = O.MhaCfg(d_model=d, num_heads=H, num_kv_heads=NK, head_dim=hd, max_seq_len=n_oracle, per_sequence=1)
             t0 = time.perf_counter()
             rpre, rpost = O.mha_forward(oc, 1, n_oracle, *oracle_weights(O, host_ws, wf, prec, w.get("dt", 1)), x_rows)
             dt = time.perf_counter() - t0
@@ -1195,7 +1198,7 @@ def run_mha(args, wname, rank, world, local, primary=True):
                 if check_parity:
                     import oracle_py as O
                     sel = [0, B // 2, B - 1]
-                    oc = O.MhaCfg(d_model=d, num_heads=H, num_kv_heads=NK, max_seq_len=T + 1, per_sequence=1)
+                    oc = O.MhaCfg(d_model=d, num_heads=H, num_kv_heads=NK, head_dim=hd, max_seq_len=T + 1, per_sequence=1)
                     _, rpost, _, _ = O.mha_decode(oc, [T] * len(sel), kc[sel].float().cpu().numpy(),
                                                   vc[sel].float().cpu().numpy(),
                                                   *oracle_weights(O, host_ws, wf, prec, w.get("dt", 1)),

@@ -342,6 +342,7 @@ __global__ void __launch_bounds__(128) decode_kernel(DecodeArgs a, int splits, i
 
 template <typename T>
 __global__ void decode_combine_kernel(DecodeArgs a, int splits) {
+  pdl_trigger();  // the next kernel (the output projection) may start loading its weights
   const int h = blockIdx.x, b = blockIdx.y, hd = a.head_dim;
   const float* P = a.partial + ((size_t)b * a.num_heads + h) * splits * (hd + 2);
   float mx = -INFINITY;

@@ -44,6 +44,14 @@ WV_DEV bool elect_one() {
   return pred != 0;
 }
 
+// ------------------------------------------- programmatic dependent launch
+// A kernel launched with programmatic stream serialization may start while its
+// predecessor on the stream is still running (once every predecessor CTA has
+// called pdl_trigger, or has exited); pdl_wait blocks the calling thread until the
+// predecessor has completed and its memory is visible. Both are no-ops otherwise.
+WV_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+WV_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // ------------------------------------------------------------------ mbarrier
 WV_DEV void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)

@@ -10,17 +10,17 @@
 // (128 weight rows = the M = 128 rows of a tcgen05 MMA) over a 512-wide K slice,
 // the batch rows are the MMA's N (a multiple of 16, zero-filled past M by TMA); a
 // thread-block cluster of ks = K / 512 CTAs (at most 8) along K covers the whole K
-// range. A TMA thread streams the slice's eight 64-wide k blocks of W (16 KB) and x
-// through a four-stage ring, one thread issues 4 UMMAs (K = 16) per block into a
-// TMEM accumulator [128 lanes = output columns][N columns = batch rows], and four
-// warps read it back. Each weight byte crosses shared memory once (an mma.sync
+// range. A TMA thread loads the slice's eight 64-wide k blocks of W (16 KB) and x —
+// all at once when the grid is one wave (one CTA per SM), else through a
+// three-stage ring (two CTAs per SM) — one thread issues 4 UMMAs (K = 16) per block
+// into a TMEM accumulator [128 lanes = output columns][N columns = batch rows], and
+// four warps read it back. Each weight byte crosses shared memory once (an mma.sync
 // form re-read the x fragments once per 8 output columns: ~1 MB of shared-memory
 // traffic per CTA, 10 us of a 15 us kernel).
 //
-// Epilogue: each CTA writes its FP32 partial tile to shared memory; after a
-// cluster barrier CTA r sums the partials of rows [r R, (r+1) R) from every CTA of
-// the cluster in cluster-rank order (distributed shared memory, four columns per
-// load; deterministic) and applies RoPE (rotate-half pairs inside a head: a head
+// Epilogue: each CTA copies the FP32 partial of batch rows [r R, (r+1) R) into CTA
+// r's inbox (16-byte distributed shared memory stores); after one cluster barrier
+// CTA r sums its inbox in cluster-rank order (deterministic) and applies RoPE (rotate-half pairs inside a head: a head
 // lies inside one 128-column tile for head_dim 32/64/128), then stores bf16 rows,
 // with the K and V column ranges scattered into the KV page pools (the cache
 // append) when kv_k is given.
@@ -37,15 +37,19 @@ constexpr int kNC = 128;         // output columns per CTA (the MMA's M)
 constexpr int kSlice = 512;      // K per CTA
 constexpr int kBK = 64;          // k per block (one 128-byte swizzled row)
 constexpr int kBlocks = kSlice / kBK;
-constexpr int kStages = 4;
 constexpr int kNBMax = 64;       // batch rows (MMA N) at most
 constexpr int kWBytes = kNC * kBK * 2;      // 16 KB
 constexpr int kXBytes = kNBMax * kBK * 2;   // 8 KB
 constexpr int kStageBytes = kWBytes + kXBytes;
-constexpr int kRedLd = kNC + 4;  // padded row of the partial tile (floats)
+constexpr int kRedLd = kNC;     // row of a partial tile (floats)
 constexpr int kMaxCluster = 8;
-constexpr int kSmem = 1024 + kStages * kStageBytes + 256;
-static_assert(2 * kNBMax * kRedLd * 4 <= kStages * kStageBytes, "partial tiles fit in the ring");
+// S stages: all eight k blocks of the slice in flight at once (S = 8, one CTA per SM,
+// for grids of one wave) or a three-stage ring (two CTAs per SM). IR: rows of the
+// inbox, ks x ceil(nb / ks) (64 when ks divides nb, at most 71).
+template <int S, int IR> constexpr int smem_bytes() { return 1024 + S * kStageBytes + IR * kRedLd * 4 + 256; }
+static_assert(smem_bytes<8, kNBMax>() <= 227 * 1024, "shared memory");
+static_assert(2 * smem_bytes<3, kNBMax + kMaxCluster>() <= 228 * 1024, "two CTAs per SM");
+static_assert(2 * kNBMax * kRedLd * 4 <= 3 * kStageBytes, "partial and summed rows fit in the ring");
 
 struct VParams {
   int M, N, K, ks, nb;  // nb: batch rows rounded up to 16 (the MMA's N)
@@ -62,12 +66,9 @@ struct VParams {
   uint32_t* err;
 };
 
-// Four floats of another CTA's shared memory (ordered by the cluster barriers
-// around the reads; no clobber, so the loads of one sum are in flight together).
-__device__ __forceinline__ float4 ld_dsmem_v4(uint32_t addr) {
-  float4 v;
-  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
-  return v;
+__device__ __forceinline__ void st_dsmem_v4(uint32_t addr, float4 v) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+               : "memory");
 }
 __device__ __forceinline__ uint32_t dsmem_addr(const void* local, uint32_t rank) {
   uint32_t r;
@@ -75,14 +76,18 @@ __device__ __forceinline__ uint32_t dsmem_addr(const void* local, uint32_t rank)
   return r;
 }
 
+template <int S, int IR>
 __global__ void __launch_bounds__(kThreads, 1)
     gemv_decode_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                        const VParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
-  uint64_t* empty = full + kStages;
-  uint64_t* acc_full = empty + kStages;
+  // inbox [source rank][row of this CTA's slice][kRedLd]: the cluster's partial sums
+  // of this CTA's rows, written by every CTA of the cluster (itself included)
+  float* inbox = reinterpret_cast<float*>(smem + S * kStageBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * kStageBytes + IR * kRedLd * 4);
+  uint64_t* empty = full + S;
+  uint64_t* acc_full = empty + S;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(acc_full + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   const int ks = p.ks;
@@ -91,9 +96,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n0 = tile * kNC;
   const int kbeg = rank * kSlice;
   const int warp = (int)warp_id(), lane = (int)lane_id(), tid = (int)threadIdx.x;
+  const int rpr = (p.nb + ks - 1) / ks;  // batch rows per CTA of the cluster
 
   if (tid == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -109,6 +115,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
+  // everything but the weight loads reads or writes what the previous kernel may
+  // still be producing or reading
+  if (warp != 0) pdl_wait();
 
   if (warp == 0) {
     // ------------------------------------------------------ TMA producer
@@ -116,9 +125,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&tmW);
       tma_prefetch_desc(&tmX);
       const uint32_t bytes = (uint32_t)(kWBytes + p.nb * kBK * 2);
-      for (int b = 0; b < kBlocks; ++b) {
-        const int s = b % kStages;
-        if (!mbar_wait(&empty[s], ((b / kStages) & 1) ^ 1, abort_flag, p.err, kErrWaitEmpty)) break;
+      // The weights do not depend on the previous kernel: the first S blocks of W
+      // are requested before waiting for it (programmatic dependent launch), x after.
+      for (int b = 0; b < S; ++b) {
+        mbar_arrive_expect_tx(&full[b], bytes);
+        tma_load_2d(smem + b * kStageBytes, &tmW, &full[b], kbeg + b * kBK, n0);
+      }
+      pdl_wait();
+      for (int b = 0; b < S; ++b) tma_load_2d(smem + b * kStageBytes + kWBytes, &tmX, &full[b], kbeg + b * kBK, 0);
+      for (int b = S; b < kBlocks; ++b) {
+        const int s = b % S;
+        if (!mbar_wait(&empty[s], ((b / S) & 1) ^ 1, abort_flag, p.err, kErrWaitEmpty)) break;
         uint8_t* st = smem + s * kStageBytes;
         mbar_arrive_expect_tx(&full[s], bytes);
         tma_load_2d(st, &tmW, &full[s], kbeg + b * kBK, n0);
@@ -130,23 +147,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       const uint32_t idesc = idesc_make(1, kNC, p.nb, 0, 0);
       for (int b = 0; b < kBlocks; ++b) {
-        const int s = b % kStages;
-        if (!mbar_wait(&full[s], (b / kStages) & 1, abort_flag, p.err, kErrWaitFull)) break;
+        const int s = b % S;
+        if (!mbar_wait(&full[s], (b / S) & 1, abort_flag, p.err, kErrWaitFull)) break;
         tc_fence_after();
         const uint32_t wa = smem_u32(smem + s * kStageBytes), xa = wa + kWBytes;
 #pragma unroll
         for (int kk = 0; kk < kBK / 16; ++kk)
           umma_f16_ss(tmem, sdesc_sw128(wa + 32 * kk, 16, 1024), sdesc_sw128(xa + 32 * kk, 16, 1024), idesc,
                       (b > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(&empty[s]);
+        if (S < kBlocks) umma_commit(&empty[s]);
       }
       umma_commit(acc_full);
     }
   }
-  // -------------------------------------------------- accumulator -> smem
+  // ---------------------------------- accumulator -> the row owners' inboxes
   // (warps 2-5: TMEM lane quadrant warp % 4 = output columns, columns = batch rows)
-  float* red = reinterpret_cast<float*>(smem);  // [nb][kRedLd] partial tile (the ring is free)
-  float* fin = red + kNBMax * kRedLd;          // [nb][kRedLd] summed rows of this CTA's slice
+  // The tile goes to shared memory first (red, over the ring: this CTA's MMAs are
+  // complete and no other CTA writes the ring), then every thread copies 16-byte
+  // pieces of its rows to their owners: batch row b belongs to cluster rank b / rpr,
+  // which receives it in inbox[rank].
+  float* red = reinterpret_cast<float*>(smem);  // [nb][kRedLd]
   bool ok = true;
   if (warp >= 2) {
     ok = mbar_wait(acc_full, 0, abort_flag, p.err, kErrWaitAccFull);
@@ -169,41 +189,37 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, kNBMax);
   }
-  // Rows of this CTA's slice, summed over the cluster in rank order. Epilogue thread
-  // t handles columns [4 (t % 32), + 4) of rows t / 32 + 4 it. (A CTA whose waits
-  // ran out still takes part in the cluster barriers; its error is recorded.)
-  const int rows = p.nb;
-  const int rpr = (rows + ks - 1) / ks;
-  const int r0 = rank * rpr, r1 = min(rows, r0 + rpr);
+  for (int i = tid; i < p.nb * (kRedLd / 4); i += kThreads) {
+    const int b = i / (kRedLd / 4), c4 = i % (kRedLd / 4);
+    const int q = b / rpr, lr = b - q * rpr;
+    const float4 v = reinterpret_cast<const float4*>(red + b * kRedLd)[c4];
+    float4* dst = reinterpret_cast<float4*>(inbox + (rank * rpr + lr) * kRedLd) + c4;
+    if (ks > 1) st_dsmem_v4(dsmem_addr(dst, (uint32_t)q), v);
+    else *dst = v;
+  }
+  if (ks > 1) cluster_sync();  // every CTA's rows are in their owners' inboxes
+  else __syncthreads();
+  // Rows of this CTA's slice summed in rank order into fin (the ring is free: this
+  // CTA's MMAs are complete, and no other CTA writes it). Epilogue thread t handles
+  // columns [4 (t % 32), + 4) of local rows t / 32 + 4 it.
+  float* fin = red + kNBMax * kRedLd;  // [rpr][kRedLd] (after red in the ring)
   const int t = tid - 64;
   const int col = 4 * (t & 31), rsub = t >> 5;
-  if (ks > 1) {
-    cluster_sync();  // every CTA's partial tile is written and visible
-    if (t >= 0) {
-      uint32_t base[kMaxCluster];
-#pragma unroll
-      for (int q = 0; q < kMaxCluster; ++q) base[q] = q < ks ? dsmem_addr(red, (uint32_t)q) : 0u;
-      for (int row = r0 + rsub; row < r1; row += 4) {
-        const uint32_t off = (uint32_t)((row * kRedLd + col) * 4);
-        float4 v[kMaxCluster];
-#pragma unroll
-        for (int q = 0; q < kMaxCluster; ++q)
-          v[q] = q < ks ? ld_dsmem_v4(base[q] + off) : make_float4(0.f, 0.f, 0.f, 0.f);
-        float4 sm = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-        for (int q = 0; q < kMaxCluster; ++q) {  // rank order (absent ranks add 0)
-          sm.x += v[q].x;
-          sm.y += v[q].y;
-          sm.z += v[q].z;
-          sm.w += v[q].w;
-        }
-        *reinterpret_cast<float4*>(fin + row * kRedLd + col) = sm;
+  const int r0 = rank * rpr, r1 = min(p.nb, r0 + rpr);
+  if (t >= 0) {
+    for (int lr = rsub; lr < r1 - r0; lr += 4) {
+      float4 sm = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int q = 0; q < ks; ++q) {
+        const float4 v = *reinterpret_cast<const float4*>(inbox + (q * rpr + lr) * kRedLd + col);
+        sm.x += v.x;
+        sm.y += v.y;
+        sm.z += v.z;
+        sm.w += v.w;
       }
+      *reinterpret_cast<float4*>(fin + lr * kRedLd + col) = sm;
     }
-    cluster_sync();  // the other CTAs are done reading this CTA's partial tile
-  } else {
-    fin = red;
   }
+  __syncthreads();
   if (t < 0 || !ok) return;
   // RoPE, then bf16 stores (q columns) or the KV page scatter (k, v columns); four
   // columns per thread stay inside one head (head_dim is a multiple of 4).
@@ -219,13 +235,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nk = p.kv_dim > 0 ? p.kv_dim / hd : 1;
   __nv_bfloat16* kv_base = is_v ? p.kv_v : p.kv_k;
   const int pcol = in_head < half ? col + half : col - half;  // rotate-half partner
-  for (int row = r0 + rsub; row < min(r1, p.M); row += 4) {
-    float4 v = *reinterpret_cast<const float4*>(fin + row * kRedLd + col);
+  for (int lr = rsub; lr < min(r1, p.M) - r0; lr += 4) {
+    const int row = r0 + lr;
+    float4 v = *reinterpret_cast<const float4*>(fin + lr * kRedLd + col);
     if (roped) {
       const int pos = p.positions ? p.positions[row] : (p.pos_mod > 0 ? row % p.pos_mod : row);
       const bool pos_ok = pos >= 0 && pos < p.rope_max_pos;
       if (!pos_ok) atomicCAS(p.err, 0u, 0x100u);
-      const float4 o = *reinterpret_cast<const float4*>(fin + row * kRedLd + pcol);
+      const float4 o = *reinterpret_cast<const float4*>(fin + lr * kRedLd + pcol);
       float vv[4] = {v.x, v.y, v.z, v.w};
       const float ov[4] = {o.x, o.y, o.z, o.w};
 #pragma unroll
@@ -249,23 +266,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+template <int S, int IR>
 cudaError_t launch(const CUtensorMap* maps, const VParams& p, int tiles, cudaStream_t s) {
-  static const cudaError_t ready =
-      cudaFuncSetAttribute(gemv_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+  auto kern = gemv_decode_kernel<S, IR>;
+  static const cudaError_t ready = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                        smem_bytes<S, IR>());
   if (ready != cudaSuccess) return ready;
   cudaLaunchConfig_t lc{};
   lc.gridDim = dim3(tiles * p.ks, 1, 1);
   lc.blockDim = dim3(kThreads, 1, 1);
-  lc.dynamicSmemBytes = kSmem;
+  lc.dynamicSmemBytes = smem_bytes<S, IR>();
   lc.stream = s;
-  cudaLaunchAttribute at[1];
+  cudaLaunchAttribute at[2];
   at[0].id = cudaLaunchAttributeClusterDimension;
   at[0].val.clusterDim.x = p.ks;
   at[0].val.clusterDim.y = 1;
   at[0].val.clusterDim.z = 1;
+  at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see pdl_wait above
+  at[1].val.programmaticStreamSerializationAllowed = 1;
   lc.attrs = at;
-  lc.numAttrs = 1;
-  return cudaLaunchKernelEx(&lc, gemv_decode_kernel, maps[0], maps[1], p);
+  lc.numAttrs = 2;
+  return cudaLaunchKernelEx(&lc, kern, maps[0], maps[1], p);
 }
 
 }  // namespace
@@ -317,7 +338,11 @@ cudaError_t gemv_decode(const GemmArgs& a, cudaStream_t s) {
   if (!make_tma_2d(&maps[0], a.b, BF16, 2, a.K, a.N, a.ldb, kBK, kNC, SW) ||
       !make_tma_2d(&maps[1], a.a, BF16, 2, a.K, a.M, a.lda, kBK, p.nb, SW))
     return cudaErrorInvalidValue;
-  return launch(maps, p, (a.N + kNC - 1) / kNC, s);
+  const int tiles = (a.N + kNC - 1) / kNC;
+  // one wave (and a cluster that divides the batch rows): every k block of a CTA in
+  // flight at once; else a ring, two CTAs per SM
+  if (tiles * p.ks <= a.sm_count && p.nb % p.ks == 0) return launch<kBlocks, kNBMax>(maps, p, tiles, s);
+  return launch<3, kNBMax + kMaxCluster>(maps, p, tiles, s);
 }
 
 }  // namespace wv

@@ -14,6 +14,8 @@ __global__ void prefill_slots_kernel(int* slots, int batch, int seq, int pps) {
 }
 
 __global__ void decode_rows_kernel(int* ctx, int* positions, int* slots, int batch, int pps) {
+  // the next kernel (the q/k/v projection) may start loading its weights
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= batch) return;
   const int L = ctx[b];
