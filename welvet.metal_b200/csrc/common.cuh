@@ -138,6 +138,8 @@ WV_DEV void tma_store_2d(const void* map, const void* src, int32_t x, int32_t y)
 WV_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // The issuing thread's bulk groups have finished reading shared memory.
 WV_DEV void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// ... at most one of them is still reading shared memory.
+WV_DEV void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 // ... and their global writes are complete.
 WV_DEV void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 

@@ -27,6 +27,8 @@ constexpr int kBM = 128;
 template <int KIND> struct GT;
 template <> struct GT<kGemmBF16> {
   static constexpr int BN = 256, BK = 64, STAGES = 4, UK = 16, NA = 1, NB = 1, ELEM = 2;
+  // output staging: per epilogue warp two slots of 32 rows x 64 bf16 columns
+  static constexpr int OUT_STAGE = 4 * 2 * 32 * 128;
   static constexpr uint32_t FMT = 1;
   static constexpr int CODE_BYTES = 0;  // B arrives ready for UMMA
   static constexpr int THREADS = 192;
@@ -57,6 +59,7 @@ template <> struct GT<kGemmI4> : GT<kGemmNF4> {};
 template <> struct GT<kGemmFP4> : GT<kGemmNF4> {};
 template <int KIND> __host__ __device__ constexpr bool byte_codes() { return KIND == kGemmFP8 || KIND == kGemmI8; }
 template <int KIND> __host__ __device__ constexpr bool nibble_codes() { return KIND == kGemmNF4 || KIND == kGemmI4 || KIND == kGemmFP4; }
+template <int KIND> __host__ __device__ constexpr int out_stage_bytes() { return KIND == kGemmBF16 ? GT<kGemmBF16>::OUT_STAGE : 0; }
 // The 16 BF16-exact values a nibble code stands for (before the epilogue scale).
 __device__ __forceinline__ float nibble_level(int kind, int c) {
   if (kind == kGemmI4) return (float)(c < 8 ? c : c - 16);                // Int4: two's complement
@@ -81,6 +84,7 @@ struct KParams {
   float* out_hi;
   float* out_lo;
   int split_only;  // FP32 output: only out_hi / out_lo are written
+  int stage_out;   // plain BF16 output: 64-column groups staged in shared memory, TMA-stored
   const float* b_scale;    // FP8: per-row scales; NF4: per-64 absmax (dequant warps)
   const float* col_scale;  // FP8 only: per-output-column scale applied in the epilogue
   int ldb;
@@ -329,6 +333,44 @@ __global__ void splitk_finish_kernel(const KParams p) {
   }
 }
 
+// Plain BF16 output through shared memory: the 32 rows of this warp (TMEM lanes)
+// are written in 64-column groups, each staged as [32 rows][128 B] in the 128-byte
+// swizzle (slot n_staged & 1 of the warp's two) and stored by one TMA store, so the
+// output leaves in whole 128-byte lines instead of one 16-byte piece of 32 rows per
+// store instruction; TMA clips rows past M and columns past N. Before a slot is
+// rewritten, lane 0 waits until at most one earlier store is still reading.
+template <int BN>
+__device__ __forceinline__ void epilogue_staged(const KParams& p, uint32_t tbase, const CUtensorMap* tmO,
+                                                uint8_t* stage, int row0, int n0, int lane, int& n_staged) {
+  for (int g = 0; g < BN / 64; ++g) {
+    const int gcol = n0 + 64 * g;
+    if (gcol >= p.N) break;
+    uint32_t x0[32], x1[32];
+    tmem_ld32(tbase + 64 * g, x0);
+    tmem_ld32(tbase + 64 * g + 32, x1);
+    tmem_ld_wait();
+    uint32_t pk[32];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      pk[e] = pack_bf16x2(__uint_as_float(x0[2 * e]), __uint_as_float(x0[2 * e + 1]));
+      pk[16 + e] = pack_bf16x2(__uint_as_float(x1[2 * e]), __uint_as_float(x1[2 * e + 1]));
+    }
+    uint8_t* buf = stage + (n_staged & 1) * 4096;
+    if (lane == 0) bulk_wait_read1();
+    __syncwarp();
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+      st_shared_v4(buf + lane * 128 + ((c ^ (lane & 7)) << 4), pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(tmO, buf, gcol, row0);
+      bulk_commit();
+    }
+    ++n_staged;
+  }
+}
+
 // 16 bytes of a 128-byte-swizzled K-major row: chunk index XOR (row mod 8).
 __device__ __forceinline__ uint32_t sw128_offset(int row, int chunk16) {
   return (uint32_t)(row * 128 + ((chunk16 ^ (row & 7)) << 4));
@@ -338,7 +380,7 @@ template <int KIND>
 __global__ void __launch_bounds__(GT<KIND>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA2,
                    const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmB2,
-                   const KParams p) {
+                   const __grid_constant__ CUtensorMap tmO, const KParams p) {
   using T = GT<KIND>;
   constexpr int BN = T::BN, BK = T::BK, S = T::STAGES;
   constexpr int A_BYTES = kBM * BK * T::ELEM;
@@ -351,7 +393,9 @@ __global__ void __launch_bounds__(GT<KIND>::THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * STAGE_BYTES);
+  constexpr int OUT_STAGE = out_stage_bytes<KIND>();
+  uint8_t* out_stage = smem + S * STAGE_BYTES;  // [warp][slot][32 rows][128 B], 1024-aligned
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * STAGE_BYTES + OUT_STAGE);
   uint64_t* empty = full + S;
   uint64_t* xfull = empty + S;  // dequantised B ready (FP8/NF4)
   uint64_t* accf = xfull + S;
@@ -469,6 +513,7 @@ __global__ void __launch_bounds__(GT<KIND>::THREADS, 1)
     const int q = warp & 3;
     int acc = 0;
     uint32_t acc_phase = 0;
+    int n_staged = 0;  // 64-column groups this warp has staged (slot = n_staged & 1)
     for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
       int mb, nb, kb0, kb1, sk;
       tile_work(t, p, mb, nb, kb0, kb1, sk);
@@ -477,6 +522,8 @@ __global__ void __launch_bounds__(GT<KIND>::THREADS, 1)
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * BN);
       if (p.ksplit > 1) epilogue_partial<BN>(p, tbase, mb * kBM + 32 * q + lane, nb * BN, sk);
+      else if (OUT_STAGE > 0 && p.stage_out)
+        epilogue_staged<BN>(p, tbase, &tmO, out_stage + q * 8192, mb * kBM + 32 * q, nb * BN, lane, n_staged);
       else epilogue_tile<BN>(p, tbase, mb * kBM + 32 * q + lane, nb * BN);
       tc_fence_before();
       mbar_arrive(&acce[acc]);
@@ -613,6 +660,9 @@ __global__ void __launch_bounds__(GT<KIND>::THREADS, 1)
     }
   }
 done:
+  // the staged output stores of each epilogue warp are complete (they read shared
+  // memory until then)
+  if (OUT_STAGE > 0 && warp >= 2 && warp < 6 && lane == 0) bulk_wait0();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -684,7 +734,7 @@ int splitk_count(const GemmArgs& g, int spatial, int k_blocks, int* kb_per, bool
 template <int KIND> size_t smem_bytes() {
   using T = GT<KIND>;
   const size_t stage = T::NA * kBM * T::BK * T::ELEM + T::NB * T::BN * T::BK * T::ELEM + T::CODE_BYTES;
-  return 1024 + T::STAGES * stage + 8 * (3 * T::STAGES + 4) + 16 + 512;
+  return 1024 + T::STAGES * stage + out_stage_bytes<KIND>() + 8 * (3 * T::STAGES + 4) + 16 + 512;
 }
 
 template <int KIND> cudaError_t launch(const GemmArgs& g, cudaStream_t stream) {
@@ -755,12 +805,21 @@ template <int KIND> cudaError_t launch(const GemmArgs& g, cudaStream_t stream) {
   p.swiglu_cols = g.swiglu_cols > 0 ? g.swiglu_cols : g.N / 2;
   p.err = g.err;
 
+  // Plain BF16 output (no split, RoPE, KV scatter, SwiGLU or TF32 split): staged
+  // 64-column groups stored by TMA ([rows][ldo], boxes of 64 columns x 32 rows).
+  CUtensorMap to = ta;
+  p.stage_out = 0;
+  if (out_stage_bytes<KIND>() > 0 && g.out_bf16 && p.ksplit == 1 && !g.swiglu && !g.kv_k && !g.out_hi &&
+      p.rope_cols == 0 && (reinterpret_cast<uintptr_t>(g.out) & 15) == 0 && ((size_t)g.ldo * 2) % 16 == 0 &&
+      make_map_2d(&to, g.out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.N, g.M, g.ldo, 64, 32,
+                  CU_TENSOR_MAP_SWIZZLE_128B))
+    p.stage_out = 1;
   const size_t smem = smem_bytes<KIND>();
   static cudaError_t attr = cudaFuncSetAttribute(gemm_tc_kernel<KIND>,
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (attr != cudaSuccess) return attr;
   const int grid = std::max(1, std::min(p.num_tiles, g.sm_count));
-  gemm_tc_kernel<KIND><<<grid, T::THREADS, smem, stream>>>(ta, ta2, tb, tb2, p);
+  gemm_tc_kernel<KIND><<<grid, T::THREADS, smem, stream>>>(ta, ta2, tb, tb2, to, p);
   if (p.ksplit > 1) {
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;

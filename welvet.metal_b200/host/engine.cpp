@@ -500,6 +500,18 @@ struct Proj {
   int kv_col0 = 0, kv_dim = 0;
 };
 
+// Chunks of a device-buffer forward with a communicator: 4, or WELVET_B200_FORWARD_CHUNKS
+// (1-16): more chunks leave less of the last chunk's collective exposed at the end,
+// at a few launches per chunk.
+int device_chunks() {
+  static const int n = [] {
+    const char* v = std::getenv("WELVET_B200_FORWARD_CHUNKS");
+    const int c = v ? std::atoi(v) : 0;
+    return c >= 1 && c <= Mha::kMaxChunks ? c : 4;
+  }();
+  return n;
+}
+
 // Few-row BF16 projections (decode) run as a GEMV streaming the weights at HBM rate
 // unless WELVET_B200_DECODE_GEMV=0 selects the split-K tensor-core GEMM.
 bool decode_gemv_enabled() {
@@ -693,7 +705,7 @@ Status mha_forward(Mha* m, int batch, int seq, const void* x, void* pre, void* p
   const bool defer_d2h = !on_device && m->comm && m->nranks > 1 && (!host_pinned(post) || !host_pinned(pre));
   // Host copies (about 40 ms per 2 GB each way on PCIe) want more, smaller chunks
   // than the all-reduce does.
-  int chunks = chunked ? std::min(batch, on_device ? 4 : Mha::kMaxChunks) : 1;
+  int chunks = chunked ? std::min(batch, on_device ? device_chunks() : Mha::kMaxChunks) : 1;
   // rows_io: chunk i takes bcl sequences of every rank (rank-major), bcl of this rank
   const int nr = rows_io ? m->nranks : 1, b_local = batch / nr;
   const int bcl = rows_io ? (b_local + std::min(b_local, Mha::kMaxChunks) - 1) / std::min(b_local, Mha::kMaxChunks)
