@@ -4,9 +4,14 @@ at 1/2/4/8 B200; % of roofline".
 
 Default workload (cfg5, the metric's 1/2/4/8-GPU configuration): batch 32 x seq
 8192, d_model 4096, 32 heads x 128, causal, RoPE, BF16 activations and weights,
-FP32 accumulation. Heads are sharded 32/N per GPU, the output projection is
-row-sharded and summed with NCCL all-reduce. A step = one prefill forward over all
-262144 tokens; value = whole-job prefill tok/s. After the timed prefill, 256
+FP32 accumulation. Heads are sharded 32/N per GPU. At N > 1 the device-timed
+prefill runs in 4 chunks of 8 sequences and rank r keeps the r-th row slice of each
+chunk (--output exchange, the default: each chunk's attention output goes to the
+rank owning its rows over NVLink peer memory, which runs the output projection over
+every head; --output reducescatter: the row-sharded output projection's partial
+sums are reduce-scattered; --output allreduce: NCCL all-reduce, every rank holds
+every row). A step = one prefill forward over all 262144 tokens; value = whole-job
+prefill tok/s. After the timed prefill, 256
 autoregressive decode steps run against the resulting KV cache and are reported
 under "decode". The line's "parity" compares rows of the timed forward's output
 with the FP64 oracle (oracle/, test infrastructure: the checker, never the thing
@@ -51,6 +56,11 @@ FP64_NOMINAL_TFLOPS = 37.0
 TRAFFIC_PREFILL_PER_TOKEN = 247.8e6 / 8192
 TRAFFIC_DECODE_PER_ROW = 135.12e6 / (2 * 4097)
 TRAFFIC_SOURCE = "ncu dram__bytes_read.sum+dram__bytes_write.sum at B=2 T=4096, scaled by units"
+
+# output collective of a device-buffer prefill at N > 1 (welvet_b200_mha_set_output_mode)
+OUTPUT_MODES = {"allreduce": 0, "reducescatter": 1, "exchange": 2}
+OUTPUT_NAMES = {"allreduce": "all-reduce", "reducescatter": "reduce-scatter",
+                "exchange": "attention-output exchange before the output projection"}
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "welvet.metal_b200"))
@@ -156,8 +166,11 @@ def workload_config_of(wname, args, world):
         return {"workload": f"{wname}: decode B={B} context {T} d={d} H={H}x{hd} NK={NK} RoPE{prec}{fmt}",
                 "global_batch": B, "seq_len": 1, "context": T, "parallelism": f"tp{world} (heads {H // world}/GPU)",
                 "l2": "KV cache larger than L2 (%.1f GB)" % (2 * B * T * NK * hd * es / 1e9)}
-    out = "" if world == 1 else (", reduce-scatter output (rank r keeps its row slice of each chunk)"
-                                 if args.output == "reducescatter" else ", all-reduce output")
+    out = "" if world == 1 else {
+        "reducescatter": ", reduce-scatter output (rank r keeps its row slice of each chunk)",
+        "exchange": ", attention-output exchange before the output projection (rank r keeps its row slice of "
+                    "each chunk)",
+        "allreduce": ", all-reduce output"}[args.output]
     return {"workload": f"{wname}: B={B} T={T} d={d} H={H}x{hd} NK={NK} causal RoPE{prec}{fmt}",
             "global_batch": B, "seq_len": T, "parallelism": f"tp{world} (heads {H // world}/GPU){out}",
             "l2": "inputs larger than L2 (x is %.1f GB)" % (B * T * d * es / 1e9)}
@@ -1000,9 +1013,11 @@ def run_mha(args, wname, rank, world, local, primary=True):
         dist.broadcast_object_list(uid, src=0)
         layer.attach_comm(uid[0], world, rank)
         # output collective of the device-timed prefill: reduce-scatter (rank r keeps
-        # the r-th row slice of each chunk summed; half the NVLink bytes) unless
-        # --output allreduce; decode and the host-buffer e2e path all-reduce
-        layer.set_output_mode(1 if args.output == "reducescatter" else 0)
+        # the r-th row slice of each chunk summed; half the NVLink bytes), the
+        # attention-output exchange (the same rows, the exchange before the output
+        # projection) or all-reduce (--output); decode and the host-buffer e2e path
+        # all-reduce
+        layer.set_output_mode(OUTPUT_MODES[args.output])
     stream = torch.cuda.current_stream()
     pk = peaks()
 
@@ -1089,10 +1104,9 @@ def run_mha(args, wname, rank, world, local, primary=True):
                 "launches_per_step": cnt / steps,
                 "kernel_ms_per_step": {k: prof[k][0] / steps for k in per_step},
                 "collective_ms_per_step": prof["allreduce"][0] / steps if world > 1 else 0.0,
-                "collective": ("reduce-scatter" if args.output == "reducescatter" else "all-reduce")
-                              if world > 1 else None,
+                "collective": OUTPUT_NAMES[args.output] if world > 1 else None,
                 "step_tflops": (pf + af) / world / (ms / 1e3) / 1e12}
-        if world > 1 and args.output == "reducescatter":
+        if world > 1 and args.output != "allreduce":
             # the same step with the all-reduce output, for comparison (3 steps)
             layer.set_output_mode(0)
             layer.forward(B, T, x, None, post, stream=stream)
@@ -1103,7 +1117,7 @@ def run_mha(args, wname, rank, world, local, primary=True):
             ev1.record(stream)
             barrier()
             roof["allreduce_output_ms_per_step"] = max_over_ranks(ev0.elapsed_time(ev1) / 3)
-            layer.set_output_mode(1)
+            layer.set_output_mode(OUTPUT_MODES[args.output])
 
         if primary and not args.no_e2e:
             # With N ranks each holds its B/N sequences in host memory and receives the
@@ -1402,7 +1416,7 @@ def main():
     ap.add_argument("--no-configs", action="store_true",
                     help="skip the cfg2/cfg3/cfg4/dequant sub-records of the default one-GPU line")
     ap.add_argument("--parity-tokens", type=int, default=1024)
-    ap.add_argument("--output", default="reducescatter", choices=["reducescatter", "allreduce"],
+    ap.add_argument("--output", default="exchange", choices=sorted(OUTPUT_MODES),
                     help="output collective of the device-timed prefill at N > 1")
     args = ap.parse_args()
 

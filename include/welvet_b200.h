@@ -87,8 +87,17 @@ WELVET_API welvet_status welvet_b200_mha_forward_rows(welvet_b200_mha* layer, in
  * must divide by N, and rank r's post holds the summed rows [c0 + r*n/N,
  * c0 + (r+1)*n/N) of each chunk (c0 its first row, n its rows); the other rows hold
  * this rank's partial sums (a sequence-sharded output, as a sequence-parallel
- * next layer consumes it). Host-buffer forwards and decode always all-reduce.
- * Code 1 for another mode. */
+ * next layer consumes it). mode 2: the same sequence-sharded output through an
+ * exchange of the attention output instead of the partial sums: each chunk's
+ * attention rows [c0 + r*n/N, c0 + (r+1)*n/N) of every rank's heads go to rank r
+ * (copy engines over NVLink peer memory, q_dim/d_model of mode 1's bytes), which
+ * runs the output projection over every head for its own rows only, so its rows
+ * equal the single-GPU layer's bit for bit; the other rows of post are not
+ * written. Needs BF16 activations, BF16 (weight format 0) weights, equal head
+ * shards and no `pre`; otherwise the call runs as mode 1. The first mode-2 forward
+ * gathers every rank's Wo columns (d_model x q_dim BF16 per rank) and sets up the
+ * receive areas: collective, like every forward with a communicator.
+ * Host-buffer forwards and decode always all-reduce. Code 1 for another mode. */
 WELVET_API welvet_status welvet_b200_mha_set_output_mode(welvet_b200_mha* layer, int32_t mode);
 
 /* Reads and clears the device error word of the layer's device after a

@@ -4,7 +4,9 @@ against the FP64 oracle's forward of the whole batch (per-sequence semantics, th
 same FP32 or BF16-rounded weights and inputs). Each rank passes only its half of
 the sequences and receives the summed output rows of that half. Then two decode
 steps over each rank's KV heads, their outputs summed through the NVLink
-peer-memory all-reduce, against the oracle's decode of the whole layer."""
+peer-memory all-reduce, against the oracle's decode of the whole layer. The
+device-buffer forward runs with the reduce-scatter output (mode 1) and with the
+attention-output exchange (mode 2); each rank's own rows against the oracle."""
 import os
 import socket
 
@@ -56,6 +58,27 @@ def _worker(rank, world, port, out_dir, precision):
     own = np.concatenate([pd[c0 + rank * 128:c0 + (rank + 1) * 128].float().cpu().numpy()
                           for c0 in range(0, B * T, 256)])
     np.save(os.path.join(out_dir, f"rs{rank}.npy"), own)
+    # device buffers, attention-output exchange (mode 2; FP32 layers run as mode 1):
+    # the same rows, two calls so both call parities of the receive areas are used
+    layer.set_output_mode(2)
+    for call in range(2):
+        pd = torch.full((B * T, d), float("nan"), device="cuda", dtype=dt)
+        layer.forward(B, T, xd, None, pd)
+        torch.cuda.synchronize()
+        layer.check_device()
+        own = np.concatenate([pd[c0 + rank * 128:c0 + (rank + 1) * 128].float().cpu().numpy()
+                              for c0 in range(0, B * T, 256)])
+        np.save(os.path.join(out_dir, f"xa{rank}_{call}.npy"), own)
+    # the unsharded layer on this GPU (no communicator) over the same inputs: mode 2
+    # sums every head in one accumulation, as this layer does
+    full = W.MhaLayer(W.MhaConfig.make(d, H, NK, precision=precision), *Ws)
+    pf = torch.zeros(B * T, d, device="cuda", dtype=dt)
+    full.forward(B, T, xd, None, pf)
+    torch.cuda.synchronize()
+    own = np.concatenate([pf[c0 + rank * 128:c0 + (rank + 1) * 128].float().cpu().numpy()
+                          for c0 in range(0, B * T, 256)])
+    np.save(os.path.join(out_dir, f"full{rank}.npy"), own)
+    full.close()
     if rank == 0:
         np.save(os.path.join(out_dir, "x.npy"), x.float().numpy())
     # decode: two steps over a paged KV cache holding this rank's KV heads; the
@@ -112,6 +135,13 @@ def test_forward_rows_two_ranks(tmp_path, precision):
         rows = np.concatenate([np.arange(c0 + r * 128, c0 + (r + 1) * 128) for c0 in range(0, B * T, 256)])
         rs = np.load(tmp_path / f"rs{r}.npy")
         assert rel_err(rs, want[rows]) < tol, (r, rel_err(rs, want[rows]))
+        full = np.load(tmp_path / f"full{r}.npy")
+        for call in range(2):  # attention-output exchange: the same rows
+            xa = np.load(tmp_path / f"xa{r}_{call}.npy")
+            assert np.isfinite(xa).all()
+            assert rel_err(xa, want[rows]) < tol, (r, call, rel_err(xa, want[rows]))
+            print(f"precision {precision} rank {r} call {call}: exchange vs oracle {rel_err(xa, want[rows]):.3e}, "
+                  f"max |exchange - unsharded layer| {np.abs(xa - full).max():.3e}")
     # decode steps: every rank holds the whole summed output
     kc, vc = np.load(tmp_path / "kc.npy"), np.load(tmp_path / "vc.npy")
     L = kc.shape[1]

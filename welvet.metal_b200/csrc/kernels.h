@@ -142,6 +142,11 @@ struct PeerRsArgs {
   uint32_t* err = nullptr;
 };
 cudaError_t peer_rs_sum(const PeerRsArgs& a, int grid, cudaStream_t s);
+// One warp waits (bounded) until flags[q] == epoch for every sender q != rank
+// (code kErrPeerWait in *err on expiry); the attention-output exchange's barrier
+// before the output projection.
+cudaError_t peer_flags_wait(const uint32_t* flags, int nranks, int rank, uint32_t epoch, uint64_t wait_ns,
+                            uint32_t* err, cudaStream_t s);
 
 // CUDA-core fallback for shapes the TMA path cannot address (FP32 and BF16
 // operands only; same epilogue semantics, RoPE excluded).

@@ -168,7 +168,35 @@ __global__ void __launch_bounds__(256) peer_rs_sum_kernel(const PeerRsArgs a) {
   }
 }
 
+// Receiving side of the attention-output exchange (output mode 2): the peers'
+// column blocks of this rank's rows arrive by copy-engine transfers, each followed by
+// a 4-byte epoch write into flags[q]. One warp, lane q waiting (bounded by time) for
+// sender q, so the output projection queued behind this kernel on the same stream
+// starts only once every block has landed. The kernel holds one SM for the wait only;
+// the data needs no further pass.
+__global__ void __launch_bounds__(32) peer_flags_wait_kernel(const uint32_t* flags, int nranks, int rank,
+                                                             uint32_t epoch, uint64_t wait_ns, uint32_t* err) {
+  const int q = (int)threadIdx.x;
+  if (q >= nranks || q == rank) return;
+  const uint64_t t0 = globaltimer();
+  while (ld_acquire_sys(flags + q) != epoch) {
+    if (globaltimer() - t0 > wait_ns) {
+      atomicCAS(err, 0u, (uint32_t)kErrPeerWait);
+      return;
+    }
+    __nanosleep(500);
+  }
+}
+
 }  // namespace
+
+cudaError_t peer_flags_wait(const uint32_t* flags, int nranks, int rank, uint32_t epoch, uint64_t wait_ns,
+                            uint32_t* err, cudaStream_t s) {
+  if (!flags || !err || nranks < 2 || nranks > kPeerMaxRanks || rank < 0 || rank >= nranks)
+    return cudaErrorInvalidValue;
+  peer_flags_wait_kernel<<<1, 32, 0, s>>>(flags, nranks, rank, epoch, wait_ns, err);
+  return cudaGetLastError();
+}
 
 cudaError_t peer_rs_sum(const PeerRsArgs& a, int grid, cudaStream_t s) {
   if (a.nranks < 2 || a.nranks > kPeerMaxRanks || a.rank < 0 || a.rank >= a.nranks || !a.own || !a.slots ||

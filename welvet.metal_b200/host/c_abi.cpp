@@ -174,7 +174,7 @@ welvet_status welvet_b200_mha_forward_rows(welvet_b200_mha* layer, int32_t batch
 }
 
 welvet_status welvet_b200_mha_set_output_mode(welvet_b200_mha* layer, int32_t mode) {
-  if (!layer || (mode != 0 && mode != 1)) return wv::to_c(Status::err(1, "mha: invalid output mode"));
+  if (!layer || mode < 0 || mode > 2) return wv::to_c(Status::err(1, "mha: invalid output mode"));
   std::lock_guard<std::mutex> lock(layer->m->mu);
   layer->m->out_mode = mode;
   return ok_status();

@@ -382,6 +382,143 @@ Status comm_peer_rs_finish(Mha* m, cudaStream_t s) {
   return Status::ok();
 }
 
+// ------------------------------------------ attention-output exchange (mode 2)
+namespace {
+void xa_release(Mha* m) {
+  for (int p = 0; p < kPeerMaxRanks; ++p) {
+    if (m->xa_areas[p] && m->xa_areas[p] != m->xa_area) cudaIpcCloseMemHandle(m->xa_areas[p]);
+    m->xa_areas[p] = nullptr;
+    if (m->xa_cs[p]) cudaStreamDestroy(m->xa_cs[p]);
+    m->xa_cs[p] = nullptr;
+    if (m->xa_done[p]) cudaEventDestroy(m->xa_done[p]);
+    m->xa_done[p] = nullptr;
+  }
+  if (m->xa_area) cudaFree(m->xa_area);
+  m->xa_area = nullptr;
+  if (m->xa_epoch_tab) cudaFree(m->xa_epoch_tab);
+  m->xa_epoch_tab = nullptr;
+  m->xa_slot_bytes = m->xa_flags_off = 0;
+  m->xa_chunks = 0;
+  m->xa_epoch = m->xa_calls = 0;
+  m->wo_full.release();
+}
+
+// Collective (the same chunks and slot size on every rank): receive area, flags,
+// IPC mappings, copy streams and the gathered Wo.
+Status xa_setup(Mha* m, int chunks, size_t slot_bytes, cudaStream_t s) {
+  if (m->xa_area && m->xa_chunks >= chunks && m->xa_slot_bytes >= slot_bytes) return Status::ok();
+  xa_release(m);
+  const int n = m->nranks;
+  const size_t slot = (slot_bytes + 255) / 256 * 256;
+  const size_t flags_off = 2 * (size_t)chunks * slot;
+  const size_t total = flags_off + 2 * (size_t)chunks * n * sizeof(uint32_t);
+  WV_CUDA(cudaMalloc(&m->xa_area, total), "exchange workspace");
+  WV_CUDA(cudaMemsetAsync(static_cast<char*>(m->xa_area) + flags_off, 0, total - flags_off, s), "flags clear");
+  std::vector<uint32_t> tab(kEpochs);
+  for (uint32_t i = 0; i < kEpochs; ++i) tab[i] = i;
+  WV_CUDA(cudaMalloc(&m->xa_epoch_tab, kEpochs * sizeof(uint32_t)), "epoch table");
+  WV_CUDA(cudaMemcpyAsync(m->xa_epoch_tab, tab.data(), kEpochs * sizeof(uint32_t), cudaMemcpyHostToDevice, s),
+          "epoch table");
+  Status st = ipc_exchange(m, m->xa_area, m->xa_areas, s);
+  if (!st) {
+    xa_release(m);
+    return st;
+  }
+  for (int p = 0; p < n; ++p) {
+    if (p == m->rank) continue;
+    WV_CUDA(cudaStreamCreateWithFlags(&m->xa_cs[p], cudaStreamNonBlocking), "copy stream");
+    WV_CUDA(cudaEventCreateWithFlags(&m->xa_done[p], cudaEventDisableTiming), "copy event");
+  }
+  // Every head's Wo columns: the ranks' [d, q_dim_l] shards are all-gathered (rank
+  // blocks one after another) and laid out as [d, q_dim], rank p's block in columns
+  // [p q_dim_l, (p+1) q_dim_l) (the exchange's column order).
+  const int64_t dm = m->cfg.c.d_model, qdl = m->qd_l;
+  DevBuf gathered;
+  WV_TRY(gathered.ensure((size_t)n * dm * qdl * 2));
+  WV_CUDA(cudaMemcpyAsync(gathered.as<char>() + (size_t)m->rank * dm * qdl * 2, m->wo.p, (size_t)dm * qdl * 2,
+                          cudaMemcpyDeviceToDevice, s), "Wo shard");
+  WV_TRY(comm_allgather(m, gathered.p, (size_t)dm * qdl, true, s));
+  WV_TRY(m->wo_full.ensure((size_t)dm * qdl * n * 2));
+  for (int p = 0; p < n; ++p)
+    WV_CUDA(cudaMemcpy2DAsync(m->wo_full.as<char>() + (size_t)p * qdl * 2, (size_t)n * qdl * 2,
+                              gathered.as<char>() + (size_t)p * dm * qdl * 2, (size_t)qdl * 2, (size_t)qdl * 2, dm,
+                              cudaMemcpyDeviceToDevice, s), "Wo layout");
+  WV_TRY(comm_wait(m, s, "exchange set-up"));  // `gathered` is freed on return
+  m->xa_slot_bytes = slot;
+  m->xa_flags_off = flags_off;
+  m->xa_chunks = chunks;
+  return Status::ok();
+}
+
+bool xa_disabled() {
+  static const bool off = [] {
+    const char* v = std::getenv("WELVET_B200_PEER_XA");
+    return v && v[0] == '0';
+  }();
+  return off;
+}
+}  // namespace
+
+bool comm_xa_ok(const Mha* m) {
+  return m->comm && m->nranks > 1 && m->nranks <= kPeerMaxRanks && m->precision == 1 && m->wfmt == 0 &&
+         m->qd_l * m->nranks == m->cfg.qd && ((int64_t)m->qd_l * 2) % 16 == 0 && !xa_disabled();
+}
+
+Status comm_xa_chunk(Mha* m, const char* attn, int64_t rows, int64_t max_rows, int chunk, int chunks,
+                     cudaEvent_t ready, cudaStream_t s, const void** a_out) {
+  const int n = m->nranks;
+  if (!comm_xa_ok(m) || rows % n || max_rows % n || chunk < 0 || chunk >= chunks || chunks > Mha::kMaxChunks)
+    return Status::err(2, "comm: attention-output exchange not available here");
+  const int64_t own = rows / n, qdl = m->qd_l, qd = (int64_t)qdl * n;
+  WV_TRY(xa_setup(m, chunks, (size_t)(max_rows / n) * qd * 2, s));
+  if (chunk == 0) ++m->xa_calls;
+  const size_t cp = m->xa_calls & 1;
+  const uint32_t epoch = m->xa_epoch++ % (kEpochs - 1) + 1;
+  m->xa_chunk_epoch[chunk] = epoch;
+  const size_t slot = cp * m->xa_chunks + chunk;  // (call parity, chunk)
+  const size_t flag0 = slot * n;                  // its first flag
+  // rows [p own, (p+1) own) of this chunk go to rank p, into columns [rank qdl, ...)
+  for (int p = 0; p < n; ++p) {
+    char* dst = static_cast<char*>(m->xa_areas[p]) + slot * m->xa_slot_bytes + (size_t)m->rank * qdl * 2;
+    const char* src = attn + (size_t)p * own * qdl * 2;
+    if (p == m->rank) {
+      WV_CUDA(cudaMemcpy2DAsync(dst, (size_t)qd * 2, src, (size_t)qdl * 2, (size_t)qdl * 2, own,
+                                cudaMemcpyDeviceToDevice, s), "own block");
+      continue;
+    }
+    WV_CUDA(cudaStreamWaitEvent(m->xa_cs[p], ready, 0), "wait");
+    WV_CUDA(cudaMemcpy2DAsync(dst, (size_t)qd * 2, src, (size_t)qdl * 2, (size_t)qdl * 2, own,
+                              cudaMemcpyDeviceToDevice, m->xa_cs[p]), "block to peer");
+    // issued after the block on the same stream: written once the block has landed
+    WV_CUDA(cudaMemcpyAsync(static_cast<char*>(m->xa_areas[p]) + m->xa_flags_off + (flag0 + m->rank) * 4,
+                            m->xa_epoch_tab + epoch, 4, cudaMemcpyDeviceToDevice, m->xa_cs[p]),
+            "flag to peer");
+  }
+  *a_out = static_cast<const char*>(m->xa_area) + slot * m->xa_slot_bytes;
+  return Status::ok();
+}
+
+Status comm_xa_wait(Mha* m, int chunk, cudaStream_t s) {
+  if (!m->xa_area || chunk < 0 || chunk >= m->xa_chunks) return Status::err(4, "comm: exchange not set up");
+  const size_t slot = (m->xa_calls & 1) * m->xa_chunks + chunk;
+  const uint32_t* flags =
+      reinterpret_cast<const uint32_t*>(static_cast<const char*>(m->xa_area) + m->xa_flags_off) + slot * m->nranks;
+  const uint64_t wait_ns = (uint64_t)std::min<int64_t>(m->comm_timeout_ms, 60000) * 1000000ull;
+  WV_CUDA(peer_flags_wait(flags, m->nranks, m->rank, m->xa_chunk_epoch[chunk], wait_ns, m->dev->err, s),
+          "peer_flags_wait");
+  count_launch();
+  return Status::ok();
+}
+
+Status comm_xa_finish(Mha* m, cudaStream_t s) {
+  for (int p = 0; p < m->nranks; ++p) {
+    if (p == m->rank || !m->xa_cs[p]) continue;
+    WV_CUDA(cudaEventRecord(m->xa_done[p], m->xa_cs[p]), "event");
+    WV_CUDA(cudaStreamWaitEvent(s, m->xa_done[p], 0), "wait");
+  }
+  return Status::ok();
+}
+
 bool comm_peer_ok(const Mha* m, size_t bytes) {
   return m->comm && m->nranks > 1 && m->nranks <= kPeerMaxRanks && bytes > 0 && bytes % 16 == 0 &&
          bytes <= kPeerMaxBytes && !peer_disabled();
@@ -450,6 +587,7 @@ void comm_release(Mha* m) {
   if (!m) return;
   peer_release(m);
   rs_release(m);
+  xa_release(m);
   if (m->comm) {
     if (nccl().ok) nccl().comm_destroy(static_cast<ncclComm_t>(m->comm));
     m->comm = nullptr;

@@ -756,11 +756,15 @@ Status mha_forward(Mha* m, int batch, int seq, const void* x, void* pre, void* p
   const int max_pos = stream_mode ? (int)M : seq;
   WV_TRY(ensure_rope(m, max_pos, s));
 
-  // QKV projection, attention and O projection of sequences [b0, b0 + bc).
-  auto run_rows = [&](int b0, int bc) -> Status {
+  // QKV projection, attention and O projection of sequences [b0, b0 + bc); with
+  // with_o false the attention output goes to attn_at and the O projection is left
+  // to the caller (the attention-output exchange).
+  auto run_rows = [&](int b0, int bc, void* attn_at = nullptr, bool with_o = true) -> Status {
     const int64_t r0 = (int64_t)b0 * seq, Mc = (int64_t)bc * seq;
     const void* xc = static_cast<const char*>(xd) + r0 * dm * es;
-    void* attn = pred ? static_cast<void*>(static_cast<char*>(pred) + r0 * m->qd_l * es) : m->attn.p;
+    void* attn = attn_at ? attn_at
+                 : pred  ? static_cast<void*>(static_cast<char*>(pred) + r0 * m->qd_l * es)
+                         : m->attn.p;
     Proj q;
     q.M = (int)Mc;
     q.K = dm;
@@ -829,6 +833,7 @@ Status mha_forward(Mha* m, int batch, int seq, const void* x, void* pre, void* p
     prof_begin(kProfAttnPrefill, s);
     WV_TRY(run_attention(m, a, s));
     prof_end(kProfAttnPrefill, s);
+    if (!with_o) return Status::ok();
 
     Proj o;
     o.M = (int)Mc;
@@ -853,8 +858,9 @@ Status mha_forward(Mha* m, int batch, int seq, const void* x, void* pre, void* p
   };
 
   // Reduce-scatter output (device buffers): chunk rows split evenly over the ranks,
-  // rank r keeps the r-th slice of each chunk summed; other rows hold its partial.
-  const bool rs_out = m->comm && m->nranks > 1 && m->out_mode == 1 && on_device && !rows_io;
+  // rank r keeps the r-th slice of each chunk summed; other rows hold its partial
+  // (mode 1), or are not written (mode 2, the attention-output exchange).
+  const bool rs_out = m->comm && m->nranks > 1 && m->out_mode >= 1 && on_device && !rows_io;
   if (rs_out && ((int64_t)bc_max * seq % m->nranks || M % m->nranks ||
                  (int64_t)(batch - (int64_t)(chunks - 1) * bc_max) * seq % m->nranks))
     return Status::err(1, "mha: reduce-scatter output needs every chunk's rows divisible by the ranks");
@@ -862,11 +868,55 @@ Status mha_forward(Mha* m, int batch, int seq, const void* x, void* pre, void* p
   // (chunked calls), else NCCL's.
   const bool peer_rs = rs_out && chunks > 1 && comm_peer_rs_ok(m) &&
                        ((int64_t)bc_max * seq / m->nranks) * dm * (int64_t)es % 16 == 0;
+  // Attention-output exchange (mode 2): the chunk's attention rows go to their
+  // owners, which run the output projection over every head (K = q_dim) for their
+  // own rows only; without it the layer takes mode 1.
+  const bool xa = rs_out && m->out_mode == 2 && chunks > 1 && comm_xa_ok(m) && !pre;
   auto reduce_out = [&](char* base, int64_t rows, cudaStream_t st) -> Status {
     if (rs_out) return comm_reducescatter(m, base, (size_t)(rows / m->nranks) * dm, !f32, st);
     return comm_allreduce(m, base, (size_t)rows * dm, !f32, st);
   };
-  if (chunks == 1) {
+  if (xa) {
+    // Per chunk: QKV projection and attention into attn (every chunk's rows kept
+    // until its copies have read them), the exchange's copies, then the previous
+    // chunk's output projection once its blocks have landed; so chunk i's transfers
+    // overlap chunk i + 1's projections and attention.
+    WV_TRY(m->attn.ensure((size_t)M * m->qd_l * es));
+    const void* a_slot[Mha::kMaxChunks] = {};
+    int64_t o_row0[Mha::kMaxChunks] = {}, o_rows[Mha::kMaxChunks] = {};
+    auto o_proj = [&](int i) -> Status {
+      WV_TRY(comm_xa_wait(m, i, s));
+      Proj o;
+      o.M = (int)o_rows[i];
+      o.K = m->cfg.qd;
+      o.lda = m->cfg.qd;
+      o.N = dm;
+      o.out = static_cast<char*>(postd) + o_row0[i] * dm * es;
+      o.ldo = dm;
+      o.w = m->wo_full.p;
+      o.a = a_slot[i];
+      prof_begin(kProfGemmO, s);
+      WV_TRY(run_proj(m, o, s));
+      prof_end(kProfGemmO, s);
+      return Status::ok();
+    };
+    int n_done = 0;
+    for (int i = 0, b0 = 0; i < chunks && b0 < batch; ++i, b0 += bc_max, ++n_done) {
+      const int bc = std::min(bc_max, batch - b0);
+      const int64_t r0 = (int64_t)b0 * seq, rows = (int64_t)bc * seq;
+      char* attn_i = m->attn.as<char>() + r0 * m->qd_l * es;
+      WV_TRY(run_rows(b0, bc, attn_i, false));
+      WV_CUDA(cudaEventRecord(m->chunk_done[i], s), "event");
+      prof_begin(kProfAllReduce, s);
+      WV_TRY(comm_xa_chunk(m, attn_i, rows, Mc_max, i, chunks, m->chunk_done[i], s, &a_slot[i]));
+      prof_end(kProfAllReduce, s);
+      o_rows[i] = rows / m->nranks;
+      o_row0[i] = r0 + m->rank * o_rows[i];
+      if (i > 0) WV_TRY(o_proj(i - 1));
+    }
+    WV_TRY(o_proj(n_done - 1));
+    WV_TRY(comm_xa_finish(m, s));  // the copies have read every chunk's rows
+  } else if (chunks == 1) {
     WV_TRY(run_rows(0, batch));
     if (m->comm) {
       prof_begin(kProfAllReduce, s);

@@ -191,6 +191,22 @@ struct Mha {
   cudaEvent_t rs_done[8] = {};
   uint32_t* rs_epoch_tab = nullptr;
   uint32_t rs_epoch = 0, rs_calls = 0;
+  // Attention-output exchange of the chunked prefill (device buffers, output mode 2):
+  // receive area [2 call parities][chunks][rows/N x q_dim] (the output projection's
+  // A operand: sender p's heads in columns [p q_dim_l, (p+1) q_dim_l)), then flags
+  // [2][chunks][N]; every rank's area opened through CUDA IPC, one copy stream per
+  // peer, a device table of epoch values for the flag writes, and every head's Wo
+  // columns [d, q_dim] gathered from the ranks on first use.
+  void* xa_area = nullptr;
+  void* xa_areas[8] = {};
+  size_t xa_slot_bytes = 0, xa_flags_off = 0;
+  int xa_chunks = 0;
+  cudaStream_t xa_cs[8] = {};
+  cudaEvent_t xa_done[8] = {};
+  uint32_t* xa_epoch_tab = nullptr;
+  uint32_t xa_epoch = 0, xa_calls = 0;
+  uint32_t xa_chunk_epoch[16] = {};
+  DevBuf wo_full;
   static constexpr int kMaxChunks = 16;
   cudaEvent_t chunk_done[kMaxChunks] = {};
   cudaEvent_t comm_done = nullptr;
@@ -252,6 +268,20 @@ Status comm_peer_rs_chunk(Mha* m, char* base, int64_t rows, int64_t max_rows, in
                           int chunks, cudaEvent_t ready, cudaStream_t st);
 // s waits until every copy of the call has read the output rows.
 Status comm_peer_rs_finish(Mha* m, cudaStream_t s);
+// Attention-output exchange of one chunk of a device-buffer forward (output mode 2,
+// BF16 layers with format-0 weights, 2-8 ranks; WELVET_B200_PEER_XA=0 turns it
+// off): once `ready` (recorded on s after the chunk's attention) has passed, rows
+// [p rows/N, (p+1) rows/N) of this rank's attention output `attn` [rows, q_dim_l]
+// go by copy engine into rank p's receive slot, columns [rank q_dim_l, ...), and
+// this rank's own block by a copy on s. *a_out = this rank's slot [rows/N, q_dim],
+// complete once comm_xa_wait(chunk) has passed on s. The first call sets up the
+// receive areas and gathers every head's Wo (m->wo_full). Collective.
+bool comm_xa_ok(const Mha* m);
+Status comm_xa_chunk(Mha* m, const char* attn, int64_t rows, int64_t max_rows, int chunk, int chunks,
+                     cudaEvent_t ready, cudaStream_t s, const void** a_out);
+Status comm_xa_wait(Mha* m, int chunk, cudaStream_t s);
+// s waits until every copy of the call has read the attention rows.
+Status comm_xa_finish(Mha* m, cudaStream_t s);
 // Asynchronous NCCL error check; on an error the communicator is aborted and
 // dropped, code 4.
 Status comm_poll(Mha* m);

@@ -430,7 +430,9 @@ class MhaLayer:
 
     def set_output_mode(self, mode: int):
         """0: all-reduce output (default); 1: reduce-scatter, rank r keeps the r-th
-        row slice of each chunk summed (welvet_b200_mha_set_output_mode)."""
+        row slice of each chunk summed; 2: the same rows through an exchange of the
+        attention output before the output projection (BF16 layers; otherwise as 1)
+        (welvet_b200_mha_set_output_mode)."""
         check(lib().welvet_b200_mha_set_output_mode(self._h, mode))
 
     def attach_comm(self, uid: bytes, nranks: int, rank: int):
