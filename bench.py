@@ -1190,7 +1190,8 @@ def run_mha(args, wname, rank, world, local, primary=True):
     decode = None
     n_dec = steps if decode_only else (args.decode_steps if primary else 0)
     if n_dec > 0 and w["kind"] != "prefill":
-        extra = n_dec + warmup + 1 + (steps if decode_only and primary and not args.no_e2e else 0)
+        n_prof = min(n_dec, 32)  # the instrumented pass (per-kernel times) after the timed one
+        extra = n_dec + n_prof + warmup + 1 + (steps if decode_only and primary and not args.no_e2e else 0)
         kv = W.KvCache(layer, B, T + extra + 16)
         xd = torch.empty(B, d, device="cuda", dtype=act)
         W.fill_synthetic(xd, 1, 1, 1.0, offset=M * d)
@@ -1234,23 +1235,29 @@ def run_mha(args, wname, rank, world, local, primary=True):
             W.launch_count(reset=True)
         barrier()
         ctx0 = T + warmup
-        W.profile_read(reset=True)
-        W.profile_enable(True)
+        # The timed pass runs uninstrumented: per-kernel events between the step's
+        # kernels would break the programmatic-dependent-launch overlap of its short
+        # kernels. A second pass of n_prof steps records the per-kernel times.
         ev0.record(stream)
         for _ in range(n_dec):
             layer.decode(kv, B, xd, None, pd, stream=stream)
         ev1.record(stream)
         barrier()
-        W.profile_enable(False)
-        dprof = W.profile_read(reset=True)
         if decode_only:
             launches = W.launch_count(reset=True)
             clk = clocks.stop()
-        layer.check_device()
         dms = max_over_ranks(ev0.elapsed_time(ev1) / n_dec)
+        W.profile_read(reset=True)
+        W.profile_enable(True)
+        for _ in range(n_prof):
+            layer.decode(kv, B, xd, None, pd, stream=stream)
+        barrier()
+        W.profile_enable(False)
+        dprof = W.profile_read(reset=True)
+        layer.check_device()
         # algorithmic bytes of one decode-attention launch: the K and V rows of every
-        # cached position (average context over the steps) + q and the output
-        avg_ctx = ctx0 + (n_dec + 1) / 2.0
+        # cached position (average context over the instrumented steps) + q and the output
+        avg_ctx = ctx0 + n_dec + (n_prof + 1) / 2.0
         attn_bytes = B * avg_ctx * kd_l * es * 2 + 2 * B * hc * hd * es
         at, ac = dprof["attn_decode"]
         a_ms = at / max(ac, 1)
@@ -1263,8 +1270,9 @@ def run_mha(args, wname, rank, world, local, primary=True):
                              else None),
                  "bytes_per_launch": attn_bytes, "avg_launch_ms": a_ms,
                  "step_bytes": step_bytes, "step_gbs": step_bytes / (dms / 1e3) / 1e9,
-                 "kernel_ms_per_step": {k: dprof[k][0] / n_dec for k in
-                                        ("gemm_qkv_decode", "attn_decode", "gemm_o_decode", "allreduce")}}
+                 "kernel_ms_per_step": {k: dprof[k][0] / n_prof for k in
+                                        ("gemm_qkv_decode", "attn_decode", "gemm_o_decode", "allreduce")},
+                 "kernel_times": f"CUDA events around each kernel over {n_prof} further steps (instrumented pass)"}
         decode = {"value": B / (dms / 1e3), "unit": "tok/s", "ms_per_step": dms, "steps": n_dec,
                   "context": f"{ctx0}..{ctx0 + n_dec}", "roofline": droof}
         if decode_only:

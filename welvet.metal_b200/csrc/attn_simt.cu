@@ -343,6 +343,7 @@ __global__ void __launch_bounds__(128) decode_kernel(DecodeArgs a, int splits, i
 template <typename T>
 __global__ void decode_combine_kernel(DecodeArgs a, int splits) {
   pdl_trigger();  // the next kernel (the output projection) may start loading its weights
+  pdl_wait();     // launched as a programmatic dependent: the split partials are complete
   const int h = blockIdx.x, b = blockIdx.y, hd = a.head_dim;
   const float* P = a.partial + ((size_t)b * a.num_heads + h) * splits * (hd + 2);
   float mx = -INFINITY;
@@ -426,7 +427,8 @@ cudaError_t attn_decode(const DecodeArgs& a, cudaStream_t s) {
     cudaError_t e = attn_decode_tc(a, splits, s);
     if (e != cudaSuccess) return e;
     if (a.is_bf16)
-      decode_combine_kernel<__nv_bfloat16><<<dim3(a.num_heads, a.batch), 128, 0, s>>>(a, splits);
+      return launch_pdl(decode_combine_kernel<__nv_bfloat16>, dim3(a.num_heads, a.batch), dim3(128), 0, s, a,
+                        splits);
     return cudaGetLastError();
   }
   const int chunk = (a.max_ctx + splits - 1) / splits;

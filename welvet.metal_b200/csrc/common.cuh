@@ -13,6 +13,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #define WV_DEV __device__ __forceinline__
 
 namespace wv {
@@ -51,6 +53,25 @@ WV_DEV bool elect_one() {
 // predecessor has completed and its memory is visible. Both are no-ops otherwise.
 WV_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 WV_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Launch as a programmatic dependent of the previous kernel on the stream: the grid
+// may start while that kernel finishes; it must call pdl_wait() before reading
+// anything the previous kernels wrote.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args&&... args) {
+  cudaLaunchConfig_t lc{};
+  lc.gridDim = grid;
+  lc.blockDim = block;
+  lc.dynamicSmemBytes = smem;
+  lc.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  lc.attrs = at;
+  lc.numAttrs = 1;
+  return cudaLaunchKernelEx(&lc, kern, std::forward<Args>(args)...);
+}
 
 // ------------------------------------------------------------------ mbarrier
 WV_DEV void mbar_init(uint64_t* bar, uint32_t count) {

@@ -85,12 +85,6 @@ __global__ void __launch_bounds__(kWarps * 32)
   uint32_t* err = a.err ? a.err : local_err;
   uint8_t* ring = smem + warp * D::RING;
 
-  const int L = a.ctx_len[b];
-  const int k0 = split * chunk, k1 = min(L, k0 + chunk);
-  const int pg0 = k0 / kPageTokens;
-  const int npages = k1 > k0 ? (k1 - k0 + kPageTokens - 1) / kPageTokens : 0;
-  const int mine = npages > warp ? (npages - warp + kWarps - 1) / kWarps : 0;  // pages of this warp
-
   if (threadIdx.x == 0) {
     *abort_flag = 0;
     *local_err = 0;
@@ -99,6 +93,17 @@ __global__ void __launch_bounds__(kWarps * 32)
     for (int s = 0; s < D::STAGES; ++s) mbar_init(&full[s], 1);
   fence_barrier_init();
   __syncthreads();
+  // Launched as a programmatic dependent of the q/k/v projection: the lengths, q and
+  // the step's appended K/V row are read only after it has completed; the combine
+  // kernel behind this one may launch now (it waits the same way).
+  pdl_wait();
+  pdl_trigger();
+
+  const int L = a.ctx_len[b];
+  const int k0 = split * chunk, k1 = min(L, k0 + chunk);
+  const int pg0 = k0 / kPageTokens;
+  const int npages = k1 > k0 ? (k1 - k0 + kPageTokens - 1) / kPageTokens : 0;
+  const int mine = npages > warp ? (npages - warp + kWarps - 1) / kWarps : 0;  // pages of this warp
 
   const int* bt = a.block_table + (size_t)b * a.max_pages;
   auto issue = [&](int i) {  // lane 0: page i of this warp into stage i % STAGES
@@ -286,8 +291,7 @@ cudaError_t launch_g(const CUtensorMap& mk, const CUtensorMap& mv, const DecodeA
   auto go = [&](auto kern) -> cudaError_t {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, D::SMEM);
     if (e != cudaSuccess) return e;
-    kern<<<grid, kWarps * 32, D::SMEM, s>>>(mk, mv, a, splits, chunk);
-    return cudaGetLastError();
+    return launch_pdl(kern, grid, dim3(kWarps * 32), D::SMEM, s, mk, mv, a, splits, chunk);
   };
   if (a.sigmoid) return a.alibi ? go(decode_tc_kernel<HD, G, true, true>) : go(decode_tc_kernel<HD, G, false, true>);
   return a.alibi ? go(decode_tc_kernel<HD, G, true, false>) : go(decode_tc_kernel<HD, G, false, false>);

@@ -43,6 +43,7 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 
 template <bool BF16>
 __global__ void __launch_bounds__(kThreads) peer_allreduce_kernel(const PeerArgs a) {
+  pdl_wait();  // launched as a programmatic dependent of the kernel producing `in`
   const int n = a.nranks, par = (int)(a.epoch & 1u), cta = blockIdx.x;
   // 16-byte units of the vector, split over the CTAs
   const size_t units = (a.count * (BF16 ? 2 : 4) + 15) / 16;
@@ -214,9 +215,8 @@ cudaError_t peer_allreduce(const PeerArgs& a, cudaStream_t s) {
     return cudaErrorInvalidValue;
   const size_t bytes = a.count * (a.bf16 ? 2 : 4);
   if (bytes % 16 || bytes > a.slot_bytes) return cudaErrorInvalidValue;
-  if (a.bf16) peer_allreduce_kernel<true><<<kPeerCtas, kThreads, 0, s>>>(a);
-  else peer_allreduce_kernel<false><<<kPeerCtas, kThreads, 0, s>>>(a);
-  return cudaGetLastError();
+  return a.bf16 ? launch_pdl(peer_allreduce_kernel<true>, dim3(kPeerCtas), dim3(kThreads), 0, s, a)
+                : launch_pdl(peer_allreduce_kernel<false>, dim3(kPeerCtas), dim3(kThreads), 0, s, a);
 }
 
 }  // namespace wv
