@@ -117,30 +117,31 @@ def test_matches_oracle_attention(torch_cuda, B, T, H, NK, hd, pos, lens, precis
 
 @pytest.mark.gpu
 def test_fewer_splits_when_default_does_not_fit(torch_cuda):
-    """B=2, 64 heads of 256 over 8 KV heads at 9600 keys: the default 37 splits need
-    2*64*258*37 floats > 2^20, so the call runs with 31 splits; checked against a
-    float32 PyTorch softmax(q k^T) v of the same bf16 inputs."""
+    """FP32 buffers (CUDA-core decode kernel), B=64 sequences, 64 heads of 128 over 8
+    KV heads, 600 cached keys: the kernel's default of 2 splits needs 2*64*64*130 floats
+    > 2^20, so the call runs with one split; checked against a float64 PyTorch
+    softmax(q k^T) v of the same inputs."""
     torch = torch_cuda
-    B, T, H, NK, hd = 2, 9600, 64, 8, 256
-    assert B * H * (hd + 2) * 37 > STATIC_FLOATS
-    cfg, q, k, v, bt, kp, vp = _setup(torch, B, T, H, NK, hd, pos=1, seed=11)
-    lens = [T, 5000]
+    B, T, H, NK, hd = 64, 600, 64, 8, 128
+    assert 2 * B * H * (hd + 2) > STATIC_FLOATS >= B * H * (hd + 2)
+    cfg, q, k, v, bt, kp, vp = _setup(torch, B, T, H, NK, hd, pos=1, seed=11, precision=0)
+    lens = [T - (b * 37) % 500 for b in range(B)]
     rows = torch.tensor([b * T + L - 1 for b, L in enumerate(lens)], device="cuda")
     q_dec = q[rows].contiguous()
     ctx = torch.tensor(lens, device="cuda", dtype=torch.int32)
     want = []
     for b, L in enumerate(lens):
-        qb = q_dec[b].float().view(H, hd)
-        kb = k[b * T:b * T + L].float().view(L, NK, hd).repeat_interleave(H // NK, dim=1)
-        vb = v[b * T:b * T + L].float().view(L, NK, hd).repeat_interleave(H // NK, dim=1)
+        qb = q_dec[b].double().view(H, hd)
+        kb = k[b * T:b * T + L].double().view(L, NK, hd).repeat_interleave(H // NK, dim=1)
+        vb = v[b * T:b * T + L].double().view(L, NK, hd).repeat_interleave(H // NK, dim=1)
         s = torch.einsum("hd,lhd->hl", qb, kb) / hd ** 0.5
         want.append(torch.einsum("hl,lhd->hd", torch.softmax(s, dim=1), vb).reshape(-1).cpu().numpy())
     want = np.stack(want)
     for call in range(2):
-        out = torch.full((B, H * hd), float("nan"), device="cuda", dtype=torch.bfloat16)
+        out = torch.full((B, H * hd), float("nan"), device="cuda", dtype=torch.float32)
         st = _call(cfg, B, T, q_dec.data_ptr(), H * hd, kp.data_ptr(), vp.data_ptr(), bt.data_ptr(), bt.shape[1],
                    ctx.data_ptr(), out.data_ptr(), H * hd)
         assert st.code == 0, st.message
         torch.cuda.synchronize()
-        assert rel_err(out.float().cpu().numpy(), want) < TOL, f"call {call}"
+        assert rel_err(out.cpu().numpy(), want) < TOL_F32, f"call {call}"
     W.device_check()

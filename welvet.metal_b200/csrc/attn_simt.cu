@@ -409,9 +409,18 @@ cudaError_t attn_prefill_simt(const AttnArgs& a, cudaStream_t s) {
 int decode_splits(const DecodeArgs& a) {
   if (a.splits > 0) return a.splits;
   const int pairs = a.batch * a.num_kv_heads;
-  const int target = 4 * a.sm_count;
-  int sp = std::max(1, (target + pairs - 1) / pairs);
   const int max_by_len = std::max(1, (a.max_ctx + 255) / 256);  // >= 256 keys per split
+  if (decode_tc_supported(a)) {
+    // Tensor-core kernel (about 96 KB of pages in flight per CTA, 2 CTAs per SM):
+    // when the (sequence, KV head) pairs leave room, as many equal splits as fill one
+    // wave, so every CTA streams its keys with all the others resident; more splits
+    // than that would leave a last wave of a few CTAs running the tail of the KV read
+    // at a fraction of the HBM bandwidth. More pairs than one wave holds: one split.
+    const int slots = decode_tc_ctas_per_sm(a.head_dim) * a.sm_count;
+    return std::max(1, std::min(max_by_len, slots / pairs));
+  }
+  const int target = 4 * a.sm_count;
+  const int sp = std::max(1, (target + pairs - 1) / pairs);
   return std::min(sp, max_by_len);
 }
 

@@ -25,6 +25,7 @@
 
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cmath>
 
 namespace wv {
@@ -310,6 +311,11 @@ cudaError_t launch_hd(const CUtensorMap& mk, const CUtensorMap& mv, const Decode
 }
 
 }  // namespace
+
+int decode_tc_ctas_per_sm(int head_dim) {
+  const int smem = head_dim == 64 ? DT<64>::SMEM : head_dim == 128 ? DT<128>::SMEM : DT<256>::SMEM;
+  return std::max(1, (228 * 1024) / (smem + 1024));  // 1 KB of each CTA's shared memory is reserved
+}
 
 bool decode_tc_supported(const DecodeArgs& a) {
   if (!a.is_bf16 || a.num_kv_heads <= 0 || a.num_heads % a.num_kv_heads) return false;

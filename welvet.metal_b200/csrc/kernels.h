@@ -283,6 +283,7 @@ size_t decode_scratch_floats(const DecodeArgs& a);
 // else the CUDA-core kernel; then the split combine.
 cudaError_t attn_decode(const DecodeArgs& a, cudaStream_t s);
 bool decode_tc_supported(const DecodeArgs& a);
+int decode_tc_ctas_per_sm(int head_dim);  // resident decode_tc_kernel CTAs per SM
 cudaError_t attn_decode_tc(const DecodeArgs& a, int splits, cudaStream_t s);
 // Append rows of k/v (token-major [rows, ld]) into the page pools at slot[row].
 // Pool layout: [page][kv_head][kPageTokens][head_dim]; slot = page*kPageTokens + row.
