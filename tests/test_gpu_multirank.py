@@ -47,6 +47,11 @@ def _worker(rank, world, port, out_dir, precision):
     for _ in range(2):  # the second call reuses the staging buffers and events
         layer.forward_rows(bl, T, xl, post)
     np.save(os.path.join(out_dir, f"rows{rank}.npy"), post.float().numpy())
+    # one sequence per rank: the forward runs as a single chunk
+    x1 = x[rank * T:(rank + 1) * T].contiguous().pin_memory()
+    p1 = torch.zeros(T, d, dtype=dt).pin_memory()
+    layer.forward_rows(1, T, x1, p1)
+    np.save(os.path.join(out_dir, f"one{rank}.npy"), p1.float().numpy())
     # device buffers, reduce-scatter output: the batch runs in 4 chunks of 2
     # sequences (256 rows); rank r keeps rows [c0 + 128 r, c0 + 128 (r + 1)) summed
     layer.set_output_mode(1)
@@ -131,6 +136,9 @@ def test_forward_rows_two_ranks(tmp_path, precision):
     got = np.concatenate([np.load(tmp_path / f"rows{r}.npy") for r in range(2)])
     tol = 1e-4 if precision == 0 else 2e-2
     assert rel_err(got, want) < tol, rel_err(got, want)
+    for r in range(2):  # one sequence per rank: sequence r
+        one = np.load(tmp_path / f"one{r}.npy")
+        assert rel_err(one, want[r * T:(r + 1) * T]) < tol, (r, rel_err(one, want[r * T:(r + 1) * T]))
     for r in range(2):  # reduce-scatter output: each rank's row slices of each chunk
         rows = np.concatenate([np.arange(c0 + r * 128, c0 + (r + 1) * 128) for c0 in range(0, B * T, 256)])
         rs = np.load(tmp_path / f"rs{r}.npy")

@@ -876,30 +876,35 @@ Status mha_forward(Mha* m, int batch, int seq, const void* x, void* pre, void* p
     if (rs_out) return comm_reducescatter(m, base, (size_t)(rows / m->nranks) * dm, !f32, st);
     return comm_allreduce(m, base, (size_t)rows * dm, !f32, st);
   };
+  // Row-sharded host I/O takes the exchange too: chunk i's row slice p is rank p's
+  // own sequences, so each rank projects and copies down exactly its rows.
+  const bool xa_rows = rows_io && comm_xa_ok(m);
+  // Exchange state: chunk i's receive slot (A operand of its output projection) and
+  // the rows of post that projection writes.
+  const void* a_slot[Mha::kMaxChunks] = {};
+  int64_t o_row0[Mha::kMaxChunks] = {}, o_rows[Mha::kMaxChunks] = {};
+  auto o_proj = [&](int i) -> Status {
+    WV_TRY(comm_xa_wait(m, i, s));
+    Proj o;
+    o.M = (int)o_rows[i];
+    o.K = m->cfg.qd;
+    o.lda = m->cfg.qd;
+    o.N = dm;
+    o.out = static_cast<char*>(postd) + o_row0[i] * dm * es;
+    o.ldo = dm;
+    o.w = m->wo_full.p;
+    o.a = a_slot[i];
+    prof_begin(kProfGemmO, s);
+    WV_TRY(run_proj(m, o, s));
+    prof_end(kProfGemmO, s);
+    return Status::ok();
+  };
+  if (xa || xa_rows) WV_TRY(m->attn.ensure((size_t)M * m->qd_l * es));
   if (xa) {
     // Per chunk: QKV projection and attention into attn (every chunk's rows kept
     // until its copies have read them), the exchange's copies, then the previous
     // chunk's output projection once its blocks have landed; so chunk i's transfers
     // overlap chunk i + 1's projections and attention.
-    WV_TRY(m->attn.ensure((size_t)M * m->qd_l * es));
-    const void* a_slot[Mha::kMaxChunks] = {};
-    int64_t o_row0[Mha::kMaxChunks] = {}, o_rows[Mha::kMaxChunks] = {};
-    auto o_proj = [&](int i) -> Status {
-      WV_TRY(comm_xa_wait(m, i, s));
-      Proj o;
-      o.M = (int)o_rows[i];
-      o.K = m->cfg.qd;
-      o.lda = m->cfg.qd;
-      o.N = dm;
-      o.out = static_cast<char*>(postd) + o_row0[i] * dm * es;
-      o.ldo = dm;
-      o.w = m->wo_full.p;
-      o.a = a_slot[i];
-      prof_begin(kProfGemmO, s);
-      WV_TRY(run_proj(m, o, s));
-      prof_end(kProfGemmO, s);
-      return Status::ok();
-    };
     int n_done = 0;
     for (int i = 0, b0 = 0; i < chunks && b0 < batch; ++i, b0 += bc_max, ++n_done) {
       const int bc = std::min(bc_max, batch - b0);
@@ -916,7 +921,7 @@ Status mha_forward(Mha* m, int batch, int seq, const void* x, void* pre, void* p
     }
     WV_TRY(o_proj(n_done - 1));
     WV_TRY(comm_xa_finish(m, s));  // the copies have read every chunk's rows
-  } else if (chunks == 1) {
+  } else if (chunks == 1 && !rows_io) {
     WV_TRY(run_rows(0, batch));
     if (m->comm) {
       prof_begin(kProfAllReduce, s);
@@ -949,10 +954,42 @@ Status mha_forward(Mha* m, int batch, int seq, const void* x, void* pre, void* p
       WV_CUDA(cudaEventRecord(m->gather_ev[i], m->comm_stream), "event");
       return Status::ok();
     };
+    // xa_rows: this rank's rows of chunk i (projected on s) go down on io_out
+    auto rows_down = [&](int i) -> Status {
+      if (defer_d2h) return Status::ok();
+      WV_CUDA(cudaEventRecord(m->io_ev[Mha::kMaxChunks + i], s), "event");
+      WV_CUDA(cudaStreamWaitEvent(m->io_out, m->io_ev[Mha::kMaxChunks + i], 0), "wait");
+      WV_CUDA(cudaMemcpyAsync(static_cast<char*>(post) + (int64_t)i * bcl * seq * dm * es,
+                              static_cast<char*>(postd) + o_row0[i] * dm * es, o_rows[i] * dm * es,
+                              cudaMemcpyDeviceToHost, m->io_out), "D2H post rows");
+      return Status::ok();
+    };
+    int xa_done = 0;
     if (rows_io) WV_TRY(gather_chunk(0));
     for (int i = 0, b0 = 0; i < chunks && b0 < batch; ++i, b0 += bc_max) {
       const int bc = std::min(bc_max, batch - b0);
       const int64_t r0 = (int64_t)b0 * seq, rows = (int64_t)bc * seq;
+      if (rows_io && xa_rows) {
+        // attention rows out to their owners, then the previous chunk's output
+        // projection over every head and its rows down to the host
+        const int64_t own = rows / nr;
+        WV_CUDA(cudaStreamWaitEvent(s, m->gather_ev[i], 0), "wait");
+        char* attn_i = m->attn.as<char>() + r0 * m->qd_l * es;
+        WV_TRY(run_rows(b0, bc, attn_i, false));
+        WV_CUDA(cudaEventRecord(m->chunk_done[i], s), "event");
+        if (i + 1 < chunks) WV_TRY(gather_chunk(i + 1));
+        prof_begin(kProfAllReduce, s);
+        WV_TRY(comm_xa_chunk(m, attn_i, rows, Mc_max, i, chunks, m->chunk_done[i], s, &a_slot[i]));
+        prof_end(kProfAllReduce, s);
+        o_rows[i] = own;
+        o_row0[i] = r0 + m->rank * own;
+        if (i > 0) {
+          WV_TRY(o_proj(i - 1));
+          WV_TRY(rows_down(i - 1));
+        }
+        ++xa_done;
+        continue;
+      }
       if (rows_io) {
         const int64_t own = rows / nr;
         WV_CUDA(cudaStreamWaitEvent(s, m->gather_ev[i], 0), "wait");
@@ -1006,6 +1043,11 @@ Status mha_forward(Mha* m, int batch, int seq, const void* x, void* pre, void* p
                                   static_cast<char*>(pred) + r0 * m->qd_l * es, rows * m->qd_l * es,
                                   cudaMemcpyDeviceToHost, m->io_out), "D2H pre");
       }
+    }
+    if (xa_done > 0) {
+      WV_TRY(o_proj(xa_done - 1));
+      WV_TRY(rows_down(xa_done - 1));
+      WV_TRY(comm_xa_finish(m, s));  // the copies have read every chunk's rows
     }
     if (m->comm) {
       WV_CUDA(cudaEventRecord(m->comm_done, m->comm_stream), "event");
