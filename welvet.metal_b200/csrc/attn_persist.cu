@@ -28,8 +28,6 @@
 
 #include <algorithm>
 #include <climits>
-#include <cstdlib>
-#include <string>
 
 namespace wv {
 namespace {
@@ -89,7 +87,7 @@ __device__ __forceinline__ Tile tile_of(const FParams& p, int t) {
   return w;
 }
 
-template <int HD, bool ALIBI, bool SIGMOID, bool EXPP>
+template <int HD, bool ALIBI, bool SIGMOID>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_persist_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
@@ -423,44 +421,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             a = v0 == -INFINITY ? 0.f : __frcp_rn(1.f + fast_exp2(-v0));
             c2 = v1 == -INFINITY ? 0.f : __frcp_rn(1.f + fast_exp2(-v1));
           });
-        } else if (EXPP && fast) {
-          // A quarter of the exponentials (every fourth pair of columns) as a
-          // polynomial on the FMA pipe, the rest on the MUFU pipe, whose 16 results
-          // per SM clock otherwise take as long as the block's MMAs. 2^y = 2^j * 2^f
-          // with j = round(y) (the 1.5 * 2^23 addition) and f in [-1/2, 1/2]; 2^f by a
-          // degree-3 polynomial fitted to relative error (Lawson-weighted least
-          // squares, 7.5e-5, far below the BF16 rounding of P); 2^j added to the
-          // exponent field. y is clamped at -125 so masked (-inf) scores give ~1e-38.
-          const uint64_t kMag = f2pack(12582912.f, 12582912.f), kNeg = f2pack(-1.f, -1.f);
-          const uint64_t kC3 = f2pack(0.055171624f, 0.055171624f), kC2 = f2pack(0.24261113f, 0.24261113f);
-          const uint64_t kC1 = f2pack(0.69326097f, 0.69326097f), kC0 = f2pack(0.99992806f, 0.99992806f);
-#pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            uint32_t pk[32];
-#pragma unroll
-            for (int c = 0; c < 32; ++c) {
-              const int i = 64 * hh + 2 * c;
-              float y0, y1, a, c2;
-              f2unpack(ffma2(f2pack(__uint_as_float(s[i]), __uint_as_float(s[i + 1])), sl2, nm2), y0, y1);
-              if ((c & 3) == 3) {
-                const uint64_t y2 = f2pack(fmaxf(y0, -125.f), fmaxf(y1, -125.f));
-                const uint64_t t2 = fadd2(y2, kMag);
-                const uint64_t fr = fadd2(y2, ffma2(t2, kNeg, kMag));
-                const uint64_t p2 = ffma2(ffma2(ffma2(kC3, fr, kC2), fr, kC1), fr, kC0);
-                float t0, t1, p0, p1;
-                f2unpack(t2, t0, t1);
-                f2unpack(p2, p0, p1);
-                a = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23));
-                c2 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
-              } else {
-                a = fast_exp2(y0);
-                c2 = fast_exp2(y1);
-              }
-              acc2[c & 3] = fadd2(acc2[c & 3], f2pack(a, c2));
-              pk[c] = pack_bf16x2(a, c2);
-            }
-            tmem_st32(tmem + lane_off + s_col + 32 * hh, pk);
-          }
         } else if (fast) {
           exp_loop([&](float x0, float x1, float& a, float& c2) {
             float y0, y1;
@@ -608,11 +568,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int HD, bool ALIBI, bool SIGMOID, bool EXPP = false>
+template <int HD, bool ALIBI, bool SIGMOID>
 cudaError_t launch_variant(const CUtensorMap* maps, const FParams& p, int* ctr, int ntiles, int grid,
                            cudaStream_t s) {
   using F = PT<HD>;
-  auto kern = attn_persist_kernel<HD, ALIBI, SIGMOID, EXPP>;
+  auto kern = attn_persist_kernel<HD, ALIBI, SIGMOID>;
   static const cudaError_t ready = [kern]() {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, F::SMEM);
     if (e != cudaSuccess) return e;
@@ -629,16 +589,6 @@ cudaError_t launch_variant(const CUtensorMap* maps, const FParams& p, int* ctr, 
   if (e != cudaSuccess) return e;
   kern<<<grid, kThreads, F::SMEM, s>>>(maps[0], maps[1], maps[2], maps[3], p, ctr, ntiles);
   return cudaGetLastError();
-}
-
-// Softmax exponentials of the fast path (no ALiBi, softmax scores): a quarter on
-// the FMA pipe (WELVET_B200_ATTN_EXP2=poly) or all on the MUFU pipe.
-bool exp_poly_enabled() {
-  static const bool on = [] {
-    const char* v = std::getenv("WELVET_B200_ATTN_EXP2");
-    return v && std::string(v) == "poly";
-  }();
-  return on;
 }
 
 template <int HD> cudaError_t launch(const AttnArgs& a, cudaStream_t s) {
@@ -677,9 +627,8 @@ template <int HD> cudaError_t launch(const AttnArgs& a, cudaStream_t s) {
   if (a.alibi)
     return a.sigmoid ? launch_variant<HD, true, true>(maps, p, a.tile_ctr, nt, grid, s)
                      : launch_variant<HD, true, false>(maps, p, a.tile_ctr, nt, grid, s);
-  if (a.sigmoid) return launch_variant<HD, false, true>(maps, p, a.tile_ctr, nt, grid, s);
-  return exp_poly_enabled() ? launch_variant<HD, false, false, true>(maps, p, a.tile_ctr, nt, grid, s)
-                            : launch_variant<HD, false, false>(maps, p, a.tile_ctr, nt, grid, s);
+  return a.sigmoid ? launch_variant<HD, false, true>(maps, p, a.tile_ctr, nt, grid, s)
+                   : launch_variant<HD, false, false>(maps, p, a.tile_ctr, nt, grid, s);
 }
 
 }  // namespace
