@@ -38,7 +38,7 @@ constexpr int kBoxBytes = kPageTokens * 128;   // one 16-row box
 template <int HD> struct DT {
   static constexpr int NBOX = HD / kBox;
   static constexpr int TILE = NBOX * kBoxBytes;                   // one page of K (or V)
-  static constexpr int STAGES = HD == 64 ? 6 : HD == 128 ? 3 : 2;  // per warp
+  static constexpr int STAGES = HD == 256 ? 2 : 3;  // per warp
   static constexpr int STAGE_BYTES = 2 * TILE;                     // K + V
   static constexpr int RING = STAGES * STAGE_BYTES;                // per warp
   static constexpr int OFF_BAR = kWarps * RING;
