@@ -7,10 +7,11 @@
 // front and the M rows ride along on m16n8k16 tensor-core MMAs.
 //
 // Work split (weights as the A operand, "swap AB"): a CTA owns 128 output columns
-// (128 weight rows = the M = 128 rows of a tcgen05 MMA) over a 512-wide K slice,
-// the batch rows are the MMA's N (a multiple of 16, zero-filled past M by TMA); a
-// thread-block cluster of ks = K / 512 CTAs (at most 8) along K covers the whole K
-// range. A TMA thread loads the slice's eight 64-wide k blocks of W (16 KB) and x —
+// (128 weight rows = the M = 128 rows of a tcgen05 MMA) over a 512-wide K slice
+// (256 or 128 wide when that keeps the grid in one wave with more CTAs), the batch
+// rows are the MMA's N (a multiple of 16, zero-filled past M by TMA); a
+// thread-block cluster of ks = K / slice CTAs (at most 8) along K covers the whole K
+// range. A TMA thread loads the slice's 64-wide k blocks of W (16 KB each) and x —
 // all at once when the grid is one wave (one CTA per SM), else through a
 // three-stage ring (two CTAs per SM) — one thread issues 4 UMMAs (K = 16) per block
 // into a TMEM accumulator [128 lanes = output columns][N columns = batch rows], and
@@ -53,6 +54,7 @@ static_assert(2 * kNBMax * kRedLd * 4 <= 3 * kStageBytes, "partial and summed ro
 
 struct VParams {
   int M, N, K, ks, nb;  // nb: batch rows rounded up to 16 (the MMA's N)
+  int kb;               // 64-wide k blocks per CTA (the K slice is kb * 64)
   __nv_bfloat16* out;
   int ldo;
   const float2* rope_tab;
@@ -94,7 +96,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int rank = ks > 1 ? (int)cluster_rank() : 0;
   const int tile = blockIdx.x / ks;
   const int n0 = tile * kNC;
-  const int kbeg = rank * kSlice;
+  const int kbeg = rank * p.kb * kBK;
   const int warp = (int)warp_id(), lane = (int)lane_id(), tid = (int)threadIdx.x;
   const int rpr = (p.nb + ks - 1) / ks;  // batch rows per CTA of the cluster
 
@@ -127,13 +129,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t bytes = (uint32_t)(kWBytes + p.nb * kBK * 2);
       // The weights do not depend on the previous kernel: the first S blocks of W
       // are requested before waiting for it (programmatic dependent launch), x after.
-      for (int b = 0; b < S; ++b) {
+      const int first = min(S, p.kb);
+      for (int b = 0; b < first; ++b) {
         mbar_arrive_expect_tx(&full[b], bytes);
         tma_load_2d(smem + b * kStageBytes, &tmW, &full[b], kbeg + b * kBK, n0);
       }
       pdl_wait();
-      for (int b = 0; b < S; ++b) tma_load_2d(smem + b * kStageBytes + kWBytes, &tmX, &full[b], kbeg + b * kBK, 0);
-      for (int b = S; b < kBlocks; ++b) {
+      for (int b = 0; b < first; ++b)
+        tma_load_2d(smem + b * kStageBytes + kWBytes, &tmX, &full[b], kbeg + b * kBK, 0);
+      for (int b = S; b < p.kb; ++b) {
         const int s = b % S;
         if (!mbar_wait(&empty[s], ((b / S) & 1) ^ 1, abort_flag, p.err, kErrWaitEmpty)) break;
         uint8_t* st = smem + s * kStageBytes;
@@ -146,7 +150,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------ UMMA issuer
     if (lane == 0) {
       const uint32_t idesc = idesc_make(1, kNC, p.nb, 0, 0);
-      for (int b = 0; b < kBlocks; ++b) {
+      for (int b = 0; b < p.kb; ++b) {
         const int s = b % S;
         if (!mbar_wait(&full[s], (b / S) & 1, abort_flag, p.err, kErrWaitFull)) break;
         tc_fence_after();
@@ -155,7 +159,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kk = 0; kk < kBK / 16; ++kk)
           umma_f16_ss(tmem, sdesc_sw128(wa + 32 * kk, 16, 1024), sdesc_sw128(xa + 32 * kk, 16, 1024), idesc,
                       (b > 0 || kk > 0) ? 1u : 0u);
-        if (S < kBlocks) umma_commit(&empty[s]);
+        if (S < p.kb) umma_commit(&empty[s]);
       }
       umma_commit(acc_full);
     }
@@ -330,7 +334,18 @@ cudaError_t gemv_decode(const GemmArgs& a, cudaStream_t s) {
   p.kv_col0 = a.kv_col0;
   p.kv_dim = a.kv_dim;
   p.err = a.err;
-  p.ks = a.K / kSlice;
+  const int tiles = (a.N + kNC - 1) / kNC;
+  // K slices of 512 (eight k blocks) per CTA; halved (down to 128) while the
+  // cluster stays at 4 CTAs or fewer and the grid within one wave, so that short-K
+  // projections (a head shard's output projection: K = 512, 32 CTAs -> 128) spread
+  // their weight stream over more SMs. Larger clusters lost more in the distributed
+  // shared-memory reduction than they gained (K = 2048 at 8 CTAs: 12.7 -> 18.8 us).
+  int slice = kSlice;
+  while (slice > 2 * kBK && a.K % (slice / 2) == 0 && a.K / (slice / 2) <= 4 &&
+         tiles * (a.K / (slice / 2)) <= a.sm_count && p.nb % (a.K / (slice / 2)) == 0)
+    slice /= 2;
+  p.ks = a.K / slice;
+  p.kb = slice / kBK;
   alignas(64) CUtensorMap maps[2];
   const int BF16 = (int)CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, SW = (int)CU_TENSOR_MAP_SWIZZLE_128B;
   // W [N rows][K]: 128-row boxes; x [M rows][K]: boxes of nb rows, rows past M
@@ -338,7 +353,6 @@ cudaError_t gemv_decode(const GemmArgs& a, cudaStream_t s) {
   if (!make_tma_2d(&maps[0], a.b, BF16, 2, a.K, a.N, a.ldb, kBK, kNC, SW) ||
       !make_tma_2d(&maps[1], a.a, BF16, 2, a.K, a.M, a.lda, kBK, p.nb, SW))
     return cudaErrorInvalidValue;
-  const int tiles = (a.N + kNC - 1) / kNC;
   // one wave (and a cluster that divides the batch rows): every k block of a CTA in
   // flight at once; else a ring, two CTAs per SM
   if (tiles * p.ks <= a.sm_count && p.nb % p.ks == 0) return launch<kBlocks, kNBMax>(maps, p, tiles, s);
