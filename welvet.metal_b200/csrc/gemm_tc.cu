@@ -16,6 +16,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <type_traits>
 #include <mutex>
 
@@ -100,8 +101,21 @@ struct KParams {
   uint32_t* err;
 };
 
+// Bytes of weights in one raster panel (WELVET_B200_GEMM_PANEL_MB, default 24). At
+// the QKV shape (K = 4096, 2 MB of BF16 weights per N-tile) 48 MB panels read 2.5x
+// the algorithmic bytes from DRAM and 24 MB panels 1.85x, the panel staying in the
+// part of the L2 that the A stream leaves it, at equal or slightly shorter times.
+inline double panel_bytes() {
+  static const double b = [] {
+    const char* v = std::getenv("WELVET_B200_GEMM_PANEL_MB");
+    const double mb = v && *v ? std::atof(v) : 0.0;
+    return (mb > 0.0 ? mb : 24.0) * 1.0e6;
+  }();
+  return b;
+}
+
 // Grouped rasterisation over N: a panel of gn N-tiles of B (the weights: at most
-// ~48 MB, chosen on the host) is swept by every M-tile before the next panel, N
+// ~24 MB, chosen on the host) is swept by every M-tile before the next panel, N
 // fastest within the panel. The panel stays L2-resident, so B is read from HBM once
 // and A once per panel (n_tiles / gn times); the CTAs of one wave share their A
 // tiles too. (Grouping 8 M-tiles across all of N instead re-read the whole weight
@@ -778,7 +792,7 @@ template <int KIND> cudaError_t launch(const GemmArgs& g, cudaStream_t stream) {
     // B bytes of one N-tile as stored in HBM (codes for FP8 / NF4, both TF32 parts)
     const double b_elem = byte_codes<KIND>() ? 1.0 : nibble_codes<KIND>() ? 0.5 : (double)(T::ELEM * T::NB);
     const double panel = (double)T::BN * g.K * b_elem;
-    const int gn = (int)std::max(1.0, std::floor(48.0e6 / std::max(panel, 1.0)));
+    const int gn = (int)std::max(1.0, std::floor(panel_bytes() / std::max(panel, 1.0)));
     p.gn = std::min(p.n_tiles, gn);
   }
   p.out = g.out;
