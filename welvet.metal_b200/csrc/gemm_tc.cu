@@ -11,6 +11,7 @@
 // (128-byte swizzle, the canonical K-major UMMA layout).
 #include "codec.cuh"
 #include "common.cuh"
+#include "gemm_raster.cuh"
 #include "kernels.h"
 
 #include <cudaTypedefs.h>
@@ -121,12 +122,7 @@ inline double panel_bytes() {
 // tiles too. (Grouping 8 M-tiles across all of N instead re-read the whole weight
 // matrix once per 8 M-tiles: 3.2x the algorithmic bytes at the QKV shape.)
 __device__ __forceinline__ void tile_coords(int t, const KParams& p, int& mb, int& nb) {
-  const int group = p.gn * p.m_tiles;
-  const int g = t / group, r = t % group;
-  const int first = g * p.gn;
-  const int gn = min(p.gn, p.n_tiles - first);
-  nb = first + r % gn;
-  mb = r / gn;
+  raster_tile(t, p.gn, p.m_tiles, p.n_tiles, mb, nb);
 }
 
 // Work of persistent tile index t: output tile (mb, nb) and k-blocks [kb0, kb1).
